@@ -1,0 +1,128 @@
+/* C-ABI of the sm_100a denoising engine (libdfb_cuda.so).
+ *
+ * This is the seam the reference crosses between its sampler loop and its GGML
+ * graph: diffuse_forward_full / diffuse_forward_cached (src/diffuse-graph.h:16-42,
+ * called from src/diffuse-sampler.cpp:149,167,187) plus the per-step candidate
+ * extraction / ordering / commit of src/diffuse-sampler.cpp:222-323.  Here one call
+ * (dfb_gen_step) runs the active-set build, the whole forward and the sampler on the
+ * device; tokens, masks, the K/V cache and the logits buffer stay in HBM.
+ *
+ * Conventions: plain C types only; every function returns 0 (DFB_OK) or a negative
+ * DFB_ERR_* code and leaves a message for dfb_last_error() (thread-local).  The
+ * library never exits the process.  Objects are single-threaded: one host thread
+ * drives a dfb_ctx at a time; a dfb_model may be shared by several contexts on the
+ * same device.
+ */
+#ifndef DIFFUSE_B200_H
+#define DIFFUSE_B200_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DFB_OK               0
+#define DFB_ERR_ARG         -1   /* bad argument / shape / type */
+#define DFB_ERR_CUDA        -2   /* CUDA runtime or driver error */
+#define DFB_ERR_NOMEM       -3   /* device allocation failed */
+#define DFB_ERR_STATE       -4   /* call out of order (e.g. step before begin) */
+#define DFB_ERR_TIMEOUT     -5   /* a kernel gave up a bounded wait */
+#define DFB_ERR_UNSUPPORTED -6   /* feature not available on this build */
+
+typedef struct dfb_model dfb_model;
+typedef struct dfb_ctx dfb_ctx;
+
+/* Hyper-parameters, as resolved from GGUF metadata by the host loader
+ * (diffuse-model.cpp:105-128). */
+typedef struct {
+    int32_t n_vocab, n_embd, n_head, n_head_kv, n_layer, n_ff, n_ctx_max, mask_token_id;
+    float   rope_theta, rms_norm_eps;
+    int32_t shift_logits; /* 1 for Dream: position i reads logits row max(i-1,0) (diffuse-sampler.cpp:74,235) */
+} dfb_hparams;
+
+/* Tensor roles (the tensors diffuse-model.cpp:146-178 resolves). */
+enum {
+    DFB_TOK_EMBD = 0, DFB_OUTPUT_NORM, DFB_OUTPUT,
+    DFB_ATTN_NORM, DFB_WQ, DFB_WK, DFB_WV, DFB_WO, DFB_BQ, DFB_BK, DFB_BV,
+    DFB_FFN_NORM, DFB_GATE, DFB_UP, DFB_DOWN,
+    DFB_N_ROLES
+};
+
+/* GGML type ids accepted for tensors: F32 0, F16 1, Q8_0 8, Q4_K 12, Q6_K 14, BF16 30. */
+
+/* Mirrors diffuse_sampler_params (include/diffuse.h) field by field. */
+typedef struct {
+    int32_t  n_steps;
+    float    temperature;
+    int32_t  schedule;          /* 0 COSINE, 1 LINEAR */
+    int32_t  remasking;         /* 0 LOW_CONFIDENCE, 1 RANDOM, 2 ENTROPY_EXIT, 3 MASKGIT_PLUS, 4 TOPK_MARGIN */
+    uint32_t seed;
+    float    entropy_threshold;
+    int32_t  use_cache;
+    int32_t  cache_refresh;
+    int32_t  cache_keep_active;
+} dfb_sampler_params;
+
+/* What one denoising step did (feeds the reference's per-step log line,
+ * diffuse-sampler.cpp:328-335). */
+typedef struct {
+    int32_t n_active;    /* query rows the forward computed */
+    int32_t n_unmasked;  /* positions committed this step */
+    int32_t n_masked;    /* positions still masked after the step */
+    int32_t used_cache;  /* 1 if the cached (active-set) forward ran */
+    float   fwd_ms;      /* device time of the forward, CUDA events */
+    float   step_ms;     /* device time of forward + sampler */
+} dfb_step_stats;
+
+const char *dfb_last_error(void);
+int dfb_device_count(int *n);
+
+/* ── model ── */
+int  dfb_model_create(const dfb_hparams *hp, int device, dfb_model **out);
+/* Upload one GGUF tensor (raw block bytes exactly as stored in the file; ne0 is the
+ * row length, ne1 the row count).  Replaces diffuse-model.cpp:146-178's binding of
+ * GGML tensors; weights are re-tiled for the GEMM on the way in. */
+int  dfb_model_set_tensor(dfb_model *m, int role, int layer, int ggml_type, int64_t ne0, int64_t ne1,
+                          const void *host_data, size_t nbytes);
+int  dfb_model_finalize(dfb_model *m);
+void dfb_model_free(dfb_model *m);
+/* Device bytes held by the model's weights. */
+int  dfb_model_bytes(const dfb_model *m, size_t *bytes);
+
+/* ── context ── */
+int  dfb_ctx_create(dfb_model *m, int n_ctx, dfb_ctx **out);
+void dfb_ctx_free(dfb_ctx *c);
+
+/* diffuse_forward (diffuse-graph.cpp:676-680): full forward over n host tokens, logits
+ * copied to the host buffer [n * n_vocab]. */
+int dfb_forward(dfb_ctx *c, const int32_t *tokens, int n, float *logits_host);
+
+/* One linear layer through the production dequant-fused GEMM: y[M x ne1] = x[M x ne0] . W^T
+ * for a model weight (host buffers).  Exposed for parity tests of the GEMM alone. */
+int dfb_linear(dfb_ctx *c, int role, int layer, const float *x_host, int M, float *y_host);
+
+/* ── generation: the device side of diffuse_sample (diffuse-sampler.cpp:60-370) ── */
+/* Set up seq = prompt ‖ MASK × n_gen, masks, cache and logits buffer on the device. */
+int dfb_gen_begin(dfb_ctx *c, const int32_t *prompt, int n_prompt, int n_gen, const dfb_sampler_params *p);
+/* One step: active set (or all positions when force_full), forward, sampler.
+ * n_unmask_sched is tokens_to_unmask(step, ...) computed by the host exactly as the
+ * reference does; for RANDOM remasking `order` holds the host-side shuffle of the
+ * candidate indices (length n_masked), else NULL.  Blocks until the step is done and
+ * fills *stats (may be NULL). */
+int dfb_gen_step(dfb_ctx *c, int step, int n_unmask_sched, int force_full, const int32_t *order,
+                 dfb_step_stats *stats);
+/* Copy the whole current sequence (prompt ‖ generated) to the host. */
+int dfb_gen_tokens(dfb_ctx *c, int32_t *seq_host, int cap);
+/* Positions / tokens committed by the last step, in commit order; returns the count. */
+int dfb_gen_commits(dfb_ctx *c, int32_t *pos_host, int32_t *tok_host, int cap);
+/* Rows [row0, row0+nrows) of the persistent logits buffer (parity checks). */
+int dfb_gen_logits(dfb_ctx *c, int row0, int nrows, float *host);
+
+/* Device stream of a context (cudaStream_t as void*), for callers that time it. */
+int dfb_ctx_stream(dfb_ctx *c, void **stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
