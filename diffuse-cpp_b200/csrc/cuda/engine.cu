@@ -1,0 +1,918 @@
+// libdfb_cuda: implementation of the C-ABI in include/diffuse_b200.h.
+//
+// Owns the device-resident model (weights re-tiled for the dequant GEMM), the
+// per-context activations / K/V cache / logits buffer / sequence state, and the
+// launch order of one denoising step:
+//   step_prepare -> embed -> L x [rmsnorm, QKV(+bias,RoPE,cache write), attention,
+//   O(+residual), rmsnorm, gate|up(SwiGLU), down(+residual)] -> rmsnorm -> lm_head
+//   (logits scattered to their positions) -> row statistics -> order + commit.
+// This is the device side of src/diffuse-sampler.cpp:127-323 with the forward of
+// src/diffuse-graph.cpp:11-160 / 395-593.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "../../../include/diffuse_b200.h"
+#include "attention.cuh"
+#include "gemm_dq.cuh"
+#include "ops.cuh"
+
+using namespace dfb;
+
+// ───────────────────────── errors ─────────────────────────
+static thread_local std::string g_err;
+static int set_err(int code, const char *fmt, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return code;
+}
+#define CK(call)                                                                                   \
+    do {                                                                                           \
+        cudaError_t e_ = (call);                                                                   \
+        if (e_ != cudaSuccess)                                                                     \
+            return set_err(e_ == cudaErrorMemoryAllocation ? DFB_ERR_NOMEM : DFB_ERR_CUDA,         \
+                           "%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_), __FILE__, __LINE__); \
+    } while (0)
+#define RET(x)                 \
+    do {                       \
+        int r_ = (x);          \
+        if (r_ != DFB_OK) return r_; \
+    } while (0)
+
+extern "C" const char *dfb_last_error(void) { return g_err.c_str(); }
+
+extern "C" int dfb_device_count(int *n) {
+    if (!n) return set_err(DFB_ERR_ARG, "null pointer");
+    cudaError_t e = cudaGetDeviceCount(n);
+    if (e != cudaSuccess) {
+        *n = 0;
+        return set_err(DFB_ERR_CUDA, "cudaGetDeviceCount: %s", cudaGetErrorString(e));
+    }
+    return DFB_OK;
+}
+
+// ───────────────────────── tensor maps ─────────────────────────
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        cudaDriverEntryPointQueryResult q;
+        void *p = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+// 2-D f16 matrix [rows][cols], 128-byte swizzled boxes of box_rows x 64.
+static int make_tmap(CUtensorMap *m, const void *ptr, uint64_t cols, uint64_t rows, uint32_t box_rows) {
+    auto fn = encode_fn();
+    if (!fn) return set_err(DFB_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    if ((cols * 2) % 16 != 0) return set_err(DFB_ERR_ARG, "row length %llu not a multiple of 8", (unsigned long long)cols);
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {cols * 2};
+    cuuint32_t box[2] = {64, box_rows};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(ptr), dims, strides, box, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_err(DFB_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return DFB_OK;
+}
+
+// ───────────────────────── host-side format helpers ─────────────────────────
+enum { G_F32 = 0, G_F16 = 1, G_Q8_0 = 8, G_Q4_K = 12, G_Q6_K = 14, G_BF16 = 30 };
+
+static int64_t ggml_row_bytes(int type, int64_t n) {
+    switch (type) {
+        case G_F32: return 4 * n;
+        case G_F16: case G_BF16: return 2 * n;
+        case G_Q8_0: return n / 32 * 34;
+        case G_Q4_K: return n / 256 * 144;
+        case G_Q6_K: return n / 256 * 210;
+        default: return -1;
+    }
+}
+static float h2f_host(uint16_t h) {
+    __half_raw r;
+    r.x = h;
+    return __half2float(__half(r));
+}
+static uint16_t f2h_host(float f) {
+    __half h = __float2half_rn(f);
+    return reinterpret_cast<__half_raw &>(h).x;
+}
+static float bf2f_host(uint16_t b) {
+    uint32_t u = (uint32_t)b << 16;
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+// Dequantize one row to f32 (host; used for norms, biases and non-F16 embeddings).
+static void dequant_row_host(int type, const uint8_t *src, int64_t n, float *dst) {
+    switch (type) {
+        case G_F32: memcpy(dst, src, n * 4); return;
+        case G_F16: for (int64_t i = 0; i < n; i++) { uint16_t h; memcpy(&h, src + 2 * i, 2); dst[i] = h2f_host(h); } return;
+        case G_BF16: for (int64_t i = 0; i < n; i++) { uint16_t h; memcpy(&h, src + 2 * i, 2); dst[i] = bf2f_host(h); } return;
+        case G_Q8_0:
+            for (int64_t b = 0; b < n / 32; b++) {
+                uint16_t dh; memcpy(&dh, src + 34 * b, 2);
+                const float d = h2f_host(dh);
+                for (int l = 0; l < 32; l++) dst[32 * b + l] = d * (float)(int8_t)src[34 * b + 2 + l];
+            }
+            return;
+        case G_Q4_K:
+            for (int64_t b = 0; b < n / 256; b++) {
+                const uint8_t *blk = src + 144 * b;
+                uint16_t dh, mh; memcpy(&dh, blk, 2); memcpy(&mh, blk + 2, 2);
+                const float d = h2f_host(dh), dmin = h2f_host(mh);
+                const uint8_t *q = blk + 4, *qs = blk + 16;
+                for (int j = 0; j < 8; j++) {
+                    int sc, mn;
+                    if (j < 4) { sc = q[j] & 63; mn = q[j + 4] & 63; }
+                    else { sc = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4); mn = (q[j + 4] >> 4) | ((q[j] >> 6) << 4); }
+                    for (int l = 0; l < 32; l++) {
+                        const int v = (j & 1) ? (qs[32 * (j >> 1) + l] >> 4) : (qs[32 * (j >> 1) + l] & 0xF);
+                        dst[256 * b + 32 * j + l] = d * sc * v - dmin * mn;
+                    }
+                }
+            }
+            return;
+        case G_Q6_K:
+            for (int64_t b = 0; b < n / 256; b++) {
+                const uint8_t *blk = src + 210 * b, *ql = blk, *qh = blk + 128;
+                const int8_t *sc = (const int8_t *)(blk + 192);
+                uint16_t dh; memcpy(&dh, blk + 208, 2);
+                const float d = h2f_host(dh);
+                for (int e = 0; e < 256; e++) {
+                    const int h = e / 128, g = (e % 128) / 32, l = e % 32;
+                    const uint8_t lb = ql[64 * h + (g & 1) * 32 + l];
+                    const int nib = (g >= 2) ? (lb >> 4) : (lb & 0xF);
+                    const int q = (nib | (((qh[32 * h + l] >> (2 * g)) & 3) << 4)) - 32;
+                    dst[256 * b + e] = d * sc[e / 16] * q;
+                }
+            }
+            return;
+    }
+}
+
+// ───────────────────────── device weights ─────────────────────────
+struct WMat {
+    int wt = -1;
+    int n_rows = 0, n_tiles = 0, K = 0, kb = 0;
+    uint8_t *d = nullptr;
+    CUtensorMap tm{};
+    size_t bytes = 0;
+};
+
+static int wt_of(int ggml_type) {
+    switch (ggml_type) {
+        case G_Q4_K: return W_Q4K;
+        case G_Q6_K: return W_Q6K;
+        case G_Q8_0: return W_Q80;
+        case G_F16: case G_F32: case G_BF16: return W_F16;
+        default: return -1;
+    }
+}
+
+// Re-tile rows (nullptr = zero row; rows.size() a multiple of 128) into the chunk
+// layouts the dequant kernel reads (see gemm_dq.cuh), or into a plain f16 matrix.
+static void retile_range(const std::vector<const uint8_t *> &rows, int type, int64_t K, int kb, int t0, int t1,
+                         uint8_t *out) {
+    const int wt = wt_of(type);
+    const int RB = raw_chunk_bytes(wt);
+    if (wt == W_F16) {
+        for (int r = t0 * 128; r < t1 * 128; r++) {
+            uint16_t *dst = reinterpret_cast<uint16_t *>(out) + (size_t)r * K;
+            const uint8_t *src = rows[r];
+            if (!src) { memset(dst, 0, K * 2); continue; }
+            if (type == G_F16) memcpy(dst, src, K * 2);
+            else if (type == G_F32) for (int64_t i = 0; i < K; i++) { float f; memcpy(&f, src + 4 * i, 4); dst[i] = f2h_host(f); }
+            else for (int64_t i = 0; i < K; i++) { uint16_t b; memcpy(&b, src + 2 * i, 2); dst[i] = f2h_host(bf2f_host(b)); }
+        }
+        return;
+    }
+    static const uint8_t zeros[288] = {0};
+    for (int t = t0; t < t1; t++)
+        for (int b = 0; b < kb; b++) {
+            uint8_t *C = out + ((size_t)t * kb + b) * RB;
+            for (int r = 0; r < 128; r++) {
+                const uint8_t *row = rows[(size_t)t * 128 + r];
+                if (wt == W_Q4K) {
+                    const uint8_t *blk = row ? row + (size_t)b * 144 : zeros;
+                    memcpy(C + 4 * r, blk, 4);
+                    memcpy(C + 512 + 12 * r, blk + 4, 12);
+                    for (int c = 0; c < 8; c++) memcpy(C + 2048 + 128 * r + ((c ^ (r & 7)) << 4), blk + 16 + 16 * c, 16);
+                } else if (wt == W_Q6K) {
+                    const uint8_t *blk = row ? row + (size_t)b * 210 : zeros;
+                    for (int c = 0; c < 8; c++) memcpy(C + 128 * r + ((c ^ (r & 7)) << 4), blk + 16 * c, 16);
+                    for (int c = 0; c < 4; c++) memcpy(C + 16384 + 64 * r + ((c ^ ((r >> 1) & 3)) << 4), blk + 128 + 16 * c, 16);
+                    memcpy(C + 24576 + 16 * r, blk + 192, 16);
+                    memcpy(C + 26624 + 2 * r, blk + 208, 2);
+                } else {  // Q8_0: 8 blocks of 32 per k-block; blocks past K are zero
+                    for (int i = 0; i < 8; i++) {
+                        const int64_t blk_idx = (int64_t)b * 8 + i;
+                        const uint8_t *blk = (row && blk_idx * 32 < K) ? row + blk_idx * 34 : zeros;
+                        memcpy(C + 16 * r + 2 * i, blk, 2);
+                        for (int hlf = 0; hlf < 2; hlf++) {
+                            const int c = 2 * i + hlf;
+                            memcpy(C + 2048 + 256 * r + (((c & 8) | ((c & 7) ^ (r & 7))) << 4), blk + 2 + 16 * hlf, 16);
+                        }
+                    }
+                }
+            }
+        }
+}
+
+static int build_wmat(const std::vector<const uint8_t *> &rows, int type, int64_t K, WMat &w) {
+    const int wt = wt_of(type);
+    if (wt < 0) return set_err(DFB_ERR_UNSUPPORTED, "GGML type %d not supported for a linear weight", type);
+    if (rows.size() % 128) return set_err(DFB_ERR_ARG, "internal: rows not padded");
+    if ((wt == W_Q4K || wt == W_Q6K) && K % 256) return set_err(DFB_ERR_ARG, "K-quant row length %lld not a multiple of 256", (long long)K);
+    if (wt == W_Q80 && K % 32) return set_err(DFB_ERR_ARG, "Q8_0 row length %lld not a multiple of 32", (long long)K);
+    if (wt == W_F16 && K % 8) return set_err(DFB_ERR_ARG, "F16 row length %lld not a multiple of 8", (long long)K);
+    w.wt = wt;
+    w.n_rows = (int)rows.size();
+    w.n_tiles = w.n_rows / 128;
+    w.K = (int)K;
+    w.kb = (int)((K + 255) / 256);
+    w.bytes = wt == W_F16 ? (size_t)w.n_rows * K * 2 : (size_t)w.n_tiles * w.kb * raw_chunk_bytes(wt);
+    std::vector<uint8_t> host(w.bytes);
+    const int nthr = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
+    std::vector<std::thread> th;
+    for (int i = 0; i < nthr; i++) {
+        const int t0 = (int)((int64_t)w.n_tiles * i / nthr), t1 = (int)((int64_t)w.n_tiles * (i + 1) / nthr);
+        th.emplace_back(retile_range, std::cref(rows), type, K, w.kb, t0, t1, host.data());
+    }
+    for (auto &t : th) t.join();
+    CK(cudaMalloc(&w.d, w.bytes));
+    CK(cudaMemcpy(w.d, host.data(), w.bytes, cudaMemcpyHostToDevice));
+    if (wt == W_F16) RET(make_tmap(&w.tm, w.d, (uint64_t)K, (uint64_t)w.n_rows, 128));
+    return DFB_OK;
+}
+
+struct LayerW {
+    WMat qkv, o, gateup, down;
+    float *attn_norm = nullptr, *ffn_norm = nullptr, *bias_qkv = nullptr;
+};
+
+struct HostTensor {
+    int type = -1;
+    int64_t ne0 = 0, ne1 = 0;
+    const uint8_t *data = nullptr;
+    size_t nbytes = 0;
+};
+
+struct dfb_model {
+    dfb_hparams hp{};
+    int device = 0, n_sm = 0;
+    int hd = 0, n_q = 0, n_kv = 0, nq_pad = 0, nk_pad = 0;
+    std::vector<HostTensor> staged;  // [role + DFB_N_ROLES * layer]
+    // device
+    void *embd = nullptr;
+    int embd_f16 = 1;
+    float *output_norm = nullptr;
+    WMat lm_head;
+    std::vector<LayerW> layers;
+    bool finalized = false;
+    size_t bytes = 0;
+    std::vector<void *> allocs;
+};
+
+static HostTensor &staged(dfb_model *m, int role, int layer) {
+    return m->staged[(size_t)layer * DFB_N_ROLES + role];
+}
+
+extern "C" int dfb_model_create(const dfb_hparams *hp, int device, dfb_model **out) {
+    if (!hp || !out) return set_err(DFB_ERR_ARG, "null pointer");
+    *out = nullptr;
+    if (hp->n_layer <= 0 || hp->n_embd <= 0 || hp->n_head <= 0 || hp->n_head_kv <= 0 || hp->n_ff <= 0 ||
+        hp->n_vocab <= 0 || hp->n_head % hp->n_head_kv || hp->n_embd % hp->n_head)
+        return set_err(DFB_ERR_ARG, "inconsistent hyper-parameters");
+    const int hd = hp->n_embd / hp->n_head;
+    if (hd != 16 && hd != 32 && hd != 64 && hd != 128)
+        return set_err(DFB_ERR_UNSUPPORTED, "head_dim %d not supported (16/32/64/128)", hd);
+    int ndev = 0;
+    CK(cudaGetDeviceCount(&ndev));
+    if (device < 0 || device >= ndev) return set_err(DFB_ERR_ARG, "device %d out of range (%d devices)", device, ndev);
+    CK(cudaSetDevice(device));
+    cudaDeviceProp prop;
+    CK(cudaGetDeviceProperties(&prop, device));
+    if (prop.major != 10) return set_err(DFB_ERR_UNSUPPORTED, "device %d is sm_%d%d; this build targets sm_100a", device, prop.major, prop.minor);
+    auto *m = new dfb_model();
+    m->hp = *hp;
+    m->device = device;
+    m->n_sm = prop.multiProcessorCount;
+    m->hd = hd;
+    m->n_q = hp->n_embd;
+    m->n_kv = hp->n_head_kv * hd;
+    m->nq_pad = (m->n_q + 127) / 128 * 128;
+    m->nk_pad = (m->n_kv + 127) / 128 * 128;
+    m->staged.resize((size_t)DFB_N_ROLES * hp->n_layer);
+    m->layers.resize(hp->n_layer);
+    *out = m;
+    return DFB_OK;
+}
+
+extern "C" int dfb_model_set_tensor(dfb_model *m, int role, int layer, int type, int64_t ne0, int64_t ne1,
+                                    const void *data, size_t nbytes) {
+    if (!m || !data) return set_err(DFB_ERR_ARG, "null pointer");
+    if (m->finalized) return set_err(DFB_ERR_STATE, "model already finalized");
+    if (role < 0 || role >= DFB_N_ROLES) return set_err(DFB_ERR_ARG, "bad role %d", role);
+    const bool global = role <= DFB_OUTPUT;
+    if (global) layer = 0;
+    else if (layer < 0 || layer >= m->hp.n_layer) return set_err(DFB_ERR_ARG, "bad layer %d", layer);
+    const int64_t rb = ggml_row_bytes(type, ne0);
+    if (rb < 0) return set_err(DFB_ERR_UNSUPPORTED, "GGML type %d not supported", type);
+    if ((int64_t)nbytes < rb * std::max<int64_t>(ne1, 1)) return set_err(DFB_ERR_ARG, "tensor role %d: %zu bytes < %lld expected", role, nbytes, (long long)(rb * ne1));
+    HostTensor &t = staged(m, role, layer);
+    t.type = type; t.ne0 = ne0; t.ne1 = std::max<int64_t>(ne1, 1); t.data = (const uint8_t *)data; t.nbytes = nbytes;
+    return DFB_OK;
+}
+
+static int upload_vec(dfb_model *m, const HostTensor &t, int64_t n, float **out) {
+    if (t.ne0 * t.ne1 < n) return set_err(DFB_ERR_ARG, "vector has %lld elements, need %lld", (long long)(t.ne0 * t.ne1), (long long)n);
+    std::vector<float> v(n);
+    dequant_row_host(t.type, t.data, n, v.data());
+    CK(cudaMalloc(out, n * 4));
+    m->allocs.push_back(*out);
+    CK(cudaMemcpy(*out, v.data(), n * 4, cudaMemcpyHostToDevice));
+    m->bytes += n * 4;
+    return DFB_OK;
+}
+
+static int check_mat(const HostTensor &t, const char *what, int64_t ne0, int64_t ne1) {
+    if (!t.data) return set_err(DFB_ERR_STATE, "tensor %s missing", what);
+    if (t.ne0 != ne0 || t.ne1 != ne1)
+        return set_err(DFB_ERR_ARG, "tensor %s has shape %lldx%lld, expected %lldx%lld", what, (long long)t.ne0,
+                       (long long)t.ne1, (long long)ne0, (long long)ne1);
+    return DFB_OK;
+}
+
+extern "C" int dfb_model_finalize(dfb_model *m) {
+    if (!m) return set_err(DFB_ERR_ARG, "null model");
+    if (m->finalized) return DFB_OK;
+    CK(cudaSetDevice(m->device));
+    const dfb_hparams &hp = m->hp;
+    const int d = hp.n_embd, ff = hp.n_ff, V = hp.n_vocab, hd = m->hd;
+    // embeddings: F16 kept, everything else dequantized to f32
+    {
+        const HostTensor &e = staged(m, DFB_TOK_EMBD, 0);
+        RET(check_mat(e, "token_embd", d, V));
+        const size_t n = (size_t)d * V;
+        if (e.type == G_F16) {
+            CK(cudaMalloc(&m->embd, n * 2));
+            CK(cudaMemcpy(m->embd, e.data, n * 2, cudaMemcpyHostToDevice));
+            m->embd_f16 = 1;
+            m->bytes += n * 2;
+        } else {
+            std::vector<float> v(n);
+            const int64_t rb = ggml_row_bytes(e.type, d);
+            for (int64_t r = 0; r < V; r++) dequant_row_host(e.type, e.data + r * rb, d, v.data() + (size_t)r * d);
+            CK(cudaMalloc(&m->embd, n * 4));
+            CK(cudaMemcpy(m->embd, v.data(), n * 4, cudaMemcpyHostToDevice));
+            m->embd_f16 = 0;
+            m->bytes += n * 4;
+        }
+        m->allocs.push_back(m->embd);
+    }
+    RET(upload_vec(m, staged(m, DFB_OUTPUT_NORM, 0), d, &m->output_norm));
+    // lm_head (tied to token_embd when output.weight is absent, diffuse-model.cpp:157-158)
+    {
+        HostTensor out = staged(m, DFB_OUTPUT, 0);
+        if (!out.data) out = staged(m, DFB_TOK_EMBD, 0);
+        RET(check_mat(out, "output", d, V));
+        const int64_t rb = ggml_row_bytes(out.type, d);
+        std::vector<const uint8_t *> rows((V + 127) / 128 * 128, nullptr);
+        for (int r = 0; r < V; r++) rows[r] = out.data + r * rb;
+        RET(build_wmat(rows, out.type, d, m->lm_head));
+        m->bytes += m->lm_head.bytes;
+    }
+    for (int l = 0; l < hp.n_layer; l++) {
+        LayerW &L = m->layers[l];
+        const HostTensor &wq = staged(m, DFB_WQ, l), &wk = staged(m, DFB_WK, l), &wv = staged(m, DFB_WV, l);
+        RET(check_mat(wq, "attn_q", d, m->n_q));
+        RET(check_mat(wk, "attn_k", d, m->n_kv));
+        RET(check_mat(wv, "attn_v", d, m->n_kv));
+        if (wq.type != wk.type || wq.type != wv.type)
+            return set_err(DFB_ERR_UNSUPPORTED, "layer %d: attn_q/k/v have different types (%d/%d/%d)", l, wq.type, wk.type, wv.type);
+        // fused QKV rows: [Q | K | V], each section padded to 128 rows; Q and K rows
+        // permuted inside each head so NEOX pairs (i, i+hd/2) sit in adjacent TMEM lanes
+        {
+            std::vector<const uint8_t *> rows(m->nq_pad + 2 * m->nk_pad, nullptr);
+            const int64_t rb = ggml_row_bytes(wq.type, d);
+            for (int r = 0; r < m->n_q; r++) {
+                const int head = r / hd, rr = r % hd, i = rr >> 1, b = rr & 1;
+                rows[r] = wq.data + (int64_t)(head * hd + i + b * (hd >> 1)) * rb;
+            }
+            for (int r = 0; r < m->n_kv; r++) {
+                const int head = r / hd, rr = r % hd, i = rr >> 1, b = rr & 1;
+                rows[m->nq_pad + r] = wk.data + (int64_t)(head * hd + i + b * (hd >> 1)) * rb;
+                rows[m->nq_pad + m->nk_pad + r] = wv.data + (int64_t)r * rb;
+            }
+            RET(build_wmat(rows, wq.type, d, L.qkv));
+        }
+        const HostTensor &bq = staged(m, DFB_BQ, l), &bk = staged(m, DFB_BK, l), &bv = staged(m, DFB_BV, l);
+        if (bq.data || bk.data || bv.data) {
+            std::vector<float> b(m->nq_pad + 2 * m->nk_pad, 0.f);
+            if (bq.data) dequant_row_host(bq.type, bq.data, m->n_q, b.data());
+            if (bk.data) dequant_row_host(bk.type, bk.data, m->n_kv, b.data() + m->nq_pad);
+            if (bv.data) dequant_row_host(bv.type, bv.data, m->n_kv, b.data() + m->nq_pad + m->nk_pad);
+            CK(cudaMalloc(&L.bias_qkv, b.size() * 4));
+            m->allocs.push_back(L.bias_qkv);
+            CK(cudaMemcpy(L.bias_qkv, b.data(), b.size() * 4, cudaMemcpyHostToDevice));
+        }
+        const HostTensor &wo = staged(m, DFB_WO, l);
+        RET(check_mat(wo, "attn_output", m->n_q, d));
+        {
+            std::vector<const uint8_t *> rows((d + 127) / 128 * 128, nullptr);
+            const int64_t rb = ggml_row_bytes(wo.type, m->n_q);
+            for (int r = 0; r < d; r++) rows[r] = wo.data + (int64_t)r * rb;
+            RET(build_wmat(rows, wo.type, m->n_q, L.o));
+        }
+        const HostTensor &wg = staged(m, DFB_GATE, l), &wu = staged(m, DFB_UP, l), &wd = staged(m, DFB_DOWN, l);
+        RET(check_mat(wg, "ffn_gate", d, ff));
+        RET(check_mat(wu, "ffn_up", d, ff));
+        RET(check_mat(wd, "ffn_down", ff, d));
+        if (wg.type != wu.type) return set_err(DFB_ERR_UNSUPPORTED, "layer %d: ffn_gate/up types differ", l);
+        {
+            std::vector<const uint8_t *> rows((2 * ff + 127) / 128 * 128, nullptr);
+            const int64_t rb = ggml_row_bytes(wg.type, d);
+            for (int i = 0; i < ff; i++) {
+                rows[2 * i] = wg.data + (int64_t)i * rb;
+                rows[2 * i + 1] = wu.data + (int64_t)i * rb;
+            }
+            RET(build_wmat(rows, wg.type, d, L.gateup));
+        }
+        {
+            std::vector<const uint8_t *> rows((d + 127) / 128 * 128, nullptr);
+            const int64_t rb = ggml_row_bytes(wd.type, ff);
+            for (int r = 0; r < d; r++) rows[r] = wd.data + (int64_t)r * rb;
+            RET(build_wmat(rows, wd.type, ff, L.down));
+        }
+        RET(upload_vec(m, staged(m, DFB_ATTN_NORM, l), d, &L.attn_norm));
+        RET(upload_vec(m, staged(m, DFB_FFN_NORM, l), d, &L.ffn_norm));
+        m->bytes += L.qkv.bytes + L.o.bytes + L.gateup.bytes + L.down.bytes;
+    }
+    m->staged.clear();
+    m->staged.shrink_to_fit();
+    m->finalized = true;
+    return DFB_OK;
+}
+
+extern "C" void dfb_model_free(dfb_model *m) {
+    if (!m) return;
+    cudaSetDevice(m->device);
+    for (void *p : m->allocs) cudaFree(p);
+    cudaFree(m->lm_head.d);
+    for (auto &L : m->layers) {
+        cudaFree(L.qkv.d); cudaFree(L.o.d); cudaFree(L.gateup.d); cudaFree(L.down.d);
+    }
+    delete m;
+}
+
+extern "C" int dfb_model_bytes(const dfb_model *m, size_t *bytes) {
+    if (!m || !bytes) return set_err(DFB_ERR_ARG, "null pointer");
+    *bytes = m->bytes;
+    return DFB_OK;
+}
+
+// ───────────────────────── context ─────────────────────────
+struct dfb_ctx {
+    dfb_model *m = nullptr;
+    cudaStream_t st = nullptr;
+    cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
+    int cap = 0;
+    // activations
+    float *x = nullptr, *logits = nullptr;
+    __half *h = nullptr, *att = nullptr, *q = nullptr, *ffh = nullptr, *kc = nullptr, *vc = nullptr;
+    float2 *rope = nullptr;
+    CUtensorMap tm_h{}, tm_att{}, tm_ffh{};
+    // sequence state
+    int32_t *seq = nullptr, *prev_seq = nullptr, *last_changed = nullptr, *cand_tok = nullptr, *commit_pos = nullptr,
+            *commit_tok = nullptr, *order = nullptr;
+    uint8_t *masked = nullptr;
+    int *active_pos = nullptr, *masked_pos = nullptr, *cnt = nullptr;
+    float *cand_conf = nullptr, *cand_ent = nullptr;
+    // GEMM scratch
+    float *ws = nullptr;
+    int *tile_cnt = nullptr, *err = nullptr;
+    int n_tile_cnt = 0;
+    // generation
+    bool gen_active = false;
+    int n_prompt = 0, n_gen = 0, total = 0, n_masked = 0;
+    dfb_sampler_params sp{};
+};
+
+static void ctx_free_buffers(dfb_ctx *c) {
+    void *ps[] = {c->x, c->logits, c->h, c->att, c->q, c->ffh, c->kc, c->vc, c->rope, c->seq, c->prev_seq,
+                  c->last_changed, c->cand_tok, c->commit_pos, c->commit_tok, c->order, c->masked, c->active_pos,
+                  c->masked_pos, c->cnt, c->cand_conf, c->cand_ent, c->ws, c->tile_cnt, c->err};
+    for (void *p : ps) cudaFree(p);
+    c->x = c->logits = nullptr; c->h = c->att = c->q = c->ffh = c->kc = c->vc = nullptr; c->rope = nullptr;
+    c->seq = c->prev_seq = c->last_changed = c->cand_tok = c->commit_pos = c->commit_tok = c->order = nullptr;
+    c->masked = nullptr; c->active_pos = c->masked_pos = c->cnt = nullptr; c->cand_conf = c->cand_ent = nullptr;
+    c->ws = nullptr; c->tile_cnt = c->err = nullptr;
+    c->cap = 0;
+}
+
+// RoPE angles exactly as the reference's GGML NEOX path computes them: theta starts
+// at the position and is multiplied by base^(-2/n_dims) once per pair, in float
+// (ggml_rope_cache_init, with the arguments of diffuse-graph.cpp:76-79).
+static void rope_table_host(int n_pos, int hd, float base, std::vector<float2> &out) {
+    out.resize((size_t)n_pos * (hd / 2));
+    const float theta_scale = powf(base, -2.0f / hd);
+    for (int p = 0; p < n_pos; p++) {
+        float theta = (float)p;
+        for (int i = 0; i < hd / 2; i++) {
+            out[(size_t)p * (hd / 2) + i] = make_float2(cosf(theta), sinf(theta));
+            theta *= theta_scale;
+        }
+    }
+}
+
+static int ctx_reserve(dfb_ctx *c, int n) {
+    if (n <= c->cap) return DFB_OK;
+    const dfb_model *m = c->m;
+    const dfb_hparams &hp = m->hp;
+    const int cap = std::max(n, 64);
+    ctx_free_buffers(c);
+    const size_t d = hp.n_embd, ff = hp.n_ff, V = hp.n_vocab, L = hp.n_layer, kvd = m->n_kv, hd = m->hd;
+#define AL(ptr, count) CK(cudaMalloc(&(ptr), sizeof(*(ptr)) * (size_t)(count)))
+    AL(c->x, cap * d); AL(c->h, cap * d); AL(c->att, cap * d); AL(c->q, cap * d); AL(c->ffh, cap * ff);
+    AL(c->kc, L * cap * kvd); AL(c->vc, L * cap * kvd); AL(c->logits, (size_t)cap * V); AL(c->rope, cap * hd / 2);
+    AL(c->seq, cap); AL(c->prev_seq, cap); AL(c->last_changed, cap); AL(c->cand_tok, cap); AL(c->commit_pos, cap);
+    AL(c->commit_tok, cap); AL(c->order, cap); AL(c->masked, cap); AL(c->active_pos, cap); AL(c->masked_pos, cap);
+    AL(c->cnt, CNT_N); AL(c->cand_conf, cap); AL(c->cand_ent, cap);
+    AL(c->ws, (size_t)m->n_sm * 2 * kWsTile); AL(c->err, 1);
+    const int n_mg_max = (cap + kMaxTok - 1) / kMaxTok;
+    int max_tiles = m->lm_head.n_tiles;
+    for (auto &Lw : m->layers) max_tiles = std::max({max_tiles, Lw.qkv.n_tiles, Lw.gateup.n_tiles, Lw.o.n_tiles, Lw.down.n_tiles});
+    c->n_tile_cnt = max_tiles * n_mg_max;
+    AL(c->tile_cnt, c->n_tile_cnt);
+#undef AL
+    CK(cudaMemset(c->tile_cnt, 0, sizeof(int) * c->n_tile_cnt));
+    CK(cudaMemset(c->err, 0, sizeof(int)));
+    CK(cudaMemset(c->cnt, 0, sizeof(int) * CNT_N));
+    CK(cudaMemset(c->x, 0, sizeof(float) * cap * d));
+    CK(cudaMemset(c->h, 0, 2 * cap * d));
+    CK(cudaMemset(c->att, 0, 2 * cap * d));
+    CK(cudaMemset(c->ffh, 0, 2 * cap * ff));
+    CK(cudaMemset(c->kc, 0, 2 * L * cap * kvd));
+    CK(cudaMemset(c->vc, 0, 2 * L * cap * kvd));
+    std::vector<float2> rope;
+    rope_table_host(cap, (int)hd, hp.rope_theta, rope);
+    CK(cudaMemcpy(c->rope, rope.data(), rope.size() * sizeof(float2), cudaMemcpyHostToDevice));
+    RET(make_tmap(&c->tm_h, c->h, d, cap, 64));
+    RET(make_tmap(&c->tm_att, c->att, d, cap, 64));
+    RET(make_tmap(&c->tm_ffh, c->ffh, ff, cap, 64));
+    c->cap = cap;
+    return DFB_OK;
+}
+
+template <int WT, int EPI>
+static int launch_gemm_t(dfb_ctx *c, const WMat &w, const CUtensorMap &tm_x, const EpiArgs &epi) {
+    auto kern = dq_gemm_kernel<WT, EPI>;
+    constexpr int smem = gemm_smem_bytes(WT);
+    static bool attr_set[64] = {false};
+    const int dev = c->m->device;
+    if (!attr_set[dev]) {
+        CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        attr_set[dev] = true;
+    }
+    GemmParams p;
+    p.w = w.d;
+    p.n_tiles = w.n_tiles;
+    p.kb = w.kb;
+    p.m_dev = c->cnt + CNT_M;
+    p.ws = c->ws;
+    p.tile_cnt = c->tile_cnt;
+    p.err = c->err;
+    p.epi = epi;
+    kern<<<c->m->n_sm, kThreads, smem, c->st>>>(tm_x, WT == W_F16 ? w.tm : tm_x, p);
+    CK(cudaGetLastError());
+    return DFB_OK;
+}
+
+template <int EPI>
+static int launch_gemm(dfb_ctx *c, const WMat &w, const CUtensorMap &tm_x, const EpiArgs &epi) {
+    switch (w.wt) {
+        case W_Q4K: return launch_gemm_t<W_Q4K, EPI>(c, w, tm_x, epi);
+        case W_Q6K: return launch_gemm_t<W_Q6K, EPI>(c, w, tm_x, epi);
+        case W_Q80: return launch_gemm_t<W_Q80, EPI>(c, w, tm_x, epi);
+        case W_F16: return launch_gemm_t<W_F16, EPI>(c, w, tm_x, epi);
+    }
+    return set_err(DFB_ERR_STATE, "weight not uploaded");
+}
+
+template <int HD>
+static int launch_attn_t(dfb_ctx *c, const __half *kc, const __half *vc, int n_keys) {
+    const dfb_model *m = c->m;
+    constexpr int smem = attn_smem_bytes<HD>();
+    static bool attr_set[64] = {false};
+    if (!attr_set[m->device]) {
+        CK(cudaFuncSetAttribute(attn_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        attr_set[m->device] = true;
+    }
+    const float scale_log2 = (1.0f / sqrtf((float)HD)) * 1.4426950408889634f;
+    dim3 grid((c->cap + kAttnRows - 1) / kAttnRows, m->hp.n_head);
+    attn_kernel<HD><<<grid, 128, smem, c->st>>>(c->q, m->n_q, kc, vc, m->n_kv, c->att, m->n_q, c->cnt + CNT_M, n_keys,
+                                                m->hp.n_head / m->hp.n_head_kv, scale_log2);
+    CK(cudaGetLastError());
+    return DFB_OK;
+}
+
+// The forward of one step over the active rows listed by step_prepare.
+static int run_forward(dfb_ctx *c, int n_total) {
+    const dfb_model *m = c->m;
+    const dfb_hparams &hp = m->hp;
+    const int d = hp.n_embd, cap = c->cap;
+    if (m->embd_f16)
+        embed_kernel<__half><<<cap, 256, 0, c->st>>>((const __half *)m->embd, d, c->seq, c->active_pos, c->cnt, c->x);
+    else
+        embed_kernel<float><<<cap, 256, 0, c->st>>>((const float *)m->embd, d, c->seq, c->active_pos, c->cnt, c->x);
+    CK(cudaGetLastError());
+    for (int l = 0; l < hp.n_layer; l++) {
+        const LayerW &L = m->layers[l];
+        __half *kc = c->kc + (size_t)l * cap * m->n_kv, *vc = c->vc + (size_t)l * cap * m->n_kv;
+        rmsnorm_kernel<<<cap, 256, 0, c->st>>>(c->x, L.attn_norm, d, hp.rms_norm_eps, c->cnt, c->h);
+        EpiArgs e;
+        e.q_out = c->q; e.ld_q = m->n_q;
+        e.k_cache = kc; e.v_cache = vc; e.ld_kv = m->n_kv;
+        e.n_q_tiles = m->nq_pad / 128; e.n_k_tiles = m->nk_pad / 128;
+        e.n_q = m->n_q; e.n_kv = m->n_kv; e.head_dim = m->hd;
+        e.bias = L.bias_qkv; e.rope = c->rope; e.pos = c->active_pos;
+        RET(launch_gemm<EPI_QKV>(c, L.qkv, c->tm_h, e));
+        switch (m->hd) {
+            case 16: RET(launch_attn_t<16>(c, kc, vc, n_total)); break;
+            case 32: RET(launch_attn_t<32>(c, kc, vc, n_total)); break;
+            case 64: RET(launch_attn_t<64>(c, kc, vc, n_total)); break;
+            default: RET(launch_attn_t<128>(c, kc, vc, n_total)); break;
+        }
+        EpiArgs eo;
+        eo.out = c->x; eo.ld = d; eo.n_valid = d;
+        RET(launch_gemm<EPI_RESID>(c, L.o, c->tm_att, eo));
+        rmsnorm_kernel<<<cap, 256, 0, c->st>>>(c->x, L.ffn_norm, d, hp.rms_norm_eps, c->cnt, c->h);
+        EpiArgs eg;
+        eg.out = c->ffh; eg.ld = hp.n_ff; eg.n_valid = 2 * hp.n_ff;
+        RET(launch_gemm<EPI_SWIGLU>(c, L.gateup, c->tm_h, eg));
+        EpiArgs ed;
+        ed.out = c->x; ed.ld = d; ed.n_valid = d;
+        RET(launch_gemm<EPI_RESID>(c, L.down, c->tm_ffh, ed));
+    }
+    rmsnorm_kernel<<<cap, 256, 0, c->st>>>(c->x, m->output_norm, d, hp.rms_norm_eps, c->cnt, c->h);
+    EpiArgs el;
+    el.out = c->logits; el.ld = hp.n_vocab; el.n_valid = hp.n_vocab; el.pos = c->active_pos;
+    RET(launch_gemm<EPI_LOGITS>(c, m->lm_head, c->tm_h, el));
+    CK(cudaGetLastError());
+    return DFB_OK;
+}
+
+static int check_err(dfb_ctx *c) {
+    int e = 0;
+    CK(cudaMemcpy(&e, c->err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (e) {
+        cudaMemset(c->err, 0, sizeof(int));
+        return set_err(DFB_ERR_TIMEOUT, "a GEMM gave up a bounded wait (code 0x%x); results of this call are invalid", e);
+    }
+    return DFB_OK;
+}
+
+extern "C" int dfb_ctx_create(dfb_model *m, int n_ctx, dfb_ctx **out) {
+    if (!m || !out) return set_err(DFB_ERR_ARG, "null pointer");
+    if (!m->finalized) return set_err(DFB_ERR_STATE, "model not finalized");
+    *out = nullptr;
+    CK(cudaSetDevice(m->device));
+    auto *c = new dfb_ctx();
+    c->m = m;
+    if (cudaStreamCreateWithFlags(&c->st, cudaStreamNonBlocking) != cudaSuccess) {
+        delete c;
+        return set_err(DFB_ERR_CUDA, "cudaStreamCreate failed");
+    }
+    for (auto &e : c->ev) cudaEventCreate(&e);
+    if (n_ctx > 0) {
+        const int r = ctx_reserve(c, n_ctx);
+        if (r != DFB_OK) { dfb_ctx_free(c); return r; }
+    }
+    *out = c;
+    return DFB_OK;
+}
+
+extern "C" void dfb_ctx_free(dfb_ctx *c) {
+    if (!c) return;
+    cudaSetDevice(c->m->device);
+    if (c->st) cudaStreamSynchronize(c->st);
+    ctx_free_buffers(c);
+    for (auto &e : c->ev) if (e) cudaEventDestroy(e);
+    if (c->st) cudaStreamDestroy(c->st);
+    delete c;
+}
+
+extern "C" int dfb_ctx_stream(dfb_ctx *c, void **stream) {
+    if (!c || !stream) return set_err(DFB_ERR_ARG, "null pointer");
+    *stream = c->st;
+    return DFB_OK;
+}
+
+extern "C" int dfb_forward(dfb_ctx *c, const int32_t *tokens, int n, float *logits_host) {
+    if (!c || !tokens || !logits_host || n <= 0) return set_err(DFB_ERR_ARG, "bad arguments");
+    CK(cudaSetDevice(c->m->device));
+    const int V = c->m->hp.n_vocab;
+    for (int i = 0; i < n; i++)
+        if (tokens[i] < 0 || tokens[i] >= V) return set_err(DFB_ERR_ARG, "token %d at %d outside [0, %d)", tokens[i], i, V);
+    RET(ctx_reserve(c, n));
+    c->gen_active = false;
+    CK(cudaMemcpyAsync(c->seq, tokens, n * sizeof(int32_t), cudaMemcpyHostToDevice, c->st));
+    CK(cudaMemsetAsync(c->masked, 0, n, c->st));
+    step_prepare_kernel<<<1, 1024, 0, c->st>>>(1, 0, 0, n, c->seq, c->prev_seq, c->last_changed, c->masked,
+                                               c->active_pos, c->masked_pos, c->cnt);
+    CK(cudaGetLastError());
+    RET(run_forward(c, n));
+    CK(cudaMemcpyAsync(logits_host, c->logits, (size_t)n * V * sizeof(float), cudaMemcpyDeviceToHost, c->st));
+    CK(cudaStreamSynchronize(c->st));
+    return check_err(c);
+}
+
+extern "C" int dfb_linear(dfb_ctx *c, int role, int layer, const float *x_host, int M, float *y_host) {
+    if (!c || !x_host || !y_host || M <= 0) return set_err(DFB_ERR_ARG, "bad arguments");
+    const dfb_model *m = c->m;
+    CK(cudaSetDevice(m->device));
+    const WMat *w = nullptr;
+    int K = 0, n_out = 0;
+    const int d = m->hp.n_embd, ff = m->hp.n_ff;
+    if (role == DFB_OUTPUT) { w = &m->lm_head; K = d; n_out = m->hp.n_vocab; }
+    else {
+        if (layer < 0 || layer >= m->hp.n_layer) return set_err(DFB_ERR_ARG, "bad layer");
+        const LayerW &L = m->layers[layer];
+        switch (role) {
+            case DFB_WQ: w = &L.qkv; K = d; n_out = m->n_q; break;
+            case DFB_WK: w = &L.qkv; K = d; n_out = m->n_kv; break;
+            case DFB_WV: w = &L.qkv; K = d; n_out = m->n_kv; break;
+            case DFB_WO: w = &L.o; K = m->n_q; n_out = d; break;
+            case DFB_GATE: case DFB_UP: w = &L.gateup; K = d; n_out = ff; break;
+            case DFB_DOWN: w = &L.down; K = ff; n_out = d; break;
+            default: return set_err(DFB_ERR_ARG, "role %d is not a linear weight", role);
+        }
+    }
+    RET(ctx_reserve(c, M));
+    __half *xh = nullptr;
+    float *xf = nullptr, *y = nullptr;
+    CK(cudaMalloc(&xh, (size_t)M * K * 2));
+    CK(cudaMalloc(&xf, (size_t)M * K * 4));
+    CK(cudaMalloc(&y, (size_t)M * w->n_rows * 4));
+    int rc = DFB_OK;
+    CUtensorMap tm;
+    do {
+        if ((rc = make_tmap(&tm, xh, K, M, 64)) != DFB_OK) break;
+        if (cudaMemcpyAsync(xf, x_host, (size_t)M * K * 4, cudaMemcpyHostToDevice, c->st) != cudaSuccess) { rc = set_err(DFB_ERR_CUDA, "H2D failed"); break; }
+        f32_to_f16_kernel<<<256, 256, 0, c->st>>>(xf, xh, (size_t)M * K);
+        if (cudaMemcpyAsync(c->cnt + CNT_M, &M, sizeof(int), cudaMemcpyHostToDevice, c->st) != cudaSuccess) { rc = set_err(DFB_ERR_CUDA, "H2D failed"); break; }
+        EpiArgs e;
+        e.out = y; e.ld = w->n_rows; e.n_valid = w->n_rows;
+        if ((rc = launch_gemm<EPI_F32>(c, *w, tm, e)) != DFB_OK) break;
+        std::vector<float> full((size_t)M * w->n_rows);
+        if (cudaMemcpyAsync(full.data(), y, full.size() * 4, cudaMemcpyDeviceToHost, c->st) != cudaSuccess ||
+            cudaStreamSynchronize(c->st) != cudaSuccess) { rc = set_err(DFB_ERR_CUDA, "GEMM failed: %s", cudaGetErrorString(cudaGetLastError())); break; }
+        if ((rc = check_err(c)) != DFB_OK) break;
+        // undo the fused-row layout
+        const int hd = m->hd;
+        for (int t = 0; t < M; t++)
+            for (int f = 0; f < n_out; f++) {
+                int r;
+                switch (role) {
+                    case DFB_WQ: case DFB_WK: {
+                        const int head = f / hd, rr = f % hd, i = rr < hd / 2 ? rr : rr - hd / 2, b = rr < hd / 2 ? 0 : 1;
+                        r = (role == DFB_WK ? m->nq_pad : 0) + head * hd + 2 * i + b;
+                    } break;
+                    case DFB_WV: r = m->nq_pad + m->nk_pad + f; break;
+                    case DFB_GATE: r = 2 * f; break;
+                    case DFB_UP: r = 2 * f + 1; break;
+                    default: r = f;
+                }
+                y_host[(size_t)t * n_out + f] = full[(size_t)t * w->n_rows + r];
+            }
+    } while (0);
+    cudaFree(xh); cudaFree(xf); cudaFree(y);
+    return rc;
+}
+
+extern "C" int dfb_gen_begin(dfb_ctx *c, const int32_t *prompt, int n_prompt, int n_gen, const dfb_sampler_params *p) {
+    if (!c || !p || n_prompt < 0 || n_gen <= 0 || (n_prompt > 0 && !prompt)) return set_err(DFB_ERR_ARG, "bad arguments");
+    if (p->temperature > 0.0f)
+        return set_err(DFB_ERR_UNSUPPORTED, "temperature > 0 sampling is not implemented on the device path");
+    if (p->remasking < 0 || p->remasking > 4) return set_err(DFB_ERR_ARG, "bad remasking %d", p->remasking);
+    const dfb_model *m = c->m;
+    CK(cudaSetDevice(m->device));
+    const int total = n_prompt + n_gen;
+    for (int i = 0; i < n_prompt; i++)
+        if (prompt[i] < 0 || prompt[i] >= m->hp.n_vocab) return set_err(DFB_ERR_ARG, "prompt token %d out of range", prompt[i]);
+    if (n_gen > 65536) return set_err(DFB_ERR_ARG, "n_generate %d too large", n_gen);
+    RET(ctx_reserve(c, total));
+    std::vector<int32_t> seq(total, m->hp.mask_token_id), neg(total, -1);
+    std::copy(prompt, prompt + n_prompt, seq.begin());
+    std::vector<uint8_t> msk(total, 0);
+    std::fill(msk.begin() + n_prompt, msk.end(), 1);
+    CK(cudaMemcpyAsync(c->seq, seq.data(), total * 4, cudaMemcpyHostToDevice, c->st));
+    CK(cudaMemcpyAsync(c->prev_seq, neg.data(), total * 4, cudaMemcpyHostToDevice, c->st));
+    CK(cudaMemcpyAsync(c->last_changed, neg.data(), total * 4, cudaMemcpyHostToDevice, c->st));
+    CK(cudaMemcpyAsync(c->masked, msk.data(), total, cudaMemcpyHostToDevice, c->st));
+    CK(cudaStreamSynchronize(c->st));
+    c->n_prompt = n_prompt;
+    c->n_gen = n_gen;
+    c->total = total;
+    c->n_masked = n_gen;
+    c->sp = *p;
+    c->gen_active = true;
+    return DFB_OK;
+}
+
+extern "C" int dfb_gen_step(dfb_ctx *c, int step, int n_unmask_sched, int force_full, const int32_t *order,
+                            dfb_step_stats *stats) {
+    if (!c) return set_err(DFB_ERR_ARG, "null context");
+    if (!c->gen_active) return set_err(DFB_ERR_STATE, "dfb_gen_begin not called");
+    const dfb_model *m = c->m;
+    CK(cudaSetDevice(m->device));
+    if (c->sp.remasking == 1) {
+        if (!order) return set_err(DFB_ERR_ARG, "RANDOM remasking needs the host shuffle order");
+        CK(cudaMemcpyAsync(c->order, order, sizeof(int32_t) * c->n_masked, cudaMemcpyHostToDevice, c->st));
+    }
+    CK(cudaEventRecord(c->ev[0], c->st));
+    step_prepare_kernel<<<1, 1024, 0, c->st>>>(force_full ? 1 : 0, step, c->sp.cache_keep_active, c->total, c->seq,
+                                               c->prev_seq, c->last_changed, c->masked, c->active_pos, c->masked_pos,
+                                               c->cnt);
+    CK(cudaGetLastError());
+    RET(run_forward(c, c->total));
+    CK(cudaEventRecord(c->ev[1], c->st));
+    const int margin = c->sp.remasking == 4 ? 1 : 0;
+    row_stats_kernel<<<c->n_gen, 512, 0, c->st>>>(c->logits, m->hp.n_vocab, m->hp.shift_logits, c->masked_pos, c->cnt,
+                                                  margin, c->cand_tok, c->cand_conf, c->cand_ent);
+    CK(cudaGetLastError());
+    int np = 1;
+    while (np < c->n_masked) np <<= 1;
+    const size_t sel_smem = sizeof(unsigned long long) * (size_t)np;
+    if (sel_smem > 48 * 1024) CK(cudaFuncSetAttribute(select_commit_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sel_smem));
+    select_commit_kernel<<<1, 1024, sel_smem, c->st>>>(c->sp.remasking, n_unmask_sched, c->sp.entropy_threshold,
+                                                       c->order, c->masked_pos, c->cand_tok, c->cand_conf, c->cand_ent,
+                                                       c->seq, c->masked, c->commit_pos, c->commit_tok, c->cnt);
+    CK(cudaGetLastError());
+    CK(cudaEventRecord(c->ev[2], c->st));
+    int h_cnt[CNT_N];
+    CK(cudaMemcpyAsync(h_cnt, c->cnt, sizeof(h_cnt), cudaMemcpyDeviceToHost, c->st));
+    CK(cudaStreamSynchronize(c->st));
+    RET(check_err(c));
+    c->n_masked = h_cnt[CNT_NMASKED];
+    if (stats) {
+        stats->n_active = h_cnt[CNT_M];
+        stats->n_unmasked = h_cnt[CNT_COMMITTED];
+        stats->n_masked = h_cnt[CNT_NMASKED];
+        stats->used_cache = h_cnt[CNT_USED_CACHE];
+        float a = 0, b = 0;
+        cudaEventElapsedTime(&a, c->ev[0], c->ev[1]);
+        cudaEventElapsedTime(&b, c->ev[0], c->ev[2]);
+        stats->fwd_ms = a;
+        stats->step_ms = b;
+    }
+    return DFB_OK;
+}
+
+extern "C" int dfb_gen_tokens(dfb_ctx *c, int32_t *seq_host, int cap) {
+    if (!c || !seq_host) return set_err(DFB_ERR_ARG, "null pointer");
+    if (!c->gen_active) return set_err(DFB_ERR_STATE, "no generation");
+    if (cap < c->total) return set_err(DFB_ERR_ARG, "buffer of %d < %d positions", cap, c->total);
+    CK(cudaMemcpyAsync(seq_host, c->seq, c->total * 4, cudaMemcpyDeviceToHost, c->st));
+    CK(cudaStreamSynchronize(c->st));
+    return DFB_OK;
+}
+
+extern "C" int dfb_gen_commits(dfb_ctx *c, int32_t *pos_host, int32_t *tok_host, int cap) {
+    if (!c || !pos_host || !tok_host) return set_err(DFB_ERR_ARG, "null pointer");
+    int h_cnt[CNT_N];
+    CK(cudaMemcpyAsync(h_cnt, c->cnt, sizeof(h_cnt), cudaMemcpyDeviceToHost, c->st));
+    CK(cudaStreamSynchronize(c->st));
+    const int n = std::min(h_cnt[CNT_COMMITTED], cap);
+    CK(cudaMemcpyAsync(pos_host, c->commit_pos, n * 4, cudaMemcpyDeviceToHost, c->st));
+    CK(cudaMemcpyAsync(tok_host, c->commit_tok, n * 4, cudaMemcpyDeviceToHost, c->st));
+    CK(cudaStreamSynchronize(c->st));
+    return n;
+}
+
+extern "C" int dfb_gen_logits(dfb_ctx *c, int row0, int nrows, float *host) {
+    if (!c || !host || row0 < 0 || nrows <= 0 || row0 + nrows > c->cap) return set_err(DFB_ERR_ARG, "bad arguments");
+    const size_t V = c->m->hp.n_vocab;
+    CK(cudaMemcpyAsync(host, c->logits + (size_t)row0 * V, (size_t)nrows * V * 4, cudaMemcpyDeviceToHost, c->st));
+    CK(cudaStreamSynchronize(c->st));
+    return DFB_OK;
+}

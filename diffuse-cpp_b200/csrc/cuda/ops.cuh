@@ -1,0 +1,299 @@
+// Memory-bound kernels of one denoising step: active-set build, embedding gather,
+// RMSNorm, and the remasking sampler (row statistics + ordering/commit).
+#pragma once
+#include <cuda_fp16.h>
+#include <cstdint>
+
+namespace dfb {
+
+// Device counters of a context.
+enum { CNT_M = 0, CNT_NMASKED = 1, CNT_COMMITTED = 2, CNT_USED_CACHE = 3, CNT_ERR = 4, CNT_N = 8 };
+
+// Block-wide exclusive scan of 0/1 flags for a 1024-thread block.  Returns this
+// thread's offset; *total receives the block count.
+__device__ __forceinline__ int block_scan_flag(bool flag, int *warp_tot, int *total) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const unsigned b = __ballot_sync(0xffffffffu, flag);
+    const int in_warp = __popc(b & ((1u << lane) - 1));
+    if (lane == 0) warp_tot[warp] = __popc(b);
+    __syncthreads();
+    if (warp == 0) {
+        const int v = warp_tot[lane];
+        int x = v;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
+        }
+        warp_tot[lane] = x - v;
+        if (lane == 31) *total = x;
+    }
+    __syncthreads();
+    const int off = warp_tot[warp] + in_warp;
+    __syncthreads();
+    return off;
+}
+
+// Active set of one step (diffuse-cache.h:78-115 and diffuse-sampler.cpp:143-182).
+// full != 0: every position is active (step 0, cache off, refresh), last_changed is
+// not touched (the reference does not call compute_active_set there).  Otherwise
+// active = changed since the last forward ∪ masked ∪ changed within keep_active steps;
+// an empty or complete active set falls back to the full forward like
+// diffuse-sampler.cpp:165-173.  Also lists the masked positions (ascending) and
+// records prev_seq = seq (update_seq, cache.h:142-145).  One block of 1024 threads.
+__global__ void __launch_bounds__(1024) step_prepare_kernel(int full, int step, int keep_active, int n_total,
+                                                            int32_t *seq, int32_t *prev_seq, int32_t *last_changed,
+                                                            const uint8_t *masked, int *active_pos, int *masked_pos,
+                                                            int *cnt) {
+    __shared__ int warp_tot[32];
+    __shared__ int tot;
+    int base_a = 0, base_m = 0;
+    for (int c0 = 0; c0 < n_total; c0 += 1024) {
+        const int i = c0 + threadIdx.x;
+        bool act = false, msk = false;
+        if (i < n_total) {
+            msk = masked[i] != 0;
+            if (full) act = true;
+            else {
+                const bool changed = seq[i] != prev_seq[i];
+                if (changed) last_changed[i] = step;
+                const int lc = last_changed[i];
+                const bool recent = keep_active > 0 && lc >= 0 && (step - lc) <= keep_active;
+                act = changed || msk || recent;
+            }
+        }
+        const int oa = block_scan_flag(act, warp_tot, &tot);
+        if (act) active_pos[base_a + oa] = i;
+        base_a += tot;
+        __syncthreads();
+        const int om = block_scan_flag(msk, warp_tot, &tot);
+        if (msk) masked_pos[base_m + om] = i;
+        base_m += tot;
+        __syncthreads();
+    }
+    const bool all = full || base_a == 0 || base_a >= n_total;
+    for (int i = threadIdx.x; i < n_total; i += 1024) {
+        if (all) active_pos[i] = i;
+        prev_seq[i] = seq[i];
+    }
+    if (threadIdx.x == 0) {
+        cnt[CNT_M] = all ? n_total : base_a;
+        cnt[CNT_NMASKED] = base_m;
+        cnt[CNT_USED_CACHE] = all ? 0 : 1;
+    }
+}
+
+// x[a] = token_embd[seq[active_pos[a]]] as f32 (ggml_get_rows, graph.cpp:43/433).
+template <typename T>
+__global__ void embed_kernel(const T *__restrict__ emb, int d, const int32_t *__restrict__ seq,
+                             const int *__restrict__ active_pos, const int *__restrict__ cnt, float *__restrict__ x) {
+    const int a = blockIdx.x;
+    if (a >= cnt[CNT_M]) return;
+    const int tok = seq[active_pos[a]];
+    const T *src = emb + (size_t)tok * d;
+    float *dst = x + (size_t)a * d;
+    for (int i = threadIdx.x; i < d; i += blockDim.x) {
+        if constexpr (sizeof(T) == 2) dst[i] = __half2float(src[i]);
+        else dst[i] = src[i];
+    }
+}
+
+__device__ __forceinline__ float block_sum(float v, float *red) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+        float w = lane < nw ? red[lane] : 0.f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) w += __shfl_xor_sync(0xffffffffu, w, o);
+        if (lane == 0) red[32] = w;
+    }
+    __syncthreads();
+    const float r = red[32];
+    __syncthreads();
+    return r;
+}
+
+// h[a] = f16(x[a] * rsqrt(mean(x[a]^2) + eps) * w)  (ggml_rms_norm + ggml_mul, graph.cpp:51-58).
+__global__ void __launch_bounds__(256) rmsnorm_kernel(const float *__restrict__ x, const float *__restrict__ w, int d,
+                                                      float eps, const int *__restrict__ cnt, __half *__restrict__ h) {
+    __shared__ float red[33];
+    const int a = blockIdx.x;
+    if (a >= cnt[CNT_M]) return;
+    const float *xr = x + (size_t)a * d;
+    float ss = 0.f;
+    if ((d & 3) == 0) {
+        for (int i = threadIdx.x * 4; i < d; i += blockDim.x * 4) {
+            const float4 v = *reinterpret_cast<const float4 *>(xr + i);
+            ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+        }
+    } else {
+        for (int i = threadIdx.x; i < d; i += blockDim.x) ss += xr[i] * xr[i];
+    }
+    ss = block_sum(ss, red);
+    const float scale = 1.0f / sqrtf(ss / (float)d + eps);
+    __half *hr = h + (size_t)a * d;
+    for (int i = threadIdx.x; i < d; i += blockDim.x) hr[i] = __float2half_rn((xr[i] * scale) * w[i]);
+}
+
+// Per-candidate statistics of one logits row (diffuse-sampler.cpp:34-57 and :239-255):
+// top-1 value and first index (strict '>' keeps the lowest index), top-2 value (the
+// largest value at any other index), entropy with the p > 1e-10 rule.  One block per
+// masked position; Dream reads row max(i-1, 0).
+struct Top2 {
+    float best;
+    int idx;
+    float second;
+};
+__device__ __forceinline__ Top2 top2_merge(Top2 a, Top2 b) {
+    Top2 r;
+    const bool a_first = a.best > b.best || (a.best == b.best && a.idx < b.idx);
+    if (a_first) { r.best = a.best; r.idx = a.idx; r.second = fmaxf(a.second, b.best); }
+    else { r.best = b.best; r.idx = b.idx; r.second = fmaxf(b.second, a.best); }
+    return r;
+}
+
+__global__ void __launch_bounds__(512) row_stats_kernel(const float *__restrict__ logits, int n_vocab, int shift,
+                                                         const int *__restrict__ masked_pos, const int *__restrict__ cnt,
+                                                         int margin, int32_t *__restrict__ cand_tok,
+                                                         float *__restrict__ cand_conf, float *__restrict__ cand_ent) {
+    __shared__ float red[33];
+    __shared__ Top2 tred[16];
+    const int b = blockIdx.x;
+    if (b >= cnt[CNT_NMASKED]) return;
+    const int i = masked_pos[b];
+    const int row = shift ? (i > 0 ? i - 1 : 0) : i;
+    const float *z = logits + (size_t)row * n_vocab;
+    Top2 t{-INFINITY, 0x7fffffff, -1e30f};
+    for (int v = threadIdx.x; v < n_vocab; v += blockDim.x) {
+        const float x = z[v];
+        if (x > t.best) { t.second = fmaxf(t.second, t.best); t.best = x; t.idx = v; }
+        else t.second = fmaxf(t.second, x);
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        Top2 u;
+        u.best = __shfl_xor_sync(0xffffffffu, t.best, o);
+        u.idx = __shfl_xor_sync(0xffffffffu, t.idx, o);
+        u.second = __shfl_xor_sync(0xffffffffu, t.second, o);
+        t = top2_merge(t, u);
+    }
+    if (lane == 0) tred[warp] = t;
+    __syncthreads();
+    if (warp == 0) {
+        t = lane < (int)(blockDim.x >> 5) ? tred[lane] : Top2{-INFINITY, 0x7fffffff, -1e30f};
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            Top2 u;
+            u.best = __shfl_xor_sync(0xffffffffu, t.best, o);
+            u.idx = __shfl_xor_sync(0xffffffffu, t.idx, o);
+            u.second = __shfl_xor_sync(0xffffffffu, t.second, o);
+            t = top2_merge(t, u);
+        }
+        if (lane == 0) tred[0] = t;
+    }
+    __syncthreads();
+    t = tred[0];
+    const float mx = t.best;
+    float se = 0.f;
+    for (int v = threadIdx.x; v < n_vocab; v += blockDim.x) se += expf(z[v] - mx);
+    se = block_sum(se, red);
+    const float log_sum = logf(se);
+    float ent = 0.f;
+    for (int v = threadIdx.x; v < n_vocab; v += blockDim.x) {
+        const float lp = (z[v] - mx) - log_sum;
+        const float p = expf(lp);
+        if (p > 1e-10f) ent -= p * lp;
+    }
+    ent = block_sum(ent, red);
+    if (threadIdx.x == 0) {
+        cand_tok[b] = t.idx;
+        cand_conf[b] = margin ? (t.best - t.second) : t.best;
+        cand_ent[b] = ent;
+    }
+}
+
+__device__ __forceinline__ uint32_t ordered_u32(float f) {
+    const uint32_t u = __float_as_uint(f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// Ordering + commit (diffuse-sampler.cpp:277-323).  Candidates are in ascending
+// position order; keys: confidence descending (LOW_CONFIDENCE / MASKGIT_PLUS /
+// TOPK_MARGIN) or entropy ascending (ENTROPY_EXIT), ties by ascending position;
+// RANDOM uses the host's shuffle.  One block of 1024 threads; dynamic shared memory
+// holds the padded key array (8 bytes per candidate, power of two).
+__global__ void __launch_bounds__(1024) select_commit_kernel(int remasking, int n_unmask_sched, float tau,
+                                                             const int32_t *__restrict__ order,
+                                                             const int *__restrict__ masked_pos,
+                                                             const int32_t *__restrict__ cand_tok,
+                                                             const float *__restrict__ cand_conf,
+                                                             const float *__restrict__ cand_ent, int32_t *seq,
+                                                             uint8_t *masked, int32_t *commit_pos,
+                                                             int32_t *commit_tok, int *cnt) {
+    extern __shared__ unsigned long long keys[];
+    __shared__ int n_easy_s;
+    const int n = cnt[CNT_NMASKED];
+    int np = 1;
+    while (np < n) np <<= 1;
+    if (threadIdx.x == 0) n_easy_s = 0;
+    __syncthreads();
+    int easy = 0;
+    for (int b = threadIdx.x; b < np; b += blockDim.x) {
+        unsigned long long k = ~0ull;
+        if (b < n) {
+            uint32_t k32;
+            if (remasking == 2) {
+                k32 = ordered_u32(cand_ent[b]);
+                easy += cand_ent[b] < tau ? 1 : 0;
+            } else {
+                k32 = ~ordered_u32(cand_conf[b]);
+            }
+            k = ((unsigned long long)k32 << 32) | (uint32_t)b;
+        }
+        keys[b] = k;
+    }
+    if (remasking == 2 && easy) atomicAdd(&n_easy_s, easy);
+    __syncthreads();
+    if (remasking != 1) {
+        for (int size = 2; size <= np; size <<= 1)
+            for (int stride = size >> 1; stride > 0; stride >>= 1) {
+                for (int i = threadIdx.x; i < np; i += blockDim.x) {
+                    const int j = i ^ stride;
+                    if (j > i) {
+                        const bool up = (i & size) == 0;
+                        const unsigned long long a = keys[i], c = keys[j];
+                        if ((a > c) == up) { keys[i] = c; keys[j] = a; }
+                    }
+                }
+                __syncthreads();
+            }
+    }
+    int n_unmask = n_unmask_sched;
+    if (remasking == 2) n_unmask = max(n_unmask, n_easy_s);
+    n_unmask = min(n_unmask, n);
+    for (int j = threadIdx.x; j < n_unmask; j += blockDim.x) {
+        const int b = remasking == 1 ? order[j] : (int)(keys[j] & 0xffffffffu);
+        const int pos = masked_pos[b];
+        const int tok = cand_tok[b];
+        seq[pos] = tok;
+        masked[pos] = 0;
+        commit_pos[j] = pos;
+        commit_tok[j] = tok;
+    }
+    if (threadIdx.x == 0) {
+        cnt[CNT_COMMITTED] = n_unmask;
+        cnt[CNT_NMASKED] = n - n_unmask;
+    }
+}
+
+// X (f32, host-provided for dfb_linear) -> f16 rows.
+__global__ void f32_to_f16_kernel(const float *__restrict__ x, __half *__restrict__ y, size_t n) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        y[i] = __float2half_rn(x[i]);
+}
+
+}  // namespace dfb
