@@ -307,6 +307,7 @@ extern "C" int dfb_model_create(const dfb_hparams *hp, int device, dfb_model **o
         return set_err(DFB_ERR_UNSUPPORTED, "head_dim %d not supported (16/32/64/128)", hd);
     int ndev = 0;
     CK(cudaGetDeviceCount(&ndev));
+    if (device < 0) CK(cudaGetDevice(&device));  // -1: the caller's current device
     if (device < 0 || device >= ndev) return set_err(DFB_ERR_ARG, "device %d out of range (%d devices)", device, ndev);
     CK(cudaSetDevice(device));
     cudaDeviceProp prop;
