@@ -821,6 +821,8 @@ extern "C" int dfb_gen_begin(dfb_ctx *c, const int32_t *prompt, int n_prompt, in
     for (int i = 0; i < n_prompt; i++)
         if (prompt[i] < 0 || prompt[i] >= m->hp.n_vocab) return set_err(DFB_ERR_ARG, "prompt token %d out of range", prompt[i]);
     if (n_gen > 65536) return set_err(DFB_ERR_ARG, "n_generate %d too large", n_gen);
+    if (m->hp.mask_token_id < 0 || m->hp.mask_token_id >= m->hp.n_vocab)
+        return set_err(DFB_ERR_ARG, "mask token id %d outside the vocabulary", m->hp.mask_token_id);
     RET(ctx_reserve(c, total));
     std::vector<int32_t> seq(total, m->hp.mask_token_id), neg(total, -1);
     std::copy(prompt, prompt + n_prompt, seq.begin());
@@ -830,6 +832,7 @@ extern "C" int dfb_gen_begin(dfb_ctx *c, const int32_t *prompt, int n_prompt, in
     CK(cudaMemcpyAsync(c->prev_seq, neg.data(), total * 4, cudaMemcpyHostToDevice, c->st));
     CK(cudaMemcpyAsync(c->last_changed, neg.data(), total * 4, cudaMemcpyHostToDevice, c->st));
     CK(cudaMemcpyAsync(c->masked, msk.data(), total, cudaMemcpyHostToDevice, c->st));
+    CK(cudaMemsetAsync(c->cnt, 0, sizeof(int) * CNT_N, c->st));
     CK(cudaStreamSynchronize(c->st));
     c->n_prompt = n_prompt;
     c->n_gen = n_gen;
@@ -865,7 +868,7 @@ extern "C" int dfb_gen_step(dfb_ctx *c, int step, int n_unmask_sched, int force_
     while (np < c->n_masked) np <<= 1;
     const size_t sel_smem = sizeof(unsigned long long) * (size_t)np;
     if (sel_smem > 48 * 1024) CK(cudaFuncSetAttribute(select_commit_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sel_smem));
-    select_commit_kernel<<<1, 1024, sel_smem, c->st>>>(c->sp.remasking, n_unmask_sched, c->sp.entropy_threshold,
+    select_commit_kernel<<<1, 1024, sel_smem, c->st>>>(c->sp.remasking, n_unmask_sched, c->sp.entropy_threshold, np,
                                                        c->order, c->masked_pos, c->cand_tok, c->cand_conf, c->cand_ent,
                                                        c->seq, c->masked, c->commit_pos, c->commit_tok, c->cnt);
     CK(cudaGetLastError());
@@ -874,6 +877,7 @@ extern "C" int dfb_gen_step(dfb_ctx *c, int step, int n_unmask_sched, int force_
     CK(cudaMemcpyAsync(h_cnt, c->cnt, sizeof(h_cnt), cudaMemcpyDeviceToHost, c->st));
     CK(cudaStreamSynchronize(c->st));
     RET(check_err(c));
+    if (h_cnt[CNT_ERR]) return set_err(DFB_ERR_STATE, "device and host disagree on the masked count");
     c->n_masked = h_cnt[CNT_NMASKED];
     if (stats) {
         stats->n_active = h_cnt[CNT_M];

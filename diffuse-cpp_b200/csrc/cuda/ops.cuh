@@ -226,7 +226,7 @@ __device__ __forceinline__ uint32_t ordered_u32(float f) {
 // TOPK_MARGIN) or entropy ascending (ENTROPY_EXIT), ties by ascending position;
 // RANDOM uses the host's shuffle.  One block of 1024 threads; dynamic shared memory
 // holds the padded key array (8 bytes per candidate, power of two).
-__global__ void __launch_bounds__(1024) select_commit_kernel(int remasking, int n_unmask_sched, float tau,
+__global__ void __launch_bounds__(1024) select_commit_kernel(int remasking, int n_unmask_sched, float tau, int key_cap,
                                                              const int32_t *__restrict__ order,
                                                              const int *__restrict__ masked_pos,
                                                              const int32_t *__restrict__ cand_tok,
@@ -239,6 +239,10 @@ __global__ void __launch_bounds__(1024) select_commit_kernel(int remasking, int 
     const int n = cnt[CNT_NMASKED];
     int np = 1;
     while (np < n) np <<= 1;
+    if (np > key_cap) {  // host and device disagree on the candidate count: commit nothing
+        if (threadIdx.x == 0) { cnt[CNT_ERR] = 1; cnt[CNT_COMMITTED] = 0; }
+        return;
+    }
     if (threadIdx.x == 0) n_easy_s = 0;
     __syncthreads();
     int easy = 0;

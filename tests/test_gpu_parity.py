@@ -1,0 +1,158 @@
+"""CUDA path against the CPU oracle (needs a B200).  Every call goes through the
+C-ABI (libdfb_cuda.so / libdiffuse.so)."""
+import numpy as np
+import pytest
+
+from conftest import MINI_DREAM, MINI_LLADA, metrics, write_tiny_gguf
+
+pytestmark = pytest.mark.gpu
+
+# north-star logits tolerances (max-abs, mean relative error sum|a-b|/sum|b|)
+LOGIT_MAXABS, LOGIT_MEANREL = 2e-2, 1e-3
+
+
+@pytest.fixture(scope="module")
+def models(pkg, model_dir):
+    m = {}
+    m["q4km"] = pkg.synth_model(model_dir / "llada_q4km.gguf", MINI_LLADA, "q4_k_m", seed=11, n_layer=3)
+    m["q8_0"] = pkg.synth_model(model_dir / "llada_q80.gguf", MINI_LLADA, "q8_0", seed=12)
+    m["f16"] = pkg.synth_model(model_dir / "llada_f16.gguf", MINI_LLADA, "f16", seed=13)
+    m["dream"] = pkg.synth_model(model_dir / "dream_q4km.gguf", MINI_DREAM, "q4_k_m", seed=14)
+    m["tiny"] = write_tiny_gguf(model_dir / "tiny.gguf")
+    m["tiny_gqa"] = write_tiny_gguf(model_dir / "tiny_gqa.gguf", kv_heads=2, bias=True, dream=True)
+    return m
+
+
+def f16_round(x):
+    return x.astype(np.float16).astype(np.float32)
+
+
+GEMM_CASES = [  # (model, role, layer, tensor name, expected GGML type)
+    ("q4km", "WQ", 1, "blk.1.attn_q.weight", 12), ("q4km", "WK", 1, "blk.1.attn_k.weight", 12),
+    ("q4km", "WV", 1, "blk.1.attn_v.weight", 12), ("q4km", "WO", 1, "blk.1.attn_output.weight", 12),
+    ("q4km", "GATE", 1, "blk.1.ffn_gate.weight", 12), ("q4km", "UP", 1, "blk.1.ffn_up.weight", 12),
+    ("q4km", "DOWN", 1, "blk.1.ffn_down.weight", 12), ("q4km", "GATE", 0, "blk.0.ffn_gate.weight", 14),
+    ("q4km", "DOWN", 2, "blk.2.ffn_down.weight", 14), ("q4km", "OUTPUT", 0, "output.weight", 14),
+    ("q8_0", "WQ", 0, "blk.0.attn_q.weight", 8), ("q8_0", "DOWN", 1, "blk.1.ffn_down.weight", 8),
+    ("q8_0", "OUTPUT", 0, "output.weight", 8), ("f16", "UP", 0, "blk.0.ffn_up.weight", 1),
+    ("f16", "WO", 1, "blk.1.attn_output.weight", 1), ("dream", "WK", 1, "blk.1.attn_k.weight", 12),
+    ("dream", "OUTPUT", 0, "output.weight", 14),
+]
+
+
+@pytest.mark.parametrize("case", GEMM_CASES, ids=lambda c: f"{c[0]}-{c[3]}")
+@pytest.mark.parametrize("M", [1, 17, 64, 200, 320, 600])
+def test_gemm_parity(pkg, orc, models, case, M):
+    name, role, layer, tname, gtype = case
+    model = pkg.Model(models[name])
+    ctx = pkg.Context(model, 0)
+    om = orc.OracleModel(models[name])
+    assert om.tensor(tname)[0] == gtype
+    K = om.tensor(tname)[1]
+    x = f16_round(np.random.default_rng(M).standard_normal((M, K)).astype(np.float32))
+    y = ctx.linear(getattr(pkg, role), layer, x)
+    ref = om.matmul(tname, x)
+    mx, rel = metrics(y, ref)
+    # operands the kernel sees: x exactly (f16), weights dequantized once to f16
+    assert rel < 1e-3 and mx < 2e-3 * np.abs(ref).max(), (mx, rel)
+    ctx.close(); model.close(); om.close()
+
+
+@pytest.mark.parametrize("name,n", [("q4km", 80), ("q4km", 320), ("q8_0", 96), ("f16", 64), ("dream", 192),
+                                    ("tiny", 40), ("tiny_gqa", 33)])
+def test_forward_logits_parity(pkg, orc, models, name, n):
+    model = pkg.Model(models[name])
+    ctx = pkg.Context(model, 0)
+    om = orc.OracleModel(models[name])
+    toks = np.random.default_rng(n).integers(0, om.n_vocab - 2, n).astype(np.int32)
+    got = ctx.forward(toks)
+    ref = om.forward(toks)
+    mx, rel = metrics(got, ref)
+    scale = max(1.0, float(np.abs(ref).max()))
+    print(f"{name} n={n}: max-abs {mx:.3e} (logit scale {scale:.1f}) mean-rel {rel:.3e}")
+    assert rel < LOGIT_MEANREL and mx < LOGIT_MAXABS * scale, (mx, rel)
+    assert (got.argmax(-1) == ref.argmax(-1)).mean() >= 0.99
+    ctx.close(); model.close(); om.close()
+
+
+def _teacher_forced(pkg, orc, path, n_prompt, n_gen, params_kw):
+    """Run the device loop step by step; before each step, replay the reference
+    sampler on the device's own logits and require identical commits."""
+    model = pkg.Model(path)
+    ctx = pkg.Context(model, 0)
+    om = orc.OracleModel(path)
+    hp = model.hparams
+    rng = np.random.default_rng(n_prompt * 7 + n_gen)
+    prompt = rng.integers(0, hp.mask_token_id - 1, n_prompt).astype(np.int32)
+    P = pkg.SamplerParams(**params_kw)
+    OP = orc.SamplerParams(**params_kw)
+    ctx.gen_begin(prompt, n_gen, P)
+    n_masked, initialized, near_ties = n_gen, False, 0
+    for step in range(P.n_steps):
+        if n_masked == 0:
+            break
+        seq = ctx.gen_tokens()
+        masked = np.zeros(seq.size, np.uint8)
+        masked[n_prompt:] = seq[n_prompt:] == hp.mask_token_id
+        force = (not P.use_cache) or (not initialized) or (P.cache_refresh > 0 and step > 0 and step % P.cache_refresh == 0)
+        k = pkg.tokens_to_unmask(step, P.n_steps, n_masked, P.schedule)
+        st = ctx.gen_step(step, k, force)
+        initialized = initialized or bool(P.use_cache)
+        pos, tok = ctx.gen_commits()
+        logits = ctx.logits_rows(0, seq.size)
+        ref = orc.sampler_step(logits, seq, masked, hp.is_dream, step, OP)
+        if P.remasking == 2:
+            # entropy keys are f32 sums in a different order: flips only between near ties
+            e = np.sort(ref["entropy"])
+            near_ties += int((np.diff(e) < 1e-5).sum())
+        assert st["n_unmasked"] == ref["n"]
+        np.testing.assert_array_equal(tok, ref["tok"])
+        np.testing.assert_array_equal(pos, ref["pos"])
+        n_masked = st["n_masked"]
+    out = ctx.gen_tokens()[n_prompt:]
+    ctx.close(); model.close(); om.close()
+    return out, near_ties
+
+
+@pytest.mark.parametrize("kw", [
+    dict(n_steps=8, remasking=0, use_cache=1),
+    dict(n_steps=8, remasking=0, use_cache=0),
+    dict(n_steps=8, remasking=4, use_cache=1),
+    dict(n_steps=8, remasking=2, use_cache=1, entropy_threshold=0.0),
+    dict(n_steps=6, remasking=3, use_cache=1, cache_refresh=3, cache_keep_active=1),
+], ids=["lowconf-cache", "lowconf-nocache", "margin", "entropy", "maskgit-refresh-keep"])
+def test_sampler_bit_exact_teacher_forced(pkg, orc, models, kw):
+    _teacher_forced(pkg, orc, models["q4km"], 16, 32, kw)
+
+
+def test_dream_shifted_logits_teacher_forced(pkg, orc, models):
+    _teacher_forced(pkg, orc, models["dream"], 24, 16, dict(n_steps=8, remasking=2, use_cache=1, entropy_threshold=1.5))
+
+
+@pytest.mark.parametrize("name,kw", [
+    ("q4km", dict(n_steps=8, remasking=0, use_cache=1)),
+    ("dream", dict(n_steps=8, remasking=2, use_cache=1, entropy_threshold=1.5)),
+    ("tiny", dict(n_steps=8, remasking=0, use_cache=0)),
+])
+def test_generate_tokens_agree_with_oracle(pkg, orc, models, name, kw):
+    model = pkg.Model(models[name])
+    ctx = pkg.Context(model, 0)
+    om = orc.OracleModel(models[name])
+    prompt = np.random.default_rng(5).integers(0, om.mask_token_id - 1, 16).astype(np.int32)
+    got, info = ctx.generate(prompt, 32, pkg.SamplerParams(**kw), trace=True)
+    ref, rtr = om.generate(prompt, 32, orc.SamplerParams(**kw))
+    agree = float((got == ref).mean())
+    print(f"{name}: token agreement {agree:.4f}, steps {info['steps_run']}")
+    assert (got != om.mask_token_id).all()
+    assert agree >= 0.995, agree
+    np.testing.assert_array_equal(info["n_unmasked"][: info["steps_run"]], rtr["n_unmask"][: rtr["steps_run"]])
+    ctx.close(); model.close(); om.close()
+
+
+def test_load_errors_are_reported(pkg, tmp_path):
+    p = tmp_path / "bad.gguf"
+    p.write_bytes(b"GGUF\x03\x00\x00\x00" + b"\x00" * 8)
+    with pytest.raises(pkg.DiffuseError):
+        pkg.Model(p)
+    with pytest.raises(pkg.DiffuseError):
+        pkg.Model(tmp_path / "nope.gguf")
