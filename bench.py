@@ -1,0 +1,375 @@
+#!/usr/bin/env python
+"""Benchmark of the denoising hot path (BASELINE.json metric: denoised tok/s per B200,
+LLaDA-8B Q4_K_M, B=256, 16 steps; ms per step).
+
+One bench "step" = one diffuse_generate call of the headline configuration (config 2):
+LLaDA-8B architecture, seeded random-init weights quantized to Q4_K_M by the reference's
+type policy, 64 uniform prompt ids, a 256-token masked block, 16 denoising steps,
+entropy_exit remasking with tau = 0 (so every step runs), inter-step K/V cache on.
+
+  value   tokens/s from the device time of the denoising steps (CUDA events on the
+          engine's stream; the model and prompt are already resident)
+  e2e     tokens/s through the public API call with host buffers (prompt in, tokens out,
+          per-step stats), wall clock
+  roofline the dequant-fused GEMMs (the dominant kernels) from a per-launch CUDA-event
+          pass after the timed region
+  cpu_baseline  the CPU oracle (a restatement of the reference's algorithm, OpenMP on
+          all host cores) on a bounded sample, extrapolated by FLOPs
+
+Multi-GPU (torchrun): every rank runs its own sequence (data parallel over independent
+sequences, no collective on the data path); the timed region is bracketed by barriers and
+the slowest rank's time sets the aggregate.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+import numpy as np
+
+ROOT = pathlib.Path(__file__).resolve().parent
+MEASURED = ROOT / "MEASURED_PEAKS.json"
+
+# DRAM bytes per launch of the dominant GEMM measured by ncu (profiles/), None until captured.
+NCU_GEMM_TRAFFIC_BYTES = None
+
+
+def load_pkg():
+    name = "diffuse_b200"
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(name, ROOT / "diffuse-cpp_b200" / "__init__.py")
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def peaks():
+    if MEASURED.exists():
+        d = json.loads(MEASURED.read_text())
+        return dict(hbm=d["hbm_gbs"], tf_burst=d["bf16_tflops"], tf_sust=d.get("bf16_tflops_sustained", d["bf16_tflops"]),
+                    src="measured")
+    return dict(hbm=6650.0, tf_burst=1590.0, tf_sust=1400.0, src="fallback")
+
+
+CONFIGS = {
+    "c2": dict(arch="llada", scheme="q4_k_m", prompt=64, block=256, steps=16, remasking=2, tau=0.0, cache=1,
+               desc="LLaDA-8B Q4_K_M random-init, prompt 64, block 256, 16 steps, entropy_exit tau=0, cache on"),
+    "c1": dict(arch="llada", scheme="q4_k_m", prompt=16, block=64, steps=16, remasking=0, tau=1.5, cache=0,
+               desc="LLaDA-8B Q4_K_M random-init, prompt 16, block 64, 16 steps, low_confidence, no cache"),
+    "c3": dict(arch="dream", scheme="q4_k_m", prompt=128, block=64, steps=16, remasking=2, tau=1.5, cache=1,
+               desc="Dream-7B Q4_K_M random-init, prompt 128, block 64, 16 steps, entropy_exit tau=1.5, cache on"),
+}
+
+
+def model_file(pkg, cfg, workdir):
+    arch = pkg.LLADA_8B if cfg["arch"] == "llada" else pkg.DREAM_7B
+    path = pathlib.Path(workdir) / f"{cfg['arch']}_{cfg['scheme']}_seed0.gguf"
+    if not path.exists():
+        tmp = path.with_suffix(".tmp")
+        pkg.synth_model(tmp, arch, cfg["scheme"], seed=0)
+        tmp.rename(path)
+    return str(path), arch
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def c2_algorithmic_flops(hp, n_active_per_step, n_keys):
+    """FLOPs the reference's graph performs for these active-row counts (linears for all
+    active rows, lm_head for all active rows, attention over all keys)."""
+    d, ff, V, L = hp.n_embd, hp.n_ff, hp.n_vocab, hp.n_layer
+    kvd = hp.n_head_kv * (d // hp.n_head)
+    per_row = L * 2 * (2 * d * d + 2 * d * kvd + 3 * d * ff) + 2 * d * V
+    att = L * 4 * n_keys * hp.n_head * (d // hp.n_head)
+    return sum(m * (per_row + att) for m in n_active_per_step)
+
+
+def cpu_sample(pkg, path, cfg, hp, n_rows=256, n_layers=2):
+    """Times the CPU oracle on one forward of n_rows tokens through the first n_layers
+    layers + lm_head of the same model; returns (GFLOP/s, seconds, threads)."""
+    sys.path.insert(0, str(ROOT))
+    from oracle import oracle
+    om = oracle.OracleModel(path)
+    toks = np.random.default_rng(7).integers(0, hp.mask_token_id - 1, n_rows).astype(np.int32)
+    t0 = time.perf_counter()
+    om.forward_layers(toks, n_layers)
+    dt = time.perf_counter() - t0
+    d, ff, V = hp.n_embd, hp.n_ff, hp.n_vocab
+    kvd = hp.n_head_kv * (d // hp.n_head)
+    flops = n_rows * (n_layers * 2 * (2 * d * d + 2 * d * kvd + 3 * d * ff) + 2 * d * V) \
+        + n_layers * 4 * n_rows * n_rows * hp.n_head * (d // hp.n_head)
+    om.close()
+    return flops / dt / 1e9, dt, os.cpu_count()
+
+
+def run_reference(args, cfg):
+    """--impl reference: the CPU oracle (the reference's algorithm restated; the reference
+    itself cannot be built: its ggml submodule is empty) on the host cores."""
+    pkg = load_pkg()
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    work = pathlib.Path(os.environ.get("DFB_BENCH_DIR", tempfile.gettempdir())) / "dfb_bench"
+    work.mkdir(parents=True, exist_ok=True)
+    path, arch = model_file(pkg, cfg, work)
+    hp = type("HP", (), dict(n_embd=arch["n_embd"], n_ff=arch["n_ff"], n_vocab=arch["n_vocab"], n_layer=arch["n_layer"],
+                             n_head=arch["n_head"], n_head_kv=arch["n_head_kv"], mask_token_id=arch["mask_token_id"]))
+    steps_active = c2_active_rows(cfg)
+    total_flops = c2_algorithmic_flops(hp, steps_active, cfg["prompt"] + cfg["block"])
+    rates = []
+    for i in range(args.warmup + args.steps):
+        gfs, dt, cores = cpu_sample(pkg, path, cfg, hp)
+        if i >= args.warmup:
+            rates.append(gfs)
+    gfs = statistics.median(rates)
+    t_run = total_flops / (gfs * 1e9)
+    tok_s = cfg["block"] / t_run
+    line = {"impl": "reference", "metric": "denoised tok/s per B200 (LLaDA-8B Q4_K_M, B=256, 16 steps)",
+            "value": tok_s, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": t_run * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": {"workload": cfg["desc"]},
+            "cpu_baseline": {"value": tok_s, "unit": "tok/s", "cores": cores, "kind": "port",
+                             "sample": "CPU oracle forward of 256 rows through 2 of 32 layers + lm_head per step; "
+                                       "tok/s extrapolated by the run's algorithmic FLOPs"},
+            "e2e": {"value": tok_s, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def c2_active_rows(cfg):
+    """Active rows per denoising step of the reference's cached loop when no position
+    changes except the committed ones (step 0 full, then masked + just committed)."""
+    from math import cos, pi
+    B, S, P = cfg["block"], cfg["steps"], cfg["prompt"]
+    rows, masked, prev_commit = [], B, 0
+    for s in range(S):
+        if masked == 0:
+            break
+        rows.append(P + B if (s == 0 or not cfg["cache"]) else masked + prev_commit)
+        t0, t1 = s / S, (s + 1) / S
+        c0, c1 = np.float32(cos(np.float32(t0) * pi * 0.5)), np.float32(cos(np.float32(t1) * pi * 0.5))
+        k = int(round(float(np.float32((c0 - c1) / c0) * masked)))
+        k = max(1, min(k, masked))
+        prev_commit = k
+        masked -= k
+    return rows
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        return run_reference(args, cfg)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as tdist
+        torch.cuda.set_device(local)
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+        dist = tdist
+    os.environ["DIFFUSE_DEVICE"] = str(local)
+    os.environ.setdefault("DIFFUSE_LOG_LEVEL", "0")
+    pkg = load_pkg()
+
+    def barrier():
+        if dist:
+            import torch
+            dist.barrier(device_ids=[local])
+            torch.cuda.synchronize()
+
+    def reduce_max(x):
+        if not dist:
+            return x
+        import torch
+        t = torch.tensor([x], dtype=torch.float64, device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    work = pathlib.Path(os.environ.get("DFB_BENCH_DIR", tempfile.gettempdir())) / "dfb_bench"
+    work.mkdir(parents=True, exist_ok=True)
+    t_synth = time.perf_counter()
+    if rank == 0:
+        path, arch = model_file(pkg, cfg, work)
+    barrier()
+    if rank != 0:
+        path, arch = model_file(pkg, cfg, work)
+    t_synth = time.perf_counter() - t_synth
+    model = pkg.Model(path)
+    hp = model.hparams
+    P, B = cfg["prompt"], cfg["block"]
+    ctx = pkg.Context(model, P + B)
+    params = pkg.SamplerParams(n_steps=cfg["steps"], remasking=cfg["remasking"], entropy_threshold=cfg["tau"],
+                               use_cache=cfg["cache"])
+    rng = np.random.default_rng(1234 + rank)
+    prompts = [rng.integers(0, min(hp.mask_token_id, hp.n_vocab) - 1, P).astype(np.int32)
+               for _ in range(args.warmup + args.steps)]
+
+    for i in range(args.warmup):
+        ctx.generate(prompts[i], B, params)
+    barrier()
+    dev_ms, wall_ms, actives = [], [], []
+    with ClockSampler(local) as clk:
+        for i in range(args.steps):
+            t0 = time.perf_counter()
+            out, tr = ctx.generate(prompts[args.warmup + i], B, params, trace=True)
+            wall_ms.append((time.perf_counter() - t0) * 1e3)
+            n = tr["steps_run"]
+            dev_ms.append(float(tr["step_ms"][:n].sum()))
+            actives = tr["n_active"][:n].tolist()
+    barrier()
+    tot_dev = reduce_max(sum(dev_ms))
+    tot_wall = reduce_max(sum(wall_ms))
+
+    # roofline pass: per-launch CUDA events around every GEMM of one generation
+    dfb, _ = pkg.native()
+    import ctypes as C
+
+    class Prof(C.Structure):
+        _fields_ = [("calls", C.c_int32), ("ms", C.c_double), ("flops", C.c_double), ("bytes", C.c_double)]
+    dfb.dfb_ctx_profile.argtypes = [C.c_void_p, C.c_int]
+    dfb.dfb_ctx_profile_read.argtypes = [C.c_void_p, C.c_void_p, C.c_int]
+    dfb.dfb_ctx_profile(ctx.engine, 1)
+    ctx.generate(prompts[-1], B, params)
+    prof = (Prof * 7)()
+    dfb.dfb_ctx_profile_read(ctx.engine, prof, 7)
+    dfb.dfb_ctx_profile(ctx.engine, 0)
+    g = prof[0]
+    pk = peaks()
+    gemm_tflops = g.flops / (g.ms * 1e-3) / 1e12 if g.ms > 0 else 0.0
+    per_launch_bytes = g.bytes / max(g.calls, 1)
+    roofline = {"bound": "tensor", "achieved": gemm_tflops, "peak": pk["tf_sust"], "unit": "TFLOP/s",
+                "frac": gemm_tflops / pk["tf_sust"], "traffic": NCU_GEMM_TRAFFIC_BYTES,
+                "peak_source": f"{pk['src']} bf16 sustained (f16 operands run at the same tensor rate)",
+                "kernel": "dq_gemm_kernel (all linears of one generation)", "launches": g.calls,
+                "avg_launch_us": g.ms * 1e3 / max(g.calls, 1), "algorithmic_bytes_per_launch": per_launch_bytes,
+                "hbm_gbs_achieved": g.bytes / (g.ms * 1e-3) / 1e9 if g.ms > 0 else 0.0,
+                "breakdown": {name: {"calls": prof[i].calls, "ms": prof[i].ms,
+                                     "tflops": prof[i].flops / (prof[i].ms * 1e-3) / 1e12 if prof[i].ms else 0}
+                              for i, name in [(1, "q4_k"), (2, "q6_k"), (5, "lm_head"), (6, "attention")]}}
+
+    tokens_all = B * args.steps * world
+    value = tokens_all / (tot_dev * 1e-3)
+    e2e = tokens_all / (tot_wall * 1e-3)
+    flops_run = c2_algorithmic_flops(hp, actives, P + B)
+    launches_per_denoise_step = 7 * hp.n_layer + 6
+    h2d = 4 * (P + B) * 3 + (P + B)            # seq, prev_seq, last_changed, masks at gen_begin
+    d2h = cfg["steps"] * (4 * 8 + 4) + 4 * (P + B)  # per-step counters + error flag, final tokens
+    line = {
+        "metric": "denoised tok/s per B200 (LLaDA-8B Q4_K_M, B=256, 16 steps)" if args.config == "c2" else
+        f"denoised tok/s ({args.config})",
+        "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": tot_dev / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f16", "data": "synthetic",
+        "config": {"workload": cfg["desc"], "prompt_len": P, "block": B, "denoise_steps": cfg["steps"],
+                   "step_definition": "one diffuse_generate call (all denoising steps of one sequence)",
+                   "l2": "inputs larger than L2: 4.4 GB of weights stream from HBM every denoising step",
+                   "parallelism": f"dp{world} (independent sequences)",
+                   "active_rows_per_denoising_step": actives,
+                   "denoising_step_ms": (tot_dev / args.steps) / max(len(actives), 1),
+                   "algorithmic_tflop_per_step": flops_run / 1e12,
+                   "model_synth_s": round(t_synth, 1)},
+        "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": tot_wall / args.steps},
+        "roofline": roofline,
+        "gpu_launches": launches_per_denoise_step * cfg["steps"] * args.steps,
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            gfs, dt, cores = cpu_sample(pkg, path, cfg, hp)
+            t_run = flops_run / (gfs * 1e9)
+            line["cpu_baseline"] = {"value": B / t_run, "unit": "tok/s", "cores": cores, "kind": "port",
+                                    "sample": f"CPU oracle forward of 256 rows through 2 of 32 layers + lm_head "
+                                              f"({dt:.1f} s, {gfs:.0f} GFLOP/s), extrapolated by the run's FLOPs"}
+        except Exception as e:  # the baseline is context, never a reason to lose the line
+            line["cpu_baseline"] = {"value": None, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+                                    "sample": f"failed: {e}"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    model.close()
+    if dist:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -173,6 +173,7 @@ static void dequant_row_host(int type, const uint8_t *src, int64_t n, float *dst
 struct WMat {
     int wt = -1;
     int n_rows = 0, n_tiles = 0, K = 0, kb = 0;
+    int n_true = 0;  // output features the model defines (before padding / fusion slack)
     uint8_t *d = nullptr;
     CUtensorMap tm{};
     size_t bytes = 0;
@@ -400,6 +401,7 @@ extern "C" int dfb_model_finalize(dfb_model *m) {
         std::vector<const uint8_t *> rows((V + 127) / 128 * 128, nullptr);
         for (int r = 0; r < V; r++) rows[r] = out.data + r * rb;
         RET(build_wmat(rows, out.type, d, m->lm_head));
+        m->lm_head.n_true = V;
         m->bytes += m->lm_head.bytes;
     }
     for (int l = 0; l < hp.n_layer; l++) {
@@ -425,6 +427,7 @@ extern "C" int dfb_model_finalize(dfb_model *m) {
                 rows[m->nq_pad + m->nk_pad + r] = wv.data + (int64_t)r * rb;
             }
             RET(build_wmat(rows, wq.type, d, L.qkv));
+            L.qkv.n_true = m->n_q + 2 * m->n_kv;
         }
         const HostTensor &bq = staged(m, DFB_BQ, l), &bk = staged(m, DFB_BK, l), &bv = staged(m, DFB_BV, l);
         if (bq.data || bk.data || bv.data) {
@@ -443,6 +446,7 @@ extern "C" int dfb_model_finalize(dfb_model *m) {
             const int64_t rb = ggml_row_bytes(wo.type, m->n_q);
             for (int r = 0; r < d; r++) rows[r] = wo.data + (int64_t)r * rb;
             RET(build_wmat(rows, wo.type, m->n_q, L.o));
+            L.o.n_true = d;
         }
         const HostTensor &wg = staged(m, DFB_GATE, l), &wu = staged(m, DFB_UP, l), &wd = staged(m, DFB_DOWN, l);
         RET(check_mat(wg, "ffn_gate", d, ff));
@@ -457,12 +461,14 @@ extern "C" int dfb_model_finalize(dfb_model *m) {
                 rows[2 * i + 1] = wu.data + (int64_t)i * rb;
             }
             RET(build_wmat(rows, wg.type, d, L.gateup));
+            L.gateup.n_true = 2 * ff;
         }
         {
             std::vector<const uint8_t *> rows((d + 127) / 128 * 128, nullptr);
             const int64_t rb = ggml_row_bytes(wd.type, ff);
             for (int r = 0; r < d; r++) rows[r] = wd.data + (int64_t)r * rb;
             RET(build_wmat(rows, wd.type, ff, L.down));
+            L.down.n_true = d;
         }
         RET(upload_vec(m, staged(m, DFB_ATTN_NORM, l), d, &L.attn_norm));
         RET(upload_vec(m, staged(m, DFB_FFN_NORM, l), d, &L.ffn_norm));
@@ -512,6 +518,16 @@ struct dfb_ctx {
     float *ws = nullptr;
     int *tile_cnt = nullptr, *err = nullptr;
     int n_tile_cnt = 0;
+    // optional per-launch timing (dfb_ctx_profile)
+    struct ProfRec {
+        cudaEvent_t a, b;
+        int cat;
+        double flops_per_row, bytes_fixed, bytes_per_row;
+    };
+    bool prof = false;
+    std::vector<ProfRec> prof_pending;
+    std::vector<cudaEvent_t> ev_pool;
+    dfb_prof_entry prof_acc[DFB_PROF_N]{};
     // generation
     bool gen_active = false;
     int n_prompt = 0, n_gen = 0, total = 0, n_masked = 0;
@@ -584,6 +600,46 @@ static int ctx_reserve(dfb_ctx *c, int n) {
     return DFB_OK;
 }
 
+static cudaEvent_t prof_event(dfb_ctx *c) {
+    if (c->ev_pool.empty()) {
+        cudaEvent_t e;
+        cudaEventCreate(&e);
+        return e;
+    }
+    cudaEvent_t e = c->ev_pool.back();
+    c->ev_pool.pop_back();
+    return e;
+}
+static void prof_begin(dfb_ctx *c, cudaEvent_t *a) {
+    if (!c->prof) return;
+    *a = prof_event(c);
+    cudaEventRecord(*a, c->st);
+}
+static void prof_end(dfb_ctx *c, cudaEvent_t a, int cat, double flops_per_row, double bytes_fixed, double bytes_per_row) {
+    if (!c->prof) return;
+    cudaEvent_t b = prof_event(c);
+    cudaEventRecord(b, c->st);
+    c->prof_pending.push_back({a, b, cat, flops_per_row, bytes_fixed, bytes_per_row});
+}
+// After the stream is synchronized: fold the pending launches of a pass over M rows.
+static void prof_collect(dfb_ctx *c, int M) {
+    for (auto &r : c->prof_pending) {
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, r.a, r.b);
+        for (int cat : {r.cat, r.cat < DFB_PROF_ATTN ? (int)DFB_PROF_GEMM_ALL : -1}) {
+            if (cat < 0) continue;
+            dfb_prof_entry &e = c->prof_acc[cat];
+            e.calls += 1;
+            e.ms += ms;
+            e.flops += r.flops_per_row * M;
+            e.bytes += r.bytes_fixed + r.bytes_per_row * M;
+        }
+        c->ev_pool.push_back(r.a);
+        c->ev_pool.push_back(r.b);
+    }
+    c->prof_pending.clear();
+}
+
 template <int WT, int EPI>
 static int launch_gemm_t(dfb_ctx *c, const WMat &w, const CUtensorMap &tm_x, const EpiArgs &epi) {
     auto kern = dq_gemm_kernel<WT, EPI>;
@@ -603,8 +659,15 @@ static int launch_gemm_t(dfb_ctx *c, const WMat &w, const CUtensorMap &tm_x, con
     p.tile_cnt = c->tile_cnt;
     p.err = c->err;
     p.epi = epi;
+    cudaEvent_t ev0 = nullptr;
+    prof_begin(c, &ev0);
     kern<<<c->m->n_sm, kThreads, smem, c->st>>>(tm_x, WT == W_F16 ? w.tm : tm_x, p);
     CK(cudaGetLastError());
+    // algorithmic work: 2*K MACs per output, weights read once, X read, Y written
+    const int out_bytes = (EPI == EPI_F16 || EPI == EPI_QKV || EPI == EPI_SWIGLU) ? 2 : 4;
+    const int cat = WT == W_Q4K ? DFB_PROF_Q4K : WT == W_Q6K ? DFB_PROF_Q6K : WT == W_Q80 ? DFB_PROF_Q80 : DFB_PROF_F16;
+    prof_end(c, ev0, EPI == EPI_LOGITS ? (int)DFB_PROF_LMHEAD : cat, 2.0 * w.K * (double)w.n_true, (double)w.bytes,
+             2.0 * w.K + (double)out_bytes * (EPI == EPI_SWIGLU ? w.n_true / 2 : w.n_true));
     return DFB_OK;
 }
 
@@ -630,9 +693,12 @@ static int launch_attn_t(dfb_ctx *c, const __half *kc, const __half *vc, int n_k
     }
     const float scale_log2 = (1.0f / sqrtf((float)HD)) * 1.4426950408889634f;
     dim3 grid((c->cap + kAttnRows - 1) / kAttnRows, m->hp.n_head);
+    cudaEvent_t ev0 = nullptr;
+    prof_begin(c, &ev0);
     attn_kernel<HD><<<grid, 128, smem, c->st>>>(c->q, m->n_q, kc, vc, m->n_kv, c->att, m->n_q, c->cnt + CNT_M, n_keys,
                                                 m->hp.n_head / m->hp.n_head_kv, scale_log2);
     CK(cudaGetLastError());
+    prof_end(c, ev0, DFB_PROF_ATTN, 4.0 * n_keys * m->hp.n_head * HD, 2.0 * 2.0 * n_keys * m->n_kv, 4.0 * m->n_q);
     return DFB_OK;
 }
 
@@ -718,8 +784,25 @@ extern "C" void dfb_ctx_free(dfb_ctx *c) {
     if (c->st) cudaStreamSynchronize(c->st);
     ctx_free_buffers(c);
     for (auto &e : c->ev) if (e) cudaEventDestroy(e);
+    for (auto &r : c->prof_pending) { cudaEventDestroy(r.a); cudaEventDestroy(r.b); }
+    for (auto e : c->ev_pool) cudaEventDestroy(e);
     if (c->st) cudaStreamDestroy(c->st);
     delete c;
+}
+
+extern "C" int dfb_ctx_profile(dfb_ctx *c, int enable) {
+    if (!c) return set_err(DFB_ERR_ARG, "null context");
+    CK(cudaStreamSynchronize(c->st));
+    prof_collect(c, 0);
+    c->prof = enable != 0;
+    for (auto &e : c->prof_acc) e = dfb_prof_entry{};
+    return DFB_OK;
+}
+
+extern "C" int dfb_ctx_profile_read(dfb_ctx *c, dfb_prof_entry *out, int n) {
+    if (!c || !out) return set_err(DFB_ERR_ARG, "null pointer");
+    for (int i = 0; i < n && i < DFB_PROF_N; i++) out[i] = c->prof_acc[i];
+    return DFB_OK;
 }
 
 extern "C" int dfb_ctx_stream(dfb_ctx *c, void **stream) {
@@ -744,6 +827,7 @@ extern "C" int dfb_forward(dfb_ctx *c, const int32_t *tokens, int n, float *logi
     RET(run_forward(c, n));
     CK(cudaMemcpyAsync(logits_host, c->logits, (size_t)n * V * sizeof(float), cudaMemcpyDeviceToHost, c->st));
     CK(cudaStreamSynchronize(c->st));
+    prof_collect(c, n);
     return check_err(c);
 }
 
@@ -876,6 +960,7 @@ extern "C" int dfb_gen_step(dfb_ctx *c, int step, int n_unmask_sched, int force_
     int h_cnt[CNT_N];
     CK(cudaMemcpyAsync(h_cnt, c->cnt, sizeof(h_cnt), cudaMemcpyDeviceToHost, c->st));
     CK(cudaStreamSynchronize(c->st));
+    prof_collect(c, h_cnt[CNT_M]);
     RET(check_err(c));
     if (h_cnt[CNT_ERR]) return set_err(DFB_ERR_STATE, "device and host disagree on the masked count");
     c->n_masked = h_cnt[CNT_NMASKED];

@@ -311,15 +311,23 @@ static uint64_t name_hash(const std::string &s, uint64_t seed) {
 }
 // N(0, std) via Box-Muller on a counter-based stream: element i of a tensor depends
 // only on (seed, tensor name, i), so rows can be generated in any order / thread.
+// Elements 2j and 2j+1 share one (u1, u2) pair.
 static void gauss_fill(float *out, int64_t i0, int64_t n, uint64_t key, float std_) {
-    for (int64_t k = 0; k < n; k++) {
+    int64_t k = 0;
+    while (k < n) {
         const int64_t i = i0 + k;
         const uint64_t r = splitmix(key ^ (uint64_t)(i >> 1) * 0xD1B54A32D192ED03ull);
-        const double u1 = ((r >> 11) + 1.0) * (1.0 / 9007199254740994.0);
-        const double u2 = (double)(splitmix(r) >> 11) * (1.0 / 9007199254740992.0);
-        const double rad = sqrt(-2.0 * log(u1));
-        const double z = (i & 1) ? rad * sin(6.283185307179586 * u2) : rad * cos(6.283185307179586 * u2);
-        out[k] = (float)(z * std_);
+        const float u1 = ((uint32_t)(r >> 40) + 1.0f) * (1.0f / 16777217.0f);
+        const float u2 = (float)((uint32_t)r >> 8) * (1.0f / 16777216.0f);
+        const float rad = sqrtf(-2.0f * logf(u1)) * std_;
+        float sn, cs;
+        sincosf(6.2831853f * u2, &sn, &cs);
+        if ((i & 1) == 0) {
+            out[k++] = rad * cs;
+            if (k < n) out[k++] = rad * sn;
+        } else {
+            out[k++] = rad * sn;
+        }
     }
 }
 

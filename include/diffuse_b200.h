@@ -119,6 +119,21 @@ int dfb_gen_commits(dfb_ctx *c, int32_t *pos_host, int32_t *tok_host, int cap);
 /* Rows [row0, row0+nrows) of the persistent logits buffer (parity checks). */
 int dfb_gen_logits(dfb_ctx *c, int row0, int nrows, float *host);
 
+/* Optional per-launch timing with CUDA events on the context's stream (off by
+ * default; adds event records around each kernel).  Categories accumulate launches,
+ * device ms, algorithmic FLOPs and algorithmic bytes (weights once + activations in
+ * + outputs) of every forward / step run while enabled. */
+enum { DFB_PROF_GEMM_ALL = 0, DFB_PROF_Q4K, DFB_PROF_Q6K, DFB_PROF_Q80, DFB_PROF_F16, DFB_PROF_LMHEAD,
+       DFB_PROF_ATTN, DFB_PROF_N };
+typedef struct {
+    int32_t calls;
+    double  ms;
+    double  flops;
+    double  bytes;
+} dfb_prof_entry;
+int dfb_ctx_profile(dfb_ctx *c, int enable);                            /* (re)start, zeroed */
+int dfb_ctx_profile_read(dfb_ctx *c, dfb_prof_entry *out, int n);      /* n <= DFB_PROF_N */
+
 /* Device stream of a context (cudaStream_t as void*), for callers that time it. */
 int dfb_ctx_stream(dfb_ctx *c, void **stream);
 

@@ -563,7 +563,7 @@ struct step_cache {
 // afterwards (update_kv, cache.h:123-139 via graph.cpp:655-669).
 void forward_rows(const orc_model &m, const int32_t *tokens, const int *pos, int M,
                   const std::vector<int> *cached_pos, step_cache *cache, float *logits,
-                  int mode, int nt) {
+                  int mode, int nt, int layer_limit = -1) {
     const hparams &hp = m.hp;
     const int d = hp.n_embd, H = hp.n_head, Hkv = hp.n_head_kv, hd = hp.hd(), ff = hp.n_ff;
     const int kvd = Hkv * hd, n_rep = H / Hkv;
@@ -582,7 +582,8 @@ void forward_rows(const orc_model &m, const int32_t *tokens, const int *pos, int
     const float kq_scale = 1.0f / sqrtf((float)hd);
     std::vector<float> Kfull((size_t)N * kvd), Vfull((size_t)N * kvd);
 
-    for (int il = 0; il < hp.n_layer; il++) {
+    const int n_layers = layer_limit >= 0 ? std::min(layer_limit, hp.n_layer) : hp.n_layer;
+    for (int il = 0; il < n_layers; il++) {
         const layer_w &L = m.layers[il];
         std::vector<float> wn = vec_f32(L.attn_norm);
         rmsnorm(x.data(), wn.data(), h.data(), M, d, hp.eps);
@@ -843,6 +844,14 @@ int orc_forward(const orc_model *m, const int32_t *tokens, int32_t n, float *log
     std::vector<int> pos(n);
     for (int i = 0; i < n; i++) pos[i] = i;
     forward_rows(*m, tokens, pos.data(), n, nullptr, nullptr, logits, mode, nthreads_or(nt));
+    return 0;
+}
+
+int orc_forward_layers(const orc_model *m, const int32_t *tokens, int32_t n, float *logits, int32_t mode,
+                       int32_t nt, int32_t n_layers) {
+    std::vector<int> pos(n);
+    for (int i = 0; i < n; i++) pos[i] = i;
+    forward_rows(*m, tokens, pos.data(), n, nullptr, nullptr, logits, mode, nthreads_or(nt), n_layers);
     return 0;
 }
 

@@ -78,6 +78,11 @@ int orc_matmul(const orc_model *m, const char *name, const float *x, int32_t M, 
 int orc_forward(const orc_model *m, const int32_t *tokens, int32_t n, float *logits,
                 int32_t mode, int32_t n_threads);
 
+// Same, through only the first n_layers transformer layers (then final norm + lm_head):
+// a bounded sample of the full forward for CPU timing.
+int orc_forward_layers(const orc_model *m, const int32_t *tokens, int32_t n, float *logits,
+                       int32_t mode, int32_t n_threads, int32_t n_layers);
+
 // The whole diffuse_sample loop. out_tokens: [n_gen]. trace may be NULL.
 int orc_generate(const orc_model *m, const int32_t *prompt, int32_t n_prompt, int32_t n_gen,
                  const orc_sampler_params *p, int32_t *out_tokens, orc_trace *trace,

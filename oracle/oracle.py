@@ -49,6 +49,7 @@ def lib():
             ("orc_load", P, [C.c_char_p]), ("orc_free", None, [P]), ("orc_hparams", I, [P, P, P]),
             ("orc_tensor", I, [P, C.c_char_p, P, P, P, P]), ("orc_dequantize", I, [I, P, C.c_int64, P]),
             ("orc_matmul", I, [P, C.c_char_p, P, I, P, I, I]), ("orc_forward", I, [P, P, I, P, I, I]),
+            ("orc_forward_layers", I, [P, P, I, P, I, I, I]),
             ("orc_generate", I, [P, P, I, I, C.POINTER(SamplerParams), P, C.POINTER(_Trace), I, I]),
             ("orc_sampler_step", I, [P, I, I, P, P, I, I, C.POINTER(SamplerParams), P, P, P, P]),
             ("orc_tokens_to_unmask", I, [I, I, I, I]), ("orc_entropy", C.c_float, [P, I]),
@@ -133,6 +134,12 @@ class OracleModel:
         t = np.ascontiguousarray(tokens, dtype=np.int32)
         out = np.empty((t.size, self.n_vocab), np.float32)
         lib().orc_forward(self.h, _p(t), t.size, _p(out), mode, n_threads)
+        return out
+
+    def forward_layers(self, tokens, n_layers, mode=EXACT, n_threads=0):
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        out = np.empty((t.size, self.n_vocab), np.float32)
+        lib().orc_forward_layers(self.h, _p(t), t.size, _p(out), mode, n_threads, n_layers)
         return out
 
     def generate(self, prompt, n_gen, params: SamplerParams, mode=EXACT, n_threads=0, final_logits=False):

@@ -96,7 +96,7 @@ def write_tiny_gguf(path, dtype=np.float32, dream=False, kv_heads=None, seed=42,
 # MHA for LLaDA, GQA 7:1 for Dream), K dims multiples of 256 for the K-quants.
 MINI_LLADA = dict(is_dream=0, n_vocab=5000, n_embd=1024, n_head=8, n_head_kv=8, n_layer=2, n_ff=2816,
                   n_ctx=4096, mask_token_id=4999, rope_theta=500000.0, rms_norm_eps=1e-5, with_bias=0)
-MINI_DREAM = dict(is_dream=1, n_vocab=6000, n_embd=896, n_head=7, n_head_kv=1, n_layer=2, n_ff=2304,
+MINI_DREAM = dict(is_dream=1, n_vocab=6000, n_embd=1792, n_head=14, n_head_kv=2, n_layer=2, n_ff=4864,
                   n_ctx=4096, mask_token_id=5999, rope_theta=1000000.0, rms_norm_eps=1e-6, with_bias=1)
 
 
