@@ -661,7 +661,9 @@ static int launch_gemm_t(dfb_ctx *c, const WMat &w, const CUtensorMap &tm_x, con
     p.epi = epi;
     cudaEvent_t ev0 = nullptr;
     prof_begin(c, &ev0);
-    kern<<<c->m->n_sm, kThreads, smem, c->st>>>(tm_x, WT == W_F16 ? w.tm : tm_x, p);
+    // A tile is split over at most grid/n_tiles + 2 CTAs; keep that within kMaxContrib.
+    const int grid = std::min(c->m->n_sm, (kMaxContrib - 2) * w.n_tiles);
+    kern<<<grid, kThreads, smem, c->st>>>(tm_x, WT == W_F16 ? w.tm : tm_x, p);
     CK(cudaGetLastError());
     // algorithmic work: 2*K MACs per output, weights read once, X read, Y written
     const int out_bytes = (EPI == EPI_F16 || EPI == EPI_QKV || EPI == EPI_SWIGLU) ? 2 : 4;

@@ -72,8 +72,10 @@ constexpr int kMaxTok = 256;             // tokens per MMA (N)
 constexpr int kWsTile = kMaxTok * 128;   // floats per partial tile
 constexpr int kErrTimeout = 0x100;
 
+constexpr int kMaxContrib = 64;  // split contributors of one tile tracked in shared memory
 __host__ __device__ constexpr int gemm_smem_bytes(int wt) {
-    return 1024 /*align slack*/ + kStages * kStageBytes + kRawStages * raw_chunk_bytes(wt) + 256 /*barriers*/;
+    return 1024 /*align slack*/ + kStages * kStageBytes + kRawStages * raw_chunk_bytes(wt) + 256 /*barriers*/ +
+           4 * kMaxTok /*token positions*/ + 8 * kMaxContrib /*contributor partial offsets*/;
 }
 
 // Static stream-K schedule, recomputed identically by every role of every CTA.
@@ -285,60 +287,115 @@ __device__ __forceinline__ void q80_slice(const uint8_t *R, int r, int s, uint8_
 // ───────────── epilogues ─────────────
 __device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
 
-// Applies the epilogue to one accumulator value.  Called by all 32 lanes of a warp
-// together (the paired epilogues exchange values with the neighbouring lane).
+// Per-thread constants of one output tile (thread = TMEM lane = one output row).
+struct EpiRow {
+    int f;          // output feature written by this lane (after un-fusing)
+    bool fvalid;    // f is a real feature (not tile padding)
+    bool writer;    // this lane stores (SwiGLU: the gate lane of each pair)
+    int sec;        // QKV: 0 Q, 1 K, 2 V
+    int ipair;      // QKV: NEOX pair index i (angle index)
+    int bpair;      // QKV: 0 for element i, 1 for element i + head_dim/2
+    float bias;     // QKV bias of this row (0 without bias)
+};
+
 template <int EPI>
-__device__ __forceinline__ void epi_apply(const EpiArgs &e, int tile, int row, int tok, bool valid, float v) {
-    if constexpr (EPI == EPI_F32 || EPI == EPI_F16 || EPI == EPI_RESID) {
-        const int f = tile * 128 + row;
-        if (valid && f < e.n_valid) {
-            if constexpr (EPI == EPI_F32) reinterpret_cast<float *>(e.out)[(size_t)tok * e.ld + f] = v;
-            else if constexpr (EPI == EPI_F16) reinterpret_cast<__half *>(e.out)[(size_t)tok * e.ld + f] = __float2half_rn(v);
-            else reinterpret_cast<float *>(e.out)[(size_t)tok * e.ld + f] += v;
-        }
-    } else if constexpr (EPI == EPI_LOGITS) {
-        const int f = tile * 128 + row;
-        if (valid && f < e.n_valid) {
-            const int p = e.pos[tok];
-            reinterpret_cast<float *>(e.out)[(size_t)p * e.ld + f] = v;
-        }
-    } else if constexpr (EPI == EPI_SWIGLU) {
+__device__ __forceinline__ EpiRow epi_row(const EpiArgs &e, int tile, int row) {
+    EpiRow r{};
+    if constexpr (EPI == EPI_SWIGLU) {
         // rows interleaved: 2i = gate_i, 2i+1 = up_i
-        const float partner = __shfl_xor_sync(0xffffffffu, v, 1);
-        if ((row & 1) == 0) {
-            const int f = tile * 64 + (row >> 1);
-            if (valid && 2 * f < e.n_valid) {
-                const float h = silu_f(v) * partner;
-                reinterpret_cast<__half *>(e.out)[(size_t)tok * e.ld + f] = __float2half_rn(h);
-            }
-        }
+        r.f = tile * 64 + (row >> 1);
+        r.fvalid = 2 * r.f < e.n_valid;
+        r.writer = (row & 1) == 0;
     } else if constexpr (EPI == EPI_QKV) {
         const int hd = e.head_dim;
-        int sec, lt;
-        if (tile < e.n_q_tiles) { sec = 0; lt = tile; }
-        else if (tile < e.n_q_tiles + e.n_k_tiles) { sec = 1; lt = tile - e.n_q_tiles; }
-        else { sec = 2; lt = tile - e.n_q_tiles - e.n_k_tiles; }
+        int lt;
+        if (tile < e.n_q_tiles) { r.sec = 0; lt = tile; }
+        else if (tile < e.n_q_tiles + e.n_k_tiles) { r.sec = 1; lt = tile - e.n_q_tiles; }
+        else { r.sec = 2; lt = tile - e.n_q_tiles - e.n_k_tiles; }
         const int fl = lt * 128 + row;
-        const int sec_off = sec == 0 ? 0 : sec == 1 ? e.n_q_tiles * 128 : (e.n_q_tiles + e.n_k_tiles) * 128;
-        const int p = valid ? e.pos[tok] : 0;
-        if (sec < 2) {
+        const int sec_off = r.sec == 0 ? 0 : r.sec == 1 ? e.n_q_tiles * 128 : (e.n_q_tiles + e.n_k_tiles) * 128;
+        if (r.sec < 2) {
             // rows permuted within each head: local 2i+b <-> feature i + b*hd/2 (NEOX pairs)
-            const int head = fl / hd, rr = fl % hd, i = rr >> 1, b = rr & 1;
-            const int orig = head * hd + i + b * (hd >> 1);
-            if (e.bias) v += e.bias[sec_off + orig];
-            const float partner = __shfl_xor_sync(0xffffffffu, v, 1);
-            const float2 cs = e.rope[(size_t)p * (hd >> 1) + i];
-            const float o = b == 0 ? (v * cs.x - partner * cs.y) : (partner * cs.y + v * cs.x);
-            if (valid) {
-                if (sec == 0) {
-                    if (orig < e.n_q) e.q_out[(size_t)tok * e.ld_q + orig] = __float2half_rn(o);
-                } else {
-                    if (orig < e.n_kv) e.k_cache[(size_t)p * e.ld_kv + orig] = __float2half_rn(o);
+            const int head = fl / hd, rr = fl % hd;
+            r.ipair = rr >> 1;
+            r.bpair = rr & 1;
+            r.f = head * hd + r.ipair + r.bpair * (hd >> 1);
+        } else {
+            r.f = fl;
+        }
+        r.fvalid = r.f < (r.sec == 0 ? e.n_q : e.n_kv);
+        r.bias = e.bias ? __ldg(e.bias + sec_off + r.f) : 0.f;
+        r.writer = true;
+    } else {
+        r.f = tile * 128 + row;
+        r.fvalid = r.f < e.n_valid;
+        r.writer = true;
+    }
+    return r;
+}
+
+// Epilogue of 16 consecutive tokens (tl0 .. tl0+15 of the segment) for this lane's row.
+// All global loads of a chunk are issued before any store, so they overlap.  Called
+// by all 32 lanes of a warp together (paired epilogues exchange values with the
+// neighbouring lane).  s_pos: positions of the segment's tokens (shared memory).
+template <int EPI>
+__device__ __forceinline__ void epi_chunk(const EpiArgs &e, const EpiRow &r, const int *s_pos, int m0, int tl0,
+                                          int ntok, float (&v)[16]) {
+    if constexpr (EPI == EPI_F32 || EPI == EPI_F16) {
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+            if (tl0 + i < ntok && r.fvalid) {
+                const size_t o = (size_t)(m0 + tl0 + i) * e.ld + r.f;
+                if constexpr (EPI == EPI_F32) reinterpret_cast<float *>(e.out)[o] = v[i];
+                else reinterpret_cast<__half *>(e.out)[o] = __float2half_rn(v[i]);
+            }
+        }
+    } else if constexpr (EPI == EPI_RESID) {
+        float *x = reinterpret_cast<float *>(e.out);
+        float old[16];
+#pragma unroll
+        for (int i = 0; i < 16; i++)
+            old[i] = (tl0 + i < ntok && r.fvalid) ? x[(size_t)(m0 + tl0 + i) * e.ld + r.f] : 0.f;
+#pragma unroll
+        for (int i = 0; i < 16; i++)
+            if (tl0 + i < ntok && r.fvalid) x[(size_t)(m0 + tl0 + i) * e.ld + r.f] = v[i] + old[i];
+    } else if constexpr (EPI == EPI_LOGITS) {
+#pragma unroll
+        for (int i = 0; i < 16; i++)
+            if (tl0 + i < ntok && r.fvalid)
+                reinterpret_cast<float *>(e.out)[(size_t)s_pos[tl0 + i] * e.ld + r.f] = v[i];
+    } else if constexpr (EPI == EPI_SWIGLU) {
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+            const float up = __shfl_xor_sync(0xffffffffu, v[i], 1);
+            if (r.writer && tl0 + i < ntok && r.fvalid)
+                reinterpret_cast<__half *>(e.out)[(size_t)(m0 + tl0 + i) * e.ld + r.f] =
+                    __float2half_rn(silu_f(v[i]) * up);
+        }
+    } else if constexpr (EPI == EPI_QKV) {
+        const int hh = e.head_dim >> 1;
+        if (r.sec < 2) {
+            float2 cs[16];
+#pragma unroll
+            for (int i = 0; i < 16; i++) {
+                const int p = tl0 + i < ntok ? s_pos[tl0 + i] : 0;
+                cs[i] = __ldg(e.rope + (size_t)p * hh + r.ipair);
+            }
+#pragma unroll
+            for (int i = 0; i < 16; i++) {
+                const float x = v[i] + r.bias;
+                const float partner = __shfl_xor_sync(0xffffffffu, x, 1);
+                const float o = r.bpair == 0 ? (x * cs[i].x - partner * cs[i].y) : (partner * cs[i].y + x * cs[i].x);
+                if (tl0 + i < ntok && r.fvalid) {
+                    if (r.sec == 0) e.q_out[(size_t)(m0 + tl0 + i) * e.ld_q + r.f] = __float2half_rn(o);
+                    else e.k_cache[(size_t)s_pos[tl0 + i] * e.ld_kv + r.f] = __float2half_rn(o);
                 }
             }
         } else {
-            if (e.bias) v += e.bias[sec_off + fl];
-            if (valid && fl < e.n_kv) e.v_cache[(size_t)p * e.ld_kv + fl] = __float2half_rn(v);
+#pragma unroll
+            for (int i = 0; i < 16; i++)
+                if (tl0 + i < ntok && r.fvalid)
+                    e.v_cache[(size_t)s_pos[tl0 + i] * e.ld_kv + r.f] = __float2half_rn(v[i] + r.bias);
         }
     }
 }
@@ -359,6 +416,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 19);
     int *bcast = reinterpret_cast<int *>(bars + 20);
     volatile int *okflag = reinterpret_cast<volatile int *>(bars + 21);
+    int *s_pos = reinterpret_cast<int *>(bars + 32);                              // [kMaxTok]
+    long long *s_contrib = reinterpret_cast<long long *>(s_pos + kMaxTok);        // [kMaxContrib]
 
     const int M = *p.m_dev;
     if (M <= 0) return;
@@ -560,16 +619,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const uint32_t taddr = tmem_base + ((uint32_t)(32 * q) << 16) + acc * 256;
             const bool whole = g.k0 == 0 && g.k1 == S.kb;
+            const EpiRow er = epi_row<EPI>(p.epi, g.tile, row);
+            if constexpr (EPI == EPI_QKV || EPI == EPI_LOGITS) {
+                for (int t = et; t < g.ntok; t += 128) s_pos[t] = p.epi.pos[g.m0 + t];
+                named_bar_sync(1, 128);
+            }
             if (whole) {
                 for (int c0 = 0; c0 < g.nmma; c0 += 16) {
-                    uint32_t v[16];
-                    tmem_ld16(taddr + c0, v);
+                    uint32_t u[16];
+                    tmem_ld16(taddr + c0, u);
                     tmem_ld_wait();
+                    float v[16];
 #pragma unroll
-                    for (int i = 0; i < 16; i++) {
-                        const int tl = c0 + i;
-                        epi_apply<EPI>(p.epi, g.tile, row, g.m0 + tl, tl < g.ntok, __uint_as_float(v[i]));
-                    }
+                    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(u[i]);
+                    epi_chunk<EPI>(p.epi, er, s_pos, g.m0, c0, g.ntok, v);
                 }
                 tc_fence_before();
                 __syncwarp();
@@ -578,11 +641,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int slot = g.ot == first_ot ? 0 : 1;
                 float *wsl = p.ws + ((size_t)blockIdx.x * 2 + slot) * kWsTile;
                 for (int c0 = 0; c0 < g.nmma; c0 += 16) {
-                    uint32_t v[16];
-                    tmem_ld16(taddr + c0, v);
+                    uint32_t u[16];
+                    tmem_ld16(taddr + c0, u);
                     tmem_ld_wait();
 #pragma unroll
-                    for (int i = 0; i < 16; i++) wsl[(size_t)(c0 + i) * 128 + row] = __uint_as_float(v[i]);
+                    for (int i = 0; i < 16; i++) wsl[(size_t)(c0 + i) * 128 + row] = __uint_as_float(u[i]);
                 }
                 tc_fence_before();
                 __syncwarp();
@@ -590,24 +653,33 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __threadfence();
                 named_bar_sync(1, 128);
                 const int c_first = S.owner(g.ot * S.kb), c_last = S.owner((g.ot + 1) * S.kb - 1);
+                const int nc = c_last - c_first + 1;
                 if (et == 0) {
                     const int old = atomicAdd(&p.tile_cnt[g.ot], 1);
-                    *bcast = (old == c_last - c_first) ? 1 : 0;
+                    *bcast = (old == nc - 1) ? 1 : 0;
+                    if (nc > kMaxContrib) atomicCAS(p.err, 0, kErrTimeout + 9);  // launcher keeps nc <= kMaxContrib
+                }
+                if (et < nc && et < kMaxContrib) {
+                    const int c = c_first + et;
+                    const int sl = (S.begin_of(c) / S.kb == g.ot) ? 0 : 1;
+                    s_contrib[et] = ((long long)c * 2 + sl) * kWsTile;
                 }
                 named_bar_sync(1, 128);
-                if (*bcast) {
+                if (*bcast && nc <= kMaxContrib) {
                     __threadfence();
                     for (int c0 = 0; c0 < g.nmma; c0 += 16) {
+                        float v[16];
 #pragma unroll
-                        for (int i = 0; i < 16; i++) {
-                            float sum = 0.f;
-                            for (int c = c_first; c <= c_last; c++) {
-                                const int sl = (S.begin_of(c) / S.kb == g.ot) ? 0 : 1;
-                                sum += __ldcg(p.ws + ((size_t)c * 2 + sl) * kWsTile + (size_t)(c0 + i) * 128 + row);
-                            }
-                            const int tl = c0 + i;
-                            epi_apply<EPI>(p.epi, g.tile, row, g.m0 + tl, tl < g.ntok, sum);
+                        for (int i = 0; i < 16; i++) v[i] = 0.f;
+                        for (int c = 0; c < nc; c++) {
+                            const float *src = p.ws + s_contrib[c] + (size_t)c0 * 128 + row;
+                            float t[16];
+#pragma unroll
+                            for (int i = 0; i < 16; i++) t[i] = __ldcg(src + i * 128);
+#pragma unroll
+                            for (int i = 0; i < 16; i++) v[i] += t[i];
                         }
+                        epi_chunk<EPI>(p.epi, er, s_pos, g.m0, c0, g.ntok, v);
                     }
                     if (et == 0) p.tile_cnt[g.ot] = 0;
                 }
