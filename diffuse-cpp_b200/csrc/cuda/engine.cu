@@ -55,6 +55,17 @@ static int set_err(int code, const char *fmt, ...) {
 
 extern "C" const char *dfb_last_error(void) { return g_err.c_str(); }
 
+#ifdef DFB_GEMM_TRACE
+unsigned long long *g_dfb_trace = nullptr;
+int g_dfb_trace_launch = 0;
+// Copies the phase stamps of the most recent GEMM launch ([grid][16] u64) to the host.
+extern "C" int dfb_debug_gemm_trace(unsigned long long *host) {  // [64][256][16]
+    if (!g_dfb_trace) return -1;
+    cudaDeviceSynchronize();
+    return cudaMemcpy(host, g_dfb_trace, sizeof(unsigned long long) * (16 * 256 + 4 * 8 * 64) * 64, cudaMemcpyDeviceToHost) == cudaSuccess ? 0 : -1;
+}
+#endif
+
 extern "C" int dfb_device_count(int *n) {
     if (!n) return set_err(DFB_ERR_ARG, "null pointer");
     cudaError_t e = cudaGetDeviceCount(n);
@@ -659,6 +670,17 @@ static int launch_gemm_t(dfb_ctx *c, const WMat &w, const CUtensorMap &tm_x, con
     p.tile_cnt = c->tile_cnt;
     p.err = c->err;
     p.epi = epi;
+#ifdef DFB_GEMM_TRACE
+    // analysis builds: stamp the last GEMM launch of each step into a per-context buffer
+    // launch i of the process stamps slice i % 64 of a [64][256][16] buffer
+    extern unsigned long long *g_dfb_trace;
+    extern int g_dfb_trace_launch;
+    if (!g_dfb_trace) {
+        cudaMalloc(&g_dfb_trace, sizeof(unsigned long long) * (16 * 256 + 4 * 8 * 64) * 64);
+        cudaMemset(g_dfb_trace, 0, sizeof(unsigned long long) * (16 * 256 + 4 * 8 * 64) * 64);
+    }
+    p.trace = g_dfb_trace + (size_t)(g_dfb_trace_launch++ % 64) * (256 * 16 + 4 * 8 * 64);
+#endif
     cudaEvent_t ev0 = nullptr;
     prof_begin(c, &ev0);
     // A tile is split over at most grid/n_tiles + 2 CTAs; keep that within kMaxContrib.

@@ -17,8 +17,10 @@
 // depend on timing) and applies the epilogue.  The token count M is read on the
 // device, so one launch configuration serves every denoising step.
 //
-// Warp roles (320 threads): w0 TMA producer, w1 MMA issuer + TMEM owner,
-// w2-w5 dequantizers (thread = weight row), w6-w9 epilogue (thread = TMEM lane).
+// Warp roles (480 threads): w0 activation TMA producer, w1 MMA issuer + TMEM owner,
+// w2-w5 dequantizers (thread = weight row), w6-w9 and w11-w14 epilogue (thread = TMEM
+// lane; the two warps of a lane quarter take alternate 16-column chunks), w10
+// weight-chunk producer (bulk copies into shared memory, L2 prefetch ahead).
 #pragma once
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -26,6 +28,23 @@
 #include "ptx.cuh"
 
 namespace dfb {
+
+// Per-CTA phase timestamps for pipeline analysis (compiled in only with -DDFB_GEMM_TRACE).
+#ifdef DFB_GEMM_TRACE
+#define GEMM_STAMP(p, slot)                                                                      \
+    do {                                                                                         \
+        if ((p).trace) (p).trace[(size_t)blockIdx.x * 16 + (slot)] = globaltimer();              \
+    } while (0)
+// Event streams of CTAs 0..3: stream s, event i -> trace[256*16 + (cta*8 + s)*64 + i].
+#define GEMM_EVENT(p, stream, idx)                                                               \
+    do {                                                                                         \
+        if ((p).trace && blockIdx.x < 4 && (idx) < 64)                                           \
+            (p).trace[256 * 16 + ((size_t)blockIdx.x * 8 + (stream)) * 64 + (idx)] = globaltimer(); \
+    } while (0)
+#else
+#define GEMM_STAMP(p, slot) do {} while (0)
+#define GEMM_EVENT(p, stream, idx) do {} while (0)
+#endif
 
 enum WType : int { W_Q4K = 0, W_Q6K = 1, W_Q80 = 2, W_F16 = 3 };
 enum EpiKind : int { EPI_F32 = 0, EPI_F16 = 1, EPI_RESID = 2, EPI_QKV = 3, EPI_SWIGLU = 4, EPI_LOGITS = 5 };
@@ -59,10 +78,13 @@ struct GemmParams {
     float *ws = nullptr;         // split-tile partials [grid][2][256 * 128]
     int *tile_cnt = nullptr;     // [n_tiles * 2] arrival counters, left at 0
     int *err = nullptr;          // first error code of any CTA
+    unsigned long long *trace = nullptr;  // DFB_GEMM_TRACE builds only: [grid][16] globaltimer stamps
     EpiArgs epi;
 };
 
-constexpr int kThreads = 320;
+constexpr int kThreads = 480;
+constexpr int kEpiThreads = 256;  // two epilogue warps per TMEM lane quarter
+constexpr int kPrefetchChunks = 6;  // weight chunks warmed in L2 ahead of the smem copy
 constexpr int kStages = 3;
 constexpr int kRawStages = 2;
 constexpr int kABytes = 128 * 128;       // 128 rows x 64 f16
@@ -73,6 +95,7 @@ constexpr int kWsTile = kMaxTok * 128;   // floats per partial tile
 constexpr int kErrTimeout = 0x100;
 
 constexpr int kMaxContrib = 64;  // split contributors of one tile tracked in shared memory
+constexpr int kFixupPeers = (kStages * kStageBytes) / 32768;  // partial chunks the stage buffers hold
 __host__ __device__ constexpr int gemm_smem_bytes(int wt) {
     return 1024 /*align slack*/ + kStages * kStageBytes + kRawStages * raw_chunk_bytes(wt) + 256 /*barriers*/ +
            4 * kMaxTok /*token positions*/ + 8 * kMaxContrib /*contributor partial offsets*/;
@@ -285,7 +308,6 @@ __device__ __forceinline__ void q80_slice(const uint8_t *R, int r, int s, uint8_
 }
 
 // ───────────── epilogues ─────────────
-__device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
 
 // Per-thread constants of one output tile (thread = TMEM lane = one output row).
 struct EpiRow {
@@ -341,36 +363,37 @@ __device__ __forceinline__ EpiRow epi_row(const EpiArgs &e, int tile, int row) {
 template <int EPI>
 __device__ __forceinline__ void epi_chunk(const EpiArgs &e, const EpiRow &r, const int *s_pos, int m0, int tl0,
                                           int ntok, float (&v)[16]) {
+    const int nvalid = r.fvalid ? min(16, ntok - tl0) : 0;  // tokens of this chunk that are stored
     if constexpr (EPI == EPI_F32 || EPI == EPI_F16) {
+        const size_t base = (size_t)(m0 + tl0) * e.ld + r.f;
 #pragma unroll
         for (int i = 0; i < 16; i++) {
-            if (tl0 + i < ntok && r.fvalid) {
-                const size_t o = (size_t)(m0 + tl0 + i) * e.ld + r.f;
-                if constexpr (EPI == EPI_F32) reinterpret_cast<float *>(e.out)[o] = v[i];
-                else reinterpret_cast<__half *>(e.out)[o] = __float2half_rn(v[i]);
+            if (i < nvalid) {
+                if constexpr (EPI == EPI_F32) reinterpret_cast<float *>(e.out)[base + (size_t)i * e.ld] = v[i];
+                else reinterpret_cast<__half *>(e.out)[base + (size_t)i * e.ld] = __float2half_rn(v[i]);
             }
         }
     } else if constexpr (EPI == EPI_RESID) {
-        float *x = reinterpret_cast<float *>(e.out);
+        float *x = reinterpret_cast<float *>(e.out) + (size_t)(m0 + tl0) * e.ld + r.f;
         float old[16];
 #pragma unroll
-        for (int i = 0; i < 16; i++)
-            old[i] = (tl0 + i < ntok && r.fvalid) ? x[(size_t)(m0 + tl0 + i) * e.ld + r.f] : 0.f;
+        for (int i = 0; i < 16; i++) old[i] = i < nvalid ? x[(size_t)i * e.ld] : 0.f;
 #pragma unroll
         for (int i = 0; i < 16; i++)
-            if (tl0 + i < ntok && r.fvalid) x[(size_t)(m0 + tl0 + i) * e.ld + r.f] = v[i] + old[i];
+            if (i < nvalid) x[(size_t)i * e.ld] = v[i] + old[i];
     } else if constexpr (EPI == EPI_LOGITS) {
+        float *out = reinterpret_cast<float *>(e.out) + r.f;
 #pragma unroll
         for (int i = 0; i < 16; i++)
-            if (tl0 + i < ntok && r.fvalid)
-                reinterpret_cast<float *>(e.out)[(size_t)s_pos[tl0 + i] * e.ld + r.f] = v[i];
+            if (i < nvalid) out[(size_t)s_pos[tl0 + i] * e.ld] = v[i];
     } else if constexpr (EPI == EPI_SWIGLU) {
+        __half *out = reinterpret_cast<__half *>(e.out) + (size_t)(m0 + tl0) * e.ld + r.f;
 #pragma unroll
         for (int i = 0; i < 16; i++) {
             const float up = __shfl_xor_sync(0xffffffffu, v[i], 1);
-            if (r.writer && tl0 + i < ntok && r.fvalid)
-                reinterpret_cast<__half *>(e.out)[(size_t)(m0 + tl0 + i) * e.ld + r.f] =
-                    __float2half_rn(silu_f(v[i]) * up);
+            const float g = v[i];
+            const float h = g * up * (1.0f / (1.0f + __expf(-g)));
+            if (r.writer && i < nvalid) out[(size_t)i * e.ld] = __float2half_rn(h);
         }
     } else if constexpr (EPI == EPI_QKV) {
         const int hh = e.head_dim >> 1;
@@ -378,15 +401,15 @@ __device__ __forceinline__ void epi_chunk(const EpiArgs &e, const EpiRow &r, con
             float2 cs[16];
 #pragma unroll
             for (int i = 0; i < 16; i++) {
-                const int p = tl0 + i < ntok ? s_pos[tl0 + i] : 0;
-                cs[i] = __ldg(e.rope + (size_t)p * hh + r.ipair);
+                const int pp = tl0 + i < ntok ? s_pos[tl0 + i] : 0;
+                cs[i] = __ldg(e.rope + (size_t)pp * hh + r.ipair);
             }
 #pragma unroll
             for (int i = 0; i < 16; i++) {
                 const float x = v[i] + r.bias;
                 const float partner = __shfl_xor_sync(0xffffffffu, x, 1);
                 const float o = r.bpair == 0 ? (x * cs[i].x - partner * cs[i].y) : (partner * cs[i].y + x * cs[i].x);
-                if (tl0 + i < ntok && r.fvalid) {
+                if (i < nvalid) {
                     if (r.sec == 0) e.q_out[(size_t)(m0 + tl0 + i) * e.ld_q + r.f] = __float2half_rn(o);
                     else e.k_cache[(size_t)s_pos[tl0 + i] * e.ld_kv + r.f] = __float2half_rn(o);
                 }
@@ -394,8 +417,7 @@ __device__ __forceinline__ void epi_chunk(const EpiArgs &e, const EpiRow &r, con
         } else {
 #pragma unroll
             for (int i = 0; i < 16; i++)
-                if (tl0 + i < ntok && r.fvalid)
-                    e.v_cache[(size_t)s_pos[tl0 + i] * e.ld_kv + r.f] = __float2half_rn(v[i] + r.bias);
+                if (i < nvalid) e.v_cache[(size_t)s_pos[tl0 + i] * e.ld_kv + r.f] = __float2half_rn(v[i] + r.bias);
         }
     }
 }
@@ -416,11 +438,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 19);
     int *bcast = reinterpret_cast<int *>(bars + 20);
     volatile int *okflag = reinterpret_cast<volatile int *>(bars + 21);
+    uint64_t *fix_bar = bars + 22;  // bulk loads of split-tile partials into the drained stage buffers
     int *s_pos = reinterpret_cast<int *>(bars + 32);                              // [kMaxTok]
     long long *s_contrib = reinterpret_cast<long long *>(s_pos + kMaxTok);        // [kMaxContrib]
 
     const int M = *p.m_dev;
     if (M <= 0) return;
+    if (threadIdx.x == 0) GEMM_STAMP(p, 0);
     Sched S;
     S.init(M, p.n_tiles, p.kb, gridDim.x, blockIdx.x);
     if ((int)blockIdx.x >= S.G) return;
@@ -436,9 +460,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&raw_full[i], 1);
             mbar_init(&raw_empty[i], 4);
             mbar_init(&acc_full[i], 1);
-            mbar_init(&acc_empty[i], 4);
+            mbar_init(&acc_empty[i], kEpiThreads / 32);  // one arrival per epilogue warp
         }
         mbar_init(drain, 1);
+        mbar_init(fix_bar, 1);
         *abort_flag = 0;
         fence_barrier_init();
     }
@@ -454,22 +479,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_holder;
+    if (threadIdx.x == 0) GEMM_STAMP(p, 1);
 
     if (warp == 0) {
-        // ── TMA producer ──
+        // ── activation TMA producer ──
         if (lane == 0) {
-            int it = 0, rit = 0;
+            int it = 0;
             bool ok = true;
             for (int u = S.u0; u < S.u1 && ok;) {
                 const Seg g = make_seg(S, u, S.u1);
                 for (int kbi = g.k0; kbi < g.k1 && ok; kbi++) {
-                    if constexpr (WT != W_F16) {
-                        const int r = rit % kRawStages;
-                        if (!(ok = mbar_wait(&raw_empty[r], ((rit / kRawStages) & 1) ^ 1, abort_flag, p.err, kErrTimeout + 1))) break;
-                        mbar_arrive_expect_tx(&raw_full[r], RAWB);
-                        bulk_g2s(raw + r * RAWB, p.w + ((size_t)g.tile * p.kb + kbi) * RAWB, RAWB, &raw_full[r]);
-                        rit++;
-                    }
                     for (int s = 0; s < 4; s++) {
                         const int st = it % kStages;
                         if (!(ok = mbar_wait(&empty[st], ((it / kStages) & 1) ^ 1, abort_flag, p.err, kErrTimeout + 2))) break;
@@ -479,19 +498,46 @@ __global__ void __launch_bounds__(kThreads, 1)
                         mbar_arrive_expect_tx(&full_b[st], bytes);
                         for (int b = 0; b < g.nbox; b++)
                             tma_load_2d(B + b * 8192, &tm_x, kbi * 256 + s * 64, g.m0 + b * 64, &full_b[st]);
+                        GEMM_EVENT(p, 0, it);
                         if constexpr (WT == W_F16) tma_load_2d(A, &tm_w, kbi * 256 + s * 64, g.tile * 128, &full_b[st]);
                         it++;
                     }
                 }
                 u += g.k1 - g.k0;
             }
+            GEMM_STAMP(p, 2);
             if (!ok) {
                 // let every copy this thread started land before the CTA exits
                 for (int i = (it > kStages ? it - kStages : 0); i < it; i++)
                     spin_bounded(&full_b[i % kStages], (i / kStages) & 1);
-                for (int i = (rit > kRawStages ? rit - kRawStages : 0); i < rit; i++)
-                    spin_bounded(&raw_full[i % kRawStages], (i / kRawStages) & 1);
             }
+        }
+        __syncwarp();
+    } else if (warp == 10) {
+        // ── weight-chunk producer: one re-tiled chunk (128 rows x 256 k) per k-block ──
+        if constexpr (WT != W_F16) {
+            if (lane == 0) {
+                auto chunk = [&](int u) {
+                    const int ot = u / S.kb, kbi = u % S.kb;
+                    return p.w + ((size_t)(ot / S.n_mg) * p.kb + kbi) * RAWB;
+                };
+                for (int u = S.u0; u < S.u1 && u < S.u0 + kPrefetchChunks; u++) bulk_prefetch_l2(chunk(u), RAWB);
+                int rit = 0;
+                bool ok = true;
+                for (int u = S.u0; u < S.u1 && ok; u++) {
+                    const int r = rit % kRawStages;
+                    if (!(ok = mbar_wait(&raw_empty[r], ((rit / kRawStages) & 1) ^ 1, abort_flag, p.err, kErrTimeout + 1))) break;
+                    if (u + kPrefetchChunks < S.u1) bulk_prefetch_l2(chunk(u + kPrefetchChunks), RAWB);
+                    mbar_arrive_expect_tx(&raw_full[r], RAWB);
+                    bulk_g2s(raw + r * RAWB, chunk(u), RAWB, &raw_full[r]);
+                    GEMM_EVENT(p, 1, rit);
+                    rit++;
+                }
+                if (!ok)
+                    for (int i = (rit > kRawStages ? rit - kRawStages : 0); i < rit; i++)
+                        spin_bounded(&raw_full[i % kRawStages], (i / kRawStages) & 1);
+            }
+            __syncwarp();
         }
     } else if (warp == 1) {
         // ── MMA issuer ──
@@ -513,6 +559,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (!(ok = mbar_wait(&full_b[st], ph, abort_flag, p.err, kErrTimeout + 4))) break;
                         if constexpr (WT != W_F16)
                             if (!(ok = mbar_wait(&full_a[st], ph, abort_flag, p.err, kErrTimeout + 5))) break;
+                        GEMM_EVENT(p, 4, it);
                         tc_fence_after();
                         const uint32_t a_addr = smem_u32(stages + st * kStageBytes);
                         const uint32_t b_addr = a_addr + kABytes;
@@ -523,6 +570,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                         issued = true;
                         mma_commit(&empty[st]);
+                        GEMM_EVENT(p, 5, it);
                         it++;
                     }
                 }
@@ -531,12 +579,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 si++;
                 u += g.k1 - g.k0;
             }
+            GEMM_STAMP(p, 3);
             if (issued) {
                 // every MMA must have retired before TMEM is released
                 mma_commit(drain);
                 spin_bounded(drain, 0);
             }
         }
+        __syncwarp();
     } else if (warp < 6) {
         // ── dequantizers: thread = weight row of the tile ──
         if constexpr (WT != W_F16) {
@@ -549,6 +599,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const int rs = rit % kRawStages;
                     ok = __all_sync(0xffffffffu, mbar_wait(&raw_full[rs], (rit / kRawStages) & 1, abort_flag, p.err, kErrTimeout + 6));
                     if (!ok) break;
+                    if (r == 0) GEMM_EVENT(p, 2, rit);
                     const uint8_t *R = raw + rs * RAWB;
                     if constexpr (WT == W_Q4K) {
                         Q4KRow meta;
@@ -562,6 +613,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             fence_proxy_async_smem();
                             __syncwarp();
                             if (lane == 0) mbar_arrive(&full_a[st]);
+                            if (r == 0) GEMM_EVENT(p, 3, it);
                             it++;
                         }
                     } else if constexpr (WT == W_Q6K) {
@@ -604,7 +656,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ── epilogue: thread = TMEM lane = output feature ──
         const int q = warp & 3;
         const int row = 32 * q + lane;
-        const int et = threadIdx.x - 192;  // 0..127
+        const int half = warp >= 11 ? 1 : 0;
+        const int et = half ? 128 + (int)threadIdx.x - 352 : (int)threadIdx.x - 192;  // 0..255
+        uint32_t fix_phase = 0;
         int si = 0;
         bool ok = true;
         const int first_ot = S.begin_of(blockIdx.x) / S.kb;
@@ -613,78 +667,137 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int acc = si & 1;
             // one thread waits, the barrier hands the outcome to the whole group
             if (et == 0) *okflag = mbar_wait(&acc_full[acc], (si >> 1) & 1, abort_flag, p.err, kErrTimeout + 8) ? 1 : 0;
-            named_bar_sync(1, 128);
+            named_bar_sync(1, kEpiThreads);
             ok = *okflag != 0;
             if (!ok) break;
+            if (et == 0 && si < 4) GEMM_STAMP(p, 4 + 2 * si);
             tc_fence_after();
             const uint32_t taddr = tmem_base + ((uint32_t)(32 * q) << 16) + acc * 256;
             const bool whole = g.k0 == 0 && g.k1 == S.kb;
             const EpiRow er = epi_row<EPI>(p.epi, g.tile, row);
             if constexpr (EPI == EPI_QKV || EPI == EPI_LOGITS) {
-                for (int t = et; t < g.ntok; t += 128) s_pos[t] = p.epi.pos[g.m0 + t];
-                named_bar_sync(1, 128);
+                for (int t = et; t < g.ntok; t += kEpiThreads) s_pos[t] = p.epi.pos[g.m0 + t];
+                named_bar_sync(1, kEpiThreads);
             }
-            if (whole) {
-                for (int c0 = 0; c0 < g.nmma; c0 += 16) {
-                    uint32_t u[16];
-                    tmem_ld16(taddr + c0, u);
-                    tmem_ld_wait();
-                    float v[16];
-#pragma unroll
-                    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(u[i]);
-                    epi_chunk<EPI>(p.epi, er, s_pos, g.m0, c0, g.ntok, v);
-                }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&acc_empty[acc]);
-            } else {
+            // mode 0: whole tile straight from TMEM; 1: finisher with the other partials
+            // bulk-staged in the drained stage buffers; 2: finisher reading partials from L2;
+            // 3: not the finisher (nothing to emit)
+            int mode = 0, nc = 1, me = 0;
+            const bool last_seg = u + (g.k1 - g.k0) == S.u1;  // stage buffers drained after this one
+            if (!whole) {
+                // Split tile.  Partials are stored [64-column chunk][column][row] (32 KB per
+                // chunk, coalesced for the writers, bank-conflict-free in shared memory).
                 const int slot = g.ot == first_ot ? 0 : 1;
                 float *wsl = p.ws + ((size_t)blockIdx.x * 2 + slot) * kWsTile;
-                for (int c0 = 0; c0 < g.nmma; c0 += 16) {
-                    uint32_t u[16];
-                    tmem_ld16(taddr + c0, u);
+                if (et == 0) GEMM_EVENT(p, 6, 5 * si + 0);
+                for (int c0 = 16 * half; c0 < g.nmma; c0 += 32) {
+                    uint32_t u16[16];
+                    tmem_ld16(taddr + c0, u16);
                     tmem_ld_wait();
+                    float *dst = wsl + (size_t)(c0 >> 6) * 8192 + (size_t)(c0 & 63) * 128 + row;
 #pragma unroll
-                    for (int i = 0; i < 16; i++) wsl[(size_t)(c0 + i) * 128 + row] = __uint_as_float(u[i]);
+                    for (int i = 0; i < 16; i++) dst[i * 128] = __uint_as_float(u16[i]);
                 }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&acc_empty[acc]);
                 __threadfence();
-                named_bar_sync(1, 128);
+                named_bar_sync(1, kEpiThreads);
                 const int c_first = S.owner(g.ot * S.kb), c_last = S.owner((g.ot + 1) * S.kb - 1);
-                const int nc = c_last - c_first + 1;
+                nc = c_last - c_first + 1;
+                me = blockIdx.x - c_first;
                 if (et == 0) {
                     const int old = atomicAdd(&p.tile_cnt[g.ot], 1);
                     *bcast = (old == nc - 1) ? 1 : 0;
                     if (nc > kMaxContrib) atomicCAS(p.err, 0, kErrTimeout + 9);  // launcher keeps nc <= kMaxContrib
                 }
-                if (et < nc && et < kMaxContrib) {
+                if (et < nc && et < kMaxContrib) {  // (et < kEpiThreads covers kMaxContrib)
                     const int c = c_first + et;
                     const int sl = (S.begin_of(c) / S.kb == g.ot) ? 0 : 1;
                     s_contrib[et] = ((long long)c * 2 + sl) * kWsTile;
                 }
-                named_bar_sync(1, 128);
-                if (*bcast && nc <= kMaxContrib) {
+                named_bar_sync(1, kEpiThreads);
+                if (et == 0) GEMM_EVENT(p, 6, 5 * si + 3);
+                if (!*bcast || nc > kMaxContrib) mode = 3;
+                else {
                     __threadfence();
-                    for (int c0 = 0; c0 < g.nmma; c0 += 16) {
-                        float v[16];
+                    mode = (last_seg && nc - 1 <= kFixupPeers) ? 1 : 2;
+                }
+            }
+            if (mode >= 2) {
+                // the accumulator is in the workspace: let the MMA warp reuse the TMEM buffer
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[acc]);
+            }
+            if (mode != 3) {
+                const float *sbuf = reinterpret_cast<const float *>(stages);
+                bool staged_ok = true;
+                for (int cb = 0; cb < g.nmma && staged_ok; cb += 64) {
+                    if (mode == 1) {
+                        // stage this 64-column chunk of every other contributor
+                        const int cols = min(64, g.nmma - cb);
+                        named_bar_sync(1, kEpiThreads);  // the previous chunk's buffers are consumed
+                        if (et == 0) {
+                            fence_proxy_async_smem();
+                            mbar_arrive_expect_tx(fix_bar, (uint32_t)(nc - 1) * cols * 512);
+                            for (int c = 0, k = 0; c < nc; c++) {
+                                if (c == me) continue;
+                                bulk_g2s(stages + (size_t)k * 32768, p.ws + s_contrib[c] + (size_t)(cb >> 6) * 8192,
+                                         (uint32_t)cols * 512, fix_bar);
+                                k++;
+                            }
+                            *okflag = mbar_wait(fix_bar, fix_phase, abort_flag, p.err, kErrTimeout + 10) ? 1 : 0;
+                        }
+                        fix_phase ^= 1;
+                        named_bar_sync(1, kEpiThreads);
+                        if (!*okflag) { staged_ok = false; break; }
+                    }
+                  for (int c0 = cb + 16 * half; c0 < min(cb + 64, g.nmma); c0 += 32) {
+                    float v[16];
+                    if (mode <= 1) {
+                        uint32_t u16[16];
+                        tmem_ld16(taddr + c0, u16);
+                        tmem_ld_wait();
 #pragma unroll
-                        for (int i = 0; i < 16; i++) v[i] = 0.f;
-                        for (int c = 0; c < nc; c++) {
-                            const float *src = p.ws + s_contrib[c] + (size_t)c0 * 128 + row;
+                        for (int i = 0; i < 16; i++) v[i] = __uint_as_float(u16[i]);
+                    }
+                    if (mode >= 1) {
+                        // ordered sum over contributors: the result does not depend on timing
+                        float own[16];
+#pragma unroll
+                        for (int i = 0; i < 16; i++) { own[i] = v[i]; v[i] = 0.f; }
+                        for (int c = 0, k = 0; c < nc; c++) {
                             float t[16];
+                            if (mode == 1 && c == me) {
 #pragma unroll
-                            for (int i = 0; i < 16; i++) t[i] = __ldcg(src + i * 128);
+                                for (int i = 0; i < 16; i++) t[i] = own[i];
+                            } else if (mode == 1) {
+                                const float *src = sbuf + (size_t)k * 8192 + (size_t)(c0 & 63) * 128 + row;
+#pragma unroll
+                                for (int i = 0; i < 16; i++) t[i] = src[i * 128];
+                                k++;
+                            } else {
+                                const float *src = p.ws + s_contrib[c] + (size_t)(c0 >> 6) * 8192 + (size_t)(c0 & 63) * 128 + row;
+#pragma unroll
+                                for (int i = 0; i < 16; i++) t[i] = __ldcg(src + i * 128);
+                            }
 #pragma unroll
                             for (int i = 0; i < 16; i++) v[i] += t[i];
                         }
-                        epi_chunk<EPI>(p.epi, er, s_pos, g.m0, c0, g.ntok, v);
                     }
-                    if (et == 0) p.tile_cnt[g.ot] = 0;
+                    epi_chunk<EPI>(p.epi, er, s_pos, g.m0, c0, g.ntok, v);
+                  }
+                }
+                if (mode >= 1 && et == 0) {
+                    p.tile_cnt[g.ot] = 0;
+                    GEMM_EVENT(p, 6, 5 * si + 4);
                 }
             }
-            named_bar_sync(1, 128);  // okflag / bcast are reused by the next segment
+            if (mode <= 1) {
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[acc]);
+            }
+            named_bar_sync(1, kEpiThreads);  // okflag / bcast are reused by the next segment
+            if (et == 0 && si < 4) GEMM_STAMP(p, 5 + 2 * si);
             si++;
             u += g.k1 - g.k0;
         }
@@ -692,6 +805,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     tc_fence_before();
     __syncthreads();
+    if (threadIdx.x == 0) GEMM_STAMP(p, 12);
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem_base, 512);

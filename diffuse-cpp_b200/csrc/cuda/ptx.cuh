@@ -13,7 +13,7 @@ __device__ __forceinline__ uint32_t smem_u32(const void *p) {
 
 __device__ __forceinline__ uint64_t globaltimer() {
     uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t)::"memory");
     return t;
 }
 
@@ -81,6 +81,10 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
             smem_u32(dst)),
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
+}
+// Warm L2 with a global range (address 16 B aligned, size multiple of 16); no smem, no barrier.
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 // 2-D tiled tensor load (x = innermost coordinate, in elements).
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
