@@ -18,6 +18,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <thread>
 #include <vector>
@@ -1028,5 +1029,116 @@ extern "C" int dfb_gen_logits(dfb_ctx *c, int row0, int nrows, float *host) {
     const size_t V = c->m->hp.n_vocab;
     CK(cudaMemcpyAsync(host, c->logits + (size_t)row0 * V, (size_t)nrows * V * 4, cudaMemcpyDeviceToHost, c->st));
     CK(cudaStreamSynchronize(c->st));
+    return DFB_OK;
+}
+
+// ───────────────────────── allocation-free linear ─────────────────────────
+// Some callers must not allocate device memory while they run: serving stacks that
+// hand every byte of the GPU to their own caching allocator up front, and callers that
+// cannot afford the device-wide synchronization cudaMalloc / cudaFree may imply in the
+// middle of their work.  dfb_linear_noalloc serves them: the only scratch the dequant
+// GEMM needs (split-tile partial sums and arrival counters) lives in the fixed arrays
+// below, compiled into this library.  Every GPU that loads the library holds them
+// (8 MiB + 8 KiB) until the process exits.
+namespace {
+constexpr int kNoallocGrid = 32;                      // CTAs per launch (bounds the scratch)
+constexpr int kNoallocMaxTokens = kMaxTok;            // one token group
+constexpr int kNoallocMaxTiles = 2040;                // 128-row output tiles (lm_head of 261k vocab)
+constexpr int kNoallocCnt = kNoallocMaxTiles + 8;     // [tiles] counters, then M, then the error flag
+static __device__ __align__(256) float g_noalloc_ws[(size_t)kNoallocGrid * 2 * kWsTile];
+static __device__ __align__(256) int g_noalloc_cnt[kNoallocCnt];
+
+struct NoallocDev {
+    float *ws = nullptr;
+    int *cnt = nullptr;
+};
+NoallocDev g_noalloc_dev[64];
+std::mutex g_noalloc_mu;
+
+// Zeroes the counters the launch will use and the error flag, stores M.
+__global__ void noalloc_prep_kernel(int *cnt, int n_tiles, int M) {
+    for (int i = threadIdx.x; i < n_tiles; i += blockDim.x) cnt[i] = 0;
+    if (threadIdx.x == 0) {
+        cnt[kNoallocMaxTiles] = M;
+        cnt[kNoallocMaxTiles + 1] = 0;
+    }
+}
+
+template <int WT>
+int noalloc_launch(const WMat &w, const CUtensorMap &tm_x, const EpiArgs &e, const NoallocDev &nd, cudaStream_t st) {
+    auto kern = dq_gemm_kernel<WT, EPI_F32>;
+    constexpr int smem = gemm_smem_bytes(WT);
+    CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    GemmParams p;
+    p.w = w.d;
+    p.n_tiles = w.n_tiles;
+    p.kb = w.kb;
+    p.m_dev = nd.cnt + kNoallocMaxTiles;
+    p.ws = nd.ws;
+    p.tile_cnt = nd.cnt;
+    p.err = nd.cnt + kNoallocMaxTiles + 1;
+    p.epi = e;
+    const int grid = std::min(kNoallocGrid, (kMaxContrib - 2) * w.n_tiles);
+    kern<<<grid, kThreads, smem, st>>>(tm_x, WT == W_F16 ? w.tm : tm_x, p);
+    CK(cudaGetLastError());
+    return DFB_OK;
+}
+}  // namespace
+
+extern "C" int dfb_linear_noalloc(const dfb_model *m, int role, int layer, const void *x_f16_dev, int M,
+                                  float *y_dev, void *stream) {
+    if (!m || !x_f16_dev || !y_dev) return set_err(DFB_ERR_ARG, "null pointer");
+    if (!m->finalized) return set_err(DFB_ERR_STATE, "model not finalized");
+    if (M <= 0 || M > kNoallocMaxTokens)
+        return set_err(DFB_ERR_ARG, "dfb_linear_noalloc: M = %d outside [1, %d] (fixed scratch size)", M,
+                       kNoallocMaxTokens);
+    const WMat *w = nullptr;
+    int K = 0;
+    if (role == DFB_OUTPUT) { w = &m->lm_head; K = m->hp.n_embd; }
+    else if (role == DFB_WO || role == DFB_DOWN) {
+        if (layer < 0 || layer >= m->hp.n_layer) return set_err(DFB_ERR_ARG, "bad layer %d", layer);
+        w = role == DFB_WO ? &m->layers[layer].o : &m->layers[layer].down;
+        K = role == DFB_WO ? m->n_q : m->hp.n_ff;
+    } else {
+        return set_err(DFB_ERR_UNSUPPORTED, "dfb_linear_noalloc serves the unfused weights (attn_output, ffn_down, output)");
+    }
+    if (w->n_tiles > kNoallocMaxTiles)
+        return set_err(DFB_ERR_ARG, "weight has %d output tiles, the fixed scratch holds %d", w->n_tiles, kNoallocMaxTiles);
+    CK(cudaSetDevice(m->device));
+    NoallocDev nd;
+    {
+        // first call on this device: resolve the device addresses of the static arrays
+        // (the host-side names are only stand-ins); do it before any stream capture
+        std::lock_guard<std::mutex> lock(g_noalloc_mu);
+        NoallocDev &d = g_noalloc_dev[m->device];
+        if (!d.ws) {
+            void *a = nullptr, *b = nullptr;
+            CK(cudaGetSymbolAddress(&a, g_noalloc_ws));
+            CK(cudaGetSymbolAddress(&b, g_noalloc_cnt));
+            d.ws = static_cast<float *>(a);
+            d.cnt = static_cast<int *>(b);
+        }
+        nd = d;
+    }
+    CUtensorMap tm;
+    RET(make_tmap(&tm, x_f16_dev, (uint64_t)K, (uint64_t)M, 64));
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    noalloc_prep_kernel<<<1, 256, 0, st>>>(nd.cnt, w->n_tiles, M);
+    CK(cudaGetLastError());
+    EpiArgs e;
+    e.out = y_dev;
+    e.ld = w->n_true;
+    e.n_valid = w->n_true;
+    switch (w->wt) {
+        case W_Q4K: RET(noalloc_launch<W_Q4K>(*w, tm, e, nd, st)); break;
+        case W_Q6K: RET(noalloc_launch<W_Q6K>(*w, tm, e, nd, st)); break;
+        case W_Q80: RET(noalloc_launch<W_Q80>(*w, tm, e, nd, st)); break;
+        case W_F16: RET(noalloc_launch<W_F16>(*w, tm, e, nd, st)); break;
+        default: return set_err(DFB_ERR_STATE, "weight not uploaded");
+    }
+    CK(cudaStreamSynchronize(st));
+    int err = 0;
+    CK(cudaMemcpy(&err, nd.cnt + kNoallocMaxTiles + 1, sizeof(int), cudaMemcpyDeviceToHost));
+    if (err) return set_err(DFB_ERR_TIMEOUT, "a GEMM gave up a bounded wait (code 0x%x)", err);
     return DFB_OK;
 }

@@ -134,6 +134,23 @@ typedef struct {
 int dfb_ctx_profile(dfb_ctx *c, int enable);                            /* (re)start, zeroed */
 int dfb_ctx_profile_read(dfb_ctx *c, dfb_prof_entry *out, int n);      /* n <= DFB_PROF_N */
 
+/* Allocation-free linear layer.  No counterpart in the reference: it exists for callers
+ * that cannot allocate device memory while they run (serving stacks whose caching
+ * allocator owns all device memory, and code that cannot afford the device-wide
+ * synchronization cudaMalloc / cudaFree can cause).  Computes
+ * y[M x n_out] = x[M x K] . W^T through the dequant GEMM for an unfused weight
+ * (DFB_WO, DFB_DOWN or DFB_OUTPUT); x_f16_dev is a device f16 matrix [M][K], y_dev a
+ * device f32 matrix [M][n_out], both owned by the caller.  The GEMM's scratch (split
+ * partial sums and arrival counters) is a fixed 8 MiB + 8 KiB array compiled into the
+ * library, held by every GPU that loads it until exit; M above 256 or a weight of more
+ * than 2040 row tiles is rejected with DFB_ERR_ARG.  Nothing is allocated: no
+ * cudaMalloc / cudaFree, no allocating library call.  The first call on a device looks
+ * up the scratch address (make it before any stream capture).  All calls share the
+ * scratch, so calls that overlap on the GPU race; the call synchronizes `stream`
+ * (cudaStream_t as void*, NULL = legacy default stream) before returning. */
+int dfb_linear_noalloc(const dfb_model *m, int role, int layer, const void *x_f16_dev, int M, float *y_dev,
+                       void *stream);
+
 /* Device stream of a context (cudaStream_t as void*), for callers that time it. */
 int dfb_ctx_stream(dfb_ctx *c, void **stream);
 
