@@ -200,6 +200,50 @@ def run_reference(args, cfg):
     return 0
 
 
+def layer_probe(args):
+    """Small profiling case (a few hundred MB on the device): one layer of LLaDA-8B width,
+    `--warmup` untimed forwards, then `--steps` forwards with the engine's per-launch
+    CUDA-event profiler on; prints calls, average launch time, TFLOP/s and algorithmic
+    GB/s per kernel class.  Launch order of one forward: embed, norm, QKV GEMM, attention,
+    output GEMM, norm, gate/up GEMM, down GEMM (Q6_K: first FFN), final norm, lm_head."""
+    import ctypes as C
+    pkg = load_pkg()
+    os.environ.setdefault("DIFFUSE_LOG_LEVEL", "0")
+    work = pathlib.Path(os.environ.get("DFB_BENCH_DIR", tempfile.gettempdir())) / "dfb_bench"
+    work.mkdir(parents=True, exist_ok=True)
+    path = work / "llada_q4_k_m_1layer_v16384.gguf"
+    if not path.exists():
+        tmp = path.with_suffix(".tmp")
+        pkg.synth_model(tmp, pkg.LLADA_8B, "q4_k_m", seed=0, n_layer=1, n_vocab=16384)
+        tmp.rename(path)
+    model = pkg.Model(str(path))
+    M = args.layer_probe
+    ctx = pkg.Context(model, max(M, 512))
+    dfb, _ = pkg.native()
+
+    class Prof(C.Structure):
+        _fields_ = [("calls", C.c_int32), ("ms", C.c_double), ("flops", C.c_double), ("bytes", C.c_double)]
+    dfb.dfb_ctx_profile.argtypes = [C.c_void_p, C.c_int]
+    dfb.dfb_ctx_profile_read.argtypes = [C.c_void_p, C.c_void_p, C.c_int]
+    toks = np.random.default_rng(0).integers(0, 16000, M).astype(np.int32)
+    for _ in range(args.warmup):
+        ctx.forward(toks)
+    dfb.dfb_ctx_profile(ctx.engine, 1)
+    for _ in range(args.steps):
+        ctx.forward(toks)
+    prof = (Prof * 7)()
+    dfb.dfb_ctx_profile_read(ctx.engine, prof, 7)
+    dfb.dfb_ctx_profile(ctx.engine, 0)
+    for i, n in enumerate(["gemm_all", "q4_k", "q6_k", "q8_0", "f16", "lm_head", "attention"]):
+        p = prof[i]
+        if p.calls:
+            print(f"rows {M:4d} {n:9s} calls {p.calls:4d} avg {p.ms / p.calls * 1e3:8.1f} us "
+                  f"{p.flops / (p.ms * 1e-3) / 1e12:7.1f} TFLOP/s {p.bytes / (p.ms * 1e-3) / 1e9:7.1f} GB/s", flush=True)
+    ctx.close()
+    model.close()
+    return 0
+
+
 def c2_active_rows(cfg):
     """Active rows per denoising step of the reference's cached loop when no position
     changes except the committed ones (step 0 full, then masked + just committed)."""
@@ -227,8 +271,13 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layer-probe", type=int, default=0, metavar="ROWS",
+                    help="profiling case instead of the benchmark: forwards of ROWS tokens through one "
+                         "LLaDA-8B-width Q4_K_M layer (vocab 16384), per-kernel-class CUDA-event timings")
     args = ap.parse_args()
     cfg = CONFIGS[args.config]
+    if args.layer_probe:
+        return layer_probe(args)
     if args.impl == "reference":
         return run_reference(args, cfg)
 

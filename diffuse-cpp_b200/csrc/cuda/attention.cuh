@@ -13,6 +13,7 @@
 #pragma once
 #include <cuda_fp16.h>
 #include <cstdint>
+#include "ptx.cuh"
 
 namespace dfb {
 
@@ -65,6 +66,8 @@ __global__ void __launch_bounds__(128) attn_kernel(const __half *__restrict__ q,
     uint8_t *Ks = att_smem;                               // [2][64][HD]
     uint8_t *Vs = att_smem + 2 * kAttnKeys * HD * 2;      // [2][64][HD]
 
+    griddep_launch_dependents();
+    griddep_wait();  // q and the K/V cache come from the previous kernels
     const int M = *m_dev;
     const int q0 = blockIdx.x * kAttnRows;
     if (q0 >= M) return;

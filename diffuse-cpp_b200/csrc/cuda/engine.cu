@@ -105,6 +105,27 @@ static int make_tmap(CUtensorMap *m, const void *ptr, uint64_t cols, uint64_t ro
     return DFB_OK;
 }
 
+// The 3-D activation views the GEMM loads its B operand through (XMaps in gemm_dq.cuh):
+// x is a row-major [rows][K] f16 matrix, K a multiple of 64, x 16-byte aligned.
+static int make_xmaps(XMaps *xm, const void *x, int K, int rows) {
+    auto fn = encode_fn();
+    if (!fn) return set_err(DFB_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    if (K % 64) return set_err(DFB_ERR_UNSUPPORTED, "activation width %d not a multiple of 64", K);
+    if (reinterpret_cast<uintptr_t>(x) % 16) return set_err(DFB_ERR_ARG, "activation matrix not 16-byte aligned");
+    for (int i = 0; i < kXMaps; i++) {
+        const int h = 16 * (i + 1);
+        cuuint64_t dims[3] = {64, (cuuint64_t)rows, (cuuint64_t)(K / 64)};
+        cuuint64_t strides[2] = {(cuuint64_t)K * 2, 128};
+        cuuint32_t box[3] = {64, (cuuint32_t)h, (cuuint32_t)x_slices(h)};
+        cuuint32_t es[3] = {1, 1, 1};
+        CUresult r = fn(&xm->m[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(x), dims, strides, box, es,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) return set_err(DFB_ERR_CUDA, "cuTensorMapEncodeTiled (activations) failed (%d)", (int)r);
+    }
+    return DFB_OK;
+}
+
 // ───────────────────────── host-side format helpers ─────────────────────────
 enum { G_F32 = 0, G_F16 = 1, G_Q8_0 = 8, G_Q4_K = 12, G_Q6_K = 14, G_BF16 = 30 };
 
@@ -250,10 +271,13 @@ static void retile_range(const std::vector<const uint8_t *> &rows, int type, int
         }
 }
 
-static int build_wmat(const std::vector<const uint8_t *> &rows, int type, int64_t K, WMat &w) {
+static int build_wmat(const std::vector<const uint8_t *> &rows_in, int type, int64_t K, WMat &w) {
     const int wt = wt_of(type);
     if (wt < 0) return set_err(DFB_ERR_UNSUPPORTED, "GGML type %d not supported for a linear weight", type);
-    if (rows.size() % 128) return set_err(DFB_ERR_ARG, "internal: rows not padded");
+    if (rows_in.size() % 128) return set_err(DFB_ERR_ARG, "internal: rows not padded");
+    // the GEMM works on pair tiles of 256 rows: an odd last tile gets a zero partner
+    std::vector<const uint8_t *> rows(rows_in);
+    rows.resize((rows.size() + 255) / 256 * 256, nullptr);
     if ((wt == W_Q4K || wt == W_Q6K) && K % 256) return set_err(DFB_ERR_ARG, "K-quant row length %lld not a multiple of 256", (long long)K);
     if (wt == W_Q80 && K % 32) return set_err(DFB_ERR_ARG, "Q8_0 row length %lld not a multiple of 32", (long long)K);
     if (wt == W_F16 && K % 8) return set_err(DFB_ERR_ARG, "F16 row length %lld not a multiple of 8", (long long)K);
@@ -519,7 +543,7 @@ struct dfb_ctx {
     float *x = nullptr, *logits = nullptr;
     __half *h = nullptr, *att = nullptr, *q = nullptr, *ffh = nullptr, *kc = nullptr, *vc = nullptr;
     float2 *rope = nullptr;
-    CUtensorMap tm_h{}, tm_att{}, tm_ffh{};
+    XMaps xm_h{}, xm_att{}, xm_ffh{};  // GEMM B-operand views of h, att, ffh
     // sequence state
     int32_t *seq = nullptr, *prev_seq = nullptr, *last_changed = nullptr, *cand_tok = nullptr, *commit_pos = nullptr,
             *commit_tok = nullptr, *order = nullptr;
@@ -605,9 +629,9 @@ static int ctx_reserve(dfb_ctx *c, int n) {
     std::vector<float2> rope;
     rope_table_host(cap, (int)hd, hp.rope_theta, rope);
     CK(cudaMemcpy(c->rope, rope.data(), rope.size() * sizeof(float2), cudaMemcpyHostToDevice));
-    RET(make_tmap(&c->tm_h, c->h, d, cap, 64));
-    RET(make_tmap(&c->tm_att, c->att, d, cap, 64));
-    RET(make_tmap(&c->tm_ffh, c->ffh, ff, cap, 64));
+    RET(make_xmaps(&c->xm_h, c->h, (int)d, cap));
+    RET(make_xmaps(&c->xm_att, c->att, m->n_q, cap));
+    RET(make_xmaps(&c->xm_ffh, c->ffh, (int)ff, cap));
     c->cap = cap;
     return DFB_OK;
 }
@@ -652,8 +676,56 @@ static void prof_collect(dfb_ctx *c, int M) {
     c->prof_pending.clear();
 }
 
+// Programmatic dependent launch: a kernel launched this way may start while the
+// previous kernel of the stream is finishing; every such kernel executes
+// griddepcontrol.wait before it touches memory the previous kernels write.
+// DIFFUSE_PDL=0 turns it off (plain stream order).
+static bool pdl_enabled() {
+    static const bool on = [] {
+        const char *e = getenv("DIFFUSE_PDL");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
+                            Args... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = (pdl && pdl_enabled()) ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
+// CTA pairs of a GEMM instantiation that fit on the device at once (one CTA per SM).
 template <int WT, int EPI>
-static int launch_gemm_t(dfb_ctx *c, const WMat &w, const CUtensorMap &tm_x, const EpiArgs &epi) {
+static int gemm_max_pairs(int device, int n_sm) {
+    static int cached[64] = {0};
+    if (device < 0 || device >= 64) return n_sm / 2;
+    if (!cached[device]) {
+        constexpr int smem = gemm_smem_bytes(WT);
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(n_sm & ~1);
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = smem;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, dq_gemm_kernel<WT, EPI>, &cfg) != cudaSuccess || n <= 0) {
+            cudaGetLastError();
+            n = n_sm / 2;
+        }
+        cached[device] = std::min(n, n_sm / 2);
+    }
+    return cached[device];
+}
+
+template <int WT, int EPI>
+static int launch_gemm_t(dfb_ctx *c, const WMat &w, const XMaps &xm, const EpiArgs &epi) {
     auto kern = dq_gemm_kernel<WT, EPI>;
     constexpr int smem = gemm_smem_bytes(WT);
     static bool attr_set[64] = {false};
@@ -664,6 +736,7 @@ static int launch_gemm_t(dfb_ctx *c, const WMat &w, const CUtensorMap &tm_x, con
     }
     GemmParams p;
     p.w = w.d;
+    p.K = w.K;
     p.n_tiles = w.n_tiles;
     p.kb = w.kb;
     p.m_dev = c->cnt + CNT_M;
@@ -684,10 +757,9 @@ static int launch_gemm_t(dfb_ctx *c, const WMat &w, const CUtensorMap &tm_x, con
 #endif
     cudaEvent_t ev0 = nullptr;
     prof_begin(c, &ev0);
-    // A tile is split over at most grid/n_tiles + 2 CTAs; keep that within kMaxContrib.
-    const int grid = std::min(c->m->n_sm, (kMaxContrib - 2) * w.n_tiles);
-    kern<<<grid, kThreads, smem, c->st>>>(tm_x, WT == W_F16 ? w.tm : tm_x, p);
-    CK(cudaGetLastError());
+    // A pair tile is split over at most n_pairs/n_ptiles + 2 pairs; keep that within kMaxContrib.
+    const int n_pairs = std::min(gemm_max_pairs<WT, EPI>(c->m->device, c->m->n_sm), (kMaxContrib - 2) * (w.n_tiles / 2));
+    CK(launch_k(kern, dim3(2 * n_pairs), dim3(kThreads), smem, c->st, !c->prof, w.tm, xm, p));
     // algorithmic work: 2*K MACs per output, weights read once, X read, Y written
     const int out_bytes = (EPI == EPI_F16 || EPI == EPI_QKV || EPI == EPI_SWIGLU) ? 2 : 4;
     const int cat = WT == W_Q4K ? DFB_PROF_Q4K : WT == W_Q6K ? DFB_PROF_Q6K : WT == W_Q80 ? DFB_PROF_Q80 : DFB_PROF_F16;
@@ -697,12 +769,12 @@ static int launch_gemm_t(dfb_ctx *c, const WMat &w, const CUtensorMap &tm_x, con
 }
 
 template <int EPI>
-static int launch_gemm(dfb_ctx *c, const WMat &w, const CUtensorMap &tm_x, const EpiArgs &epi) {
+static int launch_gemm(dfb_ctx *c, const WMat &w, const XMaps &xm, const EpiArgs &epi) {
     switch (w.wt) {
-        case W_Q4K: return launch_gemm_t<W_Q4K, EPI>(c, w, tm_x, epi);
-        case W_Q6K: return launch_gemm_t<W_Q6K, EPI>(c, w, tm_x, epi);
-        case W_Q80: return launch_gemm_t<W_Q80, EPI>(c, w, tm_x, epi);
-        case W_F16: return launch_gemm_t<W_F16, EPI>(c, w, tm_x, epi);
+        case W_Q4K: return launch_gemm_t<W_Q4K, EPI>(c, w, xm, epi);
+        case W_Q6K: return launch_gemm_t<W_Q6K, EPI>(c, w, xm, epi);
+        case W_Q80: return launch_gemm_t<W_Q80, EPI>(c, w, xm, epi);
+        case W_F16: return launch_gemm_t<W_F16, EPI>(c, w, xm, epi);
     }
     return set_err(DFB_ERR_STATE, "weight not uploaded");
 }
@@ -720,9 +792,8 @@ static int launch_attn_t(dfb_ctx *c, const __half *kc, const __half *vc, int n_k
     dim3 grid((c->cap + kAttnRows - 1) / kAttnRows, m->hp.n_head);
     cudaEvent_t ev0 = nullptr;
     prof_begin(c, &ev0);
-    attn_kernel<HD><<<grid, 128, smem, c->st>>>(c->q, m->n_q, kc, vc, m->n_kv, c->att, m->n_q, c->cnt + CNT_M, n_keys,
-                                                m->hp.n_head / m->hp.n_head_kv, scale_log2);
-    CK(cudaGetLastError());
+    CK(launch_k(attn_kernel<HD>, grid, dim3(128), smem, c->st, !c->prof, (const __half *)c->q, m->n_q, kc, vc, m->n_kv,
+                c->att, m->n_q, (const int *)(c->cnt + CNT_M), n_keys, m->hp.n_head / m->hp.n_head_kv, scale_log2));
     prof_end(c, ev0, DFB_PROF_ATTN, 4.0 * n_keys * m->hp.n_head * HD, 2.0 * 2.0 * n_keys * m->n_kv, 4.0 * m->n_q);
     return DFB_OK;
 }
@@ -740,14 +811,15 @@ static int run_forward(dfb_ctx *c, int n_total) {
     for (int l = 0; l < hp.n_layer; l++) {
         const LayerW &L = m->layers[l];
         __half *kc = c->kc + (size_t)l * cap * m->n_kv, *vc = c->vc + (size_t)l * cap * m->n_kv;
-        rmsnorm_kernel<<<cap, 256, 0, c->st>>>(c->x, L.attn_norm, d, hp.rms_norm_eps, c->cnt, c->h);
+        CK(launch_k(rmsnorm_kernel, dim3(cap), dim3(256), 0, c->st, true, (const float *)c->x, (const float *)L.attn_norm, d,
+                    hp.rms_norm_eps, (const int *)c->cnt, c->h));
         EpiArgs e;
         e.q_out = c->q; e.ld_q = m->n_q;
         e.k_cache = kc; e.v_cache = vc; e.ld_kv = m->n_kv;
         e.n_q_tiles = m->nq_pad / 128; e.n_k_tiles = m->nk_pad / 128;
         e.n_q = m->n_q; e.n_kv = m->n_kv; e.head_dim = m->hd;
         e.bias = L.bias_qkv; e.rope = c->rope; e.pos = c->active_pos;
-        RET(launch_gemm<EPI_QKV>(c, L.qkv, c->tm_h, e));
+        RET(launch_gemm<EPI_QKV>(c, L.qkv, c->xm_h, e));
         switch (m->hd) {
             case 16: RET(launch_attn_t<16>(c, kc, vc, n_total)); break;
             case 32: RET(launch_attn_t<32>(c, kc, vc, n_total)); break;
@@ -756,19 +828,21 @@ static int run_forward(dfb_ctx *c, int n_total) {
         }
         EpiArgs eo;
         eo.out = c->x; eo.ld = d; eo.n_valid = d;
-        RET(launch_gemm<EPI_RESID>(c, L.o, c->tm_att, eo));
-        rmsnorm_kernel<<<cap, 256, 0, c->st>>>(c->x, L.ffn_norm, d, hp.rms_norm_eps, c->cnt, c->h);
+        RET(launch_gemm<EPI_RESID>(c, L.o, c->xm_att, eo));
+        CK(launch_k(rmsnorm_kernel, dim3(cap), dim3(256), 0, c->st, true, (const float *)c->x, (const float *)L.ffn_norm, d,
+                    hp.rms_norm_eps, (const int *)c->cnt, c->h));
         EpiArgs eg;
         eg.out = c->ffh; eg.ld = hp.n_ff; eg.n_valid = 2 * hp.n_ff;
-        RET(launch_gemm<EPI_SWIGLU>(c, L.gateup, c->tm_h, eg));
+        RET(launch_gemm<EPI_SWIGLU>(c, L.gateup, c->xm_h, eg));
         EpiArgs ed;
         ed.out = c->x; ed.ld = d; ed.n_valid = d;
-        RET(launch_gemm<EPI_RESID>(c, L.down, c->tm_ffh, ed));
+        RET(launch_gemm<EPI_RESID>(c, L.down, c->xm_ffh, ed));
     }
-    rmsnorm_kernel<<<cap, 256, 0, c->st>>>(c->x, m->output_norm, d, hp.rms_norm_eps, c->cnt, c->h);
+    CK(launch_k(rmsnorm_kernel, dim3(cap), dim3(256), 0, c->st, true, (const float *)c->x, (const float *)m->output_norm, d,
+                hp.rms_norm_eps, (const int *)c->cnt, c->h));
     EpiArgs el;
     el.out = c->logits; el.ld = hp.n_vocab; el.n_valid = hp.n_vocab; el.pos = c->active_pos;
-    RET(launch_gemm<EPI_LOGITS>(c, m->lm_head, c->tm_h, el));
+    RET(launch_gemm<EPI_LOGITS>(c, m->lm_head, c->xm_h, el));
     CK(cudaGetLastError());
     return DFB_OK;
 }
@@ -778,6 +852,7 @@ static int check_err(dfb_ctx *c) {
     CK(cudaMemcpy(&e, c->err, sizeof(int), cudaMemcpyDeviceToHost));
     if (e) {
         cudaMemset(c->err, 0, sizeof(int));
+        cudaMemset(c->tile_cnt, 0, sizeof(int) * c->n_tile_cnt);  // an aborted launch can leave counts behind
         return set_err(DFB_ERR_TIMEOUT, "a GEMM gave up a bounded wait (code 0x%x); results of this call are invalid", e);
     }
     return DFB_OK;
@@ -884,15 +959,15 @@ extern "C" int dfb_linear(dfb_ctx *c, int role, int layer, const float *x_host, 
     CK(cudaMalloc(&xf, (size_t)M * K * 4));
     CK(cudaMalloc(&y, (size_t)M * w->n_rows * 4));
     int rc = DFB_OK;
-    CUtensorMap tm;
+    XMaps xm;
     do {
-        if ((rc = make_tmap(&tm, xh, K, M, 64)) != DFB_OK) break;
+        if ((rc = make_xmaps(&xm, xh, K, M)) != DFB_OK) break;
         if (cudaMemcpyAsync(xf, x_host, (size_t)M * K * 4, cudaMemcpyHostToDevice, c->st) != cudaSuccess) { rc = set_err(DFB_ERR_CUDA, "H2D failed"); break; }
         f32_to_f16_kernel<<<256, 256, 0, c->st>>>(xf, xh, (size_t)M * K);
         if (cudaMemcpyAsync(c->cnt + CNT_M, &M, sizeof(int), cudaMemcpyHostToDevice, c->st) != cudaSuccess) { rc = set_err(DFB_ERR_CUDA, "H2D failed"); break; }
         EpiArgs e;
         e.out = y; e.ld = w->n_rows; e.n_valid = w->n_rows;
-        if ((rc = launch_gemm<EPI_F32>(c, *w, tm, e)) != DFB_OK) break;
+        if ((rc = launch_gemm<EPI_F32>(c, *w, xm, e)) != DFB_OK) break;
         std::vector<float> full((size_t)M * w->n_rows);
         if (cudaMemcpyAsync(full.data(), y, full.size() * 4, cudaMemcpyDeviceToHost, c->st) != cudaSuccess ||
             cudaStreamSynchronize(c->st) != cudaSuccess) { rc = set_err(DFB_ERR_CUDA, "GEMM failed: %s", cudaGetErrorString(cudaGetLastError())); break; }
@@ -1065,12 +1140,13 @@ __global__ void noalloc_prep_kernel(int *cnt, int n_tiles, int M) {
 }
 
 template <int WT>
-int noalloc_launch(const WMat &w, const CUtensorMap &tm_x, const EpiArgs &e, const NoallocDev &nd, cudaStream_t st) {
+int noalloc_launch(const WMat &w, const XMaps &xm, const EpiArgs &e, const NoallocDev &nd, cudaStream_t st) {
     auto kern = dq_gemm_kernel<WT, EPI_F32>;
     constexpr int smem = gemm_smem_bytes(WT);
     CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     GemmParams p;
     p.w = w.d;
+    p.K = w.K;
     p.n_tiles = w.n_tiles;
     p.kb = w.kb;
     p.m_dev = nd.cnt + kNoallocMaxTiles;
@@ -1078,9 +1154,8 @@ int noalloc_launch(const WMat &w, const CUtensorMap &tm_x, const EpiArgs &e, con
     p.tile_cnt = nd.cnt;
     p.err = nd.cnt + kNoallocMaxTiles + 1;
     p.epi = e;
-    const int grid = std::min(kNoallocGrid, (kMaxContrib - 2) * w.n_tiles);
-    kern<<<grid, kThreads, smem, st>>>(tm_x, WT == W_F16 ? w.tm : tm_x, p);
-    CK(cudaGetLastError());
+    const int n_pairs = std::min(kNoallocGrid / 2, (kMaxContrib - 2) * (w.n_tiles / 2));
+    CK(launch_k(kern, dim3(2 * n_pairs), dim3(kThreads), smem, st, false, w.tm, xm, p));
     return DFB_OK;
 }
 }  // namespace
@@ -1089,6 +1164,8 @@ extern "C" int dfb_linear_noalloc(const dfb_model *m, int role, int layer, const
                                   float *y_dev, void *stream) {
     if (!m || !x_f16_dev || !y_dev) return set_err(DFB_ERR_ARG, "null pointer");
     if (!m->finalized) return set_err(DFB_ERR_STATE, "model not finalized");
+    if (reinterpret_cast<uintptr_t>(x_f16_dev) % 16)  // rows are read as 16-byte copies
+        return set_err(DFB_ERR_ARG, "dfb_linear_noalloc: x must be 16-byte aligned");
     if (M <= 0 || M > kNoallocMaxTokens)
         return set_err(DFB_ERR_ARG, "dfb_linear_noalloc: M = %d outside [1, %d] (fixed scratch size)", M,
                        kNoallocMaxTokens);
@@ -1104,6 +1181,8 @@ extern "C" int dfb_linear_noalloc(const dfb_model *m, int role, int layer, const
     }
     if (w->n_tiles > kNoallocMaxTiles)
         return set_err(DFB_ERR_ARG, "weight has %d output tiles, the fixed scratch holds %d", w->n_tiles, kNoallocMaxTiles);
+    XMaps xm;  // host-side descriptors of the caller's matrix (no device memory)
+    RET(make_xmaps(&xm, x_f16_dev, K, M));
     CK(cudaSetDevice(m->device));
     NoallocDev nd;
     {
@@ -1120,8 +1199,6 @@ extern "C" int dfb_linear_noalloc(const dfb_model *m, int role, int layer, const
         }
         nd = d;
     }
-    CUtensorMap tm;
-    RET(make_tmap(&tm, x_f16_dev, (uint64_t)K, (uint64_t)M, 64));
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     noalloc_prep_kernel<<<1, 256, 0, st>>>(nd.cnt, w->n_tiles, M);
     CK(cudaGetLastError());
@@ -1130,10 +1207,10 @@ extern "C" int dfb_linear_noalloc(const dfb_model *m, int role, int layer, const
     e.ld = w->n_true;
     e.n_valid = w->n_true;
     switch (w->wt) {
-        case W_Q4K: RET(noalloc_launch<W_Q4K>(*w, tm, e, nd, st)); break;
-        case W_Q6K: RET(noalloc_launch<W_Q6K>(*w, tm, e, nd, st)); break;
-        case W_Q80: RET(noalloc_launch<W_Q80>(*w, tm, e, nd, st)); break;
-        case W_F16: RET(noalloc_launch<W_F16>(*w, tm, e, nd, st)); break;
+        case W_Q4K: RET(noalloc_launch<W_Q4K>(*w, xm, e, nd, st)); break;
+        case W_Q6K: RET(noalloc_launch<W_Q6K>(*w, xm, e, nd, st)); break;
+        case W_Q80: RET(noalloc_launch<W_Q80>(*w, xm, e, nd, st)); break;
+        case W_F16: RET(noalloc_launch<W_F16>(*w, xm, e, nd, st)); break;
         default: return set_err(DFB_ERR_STATE, "weight not uploaded");
     }
     CK(cudaStreamSynchronize(st));

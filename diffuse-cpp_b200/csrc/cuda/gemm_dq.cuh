@@ -5,26 +5,26 @@
 //
 // Operands.  W is the GGUF weight (Q4_K / Q6_K / Q8_0 raw blocks re-tiled at load,
 // or F16), dequantized to f16 in registers; X is the f16 activation matrix [tokens][K].
-// The MMA is "swap-AB": the 128-row A operand is a tile of 128 output features
-// (dequantized into shared memory in the UMMA 128-byte-swizzled K-major layout) and
-// the B operand is up to 256 tokens of X (TMA tensor loads, same swizzle).  The f32
+// The MMA is "swap-AB" and paired (tcgen05 cta_group::2, M = 256): the A operand is a
+// tile of 256 output features, 128 dequantized into the shared memory of each CTA of a
+// pair (UMMA 128-byte-swizzled K-major layout); the B operand is a group of up to 256
+// tokens of X, each CTA holding half of them (TMA tensor loads, same swizzle).  The f32
 // accumulator lives in TMEM: lane = output feature, column = token.
 //
-// Work split.  Units are (output tile, k-block of 256); a persistent grid of one CTA
-// per SM takes an equal contiguous range of units ("stream-K").  A tile split across
-// CTAs is finished by whichever contributor arrives last on the tile's counter: it
-// sums every contributor's f32 partial in contributor order (so the result does not
-// depend on timing) and applies the epilogue.  The token count M is read on the
-// device, so one launch configuration serves every denoising step.
+// Work split.  Units are (pair tile of 256 output rows, token group, k-block of 256); a
+// persistent grid of CTA pairs (one CTA per SM) takes equal contiguous unit ranges
+// ("stream-K").  A tile split across pairs is finished, in each CTA of the pair, by
+// whichever contributor arrives last on the tile's counter: it sums every
+// contributor's f32 partial in contributor order (so the result does not depend on
+// timing) and applies the epilogue.  The token count M is read on the device, so one
+// launch configuration serves every denoising step.
 //
-// Warp roles (480 threads): w0 activation TMA producer, w1 MMA issuer + TMEM owner,
-// w2-w5 dequantizers (thread = weight row), w6-w9 and w11-w14 epilogue (thread = TMEM
-// lane; the two warps of a lane quarter take alternate 16-column chunks), w10
-// weight-chunk producer (bulk copies into shared memory, L2 prefetch ahead).
+// Warp roles (608 threads per CTA): see the kernel.
 #pragma once
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cstdint>
+#include <type_traits>
 #include "ptx.cuh"
 
 namespace dfb {
@@ -70,8 +70,19 @@ struct EpiArgs {
     const int *pos = nullptr;          // [tokens] position of each row (QKV, LOGITS)
 };
 
+// Activation tensor maps, one per token half-group size h = 16 (i + 1), i = 0..7: a 3-D
+// view {64 k, rows, K / 64 k-blocks} of the row-major [rows][K] f16 matrix (strides: row,
+// then 128 B), box {64, h, x_slices(h)}, 128-byte swizzle.  One load brings x_slices
+// consecutive 64-wide k-slices of h rows, each in the canonical K-major SW128 layout.
+constexpr int kXMaps = 8;
+__host__ __device__ constexpr int x_slices(int h) { return h <= 32 ? 4 : h <= 64 ? 2 : 1; }
+struct XMaps {
+    CUtensorMap m[kXMaps];
+};
+
 struct GemmParams {
     const uint8_t *w = nullptr;  // re-tiled weight chunks (quantized types)
+    int K = 0;                   // valid columns of the activations
     int n_tiles = 0;             // 128-row output tiles
     int kb = 0;                  // k-blocks of 256
     const int *m_dev = nullptr;  // token count (device)
@@ -82,57 +93,93 @@ struct GemmParams {
     EpiArgs epi;
 };
 
-constexpr int kThreads = 480;
-constexpr int kEpiThreads = 256;  // two epilogue warps per TMEM lane quarter
-constexpr int kPrefetchChunks = 6;  // weight chunks warmed in L2 ahead of the smem copy
-constexpr int kStages = 3;
-constexpr int kRawStages = 2;
-constexpr int kABytes = 128 * 128;       // 128 rows x 64 f16
-constexpr int kBBytes = 256 * 128;       // 256 tokens x 64 f16
-constexpr int kStageBytes = kABytes + kBBytes;
-constexpr int kMaxTok = 256;             // tokens per MMA (N)
-constexpr int kWsTile = kMaxTok * 128;   // floats per partial tile
+constexpr int kThreads = 640;            // 20 warps, roles below
+constexpr int kEpiThreads = 256;         // two epilogue warps per TMEM lane quarter
+constexpr int kDeqWarps = 8;             // two sets of four: even / odd k-slices
+constexpr int kABytes = 128 * 128;       // one A stage: this CTA's 128 weight rows x 64 f16
+constexpr int kMaxTok = 256;             // tokens per MMA (N) of the pair
+constexpr int kWsTile = kMaxTok * 128;   // floats per partial tile (one CTA's 128 rows)
 constexpr int kErrTimeout = 0x100;
+constexpr int kMaxAStages = 6, kMaxBSlots = 24, kMaxRawStages = 4;
 
-constexpr int kMaxContrib = 64;  // split contributors of one tile tracked in shared memory
-constexpr int kFixupPeers = (kStages * kStageBytes) / 32768;  // partial chunks the stage buffers hold
+// Ring depths per weight type, sized so that shared memory (227 KB) holds them:
+//  A ring   dequantized (or, for F16, TMA-loaded) weight slices, 16 KB each;
+//  B ring   this CTA's activation rows of one k-slice; a slot holds half the token
+//           group (2-16 KB), so small token counts keep many slices in flight and hide
+//           the L2 latency of the activation loads;
+//  raw ring re-tiled weight chunks (one k-block of 256 for 128 rows).
+__host__ __device__ constexpr int a_stages(int wt) { return 4; }
+__host__ __device__ constexpr int b_ring_bytes(int wt) { return wt == W_F16 ? 112 * 1024 : 80 * 1024; }
+// A raw stage holds raw_cpr consecutive chunks of the CTA's unit range: the weight
+// stream reached ~3.8 TB/s with 18 KB stages and ~6-7 TB/s with 36-72 KB stages
+// (same bytes in flight), so small chunks are grouped.
+__host__ __device__ constexpr int raw_stages(int wt) { return wt == W_Q4K ? 2 : wt == W_Q6K ? 3 : wt == W_Q80 ? 2 : 0; }
+__host__ __device__ constexpr int raw_cpr(int wt) { return wt == W_Q4K ? 2 : 1; }
+
+// Warp roles.  A warp runs on scheduler warp % 4 and may only access TMEM lanes
+// 32*(warp % 4)..+31.  Each scheduler gets one light role (w0 activation producer, w1
+// MMA issuer, w2 weight-chunk producer, w3 relay), one dequantizer of each set (w4-w7
+// set 0, w8-w11 set 1) and two epilogue warps (w12-w19: every lane quarter twice).
+enum WarpRole : int { R_DEQ = 0, R_MMA = 1, R_BPROD = 2, R_WPROD = 3, R_EPI = 4, R_RELAY = 5 };
+__host__ __device__ constexpr int warp_role(int w) {
+    return w == 0 ? R_BPROD : w == 1 ? R_MMA : w == 2 ? R_WPROD : w == 3 ? R_RELAY : w < 12 ? R_DEQ : R_EPI;
+}
+// dequantizer index 0..7 (set = index / 4 takes k-slices set and set + 2 of each k-block)
+__host__ __device__ constexpr int deq_index(int w) { return w - 4; }
+// epilogue thread group: warps 12-15 and 16-19 each cover the four lane quarters
+__host__ __device__ constexpr int epi_half(int w) { return w >= 16 ? 1 : 0; }
+
+constexpr int kMaxContrib = 64;     // split contributors (CTA pairs) of one tile tracked in shared memory
+constexpr int kBarBytes = 80 * 8;   // mbarriers and flags, see the kernel's shared-memory map
 __host__ __device__ constexpr int gemm_smem_bytes(int wt) {
-    return 1024 /*align slack*/ + kStages * kStageBytes + kRawStages * raw_chunk_bytes(wt) + 256 /*barriers*/ +
-           4 * kMaxTok /*token positions*/ + 8 * kMaxContrib /*contributor partial offsets*/;
+    return 1024 /*align slack*/ + a_stages(wt) * kABytes + b_ring_bytes(wt) + raw_stages(wt) * raw_cpr(wt) * raw_chunk_bytes(wt) +
+           kBarBytes /*barriers, flags*/ + 4 * kMaxTok /*token positions*/ + 8 * kMaxContrib /*contributor partial offsets*/;
 }
 
-// Static stream-K schedule, recomputed identically by every role of every CTA.
+// Static stream-K schedule over CTA pairs, recomputed identically by every role of
+// both CTAs of a pair.  Units are (pair tile of 256 weight rows, token group, k-block).
 struct Sched {
     int M, n_mg, gsz, kb, n_ot, U, G, u0, u1;
-    __device__ __forceinline__ void init(int M_, int n_tiles, int kb_, int grid, int cta) {
+    int bh, spb, bslot, nbs;  // B ring: rows per CTA (widest group), slices per load, slot bytes, slots
+    __device__ __forceinline__ void init(int M_, int n_ptiles, int kb_, int n_pairs, int pair, int ring_bytes) {
         M = M_;
         kb = kb_;
         n_mg = (M + kMaxTok - 1) / kMaxTok;
         gsz = (((M + n_mg - 1) / n_mg) + 15) & ~15;
-        n_ot = n_tiles * n_mg;
+        n_ot = n_ptiles * n_mg;
         U = n_ot * kb;
-        G = grid < U ? grid : U;
-        u0 = (int)((long long)cta * U / G);
-        u1 = (int)((long long)(cta + 1) * U / G);
+        G = n_pairs < U ? n_pairs : U;
+        if (M <= 0 || pair >= G) {
+            u0 = u1 = 0;
+        } else {
+            u0 = (int)((long long)pair * U / G);
+            u1 = (int)((long long)(pair + 1) * U / G);
+        }
+        bh = ((gsz + 31) & ~31) >> 1;  // 16..128
+        if (bh < 16) bh = 16;
+        spb = x_slices(bh);
+        bslot = bh * 128 * spb;
+        nbs = ring_bytes / bslot;
+        if (nbs > kMaxBSlots) nbs = kMaxBSlots;
     }
     __device__ __forceinline__ int owner(int u) const { return (int)(((long long)(u + 1) * G - 1) / U); }
     __device__ __forceinline__ int begin_of(int c) const { return (int)((long long)c * U / G); }
 };
 
 struct Seg {
-    int ot, tile, m0, ntok, nmma, nbox, k0, k1;
+    int ot, pt, m0, ntok, nmma, half, k0, k1;
 };
 __device__ __forceinline__ Seg make_seg(const Sched &s, int u, int u1) {
     Seg g;
     g.ot = u / s.kb;
     g.k0 = u % s.kb;
     g.k1 = min(s.kb, g.k0 + (u1 - u));
-    g.tile = g.ot / s.n_mg;
+    g.pt = g.ot / s.n_mg;
     const int mg = g.ot % s.n_mg;
     g.m0 = mg * s.gsz;
     g.ntok = min(s.gsz, s.M - g.m0);
-    g.nmma = (g.ntok + 15) & ~15;
-    g.nbox = (g.ntok + 63) / 64;
+    g.nmma = (g.ntok + 31) & ~31;  // MMA N: split evenly over the pair, 16-row multiples each
+    g.half = g.nmma >> 1;          // tokens [m0 + rank*half, +half) are this CTA's B rows
     return g;
 }
 
@@ -146,40 +193,39 @@ __device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__
 
 // Q4_K chunk layout (per 128 rows): [d,dmin f16 x2: 4 B/row][scales: 12 B/row at 512]
 // [qs: 128 B/row at 2048, 16-byte chunk c stored at c ^ (row & 7)].
-struct Q4KRow {
+// Scales of the four sub-blocks one dequant set uses: set p dequantizes k-slices p and
+// p + 2, i.e. sub-blocks 2p, 2p+1 (local 0, 1) and 2p+4, 2p+5 (local 2, 3).
+struct Q4KMeta {
     __half2 d2;
-    __half2 sc[8], nsc[8], nmo[8];  // sc, -1024*sc, -(dmin*m) per sub-block, as f16 pairs
+    __half2 sc[4], nsc[4], nmo[4];  // sc, -1024*sc, -(dmin*m) per sub-block, as f16 pairs
 };
-__device__ __forceinline__ void q4k_load_meta(const uint8_t *R, int r, Q4KRow &m) {
+__device__ __forceinline__ void q4k_load_meta(const uint8_t *R, int r, int set, Q4KMeta &m) {
     const uint32_t dm = *reinterpret_cast<const uint32_t *>(R + 4 * r);
     const __half d = __ushort_as_half((unsigned short)(dm & 0xFFFF));
     const float dmin = __half2float(__ushort_as_half((unsigned short)(dm >> 16)));
     m.d2 = __halves2half2(d, d);
     const uint32_t *sp = reinterpret_cast<const uint32_t *>(R + 512 + 12 * r);
-    uint8_t q[12];
     const uint32_t s0 = sp[0], s1 = sp[1], s2 = sp[2];
+    // byte i of the 12 packed scale bytes (i may be a runtime value: no local array)
+    auto qb = [&](int i) -> int { return (int)(((i < 4 ? s0 : i < 8 ? s1 : s2) >> (8 * (i & 3))) & 0xFF); };
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-        q[i] = (s0 >> (8 * i)) & 0xFF;
-        q[4 + i] = (s1 >> (8 * i)) & 0xFF;
-        q[8 + i] = (s2 >> (8 * i)) & 0xFF;
-    }
-#pragma unroll
-    for (int j = 0; j < 8; j++) {
+    for (int l = 0; l < 4; l++) {
+        // 6-bit scale / min of sub-block j (get_scale_min_k4 packing)
+        const int j = 2 * set + (l & 1) + 4 * (l >> 1);
         int sc, mn;
-        if (j < 4) {
-            sc = q[j] & 63;
-            mn = q[j + 4] & 63;
+        if (l < 2) {  // j < 4
+            sc = qb(j) & 63;
+            mn = qb(j + 4) & 63;
         } else {
-            sc = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4);
-            mn = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+            sc = (qb(j + 4) & 0xF) | ((qb(j - 4) >> 6) << 4);
+            mn = (qb(j + 4) >> 4) | ((qb(j) >> 6) << 4);
         }
         const __half hs = __int2half_rn(sc);
-        m.sc[j] = __halves2half2(hs, hs);
+        m.sc[l] = __halves2half2(hs, hs);
         const __half hn = __int2half_rn(-1024 * sc);
-        m.nsc[j] = __halves2half2(hn, hn);
+        m.nsc[l] = __halves2half2(hn, hn);
         const __half ho = __float2half_rn(-(dmin * (float)mn));
-        m.nmo[j] = __halves2half2(ho, ho);
+        m.nmo[l] = __halves2half2(ho, ho);
     }
 }
 // 4 nibbles (one byte lane each, values 0..15) -> two f16 pairs of q*sc*d - dmin*m.
@@ -192,40 +238,48 @@ __device__ __forceinline__ void q4k_pair(uint32_t nib, const __half2 &sc, const 
     o01 = h2u(__hfma2(t01, d2, nmo));
     o23 = h2u(__hfma2(t23, d2, nmo));
 }
-__device__ __forceinline__ void q4k_slice(const uint8_t *R, int r, int s, const Q4KRow &m, uint8_t *A) {
+// Slice s (k = 64s .. 64s+63) of row r: low nibbles of qs bytes 32s.. are sub-block 2s,
+// high nibbles sub-block 2s+1; lo = local meta index of sub-block 2s.
+__device__ __forceinline__ void q4k_slice(const uint8_t *R, int r, int s, int lo, const Q4KMeta &m, uint8_t *A) {
     const uint8_t *qrow = R + 2048 + 128 * r;
     const uint4 qa = *reinterpret_cast<const uint4 *>(qrow + (((2 * s) ^ (r & 7)) << 4));
     const uint4 qb = *reinterpret_cast<const uint4 *>(qrow + (((2 * s + 1) ^ (r & 7)) << 4));
     const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-    const int jl = 2 * s, jh = 2 * s + 1;
+    const int jl = lo, jh = lo + 1;
 #pragma unroll
     for (int c = 0; c < 4; c++) {
-        uint4 lo, hi;
+        uint4 lo4, hi4;
         const uint32_t w0 = w[2 * c], w1 = w[2 * c + 1];
-        q4k_pair(w0 & 0x0F0F0F0Fu, m.sc[jl], m.nsc[jl], m.d2, m.nmo[jl], lo.x, lo.y);
-        q4k_pair(w1 & 0x0F0F0F0Fu, m.sc[jl], m.nsc[jl], m.d2, m.nmo[jl], lo.z, lo.w);
-        q4k_pair((w0 >> 4) & 0x0F0F0F0Fu, m.sc[jh], m.nsc[jh], m.d2, m.nmo[jh], hi.x, hi.y);
-        q4k_pair((w1 >> 4) & 0x0F0F0F0Fu, m.sc[jh], m.nsc[jh], m.d2, m.nmo[jh], hi.z, hi.w);
-        st_a(A, r, c, lo);
-        st_a(A, r, 4 + c, hi);
+        q4k_pair(w0 & 0x0F0F0F0Fu, m.sc[jl], m.nsc[jl], m.d2, m.nmo[jl], lo4.x, lo4.y);
+        q4k_pair(w1 & 0x0F0F0F0Fu, m.sc[jl], m.nsc[jl], m.d2, m.nmo[jl], lo4.z, lo4.w);
+        q4k_pair((w0 >> 4) & 0x0F0F0F0Fu, m.sc[jh], m.nsc[jh], m.d2, m.nmo[jh], hi4.x, hi4.y);
+        q4k_pair((w1 >> 4) & 0x0F0F0F0Fu, m.sc[jh], m.nsc[jh], m.d2, m.nmo[jh], hi4.z, hi4.w);
+        st_a(A, r, c, lo4);
+        st_a(A, r, 4 + c, hi4);
     }
 }
 
 // Q6_K chunk layout: [ql: 128 B/row, chunk c at c ^ (row & 7)]
 // [qh: 64 B/row at 16384, chunk c at c ^ ((row >> 1) & 3)][scales i8: 16 B/row at 24576]
 // [d f16: 2 B/row at 26624].
-struct Q6KRow {
-    __half2 ds[16];  // f16(d * scale) per 16-element group
+// d * scale of the eight 16-element groups one dequant set uses: set p takes slices p
+// and p + 2, i.e. groups 4p..4p+3 (local 0-3) and 4p+8..4p+11 (local 4-7).
+struct Q6KMeta {
+    __half2 ds[8];
 };
-__device__ __forceinline__ void q6k_load_meta(const uint8_t *R, int r, Q6KRow &m) {
+__device__ __forceinline__ void q6k_load_meta(const uint8_t *R, int r, int set, Q6KMeta &m) {
     const float d = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short *>(R + 26624 + 2 * r)));
     const uint4 sv = *reinterpret_cast<const uint4 *>(R + 24576 + 16 * r);
-    const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};
 #pragma unroll
-    for (int g = 0; g < 16; g++) {
-        const int sc = (int)(int8_t)((sw[g >> 2] >> (8 * (g & 3))) & 0xFF);
-        const __half h = __float2half_rn(d * (float)sc);
-        m.ds[g] = __halves2half2(h, h);
+    for (int h = 0; h < 2; h++) {
+        const int wi = set + 2 * h;  // scale word holding groups 4*wi .. 4*wi+3
+        const uint32_t w = wi == 0 ? sv.x : wi == 1 ? sv.y : wi == 2 ? sv.z : sv.w;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int sc = (int)(int8_t)((w >> (8 * i)) & 0xFF);
+            const __half hh = __float2half_rn(d * (float)sc);
+            m.ds[4 * h + i] = __halves2half2(hh, hh);
+        }
     }
 }
 struct Q6KHalf {
@@ -254,7 +308,7 @@ __device__ __forceinline__ void q6k_pair(uint32_t q6, const __half2 &ds, uint32_
     o01 = h2u(__hmul2(__hsub2(u2h(p01), k1056), ds));
     o23 = h2u(__hmul2(__hsub2(u2h(p23), k1056), ds));
 }
-__device__ __forceinline__ void q6k_slice(const Q6KHalf &q, int r, int s, const Q6KRow &m, uint8_t *A) {
+__device__ __forceinline__ void q6k_slice(const Q6KHalf &q, int r, int s, int lo, const Q6KMeta &m, uint8_t *A) {
     const int s2 = s & 1;
 #pragma unroll
     for (int c = 0; c < 8; c++) {
@@ -268,7 +322,7 @@ __device__ __forceinline__ void q6k_slice(const Q6KHalf &q, int r, int s, const 
             const uint32_t nib = s2 ? ((lw >> 4) & 0x0F0F0F0Fu) : (lw & 0x0F0F0F0Fu);
             const uint32_t q6 = nib | (((hwd >> shift) & 0x03030303u) << 4);
             uint32_t a, b;
-            q6k_pair(q6, m.ds[4 * s + (c >> 1)], a, b);
+            q6k_pair(q6, m.ds[lo + (c >> 1)], a, b);
             if (hw == 0) { o.x = a; o.y = b; } else { o.z = a; o.w = b; }
         }
         st_a(A, r, c, o);
@@ -278,7 +332,6 @@ __device__ __forceinline__ void q6k_slice(const Q6KHalf &q, int r, int s, const 
 // Q8_0 chunk layout: [d f16 x 8: 16 B/row][qs: 256 B/row at 2048, chunk c at (c & 8) | ((c & 7) ^ (row & 7))].
 __device__ __forceinline__ void q80_slice(const uint8_t *R, int r, int s, uint8_t *A) {
     const uint4 dv = *reinterpret_cast<const uint4 *>(R + 16 * r);
-    const uint32_t dw[4] = {dv.x, dv.y, dv.z, dv.w};
     const uint8_t *qrow = R + 2048 + 256 * r;
     const __half2 k1152 = __halves2half2(__int2half_rn(1152), __int2half_rn(1152));
 #pragma unroll
@@ -286,7 +339,9 @@ __device__ __forceinline__ void q80_slice(const uint8_t *R, int r, int s, uint8_
         const int c = 4 * s + cc;
         const uint4 v = *reinterpret_cast<const uint4 *>(qrow + (((c & 8) | ((c & 7) ^ (r & 7))) << 4));
         const int blk = 2 * s + (cc >> 1);
-        const unsigned short dbits = (unsigned short)((dw[blk >> 1] >> (16 * (blk & 1))) & 0xFFFF);
+        const int wi = blk >> 1;  // may be a runtime value: select, no local array
+        const uint32_t dwd = wi == 0 ? dv.x : wi == 1 ? dv.y : wi == 2 ? dv.z : dv.w;
+        const unsigned short dbits = (unsigned short)((dwd >> (16 * (blk & 1))) & 0xFFFF);
         const __half dh = __ushort_as_half(dbits);
         const __half2 d2 = __halves2half2(dh, dh);
         const uint32_t w[4] = {v.x, v.y, v.z, v.w};
@@ -346,7 +401,7 @@ __device__ __forceinline__ EpiRow epi_row(const EpiArgs &e, int tile, int row) {
             r.f = fl;
         }
         r.fvalid = r.f < (r.sec == 0 ? e.n_q : e.n_kv);
-        r.bias = e.bias ? __ldg(e.bias + sec_off + r.f) : 0.f;
+        r.bias = (e.bias && r.fvalid) ? __ldg(e.bias + sec_off + r.f) : 0.f;
         r.writer = true;
     } else {
         r.f = tile * 128 + row;
@@ -423,250 +478,417 @@ __device__ __forceinline__ void epi_chunk(const EpiArgs &e, const EpiRow &r, con
 }
 
 // ───────────── the kernel ─────────────
+// Launched as clusters of two CTAs (a pair on one TPC).  Pair p owns the stream-K unit
+// range of pair tile pt = 256 weight rows: the even CTA (rank 0) dequantizes rows
+// [256 pt, +128), the odd one rows [256 pt + 128, +128); each CTA loads its half of the
+// token group's activation rows.  The even CTA issues the paired MMA (M = 256) and its
+// commits arrive on the barriers of both CTAs; each CTA's epilogue drains its own TMEM.
+// Barriers the MMA waits on (full_a, full_b, acc_empty) live in the even CTA; the odd
+// CTA's loads and arrivals reach them through cluster addresses.
+//
+// Shared memory (per CTA): [A ring: a_stages x 16 KB][B ring][raw ring][barriers]
+// [token positions][contributor offsets].  Slice i (64 k) of the CTA's unit range uses
+// A stage i % a_stages and part i % spb of B slot (i / spb) % nbs.
+//
+// Warps (warp_role): w0 activation producer, w1 MMA issuer (even CTA) + TMEM owner, w2
+// weight-chunk producer (F16 weights: A-tile TMA producer), w3 relay, w4-w11
+// dequantizers (two sets of four; thread = weight row), w12-w19 epilogue (thread = TMEM
+// lane; w12-15 and w16-19 take alternate 16-column chunks).
 template <int WT, int EPI>
-__global__ void __launch_bounds__(kThreads, 1)
-    dq_gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w, GemmParams p) {
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    dq_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ XMaps xm, GemmParams p) {
     constexpr int RAWB = raw_chunk_bytes(WT);
+    constexpr int NA = a_stages(WT), NRAW = raw_stages(WT), BRING = b_ring_bytes(WT);
+    constexpr int CPR = raw_cpr(WT), RSB = CPR * RAWB;  // chunks and bytes per raw stage
+    constexpr int kFixupPeers = (NA * kABytes + BRING) / 32768;  // partial chunks the drained rings hold
+    // the relay frees B slot j only after the MMA of slice j + NA: the B ring must hold at
+    // least NA slots of the widest group (16 KB) or the producer would wait on itself
+    // The relay frees a B slot once the MMA of the load's last slice + NA has completed,
+    // so the producer needs 2 + (NA - 1) / spb slots not to wait on itself; the widest
+    // group (128 rows per CTA, one slice per 16 KB load) needs the most.
+    static_assert(BRING / (kMaxTok / 2 * 128) >= 2 + (NA - 1), "B ring too shallow for the A ring");
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t *stages = smem;
-    uint8_t *raw = smem + kStages * kStageBytes;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(raw + kRawStages * RAWB);
-    uint64_t *full_b = bars, *full_a = bars + 3, *empty = bars + 6, *raw_full = bars + 9, *raw_empty = bars + 11,
-             *acc_full = bars + 13, *acc_empty = bars + 15, *drain = bars + 17;
-    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 18);
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 19);
-    int *bcast = reinterpret_cast<int *>(bars + 20);
-    volatile int *okflag = reinterpret_cast<volatile int *>(bars + 21);
-    uint64_t *fix_bar = bars + 22;  // bulk loads of split-tile partials into the drained stage buffers
-    int *s_pos = reinterpret_cast<int *>(bars + 32);                              // [kMaxTok]
+    uint8_t *aring = smem;
+    uint8_t *bring = smem + NA * kABytes;
+    uint8_t *raw = bring + BRING;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(raw + NRAW * RSB);
+    uint64_t *full_a = bars, *empty_a = bars + 6, *full_b = bars + 12, *empty_b = bars + 36, *raw_full = bars + 60,
+             *raw_empty = bars + 64, *acc_full = bars + 68, *acc_empty = bars + 70, *drain = bars + 72,
+             *fix_bar = bars + 73;
+    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 74);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 75);
+    int *bcast = reinterpret_cast<int *>(bars + 76);
+    volatile int *okflag = reinterpret_cast<volatile int *>(bars + 77);
+    int *s_pos = reinterpret_cast<int *>(bars + kBarBytes / 8);                   // [kMaxTok]
     long long *s_contrib = reinterpret_cast<long long *>(s_pos + kMaxTok);        // [kMaxContrib]
 
-    const int M = *p.m_dev;
-    if (M <= 0) return;
-    if (threadIdx.x == 0) GEMM_STAMP(p, 0);
-    Sched S;
-    S.init(M, p.n_tiles, p.kb, gridDim.x, blockIdx.x);
-    if ((int)blockIdx.x >= S.G) return;
-
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
+    // the next kernel of the stream may be scheduled now; it waits for this grid itself
+    griddep_launch_dependents();
     if (threadIdx.x == 0) {
-        for (int i = 0; i < 3; i++) {
-            mbar_init(&full_b[i], 1);
-            mbar_init(&full_a[i], 4);
-            mbar_init(&empty[i], 1);
+        GEMM_STAMP(p, 0);
+        for (int i = 0; i < NA; i++) {
+            // both CTAs' relays + F16: the expect_tx / else four dequant warps per CTA
+            mbar_init(&full_a[i], WT == W_F16 ? 3 : 10);
+            mbar_init(&empty_a[i], 1);                   // the paired MMA's commit
+        }
+        for (int i = 0; i < kMaxBSlots; i++) {
+            mbar_init(&full_b[i], 1);   // the producer's expect_tx
+            mbar_init(&empty_b[i], 1);  // the relay, once the MMA that read the slot completed
+        }
+        for (int i = 0; i < NRAW; i++) {
+            mbar_init(&raw_full[i], 1);
+            mbar_init(&raw_empty[i], kDeqWarps);
         }
         for (int i = 0; i < 2; i++) {
-            mbar_init(&raw_full[i], 1);
-            mbar_init(&raw_empty[i], 4);
             mbar_init(&acc_full[i], 1);
-            mbar_init(&acc_empty[i], kEpiThreads / 32);  // one arrival per epilogue warp
+            mbar_init(&acc_empty[i], 2 * kEpiThreads / 32);  // every epilogue warp of both CTAs
         }
         mbar_init(drain, 1);
         mbar_init(fix_bar, 1);
         *abort_flag = 0;
         fence_barrier_init();
     }
-    if (warp == 0 && lane == 0) {
-        prefetch_tmap(&tm_x);
-        if (WT == W_F16) prefetch_tmap(&tm_w);
+    const int role = warp_role(warp);
+    if (WT == W_F16 && role == R_WPROD && lane == 0) prefetch_tmap(&tm_w);
+    if (role == R_MMA) {
+        tmem_alloc2(tmem_holder, 512);
+        tmem_relinquish2();
     }
-    if (warp == 1) {
-        tmem_alloc(tmem_holder, 512);
-        tmem_relinquish();
+    if (WT != W_F16 && role == R_WPROD && lane == 0) {
+        // Weights do not depend on the previous kernel: warm L2 with this pair's first
+        // chunks before waiting for it (the token count read here may still change, which
+        // only makes the hint less useful).
+        Sched S0;
+        S0.init(*reinterpret_cast<volatile const int *>(p.m_dev), p.n_tiles >> 1, p.kb, n_pairs, pair, BRING);
+        for (int u = S0.u0; u < S0.u1 && u < S0.u0 + NRAW * CPR; u++) {
+            const int ot = u / S0.kb, kbi = u % S0.kb;
+            bulk_prefetch_l2(p.w + ((size_t)(2 * (ot / S0.n_mg) + rank) * p.kb + kbi) * RAWB, RAWB);
+        }
     }
     tc_fence_before();
     __syncthreads();
+    cluster_sync();  // barriers of both CTAs initialised, TMEM of both allocated
     tc_fence_after();
     const uint32_t tmem_base = *tmem_holder;
+    // everything below may read what the previous kernel wrote
+    griddep_wait();
+    const int M = *p.m_dev;
+    Sched S;
+    S.init(M, p.n_tiles >> 1, p.kb, n_pairs, pair, BRING);
+    const int NBS = S.nbs;
     if (threadIdx.x == 0) GEMM_STAMP(p, 1);
+    // barriers of the even CTA as cluster addresses
+    const uint32_t full_a0 = mapa_shared(full_a, 0), acc_empty0 = mapa_shared(acc_empty, 0);
 
-    if (warp == 0) {
-        // ── activation TMA producer ──
+    if (role == R_BPROD) {
+        // ── activation producer (both CTAs, local barriers): this CTA's half of the
+        //    token group, spb k-slices per tensor load.  Few large loads: the TMA unit
+        //    also streams the weights and handles only a few operations per microsecond. ──
         if (lane == 0) {
-            int it = 0;
+            const CUtensorMap *xmap = &xm.m[S.bh / 16 - 1];
+            int ob = 0;  // B loads issued
             bool ok = true;
             for (int u = S.u0; u < S.u1 && ok;) {
                 const Seg g = make_seg(S, u, S.u1);
+                const int row0 = g.m0 + (int)rank * g.half;
                 for (int kbi = g.k0; kbi < g.k1 && ok; kbi++) {
-                    for (int s = 0; s < 4; s++) {
-                        const int st = it % kStages;
-                        if (!(ok = mbar_wait(&empty[st], ((it / kStages) & 1) ^ 1, abort_flag, p.err, kErrTimeout + 2))) break;
-                        uint8_t *A = stages + st * kStageBytes;
-                        uint8_t *B = A + kABytes;
-                        const uint32_t bytes = g.nbox * 8192 + (WT == W_F16 ? kABytes : 0);
-                        mbar_arrive_expect_tx(&full_b[st], bytes);
-                        for (int b = 0; b < g.nbox; b++)
-                            tma_load_2d(B + b * 8192, &tm_x, kbi * 256 + s * 64, g.m0 + b * 64, &full_b[st]);
-                        GEMM_EVENT(p, 0, it);
-                        if constexpr (WT == W_F16) tma_load_2d(A, &tm_w, kbi * 256 + s * 64, g.tile * 128, &full_b[st]);
-                        it++;
+                    for (int s = 0; s < 4; s += S.spb) {
+                        const int sl = ob % NBS;
+                        if (!(ok = mbar_wait<128>(&empty_b[sl], ((ob / NBS) & 1) ^ 1, abort_flag, p.err, kErrTimeout + 2))) break;
+                        mbar_arrive_expect_tx(&full_b[sl], S.bslot);
+                        tma_load_3d(bring + sl * S.bslot, xmap, 0, row0, kbi * 4 + s, &full_b[sl]);
+                        GEMM_EVENT(p, 0, ob);
+                        ob++;
                     }
                 }
                 u += g.k1 - g.k0;
             }
             GEMM_STAMP(p, 2);
             if (!ok) {
-                // let every copy this thread started land before the CTA exits
-                for (int i = (it > kStages ? it - kStages : 0); i < it; i++)
-                    spin_bounded(&full_b[i % kStages], (i / kStages) & 1);
+                // let the copies in flight land before the CTA can exit
+                for (int i = (ob > NBS ? ob - NBS : 0); i < ob; i++) spin_bounded(&full_b[i % NBS], (i / NBS) & 1);
             }
         }
         __syncwarp();
-    } else if (warp == 10) {
-        // ── weight-chunk producer: one re-tiled chunk (128 rows x 256 k) per k-block ──
+    } else if (role == R_WPROD) {
         if constexpr (WT != W_F16) {
+            // ── weight-chunk producer: this CTA's re-tiled chunk (128 rows x 256 k) per k-block ──
             if (lane == 0) {
                 auto chunk = [&](int u) {
                     const int ot = u / S.kb, kbi = u % S.kb;
-                    return p.w + ((size_t)(ot / S.n_mg) * p.kb + kbi) * RAWB;
+                    return p.w + ((size_t)(2 * (ot / S.n_mg) + rank) * p.kb + kbi) * RAWB;
                 };
-                for (int u = S.u0; u < S.u1 && u < S.u0 + kPrefetchChunks; u++) bulk_prefetch_l2(chunk(u), RAWB);
                 int rit = 0;
                 bool ok = true;
-                for (int u = S.u0; u < S.u1 && ok; u++) {
-                    const int r = rit % kRawStages;
-                    if (!(ok = mbar_wait(&raw_empty[r], ((rit / kRawStages) & 1) ^ 1, abort_flag, p.err, kErrTimeout + 1))) break;
-                    if (u + kPrefetchChunks < S.u1) bulk_prefetch_l2(chunk(u + kPrefetchChunks), RAWB);
-                    mbar_arrive_expect_tx(&raw_full[r], RAWB);
-                    bulk_g2s(raw + r * RAWB, chunk(u), RAWB, &raw_full[r]);
+                for (int u = S.u0; u < S.u1 && ok; u += CPR) {
+                    const int r = rit % NRAW;
+                    if (!(ok = mbar_wait<128>(&raw_empty[r], ((rit / NRAW) & 1) ^ 1, abort_flag, p.err, kErrTimeout + 1))) break;
+                    const int nch = min(CPR, S.u1 - u);
+                    mbar_arrive_expect_tx(&raw_full[r], nch * RAWB);
+                    for (int c = 0; c < nch; c++) bulk_g2s(raw + r * RSB + c * RAWB, chunk(u + c), RAWB, &raw_full[r]);
                     GEMM_EVENT(p, 1, rit);
                     rit++;
                 }
                 if (!ok)
-                    for (int i = (rit > kRawStages ? rit - kRawStages : 0); i < rit; i++)
-                        spin_bounded(&raw_full[i % kRawStages], (i / kRawStages) & 1);
+                    for (int i = (rit > NRAW ? rit - NRAW : 0); i < rit; i++)
+                        spin_bounded(&raw_full[i % NRAW], (i / NRAW) & 1);
             }
-            __syncwarp();
+        } else {
+            // ── F16 weights: A-tile TMA producer (completions counted on the even CTA) ──
+            if (lane == 0) {
+                int it = 0;
+                bool ok = true;
+                for (int u = S.u0; u < S.u1 && ok;) {
+                    const Seg g = make_seg(S, u, S.u1);
+                    for (int kbi = g.k0; kbi < g.k1 && ok; kbi++) {
+                        for (int s = 0; s < 4; s++) {
+                            const int st = it % NA;
+                            if (!(ok = mbar_wait<128>(&empty_a[st], ((it / NA) & 1) ^ 1, abort_flag, p.err, kErrTimeout + 11))) break;
+                            if (rank == 0) mbar_arrive_expect_tx(&full_a[st], 2 * kABytes);
+                            tma_load_2d_pair(aring + st * kABytes, &tm_w, kbi * 256 + s * 64, (2 * g.pt + (int)rank) * 128,
+                                             full_a0 + 8 * st);
+                            it++;
+                        }
+                    }
+                    u += g.k1 - g.k0;
+                }
+                if (!ok) {
+                    if (rank == 0)
+                        for (int i = (it > NA ? it - NA : 0); i < it; i++) spin_bounded(&full_a[i % NA], (i / NA) & 1);
+                    const uint64_t t0 = globaltimer();
+                    while (globaltimer() - t0 < 50000) {}
+                }
+            }
         }
-    } else if (warp == 1) {
-        // ── MMA issuer ──
-        if (lane == 0) {
+        __syncwarp();
+    } else if (role == R_MMA) {
+        // ── MMA issuer (even CTA) ──
+        if (lane == 0 && rank == 0) {
             int it = 0, si = 0;
             bool ok = true, issued = false;
+#ifdef DFB_GEMM_TRACE
+            long long tm_wa = 0, tm_wb = 0, tm_mma = 0, tm_cm = 0, tm_loop = 0, tm_last = 0;
+#endif
             for (int u = S.u0; u < S.u1 && ok;) {
                 const Seg g = make_seg(S, u, S.u1);
                 const int acc = si & 1;
                 if (!(ok = mbar_wait(&acc_empty[acc], ((si >> 1) & 1) ^ 1, abort_flag, p.err, kErrTimeout + 3))) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * 256;
-                const uint32_t idesc = idesc_f16_m128((uint32_t)g.nmma);
+                const uint32_t idesc = idesc_f16(256, (uint32_t)g.nmma);
                 uint32_t accum = 0;
                 for (int kbi = g.k0; kbi < g.k1 && ok; kbi++) {
                     for (int s = 0; s < 4; s++) {
-                        const int st = it % kStages;
-                        const uint32_t ph = (it / kStages) & 1;
-                        if (!(ok = mbar_wait(&full_b[st], ph, abort_flag, p.err, kErrTimeout + 4))) break;
-                        if constexpr (WT != W_F16)
-                            if (!(ok = mbar_wait(&full_a[st], ph, abort_flag, p.err, kErrTimeout + 5))) break;
-                        GEMM_EVENT(p, 4, it);
+                        const int st = it % NA, sl = (it / S.spb) % NBS;
+#ifdef DFB_GEMM_TRACE
+                        const long long c0 = clock64();
+#endif
+                        // full_a also carries the relay's arrival: this slice's B rows have landed
+                        if (!(ok = mbar_wait(&full_a[st], (it / NA) & 1, abort_flag, p.err, kErrTimeout + 5))) break;
+#ifdef DFB_GEMM_TRACE
+                        const long long c1 = clock64();
+                        const long long c2 = c1;
+#endif
                         tc_fence_after();
-                        const uint32_t a_addr = smem_u32(stages + st * kStageBytes);
-                        const uint32_t b_addr = a_addr + kABytes;
+                        const uint32_t a_addr = smem_u32(aring + st * kABytes);
+                        const uint32_t b_addr = smem_u32(bring + sl * S.bslot + (it % S.spb) * (S.bh * 128));
 #pragma unroll
                         for (int kk = 0; kk < 4; kk++) {
-                            mma_f16_ss(d_tmem, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32), idesc, accum);
+                            mma2_f16_ss(d_tmem, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32), idesc, accum);
                             accum = 1;
                         }
+#ifdef DFB_GEMM_TRACE
+                        const long long c3 = clock64();
+#endif
                         issued = true;
-                        mma_commit(&empty[st]);
-                        GEMM_EVENT(p, 5, it);
+                        mma2_commit_mc(&empty_a[st], 0x3);
+#ifdef DFB_GEMM_TRACE
+                        const long long c4 = clock64();
+                        tm_wa += c1 - c0; tm_wb += c2 - c1; tm_mma += c3 - c2; tm_cm += c4 - c3;
+                        if (it > 0) tm_loop += c0 - tm_last;
+                        tm_last = c4;
+#endif
                         it++;
                     }
                 }
                 if (!ok) break;
-                mma_commit(&acc_full[acc]);
+                mma2_commit_mc(&acc_full[acc], 0x3);
                 si++;
                 u += g.k1 - g.k0;
             }
             GEMM_STAMP(p, 3);
+#ifdef DFB_GEMM_TRACE
+            if (p.trace && blockIdx.x < 4) {
+                unsigned long long *tp = p.trace + 256 * 16 + ((size_t)blockIdx.x * 8 + 5) * 64 + 56;
+                tp[0] = tm_wa; tp[1] = tm_wb; tp[2] = tm_mma; tp[3] = tm_cm; tp[4] = tm_loop; tp[5] = it;
+            }
+#endif
             if (issued) {
                 // every MMA must have retired before TMEM is released
-                mma_commit(drain);
+                mma2_commit(drain);
                 spin_bounded(drain, 0);
             }
         }
         __syncwarp();
-    } else if (warp < 6) {
-        // ── dequantizers: thread = weight row of the tile ──
-        if constexpr (WT != W_F16) {
-            const int r = threadIdx.x - 64;
-            int it = 0, rit = 0;
+    } else if (role == R_RELAY) {
+        // ── relay (one thread per CTA), slice by slice: once the MMA of slice j - NA has
+        //    completed (empty_a, the same wait the A writers do), B slot (j - NA) % NBS is
+        //    free again (slot of load (j - NA) / spb, after its last slice); once this
+        //    CTA's B rows of slice j have landed (full_b of load j / spb), arrive on
+        //    full_a of slice j in the even CTA.  The MMA issuer so waits on one barrier
+        //    per slice, and no relay can fall a full phase behind the barriers it polls. ──
+        if (lane == 0) {
+            int n_it = 0;
+            for (int u = S.u0; u < S.u1;) {
+                const Seg g = make_seg(S, u, S.u1);
+                n_it += 4 * (g.k1 - g.k0);
+                u += g.k1 - g.k0;
+            }
             bool ok = true;
+            const int spb = S.spb;
+            for (int j = 0; j < n_it + NA && ok; j++) {
+                if (j >= NA) {
+                    // MMA of slice j - NA done (phase (j - NA) / NA of empty_a[j % NA]); the
+                    // B slot is free once the last slice of its load is done
+                    if (!(ok = mbar_wait<32>(&empty_a[j % NA], ((j / NA) & 1) ^ 1, abort_flag, p.err, kErrTimeout + 12))) break;
+                    const int jd = j - NA;
+                    if (jd % spb == spb - 1 || jd == n_it - 1) mbar_arrive(&empty_b[(jd / spb) % NBS]);
+                }
+                if (j < n_it) {
+                    const int o = j / spb;
+                    if (j % spb == 0)
+                        if (!(ok = mbar_wait<32>(&full_b[o % NBS], (o / NBS) & 1, abort_flag, p.err, kErrTimeout + 4))) break;
+                    mbar_arrive_cluster(full_a0 + 8 * (j % NA));
+                }
+            }
+        }
+        __syncwarp();
+    } else if (role == R_DEQ) {
+        // ── dequantizers: thread = weight row of this CTA's tile; set p takes slices
+        //    p and p + 2 of every k-block ──
+        if constexpr (WT != W_F16) {
+            const int di = deq_index(warp);
+            const int set = di >> 2;
+            const int r = (di & 3) * 32 + lane;
+            int rit = 0;
+            bool ok = true;
+#ifdef DFB_GEMM_TRACE
+            long long t_fence = 0, t_sync = 0, t_arrive = 0;
+            auto publish = [&](int st) {
+                const long long c0 = clock64();
+                fence_proxy_async_smem();
+                const long long c1 = clock64();
+                __syncwarp();
+                const long long c2 = clock64();
+                if (lane == 0) mbar_arrive_cluster(full_a0 + 8 * st);
+                const long long c3 = clock64();
+                t_fence += c1 - c0; t_sync += c2 - c1; t_arrive += c3 - c2;
+            };
+#else
+            auto publish = [&](int st) {
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(full_a0 + 8 * st);
+            };
+#endif
+            // Lane 0 polls (with a short back-off) and the warp takes its verdict; then every
+            // lane observes the completed phase itself (one try_wait, which succeeds: the
+            // phase cannot advance further without this warp), for acquire ordering.
+            auto wait_warp = [&](uint64_t *bar, uint32_t parity, int code, auto sleep_tag) {
+                int okw = 1;
+                if (lane == 0) okw = mbar_wait<decltype(sleep_tag)::value>(bar, parity, abort_flag, p.err, code);
+                const bool okb = __shfl_sync(0xffffffffu, okw, 0) != 0;
+                if (okb) (void)mbar_try_wait(bar, parity);
+                return okb;
+            };
+            auto wait_a = [&](int it) {
+                return wait_warp(&empty_a[it % NA], ((it / NA) & 1) ^ 1, kErrTimeout + 7, std::integral_constant<int, 32>{});
+            };
+            const int n_units = S.u1 - S.u0;
             for (int u = S.u0; u < S.u1 && ok;) {
                 const Seg g = make_seg(S, u, S.u1);
                 for (int kbi = g.k0; kbi < g.k1 && ok; kbi++) {
-                    const int rs = rit % kRawStages;
-                    ok = __all_sync(0xffffffffu, mbar_wait(&raw_full[rs], (rit / kRawStages) & 1, abort_flag, p.err, kErrTimeout + 6));
-                    if (!ok) break;
-                    if (r == 0) GEMM_EVENT(p, 2, rit);
-                    const uint8_t *R = raw + rs * RAWB;
+                    // unit rit of the range: raw stage rit / CPR, chunk rit % CPR in it
+                    const int rst = rit / CPR, rs = rst % NRAW;
+                    if (rit % CPR == 0) {
+                        ok = wait_warp(&raw_full[rs], (rst / NRAW) & 1, kErrTimeout + 6, std::integral_constant<int, 64>{});
+                        if (!ok) break;
+                        if (r == 0 && set == 0) GEMM_EVENT(p, 2, rst);
+                    }
+                    const uint8_t *R = raw + rs * RSB + (rit % CPR) * RAWB;
                     if constexpr (WT == W_Q4K) {
-                        Q4KRow meta;
-                        q4k_load_meta(R, r, meta);
+                        Q4KMeta meta;
+                        q4k_load_meta(R, r, set, meta);
                         #pragma unroll
-                        for (int s = 0; s < 4; s++) {
-                            const int st = it % kStages;
-                            ok = __all_sync(0xffffffffu, mbar_wait(&empty[st], ((it / kStages) & 1) ^ 1, abort_flag, p.err, kErrTimeout + 7));
-                            if (!ok) break;
-                            q4k_slice(R, r, s, meta, stages + st * kStageBytes);
-                            fence_proxy_async_smem();
-                            __syncwarp();
-                            if (lane == 0) mbar_arrive(&full_a[st]);
+                        for (int h = 0; h < 2; h++) {
+                            const int s = set + 2 * h, it = 4 * rit + s;
+                            if (!(ok = wait_a(it))) break;
+                            if (r == 0 && it < 32) GEMM_EVENT(p, 7, it);
+                            q4k_slice(R, r, s, 2 * h, meta, aring + (it % NA) * kABytes);
+                            publish(it % NA);
                             if (r == 0) GEMM_EVENT(p, 3, it);
-                            it++;
                         }
                     } else if constexpr (WT == W_Q6K) {
-                        Q6KRow meta;
-                        q6k_load_meta(R, r, meta);
+                        Q6KMeta meta;
+                        q6k_load_meta(R, r, set, meta);
                         Q6KHalf qv;
                         #pragma unroll
-                        for (int s = 0; s < 4; s++) {
-                            if ((s & 1) == 0) q6k_load_half(R, r, s >> 1, qv);
-                            const int st = it % kStages;
-                            ok = __all_sync(0xffffffffu, mbar_wait(&empty[st], ((it / kStages) & 1) ^ 1, abort_flag, p.err, kErrTimeout + 7));
-                            if (!ok) break;
-                            q6k_slice(qv, r, s, meta, stages + st * kStageBytes);
-                            fence_proxy_async_smem();
-                            __syncwarp();
-                            if (lane == 0) mbar_arrive(&full_a[st]);
-                            it++;
+                        for (int h = 0; h < 2; h++) {
+                            const int s = set + 2 * h, it = 4 * rit + s;
+                            q6k_load_half(R, r, h, qv);
+                            if (!(ok = wait_a(it))) break;
+                            q6k_slice(qv, r, s, 4 * h, meta, aring + (it % NA) * kABytes);
+                            publish(it % NA);
                         }
                     } else {
                         #pragma unroll
-                        for (int s = 0; s < 4; s++) {
-                            const int st = it % kStages;
-                            ok = __all_sync(0xffffffffu, mbar_wait(&empty[st], ((it / kStages) & 1) ^ 1, abort_flag, p.err, kErrTimeout + 7));
-                            if (!ok) break;
-                            q80_slice(R, r, s, stages + st * kStageBytes);
-                            fence_proxy_async_smem();
-                            __syncwarp();
-                            if (lane == 0) mbar_arrive(&full_a[st]);
-                            it++;
+                        for (int h = 0; h < 2; h++) {
+                            const int s = set + 2 * h, it = 4 * rit + s;
+                            if (!(ok = wait_a(it))) break;
+                            q80_slice(R, r, s, aring + (it % NA) * kABytes);
+                            publish(it % NA);
                         }
                     }
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&raw_empty[rs]);
+                    if (lane == 0 && (rit % CPR == CPR - 1 || rit == n_units - 1)) mbar_arrive(&raw_empty[rs]);
                     rit++;
                 }
                 u += g.k1 - g.k0;
             }
+#ifdef DFB_GEMM_TRACE
+            if (r == 0 && set == 0 && p.trace && blockIdx.x < 4) {
+                p.trace[256 * 16 + ((size_t)blockIdx.x * 8 + 7) * 64 + 60] = (unsigned long long)t_fence;
+                p.trace[256 * 16 + ((size_t)blockIdx.x * 8 + 7) * 64 + 61] = (unsigned long long)t_sync;
+                p.trace[256 * 16 + ((size_t)blockIdx.x * 8 + 7) * 64 + 62] = (unsigned long long)t_arrive;
+                p.trace[256 * 16 + ((size_t)blockIdx.x * 8 + 7) * 64 + 63] = (unsigned long long)(2 * rit);
+            }
+#endif
         }
     } else {
-        // ── epilogue: thread = TMEM lane = output feature ──
+        // ── epilogue: thread = TMEM lane = output feature of this CTA's tile ──
         const int q = warp & 3;
         const int row = 32 * q + lane;
-        const int half = warp >= 11 ? 1 : 0;
-        const int et = half ? 128 + (int)threadIdx.x - 352 : (int)threadIdx.x - 192;  // 0..255
+        const int half = epi_half(warp);
+        const int et = half * 128 + q * 32 + lane;  // 0..255
         uint32_t fix_phase = 0;
         int si = 0;
         bool ok = true;
-        const int first_ot = S.begin_of(blockIdx.x) / S.kb;
+        const int first_ot = S.begin_of(pair) / S.kb;
+        auto release_acc = [&](int acc) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(acc_empty0 + 8 * acc);
+        };
         for (int u = S.u0; u < S.u1 && ok;) {
             const Seg g = make_seg(S, u, S.u1);
+            const int tile = 2 * g.pt + (int)rank;
             const int acc = si & 1;
             // one thread waits, the barrier hands the outcome to the whole group
-            if (et == 0) *okflag = mbar_wait(&acc_full[acc], (si >> 1) & 1, abort_flag, p.err, kErrTimeout + 8) ? 1 : 0;
+            if (et == 0) *okflag = mbar_wait<256>(&acc_full[acc], (si >> 1) & 1, abort_flag, p.err, kErrTimeout + 8) ? 1 : 0;
             named_bar_sync(1, kEpiThreads);
             ok = *okflag != 0;
             if (!ok) break;
@@ -674,16 +896,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const uint32_t taddr = tmem_base + ((uint32_t)(32 * q) << 16) + acc * 256;
             const bool whole = g.k0 == 0 && g.k1 == S.kb;
-            const EpiRow er = epi_row<EPI>(p.epi, g.tile, row);
+            const EpiRow er = epi_row<EPI>(p.epi, tile, row);
             if constexpr (EPI == EPI_QKV || EPI == EPI_LOGITS) {
                 for (int t = et; t < g.ntok; t += kEpiThreads) s_pos[t] = p.epi.pos[g.m0 + t];
                 named_bar_sync(1, kEpiThreads);
             }
             // mode 0: whole tile straight from TMEM; 1: finisher with the other partials
-            // bulk-staged in the drained stage buffers; 2: finisher reading partials from L2;
+            // bulk-staged in the drained rings; 2: finisher reading partials from L2;
             // 3: not the finisher (nothing to emit)
             int mode = 0, nc = 1, me = 0;
-            const bool last_seg = u + (g.k1 - g.k0) == S.u1;  // stage buffers drained after this one
+            const bool last_seg = u + (g.k1 - g.k0) == S.u1;  // rings drained after this one
             if (!whole) {
                 // Split tile.  Partials are stored [64-column chunk][column][row] (32 KB per
                 // chunk, coalesced for the writers, bank-conflict-free in shared memory).
@@ -702,16 +924,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 named_bar_sync(1, kEpiThreads);
                 const int c_first = S.owner(g.ot * S.kb), c_last = S.owner((g.ot + 1) * S.kb - 1);
                 nc = c_last - c_first + 1;
-                me = blockIdx.x - c_first;
+                me = pair - c_first;
                 if (et == 0) {
-                    const int old = atomicAdd(&p.tile_cnt[g.ot], 1);
+                    const int old = atomicAdd(&p.tile_cnt[2 * g.ot + rank], 1);
                     *bcast = (old == nc - 1) ? 1 : 0;
                     if (nc > kMaxContrib) atomicCAS(p.err, 0, kErrTimeout + 9);  // launcher keeps nc <= kMaxContrib
                 }
                 if (et < nc && et < kMaxContrib) {  // (et < kEpiThreads covers kMaxContrib)
                     const int c = c_first + et;
                     const int sl = (S.begin_of(c) / S.kb == g.ot) ? 0 : 1;
-                    s_contrib[et] = ((long long)c * 2 + sl) * kWsTile;
+                    s_contrib[et] = ((long long)(2 * c + (int)rank) * 2 + sl) * kWsTile;
                 }
                 named_bar_sync(1, kEpiThreads);
                 if (et == 0) GEMM_EVENT(p, 6, 5 * si + 3);
@@ -721,14 +943,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     mode = (last_seg && nc - 1 <= kFixupPeers) ? 1 : 2;
                 }
             }
-            if (mode >= 2) {
-                // the accumulator is in the workspace: let the MMA warp reuse the TMEM buffer
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&acc_empty[acc]);
-            }
+            // the accumulator is in the workspace: let the MMA reuse the TMEM buffer
+            if (mode >= 2) release_acc(acc);
             if (mode != 3) {
-                const float *sbuf = reinterpret_cast<const float *>(stages);
+                const float *sbuf = reinterpret_cast<const float *>(aring);
                 bool staged_ok = true;
                 for (int cb = 0; cb < g.nmma && staged_ok; cb += 64) {
                     if (mode == 1) {
@@ -740,7 +958,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             mbar_arrive_expect_tx(fix_bar, (uint32_t)(nc - 1) * cols * 512);
                             for (int c = 0, k = 0; c < nc; c++) {
                                 if (c == me) continue;
-                                bulk_g2s(stages + (size_t)k * 32768, p.ws + s_contrib[c] + (size_t)(cb >> 6) * 8192,
+                                bulk_g2s(aring + (size_t)k * 32768, p.ws + s_contrib[c] + (size_t)(cb >> 6) * 8192,
                                          (uint32_t)cols * 512, fix_bar);
                                 k++;
                             }
@@ -787,15 +1005,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                   }
                 }
                 if (mode >= 1 && et == 0) {
-                    p.tile_cnt[g.ot] = 0;
+                    p.tile_cnt[2 * g.ot + rank] = 0;
                     GEMM_EVENT(p, 6, 5 * si + 4);
                 }
             }
-            if (mode <= 1) {
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&acc_empty[acc]);
-            }
+            if (mode <= 1) release_acc(acc);
             named_bar_sync(1, kEpiThreads);  // okflag / bcast are reused by the next segment
             if (et == 0 && si < 4) GEMM_STAMP(p, 5 + 2 * si);
             si++;
@@ -805,10 +1019,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     tc_fence_before();
     __syncthreads();
+    cluster_sync();  // no remote arrival or copy of either CTA is still in flight
     if (threadIdx.x == 0) GEMM_STAMP(p, 12);
-    if (warp == 1) {
+    if (role == R_MMA) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, 512);
+        tmem_dealloc2(tmem_base, 512);
     }
 }
 

@@ -3,6 +3,7 @@
 #pragma once
 #include <cuda_fp16.h>
 #include <cstdint>
+#include "ptx.cuh"
 
 namespace dfb {
 
@@ -120,6 +121,8 @@ __device__ __forceinline__ float block_sum(float v, float *red) {
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const float *__restrict__ x, const float *__restrict__ w, int d,
                                                       float eps, const int *__restrict__ cnt, __half *__restrict__ h) {
     __shared__ float red[33];
+    griddep_launch_dependents();
+    griddep_wait();  // x and the row count come from the previous kernels
     const int a = blockIdx.x;
     if (a >= cnt[CNT_M]) return;
     const float *xr = x + (size_t)a * d;

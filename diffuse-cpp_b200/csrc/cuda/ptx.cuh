@@ -1,5 +1,5 @@
 // Thin inline-PTX wrappers for the sm_100a features the kernels use:
-// mbarriers, TMA (bulk and tensor, never multicast), tcgen05 MMA/TMEM.
+// mbarriers, TMA (bulk and tensor loads, never multicast), CTA pairs, tcgen05 MMA/TMEM.
 #pragma once
 #include <cstdint>
 #include <cuda.h>
@@ -42,18 +42,38 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+// Acquire at cluster scope: for barriers the peer CTA arrives on.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
 
 // Bounded wait.  Returns false (and raises *abort and the global error code) when
-// the phase has not completed within timeout_ns, or when another role of the CTA
-// already aborted.  No wait in this library can spin forever.
+// the phase has not completed within timeout_ns, or when another role of the CTA or
+// another CTA of the launch already gave up.  No wait in this library can spin forever.
 constexpr uint64_t kWaitTimeoutNs = 4000000000ull;  // 4 s
+// kSleepNs > 0: back off between polls, for waiters off the critical path (a polling
+// warp takes issue slots from the MMA issuer on its scheduler).
+template <int kSleepNs = 0, bool kCluster = false>
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
                                           int *err, int code) {
     uint64_t t0 = 0;
     for (uint32_t it = 0;; ++it) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if (kCluster ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) return true;
+        if (kSleepNs > 0) __nanosleep(kSleepNs);
         if ((it & 63) == 63) {
             if (*abort_flag) return false;
+            if (*reinterpret_cast<volatile int *>(err)) {
+                *abort_flag = 1;
+                return false;
+            }
             const uint64_t now = globaltimer();
             if (t0 == 0) t0 = now;
             else if (now - t0 > kWaitTimeoutNs) {
@@ -102,17 +122,79 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-// ── tcgen05 ──
-__device__ __forceinline__ void tmem_alloc(uint32_t *holder_smem, uint32_t ncols) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(holder_smem)),
+// ── clusters (CTA pairs) and programmatic dependent launch ──
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// shared::cluster address of the object at the same offset in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t mapa_shared(const void *p, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+    return r;
+}
+// Every thread of every CTA of the cluster (release / acquire at cluster scope).
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Arrive on an mbarrier named by its shared::cluster address (this CTA's or the peer's).
+// Default (CTA-scope release) semantics: a cluster-scope release would first wait for
+// every earlier memory operation of the thread to become visible cluster-wide (about
+// 900 cycles per arrival measured here), and the data these arrivals publish is read
+// by the tensor core after the writer's proxy fence.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// Let the next kernel of the stream be scheduled / wait until the previous one has
+// completed and its memory is visible (no-ops without programmatic serialization).
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// 2-D tiled tensor load into this CTA's shared memory whose completion is counted on an
+// mbarrier of either CTA of the pair (cluster address).  Not a multicast load.
+__device__ __forceinline__ void tma_load_2d_pair(void *dst, const CUtensorMap *map, int x, int y, uint32_t bar_cluster) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+            "r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar_cluster)
+        : "memory");
+}
+
+// 3-D tiled tensor load (coordinates innermost first).
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int x, int y, int z, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::
+            "r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// 16-byte async copy global -> shared (LDGSTS path, not the TMA unit); src_bytes 0
+// fills the 16 bytes with zeros and reads nothing.
+__device__ __forceinline__ void cp_async16(uint32_t dst_smem, const void *src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst_smem), "l"(src), "r"(src_bytes) : "memory");
+}
+// Arrive on the mbarrier once every cp.async this thread issued so far has completed
+// (the arrival is pre-counted in the barrier's expected count).
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t *bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// ── tcgen05, CTA-pair form (every tcgen05 instruction of a kernel uses one cta_group) ──
+// Issued by the same warp of both CTAs of the pair.
+__device__ __forceinline__ void tmem_alloc2(uint32_t *holder_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(holder_smem)),
                  "r"(ncols)
                  : "memory");
 }
-__device__ __forceinline__ void tmem_relinquish() {
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+__device__ __forceinline__ void tmem_relinquish2() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
 }
-__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+__device__ __forceinline__ void tmem_dealloc2(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 __device__ __forceinline__ void tc_fence_before() {
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -120,20 +202,31 @@ __device__ __forceinline__ void tc_fence_before() {
 __device__ __forceinline__ void tc_fence_after() {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
-// D[tmem] (+)= A[smem] * B[smem]^T, kind::f16, one CTA.
-__device__ __forceinline__ void mma_f16_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                           uint32_t accumulate) {
+// D[tmem] (+)= A[smem] * B[smem]^T, kind::f16, issued by the even CTA of the pair:
+// A rows 0-127 come from the even CTA and 128-255 from the odd one (same smem offset),
+// B columns [0, N/2) from the even CTA and [N/2, N) from the odd one; each CTA's TMEM
+// receives its own 128 rows of D.
+__device__ __forceinline__ void mma2_f16_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
-// Arrive on an mbarrier once every previously issued tcgen05.mma of this thread completed.
-__device__ __forceinline__ void mma_commit(uint64_t *bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                     smem_u32(bar))
+// Arrive once on the mbarrier at this smem offset in every CTA of cta_mask when all
+// previously issued tcgen05.mma of this thread have completed.
+__device__ __forceinline__ void mma2_commit_mc(uint64_t *bar, uint16_t cta_mask) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            smem_u32(bar)),
+        "h"(cta_mask)
+        : "memory");
+}
+// Same, on this CTA's barrier only.
+__device__ __forceinline__ void mma2_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                  : "memory");
 }
 // 32 lanes x 16 columns of 32-bit: this thread's lane, columns [col, col+16).
@@ -159,12 +252,12 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t smem_addr) {
     d |= (uint64_t)2 << 61;                        // SWIZZLE_128B
     return d;
 }
-// Instruction descriptor: kind::f16, A/B f16, D f32, both K-major, M=128, N=n.
-__host__ __device__ __forceinline__ uint32_t idesc_f16_m128(uint32_t n) {
+// Instruction descriptor: kind::f16, A/B f16, D f32, both K-major, M=m, N=n.
+__host__ __device__ __forceinline__ uint32_t idesc_f16(uint32_t m, uint32_t n) {
     return (1u << 4)              // D = F32
            | (0u << 7) | (0u << 10)  // A, B = F16
            | ((n >> 3) << 17)     // N >> 3
-           | ((128u >> 4) << 24); // M >> 4
+           | ((m >> 4) << 24);    // M >> 4
 }
 
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
