@@ -24,7 +24,6 @@
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cstdint>
-#include <type_traits>
 #include "ptx.cuh"
 
 namespace dfb {
@@ -96,19 +95,22 @@ struct GemmParams {
 constexpr int kThreads = 640;            // 20 warps, roles below
 constexpr int kEpiThreads = 256;         // two epilogue warps per TMEM lane quarter
 constexpr int kDeqWarps = 8;             // two sets of four: even / odd k-slices
-constexpr int kABytes = 128 * 128;       // one A stage: this CTA's 128 weight rows x 64 f16
+constexpr int kSliceBytes = 128 * 128;   // one 64-wide k-slice of this CTA's 128 weight rows (f16)
+constexpr int kABytes = 2 * kSliceBytes;  // one A stage: two consecutive k-slices
 constexpr int kMaxTok = 256;             // tokens per MMA (N) of the pair
 constexpr int kWsTile = kMaxTok * 128;   // floats per partial tile (one CTA's 128 rows)
 constexpr int kErrTimeout = 0x100;
 constexpr int kMaxAStages = 6, kMaxBSlots = 24, kMaxRawStages = 4;
 
 // Ring depths per weight type, sized so that shared memory (227 KB) holds them:
-//  A ring   dequantized (or, for F16, TMA-loaded) weight slices, 16 KB each;
+//  A ring   dequantized (or, for F16, TMA-loaded) weights, two k-slices (32 KB) per
+//           stage: the MMA issuer waits and commits once per stage and each dequantizer
+//           fences once per stage;
 //  B ring   this CTA's activation rows of one k-slice; a slot holds half the token
 //           group (2-16 KB), so small token counts keep many slices in flight and hide
 //           the L2 latency of the activation loads;
 //  raw ring re-tiled weight chunks (one k-block of 256 for 128 rows).
-__host__ __device__ constexpr int a_stages(int wt) { return 4; }
+__host__ __device__ constexpr int a_stages(int wt) { return 2; }
 __host__ __device__ constexpr int b_ring_bytes(int wt) { return wt == W_F16 ? 112 * 1024 : 80 * 1024; }
 // A raw stage holds raw_cpr consecutive chunks of the CTA's unit range: the weight
 // stream reached ~3.8 TB/s with 18 KB stages and ~6-7 TB/s with 36-72 KB stages
@@ -124,7 +126,7 @@ enum WarpRole : int { R_DEQ = 0, R_MMA = 1, R_BPROD = 2, R_WPROD = 3, R_EPI = 4,
 __host__ __device__ constexpr int warp_role(int w) {
     return w == 0 ? R_BPROD : w == 1 ? R_MMA : w == 2 ? R_WPROD : w == 3 ? R_RELAY : w < 12 ? R_DEQ : R_EPI;
 }
-// dequantizer index 0..7 (set = index / 4 takes k-slices set and set + 2 of each k-block)
+// dequantizer index 0..7 (set = index / 4 takes k-slices 2 set, 2 set + 1 of each k-block)
 __host__ __device__ constexpr int deq_index(int w) { return w - 4; }
 // epilogue thread group: warps 12-15 and 16-19 each cover the four lane quarters
 __host__ __device__ constexpr int epi_half(int w) { return w >= 16 ? 1 : 0; }
@@ -193,8 +195,8 @@ __device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__
 
 // Q4_K chunk layout (per 128 rows): [d,dmin f16 x2: 4 B/row][scales: 12 B/row at 512]
 // [qs: 128 B/row at 2048, 16-byte chunk c stored at c ^ (row & 7)].
-// Scales of the four sub-blocks one dequant set uses: set p dequantizes k-slices p and
-// p + 2, i.e. sub-blocks 2p, 2p+1 (local 0, 1) and 2p+4, 2p+5 (local 2, 3).
+// Scales of the four sub-blocks one dequant set uses: set p dequantizes k-slices 2p and
+// 2p + 1, i.e. sub-blocks 4p .. 4p + 3 (local 0 .. 3).
 struct Q4KMeta {
     __half2 d2;
     __half2 sc[4], nsc[4], nmo[4];  // sc, -1024*sc, -(dmin*m) per sub-block, as f16 pairs
@@ -211,9 +213,9 @@ __device__ __forceinline__ void q4k_load_meta(const uint8_t *R, int r, int set, 
 #pragma unroll
     for (int l = 0; l < 4; l++) {
         // 6-bit scale / min of sub-block j (get_scale_min_k4 packing)
-        const int j = 2 * set + (l & 1) + 4 * (l >> 1);
+        const int j = 4 * set + l;
         int sc, mn;
-        if (l < 2) {  // j < 4
+        if (set == 0) {  // j < 4
             sc = qb(j) & 63;
             mn = qb(j + 4) & 63;
         } else {
@@ -262,8 +264,8 @@ __device__ __forceinline__ void q4k_slice(const uint8_t *R, int r, int s, int lo
 // Q6_K chunk layout: [ql: 128 B/row, chunk c at c ^ (row & 7)]
 // [qh: 64 B/row at 16384, chunk c at c ^ ((row >> 1) & 3)][scales i8: 16 B/row at 24576]
 // [d f16: 2 B/row at 26624].
-// d * scale of the eight 16-element groups one dequant set uses: set p takes slices p
-// and p + 2, i.e. groups 4p..4p+3 (local 0-3) and 4p+8..4p+11 (local 4-7).
+// d * scale of the eight 16-element groups one dequant set uses: set p takes slices 2p
+// and 2p + 1, i.e. groups 8p .. 8p + 7 (scale words 2p and 2p + 1).
 struct Q6KMeta {
     __half2 ds[8];
 };
@@ -272,7 +274,7 @@ __device__ __forceinline__ void q6k_load_meta(const uint8_t *R, int r, int set, 
     const uint4 sv = *reinterpret_cast<const uint4 *>(R + 24576 + 16 * r);
 #pragma unroll
     for (int h = 0; h < 2; h++) {
-        const int wi = set + 2 * h;  // scale word holding groups 4*wi .. 4*wi+3
+        const int wi = 2 * set + h;  // scale word holding groups 4*wi .. 4*wi+3
         const uint32_t w = wi == 0 ? sv.x : wi == 1 ? sv.y : wi == 2 ? sv.z : sv.w;
 #pragma unroll
         for (int i = 0; i < 4; i++) {
@@ -486,9 +488,9 @@ __device__ __forceinline__ void epi_chunk(const EpiArgs &e, const EpiRow &r, con
 // Barriers the MMA waits on (full_a, full_b, acc_empty) live in the even CTA; the odd
 // CTA's loads and arrivals reach them through cluster addresses.
 //
-// Shared memory (per CTA): [A ring: a_stages x 16 KB][B ring][raw ring][barriers]
+// Shared memory (per CTA): [A ring: a_stages x 32 KB][B ring][raw ring][barriers]
 // [token positions][contributor offsets].  Slice i (64 k) of the CTA's unit range uses
-// A stage i % a_stages and part i % spb of B slot (i / spb) % nbs.
+// half i % 2 of A stage (i / 2) % a_stages and part i % spb of B slot (i / spb) % nbs.
 //
 // Warps (warp_role): w0 activation producer, w1 MMA issuer (even CTA) + TMEM owner, w2
 // weight-chunk producer (F16 weights: A-tile TMA producer), w3 relay, w4-w11
@@ -501,12 +503,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     constexpr int NA = a_stages(WT), NRAW = raw_stages(WT), BRING = b_ring_bytes(WT);
     constexpr int CPR = raw_cpr(WT), RSB = CPR * RAWB;  // chunks and bytes per raw stage
     constexpr int kFixupPeers = (NA * kABytes + BRING) / 32768;  // partial chunks the drained rings hold
-    // the relay frees B slot j only after the MMA of slice j + NA: the B ring must hold at
-    // least NA slots of the widest group (16 KB) or the producer would wait on itself
-    // The relay frees a B slot once the MMA of the load's last slice + NA has completed,
-    // so the producer needs 2 + (NA - 1) / spb slots not to wait on itself; the widest
-    // group (128 rows per CTA, one slice per 16 KB load) needs the most.
-    static_assert(BRING / (kMaxTok / 2 * 128) >= 2 + (NA - 1), "B ring too shallow for the A ring");
+    // The relay frees the B slots of stage j - NA's slices while it handles stage j, after
+    // waiting for the B loads of stages up to j - 1: with one slice per load (the widest
+    // group, 16 KB loads) the producer needs 2 NA + 1 slots not to wait on itself.
+    static_assert(BRING / (kMaxTok / 2 * 128) >= 2 * NA + 1, "B ring too shallow for the A ring");
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *aring = smem;
@@ -598,7 +598,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 for (int kbi = g.k0; kbi < g.k1 && ok; kbi++) {
                     for (int s = 0; s < 4; s += S.spb) {
                         const int sl = ob % NBS;
-                        if (!(ok = mbar_wait<128>(&empty_b[sl], ((ob / NBS) & 1) ^ 1, abort_flag, p.err, kErrTimeout + 2))) break;
+                        if (!(ok = mbar_wait(&empty_b[sl], ((ob / NBS) & 1) ^ 1, abort_flag, p.err, kErrTimeout + 2))) break;
                         mbar_arrive_expect_tx(&full_b[sl], S.bslot);
                         tma_load_3d(bring + sl * S.bslot, xmap, 0, row0, kbi * 4 + s, &full_b[sl]);
                         GEMM_EVENT(p, 0, ob);
@@ -626,7 +626,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 bool ok = true;
                 for (int u = S.u0; u < S.u1 && ok; u += CPR) {
                     const int r = rit % NRAW;
-                    if (!(ok = mbar_wait<128>(&raw_empty[r], ((rit / NRAW) & 1) ^ 1, abort_flag, p.err, kErrTimeout + 1))) break;
+                    if (!(ok = mbar_wait(&raw_empty[r], ((rit / NRAW) & 1) ^ 1, abort_flag, p.err, kErrTimeout + 1))) break;
                     const int nch = min(CPR, S.u1 - u);
                     mbar_arrive_expect_tx(&raw_full[r], nch * RAWB);
                     for (int c = 0; c < nch; c++) bulk_g2s(raw + r * RSB + c * RAWB, chunk(u + c), RAWB, &raw_full[r]);
@@ -645,12 +645,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 for (int u = S.u0; u < S.u1 && ok;) {
                     const Seg g = make_seg(S, u, S.u1);
                     for (int kbi = g.k0; kbi < g.k1 && ok; kbi++) {
-                        for (int s = 0; s < 4; s++) {
+                        for (int s = 0; s < 4; s += 2) {  // one stage = two k-slices
                             const int st = it % NA;
-                            if (!(ok = mbar_wait<128>(&empty_a[st], ((it / NA) & 1) ^ 1, abort_flag, p.err, kErrTimeout + 11))) break;
+                            if (!(ok = mbar_wait(&empty_a[st], ((it / NA) & 1) ^ 1, abort_flag, p.err, kErrTimeout + 11))) break;
                             if (rank == 0) mbar_arrive_expect_tx(&full_a[st], 2 * kABytes);
-                            tma_load_2d_pair(aring + st * kABytes, &tm_w, kbi * 256 + s * 64, (2 * g.pt + (int)rank) * 128,
-                                             full_a0 + 8 * st);
+                            for (int h = 0; h < 2; h++)
+                                tma_load_2d_pair(aring + st * kABytes + h * kSliceBytes, &tm_w, kbi * 256 + (s + h) * 64,
+                                                 (2 * g.pt + (int)rank) * 128, full_a0 + 8 * st);
                             it++;
                         }
                     }
@@ -668,7 +669,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     } else if (role == R_MMA) {
         // ── MMA issuer (even CTA) ──
         if (lane == 0 && rank == 0) {
-            int it = 0, si = 0;
+            int ia = 0, si = 0;  // A stages consumed, accumulator segments
             bool ok = true, issued = false;
 #ifdef DFB_GEMM_TRACE
             long long tm_wa = 0, tm_wb = 0, tm_mma = 0, tm_cm = 0, tm_loop = 0, tm_last = 0;
@@ -682,24 +683,31 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 const uint32_t idesc = idesc_f16(256, (uint32_t)g.nmma);
                 uint32_t accum = 0;
                 for (int kbi = g.k0; kbi < g.k1 && ok; kbi++) {
-                    for (int s = 0; s < 4; s++) {
-                        const int st = it % NA, sl = (it / S.spb) % NBS;
+                    for (int s2 = 0; s2 < 2; s2++) {  // A stages of this k-block
+                        const int st = ia % NA;
 #ifdef DFB_GEMM_TRACE
                         const long long c0 = clock64();
 #endif
-                        // full_a also carries the relay's arrival: this slice's B rows have landed
-                        if (!(ok = mbar_wait(&full_a[st], (it / NA) & 1, abort_flag, p.err, kErrTimeout + 5))) break;
+                        // full_a also carries the relays' arrivals: this stage's B rows have landed
+                        if (!(ok = mbar_wait(&full_a[st], (ia / NA) & 1, abort_flag, p.err, kErrTimeout + 5))) break;
 #ifdef DFB_GEMM_TRACE
                         const long long c1 = clock64();
                         const long long c2 = c1;
 #endif
+                        GEMM_EVENT(p, 4, ia);
                         tc_fence_after();
                         const uint32_t a_addr = smem_u32(aring + st * kABytes);
-                        const uint32_t b_addr = smem_u32(bring + sl * S.bslot + (it % S.spb) * (S.bh * 128));
 #pragma unroll
-                        for (int kk = 0; kk < 4; kk++) {
-                            mma2_f16_ss(d_tmem, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32), idesc, accum);
-                            accum = 1;
+                        for (int h = 0; h < 2; h++) {
+                            const int it = 2 * ia + h;
+                            const uint32_t b_addr =
+                                smem_u32(bring + ((it / S.spb) % NBS) * S.bslot + (it % S.spb) * (S.bh * 128));
+#pragma unroll
+                            for (int kk = 0; kk < 4; kk++) {
+                                mma2_f16_ss(d_tmem, sw128_desc(a_addr + h * kSliceBytes + kk * 32),
+                                            sw128_desc(b_addr + kk * 32), idesc, accum);
+                                accum = 1;
+                            }
                         }
 #ifdef DFB_GEMM_TRACE
                         const long long c3 = clock64();
@@ -709,10 +717,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #ifdef DFB_GEMM_TRACE
                         const long long c4 = clock64();
                         tm_wa += c1 - c0; tm_wb += c2 - c1; tm_mma += c3 - c2; tm_cm += c4 - c3;
-                        if (it > 0) tm_loop += c0 - tm_last;
+                        if (ia > 0) tm_loop += c0 - tm_last;
                         tm_last = c4;
 #endif
-                        it++;
+                        GEMM_EVENT(p, 5, ia);
+                        ia++;
                     }
                 }
                 if (!ok) break;
@@ -724,7 +733,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #ifdef DFB_GEMM_TRACE
             if (p.trace && blockIdx.x < 4) {
                 unsigned long long *tp = p.trace + 256 * 16 + ((size_t)blockIdx.x * 8 + 5) * 64 + 56;
-                tp[0] = tm_wa; tp[1] = tm_wb; tp[2] = tm_mma; tp[3] = tm_cm; tp[4] = tm_loop; tp[5] = it;
+                tp[0] = tm_wa; tp[1] = tm_wb; tp[2] = tm_mma; tp[3] = tm_cm; tp[4] = tm_loop; tp[5] = ia;
             }
 #endif
             if (issued) {
@@ -735,12 +744,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
     } else if (role == R_RELAY) {
-        // ── relay (one thread per CTA), slice by slice: once the MMA of slice j - NA has
-        //    completed (empty_a, the same wait the A writers do), B slot (j - NA) % NBS is
-        //    free again (slot of load (j - NA) / spb, after its last slice); once this
-        //    CTA's B rows of slice j have landed (full_b of load j / spb), arrive on
-        //    full_a of slice j in the even CTA.  The MMA issuer so waits on one barrier
-        //    per slice, and no relay can fall a full phase behind the barriers it polls. ──
+        // ── relay (one thread per CTA), A stage by A stage: once the MMA of stage j - NA
+        //    has completed (empty_a, the same wait the A writers do), the B slots of its
+        //    slices are free again (a slot after the last slice of its load); once this
+        //    CTA's B rows of stage j have landed (full_b), arrive on full_a of stage j in
+        //    the even CTA.  The MMA issuer so waits on one barrier per stage, and no relay
+        //    can fall a full phase behind the barriers it polls. ──
         if (lane == 0) {
             int n_it = 0;
             for (int u = S.u0; u < S.u1;) {
@@ -749,19 +758,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 u += g.k1 - g.k0;
             }
             bool ok = true;
-            const int spb = S.spb;
-            for (int j = 0; j < n_it + NA && ok; j++) {
+            const int spb = S.spb, n_st = n_it / 2;
+            for (int j = 0; j < n_st + NA && ok; j++) {  // A stage j = slices 2j, 2j + 1
                 if (j >= NA) {
-                    // MMA of slice j - NA done (phase (j - NA) / NA of empty_a[j % NA]); the
-                    // B slot is free once the last slice of its load is done
-                    if (!(ok = mbar_wait<32>(&empty_a[j % NA], ((j / NA) & 1) ^ 1, abort_flag, p.err, kErrTimeout + 12))) break;
-                    const int jd = j - NA;
-                    if (jd % spb == spb - 1 || jd == n_it - 1) mbar_arrive(&empty_b[(jd / spb) % NBS]);
+                    // MMA of stage j - NA done (phase (j - NA) / NA of empty_a[j % NA]): free
+                    // the B slots whose last slice lies in it
+                    if (!(ok = mbar_wait(&empty_a[j % NA], ((j / NA) & 1) ^ 1, abort_flag, p.err, kErrTimeout + 12))) break;
+                    for (int jd = 2 * (j - NA); jd < 2 * (j - NA) + 2; jd++)
+                        if (jd % spb == spb - 1) mbar_arrive(&empty_b[(jd / spb) % NBS]);
                 }
-                if (j < n_it) {
-                    const int o = j / spb;
-                    if (j % spb == 0)
-                        if (!(ok = mbar_wait<32>(&full_b[o % NBS], (o / NBS) & 1, abort_flag, p.err, kErrTimeout + 4))) break;
+                if (j < n_st) {
+                    for (int js = 2 * j; js < 2 * j + 2 && ok; js++) {
+                        const int o = js / spb;
+                        if (js % spb == 0)
+                            ok = mbar_wait(&full_b[o % NBS], (o / NBS) & 1, abort_flag, p.err, kErrTimeout + 4);
+                    }
+                    if (!ok) break;
                     mbar_arrive_cluster(full_a0 + 8 * (j % NA));
                 }
             }
@@ -795,18 +807,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 if (lane == 0) mbar_arrive_cluster(full_a0 + 8 * st);
             };
 #endif
-            // Lane 0 polls (with a short back-off) and the warp takes its verdict; then every
+            // Lane 0 waits and the warp takes its verdict; then every
             // lane observes the completed phase itself (one try_wait, which succeeds: the
             // phase cannot advance further without this warp), for acquire ordering.
-            auto wait_warp = [&](uint64_t *bar, uint32_t parity, int code, auto sleep_tag) {
+            auto wait_warp = [&](uint64_t *bar, uint32_t parity, int code) {
                 int okw = 1;
-                if (lane == 0) okw = mbar_wait<decltype(sleep_tag)::value>(bar, parity, abort_flag, p.err, code);
+                if (lane == 0) okw = mbar_wait(bar, parity, abort_flag, p.err, code);
                 const bool okb = __shfl_sync(0xffffffffu, okw, 0) != 0;
                 if (okb) (void)mbar_try_wait(bar, parity);
                 return okb;
             };
-            auto wait_a = [&](int it) {
-                return wait_warp(&empty_a[it % NA], ((it / NA) & 1) ^ 1, kErrTimeout + 7, std::integral_constant<int, 32>{});
+            auto wait_a = [&](int ia) {
+                return wait_warp(&empty_a[ia % NA], ((ia / NA) & 1) ^ 1, kErrTimeout + 7);
             };
             const int n_units = S.u1 - S.u0;
             for (int u = S.u0; u < S.u1 && ok;) {
@@ -815,43 +827,37 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     // unit rit of the range: raw stage rit / CPR, chunk rit % CPR in it
                     const int rst = rit / CPR, rs = rst % NRAW;
                     if (rit % CPR == 0) {
-                        ok = wait_warp(&raw_full[rs], (rst / NRAW) & 1, kErrTimeout + 6, std::integral_constant<int, 64>{});
+                        ok = wait_warp(&raw_full[rs], (rst / NRAW) & 1, kErrTimeout + 6);
                         if (!ok) break;
                         if (r == 0 && set == 0) GEMM_EVENT(p, 2, rst);
                     }
                     const uint8_t *R = raw + rs * RSB + (rit % CPR) * RAWB;
+                    // this set's A stage of the k-block: slices 2 set, 2 set + 1
+                    const int ia = 2 * rit + set;
+                    uint8_t *A = aring + (ia % NA) * kABytes;
                     if constexpr (WT == W_Q4K) {
                         Q4KMeta meta;
                         q4k_load_meta(R, r, set, meta);
+                        if (!(ok = wait_a(ia))) break;
+                        if (r == 0 && ia < 32) GEMM_EVENT(p, 7, ia);
                         #pragma unroll
-                        for (int h = 0; h < 2; h++) {
-                            const int s = set + 2 * h, it = 4 * rit + s;
-                            if (!(ok = wait_a(it))) break;
-                            if (r == 0 && it < 32) GEMM_EVENT(p, 7, it);
-                            q4k_slice(R, r, s, 2 * h, meta, aring + (it % NA) * kABytes);
-                            publish(it % NA);
-                            if (r == 0) GEMM_EVENT(p, 3, it);
-                        }
+                        for (int h = 0; h < 2; h++) q4k_slice(R, r, 2 * set + h, 2 * h, meta, A + h * kSliceBytes);
+                        publish(ia % NA);
+                        if (r == 0) GEMM_EVENT(p, 3, ia);
                     } else if constexpr (WT == W_Q6K) {
                         Q6KMeta meta;
                         q6k_load_meta(R, r, set, meta);
                         Q6KHalf qv;
+                        q6k_load_half(R, r, set, qv);  // slices 2 set, 2 set + 1 share one half of ql / qh
+                        if (!(ok = wait_a(ia))) break;
                         #pragma unroll
-                        for (int h = 0; h < 2; h++) {
-                            const int s = set + 2 * h, it = 4 * rit + s;
-                            q6k_load_half(R, r, h, qv);
-                            if (!(ok = wait_a(it))) break;
-                            q6k_slice(qv, r, s, 4 * h, meta, aring + (it % NA) * kABytes);
-                            publish(it % NA);
-                        }
+                        for (int h = 0; h < 2; h++) q6k_slice(qv, r, 2 * set + h, 4 * h, meta, A + h * kSliceBytes);
+                        publish(ia % NA);
                     } else {
+                        if (!(ok = wait_a(ia))) break;
                         #pragma unroll
-                        for (int h = 0; h < 2; h++) {
-                            const int s = set + 2 * h, it = 4 * rit + s;
-                            if (!(ok = wait_a(it))) break;
-                            q80_slice(R, r, s, aring + (it % NA) * kABytes);
-                            publish(it % NA);
-                        }
+                        for (int h = 0; h < 2; h++) q80_slice(R, r, 2 * set + h, A + h * kSliceBytes);
+                        publish(ia % NA);
                     }
                     __syncwarp();
                     if (lane == 0 && (rit % CPR == CPR - 1 || rit == n_units - 1)) mbar_arrive(&raw_empty[rs]);
@@ -864,7 +870,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 p.trace[256 * 16 + ((size_t)blockIdx.x * 8 + 7) * 64 + 60] = (unsigned long long)t_fence;
                 p.trace[256 * 16 + ((size_t)blockIdx.x * 8 + 7) * 64 + 61] = (unsigned long long)t_sync;
                 p.trace[256 * 16 + ((size_t)blockIdx.x * 8 + 7) * 64 + 62] = (unsigned long long)t_arrive;
-                p.trace[256 * 16 + ((size_t)blockIdx.x * 8 + 7) * 64 + 63] = (unsigned long long)(2 * rit);
+                p.trace[256 * 16 + ((size_t)blockIdx.x * 8 + 7) * 64 + 63] = (unsigned long long)rit;
             }
 #endif
         }
@@ -888,7 +894,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const int tile = 2 * g.pt + (int)rank;
             const int acc = si & 1;
             // one thread waits, the barrier hands the outcome to the whole group
-            if (et == 0) *okflag = mbar_wait<256>(&acc_full[acc], (si >> 1) & 1, abort_flag, p.err, kErrTimeout + 8) ? 1 : 0;
+            if (et == 0) *okflag = mbar_wait(&acc_full[acc], (si >> 1) & 1, abort_flag, p.err, kErrTimeout + 8) ? 1 : 0;
             named_bar_sync(1, kEpiThreads);
             ok = *okflag != 0;
             if (!ok) break;

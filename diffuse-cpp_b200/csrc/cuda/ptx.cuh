@@ -42,15 +42,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// Acquire at cluster scope: for barriers the peer CTA arrives on.
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t parity) {
+// try_wait with a suspend-time hint: the thread sleeps in the instruction until the
+// phase completes (it is woken then) or the hint elapses, instead of spinning and
+// taking issue slots from busy warps on its scheduler.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity, uint32_t hint_ns) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
         : "memory");
     return ok != 0;
 }
@@ -59,28 +61,22 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t pa
 // the phase has not completed within timeout_ns, or when another role of the CTA or
 // another CTA of the launch already gave up.  No wait in this library can spin forever.
 constexpr uint64_t kWaitTimeoutNs = 4000000000ull;  // 4 s
-// kSleepNs > 0: back off between polls, for waiters off the critical path (a polling
-// warp takes issue slots from the MMA issuer on its scheduler).
-template <int kSleepNs = 0, bool kCluster = false>
+constexpr uint32_t kSuspendHintNs = 200000;         // 0.2 ms per try_wait, then re-check the flags
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
                                           int *err, int code) {
-    uint64_t t0 = 0;
-    for (uint32_t it = 0;; ++it) {
-        if (kCluster ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) return true;
-        if (kSleepNs > 0) __nanosleep(kSleepNs);
-        if ((it & 63) == 63) {
-            if (*abort_flag) return false;
-            if (*reinterpret_cast<volatile int *>(err)) {
-                *abort_flag = 1;
-                return false;
-            }
-            const uint64_t now = globaltimer();
-            if (t0 == 0) t0 = now;
-            else if (now - t0 > kWaitTimeoutNs) {
-                *abort_flag = 1;
-                atomicCAS(err, 0, code);
-                return false;
-            }
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer();
+    for (;;) {
+        if (mbar_try_wait_sleep(bar, parity, kSuspendHintNs)) return true;
+        if (*abort_flag) return false;
+        if (*reinterpret_cast<volatile int *>(err)) {
+            *abort_flag = 1;
+            return false;
+        }
+        if (globaltimer() - t0 > kWaitTimeoutNs) {
+            *abort_flag = 1;
+            atomicCAS(err, 0, code);
+            return false;
         }
     }
 }
