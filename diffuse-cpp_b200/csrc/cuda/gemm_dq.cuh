@@ -119,15 +119,19 @@ __host__ __device__ constexpr int raw_stages(int wt) { return wt == W_Q4K ? 2 : 
 __host__ __device__ constexpr int raw_cpr(int wt) { return wt == W_Q4K ? 2 : 1; }
 
 // Warp roles.  A warp runs on scheduler warp % 4 and may only access TMEM lanes
-// 32*(warp % 4)..+31.  Each scheduler gets one light role (w0 activation producer, w1
-// MMA issuer, w2 weight-chunk producer, w3 relay), one dequantizer of each set (w4-w7
-// set 0, w8-w11 set 1) and two epilogue warps (w12-w19: every lane quarter twice).
+// 32*(warp % 4)..+31.  The MMA issuer (w1) shares its scheduler only with light roles
+// (w5 activation producer, w9 relay) and two epilogue warps: next to busy dequantizers
+// each tcgen05.mma took ~170 cycles to issue instead of ~75.  The eight dequantizers
+// (set 0: w0 w2 w3 w8, set 1: w4 w6 w7 w10) and the weight-chunk producer (w11) fill the
+// other three schedulers; w12-w19 are the epilogue (every lane quarter twice).
 enum WarpRole : int { R_DEQ = 0, R_MMA = 1, R_BPROD = 2, R_WPROD = 3, R_EPI = 4, R_RELAY = 5 };
 __host__ __device__ constexpr int warp_role(int w) {
-    return w == 0 ? R_BPROD : w == 1 ? R_MMA : w == 2 ? R_WPROD : w == 3 ? R_RELAY : w < 12 ? R_DEQ : R_EPI;
+    return w == 1 ? R_MMA : w == 5 ? R_BPROD : w == 9 ? R_RELAY : w == 11 ? R_WPROD : w >= 12 ? R_EPI : R_DEQ;
 }
 // dequantizer index 0..7 (set = index / 4 takes k-slices 2 set, 2 set + 1 of each k-block)
-__host__ __device__ constexpr int deq_index(int w) { return w - 4; }
+__host__ __device__ constexpr int deq_index(int w) {
+    return w == 0 ? 0 : w == 2 ? 1 : w == 3 ? 2 : w == 8 ? 3 : w == 4 ? 4 : w == 6 ? 5 : w == 7 ? 6 : 7;  // w10 -> 7
+}
 // epilogue thread group: warps 12-15 and 16-19 each cover the four lane quarters
 __host__ __device__ constexpr int epi_half(int w) { return w >= 16 ? 1 : 0; }
 
@@ -492,10 +496,10 @@ __device__ __forceinline__ void epi_chunk(const EpiArgs &e, const EpiRow &r, con
 // [token positions][contributor offsets].  Slice i (64 k) of the CTA's unit range uses
 // half i % 2 of A stage (i / 2) % a_stages and part i % spb of B slot (i / spb) % nbs.
 //
-// Warps (warp_role): w0 activation producer, w1 MMA issuer (even CTA) + TMEM owner, w2
-// weight-chunk producer (F16 weights: A-tile TMA producer), w3 relay, w4-w11
-// dequantizers (two sets of four; thread = weight row), w12-w19 epilogue (thread = TMEM
-// lane; w12-15 and w16-19 take alternate 16-column chunks).
+// Warps (warp_role): w1 MMA issuer (even CTA) + TMEM owner, w5 activation producer, w9
+// relay, w11 weight-chunk producer (F16 weights: A-tile TMA producer), w0 w2-w4 w6-w8
+// w10 dequantizers (two sets of four; thread = weight row), w12-w19 epilogue (thread =
+// TMEM lane; w12-15 and w16-19 take alternate 16-column chunks).
 template <int WT, int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     dq_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ XMaps xm, GemmParams p) {
