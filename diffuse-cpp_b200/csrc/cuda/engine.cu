@@ -1114,12 +1114,14 @@ extern "C" int dfb_gen_logits(dfb_ctx *c, int row0, int nrows, float *host) {
 // middle of their work.  dfb_linear_noalloc serves them: the only scratch the dequant
 // GEMM needs (split-tile partial sums and arrival counters) lives in the fixed arrays
 // below, compiled into this library.  Every GPU that loads the library holds them
-// (8 MiB + 8 KiB) until the process exits.
+// (6 MiB + 16 KiB) until the process exits.
 namespace {
 constexpr int kNoallocGrid = 32;                      // CTAs per launch (bounds the scratch)
-constexpr int kNoallocMaxTokens = kMaxTok;            // one token group
+constexpr int kNoallocMaxTokens = 256;                // at most two token groups
+constexpr int kNoallocMaxGroups = (kNoallocMaxTokens + kMaxTok - 1) / kMaxTok;
 constexpr int kNoallocMaxTiles = 2040;                // 128-row output tiles (lm_head of 261k vocab)
-constexpr int kNoallocCnt = kNoallocMaxTiles + 8;     // [tiles] counters, then M, then the error flag
+constexpr int kCntM = kNoallocMaxGroups * kNoallocMaxTiles;  // [groups x tiles] counters, then M, then the error flag
+constexpr int kNoallocCnt = kCntM + 8;
 static __device__ __align__(256) float g_noalloc_ws[(size_t)kNoallocGrid * 2 * kWsTile];
 static __device__ __align__(256) int g_noalloc_cnt[kNoallocCnt];
 
@@ -1132,10 +1134,10 @@ std::mutex g_noalloc_mu;
 
 // Zeroes the counters the launch will use and the error flag, stores M.
 __global__ void noalloc_prep_kernel(int *cnt, int n_tiles, int M) {
-    for (int i = threadIdx.x; i < n_tiles; i += blockDim.x) cnt[i] = 0;
+    for (int i = threadIdx.x; i < kNoallocMaxGroups * n_tiles; i += blockDim.x) cnt[i] = 0;
     if (threadIdx.x == 0) {
-        cnt[kNoallocMaxTiles] = M;
-        cnt[kNoallocMaxTiles + 1] = 0;
+        cnt[kCntM] = M;
+        cnt[kCntM + 1] = 0;
     }
 }
 
@@ -1149,10 +1151,10 @@ int noalloc_launch(const WMat &w, const XMaps &xm, const EpiArgs &e, const Noall
     p.K = w.K;
     p.n_tiles = w.n_tiles;
     p.kb = w.kb;
-    p.m_dev = nd.cnt + kNoallocMaxTiles;
+    p.m_dev = nd.cnt + kCntM;
     p.ws = nd.ws;
     p.tile_cnt = nd.cnt;
-    p.err = nd.cnt + kNoallocMaxTiles + 1;
+    p.err = nd.cnt + kCntM + 1;
     p.epi = e;
     const int n_pairs = std::min(kNoallocGrid / 2, (kMaxContrib - 2) * (w.n_tiles / 2));
     CK(launch_k(kern, dim3(2 * n_pairs), dim3(kThreads), smem, st, false, w.tm, xm, p));
@@ -1215,7 +1217,7 @@ extern "C" int dfb_linear_noalloc(const dfb_model *m, int role, int layer, const
     }
     CK(cudaStreamSynchronize(st));
     int err = 0;
-    CK(cudaMemcpy(&err, nd.cnt + kNoallocMaxTiles + 1, sizeof(int), cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy(&err, nd.cnt + kCntM + 1, sizeof(int), cudaMemcpyDeviceToHost));
     if (err) return set_err(DFB_ERR_TIMEOUT, "a GEMM gave up a bounded wait (code 0x%x)", err);
     return DFB_OK;
 }

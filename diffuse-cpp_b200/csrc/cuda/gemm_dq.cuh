@@ -6,10 +6,11 @@
 // Operands.  W is the GGUF weight (Q4_K / Q6_K / Q8_0 raw blocks re-tiled at load,
 // or F16), dequantized to f16 in registers; X is the f16 activation matrix [tokens][K].
 // The MMA is "swap-AB" and paired (tcgen05 cta_group::2, M = 256): the A operand is a
-// tile of 256 output features, 128 dequantized into the shared memory of each CTA of a
-// pair (UMMA 128-byte-swizzled K-major layout); the B operand is a group of up to 256
-// tokens of X, each CTA holding half of them (TMA tensor loads, same swizzle).  The f32
-// accumulator lives in TMEM: lane = output feature, column = token.
+// tile of 256 output features, 128 dequantized into the TMEM of each CTA of a pair (F16
+// weights: TMA-loaded into shared memory, 128-byte-swizzled K-major); the B operand is a
+// group of up to 192 tokens of X, each CTA holding half of them (TMA tensor loads into
+// shared memory, same swizzle).  The f32 accumulator lives in TMEM: lane = output
+// feature, column = token.
 //
 // Work split.  Units are (pair tile of 256 output rows, token group, k-block of 256); a
 // persistent grid of CTA pairs (one CTA per SM) takes equal contiguous unit ranges
@@ -97,48 +98,51 @@ constexpr int kEpiThreads = 256;         // two epilogue warps per TMEM lane qua
 constexpr int kDeqWarps = 8;             // two sets of four: even / odd k-slices
 constexpr int kSliceBytes = 128 * 128;   // one 64-wide k-slice of this CTA's 128 weight rows (f16)
 constexpr int kABytes = 2 * kSliceBytes;  // one A stage: two consecutive k-slices
-constexpr int kMaxTok = 256;             // tokens per MMA (N) of the pair
+constexpr int kMaxTok = 192;             // tokens per MMA group (N) of the pair
 constexpr int kWsTile = kMaxTok * 128;   // floats per partial tile (one CTA's 128 rows)
 constexpr int kErrTimeout = 0x100;
 constexpr int kMaxAStages = 6, kMaxBSlots = 24, kMaxRawStages = 4;
+// TMEM (512 columns per CTA): accumulators [0, 192) and [192, 384); dequantized A stages
+// (quantized weights) at [384 + 64 st, +64): lane = weight row, 32 columns per k-slice.
+constexpr int kTmemA = 2 * kMaxTok;
+constexpr int kTmemAStage = 64;
 
-// Ring depths per weight type, sized so that shared memory (227 KB) holds them:
-//  A ring   dequantized (or, for F16, TMA-loaded) weights, two k-slices (32 KB) per
-//           stage: the MMA issuer waits and commits once per stage and each dequantizer
-//           fences once per stage;
-//  B ring   this CTA's activation rows of one k-slice; a slot holds half the token
-//           group (2-16 KB), so small token counts keep many slices in flight and hide
-//           the L2 latency of the activation loads;
-//  raw ring re-tiled weight chunks (one k-block of 256 for 128 rows).
+// Rings per weight type, sized so that shared memory (227 KB) holds them:
+//  A        two k-slices per stage, two stages: dequantized weights go to TMEM (written
+//           by tcgen05.st, read by the MMA from TMEM: no shared-memory round trip and no
+//           proxy fence, which cost ~1.2k cycles per warp and stage); F16 weights are
+//           TMA-loaded into a shared-memory ring instead;
+//  B ring   this CTA's activation rows of 1-4 k-slices per slot (2-12 KB), so small
+//           token counts keep many slices in flight and hide the L2 latency;
+//  raw ring re-tiled weight chunks (one k-block of 256 for 128 rows), grouped.
 __host__ __device__ constexpr int a_stages(int wt) { return 2; }
-__host__ __device__ constexpr int b_ring_bytes(int wt) { return wt == W_F16 ? 112 * 1024 : 80 * 1024; }
+__host__ __device__ constexpr int a_ring_bytes(int wt) { return wt == W_F16 ? 2 * kABytes : 0; }
+__host__ __device__ constexpr int b_ring_bytes(int wt) { return 112 * 1024; }
 // A raw stage holds raw_cpr consecutive chunks of the CTA's unit range: the weight
 // stream reached ~3.8 TB/s with 18 KB stages and ~6-7 TB/s with 36-72 KB stages
 // (same bytes in flight), so small chunks are grouped.
-__host__ __device__ constexpr int raw_stages(int wt) { return wt == W_Q4K ? 2 : wt == W_Q6K ? 3 : wt == W_Q80 ? 2 : 0; }
+__host__ __device__ constexpr int raw_stages(int wt) { return wt == W_Q4K ? 3 : wt == W_Q6K ? 4 : wt == W_Q80 ? 3 : 0; }
 __host__ __device__ constexpr int raw_cpr(int wt) { return wt == W_Q4K ? 2 : 1; }
 
 // Warp roles.  A warp runs on scheduler warp % 4 and may only access TMEM lanes
-// 32*(warp % 4)..+31.  The MMA issuer (w1) shares its scheduler only with light roles
-// (w5 activation producer, w9 relay) and two epilogue warps: next to busy dequantizers
-// each tcgen05.mma took ~170 cycles to issue instead of ~75.  The eight dequantizers
-// (set 0: w0 w2 w3 w8, set 1: w4 w6 w7 w10) and the weight-chunk producer (w11) fill the
-// other three schedulers; w12-w19 are the epilogue (every lane quarter twice).
+// 32*(warp % 4)..+31, so the dequantizers (they write A into TMEM) and the epilogue cover
+// every lane quarter: w4-w7 dequantizer set 0, w8-w11 set 1, w12-w19 epilogue (each
+// quarter twice); w0 activation producer, w1 MMA issuer, w2 weight-chunk producer, w3
+// relay.
 enum WarpRole : int { R_DEQ = 0, R_MMA = 1, R_BPROD = 2, R_WPROD = 3, R_EPI = 4, R_RELAY = 5 };
 __host__ __device__ constexpr int warp_role(int w) {
-    return w == 1 ? R_MMA : w == 5 ? R_BPROD : w == 9 ? R_RELAY : w == 11 ? R_WPROD : w >= 12 ? R_EPI : R_DEQ;
+    return w == 0 ? R_BPROD : w == 1 ? R_MMA : w == 2 ? R_WPROD : w == 3 ? R_RELAY : w < 12 ? R_DEQ : R_EPI;
 }
-// dequantizer index 0..7 (set = index / 4 takes k-slices 2 set, 2 set + 1 of each k-block)
-__host__ __device__ constexpr int deq_index(int w) {
-    return w == 0 ? 0 : w == 2 ? 1 : w == 3 ? 2 : w == 8 ? 3 : w == 4 ? 4 : w == 6 ? 5 : w == 7 ? 6 : 7;  // w10 -> 7
-}
+// dequantizer index 0..7: set = index / 4 takes k-slices 2 set, 2 set + 1 of each k-block;
+// its weight rows are the warp's TMEM lane quarter
+__host__ __device__ constexpr int deq_index(int w) { return w - 4; }
 // epilogue thread group: warps 12-15 and 16-19 each cover the four lane quarters
 __host__ __device__ constexpr int epi_half(int w) { return w >= 16 ? 1 : 0; }
 
 constexpr int kMaxContrib = 64;     // split contributors (CTA pairs) of one tile tracked in shared memory
 constexpr int kBarBytes = 80 * 8;   // mbarriers and flags, see the kernel's shared-memory map
 __host__ __device__ constexpr int gemm_smem_bytes(int wt) {
-    return 1024 /*align slack*/ + a_stages(wt) * kABytes + b_ring_bytes(wt) + raw_stages(wt) * raw_cpr(wt) * raw_chunk_bytes(wt) +
+    return 1024 /*align slack*/ + a_ring_bytes(wt) + b_ring_bytes(wt) + raw_stages(wt) * raw_cpr(wt) * raw_chunk_bytes(wt) +
            kBarBytes /*barriers, flags*/ + 4 * kMaxTok /*token positions*/ + 8 * kMaxContrib /*contributor partial offsets*/;
 }
 
@@ -161,7 +165,7 @@ struct Sched {
             u0 = (int)((long long)pair * U / G);
             u1 = (int)((long long)(pair + 1) * U / G);
         }
-        bh = ((gsz + 31) & ~31) >> 1;  // 16..128
+        bh = ((gsz + 31) & ~31) >> 1;  // 16..96
         if (bh < 16) bh = 16;
         spb = x_slices(bh);
         bslot = bh * 128 * spb;
@@ -190,9 +194,11 @@ __device__ __forceinline__ Seg make_seg(const Sched &s, int u, int u1) {
 }
 
 // ───────────── dequantization of one 64-wide k-slice of one weight row ─────────────
-// A stage: row r at r*128 B; logical 16-byte chunk c (k = 8c..8c+7) stored at c ^ (r & 7).
-__device__ __forceinline__ void st_a(uint8_t *A, int r, int c, uint4 v) {
-    *reinterpret_cast<uint4 *>(A + r * 128 + ((c ^ (r & 7)) << 4)) = v;
+// The slice is produced in 32 registers of f16 pairs in k order (register j holds k = 2j
+// in its low half and 2j + 1 in its high half), the layout of one TMEM lane of a 32-column
+// A operand; put() fills the 8 k-values of 16-byte chunk c.
+__device__ __forceinline__ void put(uint32_t (&o)[32], int c, uint4 v) {
+    o[4 * c] = v.x; o[4 * c + 1] = v.y; o[4 * c + 2] = v.z; o[4 * c + 3] = v.w;
 }
 __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
 __device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
@@ -246,7 +252,7 @@ __device__ __forceinline__ void q4k_pair(uint32_t nib, const __half2 &sc, const 
 }
 // Slice s (k = 64s .. 64s+63) of row r: low nibbles of qs bytes 32s.. are sub-block 2s,
 // high nibbles sub-block 2s+1; lo = local meta index of sub-block 2s.
-__device__ __forceinline__ void q4k_slice(const uint8_t *R, int r, int s, int lo, const Q4KMeta &m, uint8_t *A) {
+__device__ __forceinline__ void q4k_slice(const uint8_t *R, int r, int s, int lo, const Q4KMeta &m, uint32_t (&o)[32]) {
     const uint8_t *qrow = R + 2048 + 128 * r;
     const uint4 qa = *reinterpret_cast<const uint4 *>(qrow + (((2 * s) ^ (r & 7)) << 4));
     const uint4 qb = *reinterpret_cast<const uint4 *>(qrow + (((2 * s + 1) ^ (r & 7)) << 4));
@@ -260,8 +266,8 @@ __device__ __forceinline__ void q4k_slice(const uint8_t *R, int r, int s, int lo
         q4k_pair(w1 & 0x0F0F0F0Fu, m.sc[jl], m.nsc[jl], m.d2, m.nmo[jl], lo4.z, lo4.w);
         q4k_pair((w0 >> 4) & 0x0F0F0F0Fu, m.sc[jh], m.nsc[jh], m.d2, m.nmo[jh], hi4.x, hi4.y);
         q4k_pair((w1 >> 4) & 0x0F0F0F0Fu, m.sc[jh], m.nsc[jh], m.d2, m.nmo[jh], hi4.z, hi4.w);
-        st_a(A, r, c, lo4);
-        st_a(A, r, 4 + c, hi4);
+        put(o, c, lo4);
+        put(o, 4 + c, hi4);
     }
 }
 
@@ -314,7 +320,7 @@ __device__ __forceinline__ void q6k_pair(uint32_t q6, const __half2 &ds, uint32_
     o01 = h2u(__hmul2(__hsub2(u2h(p01), k1056), ds));
     o23 = h2u(__hmul2(__hsub2(u2h(p23), k1056), ds));
 }
-__device__ __forceinline__ void q6k_slice(const Q6KHalf &q, int r, int s, int lo, const Q6KMeta &m, uint8_t *A) {
+__device__ __forceinline__ void q6k_slice(const Q6KHalf &q, int s, int lo, const Q6KMeta &m, uint32_t (&out)[32]) {
     const int s2 = s & 1;
 #pragma unroll
     for (int c = 0; c < 8; c++) {
@@ -331,12 +337,12 @@ __device__ __forceinline__ void q6k_slice(const Q6KHalf &q, int r, int s, int lo
             q6k_pair(q6, m.ds[lo + (c >> 1)], a, b);
             if (hw == 0) { o.x = a; o.y = b; } else { o.z = a; o.w = b; }
         }
-        st_a(A, r, c, o);
+        put(out, c, o);
     }
 }
 
 // Q8_0 chunk layout: [d f16 x 8: 16 B/row][qs: 256 B/row at 2048, chunk c at (c & 8) | ((c & 7) ^ (row & 7))].
-__device__ __forceinline__ void q80_slice(const uint8_t *R, int r, int s, uint8_t *A) {
+__device__ __forceinline__ void q80_slice(const uint8_t *R, int r, int s, uint32_t (&out)[32]) {
     const uint4 dv = *reinterpret_cast<const uint4 *>(R + 16 * r);
     const uint8_t *qrow = R + 2048 + 256 * r;
     const __half2 k1152 = __halves2half2(__int2half_rn(1152), __int2half_rn(1152));
@@ -363,7 +369,7 @@ __device__ __forceinline__ void q80_slice(const uint8_t *R, int r, int s, uint8_
                 op[2 * i] = h2u(__hmul2(__hsub2(u2h(p01), k1152), d2));
                 op[2 * i + 1] = h2u(__hmul2(__hsub2(u2h(p23), k1152), d2));
             }
-            st_a(A, r, 2 * cc + half_, o);
+            put(out, 2 * cc + half_, o);
         }
     }
 }
@@ -492,29 +498,30 @@ __device__ __forceinline__ void epi_chunk(const EpiArgs &e, const EpiRow &r, con
 // Barriers the MMA waits on (full_a, full_b, acc_empty) live in the even CTA; the odd
 // CTA's loads and arrivals reach them through cluster addresses.
 //
-// Shared memory (per CTA): [A ring: a_stages x 32 KB][B ring][raw ring][barriers]
-// [token positions][contributor offsets].  Slice i (64 k) of the CTA's unit range uses
-// half i % 2 of A stage (i / 2) % a_stages and part i % spb of B slot (i / spb) % nbs.
+// Shared memory (per CTA): [A ring (F16 weights only): a_stages x 32 KB][B ring][raw ring]
+// [barriers][token positions][contributor offsets].  Slice i (64 k) of the CTA's unit
+// range uses half i % 2 of A stage (i / 2) % a_stages (TMEM columns kTmemA + 64 stage
+// + 32 half for quantized weights) and part i % spb of B slot (i / spb) % nbs.
 //
-// Warps (warp_role): w1 MMA issuer (even CTA) + TMEM owner, w5 activation producer, w9
-// relay, w11 weight-chunk producer (F16 weights: A-tile TMA producer), w0 w2-w4 w6-w8
-// w10 dequantizers (two sets of four; thread = weight row), w12-w19 epilogue (thread =
-// TMEM lane; w12-15 and w16-19 take alternate 16-column chunks).
+// Warps (warp_role): w0 activation producer, w1 MMA issuer (even CTA) + TMEM owner, w2
+// weight-chunk producer (F16 weights: A-tile TMA producer), w3 relay, w4-w11 dequantizers
+// (two sets of four; thread = weight row = TMEM lane), w12-w19 epilogue (thread = TMEM
+// lane; w12-15 and w16-19 take alternate 16-column chunks).
 template <int WT, int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     dq_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ XMaps xm, GemmParams p) {
     constexpr int RAWB = raw_chunk_bytes(WT);
-    constexpr int NA = a_stages(WT), NRAW = raw_stages(WT), BRING = b_ring_bytes(WT);
+    constexpr int NA = a_stages(WT), NRAW = raw_stages(WT), BRING = b_ring_bytes(WT), AR = a_ring_bytes(WT);
     constexpr int CPR = raw_cpr(WT), RSB = CPR * RAWB;  // chunks and bytes per raw stage
-    constexpr int kFixupPeers = (NA * kABytes + BRING) / 32768;  // partial chunks the drained rings hold
+    constexpr int kFixupPeers = (AR + BRING) / 32768;  // partial chunks the drained rings hold
     // The relay frees the B slots of stage j - NA's slices while it handles stage j, after
     // waiting for the B loads of stages up to j - 1: with one slice per load (the widest
     // group, 16 KB loads) the producer needs 2 NA + 1 slots not to wait on itself.
     static_assert(BRING / (kMaxTok / 2 * 128) >= 2 * NA + 1, "B ring too shallow for the A ring");
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t *aring = smem;
-    uint8_t *bring = smem + NA * kABytes;
+    uint8_t *aring = smem;  // F16 weights only
+    uint8_t *bring = smem + AR;
     uint8_t *raw = bring + BRING;
     uint64_t *bars = reinterpret_cast<uint64_t *>(raw + NRAW * RSB);
     uint64_t *full_a = bars, *empty_a = bars + 6, *full_b = bars + 12, *empty_b = bars + 36, *raw_full = bars + 60,
@@ -683,7 +690,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 const int acc = si & 1;
                 if (!(ok = mbar_wait(&acc_empty[acc], ((si >> 1) & 1) ^ 1, abort_flag, p.err, kErrTimeout + 3))) break;
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + acc * 256;
+                const uint32_t d_tmem = tmem_base + acc * kMaxTok;
                 const uint32_t idesc = idesc_f16(256, (uint32_t)g.nmma);
                 uint32_t accum = 0;
                 for (int kbi = g.k0; kbi < g.k1 && ok; kbi++) {
@@ -700,7 +707,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #endif
                         GEMM_EVENT(p, 4, ia);
                         tc_fence_after();
-                        const uint32_t a_addr = smem_u32(aring + st * kABytes);
+                        const uint32_t a_addr = smem_u32(aring + st * kABytes);             // F16
+                        const uint32_t a_tmem = tmem_base + kTmemA + st * kTmemAStage;      // dequantized
 #pragma unroll
                         for (int h = 0; h < 2; h++) {
                             const int it = 2 * ia + h;
@@ -708,8 +716,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                 smem_u32(bring + ((it / S.spb) % NBS) * S.bslot + (it % S.spb) * (S.bh * 128));
 #pragma unroll
                             for (int kk = 0; kk < 4; kk++) {
-                                mma2_f16_ss(d_tmem, sw128_desc(a_addr + h * kSliceBytes + kk * 32),
-                                            sw128_desc(b_addr + kk * 32), idesc, accum);
+                                if constexpr (WT == W_F16)
+                                    mma2_f16_ss(d_tmem, sw128_desc(a_addr + h * kSliceBytes + kk * 32),
+                                                sw128_desc(b_addr + kk * 32), idesc, accum);
+                                else
+                                    mma2_f16_ts(d_tmem, a_tmem + h * 32 + kk * 8, sw128_desc(b_addr + kk * 32), idesc, accum);
                                 accum = 1;
                             }
                         }
@@ -792,25 +803,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const int r = (di & 3) * 32 + lane;
             int rit = 0;
             bool ok = true;
-#ifdef DFB_GEMM_TRACE
-            long long t_fence = 0, t_sync = 0, t_arrive = 0;
+            // This warp's TMEM lane quarter holds its 32 weight rows of every A stage.
+            const uint32_t a_lane = tmem_base + ((uint32_t)(32 * (warp & 3)) << 16) + kTmemA;
+            // The stage's tcgen05.st have completed; order them before the arrival the MMA
+            // issuer waits on (no shared memory, so no proxy fence).
             auto publish = [&](int st) {
-                const long long c0 = clock64();
-                fence_proxy_async_smem();
-                const long long c1 = clock64();
-                __syncwarp();
-                const long long c2 = clock64();
-                if (lane == 0) mbar_arrive_cluster(full_a0 + 8 * st);
-                const long long c3 = clock64();
-                t_fence += c1 - c0; t_sync += c2 - c1; t_arrive += c3 - c2;
-            };
-#else
-            auto publish = [&](int st) {
-                fence_proxy_async_smem();
+                tmem_st_wait();
+                tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive_cluster(full_a0 + 8 * st);
             };
-#endif
             // Lane 0 waits and the warp takes its verdict; then every
             // lane observes the completed phase itself (one try_wait, which succeeds: the
             // phase cannot advance further without this warp), for acquire ordering.
@@ -838,14 +840,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     const uint8_t *R = raw + rs * RSB + (rit % CPR) * RAWB;
                     // this set's A stage of the k-block: slices 2 set, 2 set + 1
                     const int ia = 2 * rit + set;
-                    uint8_t *A = aring + (ia % NA) * kABytes;
+                    const uint32_t ta = a_lane + (ia % NA) * kTmemAStage;
+                    uint32_t o[32];
                     if constexpr (WT == W_Q4K) {
                         Q4KMeta meta;
                         q4k_load_meta(R, r, set, meta);
                         if (!(ok = wait_a(ia))) break;
+                        tc_fence_after();  // after the MMA that read this stage
                         if (r == 0 && ia < 32) GEMM_EVENT(p, 7, ia);
                         #pragma unroll
-                        for (int h = 0; h < 2; h++) q4k_slice(R, r, 2 * set + h, 2 * h, meta, A + h * kSliceBytes);
+                        for (int h = 0; h < 2; h++) {
+                            q4k_slice(R, r, 2 * set + h, 2 * h, meta, o);
+                            tmem_st32(ta + 32 * h, o);
+                        }
                         publish(ia % NA);
                         if (r == 0) GEMM_EVENT(p, 3, ia);
                     } else if constexpr (WT == W_Q6K) {
@@ -854,13 +861,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         Q6KHalf qv;
                         q6k_load_half(R, r, set, qv);  // slices 2 set, 2 set + 1 share one half of ql / qh
                         if (!(ok = wait_a(ia))) break;
+                        tc_fence_after();
                         #pragma unroll
-                        for (int h = 0; h < 2; h++) q6k_slice(qv, r, 2 * set + h, 4 * h, meta, A + h * kSliceBytes);
+                        for (int h = 0; h < 2; h++) {
+                            q6k_slice(qv, 2 * set + h, 4 * h, meta, o);
+                            tmem_st32(ta + 32 * h, o);
+                        }
                         publish(ia % NA);
                     } else {
                         if (!(ok = wait_a(ia))) break;
+                        tc_fence_after();
                         #pragma unroll
-                        for (int h = 0; h < 2; h++) q80_slice(R, r, 2 * set + h, A + h * kSliceBytes);
+                        for (int h = 0; h < 2; h++) {
+                            q80_slice(R, r, 2 * set + h, o);
+                            tmem_st32(ta + 32 * h, o);
+                        }
                         publish(ia % NA);
                     }
                     __syncwarp();
@@ -869,14 +884,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 }
                 u += g.k1 - g.k0;
             }
-#ifdef DFB_GEMM_TRACE
-            if (r == 0 && set == 0 && p.trace && blockIdx.x < 4) {
-                p.trace[256 * 16 + ((size_t)blockIdx.x * 8 + 7) * 64 + 60] = (unsigned long long)t_fence;
-                p.trace[256 * 16 + ((size_t)blockIdx.x * 8 + 7) * 64 + 61] = (unsigned long long)t_sync;
-                p.trace[256 * 16 + ((size_t)blockIdx.x * 8 + 7) * 64 + 62] = (unsigned long long)t_arrive;
-                p.trace[256 * 16 + ((size_t)blockIdx.x * 8 + 7) * 64 + 63] = (unsigned long long)rit;
-            }
-#endif
         }
     } else {
         // ── epilogue: thread = TMEM lane = output feature of this CTA's tile ──
@@ -904,7 +911,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             if (!ok) break;
             if (et == 0 && si < 4) GEMM_STAMP(p, 4 + 2 * si);
             tc_fence_after();
-            const uint32_t taddr = tmem_base + ((uint32_t)(32 * q) << 16) + acc * 256;
+            const uint32_t taddr = tmem_base + ((uint32_t)(32 * q) << 16) + acc * kMaxTok;
             const bool whole = g.k0 == 0 && g.k1 == S.kb;
             const EpiRow er = epi_row<EPI>(p.epi, tile, row);
             if constexpr (EPI == EPI_QKV || EPI == EPI_LOGITS) {
@@ -956,7 +963,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             // the accumulator is in the workspace: let the MMA reuse the TMEM buffer
             if (mode >= 2) release_acc(acc);
             if (mode != 3) {
-                const float *sbuf = reinterpret_cast<const float *>(aring);
+                const float *sbuf = reinterpret_cast<const float *>(smem);
                 bool staged_ok = true;
                 for (int cb = 0; cb < g.nmma && staged_ok; cb += 64) {
                     if (mode == 1) {
@@ -968,7 +975,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                             mbar_arrive_expect_tx(fix_bar, (uint32_t)(nc - 1) * cols * 512);
                             for (int c = 0, k = 0; c < nc; c++) {
                                 if (c == me) continue;
-                                bulk_g2s(aring + (size_t)k * 32768, p.ws + s_contrib[c] + (size_t)(cb >> 6) * 8192,
+                                bulk_g2s(smem + (size_t)k * 32768, p.ws + s_contrib[c] + (size_t)(cb >> 6) * 8192,
                                          (uint32_t)cols * 512, fix_bar);
                                 k++;
                             }
