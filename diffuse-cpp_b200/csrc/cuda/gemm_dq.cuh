@@ -703,10 +703,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         if (!(ok = mbar_wait(&full_a[st], (ia / NA) & 1, abort_flag, p.err, kErrTimeout + 5))) break;
 #ifdef DFB_GEMM_TRACE
                         const long long c1 = clock64();
-                        const long long c2 = c1;
 #endif
-                        GEMM_EVENT(p, 4, ia);
                         tc_fence_after();
+#ifdef DFB_GEMM_TRACE
+                        const long long c2 = clock64();
+#endif
                         const uint32_t a_addr = smem_u32(aring + st * kABytes);             // F16
                         const uint32_t a_tmem = tmem_base + kTmemA + st * kTmemAStage;      // dequantized
 #pragma unroll
@@ -736,6 +737,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         tm_last = c4;
 #endif
                         GEMM_EVENT(p, 5, ia);
+                        if (ia < 64) GEMM_EVENT(p, 4, ia);
                         ia++;
                     }
                 }

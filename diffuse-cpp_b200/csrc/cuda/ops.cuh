@@ -99,6 +99,8 @@ __global__ void embed_kernel(const T *__restrict__ emb, int d, const int32_t *__
     }
 }
 
+__device__ __forceinline__ uint32_t h2u_(__half2 v) { return *reinterpret_cast<uint32_t *>(&v); }
+
 __device__ __forceinline__ float block_sum(float v, float *red) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
 #pragma unroll
@@ -118,6 +120,7 @@ __device__ __forceinline__ float block_sum(float v, float *red) {
 }
 
 // h[a] = f16(x[a] * rsqrt(mean(x[a]^2) + eps) * w)  (ggml_rms_norm + ggml_mul, graph.cpp:51-58).
+// One block per row; 8 elements per thread per step (two float4 loads, one 16-byte store).
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const float *__restrict__ x, const float *__restrict__ w, int d,
                                                       float eps, const int *__restrict__ cnt, __half *__restrict__ h) {
     __shared__ float red[33];
@@ -126,19 +129,35 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const float *__restrict__ 
     const int a = blockIdx.x;
     if (a >= cnt[CNT_M]) return;
     const float *xr = x + (size_t)a * d;
+    __half *hr = h + (size_t)a * d;
     float ss = 0.f;
-    if ((d & 3) == 0) {
-        for (int i = threadIdx.x * 4; i < d; i += blockDim.x * 4) {
-            const float4 v = *reinterpret_cast<const float4 *>(xr + i);
-            ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    if ((d & 7) == 0) {
+        for (int i = threadIdx.x * 8; i < d; i += blockDim.x * 8) {
+            const float4 v0 = *reinterpret_cast<const float4 *>(xr + i);
+            const float4 v1 = *reinterpret_cast<const float4 *>(xr + i + 4);
+            ss += v0.x * v0.x + v0.y * v0.y + v0.z * v0.z + v0.w * v0.w;
+            ss += v1.x * v1.x + v1.y * v1.y + v1.z * v1.z + v1.w * v1.w;
+        }
+        ss = block_sum(ss, red);
+        const float scale = 1.0f / sqrtf(ss / (float)d + eps);
+        for (int i = threadIdx.x * 8; i < d; i += blockDim.x * 8) {
+            const float4 v0 = *reinterpret_cast<const float4 *>(xr + i);
+            const float4 v1 = *reinterpret_cast<const float4 *>(xr + i + 4);
+            const float4 w0 = __ldg(reinterpret_cast<const float4 *>(w + i));
+            const float4 w1 = __ldg(reinterpret_cast<const float4 *>(w + i + 4));
+            uint4 o;
+            o.x = h2u_(__floats2half2_rn((v0.x * scale) * w0.x, (v0.y * scale) * w0.y));
+            o.y = h2u_(__floats2half2_rn((v0.z * scale) * w0.z, (v0.w * scale) * w0.w));
+            o.z = h2u_(__floats2half2_rn((v1.x * scale) * w1.x, (v1.y * scale) * w1.y));
+            o.w = h2u_(__floats2half2_rn((v1.z * scale) * w1.z, (v1.w * scale) * w1.w));
+            *reinterpret_cast<uint4 *>(hr + i) = o;
         }
     } else {
         for (int i = threadIdx.x; i < d; i += blockDim.x) ss += xr[i] * xr[i];
+        ss = block_sum(ss, red);
+        const float scale = 1.0f / sqrtf(ss / (float)d + eps);
+        for (int i = threadIdx.x; i < d; i += blockDim.x) hr[i] = __float2half_rn((xr[i] * scale) * w[i]);
     }
-    ss = block_sum(ss, red);
-    const float scale = 1.0f / sqrtf(ss / (float)d + eps);
-    __half *hr = h + (size_t)a * d;
-    for (int i = threadIdx.x; i < d; i += blockDim.x) hr[i] = __float2half_rn((xr[i] * scale) * w[i]);
 }
 
 // Per-candidate statistics of one logits row (diffuse-sampler.cpp:34-57 and :239-255):
@@ -169,11 +188,35 @@ __global__ void __launch_bounds__(512) row_stats_kernel(const float *__restrict_
     const int i = masked_pos[b];
     const int row = shift ? (i > 0 ? i - 1 : 0) : i;
     const float *z = logits + (size_t)row * n_vocab;
+    // Each pass reads the row as float4 (n_vocab % 4 == 0) with four loads in flight per
+    // thread; a thread visits its elements in increasing index order, so the strict '>'
+    // still keeps the lowest index of equal maxima.
+    const bool vec = (n_vocab & 3) == 0;
+    const int n4 = n_vocab >> 2;
+    const float4 *z4 = reinterpret_cast<const float4 *>(z);
     Top2 t{-INFINITY, 0x7fffffff, -1e30f};
-    for (int v = threadIdx.x; v < n_vocab; v += blockDim.x) {
-        const float x = z[v];
+    auto see = [&](float x, int v) {
         if (x > t.best) { t.second = fmaxf(t.second, t.best); t.best = x; t.idx = v; }
         else t.second = fmaxf(t.second, x);
+    };
+    if (vec) {
+        int q = threadIdx.x;
+        for (; q + 3 * (int)blockDim.x < n4; q += 4 * blockDim.x) {
+            float4 f[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) f[u] = z4[q + u * blockDim.x];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int v = 4 * (q + u * blockDim.x);
+                see(f[u].x, v); see(f[u].y, v + 1); see(f[u].z, v + 2); see(f[u].w, v + 3);
+            }
+        }
+        for (; q < n4; q += blockDim.x) {
+            const float4 f = z4[q];
+            see(f.x, 4 * q); see(f.y, 4 * q + 1); see(f.z, 4 * q + 2); see(f.w, 4 * q + 3);
+        }
+    } else {
+        for (int v = threadIdx.x; v < n_vocab; v += blockDim.x) see(z[v], v);
     }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 #pragma unroll
@@ -202,14 +245,45 @@ __global__ void __launch_bounds__(512) row_stats_kernel(const float *__restrict_
     t = tred[0];
     const float mx = t.best;
     float se = 0.f;
-    for (int v = threadIdx.x; v < n_vocab; v += blockDim.x) se += expf(z[v] - mx);
+    if (vec) {
+        int q = threadIdx.x;
+        for (; q + 3 * (int)blockDim.x < n4; q += 4 * blockDim.x) {
+            float4 f[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) f[u] = z4[q + u * blockDim.x];
+#pragma unroll
+            for (int u = 0; u < 4; u++) se += expf(f[u].x - mx) + expf(f[u].y - mx) + expf(f[u].z - mx) + expf(f[u].w - mx);
+        }
+        for (; q < n4; q += blockDim.x) {
+            const float4 f = z4[q];
+            se += expf(f.x - mx) + expf(f.y - mx) + expf(f.z - mx) + expf(f.w - mx);
+        }
+    } else {
+        for (int v = threadIdx.x; v < n_vocab; v += blockDim.x) se += expf(z[v] - mx);
+    }
     se = block_sum(se, red);
     const float log_sum = logf(se);
     float ent = 0.f;
-    for (int v = threadIdx.x; v < n_vocab; v += blockDim.x) {
-        const float lp = (z[v] - mx) - log_sum;
+    auto term = [&](float x) {
+        const float lp = (x - mx) - log_sum;
         const float p = expf(lp);
         if (p > 1e-10f) ent -= p * lp;
+    };
+    if (vec) {
+        int q = threadIdx.x;
+        for (; q + 3 * (int)blockDim.x < n4; q += 4 * blockDim.x) {
+            float4 f[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) f[u] = z4[q + u * blockDim.x];
+#pragma unroll
+            for (int u = 0; u < 4; u++) { term(f[u].x); term(f[u].y); term(f[u].z); term(f[u].w); }
+        }
+        for (; q < n4; q += blockDim.x) {
+            const float4 f = z4[q];
+            term(f.x); term(f.y); term(f.z); term(f.w);
+        }
+    } else {
+        for (int v = threadIdx.x; v < n_vocab; v += blockDim.x) term(z[v]);
     }
     ent = block_sum(ent, red);
     if (threadIdx.x == 0) {
