@@ -97,26 +97,26 @@ constexpr int kThreads = 640;            // 20 warps, roles below
 constexpr int kEpiThreads = 256;         // two epilogue warps per TMEM lane quarter
 constexpr int kDeqWarps = 8;             // two sets of four: even / odd k-slices
 constexpr int kSliceBytes = 128 * 128;   // one 64-wide k-slice of this CTA's 128 weight rows (f16)
-constexpr int kABytes = 2 * kSliceBytes;  // one A stage: two consecutive k-slices
+constexpr int kABytes = kSliceBytes;      // one A stage: one k-slice
 constexpr int kMaxTok = 192;             // tokens per MMA group (N) of the pair
 constexpr int kWsTile = kMaxTok * 128;   // floats per partial tile (one CTA's 128 rows)
 constexpr int kErrTimeout = 0x100;
 constexpr int kMaxAStages = 6, kMaxBSlots = 24, kMaxRawStages = 4;
 // TMEM (512 columns per CTA): accumulators [0, 192) and [192, 384); dequantized A stages
-// (quantized weights) at [384 + 64 st, +64): lane = weight row, 32 columns per k-slice.
+// (quantized weights) at [384 + 32 st, +32): lane = weight row, one k-slice each.
 constexpr int kTmemA = 2 * kMaxTok;
-constexpr int kTmemAStage = 64;
+constexpr int kTmemAStage = 32;
 
 // Rings per weight type, sized so that shared memory (227 KB) holds them:
-//  A        two k-slices per stage, two stages: dequantized weights go to TMEM (written
-//           by tcgen05.st, read by the MMA from TMEM: no shared-memory round trip and no
-//           proxy fence, which cost ~1.2k cycles per warp and stage); F16 weights are
-//           TMA-loaded into a shared-memory ring instead;
+//  A        one k-slice per stage, four stages (one k-block): dequantized weights go to
+//           TMEM (written by tcgen05.st, read by the MMA from TMEM: no shared-memory round
+//           trip and no proxy fence, which cost ~1.2k cycles per warp and stage); F16
+//           weights are TMA-loaded into a shared-memory ring instead;
 //  B ring   this CTA's activation rows of 1-4 k-slices per slot (2-12 KB), so small
 //           token counts keep many slices in flight and hide the L2 latency;
 //  raw ring re-tiled weight chunks (one k-block of 256 for 128 rows), grouped.
-__host__ __device__ constexpr int a_stages(int wt) { return 2; }
-__host__ __device__ constexpr int a_ring_bytes(int wt) { return wt == W_F16 ? 2 * kABytes : 0; }
+__host__ __device__ constexpr int a_stages(int wt) { return 4; }
+__host__ __device__ constexpr int a_ring_bytes(int wt) { return wt == W_F16 ? 4 * kABytes : 0; }
 __host__ __device__ constexpr int b_ring_bytes(int wt) { return 112 * 1024; }
 // A raw stage holds raw_cpr consecutive chunks of the CTA's unit range: the weight
 // stream reached ~3.8 TB/s with 18 KB stages and ~6-7 TB/s with 36-72 KB stages
@@ -133,7 +133,7 @@ enum WarpRole : int { R_DEQ = 0, R_MMA = 1, R_BPROD = 2, R_WPROD = 3, R_EPI = 4,
 __host__ __device__ constexpr int warp_role(int w) {
     return w == 0 ? R_BPROD : w == 1 ? R_MMA : w == 2 ? R_WPROD : w == 3 ? R_RELAY : w < 12 ? R_DEQ : R_EPI;
 }
-// dequantizer index 0..7: set = index / 4 takes k-slices 2 set, 2 set + 1 of each k-block;
+// dequantizer index 0..7: set = index / 4 takes k-slices set and set + 2 of each k-block;
 // its weight rows are the warp's TMEM lane quarter
 __host__ __device__ constexpr int deq_index(int w) { return w - 4; }
 // epilogue thread group: warps 12-15 and 16-19 each cover the four lane quarters
@@ -205,8 +205,8 @@ __device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__
 
 // Q4_K chunk layout (per 128 rows): [d,dmin f16 x2: 4 B/row][scales: 12 B/row at 512]
 // [qs: 128 B/row at 2048, 16-byte chunk c stored at c ^ (row & 7)].
-// Scales of the four sub-blocks one dequant set uses: set p dequantizes k-slices 2p and
-// 2p + 1, i.e. sub-blocks 4p .. 4p + 3 (local 0 .. 3).
+// Scales of the four sub-blocks one dequant set uses: set p dequantizes k-slices p and
+// p + 2, i.e. sub-blocks 2p, 2p + 1 (local 0, 1) and 2p + 4, 2p + 5 (local 2, 3).
 struct Q4KMeta {
     __half2 d2;
     __half2 sc[4], nsc[4], nmo[4];  // sc, -1024*sc, -(dmin*m) per sub-block, as f16 pairs
@@ -223,9 +223,9 @@ __device__ __forceinline__ void q4k_load_meta(const uint8_t *R, int r, int set, 
 #pragma unroll
     for (int l = 0; l < 4; l++) {
         // 6-bit scale / min of sub-block j (get_scale_min_k4 packing)
-        const int j = 4 * set + l;
+        const int j = 2 * set + (l & 1) + 4 * (l >> 1);
         int sc, mn;
-        if (set == 0) {  // j < 4
+        if (l < 2) {  // j < 4
             sc = qb(j) & 63;
             mn = qb(j + 4) & 63;
         } else {
@@ -274,8 +274,8 @@ __device__ __forceinline__ void q4k_slice(const uint8_t *R, int r, int s, int lo
 // Q6_K chunk layout: [ql: 128 B/row, chunk c at c ^ (row & 7)]
 // [qh: 64 B/row at 16384, chunk c at c ^ ((row >> 1) & 3)][scales i8: 16 B/row at 24576]
 // [d f16: 2 B/row at 26624].
-// d * scale of the eight 16-element groups one dequant set uses: set p takes slices 2p
-// and 2p + 1, i.e. groups 8p .. 8p + 7 (scale words 2p and 2p + 1).
+// d * scale of the eight 16-element groups one dequant set uses: set p takes slices p
+// and p + 2, i.e. groups 4p .. 4p + 3 and 4p + 8 .. 4p + 11 (scale words p and p + 2).
 struct Q6KMeta {
     __half2 ds[8];
 };
@@ -284,7 +284,7 @@ __device__ __forceinline__ void q6k_load_meta(const uint8_t *R, int r, int set, 
     const uint4 sv = *reinterpret_cast<const uint4 *>(R + 24576 + 16 * r);
 #pragma unroll
     for (int h = 0; h < 2; h++) {
-        const int wi = 2 * set + h;  // scale word holding groups 4*wi .. 4*wi+3
+        const int wi = set + 2 * h;  // scale word holding groups 4*wi .. 4*wi+3
         const uint32_t w = wi == 0 ? sv.x : wi == 1 ? sv.y : wi == 2 ? sv.z : sv.w;
 #pragma unroll
         for (int i = 0; i < 4; i++) {
@@ -498,10 +498,10 @@ __device__ __forceinline__ void epi_chunk(const EpiArgs &e, const EpiRow &r, con
 // Barriers the MMA waits on (full_a, full_b, acc_empty) live in the even CTA; the odd
 // CTA's loads and arrivals reach them through cluster addresses.
 //
-// Shared memory (per CTA): [A ring (F16 weights only): a_stages x 32 KB][B ring][raw ring]
+// Shared memory (per CTA): [A ring (F16 weights only): a_stages x 16 KB][B ring][raw ring]
 // [barriers][token positions][contributor offsets].  Slice i (64 k) of the CTA's unit
-// range uses half i % 2 of A stage (i / 2) % a_stages (TMEM columns kTmemA + 64 stage
-// + 32 half for quantized weights) and part i % spb of B slot (i / spb) % nbs.
+// range uses A stage i % a_stages (TMEM columns kTmemA + 32 stage for quantized weights)
+// and part i % spb of B slot (i / spb) % nbs.
 //
 // Warps (warp_role): w0 activation producer, w1 MMA issuer (even CTA) + TMEM owner, w2
 // weight-chunk producer (F16 weights: A-tile TMA producer), w3 relay, w4-w11 dequantizers
@@ -514,10 +514,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     constexpr int NA = a_stages(WT), NRAW = raw_stages(WT), BRING = b_ring_bytes(WT), AR = a_ring_bytes(WT);
     constexpr int CPR = raw_cpr(WT), RSB = CPR * RAWB;  // chunks and bytes per raw stage
     constexpr int kFixupPeers = (AR + BRING) / 32768;  // partial chunks the drained rings hold
-    // The relay frees the B slots of stage j - NA's slices while it handles stage j, after
-    // waiting for the B loads of stages up to j - 1: with one slice per load (the widest
-    // group, 16 KB loads) the producer needs 2 NA + 1 slots not to wait on itself.
-    static_assert(BRING / (kMaxTok / 2 * 128) >= 2 * NA + 1, "B ring too shallow for the A ring");
+    // The relay frees the B slot of slice j - NA while it handles slice j, after waiting
+    // for the B loads up to slice j - 1: with one slice per load (the widest group, 12 KB
+    // loads) the producer needs 2 + (NA - 1) slots not to wait on itself.
+    static_assert(BRING / (kMaxTok / 2 * 128) >= 2 + (NA - 1), "B ring too shallow for the A ring");
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *aring = smem;  // F16 weights only
@@ -601,19 +601,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         //    also streams the weights and handles only a few operations per microsecond. ──
         if (lane == 0) {
             const CUtensorMap *xmap = &xm.m[S.bh / 16 - 1];
-            int ob = 0;  // B loads issued
+            int ob = 0, sl = 0;  // B loads issued, slot of the next one
+            uint32_t ph = 0;     // ring pass parity of the next load
             bool ok = true;
             for (int u = S.u0; u < S.u1 && ok;) {
                 const Seg g = make_seg(S, u, S.u1);
                 const int row0 = g.m0 + (int)rank * g.half;
                 for (int kbi = g.k0; kbi < g.k1 && ok; kbi++) {
                     for (int s = 0; s < 4; s += S.spb) {
-                        const int sl = ob % NBS;
-                        if (!(ok = mbar_wait(&empty_b[sl], ((ob / NBS) & 1) ^ 1, abort_flag, p.err, kErrTimeout + 2))) break;
+                        if (!(ok = mbar_wait(&empty_b[sl], ph ^ 1, abort_flag, p.err, kErrTimeout + 2))) break;
                         mbar_arrive_expect_tx(&full_b[sl], S.bslot);
                         tma_load_3d(bring + sl * S.bslot, xmap, 0, row0, kbi * 4 + s, &full_b[sl]);
                         GEMM_EVENT(p, 0, ob);
                         ob++;
+                        if (++sl == NBS) { sl = 0; ph ^= 1; }
                     }
                 }
                 u += g.k1 - g.k0;
@@ -656,13 +657,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 for (int u = S.u0; u < S.u1 && ok;) {
                     const Seg g = make_seg(S, u, S.u1);
                     for (int kbi = g.k0; kbi < g.k1 && ok; kbi++) {
-                        for (int s = 0; s < 4; s += 2) {  // one stage = two k-slices
+                        for (int s = 0; s < 4; s++) {  // one stage = one k-slice
                             const int st = it % NA;
                             if (!(ok = mbar_wait(&empty_a[st], ((it / NA) & 1) ^ 1, abort_flag, p.err, kErrTimeout + 11))) break;
                             if (rank == 0) mbar_arrive_expect_tx(&full_a[st], 2 * kABytes);
-                            for (int h = 0; h < 2; h++)
-                                tma_load_2d_pair(aring + st * kABytes + h * kSliceBytes, &tm_w, kbi * 256 + (s + h) * 64,
-                                                 (2 * g.pt + (int)rank) * 128, full_a0 + 8 * st);
+                            tma_load_2d_pair(aring + st * kABytes, &tm_w, kbi * 256 + s * 64, (2 * g.pt + (int)rank) * 128,
+                                             full_a0 + 8 * st);
                             it++;
                         }
                     }
@@ -683,8 +683,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             int ia = 0, si = 0;  // A stages consumed, accumulator segments
             bool ok = true, issued = false;
 #ifdef DFB_GEMM_TRACE
-            long long tm_wa = 0, tm_wb = 0, tm_mma = 0, tm_cm = 0, tm_loop = 0, tm_last = 0;
+            long long tm_wa = 0, tm_wb = 0, tm_mma = 0, tm_cm = 0, tm_loop = 0, tm_last = 0, tm_each[4] = {0, 0, 0, 0};
 #endif
+            const uint64_t bdesc0 = sw128_desc(smem_u32(bring)), adesc0 = sw128_desc(smem_u32(aring));
+            const int spb = S.spb;
+            const uint32_t bstep_part = S.bh * 128, bstep_slot = S.bslot - (spb - 1) * S.bh * 128;
+            int bsl = 0, bpart = 0;
+            uint32_t boff = 0;
             for (int u = S.u0; u < S.u1 && ok;) {
                 const Seg g = make_seg(S, u, S.u1);
                 const int acc = si & 1;
@@ -694,7 +699,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 const uint32_t idesc = idesc_f16(256, (uint32_t)g.nmma);
                 uint32_t accum = 0;
                 for (int kbi = g.k0; kbi < g.k1 && ok; kbi++) {
-                    for (int s2 = 0; s2 < 2; s2++) {  // A stages of this k-block
+                    for (int s2 = 0; s2 < 4; s2++) {  // A stages (k-slices) of this k-block
                         const int st = ia % NA;
 #ifdef DFB_GEMM_TRACE
                         const long long c0 = clock64();
@@ -708,22 +713,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #ifdef DFB_GEMM_TRACE
                         const long long c2 = clock64();
 #endif
-                        const uint32_t a_addr = smem_u32(aring + st * kABytes);             // F16
-                        const uint32_t a_tmem = tmem_base + kTmemA + st * kTmemAStage;      // dequantized
-#pragma unroll
-                        for (int h = 0; h < 2; h++) {
-                            const int it = 2 * ia + h;
-                            const uint32_t b_addr =
-                                smem_u32(bring + ((it / S.spb) % NBS) * S.bslot + (it % S.spb) * (S.bh * 128));
-#pragma unroll
-                            for (int kk = 0; kk < 4; kk++) {
-                                if constexpr (WT == W_F16)
-                                    mma2_f16_ss(d_tmem, sw128_desc(a_addr + h * kSliceBytes + kk * 32),
-                                                sw128_desc(b_addr + kk * 32), idesc, accum);
-                                else
-                                    mma2_f16_ts(d_tmem, a_tmem + h * 32 + kk * 8, sw128_desc(b_addr + kk * 32), idesc, accum);
-                                accum = 1;
-                            }
+                        // this slice's B rows: descriptor of the ring base + running byte offset
+                        // (no divisions on the issuer's path: its scheduler is shared with
+                        // dequantizers, and each instruction costs several cycles there)
+                        const uint64_t bdesc = bdesc0 + (uint64_t)(boff >> 4);
+                        if constexpr (WT == W_F16)
+                            mma2_f16_ss_k64(d_tmem, adesc0 + (uint64_t)((st * kABytes) >> 4), bdesc, idesc, accum);
+                        else {
+                            const uint32_t a_tmem = tmem_base + kTmemA + st * kTmemAStage;
+#ifdef DFB_GEMM_TRACE
+                            long long tt[5];
+                            mma2_f16_ts_k64_timed(d_tmem, a_tmem, bdesc, idesc, accum, tt);
+                            for (int q5 = 0; q5 < 4; q5++) tm_each[q5] += tt[q5 + 1] - tt[q5];
+#else
+                            mma2_f16_ts_k64(d_tmem, a_tmem, bdesc, idesc, accum);
+#endif
+                        }
+                        accum = 1;
+                        // next slice's B position: part of the slot, then the next slot
+                        if (++bpart == spb) {
+                            bpart = 0;
+                            if (++bsl == NBS) { bsl = 0; boff = 0; }
+                            else boff += bstep_slot;
+                        } else {
+                            boff += bstep_part;
                         }
 #ifdef DFB_GEMM_TRACE
                         const long long c3 = clock64();
@@ -751,6 +764,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             if (p.trace && blockIdx.x < 4) {
                 unsigned long long *tp = p.trace + 256 * 16 + ((size_t)blockIdx.x * 8 + 5) * 64 + 56;
                 tp[0] = tm_wa; tp[1] = tm_wb; tp[2] = tm_mma; tp[3] = tm_cm; tp[4] = tm_loop; tp[5] = ia;
+                unsigned long long *te = p.trace + 256 * 16 + ((size_t)blockIdx.x * 8 + 4) * 64 + 56;
+                for (int q5 = 0; q5 < 4; q5++) te[q5] = tm_each[q5];
             }
 #endif
             if (issued) {
@@ -761,11 +776,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
     } else if (role == R_RELAY) {
-        // ── relay (one thread per CTA), A stage by A stage: once the MMA of stage j - NA
-        //    has completed (empty_a, the same wait the A writers do), the B slots of its
-        //    slices are free again (a slot after the last slice of its load); once this
-        //    CTA's B rows of stage j have landed (full_b), arrive on full_a of stage j in
-        //    the even CTA.  The MMA issuer so waits on one barrier per stage, and no relay
+        // ── relay (one thread per CTA), slice by slice: once the MMA of slice j - NA has
+        //    completed (empty_a, the same wait the A writers do), its B slot is free again
+        //    (after the last slice of the slot's load); once this CTA's B rows of slice j
+        //    have landed (full_b), arrive on full_a of slice j in the even CTA.  The MMA issuer so waits on one barrier per stage, and no relay
         //    can fall a full phase behind the barriers it polls. ──
         if (lane == 0) {
             int n_it = 0;
@@ -775,23 +789,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 u += g.k1 - g.k0;
             }
             bool ok = true;
-            const int spb = S.spb, n_st = n_it / 2;
-            for (int j = 0; j < n_st + NA && ok; j++) {  // A stage j = slices 2j, 2j + 1
+            const int spb = S.spb;
+            // running ring positions (no divisions): B load of slice j and of slice j - NA
+            int fo_sl = 0, fo_part = 0, eo_sl = 0, eo_part = 0;
+            uint32_t fo_ph = 0;
+            for (int j = 0; j < n_it + NA && ok; j++) {  // A stage = slice j
                 if (j >= NA) {
-                    // MMA of stage j - NA done (phase (j - NA) / NA of empty_a[j % NA]): free
-                    // the B slots whose last slice lies in it
+                    // MMA of slice j - NA done (phase (j - NA) / NA of empty_a[j % NA]); its B
+                    // slot is free once the last slice of the slot's load is done
                     if (!(ok = mbar_wait(&empty_a[j % NA], ((j / NA) & 1) ^ 1, abort_flag, p.err, kErrTimeout + 12))) break;
-                    for (int jd = 2 * (j - NA); jd < 2 * (j - NA) + 2; jd++)
-                        if (jd % spb == spb - 1) mbar_arrive(&empty_b[(jd / spb) % NBS]);
-                }
-                if (j < n_st) {
-                    for (int js = 2 * j; js < 2 * j + 2 && ok; js++) {
-                        const int o = js / spb;
-                        if (js % spb == 0)
-                            ok = mbar_wait(&full_b[o % NBS], (o / NBS) & 1, abort_flag, p.err, kErrTimeout + 4);
+                    if (++eo_part == spb) {
+                        eo_part = 0;
+                        mbar_arrive(&empty_b[eo_sl]);
+                        if (++eo_sl == NBS) eo_sl = 0;
                     }
-                    if (!ok) break;
+                }
+                if (j < n_it) {
+                    if (fo_part == 0)
+                        if (!(ok = mbar_wait(&full_b[fo_sl], fo_ph, abort_flag, p.err, kErrTimeout + 4))) break;
                     mbar_arrive_cluster(full_a0 + 8 * (j % NA));
+                    if (++fo_part == spb) {
+                        fo_part = 0;
+                        if (++fo_sl == NBS) { fo_sl = 0; fo_ph ^= 1; }
+                    }
                 }
             }
         }
@@ -840,45 +860,46 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         if (r == 0 && set == 0) GEMM_EVENT(p, 2, rst);
                     }
                     const uint8_t *R = raw + rs * RSB + (rit % CPR) * RAWB;
-                    // this set's A stage of the k-block: slices 2 set, 2 set + 1
-                    const int ia = 2 * rit + set;
-                    const uint32_t ta = a_lane + (ia % NA) * kTmemAStage;
+                    // this set's k-slices of the k-block: set and set + 2, one A stage each
                     uint32_t o[32];
                     if constexpr (WT == W_Q4K) {
                         Q4KMeta meta;
                         q4k_load_meta(R, r, set, meta);
-                        if (!(ok = wait_a(ia))) break;
-                        tc_fence_after();  // after the MMA that read this stage
-                        if (r == 0 && ia < 32) GEMM_EVENT(p, 7, ia);
                         #pragma unroll
                         for (int h = 0; h < 2; h++) {
-                            q4k_slice(R, r, 2 * set + h, 2 * h, meta, o);
-                            tmem_st32(ta + 32 * h, o);
+                            const int sl = set + 2 * h, ia = 4 * rit + sl;
+                            q4k_slice(R, r, sl, 2 * h, meta, o);
+                            if (!(ok = wait_a(ia))) break;
+                            tc_fence_after();  // after the MMA that read this stage
+                            if (r == 0 && ia < 32) GEMM_EVENT(p, 7, ia);
+                            tmem_st32(a_lane + (ia % NA) * kTmemAStage, o);
+                            publish(ia % NA);
+                            if (r == 0) GEMM_EVENT(p, 3, ia);
                         }
-                        publish(ia % NA);
-                        if (r == 0) GEMM_EVENT(p, 3, ia);
                     } else if constexpr (WT == W_Q6K) {
                         Q6KMeta meta;
                         q6k_load_meta(R, r, set, meta);
-                        Q6KHalf qv;
-                        q6k_load_half(R, r, set, qv);  // slices 2 set, 2 set + 1 share one half of ql / qh
-                        if (!(ok = wait_a(ia))) break;
-                        tc_fence_after();
                         #pragma unroll
                         for (int h = 0; h < 2; h++) {
-                            q6k_slice(qv, 2 * set + h, 4 * h, meta, o);
-                            tmem_st32(ta + 32 * h, o);
+                            const int sl = set + 2 * h, ia = 4 * rit + sl;
+                            Q6KHalf qv;
+                            q6k_load_half(R, r, h, qv);  // slice sl uses half sl / 2 = h of ql / qh
+                            q6k_slice(qv, sl, 4 * h, meta, o);
+                            if (!(ok = wait_a(ia))) break;
+                            tc_fence_after();
+                            tmem_st32(a_lane + (ia % NA) * kTmemAStage, o);
+                            publish(ia % NA);
                         }
-                        publish(ia % NA);
                     } else {
-                        if (!(ok = wait_a(ia))) break;
-                        tc_fence_after();
                         #pragma unroll
                         for (int h = 0; h < 2; h++) {
-                            q80_slice(R, r, 2 * set + h, o);
-                            tmem_st32(ta + 32 * h, o);
+                            const int sl = set + 2 * h, ia = 4 * rit + sl;
+                            q80_slice(R, r, sl, o);
+                            if (!(ok = wait_a(ia))) break;
+                            tc_fence_after();
+                            tmem_st32(a_lane + (ia % NA) * kTmemAStage, o);
+                            publish(ia % NA);
                         }
-                        publish(ia % NA);
                     }
                     __syncwarp();
                     if (lane == 0 && (rit % CPR == CPR - 1 || rit == n_units - 1)) mbar_arrive(&raw_empty[rs]);

@@ -223,6 +223,65 @@ __device__ __forceinline__ void mma2_f16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
         "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
+// One 64-wide k-slice = four K = 16 MMAs in one statement, few instructions around them
+// (the issuing warp competes for issue slots with busy dequantizer warps): A from TMEM
+// (8 columns per step), B descriptor advanced by 32 bytes per step; accumulate only
+// the first step decides, the others always accumulate.
+__device__ __forceinline__ void mma2_f16_ts_k64(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                                uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p0, p1;\n\t.reg .b32 a1, a2, a3;\n\t.reg .b64 b1, b2, b3;\n\t"
+        "setp.ne.b32 p0, %4, 0;\n\t"
+        "setp.eq.b32 p1, %4, %4;\n\t"
+        "add.u32 a1, %1, 8;\n\tadd.u32 a2, %1, 16;\n\tadd.u32 a3, %1, 24;\n\t"
+        "add.u64 b1, %2, 2;\n\tadd.u64 b2, %2, 4;\n\tadd.u64 b3, %2, 6;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [a1], b1, %3, p1;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [a2], b2, %3, p1;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [a3], b3, %3, p1;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+#ifdef DFB_GEMM_TRACE
+// Analysis builds: the same four MMAs with a clock read before each and after the last.
+__device__ __forceinline__ void mma2_f16_ts_k64_timed(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                                      uint32_t accumulate, long long (&t)[5]) {
+    asm volatile(
+        "{\n\t.reg .pred p0, p1;\n\t.reg .b32 a1, a2, a3;\n\t.reg .b64 b1, b2, b3;\n\t"
+        "setp.ne.b32 p0, %9, 0;\n\t"
+        "setp.eq.b32 p1, %9, %9;\n\t"
+        "add.u32 a1, %6, 8;\n\tadd.u32 a2, %6, 16;\n\tadd.u32 a3, %6, 24;\n\t"
+        "add.u64 b1, %7, 2;\n\tadd.u64 b2, %7, 4;\n\tadd.u64 b3, %7, 6;\n\t"
+        "mov.u64 %0, %%clock64;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%5], [%6], %7, %8, p0;\n\t"
+        "mov.u64 %1, %%clock64;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%5], [a1], b1, %8, p1;\n\t"
+        "mov.u64 %2, %%clock64;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%5], [a2], b2, %8, p1;\n\t"
+        "mov.u64 %3, %%clock64;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%5], [a3], b3, %8, p1;\n\t"
+        "mov.u64 %4, %%clock64;\n\t}"
+        : "=l"(t[0]), "=l"(t[1]), "=l"(t[2]), "=l"(t[3]), "=l"(t[4])
+        : "r"(d_tmem), "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+#endif
+// Same with A from shared memory (descriptor advanced by 32 bytes per step).
+__device__ __forceinline__ void mma2_f16_ss_k64(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                                uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p0, p1;\n\t.reg .b64 a1, a2, a3, b1, b2, b3;\n\t"
+        "setp.ne.b32 p0, %4, 0;\n\t"
+        "setp.eq.b32 p1, %4, %4;\n\t"
+        "add.u64 a1, %1, 2;\n\tadd.u64 a2, %1, 4;\n\tadd.u64 a3, %1, 6;\n\t"
+        "add.u64 b1, %2, 2;\n\tadd.u64 b2, %2, 4;\n\tadd.u64 b3, %2, 6;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], a1, b1, %3, p1;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], a2, b2, %3, p1;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], a3, b3, %3, p1;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
 // 32 lanes x 32 columns of 32-bit: this thread's lane, columns [col, col+32).
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
     asm volatile(
