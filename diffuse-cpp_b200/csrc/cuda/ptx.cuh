@@ -61,7 +61,10 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t pari
 // the phase has not completed within timeout_ns, or when another role of the CTA or
 // another CTA of the launch already gave up.  No wait in this library can spin forever.
 constexpr uint64_t kWaitTimeoutNs = 4000000000ull;  // 4 s
-constexpr uint32_t kSuspendHintNs = 200000;         // 0.2 ms per try_wait, then re-check the flags
+#ifndef DFB_WAIT_HINT_NS
+#define DFB_WAIT_HINT_NS 200000
+#endif
+constexpr uint32_t kSuspendHintNs = DFB_WAIT_HINT_NS;  // per try_wait, then re-check the flags
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
                                           int *err, int code) {
     if (mbar_try_wait(bar, parity)) return true;
