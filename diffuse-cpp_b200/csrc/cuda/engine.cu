@@ -1114,10 +1114,10 @@ extern "C" int dfb_gen_logits(dfb_ctx *c, int row0, int nrows, float *host) {
 // middle of their work.  dfb_linear_noalloc serves them: the only scratch the dequant
 // GEMM needs (split-tile partial sums and arrival counters) lives in the fixed arrays
 // below, compiled into this library.  Every GPU that loads the library holds them
-// (6 MiB + 16 KiB) until the process exits.
+// (8 MiB + 8 KiB) until the process exits.
 namespace {
 constexpr int kNoallocGrid = 32;                      // CTAs per launch (bounds the scratch)
-constexpr int kNoallocMaxTokens = 256;                // at most two token groups
+constexpr int kNoallocMaxTokens = 256;                // one token group
 constexpr int kNoallocMaxGroups = (kNoallocMaxTokens + kMaxTok - 1) / kMaxTok;
 constexpr int kNoallocMaxTiles = 2040;                // 128-row output tiles (lm_head of 261k vocab)
 constexpr int kCntM = kNoallocMaxGroups * kNoallocMaxTiles;  // [groups x tiles] counters, then M, then the error flag

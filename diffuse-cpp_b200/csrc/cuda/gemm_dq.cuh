@@ -8,19 +8,20 @@
 // The MMA is "swap-AB" and paired (tcgen05 cta_group::2, M = 256): the A operand is a
 // tile of 256 output features, 128 dequantized into the TMEM of each CTA of a pair (F16
 // weights: TMA-loaded into shared memory, 128-byte-swizzled K-major); the B operand is a
-// group of up to 192 tokens of X, each CTA holding half of them (TMA tensor loads into
+// group of up to 256 tokens of X, each CTA holding half of them (TMA tensor loads into
 // shared memory, same swizzle).  The f32 accumulator lives in TMEM: lane = output
 // feature, column = token.
 //
 // Work split.  Units are (pair tile of 256 output rows, token group, k-block of 256); a
 // persistent grid of CTA pairs (one CTA per SM) takes equal contiguous unit ranges
-// ("stream-K").  A tile split across pairs is finished, in each CTA of the pair, by
-// whichever contributor arrives last on the tile's counter: it sums every
-// contributor's f32 partial in contributor order (so the result does not depend on
-// timing) and applies the epilogue.  The token count M is read on the device, so one
-// launch configuration serves every denoising step.
+// ("stream-K").  A tile split across pairs is finished by all of its contributors
+// together once each has written its f32 partial: every contributor takes an equal
+// share of the tile's token columns and sums all partials for them in contributor
+// order (so the result does not depend on timing), then applies the epilogue.  The
+// token count M is read on the device, so one launch configuration serves every
+// denoising step.
 //
-// Warp roles (608 threads per CTA): see the kernel.
+// Warp roles (640 threads per CTA): see the kernel.
 #pragma once
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -87,7 +88,7 @@ struct GemmParams {
     int kb = 0;                  // k-blocks of 256
     const int *m_dev = nullptr;  // token count (device)
     float *ws = nullptr;         // split-tile partials [grid][2][256 * 128]
-    int *tile_cnt = nullptr;     // [n_tiles * 2] arrival counters, left at 0
+    int *tile_cnt = nullptr;     // [n_tiles x token groups] arrival + departure counters, left at 0
     int *err = nullptr;          // first error code of any CTA
     unsigned long long *trace = nullptr;  // DFB_GEMM_TRACE builds only: [grid][16] globaltimer stamps
     EpiArgs epi;
@@ -98,13 +99,17 @@ constexpr int kEpiThreads = 256;         // two epilogue warps per TMEM lane qua
 constexpr int kDeqWarps = 8;             // two sets of four: even / odd k-slices
 constexpr int kSliceBytes = 128 * 128;   // one 64-wide k-slice of this CTA's 128 weight rows (f16)
 constexpr int kABytes = kSliceBytes;      // one A stage: one k-slice
-constexpr int kMaxTok = 192;             // tokens per MMA group (N) of the pair
+constexpr int kMaxTok = 256;             // tokens per MMA group (N) of the pair
+constexpr int kDblTok = 192;             // groups up to this size double-buffer the accumulator
 constexpr int kWsTile = kMaxTok * 128;   // floats per partial tile (one CTA's 128 rows)
 constexpr int kErrTimeout = 0x100;
 constexpr int kMaxAStages = 6, kMaxBSlots = 24, kMaxRawStages = 4;
-// TMEM (512 columns per CTA): accumulators [0, 192) and [192, 384); dequantized A stages
-// (quantized weights) at [384 + 32 st, +32): lane = weight row, one k-slice each.
-constexpr int kTmemA = 2 * kMaxTok;
+// TMEM (512 columns per CTA): accumulators [0, 192) and [192, 384) for token groups of up
+// to 192, one accumulator [0, 256) for larger groups (the MMA of the next segment then
+// waits for the epilogue to drain it, which costs less than dequantizing the weights once
+// per group of 128); dequantized A stages (quantized weights) at [384 + 32 st, +32):
+// lane = weight row, one k-slice each.
+constexpr int kTmemA = 2 * kDblTok;
 constexpr int kTmemAStage = 32;
 
 // Rings per weight type, sized so that shared memory (227 KB) holds them:
@@ -150,12 +155,14 @@ __host__ __device__ constexpr int gemm_smem_bytes(int wt) {
 // both CTAs of a pair.  Units are (pair tile of 256 weight rows, token group, k-block).
 struct Sched {
     int M, n_mg, gsz, kb, n_ot, U, G, u0, u1;
+    bool dbl;                 // double-buffered accumulator (gsz <= kDblTok)
     int bh, spb, bslot, nbs;  // B ring: rows per CTA (widest group), slices per load, slot bytes, slots
     __device__ __forceinline__ void init(int M_, int n_ptiles, int kb_, int n_pairs, int pair, int ring_bytes) {
         M = M_;
         kb = kb_;
         n_mg = (M + kMaxTok - 1) / kMaxTok;
         gsz = (((M + n_mg - 1) / n_mg) + 15) & ~15;
+        dbl = gsz <= kDblTok;
         n_ot = n_ptiles * n_mg;
         U = n_ot * kb;
         G = n_pairs < U ? n_pairs : U;
@@ -165,13 +172,16 @@ struct Sched {
             u0 = (int)((long long)pair * U / G);
             u1 = (int)((long long)(pair + 1) * U / G);
         }
-        bh = ((gsz + 31) & ~31) >> 1;  // 16..96
+        bh = ((gsz + 31) & ~31) >> 1;  // 16..128
         if (bh < 16) bh = 16;
         spb = x_slices(bh);
         bslot = bh * 128 * spb;
         nbs = ring_bytes / bslot;
         if (nbs > kMaxBSlots) nbs = kMaxBSlots;
     }
+    // accumulator buffer of segment si and how many segments used it before
+    __device__ __forceinline__ int acc_of(int si) const { return dbl ? (si & 1) : 0; }
+    __device__ __forceinline__ int acc_uses(int si) const { return dbl ? (si >> 1) : si; }
     __device__ __forceinline__ int owner(int u) const { return (int)(((long long)(u + 1) * G - 1) / U); }
     __device__ __forceinline__ int begin_of(int c) const { return (int)((long long)c * U / G); }
 };
@@ -513,7 +523,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     constexpr int RAWB = raw_chunk_bytes(WT);
     constexpr int NA = a_stages(WT), NRAW = raw_stages(WT), BRING = b_ring_bytes(WT), AR = a_ring_bytes(WT);
     constexpr int CPR = raw_cpr(WT), RSB = CPR * RAWB;  // chunks and bytes per raw stage
-    constexpr int kFixupPeers = (AR + BRING) / 32768;  // partial chunks the drained rings hold
     // The relay frees the B slot of slice j - NA while it handles slice j, after waiting
     // for the B loads up to slice j - 1: with one slice per load (the widest group, 12 KB
     // loads) the producer needs 2 + (NA - 1) slots not to wait on itself.
@@ -529,7 +538,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
              *fix_bar = bars + 73;
     uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 74);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 75);
-    int *bcast = reinterpret_cast<int *>(bars + 76);
     volatile int *okflag = reinterpret_cast<volatile int *>(bars + 77);
     int *s_pos = reinterpret_cast<int *>(bars + kBarBytes / 8);                   // [kMaxTok]
     long long *s_contrib = reinterpret_cast<long long *>(s_pos + kMaxTok);        // [kMaxContrib]
@@ -692,10 +700,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             uint32_t boff = 0;
             for (int u = S.u0; u < S.u1 && ok;) {
                 const Seg g = make_seg(S, u, S.u1);
-                const int acc = si & 1;
-                if (!(ok = mbar_wait(&acc_empty[acc], ((si >> 1) & 1) ^ 1, abort_flag, p.err, kErrTimeout + 3))) break;
+                const int acc = S.acc_of(si);
+                if (!(ok = mbar_wait(&acc_empty[acc], (S.acc_uses(si) & 1) ^ 1, abort_flag, p.err, kErrTimeout + 3))) break;
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + acc * kMaxTok;
+                const uint32_t d_tmem = tmem_base + acc * kDblTok;
                 const uint32_t idesc = idesc_f16(256, (uint32_t)g.nmma);
                 uint32_t accum = 0;
                 for (int kbi = g.k0; kbi < g.k1 && ok; kbi++) {
@@ -910,14 +918,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
     } else {
         // ── epilogue: thread = TMEM lane = output feature of this CTA's tile ──
+        // A whole tile is finished straight from TMEM.  A split tile's partial goes to
+        // the workspace ([column][row] f32, slot 0 for the pair's first tile, 1 for its
+        // last) and its arrival is counted; once every MMA of this CTA is done, each
+        // contributor of a split tile finishes its share of the tile's 16-column chunks,
+        // summing all contributors' partials in contributor order (so the result does
+        // not depend on timing), staged into the drained rings by bulk copies.
         const int q = warp & 3;
         const int row = 32 * q + lane;
         const int half = epi_half(warp);
         const int et = half * 128 + q * 32 + lane;  // 0..255
-        uint32_t fix_phase = 0;
         int si = 0;
         bool ok = true;
         const int first_ot = S.begin_of(pair) / S.kb;
+        int split_u0 = -1, split_u1 = -1;  // first units of this CTA's split segments (first, last)
         auto release_acc = [&](int acc) {
             tc_fence_before();
             __syncwarp();
@@ -926,29 +940,33 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         for (int u = S.u0; u < S.u1 && ok;) {
             const Seg g = make_seg(S, u, S.u1);
             const int tile = 2 * g.pt + (int)rank;
-            const int acc = si & 1;
+            const int acc = S.acc_of(si);
             // one thread waits, the barrier hands the outcome to the whole group
-            if (et == 0) *okflag = mbar_wait(&acc_full[acc], (si >> 1) & 1, abort_flag, p.err, kErrTimeout + 8) ? 1 : 0;
+            if (et == 0) *okflag = mbar_wait(&acc_full[acc], S.acc_uses(si) & 1, abort_flag, p.err, kErrTimeout + 8) ? 1 : 0;
             named_bar_sync(1, kEpiThreads);
             ok = *okflag != 0;
             if (!ok) break;
             if (et == 0 && si < 4) GEMM_STAMP(p, 4 + 2 * si);
             tc_fence_after();
-            const uint32_t taddr = tmem_base + ((uint32_t)(32 * q) << 16) + acc * kMaxTok;
+            const uint32_t taddr = tmem_base + ((uint32_t)(32 * q) << 16) + acc * kDblTok;
             const bool whole = g.k0 == 0 && g.k1 == S.kb;
-            const EpiRow er = epi_row<EPI>(p.epi, tile, row);
-            if constexpr (EPI == EPI_QKV || EPI == EPI_LOGITS) {
-                for (int t = et; t < g.ntok; t += kEpiThreads) s_pos[t] = p.epi.pos[g.m0 + t];
-                named_bar_sync(1, kEpiThreads);
-            }
-            // mode 0: whole tile straight from TMEM; 1: finisher with the other partials
-            // bulk-staged in the drained rings; 2: finisher reading partials from L2;
-            // 3: not the finisher (nothing to emit)
-            int mode = 0, nc = 1, me = 0;
-            const bool last_seg = u + (g.k1 - g.k0) == S.u1;  // rings drained after this one
-            if (!whole) {
-                // Split tile.  Partials are stored [64-column chunk][column][row] (32 KB per
-                // chunk, coalesced for the writers, bank-conflict-free in shared memory).
+            if (whole) {
+                const EpiRow er = epi_row<EPI>(p.epi, tile, row);
+                if constexpr (EPI == EPI_QKV || EPI == EPI_LOGITS) {
+                    for (int t = et; t < g.ntok; t += kEpiThreads) s_pos[t] = p.epi.pos[g.m0 + t];
+                    named_bar_sync(1, kEpiThreads);
+                }
+                for (int c0 = 16 * half; c0 < g.nmma; c0 += 32) {
+                    uint32_t u16[16];
+                    tmem_ld16(taddr + c0, u16);
+                    tmem_ld_wait();
+                    float v[16];
+#pragma unroll
+                    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(u16[i]);
+                    epi_chunk<EPI>(p.epi, er, s_pos, g.m0, c0, g.ntok, v);
+                }
+                release_acc(acc);
+            } else {
                 const int slot = g.ot == first_ot ? 0 : 1;
                 float *wsl = p.ws + ((size_t)blockIdx.x * 2 + slot) * kWsTile;
                 if (et == 0) GEMM_EVENT(p, 6, 5 * si + 0);
@@ -956,104 +974,113 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     uint32_t u16[16];
                     tmem_ld16(taddr + c0, u16);
                     tmem_ld_wait();
-                    float *dst = wsl + (size_t)(c0 >> 6) * 8192 + (size_t)(c0 & 63) * 128 + row;
+                    float *dst = wsl + (size_t)c0 * 128 + row;
 #pragma unroll
                     for (int i = 0; i < 16; i++) dst[i * 128] = __uint_as_float(u16[i]);
                 }
+                // the accumulator is in registers / on its way to the workspace
+                release_acc(acc);
                 __threadfence();
                 named_bar_sync(1, kEpiThreads);
-                const int c_first = S.owner(g.ot * S.kb), c_last = S.owner((g.ot + 1) * S.kb - 1);
-                nc = c_last - c_first + 1;
-                me = pair - c_first;
-                if (et == 0) {
-                    const int old = atomicAdd(&p.tile_cnt[2 * g.ot + rank], 1);
-                    *bcast = (old == nc - 1) ? 1 : 0;
-                    if (nc > kMaxContrib) atomicCAS(p.err, 0, kErrTimeout + 9);  // launcher keeps nc <= kMaxContrib
-                }
-                if (et < nc && et < kMaxContrib) {  // (et < kEpiThreads covers kMaxContrib)
-                    const int c = c_first + et;
-                    const int sl = (S.begin_of(c) / S.kb == g.ot) ? 0 : 1;
-                    s_contrib[et] = ((long long)(2 * c + (int)rank) * 2 + sl) * kWsTile;
-                }
-                named_bar_sync(1, kEpiThreads);
+                if (et == 0) atomicAdd(&p.tile_cnt[2 * g.ot + rank], 1);
+                if (slot == 0) split_u0 = u;
+                else split_u1 = u;
                 if (et == 0) GEMM_EVENT(p, 6, 5 * si + 3);
-                if (!*bcast || nc > kMaxContrib) mode = 3;
-                else {
-                    __threadfence();
-                    mode = (last_seg && nc - 1 <= kFixupPeers) ? 1 : 2;
-                }
             }
-            // the accumulator is in the workspace: let the MMA reuse the TMEM buffer
-            if (mode >= 2) release_acc(acc);
-            if (mode != 3) {
-                const float *sbuf = reinterpret_cast<const float *>(smem);
-                bool staged_ok = true;
-                for (int cb = 0; cb < g.nmma && staged_ok; cb += 64) {
-                    if (mode == 1) {
-                        // stage this 64-column chunk of every other contributor
-                        const int cols = min(64, g.nmma - cb);
-                        named_bar_sync(1, kEpiThreads);  // the previous chunk's buffers are consumed
-                        if (et == 0) {
-                            fence_proxy_async_smem();
-                            mbar_arrive_expect_tx(fix_bar, (uint32_t)(nc - 1) * cols * 512);
-                            for (int c = 0, k = 0; c < nc; c++) {
-                                if (c == me) continue;
-                                bulk_g2s(smem + (size_t)k * 32768, p.ws + s_contrib[c] + (size_t)(cb >> 6) * 8192,
-                                         (uint32_t)cols * 512, fix_bar);
-                                k++;
-                            }
-                            *okflag = mbar_wait(fix_bar, fix_phase, abort_flag, p.err, kErrTimeout + 10) ? 1 : 0;
-                        }
-                        fix_phase ^= 1;
-                        named_bar_sync(1, kEpiThreads);
-                        if (!*okflag) { staged_ok = false; break; }
-                    }
-                  for (int c0 = cb + 16 * half; c0 < min(cb + 64, g.nmma); c0 += 32) {
-                    float v[16];
-                    if (mode <= 1) {
-                        uint32_t u16[16];
-                        tmem_ld16(taddr + c0, u16);
-                        tmem_ld_wait();
-#pragma unroll
-                        for (int i = 0; i < 16; i++) v[i] = __uint_as_float(u16[i]);
-                    }
-                    if (mode >= 1) {
-                        // ordered sum over contributors: the result does not depend on timing
-                        float own[16];
-#pragma unroll
-                        for (int i = 0; i < 16; i++) { own[i] = v[i]; v[i] = 0.f; }
-                        for (int c = 0, k = 0; c < nc; c++) {
-                            float t[16];
-                            if (mode == 1 && c == me) {
-#pragma unroll
-                                for (int i = 0; i < 16; i++) t[i] = own[i];
-                            } else if (mode == 1) {
-                                const float *src = sbuf + (size_t)k * 8192 + (size_t)(c0 & 63) * 128 + row;
-#pragma unroll
-                                for (int i = 0; i < 16; i++) t[i] = src[i * 128];
-                                k++;
-                            } else {
-                                const float *src = p.ws + s_contrib[c] + (size_t)(c0 >> 6) * 8192 + (size_t)(c0 & 63) * 128 + row;
-#pragma unroll
-                                for (int i = 0; i < 16; i++) t[i] = __ldcg(src + i * 128);
-                            }
-#pragma unroll
-                            for (int i = 0; i < 16; i++) v[i] += t[i];
-                        }
-                    }
-                    epi_chunk<EPI>(p.epi, er, s_pos, g.m0, c0, g.ntok, v);
-                  }
-                }
-                if (mode >= 1 && et == 0) {
-                    p.tile_cnt[2 * g.ot + rank] = 0;
-                    GEMM_EVENT(p, 6, 5 * si + 4);
-                }
-            }
-            if (mode <= 1) release_acc(acc);
-            named_bar_sync(1, kEpiThreads);  // okflag / bcast are reused by the next segment
+            named_bar_sync(1, kEpiThreads);  // okflag / s_pos are reused by the next segment
             if (et == 0 && si < 4) GEMM_STAMP(p, 5 + 2 * si);
             si++;
             u += g.k1 - g.k0;
+        }
+
+        // ── deferred split-tile fixups: every MMA of this CTA has completed, so the rings
+        //    (everything below the barriers) are free for staging ──
+        constexpr int kStageBytes = AR + BRING + NRAW * RSB;
+        constexpr int kChunkBytes = 16 * 128 * 4;  // one 16-column chunk of one partial
+        const float *sbuf = reinterpret_cast<const float *>(smem);
+        uint32_t fix_phase = 0;
+        for (int i = 0; i < 2 && ok; i++) {
+            const int su = i == 0 ? split_u0 : split_u1;
+            if (su < 0) continue;
+            const Seg g = make_seg(S, su, S.u1);
+            const int tile = 2 * g.pt + (int)rank;
+            const int c_first = S.owner(g.ot * S.kb), c_last = S.owner((g.ot + 1) * S.kb - 1);
+            const int nc = c_last - c_first + 1, me = pair - c_first;
+            const int nch = g.nmma >> 4;
+            const int ch0 = me * nch / nc, ch1 = (me + 1) * nch / nc;
+            int *cntp = p.tile_cnt + 2 * g.ot + rank;
+            if (et < nc && et < kMaxContrib) {
+                const int c = c_first + et;
+                const int sl = (S.begin_of(c) / S.kb == g.ot) ? 0 : 1;
+                s_contrib[et] = ((long long)(2 * c + (int)rank) * 2 + sl) * kWsTile;
+            }
+            if constexpr (EPI == EPI_QKV || EPI == EPI_LOGITS) {
+                for (int t = et; t < g.ntok; t += kEpiThreads) s_pos[t] = p.epi.pos[g.m0 + t];
+            }
+            if (et == 0) {
+                int okw = nc <= kMaxContrib;  // the launcher keeps nc <= kMaxContrib
+                if (!okw) atomicCAS(p.err, 0, kErrTimeout + 9);
+                else okw = wait_count(cntp, nc, abort_flag, p.err, kErrTimeout + 13);
+                *okflag = okw;
+                if (okw) fence_proxy_async_all();  // the partials, seen here, before the bulk reads
+            }
+            named_bar_sync(1, kEpiThreads);
+            ok = *okflag != 0;
+            if (!ok) break;
+            if (et == 0) GEMM_EVENT(p, 6, 5 * si + 0);
+            const EpiRow er = epi_row<EPI>(p.epi, tile, row);
+            const bool staged = nc * kChunkBytes <= kStageBytes;
+            const int per_round = staged ? kStageBytes / (nc * kChunkBytes) : 1;
+            for (int r0 = ch0; r0 < ch1; r0 += per_round) {
+                const int nr = min(ch1, r0 + per_round) - r0;
+                if (staged) {
+                    if (et == 0) {
+                        mbar_arrive_expect_tx(fix_bar, (uint32_t)(nc * nr * kChunkBytes));
+                        for (int c = 0; c < nc; c++)
+                            bulk_g2s(smem + (size_t)c * nr * kChunkBytes, p.ws + s_contrib[c] + (size_t)r0 * 2048,
+                                     (uint32_t)(nr * kChunkBytes), fix_bar);
+                        *okflag = mbar_wait(fix_bar, fix_phase, abort_flag, p.err, kErrTimeout + 10) ? 1 : 0;
+                    }
+                    fix_phase ^= 1;
+                    named_bar_sync(1, kEpiThreads);
+                    if (!*okflag) { ok = false; break; }
+                    if (et == 0 && r0 == ch0) GEMM_EVENT(p, 6, 5 * si + 1);
+                }
+                for (int ch = r0 + half; ch < r0 + nr; ch += 2) {
+                    float v[16];
+#pragma unroll
+                    for (int k = 0; k < 16; k++) v[k] = 0.f;
+                    for (int c = 0; c < nc; c++) {
+                        if (staged) {
+                            const float *src = sbuf + ((size_t)c * nr + (ch - r0)) * 2048 + row;
+#pragma unroll
+                            for (int k = 0; k < 16; k++) v[k] += src[k * 128];
+                        } else {
+                            const float *src = p.ws + s_contrib[c] + (size_t)ch * 2048 + row;
+                            float t[16];
+#pragma unroll
+                            for (int k = 0; k < 16; k++) t[k] = __ldcg(src + k * 128);
+#pragma unroll
+                            for (int k = 0; k < 16; k++) v[k] += t[k];
+                        }
+                    }
+                    epi_chunk<EPI>(p.epi, er, s_pos, g.m0, ch * 16, g.ntok, v);
+                }
+                // staged chunks consumed before the next round's copies; generic reads of the
+                // staging area before the async-proxy writes
+                named_bar_sync(1, kEpiThreads);
+                if (et == 0) fence_proxy_async_smem();
+                if (et == 0 && r0 == ch0) GEMM_EVENT(p, 6, 5 * si + 2);
+            }
+            if (!ok) break;
+            // departure: the last of the nc contributors resets the counter for the next launch
+            if (et == 0) {
+                const int old = atomicAdd(cntp, 1);
+                if (old == 2 * nc - 1) *cntp = 0;
+                GEMM_EVENT(p, 6, 5 * si + 4);
+            }
+            named_bar_sync(1, kEpiThreads);  // s_contrib / s_pos / okflag reused
+            si++;
         }
     }
 

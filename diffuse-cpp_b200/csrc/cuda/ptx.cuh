@@ -117,6 +117,33 @@ __device__ __forceinline__ void prefetch_tmap(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 // Make generic-proxy shared-memory writes visible to the async proxy (tensor core).
+// Generic-proxy accesses (global and shared) before later async-proxy (bulk copy) ones.
+__device__ __forceinline__ void fence_proxy_async_all() { asm volatile("fence.proxy.async;" ::: "memory"); }
+__device__ __forceinline__ int ld_acquire_gpu(const int *p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+// Bounded wait until the global counter *c reaches target (acquire), with the abort
+// rules of mbar_wait.  Every CTA of a launch is resident at once (one per SM), so the
+// CTAs whose arrivals this waits for are running.
+__device__ __forceinline__ bool wait_count(const int *c, int target, volatile int *abort_flag, int *err, int code) {
+    const uint64_t t0 = globaltimer();
+    for (;;) {
+        if (ld_acquire_gpu(c) >= target) return true;
+        if (*abort_flag) return false;
+        if (*reinterpret_cast<volatile int *>(err)) {
+            *abort_flag = 1;
+            return false;
+        }
+        if (globaltimer() - t0 > kWaitTimeoutNs) {
+            *abort_flag = 1;
+            atomicCAS(err, 0, code);
+            return false;
+        }
+        __nanosleep(32);
+    }
+}
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

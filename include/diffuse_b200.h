@@ -141,7 +141,7 @@ int dfb_ctx_profile_read(dfb_ctx *c, dfb_prof_entry *out, int n);      /* n <= D
  * y[M x n_out] = x[M x K] . W^T through the dequant GEMM for an unfused weight
  * (DFB_WO, DFB_DOWN or DFB_OUTPUT); x_f16_dev is a device f16 matrix [M][K] (16-byte
  * aligned), y_dev a device f32 matrix [M][n_out], both owned by the caller.  The GEMM's scratch (split
- * partial sums and arrival counters) is a fixed 6 MiB + 16 KiB array compiled into the
+ * partial sums and arrival counters) is a fixed 8 MiB + 8 KiB array compiled into the
  * library, held by every GPU that loads it until exit; M above 256 or a weight of more
  * than 2040 row tiles is rejected with DFB_ERR_ARG.  Nothing is allocated: no
  * cudaMalloc / cudaFree, no allocating library call.  The first call on a device looks
