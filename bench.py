@@ -285,35 +285,14 @@ def main():
     if args.impl == "reference":
         return run_reference(args, cfg)
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    dist = None
-    if world > 1:
-        import datetime
-
-        import torch
-        import torch.distributed as tdist
-        torch.cuda.set_device(local)
-        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
-        dist = tdist
+    pkg = load_pkg()
+    # one process per GPU (torchrun); each rank generates its own sequences, nothing
+    # crosses ranks on the data path (diffuse-cpp_b200/dp.py)
+    dp = pkg.dp.DataParallel.from_env(timeout_s=600, backend="nccl")
+    world, rank, local = dp.world, dp.rank, dp.local
     os.environ["DIFFUSE_DEVICE"] = str(local)
     os.environ.setdefault("DIFFUSE_LOG_LEVEL", "0")
-    pkg = load_pkg()
-
-    def barrier():
-        if dist:
-            import torch
-            dist.barrier(device_ids=[local])
-            torch.cuda.synchronize()
-
-    def reduce_max(x):
-        if not dist:
-            return x
-        import torch
-        t = torch.tensor([x], dtype=torch.float64, device=f"cuda:{local}")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+    barrier, reduce_max = dp.barrier, dp.max_over_ranks
 
     work = pathlib.Path(os.environ.get("DFB_BENCH_DIR", tempfile.gettempdir())) / "dfb_bench"
     work.mkdir(parents=True, exist_ok=True)
@@ -419,9 +398,7 @@ def main():
         print(json.dumps(line), flush=True)
     ctx.close()
     model.close()
-    if dist:
-        dist.barrier(device_ids=[local])
-        dist.destroy_process_group()
+    dp.close()
     return 0
 
 

@@ -329,3 +329,6 @@ class Context:
             self.close()
         except Exception:
             pass
+
+
+from . import dp  # noqa: E402  (data-parallel plumbing over independent sequences)
