@@ -3,9 +3,10 @@
 // Owns the device-resident model (weights re-tiled for the dequant GEMM), the
 // per-context activations / K/V cache / logits buffer / sequence state, and the
 // launch order of one denoising step:
-//   step_prepare -> embed -> L x [rmsnorm, QKV(+bias,RoPE,cache write), attention,
-//   O(+residual), rmsnorm, gate|up(SwiGLU), down(+residual)] -> rmsnorm -> lm_head
-//   (logits scattered to their positions) -> row statistics -> order + commit.
+//   step_prepare -> embed -> L x [(residual +) rmsnorm, QKV(+bias,RoPE,cache write),
+//   attention, O, residual + rmsnorm, gate|up(SwiGLU), down] -> residual + rmsnorm ->
+//   lm_head (logits scattered to their positions) -> row statistics -> order + commit.
+// The O and down projections write y; the next RMSNorm adds y into the residual stream x.
 // This is the device side of src/diffuse-sampler.cpp:127-323 with the forward of
 // src/diffuse-graph.cpp:11-160 / 395-593.
 #include <cuda.h>
@@ -540,7 +541,7 @@ struct dfb_ctx {
     cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
     int cap = 0;
     // activations
-    float *x = nullptr, *logits = nullptr;
+    float *x = nullptr, *y = nullptr, *logits = nullptr;  // residual stream, projection output, logits
     __half *h = nullptr, *att = nullptr, *q = nullptr, *ffh = nullptr, *kc = nullptr, *vc = nullptr;
     float2 *rope = nullptr;
     XMaps xm_h{}, xm_att{}, xm_ffh{};  // GEMM B-operand views of h, att, ffh
@@ -571,11 +572,11 @@ struct dfb_ctx {
 };
 
 static void ctx_free_buffers(dfb_ctx *c) {
-    void *ps[] = {c->x, c->logits, c->h, c->att, c->q, c->ffh, c->kc, c->vc, c->rope, c->seq, c->prev_seq,
+    void *ps[] = {c->x, c->y, c->logits, c->h, c->att, c->q, c->ffh, c->kc, c->vc, c->rope, c->seq, c->prev_seq,
                   c->last_changed, c->cand_tok, c->commit_pos, c->commit_tok, c->order, c->masked, c->active_pos,
                   c->masked_pos, c->cnt, c->cand_conf, c->cand_ent, c->ws, c->tile_cnt, c->err};
     for (void *p : ps) cudaFree(p);
-    c->x = c->logits = nullptr; c->h = c->att = c->q = c->ffh = c->kc = c->vc = nullptr; c->rope = nullptr;
+    c->x = c->y = c->logits = nullptr; c->h = c->att = c->q = c->ffh = c->kc = c->vc = nullptr; c->rope = nullptr;
     c->seq = c->prev_seq = c->last_changed = c->cand_tok = c->commit_pos = c->commit_tok = c->order = nullptr;
     c->masked = nullptr; c->active_pos = c->masked_pos = c->cnt = nullptr; c->cand_conf = c->cand_ent = nullptr;
     c->ws = nullptr; c->tile_cnt = c->err = nullptr;
@@ -605,7 +606,7 @@ static int ctx_reserve(dfb_ctx *c, int n) {
     ctx_free_buffers(c);
     const size_t d = hp.n_embd, ff = hp.n_ff, V = hp.n_vocab, L = hp.n_layer, kvd = m->n_kv, hd = m->hd;
 #define AL(ptr, count) CK(cudaMalloc(&(ptr), sizeof(*(ptr)) * (size_t)(count)))
-    AL(c->x, cap * d); AL(c->h, cap * d); AL(c->att, cap * d); AL(c->q, cap * d); AL(c->ffh, cap * ff);
+    AL(c->x, cap * d); AL(c->y, cap * d); AL(c->h, cap * d); AL(c->att, cap * d); AL(c->q, cap * d); AL(c->ffh, cap * ff);
     AL(c->kc, L * cap * kvd); AL(c->vc, L * cap * kvd); AL(c->logits, (size_t)cap * V); AL(c->rope, cap * hd / 2);
     AL(c->seq, cap); AL(c->prev_seq, cap); AL(c->last_changed, cap); AL(c->cand_tok, cap); AL(c->commit_pos, cap);
     AL(c->commit_tok, cap); AL(c->order, cap); AL(c->masked, cap); AL(c->active_pos, cap); AL(c->masked_pos, cap);
@@ -621,6 +622,7 @@ static int ctx_reserve(dfb_ctx *c, int n) {
     CK(cudaMemset(c->err, 0, sizeof(int)));
     CK(cudaMemset(c->cnt, 0, sizeof(int) * CNT_N));
     CK(cudaMemset(c->x, 0, sizeof(float) * cap * d));
+    CK(cudaMemset(c->y, 0, sizeof(float) * cap * d));
     CK(cudaMemset(c->h, 0, 2 * cap * d));
     CK(cudaMemset(c->att, 0, 2 * cap * d));
     CK(cudaMemset(c->ffh, 0, 2 * cap * ff));
@@ -811,8 +813,9 @@ static int run_forward(dfb_ctx *c, int n_total) {
     for (int l = 0; l < hp.n_layer; l++) {
         const LayerW &L = m->layers[l];
         __half *kc = c->kc + (size_t)l * cap * m->n_kv, *vc = c->vc + (size_t)l * cap * m->n_kv;
-        CK(launch_k(rmsnorm_kernel, dim3(cap), dim3(256), 0, c->st, true, (const float *)c->x, (const float *)L.attn_norm, d,
-                    hp.rms_norm_eps, (const int *)c->cnt, c->h));
+        // the previous layer's down projection is added to the residual stream here
+        CK(launch_k(rmsnorm_kernel, dim3(cap), dim3(256), 0, c->st, true, c->x, (const float *)(l ? c->y : nullptr),
+                    (const float *)L.attn_norm, d, hp.rms_norm_eps, (const int *)c->cnt, c->h));
         EpiArgs e;
         e.q_out = c->q; e.ld_q = m->n_q;
         e.k_cache = kc; e.v_cache = vc; e.ld_kv = m->n_kv;
@@ -826,20 +829,20 @@ static int run_forward(dfb_ctx *c, int n_total) {
             case 64: RET(launch_attn_t<64>(c, kc, vc, n_total)); break;
             default: RET(launch_attn_t<128>(c, kc, vc, n_total)); break;
         }
-        EpiArgs eo;
-        eo.out = c->x; eo.ld = d; eo.n_valid = d;
-        RET(launch_gemm<EPI_RESID>(c, L.o, c->xm_att, eo));
-        CK(launch_k(rmsnorm_kernel, dim3(cap), dim3(256), 0, c->st, true, (const float *)c->x, (const float *)L.ffn_norm, d,
-                    hp.rms_norm_eps, (const int *)c->cnt, c->h));
+        EpiArgs eo;  // attention output projection -> y, added to x by the next norm
+        eo.out = c->y; eo.ld = d; eo.n_valid = d;
+        RET(launch_gemm<EPI_F32>(c, L.o, c->xm_att, eo));
+        CK(launch_k(rmsnorm_kernel, dim3(cap), dim3(256), 0, c->st, true, c->x, (const float *)c->y,
+                    (const float *)L.ffn_norm, d, hp.rms_norm_eps, (const int *)c->cnt, c->h));
         EpiArgs eg;
         eg.out = c->ffh; eg.ld = hp.n_ff; eg.n_valid = 2 * hp.n_ff;
         RET(launch_gemm<EPI_SWIGLU>(c, L.gateup, c->xm_h, eg));
-        EpiArgs ed;
-        ed.out = c->x; ed.ld = d; ed.n_valid = d;
-        RET(launch_gemm<EPI_RESID>(c, L.down, c->xm_ffh, ed));
+        EpiArgs ed;  // FFN down projection -> y, added to x by the next norm
+        ed.out = c->y; ed.ld = d; ed.n_valid = d;
+        RET(launch_gemm<EPI_F32>(c, L.down, c->xm_ffh, ed));
     }
-    CK(launch_k(rmsnorm_kernel, dim3(cap), dim3(256), 0, c->st, true, (const float *)c->x, (const float *)m->output_norm, d,
-                hp.rms_norm_eps, (const int *)c->cnt, c->h));
+    CK(launch_k(rmsnorm_kernel, dim3(cap), dim3(256), 0, c->st, true, c->x, (const float *)(hp.n_layer ? c->y : nullptr),
+                (const float *)m->output_norm, d, hp.rms_norm_eps, (const int *)c->cnt, c->h));
     EpiArgs el;
     el.out = c->logits; el.ld = hp.n_vocab; el.n_valid = hp.n_vocab; el.pos = c->active_pos;
     RET(launch_gemm<EPI_LOGITS>(c, m->lm_head, c->xm_h, el));

@@ -48,7 +48,7 @@ namespace dfb {
 #endif
 
 enum WType : int { W_Q4K = 0, W_Q6K = 1, W_Q80 = 2, W_F16 = 3 };
-enum EpiKind : int { EPI_F32 = 0, EPI_F16 = 1, EPI_RESID = 2, EPI_QKV = 3, EPI_SWIGLU = 4, EPI_LOGITS = 5 };
+enum EpiKind : int { EPI_F32 = 0, EPI_F16 = 1, EPI_QKV = 3, EPI_SWIGLU = 4, EPI_LOGITS = 5 };
 
 // Bytes of one re-tiled chunk (128 rows x one k-block of 256 elements).
 __host__ __device__ constexpr int raw_chunk_bytes(int wt) {
@@ -122,7 +122,7 @@ constexpr int kTmemAStage = 32;
 //  raw ring re-tiled weight chunks (one k-block of 256 for 128 rows), grouped.
 __host__ __device__ constexpr int a_stages(int wt) { return 4; }
 __host__ __device__ constexpr int a_ring_bytes(int wt) { return wt == W_F16 ? 4 * kABytes : 0; }
-__host__ __device__ constexpr int b_ring_bytes(int wt) { return 112 * 1024; }
+__host__ __device__ constexpr int b_ring_bytes(int wt) { return 96 * 1024; }
 // A raw stage holds raw_cpr consecutive chunks of the CTA's unit range: the weight
 // stream reached ~3.8 TB/s with 18 KB stages and ~6-7 TB/s with 36-72 KB stages
 // (same bytes in flight), so small chunks are grouped.
@@ -144,11 +144,12 @@ __host__ __device__ constexpr int deq_index(int w) { return w - 4; }
 // epilogue thread group: warps 12-15 and 16-19 each cover the four lane quarters
 __host__ __device__ constexpr int epi_half(int w) { return w >= 16 ? 1 : 0; }
 
+constexpr int kEpiStageBytes = 16 * 128 * 4;  // epilogue output staging per half: 16 tokens x 128 f32
 constexpr int kMaxContrib = 64;     // split contributors (CTA pairs) of one tile tracked in shared memory
 constexpr int kBarBytes = 80 * 8;   // mbarriers and flags, see the kernel's shared-memory map
 __host__ __device__ constexpr int gemm_smem_bytes(int wt) {
     return 1024 /*align slack*/ + a_ring_bytes(wt) + b_ring_bytes(wt) + raw_stages(wt) * raw_cpr(wt) * raw_chunk_bytes(wt) +
-           kBarBytes /*barriers, flags*/ + 4 * kMaxTok /*token positions*/ + 8 * kMaxContrib /*contributor partial offsets*/;
+           2 * kEpiStageBytes /*epilogue output staging*/ + kBarBytes /*barriers, flags*/ + 4 * kMaxTok /*token positions*/ + 8 * kMaxContrib /*contributor partial offsets*/;
 }
 
 // Static stream-K schedule over CTA pairs, recomputed identically by every role of
@@ -389,6 +390,7 @@ __device__ __forceinline__ void q80_slice(const uint8_t *R, int r, int s, uint32
 // Per-thread constants of one output tile (thread = TMEM lane = one output row).
 struct EpiRow {
     int f;          // output feature written by this lane (after un-fusing)
+    int col;        // its column in the tile's staging rows
     bool fvalid;    // f is a real feature (not tile padding)
     bool writer;    // this lane stores (SwiGLU: the gate lane of each pair)
     int sec;        // QKV: 0 Q, 1 K, 2 V
@@ -397,20 +399,27 @@ struct EpiRow {
     float bias;     // QKV bias of this row (0 without bias)
 };
 
+// QKV tile -> section (0 Q, 1 K, 2 V) and tile index within it.
+__device__ __forceinline__ int qkv_section(const EpiArgs &e, int tile, int &lt) {
+    if (tile < e.n_q_tiles) { lt = tile; return 0; }
+    if (tile < e.n_q_tiles + e.n_k_tiles) { lt = tile - e.n_q_tiles; return 1; }
+    lt = tile - e.n_q_tiles - e.n_k_tiles;
+    return 2;
+}
+
 template <int EPI>
 __device__ __forceinline__ EpiRow epi_row(const EpiArgs &e, int tile, int row) {
     EpiRow r{};
     if constexpr (EPI == EPI_SWIGLU) {
         // rows interleaved: 2i = gate_i, 2i+1 = up_i
         r.f = tile * 64 + (row >> 1);
+        r.col = row >> 1;
         r.fvalid = 2 * r.f < e.n_valid;
         r.writer = (row & 1) == 0;
     } else if constexpr (EPI == EPI_QKV) {
         const int hd = e.head_dim;
         int lt;
-        if (tile < e.n_q_tiles) { r.sec = 0; lt = tile; }
-        else if (tile < e.n_q_tiles + e.n_k_tiles) { r.sec = 1; lt = tile - e.n_q_tiles; }
-        else { r.sec = 2; lt = tile - e.n_q_tiles - e.n_k_tiles; }
+        r.sec = qkv_section(e, tile, lt);
         const int fl = lt * 128 + row;
         const int sec_off = r.sec == 0 ? 0 : r.sec == 1 ? e.n_q_tiles * 128 : (e.n_q_tiles + e.n_k_tiles) * 128;
         if (r.sec < 2) {
@@ -422,79 +431,134 @@ __device__ __forceinline__ EpiRow epi_row(const EpiArgs &e, int tile, int row) {
         } else {
             r.f = fl;
         }
+        r.col = r.f - lt * 128;  // heads divide the 128-row tile, so the tile's features stay in it
         r.fvalid = r.f < (r.sec == 0 ? e.n_q : e.n_kv);
         r.bias = (e.bias && r.fvalid) ? __ldg(e.bias + sec_off + r.f) : 0.f;
         r.writer = true;
     } else {
         r.f = tile * 128 + row;
+        r.col = row;
         r.fvalid = r.f < e.n_valid;
         r.writer = true;
     }
     return r;
 }
 
-// Epilogue of 16 consecutive tokens (tl0 .. tl0+15 of the segment) for this lane's row.
-// All global loads of a chunk are issued before any store, so they overlap.  Called
-// by all 32 lanes of a warp together (paired epilogues exchange values with the
-// neighbouring lane).  s_pos: positions of the segment's tokens (shared memory).
+// Output staging: a chunk of 16 tokens x the tile's output features, one per epilogue
+// half, written by the row threads and stored to global memory as whole token rows.
+template <int EPI> struct EpiFmt {
+    static constexpr int esize = (EPI == EPI_F32 || EPI == EPI_LOGITS) ? 4 : 2;
+    static constexpr int width = EPI == EPI_SWIGLU ? 64 : 128;  // output features per tile
+    static constexpr int row_bytes = esize * width;            // staging row pitch
+};
+
+// Where one tile's token rows go.
+struct EpiDst {
+    char *base;      // the tile's first output feature in row 0
+    long long ld;    // bytes between rows
+    int nbytes;      // valid bytes per row (0: the tile is padding)
+    bool by_pos;     // row index = the token's position (else m0 + token)
+    bool vec;        // 16-byte vector stores are aligned
+};
 template <int EPI>
-__device__ __forceinline__ void epi_chunk(const EpiArgs &e, const EpiRow &r, const int *s_pos, int m0, int tl0,
-                                          int ntok, float (&v)[16]) {
-    const int nvalid = r.fvalid ? min(16, ntok - tl0) : 0;  // tokens of this chunk that are stored
-    if constexpr (EPI == EPI_F32 || EPI == EPI_F16) {
-        const size_t base = (size_t)(m0 + tl0) * e.ld + r.f;
+__device__ __forceinline__ EpiDst epi_dst(const EpiArgs &e, int tile) {
+    constexpr int es = EpiFmt<EPI>::esize, W = EpiFmt<EPI>::width;
+    EpiDst d{};
+    long long ld_el;
+    int n_feat, f0;
+    if constexpr (EPI == EPI_QKV) {
+        int lt;
+        const int sec = qkv_section(e, tile, lt);
+        f0 = lt * 128;
+        char *b = reinterpret_cast<char *>(sec == 0 ? e.q_out : sec == 1 ? e.k_cache : e.v_cache);
+        d.base = b + (size_t)f0 * es;
+        ld_el = sec == 0 ? e.ld_q : e.ld_kv;
+        n_feat = (sec == 0 ? e.n_q : e.n_kv) - f0;
+        d.by_pos = sec != 0;
+    } else {
+        f0 = tile * W;
+        d.base = reinterpret_cast<char *>(e.out) + (size_t)f0 * es;
+        ld_el = e.ld;
+        n_feat = (EPI == EPI_SWIGLU ? e.n_valid / 2 : e.n_valid) - f0;
+        d.by_pos = EPI == EPI_LOGITS;
+    }
+    d.ld = ld_el * es;
+    d.nbytes = max(0, min(W, n_feat)) * es;
+    d.vec = (reinterpret_cast<uintptr_t>(d.base) % 16 == 0) && (d.ld % 16 == 0);
+    return d;
+}
+
+// Epilogue math of 16 consecutive tokens (tl0 .. tl0+15 of the segment) for this lane's
+// row, into the staging rows.  Called by all 32 lanes of a warp together (paired
+// epilogues exchange values with the neighbouring lane).  s_pos: positions of the
+// segment's tokens (shared memory).
+template <int EPI>
+__device__ __forceinline__ void epi_values(const EpiArgs &e, const EpiRow &r, const int *s_pos, int tl0, int ntok,
+                                           float (&v)[16], uint8_t *stage) {
+    constexpr int RB = EpiFmt<EPI>::row_bytes;
+    if constexpr (EPI == EPI_F32 || EPI == EPI_LOGITS) {
 #pragma unroll
-        for (int i = 0; i < 16; i++) {
-            if (i < nvalid) {
-                if constexpr (EPI == EPI_F32) reinterpret_cast<float *>(e.out)[base + (size_t)i * e.ld] = v[i];
-                else reinterpret_cast<__half *>(e.out)[base + (size_t)i * e.ld] = __float2half_rn(v[i]);
-            }
-        }
-    } else if constexpr (EPI == EPI_RESID) {
-        float *x = reinterpret_cast<float *>(e.out) + (size_t)(m0 + tl0) * e.ld + r.f;
-        float old[16];
+        for (int i = 0; i < 16; i++) reinterpret_cast<float *>(stage + i * RB)[r.col] = v[i];
+    } else if constexpr (EPI == EPI_F16) {
 #pragma unroll
-        for (int i = 0; i < 16; i++) old[i] = i < nvalid ? x[(size_t)i * e.ld] : 0.f;
-#pragma unroll
-        for (int i = 0; i < 16; i++)
-            if (i < nvalid) x[(size_t)i * e.ld] = v[i] + old[i];
-    } else if constexpr (EPI == EPI_LOGITS) {
-        float *out = reinterpret_cast<float *>(e.out) + r.f;
-#pragma unroll
-        for (int i = 0; i < 16; i++)
-            if (i < nvalid) out[(size_t)s_pos[tl0 + i] * e.ld] = v[i];
+        for (int i = 0; i < 16; i++) reinterpret_cast<__half *>(stage + i * RB)[r.col] = __float2half_rn(v[i]);
     } else if constexpr (EPI == EPI_SWIGLU) {
-        __half *out = reinterpret_cast<__half *>(e.out) + (size_t)(m0 + tl0) * e.ld + r.f;
 #pragma unroll
         for (int i = 0; i < 16; i++) {
             const float up = __shfl_xor_sync(0xffffffffu, v[i], 1);
             const float g = v[i];
-            const float h = g * up * (1.0f / (1.0f + __expf(-g)));
-            if (r.writer && i < nvalid) out[(size_t)i * e.ld] = __float2half_rn(h);
+            const float h = __fdividef(g * up, 1.0f + __expf(-g));  // silu(g) * up
+            if (r.writer) reinterpret_cast<__half *>(stage + i * RB)[r.col] = __float2half_rn(h);
         }
     } else if constexpr (EPI == EPI_QKV) {
-        const int hh = e.head_dim >> 1;
         if (r.sec < 2) {
-            float2 cs[16];
+            const int hh = e.head_dim >> 1;
+            float2 csv[16];
 #pragma unroll
             for (int i = 0; i < 16; i++) {
                 const int pp = tl0 + i < ntok ? s_pos[tl0 + i] : 0;
-                cs[i] = __ldg(e.rope + (size_t)pp * hh + r.ipair);
+                csv[i] = __ldg(e.rope + (size_t)pp * hh + r.ipair);
             }
 #pragma unroll
             for (int i = 0; i < 16; i++) {
+                const float2 cs = csv[i];
                 const float x = v[i] + r.bias;
                 const float partner = __shfl_xor_sync(0xffffffffu, x, 1);
-                const float o = r.bpair == 0 ? (x * cs[i].x - partner * cs[i].y) : (partner * cs[i].y + x * cs[i].x);
-                if (i < nvalid) {
-                    if (r.sec == 0) e.q_out[(size_t)(m0 + tl0 + i) * e.ld_q + r.f] = __float2half_rn(o);
-                    else e.k_cache[(size_t)s_pos[tl0 + i] * e.ld_kv + r.f] = __float2half_rn(o);
-                }
+                const float o = r.bpair == 0 ? (x * cs.x - partner * cs.y) : (partner * cs.y + x * cs.x);
+                if (r.col < 128) reinterpret_cast<__half *>(stage + i * RB)[r.col] = __float2half_rn(o);
             }
         } else {
 #pragma unroll
             for (int i = 0; i < 16; i++)
-                if (i < nvalid) e.v_cache[(size_t)s_pos[tl0 + i] * e.ld_kv + r.f] = __float2half_rn(v[i] + r.bias);
+                if (r.col < 128) reinterpret_cast<__half *>(stage + i * RB)[r.col] = __float2half_rn(v[i] + r.bias);
+        }
+    }
+}
+
+// Stores the staged chunk as token rows: lanes of a warp cover a row in 16-byte pieces.
+// tid: 0..127 within the epilogue half.
+template <int EPI>
+__device__ __forceinline__ void epi_copyout(const EpiDst &d, const int *s_pos, int m0, int tl0, int ntok,
+                                            const uint8_t *stage, int tid) {
+    constexpr int es = EpiFmt<EPI>::esize, RB = EpiFmt<EPI>::row_bytes;
+    constexpr int LPR = RB / 16, RPW = 32 / LPR;  // lanes per row, rows per warp pass
+    const int w = tid >> 5, lane = tid & 31;
+    const int off = (lane % LPR) * 16;
+    if (off >= d.nbytes) return;
+    for (int i = w * RPW + lane / LPR; i < 16; i += 4 * RPW) {
+        const int t = tl0 + i;
+        if (t >= ntok) break;
+        const long long rowi = d.by_pos ? (long long)s_pos[t] : (long long)(m0 + t);
+        char *dst = d.base + rowi * d.ld + off;
+        const uint8_t *src = stage + i * RB + off;
+        if (d.vec && off + 16 <= d.nbytes) {
+            *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<const uint4 *>(src);
+        } else {
+            const int nb = min(16, d.nbytes - off);
+            for (int b = 0; b < nb; b += es) {
+                if constexpr (es == 4) *reinterpret_cast<float *>(dst + b) = *reinterpret_cast<const float *>(src + b);
+                else *reinterpret_cast<__half *>(dst + b) = *reinterpret_cast<const __half *>(src + b);
+            }
         }
     }
 }
@@ -532,7 +596,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     uint8_t *aring = smem;  // F16 weights only
     uint8_t *bring = smem + AR;
     uint8_t *raw = bring + BRING;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(raw + NRAW * RSB);
+    uint8_t *epi_stage = raw + NRAW * RSB;  // [2 halves][kEpiStageBytes]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(epi_stage + 2 * kEpiStageBytes);
     uint64_t *full_a = bars, *empty_a = bars + 6, *full_b = bars + 12, *empty_b = bars + 36, *raw_full = bars + 60,
              *raw_empty = bars + 64, *acc_full = bars + 68, *acc_empty = bars + 70, *drain = bars + 72,
              *fix_bar = bars + 73;
@@ -919,8 +984,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     } else {
         // ── epilogue: thread = TMEM lane = output feature of this CTA's tile ──
         // A whole tile is finished straight from TMEM.  A split tile's partial goes to
-        // the workspace ([column][row] f32, slot 0 for the pair's first tile, 1 for its
-        // last) and its arrival is counted; once every MMA of this CTA is done, each
+        // the workspace (f32 [column / 4][row][column % 4], slot 0 for the pair's first
+        // tile, 1 for its last) and its arrival is counted; once every MMA of this CTA is done, each
         // contributor of a split tile finishes its share of the tile's 16-column chunks,
         // summing all contributors' partials in contributor order (so the result does
         // not depend on timing), staged into the drained rings by bulk copies.
@@ -928,6 +993,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const int row = 32 * q + lane;
         const int half = epi_half(warp);
         const int et = half * 128 + q * 32 + lane;  // 0..255
+        const int tid_h = q * 32 + lane;            // 0..127 within the half
+        uint8_t *my_stage = epi_stage + half * kEpiStageBytes;
         int si = 0;
         bool ok = true;
         const int first_ot = S.begin_of(pair) / S.kb;
@@ -952,6 +1019,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const bool whole = g.k0 == 0 && g.k1 == S.kb;
             if (whole) {
                 const EpiRow er = epi_row<EPI>(p.epi, tile, row);
+                const EpiDst dd = epi_dst<EPI>(p.epi, tile);
                 if constexpr (EPI == EPI_QKV || EPI == EPI_LOGITS) {
                     for (int t = et; t < g.ntok; t += kEpiThreads) s_pos[t] = p.epi.pos[g.m0 + t];
                     named_bar_sync(1, kEpiThreads);
@@ -963,7 +1031,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     float v[16];
 #pragma unroll
                     for (int i = 0; i < 16; i++) v[i] = __uint_as_float(u16[i]);
-                    epi_chunk<EPI>(p.epi, er, s_pos, g.m0, c0, g.ntok, v);
+                    epi_values<EPI>(p.epi, er, s_pos, c0, g.ntok, v, my_stage);
+                    named_bar_sync(2 + half, kEpiThreads / 2);
+                    epi_copyout<EPI>(dd, s_pos, g.m0, c0, g.ntok, my_stage, tid_h);
+                    named_bar_sync(2 + half, kEpiThreads / 2);
                 }
                 release_acc(acc);
             } else {
@@ -974,9 +1045,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     uint32_t u16[16];
                     tmem_ld16(taddr + c0, u16);
                     tmem_ld_wait();
-                    float *dst = wsl + (size_t)c0 * 128 + row;
+                    float *dst = wsl + (size_t)c0 * 128 + row * 4;  // column group c0/4, this row
 #pragma unroll
-                    for (int i = 0; i < 16; i++) dst[i * 128] = __uint_as_float(u16[i]);
+                    for (int j = 0; j < 4; j++)
+                        *reinterpret_cast<uint4 *>(dst + j * 512) =
+                            make_uint4(u16[4 * j], u16[4 * j + 1], u16[4 * j + 2], u16[4 * j + 3]);
                 }
                 // the accumulator is in registers / on its way to the workspace
                 release_acc(acc);
@@ -1029,6 +1102,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             if (!ok) break;
             if (et == 0) GEMM_EVENT(p, 6, 5 * si + 0);
             const EpiRow er = epi_row<EPI>(p.epi, tile, row);
+            const EpiDst dd = epi_dst<EPI>(p.epi, tile);
             const bool staged = nc * kChunkBytes <= kStageBytes;
             const int per_round = staged ? kStageBytes / (nc * kChunkBytes) : 1;
             for (int r0 = ch0; r0 < ch1; r0 += per_round) {
@@ -1051,20 +1125,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int k = 0; k < 16; k++) v[k] = 0.f;
                     for (int c = 0; c < nc; c++) {
+                        float4 t[4];
                         if (staged) {
-                            const float *src = sbuf + ((size_t)c * nr + (ch - r0)) * 2048 + row;
+                            const float4 *src =
+                                reinterpret_cast<const float4 *>(sbuf + ((size_t)c * nr + (ch - r0)) * 2048 + row * 4);
 #pragma unroll
-                            for (int k = 0; k < 16; k++) v[k] += src[k * 128];
+                            for (int j = 0; j < 4; j++) t[j] = src[j * 128];
                         } else {
-                            const float *src = p.ws + s_contrib[c] + (size_t)ch * 2048 + row;
-                            float t[16];
+                            const float4 *src = reinterpret_cast<const float4 *>(p.ws + s_contrib[c] + (size_t)ch * 2048 + row * 4);
 #pragma unroll
-                            for (int k = 0; k < 16; k++) t[k] = __ldcg(src + k * 128);
+                            for (int j = 0; j < 4; j++) t[j] = __ldcg(src + j * 128);
+                        }
 #pragma unroll
-                            for (int k = 0; k < 16; k++) v[k] += t[k];
+                        for (int j = 0; j < 4; j++) {
+                            v[4 * j] += t[j].x;
+                            v[4 * j + 1] += t[j].y;
+                            v[4 * j + 2] += t[j].z;
+                            v[4 * j + 3] += t[j].w;
                         }
                     }
-                    epi_chunk<EPI>(p.epi, er, s_pos, g.m0, ch * 16, g.ntok, v);
+                    epi_values<EPI>(p.epi, er, s_pos, ch * 16, g.ntok, v, my_stage);
+                    named_bar_sync(2 + half, kEpiThreads / 2);
+                    epi_copyout<EPI>(dd, s_pos, g.m0, ch * 16, g.ntok, my_stage, tid_h);
+                    named_bar_sync(2 + half, kEpiThreads / 2);
                 }
                 // staged chunks consumed before the next round's copies; generic reads of the
                 // staging area before the async-proxy writes

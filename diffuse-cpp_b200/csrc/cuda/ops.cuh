@@ -119,22 +119,35 @@ __device__ __forceinline__ float block_sum(float v, float *red) {
     return r;
 }
 
-// h[a] = f16(x[a] * rsqrt(mean(x[a]^2) + eps) * w)  (ggml_rms_norm + ggml_mul, graph.cpp:51-58).
-// One block per row; 8 elements per thread per step (two float4 loads, one 16-byte store).
-__global__ void __launch_bounds__(256) rmsnorm_kernel(const float *__restrict__ x, const float *__restrict__ w, int d,
-                                                      float eps, const int *__restrict__ cnt, __half *__restrict__ h) {
+// h[a] = f16(x[a] * rsqrt(mean(x[a]^2) + eps) * w)  (ggml_rms_norm + ggml_mul, graph.cpp:51-58),
+// with the residual add of the projection before it folded in when y is given:
+// x[a] += y[a] first (ggml_add, graph.cpp:123 / :142), written back as the new residual
+// stream.  One block per row; 8 elements per thread per step (float4 loads, one 16-byte
+// f16 store); each thread re-reads in the second pass only the elements it wrote.
+__global__ void __launch_bounds__(256) rmsnorm_kernel(float *__restrict__ x, const float *__restrict__ y,
+                                                      const float *__restrict__ w, int d, float eps,
+                                                      const int *__restrict__ cnt, __half *__restrict__ h) {
     __shared__ float red[33];
     griddep_launch_dependents();
-    griddep_wait();  // x and the row count come from the previous kernels
+    griddep_wait();  // x, y and the row count come from the previous kernels
     const int a = blockIdx.x;
     if (a >= cnt[CNT_M]) return;
-    const float *xr = x + (size_t)a * d;
+    float *xr = x + (size_t)a * d;
+    const float *yr = y ? y + (size_t)a * d : nullptr;
     __half *hr = h + (size_t)a * d;
     float ss = 0.f;
     if ((d & 7) == 0) {
         for (int i = threadIdx.x * 8; i < d; i += blockDim.x * 8) {
-            const float4 v0 = *reinterpret_cast<const float4 *>(xr + i);
-            const float4 v1 = *reinterpret_cast<const float4 *>(xr + i + 4);
+            float4 v0 = *reinterpret_cast<const float4 *>(xr + i);
+            float4 v1 = *reinterpret_cast<const float4 *>(xr + i + 4);
+            if (yr) {
+                const float4 y0 = *reinterpret_cast<const float4 *>(yr + i);
+                const float4 y1 = *reinterpret_cast<const float4 *>(yr + i + 4);
+                v0.x += y0.x; v0.y += y0.y; v0.z += y0.z; v0.w += y0.w;
+                v1.x += y1.x; v1.y += y1.y; v1.z += y1.z; v1.w += y1.w;
+                *reinterpret_cast<float4 *>(xr + i) = v0;
+                *reinterpret_cast<float4 *>(xr + i + 4) = v1;
+            }
             ss += v0.x * v0.x + v0.y * v0.y + v0.z * v0.z + v0.w * v0.w;
             ss += v1.x * v1.x + v1.y * v1.y + v1.z * v1.z + v1.w * v1.w;
         }
@@ -153,7 +166,14 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const float *__restrict__ 
             *reinterpret_cast<uint4 *>(hr + i) = o;
         }
     } else {
-        for (int i = threadIdx.x; i < d; i += blockDim.x) ss += xr[i] * xr[i];
+        for (int i = threadIdx.x; i < d; i += blockDim.x) {
+            float v = xr[i];
+            if (yr) {
+                v += yr[i];
+                xr[i] = v;
+            }
+            ss += v * v;
+        }
         ss = block_sum(ss, red);
         const float scale = 1.0f / sqrtf(ss / (float)d + eps);
         for (int i = threadIdx.x; i < d; i += blockDim.x) hr[i] = __float2half_rn((xr[i] * scale) * w[i]);
