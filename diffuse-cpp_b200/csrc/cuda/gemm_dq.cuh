@@ -752,17 +752,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         __syncwarp();
     } else if (role == R_MMA) {
         // ── MMA issuer (even CTA) ──
+        // Every instruction on this thread's path between two slices leaves the tensor
+        // pipe idle (the queue holds about one MMA), so the per-slice work is only: wait
+        // for the stage, fence, four MMAs, commit.  Each unit is one k-block = four
+        // slices, so the A stage of slice s2 is s2 (a_stages == 4) and its barrier parity
+        // flips per k-block; the four B descriptors are computed once per k-block.
+        static_assert(NA == 4, "one A stage per k-slice of a k-block");
         if (lane == 0 && rank == 0) {
-            int ia = 0, si = 0;  // A stages consumed, accumulator segments
+            int si = 0, ka = 0;  // accumulator segments, k-blocks consumed
             bool ok = true, issued = false;
-#ifdef DFB_GEMM_TRACE
-            long long tm_wa = 0, tm_wb = 0, tm_mma = 0, tm_cm = 0, tm_loop = 0, tm_last = 0, tm_each[4] = {0, 0, 0, 0};
-#endif
             const uint64_t bdesc0 = sw128_desc(smem_u32(bring)), adesc0 = sw128_desc(smem_u32(aring));
-            const int spb = S.spb;
-            const uint32_t bstep_part = S.bh * 128, bstep_slot = S.bslot - (spb - 1) * S.bh * 128;
-            int bsl = 0, bpart = 0;
-            uint32_t boff = 0;
+            const int lg_spb = S.spb == 1 ? 0 : S.spb == 2 ? 1 : 2;  // B slices per ring slot: 1, 2 or 4
+            const uint32_t bpart_bytes = S.bh * 128;
+            int bslot = 0;  // ring slot of the first slice of the next k-block
             for (int u = S.u0; u < S.u1 && ok;) {
                 const Seg g = make_seg(S, u, S.u1);
                 const int acc = S.acc_of(si);
@@ -771,61 +773,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 const uint32_t d_tmem = tmem_base + acc * kDblTok;
                 const uint32_t idesc = idesc_f16(256, (uint32_t)g.nmma);
                 uint32_t accum = 0;
-                for (int kbi = g.k0; kbi < g.k1 && ok; kbi++) {
-                    for (int s2 = 0; s2 < 4; s2++) {  // A stages (k-slices) of this k-block
-                        const int st = ia % NA;
-#ifdef DFB_GEMM_TRACE
-                        const long long c0 = clock64();
-#endif
-                        // full_a also carries the relays' arrivals: this stage's B rows have landed
-                        if (!(ok = mbar_wait(&full_a[st], (ia / NA) & 1, abort_flag, p.err, kErrTimeout + 5))) break;
-#ifdef DFB_GEMM_TRACE
-                        const long long c1 = clock64();
-#endif
-                        tc_fence_after();
-#ifdef DFB_GEMM_TRACE
-                        const long long c2 = clock64();
-#endif
-                        // this slice's B rows: descriptor of the ring base + running byte offset
-                        // (no divisions on the issuer's path: its scheduler is shared with
-                        // dequantizers, and each instruction costs several cycles there)
-                        const uint64_t bdesc = bdesc0 + (uint64_t)(boff >> 4);
-                        if constexpr (WT == W_F16)
-                            mma2_f16_ss_k64(d_tmem, adesc0 + (uint64_t)((st * kABytes) >> 4), bdesc, idesc, accum);
-                        else {
-                            const uint32_t a_tmem = tmem_base + kTmemA + st * kTmemAStage;
-#ifdef DFB_GEMM_TRACE
-                            long long tt[5];
-                            mma2_f16_ts_k64_timed(d_tmem, a_tmem, bdesc, idesc, accum, tt);
-                            for (int q5 = 0; q5 < 4; q5++) tm_each[q5] += tt[q5 + 1] - tt[q5];
-#else
-                            mma2_f16_ts_k64(d_tmem, a_tmem, bdesc, idesc, accum);
-#endif
-                        }
-                        accum = 1;
-                        // next slice's B position: part of the slot, then the next slot
-                        if (++bpart == spb) {
-                            bpart = 0;
-                            if (++bsl == NBS) { bsl = 0; boff = 0; }
-                            else boff += bstep_slot;
-                        } else {
-                            boff += bstep_part;
-                        }
-#ifdef DFB_GEMM_TRACE
-                        const long long c3 = clock64();
-#endif
-                        issued = true;
-                        mma2_commit_mc(&empty_a[st], 0x3);
-#ifdef DFB_GEMM_TRACE
-                        const long long c4 = clock64();
-                        tm_wa += c1 - c0; tm_wb += c2 - c1; tm_mma += c3 - c2; tm_cm += c4 - c3;
-                        if (ia > 0) tm_loop += c0 - tm_last;
-                        tm_last = c4;
-#endif
-                        GEMM_EVENT(p, 5, ia);
-                        if (ia < 64) GEMM_EVENT(p, 4, ia);
-                        ia++;
+                for (int kbi = g.k0; kbi < g.k1; kbi++, ka++) {
+                    uint64_t bd[4];
+#pragma unroll
+                    for (int s2 = 0; s2 < 4; s2++) {
+                        int sl = bslot + (s2 >> lg_spb);
+                        if (sl >= NBS) sl -= NBS;
+                        bd[s2] = bdesc0 + (uint64_t)((sl * S.bslot + (s2 & (S.spb - 1)) * bpart_bytes) >> 4);
                     }
+                    bslot += 4 >> lg_spb;
+                    if (bslot >= NBS) bslot -= NBS;
+                    const uint32_t par = ka & 1;
+#pragma unroll
+                    for (int s2 = 0; s2 < 4; s2++) {
+                        // full_a also carries the relays' arrivals: this stage's B rows have landed
+                        if (!(ok = mbar_wait(&full_a[s2], par, abort_flag, p.err, kErrTimeout + 5))) break;
+                        tc_fence_after();
+                        if constexpr (WT == W_F16)
+                            mma2_f16_ss_k64(d_tmem, adesc0 + (uint64_t)((s2 * kABytes) >> 4), bd[s2], idesc, accum);
+                        else
+                            mma2_f16_ts_k64(d_tmem, tmem_base + kTmemA + s2 * kTmemAStage, bd[s2], idesc, accum);
+                        accum = 1;
+                        mma2_commit_mc(&empty_a[s2], 0x3);
+                        GEMM_EVENT(p, 4, 4 * ka + s2);
+                    }
+                    issued = true;
+                    if (!ok) break;
                 }
                 if (!ok) break;
                 mma2_commit_mc(&acc_full[acc], 0x3);
@@ -833,14 +806,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 u += g.k1 - g.k0;
             }
             GEMM_STAMP(p, 3);
-#ifdef DFB_GEMM_TRACE
-            if (p.trace && blockIdx.x < 4) {
-                unsigned long long *tp = p.trace + 256 * 16 + ((size_t)blockIdx.x * 8 + 5) * 64 + 56;
-                tp[0] = tm_wa; tp[1] = tm_wb; tp[2] = tm_mma; tp[3] = tm_cm; tp[4] = tm_loop; tp[5] = ia;
-                unsigned long long *te = p.trace + 256 * 16 + ((size_t)blockIdx.x * 8 + 4) * 64 + 56;
-                for (int q5 = 0; q5 < 4; q5++) te[q5] = tm_each[q5];
-            }
-#endif
             if (issued) {
                 // every MMA must have retired before TMEM is released
                 mma2_commit(drain);

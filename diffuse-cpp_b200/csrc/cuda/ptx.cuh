@@ -116,7 +116,6 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
-// Make generic-proxy shared-memory writes visible to the async proxy (tensor core).
 // Generic-proxy accesses (global and shared) before later async-proxy (bulk copy) ones.
 __device__ __forceinline__ void fence_proxy_async_all() { asm volatile("fence.proxy.async;" ::: "memory"); }
 __device__ __forceinline__ int ld_acquire_gpu(const int *p) {
@@ -144,6 +143,7 @@ __device__ __forceinline__ bool wait_count(const int *c, int target, volatile in
         __nanosleep(32);
     }
 }
+// Make generic-proxy shared-memory writes visible to the async proxy (tensor core).
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -272,30 +272,6 @@ __device__ __forceinline__ void mma2_f16_ts_k64(uint32_t d_tmem, uint32_t a_tmem
         "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
-#ifdef DFB_GEMM_TRACE
-// Analysis builds: the same four MMAs with a clock read before each and after the last.
-__device__ __forceinline__ void mma2_f16_ts_k64_timed(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
-                                                      uint32_t accumulate, long long (&t)[5]) {
-    asm volatile(
-        "{\n\t.reg .pred p0, p1;\n\t.reg .b32 a1, a2, a3;\n\t.reg .b64 b1, b2, b3;\n\t"
-        "setp.ne.b32 p0, %9, 0;\n\t"
-        "setp.eq.b32 p1, %9, %9;\n\t"
-        "add.u32 a1, %6, 8;\n\tadd.u32 a2, %6, 16;\n\tadd.u32 a3, %6, 24;\n\t"
-        "add.u64 b1, %7, 2;\n\tadd.u64 b2, %7, 4;\n\tadd.u64 b3, %7, 6;\n\t"
-        "mov.u64 %0, %%clock64;\n\t"
-        "tcgen05.mma.cta_group::2.kind::f16 [%5], [%6], %7, %8, p0;\n\t"
-        "mov.u64 %1, %%clock64;\n\t"
-        "tcgen05.mma.cta_group::2.kind::f16 [%5], [a1], b1, %8, p1;\n\t"
-        "mov.u64 %2, %%clock64;\n\t"
-        "tcgen05.mma.cta_group::2.kind::f16 [%5], [a2], b2, %8, p1;\n\t"
-        "mov.u64 %3, %%clock64;\n\t"
-        "tcgen05.mma.cta_group::2.kind::f16 [%5], [a3], b3, %8, p1;\n\t"
-        "mov.u64 %4, %%clock64;\n\t}"
-        : "=l"(t[0]), "=l"(t[1]), "=l"(t[2]), "=l"(t[3]), "=l"(t[4])
-        : "r"(d_tmem), "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-#endif
 // Same with A from shared memory (descriptor advanced by 32 bytes per step).
 __device__ __forceinline__ void mma2_f16_ss_k64(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                                 uint32_t accumulate) {
