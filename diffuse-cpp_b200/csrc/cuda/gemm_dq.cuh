@@ -36,12 +36,17 @@ namespace dfb {
     do {                                                                                         \
         if ((p).trace) (p).trace[(size_t)blockIdx.x * 16 + (slot)] = globaltimer();              \
     } while (0)
-// Event streams of CTAs 0..3: stream s, event i -> trace[256*16 + (cta*8 + s)*64 + i].
+// Event streams of CTAs 0..3 (also -DDFB_GEMM_EVENTS, which perturbs the timing it records):
+// stream s, event i -> trace[256*16 + (cta*8 + s)*64 + i].
+#ifdef DFB_GEMM_EVENTS
 #define GEMM_EVENT(p, stream, idx)                                                               \
     do {                                                                                         \
         if ((p).trace && blockIdx.x < 4 && (idx) < 64)                                           \
             (p).trace[256 * 16 + ((size_t)blockIdx.x * 8 + (stream)) * 64 + (idx)] = globaltimer(); \
     } while (0)
+#else
+#define GEMM_EVENT(p, stream, idx) do {} while (0)
+#endif
 #else
 #define GEMM_STAMP(p, slot) do {} while (0)
 #define GEMM_EVENT(p, stream, idx) do {} while (0)
@@ -642,29 +647,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         tmem_alloc2(tmem_holder, 512);
         tmem_relinquish2();
     }
-    if (WT != W_F16 && role == R_WPROD && lane == 0) {
-        // Weights do not depend on the previous kernel: warm L2 with this pair's first
-        // chunks before waiting for it (the token count read here may still change, which
-        // only makes the hint less useful).
-        Sched S0;
-        S0.init(*reinterpret_cast<volatile const int *>(p.m_dev), p.n_tiles >> 1, p.kb, n_pairs, pair, BRING);
-        for (int u = S0.u0; u < S0.u1 && u < S0.u0 + NRAW * CPR; u++) {
-            const int ot = u / S0.kb, kbi = u % S0.kb;
-            bulk_prefetch_l2(p.w + ((size_t)(2 * (ot / S0.n_mg) + rank) * p.kb + kbi) * RAWB, RAWB);
-        }
-    }
     tc_fence_before();
     __syncthreads();
     cluster_sync();  // barriers of both CTAs initialised, TMEM of both allocated
     tc_fence_after();
     const uint32_t tmem_base = *tmem_holder;
-    // everything below may read what the previous kernel wrote
-    griddep_wait();
-    const int M = *p.m_dev;
+    // The schedule needs only the token count, which is final before any GEMM of a
+    // forward starts (the step-preparation kernel or the host writes it ahead of the
+    // forward's first launch), and the weights do not depend on the previous kernel.  So
+    // the weight producer and the dequantizers start now and fill the pipeline while the
+    // previous kernel finishes; the activation producer and the epilogue wait for it
+    // (griddepcontrol.wait) before they read or write anything it touches, and the MMAs
+    // wait for the activations.
+    const int M = *reinterpret_cast<volatile const int *>(p.m_dev);
     Sched S;
     S.init(M, p.n_tiles >> 1, p.kb, n_pairs, pair, BRING);
     const int NBS = S.nbs;
-    if (threadIdx.x == 0) GEMM_STAMP(p, 1);
     // barriers of the even CTA as cluster addresses
     const uint32_t full_a0 = mapa_shared(full_a, 0), acc_empty0 = mapa_shared(acc_empty, 0);
 
@@ -672,7 +670,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         // ── activation producer (both CTAs, local barriers): this CTA's half of the
         //    token group, spb k-slices per tensor load.  Few large loads: the TMA unit
         //    also streams the weights and handles only a few operations per microsecond. ──
+        griddep_wait();  // the activations are the previous kernel's output
         if (lane == 0) {
+            GEMM_STAMP(p, 1);
+            if (*reinterpret_cast<volatile const int *>(p.m_dev) != M) atomicCAS(p.err, 0, kErrTimeout + 14);
             const CUtensorMap *xmap = &xm.m[S.bh / 16 - 1];
             int ob = 0, sl = 0;  // B loads issued, slot of the next one
             uint32_t ph = 0;     // ring pass parity of the next load
@@ -761,6 +762,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         if (lane == 0 && rank == 0) {
             int si = 0, ka = 0;  // accumulator segments, k-blocks consumed
             bool ok = true, issued = false;
+#ifdef DFB_GEMM_TRACE
+            long long tr_nwait = 0, tr_wcyc = 0, tr_t0 = clock64();
+#endif
             const uint64_t bdesc0 = sw128_desc(smem_u32(bring)), adesc0 = sw128_desc(smem_u32(aring));
             const int lg_spb = S.spb == 1 ? 0 : S.spb == 2 ? 1 : 2;  // B slices per ring slot: 1, 2 or 4
             const uint32_t bpart_bytes = S.bh * 128;
@@ -787,7 +791,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int s2 = 0; s2 < 4; s2++) {
                         // full_a also carries the relays' arrivals: this stage's B rows have landed
+#ifdef DFB_GEMM_TRACE
+                        if (!mbar_try_wait(&full_a[s2], par)) {
+                            const long long w0 = clock64();
+                            ok = mbar_wait(&full_a[s2], par, abort_flag, p.err, kErrTimeout + 5);
+                            tr_nwait++;
+                            tr_wcyc += clock64() - w0;
+                        }
+                        if (!ok) break;
+#else
                         if (!(ok = mbar_wait(&full_a[s2], par, abort_flag, p.err, kErrTimeout + 5))) break;
+#endif
                         tc_fence_after();
                         if constexpr (WT == W_F16)
                             mma2_f16_ss_k64(d_tmem, adesc0 + (uint64_t)((s2 * kABytes) >> 4), bd[s2], idesc, accum);
@@ -806,6 +820,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 u += g.k1 - g.k0;
             }
             GEMM_STAMP(p, 3);
+#ifdef DFB_GEMM_TRACE
+            if (p.trace && blockIdx.x < 4) {  // full_a waits that had to block: count, cycles; loop cycles; slices
+                unsigned long long *tp = p.trace + 256 * 16 + ((size_t)blockIdx.x * 8 + 5) * 64 + 56;
+                tp[0] = tr_nwait; tp[1] = tr_wcyc; tp[2] = clock64() - tr_t0; tp[3] = 4 * ka;
+            }
+#endif
             if (issued) {
                 // every MMA must have retired before TMEM is released
                 mma2_commit(drain);
@@ -948,6 +968,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
     } else {
         // ── epilogue: thread = TMEM lane = output feature of this CTA's tile ──
+        griddep_wait();  // outputs, workspace and counters are the previous kernel's until it completes
         // A whole tile is finished straight from TMEM.  A split tile's partial goes to
         // the workspace (f32 [column / 4][row][column % 4], slot 0 for the pair's first
         // tile, 1 for its last) and its arrival is counted; once every MMA of this CTA is done, each
