@@ -8,8 +8,11 @@
 // kernel.  GQA: query head h reads kv head h / n_rep, as ggml_repeat's grouped layout
 // does (graph.cpp:84-95).  RoPE was applied when K and Q were produced.
 //
-// One CTA = 4 warps = 64 query rows of one head; keys stream through shared memory in
-// tiles of 64 (cp.async double buffer); online softmax in f32 registers.
+// One CTA = 64 query rows of one head, two groups of 4 warps: group g takes the key tiles
+// t = g (mod 2) of 64 keys (its own cp.async double buffer) with an online softmax in f32
+// registers; at the end group 1 hands its running max, sum and output rows to group 0
+// through shared memory, which merges them (the log-sum-exp combination of two softmax
+// partials) and writes the rows.  Two groups double the warps per SM at the same grid.
 #pragma once
 #include <cuda_fp16.h>
 #include <cstdint>
@@ -53,8 +56,10 @@ __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
 }
 
 // q: [M][ld_q] (head h at h*HD), kc/vc: [n_keys][ld_kv] (kv head at kvh*HD), o: [M][ld_o].
+constexpr int kAttnThreads = 256;
+
 template <int HD>
-__global__ void __launch_bounds__(128) attn_kernel(const __half *__restrict__ q, int ld_q,
+__global__ void __launch_bounds__(kAttnThreads) attn_kernel(const __half *__restrict__ q, int ld_q,
                                                    const __half *__restrict__ kc, const __half *__restrict__ vc,
                                                    int ld_kv, __half *__restrict__ o, int ld_o,
                                                    const int *__restrict__ m_dev, int n_keys, int n_rep,
@@ -63,8 +68,9 @@ __global__ void __launch_bounds__(128) attn_kernel(const __half *__restrict__ q,
     constexpr int KT = HD / 16;           // k-steps for Q K^T
     constexpr int DT = HD / 8;            // n-tiles of the output
     extern __shared__ __align__(128) uint8_t att_smem[];
-    uint8_t *Ks = att_smem;                               // [2][64][HD]
-    uint8_t *Vs = att_smem + 2 * kAttnKeys * HD * 2;      // [2][64][HD]
+    const int grp = threadIdx.x >> 7, gtid = threadIdx.x & 127;
+    uint8_t *Ks = att_smem + grp * 4 * kAttnKeys * HD * 2;  // this group's [2][64][HD]
+    uint8_t *Vs = Ks + 2 * kAttnKeys * HD * 2;              // [2][64][HD]
 
     griddep_launch_dependents();
     griddep_wait();  // q and the K/V cache come from the previous kernels
@@ -72,7 +78,7 @@ __global__ void __launch_bounds__(128) attn_kernel(const __half *__restrict__ q,
     const int q0 = blockIdx.x * kAttnRows;
     if (q0 >= M) return;
     const int h = blockIdx.y, kvh = h / n_rep;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int warp = (threadIdx.x >> 5) & 3, lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3;
     const int r0 = q0 + warp * 16 + g, r1 = r0 + 8;
 
@@ -95,7 +101,7 @@ __global__ void __launch_bounds__(128) attn_kernel(const __half *__restrict__ q,
     auto load_tile = [&](int tile, int buf) {
         const int k0 = tile * kAttnKeys;
         uint8_t *kd = Ks + buf * kAttnKeys * HD * 2, *vd = Vs + buf * kAttnKeys * HD * 2;
-        for (int idx = threadIdx.x; idx < kAttnKeys * NCH; idx += 128) {
+        for (int idx = gtid; idx < kAttnKeys * NCH; idx += 128) {
             const int row = idx / NCH, ch = idx % NCH;
             const int key = k0 + row;
             const bool valid = key < n_keys;
@@ -112,16 +118,16 @@ __global__ void __launch_bounds__(128) attn_kernel(const __half *__restrict__ q,
     float m_0 = -INFINITY, m_1 = -INFINITY, l_0 = 0.f, l_1 = 0.f;
 
     const int n_tiles = (n_keys + kAttnKeys - 1) / kAttnKeys;
-    load_tile(0, 0);
-    for (int tile = 0; tile < n_tiles; tile++) {
-        const int buf = tile & 1;
-        if (tile + 1 < n_tiles) {
-            load_tile(tile + 1, buf ^ 1);
+    if (grp < n_tiles) load_tile(grp, 0);
+    for (int tile = grp, it = 0; tile < n_tiles; tile += 2, it++) {
+        const int buf = it & 1;
+        if (tile + 2 < n_tiles) {
+            load_tile(tile + 2, buf ^ 1);
             cp_async_wait<1>();
         } else {
             cp_async_wait<0>();
         }
-        __syncthreads();
+        named_bar_sync(1 + grp, 128);
         const uint8_t *kb = Ks + buf * kAttnKeys * HD * 2;
         const uint8_t *vb = Vs + buf * kAttnKeys * HD * 2;
 
@@ -199,7 +205,38 @@ __global__ void __launch_bounds__(128) attn_kernel(const __half *__restrict__ q,
                 mma16816(acc[dt + 1], pa, b2, b3);
             }
         }
-        __syncthreads();
+        named_bar_sync(1 + grp, 128);
+    }
+    // merge group 1 into group 0: per thread, the same rows and columns in both groups
+    __syncthreads();  // both groups are done with their tiles; reuse the tile buffers
+    float *xch = reinterpret_cast<float *>(att_smem);  // [DT*4 + 4][128]
+    if (grp == 1) {
+#pragma unroll
+        for (int i = 0; i < DT; i++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) xch[(i * 4 + e) * 128 + gtid] = acc[i][e];
+        xch[(DT * 4 + 0) * 128 + gtid] = m_0;
+        xch[(DT * 4 + 1) * 128 + gtid] = m_1;
+        xch[(DT * 4 + 2) * 128 + gtid] = l_0;
+        xch[(DT * 4 + 3) * 128 + gtid] = l_1;
+    }
+    __syncthreads();
+    if (grp == 1) return;
+    {
+        const float bm0 = xch[(DT * 4 + 0) * 128 + gtid], bm1 = xch[(DT * 4 + 1) * 128 + gtid];
+        const float nm0 = fmaxf(m_0, bm0), nm1 = fmaxf(m_1, bm1);
+        // a group without tiles has max -inf and contributes nothing
+        const float ca0 = m_0 == -INFINITY ? 0.f : exp2f(m_0 - nm0), cb0 = bm0 == -INFINITY ? 0.f : exp2f(bm0 - nm0);
+        const float ca1 = m_1 == -INFINITY ? 0.f : exp2f(m_1 - nm1), cb1 = bm1 == -INFINITY ? 0.f : exp2f(bm1 - nm1);
+        l_0 = l_0 * ca0 + xch[(DT * 4 + 2) * 128 + gtid] * cb0;
+        l_1 = l_1 * ca1 + xch[(DT * 4 + 3) * 128 + gtid] * cb1;
+#pragma unroll
+        for (int i = 0; i < DT; i++) {
+            acc[i][0] = acc[i][0] * ca0 + xch[(i * 4 + 0) * 128 + gtid] * cb0;
+            acc[i][1] = acc[i][1] * ca0 + xch[(i * 4 + 1) * 128 + gtid] * cb0;
+            acc[i][2] = acc[i][2] * ca1 + xch[(i * 4 + 2) * 128 + gtid] * cb1;
+            acc[i][3] = acc[i][3] * ca1 + xch[(i * 4 + 3) * 128 + gtid] * cb1;
+        }
     }
     l_0 += __shfl_xor_sync(0xffffffffu, l_0, 1);
     l_0 += __shfl_xor_sync(0xffffffffu, l_0, 2);
@@ -216,7 +253,9 @@ __global__ void __launch_bounds__(128) attn_kernel(const __half *__restrict__ q,
 
 template <int HD>
 constexpr int attn_smem_bytes() {
-    return 4 * kAttnKeys * HD * 2;
+    // two groups x double-buffered K and V tiles (the merge reuses the first group's)
+    return 2 * 4 * kAttnKeys * HD * 2;
 }
+static_assert(attn_smem_bytes<16>() >= (16 / 8 * 4 + 4) * 128 * 4, "merge buffer fits in the tile buffers");
 
 }  // namespace dfb

@@ -794,7 +794,7 @@ static int launch_attn_t(dfb_ctx *c, const __half *kc, const __half *vc, int n_k
     dim3 grid((c->cap + kAttnRows - 1) / kAttnRows, m->hp.n_head);
     cudaEvent_t ev0 = nullptr;
     prof_begin(c, &ev0);
-    CK(launch_k(attn_kernel<HD>, grid, dim3(128), smem, c->st, !c->prof, (const __half *)c->q, m->n_q, kc, vc, m->n_kv,
+    CK(launch_k(attn_kernel<HD>, grid, dim3(kAttnThreads), smem, c->st, !c->prof, (const __half *)c->q, m->n_q, kc, vc, m->n_kv,
                 c->att, m->n_q, (const int *)(c->cnt + CNT_M), n_keys, m->hp.n_head / m->hp.n_head_kv, scale_log2));
     prof_end(c, ev0, DFB_PROF_ATTN, 4.0 * n_keys * m->hp.n_head * HD, 2.0 * 2.0 * n_keys * m->n_kv, 4.0 * m->n_q);
     return DFB_OK;
