@@ -850,13 +850,36 @@ static int run_forward(dfb_ctx *c, int n_total) {
     return DFB_OK;
 }
 
+// What a GEMM error code (the first code any CTA raised) means: which bounded wait gave up,
+// or which consistency check failed.
+static const char *gemm_err_str(int code) {
+    switch (code - kErrTimeout) {
+        case 1: return "weight producer waited for a free weight stage";
+        case 2: return "activation producer waited for a free activation slot";
+        case 3: return "MMA issuer waited for a drained accumulator";
+        case 4: return "relay waited for activations to land";
+        case 5: return "MMA issuer waited for a dequantized A stage";
+        case 6: return "dequantizer waited for a weight chunk to land";
+        case 7: return "dequantizer waited for a free A stage";
+        case 8: return "epilogue waited for a finished accumulator";
+        case 9: return "a split tile has more contributors than tracked";
+        case 10: return "epilogue waited for staged partial sums";
+        case 11: return "F16 weight producer waited for a free A stage";
+        case 12: return "relay waited for an MMA to release its stage";
+        case 13: return "split-tile contributor waited for the other contributors' partial sums";
+        case 14: return "token count changed between the launch and the grid-dependency wait";
+        default: return "unknown";
+    }
+}
+
 static int check_err(dfb_ctx *c) {
     int e = 0;
     CK(cudaMemcpy(&e, c->err, sizeof(int), cudaMemcpyDeviceToHost));
     if (e) {
         cudaMemset(c->err, 0, sizeof(int));
         cudaMemset(c->tile_cnt, 0, sizeof(int) * c->n_tile_cnt);  // an aborted launch can leave counts behind
-        return set_err(DFB_ERR_TIMEOUT, "a GEMM gave up a bounded wait (code 0x%x); results of this call are invalid", e);
+        return set_err(DFB_ERR_TIMEOUT, "a GEMM stopped (code 0x%x: %s); results of this call are invalid", e,
+                       gemm_err_str(e));
     }
     return DFB_OK;
 }
@@ -1221,6 +1244,6 @@ extern "C" int dfb_linear_noalloc(const dfb_model *m, int role, int layer, const
     CK(cudaStreamSynchronize(st));
     int err = 0;
     CK(cudaMemcpy(&err, nd.cnt + kCntM + 1, sizeof(int), cudaMemcpyDeviceToHost));
-    if (err) return set_err(DFB_ERR_TIMEOUT, "a GEMM gave up a bounded wait (code 0x%x)", err);
+    if (err) return set_err(DFB_ERR_TIMEOUT, "a GEMM stopped (code 0x%x: %s)", err, gemm_err_str(err));
     return DFB_OK;
 }
