@@ -50,6 +50,13 @@ __device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t &r0, uint3
                  : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
                  : "r"(addr));
 }
+// Four 8x8 b16 matrices, not transposed: lane l addresses row l % 8 of matrix l / 8 and
+// receives, of each matrix, row l / 4, elements 2 (l % 4) and 2 (l % 4) + 1.
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
 __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
     __half2 h = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<uint32_t *>(&h);
@@ -136,14 +143,27 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const __half *__rest
 #pragma unroll
         for (int nt = 0; nt < 8; nt++) {
             s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
-            const int krow = nt * 8 + g;
+            if constexpr (KT % 2 == 0) {
+                // B fragments of two k-steps per ldmatrix: matrices = (keys nt*8..+7) x
+                // (16-byte chunks 2kk, 2kk+1, 2kk+2, 2kk+3) of the K rows
+                const uint32_t kaddr = static_cast<uint32_t>(__cvta_generic_to_shared(kb));
 #pragma unroll
-            for (int kk = 0; kk < KT; kk++) {
-                const int col = 16 * kk + 2 * t;
-                const uint32_t b0 = *reinterpret_cast<const uint32_t *>(kb + attn_swz<HD>(krow, col >> 3) + (col & 7) * 2);
-                const uint32_t b1 =
-                    *reinterpret_cast<const uint32_t *>(kb + attn_swz<HD>(krow, (col + 8) >> 3) + (col & 7) * 2);
-                mma16816(s[nt], qa[kk], b0, b1);
+                for (int kk = 0; kk < KT; kk += 2) {
+                    uint32_t b0, b1, b2, b3;
+                    ldsm_x4(kaddr + attn_swz<HD>(nt * 8 + (lane & 7), 2 * kk + (lane >> 3)), b0, b1, b2, b3);
+                    mma16816(s[nt], qa[kk], b0, b1);
+                    mma16816(s[nt], qa[kk + 1], b2, b3);
+                }
+            } else {
+                const int krow = nt * 8 + g;
+#pragma unroll
+                for (int kk = 0; kk < KT; kk++) {
+                    const int col = 16 * kk + 2 * t;
+                    const uint32_t b0 = *reinterpret_cast<const uint32_t *>(kb + attn_swz<HD>(krow, col >> 3) + (col & 7) * 2);
+                    const uint32_t b1 =
+                        *reinterpret_cast<const uint32_t *>(kb + attn_swz<HD>(krow, (col + 8) >> 3) + (col & 7) * 2);
+                    mma16816(s[nt], qa[kk], b0, b1);
+                }
             }
         }
         // mask keys past the end, row max
