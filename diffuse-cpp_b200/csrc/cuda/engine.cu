@@ -872,6 +872,16 @@ static const char *gemm_err_str(int code) {
     }
 }
 
+// One entry point's GPU work at a time per device.  A dequant GEMM launch relies on all of
+// its CTAs being resident together (split-tile contributors wait for each other), which
+// holds when its launches follow each other in one stream, but not when two host threads
+// interleave GEMM launches of two contexts on one device (both launches could end up
+// partly resident and stall until their bounded waits fail).  Every entry point below that
+// launches a GEMM synchronizes its stream before returning, so holding this lock for the
+// call serializes the GEMMs of all contexts of the device.
+static std::mutex g_device_mu[64];
+static std::mutex &device_lock(int device) { return g_device_mu[device & 63]; }
+
 static int check_err(dfb_ctx *c) {
     int e = 0;
     CK(cudaMemcpy(&e, c->err, sizeof(int), cudaMemcpyDeviceToHost));
@@ -939,6 +949,7 @@ extern "C" int dfb_ctx_stream(dfb_ctx *c, void **stream) {
 
 extern "C" int dfb_forward(dfb_ctx *c, const int32_t *tokens, int n, float *logits_host) {
     if (!c || !tokens || !logits_host || n <= 0) return set_err(DFB_ERR_ARG, "bad arguments");
+    std::lock_guard<std::mutex> lk(device_lock(c->m->device));
     CK(cudaSetDevice(c->m->device));
     const int V = c->m->hp.n_vocab;
     for (int i = 0; i < n; i++)
@@ -960,6 +971,7 @@ extern "C" int dfb_forward(dfb_ctx *c, const int32_t *tokens, int n, float *logi
 extern "C" int dfb_linear(dfb_ctx *c, int role, int layer, const float *x_host, int M, float *y_host) {
     if (!c || !x_host || !y_host || M <= 0) return set_err(DFB_ERR_ARG, "bad arguments");
     const dfb_model *m = c->m;
+    std::lock_guard<std::mutex> lk(device_lock(m->device));
     CK(cudaSetDevice(m->device));
     const WMat *w = nullptr;
     int K = 0, n_out = 0;
@@ -1058,6 +1070,7 @@ extern "C" int dfb_gen_step(dfb_ctx *c, int step, int n_unmask_sched, int force_
     if (!c) return set_err(DFB_ERR_ARG, "null context");
     if (!c->gen_active) return set_err(DFB_ERR_STATE, "dfb_gen_begin not called");
     const dfb_model *m = c->m;
+    std::lock_guard<std::mutex> lk(device_lock(m->device));
     CK(cudaSetDevice(m->device));
     if (c->sp.remasking == 1) {
         if (!order) return set_err(DFB_ERR_ARG, "RANDOM remasking needs the host shuffle order");
@@ -1211,6 +1224,7 @@ extern "C" int dfb_linear_noalloc(const dfb_model *m, int role, int layer, const
         return set_err(DFB_ERR_ARG, "weight has %d output tiles, the fixed scratch holds %d", w->n_tiles, kNoallocMaxTiles);
     XMaps xm;  // host-side descriptors of the caller's matrix (no device memory)
     RET(make_xmaps(&xm, x_f16_dev, K, M));
+    std::lock_guard<std::mutex> lk(device_lock(m->device));
     CK(cudaSetDevice(m->device));
     NoallocDev nd;
     {

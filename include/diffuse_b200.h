@@ -11,7 +11,10 @@
  * DFB_ERR_* code and leaves a message for dfb_last_error() (thread-local).  The
  * library never exits the process.  Objects are single-threaded: one host thread
  * drives a dfb_ctx at a time; a dfb_model may be shared by several contexts on the
- * same device.
+ * same device.  Calls that run the GEMM (dfb_forward, dfb_linear, dfb_gen_step,
+ * dfb_linear_noalloc) hold a per-device lock until their work has finished: contexts of
+ * one device driven from several host threads take turns, call by call (a GEMM launch
+ * needs all of its CTAs resident at once, which two interleaved launches could deny).
  */
 #ifndef DIFFUSE_B200_H
 #define DIFFUSE_B200_H
