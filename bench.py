@@ -71,6 +71,11 @@ CONFIGS = {
                desc="LLaDA-8B Q4_K_M random-init, prompt 64, block 256, 16 steps, entropy_exit tau=0, cache on"),
     "c1": dict(arch="llada", scheme="q4_k_m", prompt=16, block=64, steps=16, remasking=0, tau=1.5, cache=0,
                desc="LLaDA-8B Q4_K_M random-init, prompt 16, block 64, 16 steps, low_confidence, no cache"),
+    # 64 independent sequences sharded over the ranks (dp.shard); one bench step generates all of
+    # this rank's sequences, one after another on its GPU
+    "c4": dict(arch="llada", scheme="q8_0", prompt=512, block=256, steps=16, remasking=2, tau=0.0, cache=1, n_seq=64,
+               desc="LLaDA-8B Q8_0 random-init, 64 sequences x (prompt 512, block 256), 16 steps, entropy_exit tau=0, "
+                    "cache on, sequences sharded over the ranks"),
     "c3": dict(arch="dream", scheme="q4_k_m", prompt=128, block=64, steps=16, remasking=2, tau=1.5, cache=1,
                desc="Dream-7B Q4_K_M random-init, prompt 128, block 64, 16 steps, entropy_exit tau=1.5, cache on"),
 }
@@ -310,21 +315,28 @@ def main():
     params = pkg.SamplerParams(n_steps=cfg["steps"], remasking=cfg["remasking"], entropy_threshold=cfg["tau"],
                                use_cache=cfg["cache"])
     rng = np.random.default_rng(1234 + rank)
-    prompts = [rng.integers(0, min(hp.mask_token_id, hp.n_vocab) - 1, P).astype(np.int32)
+    # sequences of one bench step on this rank: one (configs 1-3) or this rank's share of n_seq
+    my_seq = pkg.dp.shard(cfg["n_seq"], rank, world) if cfg.get("n_seq") else range(1)
+    n_seq_total = cfg.get("n_seq", world)
+    prompts = [[rng.integers(0, min(hp.mask_token_id, hp.n_vocab) - 1, P).astype(np.int32) for _ in my_seq]
                for _ in range(args.warmup + args.steps)]
 
     for i in range(args.warmup):
-        ctx.generate(prompts[i], B, params)
+        for pr in prompts[i]:
+            ctx.generate(pr, B, params)
     barrier()
     dev_ms, wall_ms, actives = [], [], []
     with ClockSampler(local) as clk:
         for i in range(args.steps):
             t0 = time.perf_counter()
-            out, tr = ctx.generate(prompts[args.warmup + i], B, params, trace=True)
+            d = 0.0
+            for pr in prompts[args.warmup + i]:
+                out, tr = ctx.generate(pr, B, params, trace=True)
+                n = tr["steps_run"]
+                d += float(tr["step_ms"][:n].sum())
+                actives = tr["n_active"][:n].tolist()
             wall_ms.append((time.perf_counter() - t0) * 1e3)
-            n = tr["steps_run"]
-            dev_ms.append(float(tr["step_ms"][:n].sum()))
-            actives = tr["n_active"][:n].tolist()
+            dev_ms.append(d)
     barrier()
     tot_dev = reduce_max(sum(dev_ms))
     tot_wall = reduce_max(sum(wall_ms))
@@ -338,7 +350,8 @@ def main():
     dfb.dfb_ctx_profile.argtypes = [C.c_void_p, C.c_int]
     dfb.dfb_ctx_profile_read.argtypes = [C.c_void_p, C.c_void_p, C.c_int]
     dfb.dfb_ctx_profile(ctx.engine, 1)
-    ctx.generate(prompts[-1], B, params)
+    prof_prompt = prompts[-1][0] if prompts[-1] else rng.integers(0, min(hp.mask_token_id, hp.n_vocab) - 1, P).astype(np.int32)
+    ctx.generate(prof_prompt, B, params)
     prof = (Prof * 7)()
     dfb.dfb_ctx_profile_read(ctx.engine, prof, 7)
     dfb.dfb_ctx_profile(ctx.engine, 0)
@@ -357,7 +370,7 @@ def main():
                                      "tflops": prof[i].flops / (prof[i].ms * 1e-3) / 1e12 if prof[i].ms else 0}
                               for i, name in [(1, "q4_k"), (2, "q6_k"), (5, "lm_head"), (6, "attention")]}}
 
-    tokens_all = B * args.steps * world
+    tokens_all = B * args.steps * n_seq_total
     value = tokens_all / (tot_dev * 1e-3)
     e2e = tokens_all / (tot_wall * 1e-3)
     flops_run = c2_algorithmic_flops(hp, actives, P + B)
@@ -381,7 +394,7 @@ def main():
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": tot_wall / args.steps},
         "roofline": roofline,
-        "gpu_launches": launches_per_denoise_step * cfg["steps"] * args.steps,
+        "gpu_launches": launches_per_denoise_step * cfg["steps"] * args.steps * len(my_seq),
         "clocks": clk.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
