@@ -101,18 +101,6 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
 }
-// Warm L2 with a global range (address 16 B aligned, size multiple of 16); no smem, no barrier.
-__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
-}
-// 2-D tiled tensor load (x = innermost coordinate, in elements).
-__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
-            "r"(smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-        : "memory");
-}
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -198,16 +186,6 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, i
         : "memory");
 }
 
-// 16-byte async copy global -> shared (LDGSTS path, not the TMA unit); src_bytes 0
-// fills the 16 bytes with zeros and reads nothing.
-__device__ __forceinline__ void cp_async16(uint32_t dst_smem, const void *src, uint32_t src_bytes) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst_smem), "l"(src), "r"(src_bytes) : "memory");
-}
-// Arrive on the mbarrier once every cp.async this thread issued so far has completed
-// (the arrival is pre-counted in the barrier's expected count).
-__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t *bar) {
-    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
 
 // ── tcgen05, CTA-pair form (every tcgen05 instruction of a kernel uses one cta_group) ──
 // Issued by the same warp of both CTAs of the pair.
@@ -228,35 +206,15 @@ __device__ __forceinline__ void tc_fence_before() {
 __device__ __forceinline__ void tc_fence_after() {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
-// D[tmem] (+)= A[smem] * B[smem]^T, kind::f16, issued by the even CTA of the pair:
-// A rows 0-127 come from the even CTA and 128-255 from the odd one (same smem offset),
-// B columns [0, N/2) from the even CTA and [N/2, N) from the odd one; each CTA's TMEM
-// receives its own 128 rows of D.
-__device__ __forceinline__ void mma2_f16_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                            uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-// Same with A read from TMEM (this CTA's and the peer's, at the same column address):
-// lane = row of A, one 32-bit column per two consecutive k elements (lower k in the low
-// half), 8 columns per K = 16 step.
-__device__ __forceinline__ void mma2_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
-                                            uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
+// D[tmem] (+)= A * B^T, kind::f16, cta_group::2, issued by the even CTA of the pair: A
+// rows 0-127 come from the even CTA and 128-255 from the odd one (same TMEM column or
+// shared-memory offset), B columns [0, N/2) from the even CTA and [N/2, N) from the odd
+// one; each CTA's TMEM receives its own 128 rows of D.  A in TMEM: lane = row of A, one
+// 32-bit column per two consecutive k elements (lower k in the low half).
 // One 64-wide k-slice = four K = 16 MMAs in one statement, few instructions around them
-// (the issuing warp competes for issue slots with busy dequantizer warps): A from TMEM
-// (8 columns per step), B descriptor advanced by 32 bytes per step; accumulate only
-// the first step decides, the others always accumulate.
+// (every instruction on the issuing thread's path leaves the tensor pipe idle): A from
+// TMEM (8 columns per step), B descriptor advanced by 32 bytes per step; only the first
+// step's accumulate flag is the caller's, the others always accumulate.
 __device__ __forceinline__ void mma2_f16_ts_k64(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
                                                 uint32_t accumulate) {
     asm volatile(
