@@ -333,3 +333,4 @@ class Context:
 
 from . import dp  # noqa: E402  (data-parallel plumbing over independent sequences)
 from . import serve  # noqa: E402  (request server over a pool of contexts)
+from . import tp  # noqa: E402  (tensor-parallel shard plan and its numpy execution)
