@@ -89,6 +89,7 @@ def _load():
         (dfb, "dfb_device_count"): (I, [C.POINTER(I)]),
         (dfb, "dfb_forward"): (I, [P, P, I, P]),
         (dfb, "dfb_linear"): (I, [P, I, I, P, I, P]),
+        (dfb, "dfb_debug_stalled_linear"): (I, [P, I, I, P, I, P, C.c_ulonglong]),
         (dfb, "dfb_gen_begin"): (I, [P, P, I, I, C.POINTER(SamplerParams)]),
         (dfb, "dfb_gen_step"): (I, [P, I, I, I, P, P]),
         (dfb, "dfb_gen_tokens"): (I, [P, P, I]),

@@ -57,16 +57,6 @@ static int set_err(int code, const char *fmt, ...) {
 
 extern "C" const char *dfb_last_error(void) { return g_err.c_str(); }
 
-#ifdef DFB_GEMM_TRACE
-unsigned long long *g_dfb_trace = nullptr;
-int g_dfb_trace_launch = 0;
-// Copies the phase stamps of the most recent GEMM launch ([grid][16] u64) to the host.
-extern "C" int dfb_debug_gemm_trace(unsigned long long *host) {  // [64][256][16]
-    if (!g_dfb_trace) return -1;
-    cudaDeviceSynchronize();
-    return cudaMemcpy(host, g_dfb_trace, sizeof(unsigned long long) * (16 * 256 + 4 * 8 * 64) * 64, cudaMemcpyDeviceToHost) == cudaSuccess ? 0 : -1;
-}
-#endif
 
 extern "C" int dfb_device_count(int *n) {
     if (!n) return set_err(DFB_ERR_ARG, "null pointer");
@@ -107,17 +97,18 @@ static int make_tmap(CUtensorMap *m, const void *ptr, uint64_t cols, uint64_t ro
 }
 
 // The 3-D activation views the GEMM loads its B operand through (XMaps in gemm_dq.cuh):
-// x is a row-major [rows][K] f16 matrix, K a multiple of 64, x 16-byte aligned.
-static int make_xmaps(XMaps *xm, const void *x, int K, int rows) {
+// x is a row-major f16 matrix of rows of xs * K values (xs = 2: pair rows, xs = 1: plain),
+// K a multiple of 64, x 16-byte aligned.
+static int make_xmaps(XMaps *xm, const void *x, int K, int rows, int xs) {
     auto fn = encode_fn();
     if (!fn) return set_err(DFB_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
     if (K % 64) return set_err(DFB_ERR_UNSUPPORTED, "activation width %d not a multiple of 64", K);
     if (reinterpret_cast<uintptr_t>(x) % 16) return set_err(DFB_ERR_ARG, "activation matrix not 16-byte aligned");
     for (int i = 0; i < kXMaps; i++) {
         const int h = 16 * (i + 1);
-        cuuint64_t dims[3] = {64, (cuuint64_t)rows, (cuuint64_t)(K / 64)};
-        cuuint64_t strides[2] = {(cuuint64_t)K * 2, 128};
-        cuuint32_t box[3] = {64, (cuuint32_t)h, (cuuint32_t)x_slices(h)};
+        cuuint64_t dims[3] = {64, (cuuint64_t)rows, (cuuint64_t)(xs * K / 64)};
+        cuuint64_t strides[2] = {(cuuint64_t)xs * K * 2, 128};
+        cuuint32_t box[3] = {64, (cuuint32_t)h, (cuuint32_t)(xs * x_slices(h))};
         cuuint32_t es[3] = {1, 1, 1};
         CUresult r = fn(&xm->m[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(x), dims, strides, box, es,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -207,9 +198,10 @@ static void dequant_row_host(int type, const uint8_t *src, int64_t n, float *dst
 struct WMat {
     int wt = -1;
     int n_rows = 0, n_tiles = 0, K = 0, kb = 0;
-    int n_true = 0;  // output features the model defines (before padding / fusion slack)
+    int n_true = 0;     // output features the model defines (before padding / fusion slack)
+    float wscale = 1.f; // power-of-two pre-scale of the dequantized weights (quantized types)
     uint8_t *d = nullptr;
-    CUtensorMap tm{};
+    CUtensorMap tm{};   // f16 tiles (W_F16; W_F32: hi rows [0, n_rows), lo rows [n_rows, 2 n_rows))
     size_t bytes = 0;
 };
 
@@ -218,25 +210,38 @@ static int wt_of(int ggml_type) {
         case G_Q4_K: return W_Q4K;
         case G_Q6_K: return W_Q6K;
         case G_Q8_0: return W_Q80;
-        case G_F16: case G_F32: case G_BF16: return W_F16;
+        case G_F16: return W_F16;
+        case G_F32: case G_BF16: return W_F32;
         default: return -1;
     }
 }
 
 // Re-tile rows (nullptr = zero row; rows.size() a multiple of 128) into the chunk
-// layouts the dequant kernel reads (see gemm_dq.cuh), or into a plain f16 matrix.
+// layouts the dequant kernel reads (dequant.cuh), or into f16 matrices: W_F16 one [rows][K]
+// matrix, W_F32 (F32 / BF16 sources) the hi matrix followed by the lo matrix.
 static void retile_range(const std::vector<const uint8_t *> &rows, int type, int64_t K, int kb, int t0, int t1,
                          uint8_t *out) {
     const int wt = wt_of(type);
     const int RB = raw_chunk_bytes(wt);
-    if (wt == W_F16) {
+    if (wt == W_F16 || wt == W_F32) {
+        const size_t n_rows = rows.size();
         for (int r = t0 * 128; r < t1 * 128; r++) {
             uint16_t *dst = reinterpret_cast<uint16_t *>(out) + (size_t)r * K;
+            uint16_t *dlo = reinterpret_cast<uint16_t *>(out) + (n_rows + r) * K;
             const uint8_t *src = rows[r];
-            if (!src) { memset(dst, 0, K * 2); continue; }
-            if (type == G_F16) memcpy(dst, src, K * 2);
-            else if (type == G_F32) for (int64_t i = 0; i < K; i++) { float f; memcpy(&f, src + 4 * i, 4); dst[i] = f2h_host(f); }
-            else for (int64_t i = 0; i < K; i++) { uint16_t b; memcpy(&b, src + 2 * i, 2); dst[i] = f2h_host(bf2f_host(b)); }
+            if (!src) {
+                memset(dst, 0, K * 2);
+                if (wt == W_F32) memset(dlo, 0, K * 2);
+                continue;
+            }
+            if (type == G_F16) { memcpy(dst, src, K * 2); continue; }
+            for (int64_t i = 0; i < K; i++) {
+                float f;
+                if (type == G_F32) memcpy(&f, src + 4 * i, 4);
+                else { uint16_t b; memcpy(&b, src + 2 * i, 2); f = bf2f_host(b); }
+                dst[i] = f2h_host(f);
+                dlo[i] = f2h_host(f - h2f_host(dst[i]));
+            }
         }
         return;
     }
@@ -272,6 +277,45 @@ static void retile_range(const std::vector<const uint8_t *> &rows, int type, int
         }
 }
 
+// Upper bound of |w| over rows [r0, r1) of a quantized matrix, from the block scales:
+// Q4_K |d|*63*15 + |dmin|*63, Q6_K |d|*128*32, Q8_0 |d|*128.
+static float weight_bound_range(const std::vector<const uint8_t *> &rows, int type, int64_t K, size_t r0, size_t r1) {
+    float b = 0.f;
+    for (size_t r = r0; r < r1; r++) {
+        const uint8_t *row = rows[r];
+        if (!row) continue;
+        if (type == G_Q4_K) {
+            for (int64_t k = 0; k < K / 256; k++) {
+                uint16_t dh, mh;
+                memcpy(&dh, row + 144 * k, 2);
+                memcpy(&mh, row + 144 * k + 2, 2);
+                b = std::max(b, fabsf(h2f_host(dh)) * 945.f + fabsf(h2f_host(mh)) * 63.f);
+            }
+        } else if (type == G_Q6_K) {
+            for (int64_t k = 0; k < K / 256; k++) {
+                uint16_t dh;
+                memcpy(&dh, row + 210 * k + 208, 2);
+                b = std::max(b, fabsf(h2f_host(dh)) * 4096.f);
+            }
+        } else if (type == G_Q8_0) {
+            for (int64_t k = 0; k < K / 32; k++) {
+                uint16_t dh;
+                memcpy(&dh, row + 34 * k, 2);
+                b = std::max(b, fabsf(h2f_host(dh)) * 128.f);
+            }
+        }
+    }
+    return b;
+}
+
+// The pre-scale 2^e that puts the largest weight near 2^14: hi parts stay far below
+// f16's maximum (65504) and the lo parts of all but negligible weights stay normal.
+static float weight_prescale(float bound) {
+    if (!(bound > 0.f) || !std::isfinite(bound)) return 1.f;
+    const int e = std::max(-60, std::min(60, (int)floorf(log2f(16384.f / bound))));
+    return ldexpf(1.f, e);
+}
+
 static int build_wmat(const std::vector<const uint8_t *> &rows_in, int type, int64_t K, WMat &w) {
     const int wt = wt_of(type);
     if (wt < 0) return set_err(DFB_ERR_UNSUPPORTED, "GGML type %d not supported for a linear weight", type);
@@ -281,24 +325,31 @@ static int build_wmat(const std::vector<const uint8_t *> &rows_in, int type, int
     rows.resize((rows.size() + 255) / 256 * 256, nullptr);
     if ((wt == W_Q4K || wt == W_Q6K) && K % 256) return set_err(DFB_ERR_ARG, "K-quant row length %lld not a multiple of 256", (long long)K);
     if (wt == W_Q80 && K % 32) return set_err(DFB_ERR_ARG, "Q8_0 row length %lld not a multiple of 32", (long long)K);
-    if (wt == W_F16 && K % 8) return set_err(DFB_ERR_ARG, "F16 row length %lld not a multiple of 8", (long long)K);
+    if (w_smem(wt) && K % 8) return set_err(DFB_ERR_ARG, "F16/F32 row length %lld not a multiple of 8", (long long)K);
     w.wt = wt;
     w.n_rows = (int)rows.size();
     w.n_tiles = w.n_rows / 128;
     w.K = (int)K;
     w.kb = (int)((K + 255) / 256);
-    w.bytes = wt == W_F16 ? (size_t)w.n_rows * K * 2 : (size_t)w.n_tiles * w.kb * raw_chunk_bytes(wt);
+    w.bytes = wt == W_F16 ? (size_t)w.n_rows * K * 2
+              : wt == W_F32 ? (size_t)2 * w.n_rows * K * 2
+                            : (size_t)w.n_tiles * w.kb * raw_chunk_bytes(wt);
     std::vector<uint8_t> host(w.bytes);
     const int nthr = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
     std::vector<std::thread> th;
+    std::vector<float> bounds(nthr, 0.f);
     for (int i = 0; i < nthr; i++) {
         const int t0 = (int)((int64_t)w.n_tiles * i / nthr), t1 = (int)((int64_t)w.n_tiles * (i + 1) / nthr);
-        th.emplace_back(retile_range, std::cref(rows), type, K, w.kb, t0, t1, host.data());
+        th.emplace_back([&, t0, t1, i] {
+            retile_range(rows, type, K, w.kb, t0, t1, host.data());
+            if (!w_smem(wt)) bounds[i] = weight_bound_range(rows, type, K, (size_t)t0 * 128, (size_t)t1 * 128);
+        });
     }
     for (auto &t : th) t.join();
+    w.wscale = w_smem(wt) ? 1.f : weight_prescale(*std::max_element(bounds.begin(), bounds.end()));
     CK(cudaMalloc(&w.d, w.bytes));
     CK(cudaMemcpy(w.d, host.data(), w.bytes, cudaMemcpyHostToDevice));
-    if (wt == W_F16) RET(make_tmap(&w.tm, w.d, (uint64_t)K, (uint64_t)w.n_rows, 128));
+    if (w_smem(wt)) RET(make_tmap(&w.tm, w.d, (uint64_t)K, (uint64_t)(wt == W_F32 ? 2 : 1) * w.n_rows, 128));
     return DFB_OK;
 }
 
@@ -343,6 +394,9 @@ extern "C" int dfb_model_create(const dfb_hparams *hp, int device, dfb_model **o
     const int hd = hp->n_embd / hp->n_head;
     if (hd != 16 && hd != 32 && hd != 64 && hd != 128)
         return set_err(DFB_ERR_UNSUPPORTED, "head_dim %d not supported (16/32/64/128)", hd);
+    // GEMM activations are stored as pair rows of 64-wide slices
+    if (hp->n_embd % 64 || hp->n_ff % 64)
+        return set_err(DFB_ERR_UNSUPPORTED, "n_embd %d / n_ff %d not multiples of 64", hp->n_embd, hp->n_ff);
     int ndev = 0;
     CK(cudaGetDeviceCount(&ndev));
     if (device < 0) CK(cudaGetDevice(&device));  // -1: the caller's current device
@@ -542,7 +596,8 @@ struct dfb_ctx {
     int cap = 0;
     // activations
     float *x = nullptr, *y = nullptr, *logits = nullptr;  // residual stream, projection output, logits
-    __half *h = nullptr, *att = nullptr, *q = nullptr, *ffh = nullptr, *kc = nullptr, *vc = nullptr;
+    float *q = nullptr, *kc = nullptr, *vc = nullptr;      // Q rows, K/V cache [layer][position][n_kv] (f32)
+    __half *h = nullptr, *att = nullptr, *ffh = nullptr;  // GEMM inputs as pair rows (2 f16 per value)
     float2 *rope = nullptr;
     XMaps xm_h{}, xm_att{}, xm_ffh{};  // GEMM B-operand views of h, att, ffh
     // sequence state
@@ -555,6 +610,10 @@ struct dfb_ctx {
     float *ws = nullptr;
     int *tile_cnt = nullptr, *err = nullptr;
     int n_tile_cnt = 0;
+    // failure-detection test hook (dfb_debug_stalled_linear): the next GEMM launch starts
+    // with tile counter 0 poisoned and every wait limited to stall_timeout_ns
+    bool stall_next = false;
+    unsigned long long stall_timeout_ns = 0;
     // optional per-launch timing (dfb_ctx_profile)
     struct ProfRec {
         cudaEvent_t a, b;
@@ -576,7 +635,7 @@ static void ctx_free_buffers(dfb_ctx *c) {
                   c->last_changed, c->cand_tok, c->commit_pos, c->commit_tok, c->order, c->masked, c->active_pos,
                   c->masked_pos, c->cnt, c->cand_conf, c->cand_ent, c->ws, c->tile_cnt, c->err};
     for (void *p : ps) cudaFree(p);
-    c->x = c->y = c->logits = nullptr; c->h = c->att = c->q = c->ffh = c->kc = c->vc = nullptr; c->rope = nullptr;
+    c->x = c->y = c->logits = c->q = c->kc = c->vc = nullptr; c->h = c->att = c->ffh = nullptr; c->rope = nullptr;
     c->seq = c->prev_seq = c->last_changed = c->cand_tok = c->commit_pos = c->commit_tok = c->order = nullptr;
     c->masked = nullptr; c->active_pos = c->masked_pos = c->cnt = nullptr; c->cand_conf = c->cand_ent = nullptr;
     c->ws = nullptr; c->tile_cnt = c->err = nullptr;
@@ -606,7 +665,8 @@ static int ctx_reserve(dfb_ctx *c, int n) {
     ctx_free_buffers(c);
     const size_t d = hp.n_embd, ff = hp.n_ff, V = hp.n_vocab, L = hp.n_layer, kvd = m->n_kv, hd = m->hd;
 #define AL(ptr, count) CK(cudaMalloc(&(ptr), sizeof(*(ptr)) * (size_t)(count)))
-    AL(c->x, cap * d); AL(c->y, cap * d); AL(c->h, cap * d); AL(c->att, cap * d); AL(c->q, cap * d); AL(c->ffh, cap * ff);
+    AL(c->x, cap * d); AL(c->y, cap * d); AL(c->h, 2 * cap * d); AL(c->att, 2 * cap * d); AL(c->q, cap * d);
+    AL(c->ffh, 2 * cap * ff);
     AL(c->kc, L * cap * kvd); AL(c->vc, L * cap * kvd); AL(c->logits, (size_t)cap * V); AL(c->rope, cap * hd / 2);
     AL(c->seq, cap); AL(c->prev_seq, cap); AL(c->last_changed, cap); AL(c->cand_tok, cap); AL(c->commit_pos, cap);
     AL(c->commit_tok, cap); AL(c->order, cap); AL(c->masked, cap); AL(c->active_pos, cap); AL(c->masked_pos, cap);
@@ -623,17 +683,17 @@ static int ctx_reserve(dfb_ctx *c, int n) {
     CK(cudaMemset(c->cnt, 0, sizeof(int) * CNT_N));
     CK(cudaMemset(c->x, 0, sizeof(float) * cap * d));
     CK(cudaMemset(c->y, 0, sizeof(float) * cap * d));
-    CK(cudaMemset(c->h, 0, 2 * cap * d));
-    CK(cudaMemset(c->att, 0, 2 * cap * d));
-    CK(cudaMemset(c->ffh, 0, 2 * cap * ff));
-    CK(cudaMemset(c->kc, 0, 2 * L * cap * kvd));
-    CK(cudaMemset(c->vc, 0, 2 * L * cap * kvd));
+    CK(cudaMemset(c->h, 0, 4 * cap * d));
+    CK(cudaMemset(c->att, 0, 4 * cap * d));
+    CK(cudaMemset(c->ffh, 0, 4 * cap * ff));
+    CK(cudaMemset(c->kc, 0, 4 * L * cap * kvd));
+    CK(cudaMemset(c->vc, 0, 4 * L * cap * kvd));
     std::vector<float2> rope;
     rope_table_host(cap, (int)hd, hp.rope_theta, rope);
     CK(cudaMemcpy(c->rope, rope.data(), rope.size() * sizeof(float2), cudaMemcpyHostToDevice));
-    RET(make_xmaps(&c->xm_h, c->h, (int)d, cap));
-    RET(make_xmaps(&c->xm_att, c->att, m->n_q, cap));
-    RET(make_xmaps(&c->xm_ffh, c->ffh, (int)ff, cap));
+    RET(make_xmaps(&c->xm_h, c->h, (int)d, cap, 2));
+    RET(make_xmaps(&c->xm_att, c->att, m->n_q, cap, 2));
+    RET(make_xmaps(&c->xm_ffh, c->ffh, (int)ff, cap, 2));
     c->cap = cap;
     return DFB_OK;
 }
@@ -706,7 +766,7 @@ static cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_
 }
 
 // CTA pairs of a GEMM instantiation that fit on the device at once (one CTA per SM).
-template <int WT, int EPI>
+template <int WT, int EPI, int XS>
 static int gemm_max_pairs(int device, int n_sm) {
     static int cached[64] = {0};
     if (device < 0 || device >= 64) return n_sm / 2;
@@ -717,7 +777,7 @@ static int gemm_max_pairs(int device, int n_sm) {
         cfg.blockDim = dim3(kThreads);
         cfg.dynamicSmemBytes = smem;
         int n = 0;
-        if (cudaOccupancyMaxActiveClusters(&n, dq_gemm_kernel<WT, EPI>, &cfg) != cudaSuccess || n <= 0) {
+        if (cudaOccupancyMaxActiveClusters(&n, dq_gemm_kernel<WT, EPI, XS>, &cfg) != cudaSuccess || n <= 0) {
             cudaGetLastError();
             n = n_sm / 2;
         }
@@ -726,9 +786,27 @@ static int gemm_max_pairs(int device, int n_sm) {
     return cached[device];
 }
 
+// Parameters of one launch of the dequant GEMM on weight w (scratch supplied by the caller).
+static GemmParams gemm_params(const WMat &w, const int *m_dev, float *ws, int *tile_cnt, int *err, const EpiArgs &epi) {
+    GemmParams p;
+    p.w = w.d;
+    p.K = w.K;
+    p.n_tiles = w.n_tiles;
+    p.kb = w.kb;
+    p.wscale = w.wscale;
+    p.lo_row = w.n_rows;
+    p.m_dev = m_dev;
+    p.ws = ws;
+    p.tile_cnt = tile_cnt;
+    p.err = err;
+    p.epi = epi;
+    p.epi.out_scale = 1.0f / w.wscale;  // a power of two: exact
+    return p;
+}
+
 template <int WT, int EPI>
 static int launch_gemm_t(dfb_ctx *c, const WMat &w, const XMaps &xm, const EpiArgs &epi) {
-    auto kern = dq_gemm_kernel<WT, EPI>;
+    auto kern = dq_gemm_kernel<WT, EPI, 2>;
     constexpr int smem = gemm_smem_bytes(WT);
     static bool attr_set[64] = {false};
     const int dev = c->m->device;
@@ -736,37 +814,24 @@ static int launch_gemm_t(dfb_ctx *c, const WMat &w, const XMaps &xm, const EpiAr
         CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
         attr_set[dev] = true;
     }
-    GemmParams p;
-    p.w = w.d;
-    p.K = w.K;
-    p.n_tiles = w.n_tiles;
-    p.kb = w.kb;
-    p.m_dev = c->cnt + CNT_M;
-    p.ws = c->ws;
-    p.tile_cnt = c->tile_cnt;
-    p.err = c->err;
-    p.epi = epi;
-#ifdef DFB_GEMM_TRACE
-    // analysis builds: stamp the last GEMM launch of each step into a per-context buffer
-    // launch i of the process stamps slice i % 64 of a [64][256][16] buffer
-    extern unsigned long long *g_dfb_trace;
-    extern int g_dfb_trace_launch;
-    if (!g_dfb_trace) {
-        cudaMalloc(&g_dfb_trace, sizeof(unsigned long long) * (16 * 256 + 4 * 8 * 64) * 64);
-        cudaMemset(g_dfb_trace, 0, sizeof(unsigned long long) * (16 * 256 + 4 * 8 * 64) * 64);
+    GemmParams p = gemm_params(w, c->cnt + CNT_M, c->ws, c->tile_cnt, c->err, epi);
+    if (c->stall_next) {
+        // a split tile's contributors wait for arrivals that cannot reach this count
+        static const int kPoison = -(1 << 30);
+        CK(cudaMemcpyAsync(c->tile_cnt, &kPoison, sizeof(int), cudaMemcpyHostToDevice, c->st));
+        p.timeout_ns = c->stall_timeout_ns;
+        c->stall_next = false;
     }
-    p.trace = g_dfb_trace + (size_t)(g_dfb_trace_launch++ % 64) * (256 * 16 + 4 * 8 * 64);
-#endif
     cudaEvent_t ev0 = nullptr;
     prof_begin(c, &ev0);
     // A pair tile is split over at most n_pairs/n_ptiles + 2 pairs; keep that within kMaxContrib.
-    const int n_pairs = std::min(gemm_max_pairs<WT, EPI>(c->m->device, c->m->n_sm), (kMaxContrib - 2) * (w.n_tiles / 2));
+    const int n_pairs = std::min(gemm_max_pairs<WT, EPI, 2>(c->m->device, c->m->n_sm), (kMaxContrib - 2) * (w.n_tiles / 2));
     CK(launch_k(kern, dim3(2 * n_pairs), dim3(kThreads), smem, c->st, !c->prof, w.tm, xm, p));
-    // algorithmic work: 2*K MACs per output, weights read once, X read, Y written
-    const int out_bytes = (EPI == EPI_F16 || EPI == EPI_QKV || EPI == EPI_SWIGLU) ? 2 : 4;
+    // algorithmic work: 2*K MACs per output, weights read once, X read (pair rows, 4 B per
+    // value), Y written (f32, or pair rows for SwiGLU: 4 B per output feature either way)
     const int cat = WT == W_Q4K ? DFB_PROF_Q4K : WT == W_Q6K ? DFB_PROF_Q6K : WT == W_Q80 ? DFB_PROF_Q80 : DFB_PROF_F16;
     prof_end(c, ev0, EPI == EPI_LOGITS ? (int)DFB_PROF_LMHEAD : cat, 2.0 * w.K * (double)w.n_true, (double)w.bytes,
-             2.0 * w.K + (double)out_bytes * (EPI == EPI_SWIGLU ? w.n_true / 2 : w.n_true));
+             4.0 * w.K + 4.0 * (EPI == EPI_SWIGLU ? w.n_true / 2 : w.n_true));
     return DFB_OK;
 }
 
@@ -777,12 +842,13 @@ static int launch_gemm(dfb_ctx *c, const WMat &w, const XMaps &xm, const EpiArgs
         case W_Q6K: return launch_gemm_t<W_Q6K, EPI>(c, w, xm, epi);
         case W_Q80: return launch_gemm_t<W_Q80, EPI>(c, w, xm, epi);
         case W_F16: return launch_gemm_t<W_F16, EPI>(c, w, xm, epi);
+        case W_F32: return launch_gemm_t<W_F32, EPI>(c, w, xm, epi);
     }
     return set_err(DFB_ERR_STATE, "weight not uploaded");
 }
 
 template <int HD>
-static int launch_attn_t(dfb_ctx *c, const __half *kc, const __half *vc, int n_keys) {
+static int launch_attn_t(dfb_ctx *c, const float *kc, const float *vc, int n_keys) {
     const dfb_model *m = c->m;
     constexpr int smem = attn_smem_bytes<HD>();
     static bool attr_set[64] = {false};
@@ -794,9 +860,11 @@ static int launch_attn_t(dfb_ctx *c, const __half *kc, const __half *vc, int n_k
     dim3 grid((c->cap + kAttnRows - 1) / kAttnRows, m->hp.n_head);
     cudaEvent_t ev0 = nullptr;
     prof_begin(c, &ev0);
-    CK(launch_k(attn_kernel<HD>, grid, dim3(kAttnThreads), smem, c->st, !c->prof, (const __half *)c->q, m->n_q, kc, vc, m->n_kv,
-                c->att, m->n_q, (const int *)(c->cnt + CNT_M), n_keys, m->hp.n_head / m->hp.n_head_kv, scale_log2));
-    prof_end(c, ev0, DFB_PROF_ATTN, 4.0 * n_keys * m->hp.n_head * HD, 2.0 * 2.0 * n_keys * m->n_kv, 4.0 * m->n_q);
+    CK(launch_k(attn_kernel<HD>, grid, dim3(kAttnThreads), smem, c->st, !c->prof, (const float *)c->q, m->n_q, kc, vc,
+                m->n_kv, c->att, 2 * m->n_q, (const int *)(c->cnt + CNT_M), n_keys, m->hp.n_head / m->hp.n_head_kv,
+                scale_log2));
+    // algorithmic bytes: K and V of every key once (f32), Q in (f32), O out (pair rows)
+    prof_end(c, ev0, DFB_PROF_ATTN, 4.0 * n_keys * m->hp.n_head * HD, 2.0 * 4.0 * n_keys * m->n_kv, 8.0 * m->n_q);
     return DFB_OK;
 }
 
@@ -812,7 +880,7 @@ static int run_forward(dfb_ctx *c, int n_total) {
     CK(cudaGetLastError());
     for (int l = 0; l < hp.n_layer; l++) {
         const LayerW &L = m->layers[l];
-        __half *kc = c->kc + (size_t)l * cap * m->n_kv, *vc = c->vc + (size_t)l * cap * m->n_kv;
+        float *kc = c->kc + (size_t)l * cap * m->n_kv, *vc = c->vc + (size_t)l * cap * m->n_kv;
         // the previous layer's down projection is added to the residual stream here
         CK(launch_k(rmsnorm_kernel, dim3(cap), dim3(256), 0, c->st, true, c->x, (const float *)(l ? c->y : nullptr),
                     (const float *)L.attn_norm, d, hp.rms_norm_eps, (const int *)c->cnt, c->h));
@@ -835,7 +903,7 @@ static int run_forward(dfb_ctx *c, int n_total) {
         CK(launch_k(rmsnorm_kernel, dim3(cap), dim3(256), 0, c->st, true, c->x, (const float *)c->y,
                     (const float *)L.ffn_norm, d, hp.rms_norm_eps, (const int *)c->cnt, c->h));
         EpiArgs eg;
-        eg.out = c->ffh; eg.ld = hp.n_ff; eg.n_valid = 2 * hp.n_ff;
+        eg.out = c->ffh; eg.ld = 2 * hp.n_ff; eg.n_valid = 2 * hp.n_ff;  // pair rows
         RET(launch_gemm<EPI_SWIGLU>(c, L.gateup, c->xm_h, eg));
         EpiArgs ed;  // FFN down projection -> y, added to x by the next norm
         ed.out = c->y; ed.ld = d; ed.n_valid = d;
@@ -993,15 +1061,15 @@ extern "C" int dfb_linear(dfb_ctx *c, int role, int layer, const float *x_host, 
     RET(ctx_reserve(c, M));
     __half *xh = nullptr;
     float *xf = nullptr, *y = nullptr;
-    CK(cudaMalloc(&xh, (size_t)M * K * 2));
+    CK(cudaMalloc(&xh, (size_t)M * K * 4));  // pair rows
     CK(cudaMalloc(&xf, (size_t)M * K * 4));
     CK(cudaMalloc(&y, (size_t)M * w->n_rows * 4));
     int rc = DFB_OK;
     XMaps xm;
     do {
-        if ((rc = make_xmaps(&xm, xh, K, M)) != DFB_OK) break;
+        if ((rc = make_xmaps(&xm, xh, K, M, 2)) != DFB_OK) break;
         if (cudaMemcpyAsync(xf, x_host, (size_t)M * K * 4, cudaMemcpyHostToDevice, c->st) != cudaSuccess) { rc = set_err(DFB_ERR_CUDA, "H2D failed"); break; }
-        f32_to_f16_kernel<<<256, 256, 0, c->st>>>(xf, xh, (size_t)M * K);
+        f32_to_pair_kernel<<<256, 256, 0, c->st>>>(xf, xh, M, K);
         if (cudaMemcpyAsync(c->cnt + CNT_M, &M, sizeof(int), cudaMemcpyHostToDevice, c->st) != cudaSuccess) { rc = set_err(DFB_ERR_CUDA, "H2D failed"); break; }
         EpiArgs e;
         e.out = y; e.ld = w->n_rows; e.n_valid = w->n_rows;
@@ -1029,6 +1097,17 @@ extern "C" int dfb_linear(dfb_ctx *c, int role, int layer, const float *x_host, 
             }
     } while (0);
     cudaFree(xh); cudaFree(xf); cudaFree(y);
+    return rc;
+}
+
+extern "C" int dfb_debug_stalled_linear(dfb_ctx *c, int role, int layer, const float *x_host, int M, float *y_host,
+                                        unsigned long long timeout_ns) {
+    if (!c) return set_err(DFB_ERR_ARG, "null context");
+    if (timeout_ns == 0 || timeout_ns > 4000000000ull) return set_err(DFB_ERR_ARG, "timeout_ns outside (0, 4 s]");
+    c->stall_next = true;
+    c->stall_timeout_ns = timeout_ns;
+    const int rc = dfb_linear(c, role, layer, x_host, M, y_host);
+    c->stall_next = false;
     return rc;
 }
 
@@ -1181,20 +1260,16 @@ __global__ void noalloc_prep_kernel(int *cnt, int n_tiles, int M) {
 }
 
 template <int WT>
-int noalloc_launch(const WMat &w, const XMaps &xm, const EpiArgs &e, const NoallocDev &nd, cudaStream_t st) {
-    auto kern = dq_gemm_kernel<WT, EPI_F32>;
+int noalloc_launch(const WMat &w, const XMaps &xm, const EpiArgs &e, const NoallocDev &nd, int device, cudaStream_t st) {
+    // the caller's x is a plain f16 matrix: one activation part (W_hi.x + W_lo.x)
+    auto kern = dq_gemm_kernel<WT, EPI_F32, 1>;
     constexpr int smem = gemm_smem_bytes(WT);
-    CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    GemmParams p;
-    p.w = w.d;
-    p.K = w.K;
-    p.n_tiles = w.n_tiles;
-    p.kb = w.kb;
-    p.m_dev = nd.cnt + kCntM;
-    p.ws = nd.ws;
-    p.tile_cnt = nd.cnt;
-    p.err = nd.cnt + kCntM + 1;
-    p.epi = e;
+    static bool attr_set[64] = {false};  // once per device (the caller holds the device lock)
+    if (!attr_set[device & 63]) {
+        CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        attr_set[device & 63] = true;
+    }
+    const GemmParams p = gemm_params(w, nd.cnt + kCntM, nd.ws, nd.cnt, nd.cnt + kCntM + 1, e);
     const int n_pairs = std::min(kNoallocGrid / 2, (kMaxContrib - 2) * (w.n_tiles / 2));
     CK(launch_k(kern, dim3(2 * n_pairs), dim3(kThreads), smem, st, false, w.tm, xm, p));
     return DFB_OK;
@@ -1223,7 +1298,7 @@ extern "C" int dfb_linear_noalloc(const dfb_model *m, int role, int layer, const
     if (w->n_tiles > kNoallocMaxTiles)
         return set_err(DFB_ERR_ARG, "weight has %d output tiles, the fixed scratch holds %d", w->n_tiles, kNoallocMaxTiles);
     XMaps xm;  // host-side descriptors of the caller's matrix (no device memory)
-    RET(make_xmaps(&xm, x_f16_dev, K, M));
+    RET(make_xmaps(&xm, x_f16_dev, K, M, 1));
     std::lock_guard<std::mutex> lk(device_lock(m->device));
     CK(cudaSetDevice(m->device));
     NoallocDev nd;
@@ -1249,10 +1324,11 @@ extern "C" int dfb_linear_noalloc(const dfb_model *m, int role, int layer, const
     e.ld = w->n_true;
     e.n_valid = w->n_true;
     switch (w->wt) {
-        case W_Q4K: RET(noalloc_launch<W_Q4K>(*w, xm, e, nd, st)); break;
-        case W_Q6K: RET(noalloc_launch<W_Q6K>(*w, xm, e, nd, st)); break;
-        case W_Q80: RET(noalloc_launch<W_Q80>(*w, xm, e, nd, st)); break;
-        case W_F16: RET(noalloc_launch<W_F16>(*w, xm, e, nd, st)); break;
+        case W_Q4K: RET(noalloc_launch<W_Q4K>(*w, xm, e, nd, m->device, st)); break;
+        case W_Q6K: RET(noalloc_launch<W_Q6K>(*w, xm, e, nd, m->device, st)); break;
+        case W_Q80: RET(noalloc_launch<W_Q80>(*w, xm, e, nd, m->device, st)); break;
+        case W_F16: RET(noalloc_launch<W_F16>(*w, xm, e, nd, m->device, st)); break;
+        case W_F32: RET(noalloc_launch<W_F32>(*w, xm, e, nd, m->device, st)); break;
         default: return set_err(DFB_ERR_STATE, "weight not uploaded");
     }
     CK(cudaStreamSynchronize(st));

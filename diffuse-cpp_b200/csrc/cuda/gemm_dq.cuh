@@ -3,14 +3,23 @@
 // Replaces every ggml_mul_mat(W, x) of the reference forward (src/diffuse-graph.cpp
 // :61-63, 122, 136-140, 154 and the cached variants :451-453, 556, 570-574, 587).
 //
-// Operands.  W is the GGUF weight (Q4_K / Q6_K / Q8_0 raw blocks re-tiled at load,
-// or F16), dequantized to f16 in registers; X is the f16 activation matrix [tokens][K].
-// The MMA is "swap-AB" and paired (tcgen05 cta_group::2, M = 256): the A operand is a
-// tile of 256 output features, 128 dequantized into the TMEM of each CTA of a pair (F16
-// weights: TMA-loaded into shared memory, 128-byte-swizzled K-major); the B operand is a
-// group of up to 256 tokens of X, each CTA holding half of them (TMA tensor loads into
-// shared memory, same swizzle).  The f32 accumulator lives in TMEM: lane = output
-// feature, column = token.
+// Precision.  The products are those of the model's f32 mathematics to ~2^-22: each
+// operand is carried as an unevaluated sum of two f16 values (hi = f16(v), lo =
+// f16(v - hi), ~22 significant bits) and the MMA computes W_hi.X_hi + W_hi.X_lo +
+// W_lo.X_hi (the dropped W_lo.X_lo term is ~2^-22 of the product) into one f32
+// accumulator.  Quantized weights are dequantized in f32 (exact: Q4_K d*sc*q - dmin*m is
+// one f32 rounding, Q6_K / Q8_0 products are exact) after a power-of-two pre-scale that
+// keeps W_lo in f16's normal range; the epilogue undoes the scale.  F16 weights are
+// exact as they are (two MMAs); F32 / BF16 weights are stored as hi and lo f16 matrices.
+//
+// Operands.  W is the GGUF weight (Q4_K / Q6_K / Q8_0 raw blocks re-tiled at load, or
+// f16 matrices); X is the activation matrix [tokens][K] in "pair" layout: per 64-wide
+// k-slice, 64 hi values then 64 lo values (row length 2K f16).  The MMA is "swap-AB" and
+// paired (tcgen05 cta_group::2, M = 256): the A operand is a tile of 256 output
+// features, 128 dequantized into the TMEM of each CTA of a pair (f16 weights: TMA-loaded
+// into shared memory, 128-byte-swizzled K-major); the B operand is a group of up to 256
+// tokens of X, each CTA holding half of them (TMA tensor loads into shared memory, same
+// swizzle).  The f32 accumulator lives in TMEM: lane = output feature, column = token.
 //
 // Work split.  Units are (pair tile of 256 output rows, token group, k-block of 256); a
 // persistent grid of CTA pairs (one CTA per SM) takes equal contiguous unit ranges
@@ -26,34 +35,19 @@
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cstdint>
+#include "dequant.cuh"
 #include "ptx.cuh"
 
 namespace dfb {
 
-// Per-CTA phase timestamps for pipeline analysis (compiled in only with -DDFB_GEMM_TRACE).
-#ifdef DFB_GEMM_TRACE
-#define GEMM_STAMP(p, slot)                                                                      \
-    do {                                                                                         \
-        if ((p).trace) (p).trace[(size_t)blockIdx.x * 16 + (slot)] = globaltimer();              \
-    } while (0)
-// Event streams of CTAs 0..3 (also -DDFB_GEMM_EVENTS, which perturbs the timing it records):
-// stream s, event i -> trace[256*16 + (cta*8 + s)*64 + i].
-#ifdef DFB_GEMM_EVENTS
-#define GEMM_EVENT(p, stream, idx)                                                               \
-    do {                                                                                         \
-        if ((p).trace && blockIdx.x < 4 && (idx) < 64)                                           \
-            (p).trace[256 * 16 + ((size_t)blockIdx.x * 8 + (stream)) * 64 + (idx)] = globaltimer(); \
-    } while (0)
-#else
-#define GEMM_EVENT(p, stream, idx) do {} while (0)
-#endif
-#else
-#define GEMM_STAMP(p, slot) do {} while (0)
-#define GEMM_EVENT(p, stream, idx) do {} while (0)
-#endif
-
-enum WType : int { W_Q4K = 0, W_Q6K = 1, W_Q80 = 2, W_F16 = 3 };
-enum EpiKind : int { EPI_F32 = 0, EPI_F16 = 1, EPI_QKV = 3, EPI_SWIGLU = 4, EPI_LOGITS = 5 };
+// W_F16: one f16 matrix (exact); W_F32: hi and lo f16 matrices of F32 / BF16 weights.
+enum WType : int { W_Q4K = 0, W_Q6K = 1, W_Q80 = 2, W_F16 = 3, W_F32 = 4 };
+__host__ __device__ constexpr bool w_smem(int wt) { return wt == W_F16 || wt == W_F32; }  // A by TMA into shared memory
+__host__ __device__ constexpr bool w_split(int wt) { return wt != W_F16; }               // A has a lo part
+// EPI_F32: f32 rows; EPI_QKV: Q rows and K/V cache rows (f32) with bias and RoPE;
+// EPI_SWIGLU: silu(gate) * up as pair-layout rows (the down projection's X);
+// EPI_LOGITS: f32 rows at the tokens' positions.
+enum EpiKind : int { EPI_F32 = 0, EPI_QKV = 3, EPI_SWIGLU = 4, EPI_LOGITS = 5 };
 
 // Bytes of one re-tiled chunk (128 rows x one k-block of 256 elements).
 __host__ __device__ constexpr int raw_chunk_bytes(int wt) {
@@ -61,13 +55,14 @@ __host__ __device__ constexpr int raw_chunk_bytes(int wt) {
 }
 
 struct EpiArgs {
-    void *out = nullptr;   // F32/F16/RESID/SWIGLU/LOGITS destination
-    int ld = 0;            // its row stride (elements)
+    void *out = nullptr;   // F32 / SWIGLU / LOGITS destination
+    int ld = 0;            // its row stride (elements; SWIGLU: f16 elements of the pair rows)
     int n_valid = 0;       // valid output features (rows of W before padding)
-    // QKV
-    __half *q_out = nullptr;
+    float out_scale = 1.f; // undoes the weights' power-of-two pre-scale (exact)
+    // QKV (f32 outputs)
+    float *q_out = nullptr;
     int ld_q = 0;
-    __half *k_cache = nullptr, *v_cache = nullptr;  // [position][n_kv] of this layer
+    float *k_cache = nullptr, *v_cache = nullptr;  // [position][n_kv] of this layer
     int ld_kv = 0;
     int n_q_tiles = 0, n_k_tiles = 0;  // tiles in the (padded) Q and K sections
     int n_q = 0, n_kv = 0, head_dim = 0;
@@ -77,9 +72,11 @@ struct EpiArgs {
 };
 
 // Activation tensor maps, one per token half-group size h = 16 (i + 1), i = 0..7: a 3-D
-// view {64 k, rows, K / 64 k-blocks} of the row-major [rows][K] f16 matrix (strides: row,
-// then 128 B), box {64, h, x_slices(h)}, 128-byte swizzle.  One load brings x_slices
-// consecutive 64-wide k-slices of h rows, each in the canonical K-major SW128 layout.
+// view {64 k, rows, XS * K / 64 slices} of the row-major activation matrix (XS = 2: pair
+// layout, a hi slice then a lo slice per 64-wide k-slice; XS = 1: plain f16), strides
+// row, then 128 B; box {64, h, XS * x_slices(h)}, 128-byte swizzle.  One load brings
+// x_slices consecutive k-slices (both parts) of h rows, each part in the canonical
+// K-major SW128 layout.
 constexpr int kXMaps = 8;
 __host__ __device__ constexpr int x_slices(int h) { return h <= 32 ? 4 : h <= 64 ? 2 : 1; }
 struct XMaps {
@@ -91,11 +88,13 @@ struct GemmParams {
     int K = 0;                   // valid columns of the activations
     int n_tiles = 0;             // 128-row output tiles
     int kb = 0;                  // k-blocks of 256
+    float wscale = 1.f;          // power-of-two pre-scale of the dequantized weights
+    int lo_row = 0;              // W_F32: row of the lo matrix in the weight tensor map
     const int *m_dev = nullptr;  // token count (device)
     float *ws = nullptr;         // split-tile partials [grid][2][256 * 128]
     int *tile_cnt = nullptr;     // [n_tiles x token groups] arrival + departure counters, left at 0
     int *err = nullptr;          // first error code of any CTA
-    unsigned long long *trace = nullptr;  // DFB_GEMM_TRACE builds only: [grid][16] globaltimer stamps
+    unsigned long long timeout_ns = 4000000000ull;  // limit of every wait (4 s; tests shorten it)
     EpiArgs epi;
 };
 
@@ -103,7 +102,6 @@ constexpr int kThreads = 640;            // 20 warps, roles below
 constexpr int kEpiThreads = 256;         // two epilogue warps per TMEM lane quarter
 constexpr int kDeqWarps = 8;             // two sets of four: even / odd k-slices
 constexpr int kSliceBytes = 128 * 128;   // one 64-wide k-slice of this CTA's 128 weight rows (f16)
-constexpr int kABytes = kSliceBytes;      // one A stage: one k-slice
 constexpr int kMaxTok = 256;             // tokens per MMA group (N) of the pair
 constexpr int kDblTok = 192;             // groups up to this size double-buffer the accumulator
 constexpr int kWsTile = kMaxTok * 128;   // floats per partial tile (one CTA's 128 rows)
@@ -112,21 +110,24 @@ constexpr int kMaxAStages = 6, kMaxBSlots = 24, kMaxRawStages = 4;
 // TMEM (512 columns per CTA): accumulators [0, 192) and [192, 384) for token groups of up
 // to 192, one accumulator [0, 256) for larger groups (the MMA of the next segment then
 // waits for the epilogue to drain it, which costs less than dequantizing the weights once
-// per group of 128); dequantized A stages (quantized weights) at [384 + 32 st, +32):
-// lane = weight row, one k-slice each.
+// per group of 128); dequantized A stages (quantized weights) at [384 + 64 st, +64):
+// lane = weight row, one k-slice each, hi part in the first 32 columns, lo in the next.
 constexpr int kTmemA = 2 * kDblTok;
-constexpr int kTmemAStage = 32;
+constexpr int kTmemAStage = 64;
+constexpr int kTmemALo = 32;
+constexpr int kNA = 2;                   // A stages: set p of the dequantizers fills stage p
 
 // Rings per weight type, sized so that shared memory (227 KB) holds them:
-//  A        one k-slice per stage, four stages (one k-block): dequantized weights go to
-//           TMEM (written by tcgen05.st, read by the MMA from TMEM: no shared-memory round
-//           trip and no proxy fence, which cost ~1.2k cycles per warp and stage); F16
-//           weights are TMA-loaded into a shared-memory ring instead;
-//  B ring   this CTA's activation rows of 1-4 k-slices per slot (2-12 KB), so small
-//           token counts keep many slices in flight and hide the L2 latency;
+//  A        one k-slice per stage, two stages: dequantized weights go to TMEM (written by
+//           tcgen05.st, read by the MMA from TMEM: no shared-memory round trip and no
+//           proxy fence, which cost ~1.2k cycles per warp and stage); f16 weight tiles
+//           are TMA-loaded into a shared-memory ring instead (hi and lo tiles for W_F32);
+//  B ring   this CTA's activation rows of 1-4 k-slices per slot, so small token counts
+//           keep many slices in flight and hide the L2 latency;
 //  raw ring re-tiled weight chunks (one k-block of 256 for 128 rows), grouped.
-__host__ __device__ constexpr int a_stages(int wt) { return 4; }
-__host__ __device__ constexpr int a_ring_bytes(int wt) { return wt == W_F16 ? 4 * kABytes : 0; }
+__host__ __device__ constexpr int a_stages(int wt) { return kNA; }
+__host__ __device__ constexpr int a_stage_bytes(int wt) { return wt == W_F32 ? 2 * kSliceBytes : kSliceBytes; }
+__host__ __device__ constexpr int a_ring_bytes(int wt) { return w_smem(wt) ? kNA * a_stage_bytes(wt) : 0; }
 __host__ __device__ constexpr int b_ring_bytes(int wt) { return 96 * 1024; }
 // A raw stage holds raw_cpr consecutive chunks of the CTA's unit range: the weight
 // stream reached ~3.8 TB/s with 18 KB stages and ~6-7 TB/s with 36-72 KB stages
@@ -162,8 +163,9 @@ __host__ __device__ constexpr int gemm_smem_bytes(int wt) {
 struct Sched {
     int M, n_mg, gsz, kb, n_ot, U, G, u0, u1;
     bool dbl;                 // double-buffered accumulator (gsz <= kDblTok)
-    int bh, spb, bslot, nbs;  // B ring: rows per CTA (widest group), slices per load, slot bytes, slots
-    __device__ __forceinline__ void init(int M_, int n_ptiles, int kb_, int n_pairs, int pair, int ring_bytes) {
+    int bh, spb, bpart, bslot, nbs;  // B ring: rows per CTA (widest group), k-slices per load, bytes per
+                                     // k-slice (all parts), slot bytes, slots
+    __device__ __forceinline__ void init(int M_, int n_ptiles, int kb_, int n_pairs, int pair, int ring_bytes, int xs) {
         M = M_;
         kb = kb_;
         n_mg = (M + kMaxTok - 1) / kMaxTok;
@@ -181,7 +183,8 @@ struct Sched {
         bh = ((gsz + 31) & ~31) >> 1;  // 16..128
         if (bh < 16) bh = 16;
         spb = x_slices(bh);
-        bslot = bh * 128 * spb;
+        bpart = bh * 128 * xs;
+        bslot = bpart * spb;
         nbs = ring_bytes / bslot;
         if (nbs > kMaxBSlots) nbs = kMaxBSlots;
     }
@@ -207,187 +210,6 @@ __device__ __forceinline__ Seg make_seg(const Sched &s, int u, int u1) {
     g.nmma = (g.ntok + 31) & ~31;  // MMA N: split evenly over the pair, 16-row multiples each
     g.half = g.nmma >> 1;          // tokens [m0 + rank*half, +half) are this CTA's B rows
     return g;
-}
-
-// ───────────── dequantization of one 64-wide k-slice of one weight row ─────────────
-// The slice is produced in 32 registers of f16 pairs in k order (register j holds k = 2j
-// in its low half and 2j + 1 in its high half), the layout of one TMEM lane of a 32-column
-// A operand; put() fills the 8 k-values of 16-byte chunk c.
-__device__ __forceinline__ void put(uint32_t (&o)[32], int c, uint4 v) {
-    o[4 * c] = v.x; o[4 * c + 1] = v.y; o[4 * c + 2] = v.z; o[4 * c + 3] = v.w;
-}
-__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
-__device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
-
-// Q4_K chunk layout (per 128 rows): [d,dmin f16 x2: 4 B/row][scales: 12 B/row at 512]
-// [qs: 128 B/row at 2048, 16-byte chunk c stored at c ^ (row & 7)].
-// Scales of the four sub-blocks one dequant set uses: set p dequantizes k-slices p and
-// p + 2, i.e. sub-blocks 2p, 2p + 1 (local 0, 1) and 2p + 4, 2p + 5 (local 2, 3).
-struct Q4KMeta {
-    __half2 d2;
-    __half2 sc[4], nsc[4], nmo[4];  // sc, -1024*sc, -(dmin*m) per sub-block, as f16 pairs
-};
-__device__ __forceinline__ void q4k_load_meta(const uint8_t *R, int r, int set, Q4KMeta &m) {
-    const uint32_t dm = *reinterpret_cast<const uint32_t *>(R + 4 * r);
-    const __half d = __ushort_as_half((unsigned short)(dm & 0xFFFF));
-    const float dmin = __half2float(__ushort_as_half((unsigned short)(dm >> 16)));
-    m.d2 = __halves2half2(d, d);
-    const uint32_t *sp = reinterpret_cast<const uint32_t *>(R + 512 + 12 * r);
-    const uint32_t s0 = sp[0], s1 = sp[1], s2 = sp[2];
-    // byte i of the 12 packed scale bytes (i may be a runtime value: no local array)
-    auto qb = [&](int i) -> int { return (int)(((i < 4 ? s0 : i < 8 ? s1 : s2) >> (8 * (i & 3))) & 0xFF); };
-#pragma unroll
-    for (int l = 0; l < 4; l++) {
-        // 6-bit scale / min of sub-block j (get_scale_min_k4 packing)
-        const int j = 2 * set + (l & 1) + 4 * (l >> 1);
-        int sc, mn;
-        if (l < 2) {  // j < 4
-            sc = qb(j) & 63;
-            mn = qb(j + 4) & 63;
-        } else {
-            sc = (qb(j + 4) & 0xF) | ((qb(j - 4) >> 6) << 4);
-            mn = (qb(j + 4) >> 4) | ((qb(j) >> 6) << 4);
-        }
-        const __half hs = __int2half_rn(sc);
-        m.sc[l] = __halves2half2(hs, hs);
-        const __half hn = __int2half_rn(-1024 * sc);
-        m.nsc[l] = __halves2half2(hn, hn);
-        const __half ho = __float2half_rn(-(dmin * (float)mn));
-        m.nmo[l] = __halves2half2(ho, ho);
-    }
-}
-// 4 nibbles (one byte lane each, values 0..15) -> two f16 pairs of q*sc*d - dmin*m.
-__device__ __forceinline__ void q4k_pair(uint32_t nib, const __half2 &sc, const __half2 &nsc, const __half2 &d2,
-                                         const __half2 &nmo, uint32_t &o01, uint32_t &o23) {
-    const uint32_t p01 = __byte_perm(nib, 0x64646464u, 0x4140);  // (1024 + q0, 1024 + q1)
-    const uint32_t p23 = __byte_perm(nib, 0x64646464u, 0x4342);
-    const __half2 t01 = __hfma2(u2h(p01), sc, nsc);  // q*sc, exact
-    const __half2 t23 = __hfma2(u2h(p23), sc, nsc);
-    o01 = h2u(__hfma2(t01, d2, nmo));
-    o23 = h2u(__hfma2(t23, d2, nmo));
-}
-// Slice s (k = 64s .. 64s+63) of row r: low nibbles of qs bytes 32s.. are sub-block 2s,
-// high nibbles sub-block 2s+1; lo = local meta index of sub-block 2s.
-__device__ __forceinline__ void q4k_slice(const uint8_t *R, int r, int s, int lo, const Q4KMeta &m, uint32_t (&o)[32]) {
-    const uint8_t *qrow = R + 2048 + 128 * r;
-    const uint4 qa = *reinterpret_cast<const uint4 *>(qrow + (((2 * s) ^ (r & 7)) << 4));
-    const uint4 qb = *reinterpret_cast<const uint4 *>(qrow + (((2 * s + 1) ^ (r & 7)) << 4));
-    const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-    const int jl = lo, jh = lo + 1;
-#pragma unroll
-    for (int c = 0; c < 4; c++) {
-        uint4 lo4, hi4;
-        const uint32_t w0 = w[2 * c], w1 = w[2 * c + 1];
-        q4k_pair(w0 & 0x0F0F0F0Fu, m.sc[jl], m.nsc[jl], m.d2, m.nmo[jl], lo4.x, lo4.y);
-        q4k_pair(w1 & 0x0F0F0F0Fu, m.sc[jl], m.nsc[jl], m.d2, m.nmo[jl], lo4.z, lo4.w);
-        q4k_pair((w0 >> 4) & 0x0F0F0F0Fu, m.sc[jh], m.nsc[jh], m.d2, m.nmo[jh], hi4.x, hi4.y);
-        q4k_pair((w1 >> 4) & 0x0F0F0F0Fu, m.sc[jh], m.nsc[jh], m.d2, m.nmo[jh], hi4.z, hi4.w);
-        put(o, c, lo4);
-        put(o, 4 + c, hi4);
-    }
-}
-
-// Q6_K chunk layout: [ql: 128 B/row, chunk c at c ^ (row & 7)]
-// [qh: 64 B/row at 16384, chunk c at c ^ ((row >> 1) & 3)][scales i8: 16 B/row at 24576]
-// [d f16: 2 B/row at 26624].
-// d * scale of the eight 16-element groups one dequant set uses: set p takes slices p
-// and p + 2, i.e. groups 4p .. 4p + 3 and 4p + 8 .. 4p + 11 (scale words p and p + 2).
-struct Q6KMeta {
-    __half2 ds[8];
-};
-__device__ __forceinline__ void q6k_load_meta(const uint8_t *R, int r, int set, Q6KMeta &m) {
-    const float d = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short *>(R + 26624 + 2 * r)));
-    const uint4 sv = *reinterpret_cast<const uint4 *>(R + 24576 + 16 * r);
-#pragma unroll
-    for (int h = 0; h < 2; h++) {
-        const int wi = set + 2 * h;  // scale word holding groups 4*wi .. 4*wi+3
-        const uint32_t w = wi == 0 ? sv.x : wi == 1 ? sv.y : wi == 2 ? sv.z : sv.w;
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const int sc = (int)(int8_t)((w >> (8 * i)) & 0xFF);
-            const __half hh = __float2half_rn(d * (float)sc);
-            m.ds[4 * h + i] = __halves2half2(hh, hh);
-        }
-    }
-}
-struct Q6KHalf {
-    uint32_t ql[16];
-    uint32_t qh[8];
-};
-__device__ __forceinline__ void q6k_load_half(const uint8_t *R, int r, int h, Q6KHalf &q) {
-    const uint8_t *qlrow = R + 128 * r;
-#pragma unroll
-    for (int c = 0; c < 4; c++) {
-        const uint4 v = *reinterpret_cast<const uint4 *>(qlrow + (((4 * h + c) ^ (r & 7)) << 4));
-        q.ql[4 * c] = v.x; q.ql[4 * c + 1] = v.y; q.ql[4 * c + 2] = v.z; q.ql[4 * c + 3] = v.w;
-    }
-    const uint8_t *qhrow = R + 16384 + 64 * r;
-#pragma unroll
-    for (int c = 0; c < 2; c++) {
-        const uint4 v = *reinterpret_cast<const uint4 *>(qhrow + (((2 * h + c) ^ ((r >> 1) & 3)) << 4));
-        q.qh[4 * c] = v.x; q.qh[4 * c + 1] = v.y; q.qh[4 * c + 2] = v.z; q.qh[4 * c + 3] = v.w;
-    }
-}
-// 4 six-bit values (byte lanes) -> two f16 pairs of d*sc*(q-32).
-__device__ __forceinline__ void q6k_pair(uint32_t q6, const __half2 &ds, uint32_t &o01, uint32_t &o23) {
-    const __half2 k1056 = __halves2half2(__int2half_rn(1056), __int2half_rn(1056));
-    const uint32_t p01 = __byte_perm(q6, 0x64646464u, 0x4140);
-    const uint32_t p23 = __byte_perm(q6, 0x64646464u, 0x4342);
-    o01 = h2u(__hmul2(__hsub2(u2h(p01), k1056), ds));
-    o23 = h2u(__hmul2(__hsub2(u2h(p23), k1056), ds));
-}
-__device__ __forceinline__ void q6k_slice(const Q6KHalf &q, int s, int lo, const Q6KMeta &m, uint32_t (&out)[32]) {
-    const int s2 = s & 1;
-#pragma unroll
-    for (int c = 0; c < 8; c++) {
-        const int hiq = c >= 4 ? 1 : 0;
-        const int shift = 4 * s2 + 2 * hiq;
-        uint4 o;
-#pragma unroll
-        for (int hw = 0; hw < 2; hw++) {
-            const uint32_t lw = q.ql[8 * hiq + 2 * (c & 3) + hw];
-            const uint32_t hwd = q.qh[2 * (c & 3) + hw];
-            const uint32_t nib = s2 ? ((lw >> 4) & 0x0F0F0F0Fu) : (lw & 0x0F0F0F0Fu);
-            const uint32_t q6 = nib | (((hwd >> shift) & 0x03030303u) << 4);
-            uint32_t a, b;
-            q6k_pair(q6, m.ds[lo + (c >> 1)], a, b);
-            if (hw == 0) { o.x = a; o.y = b; } else { o.z = a; o.w = b; }
-        }
-        put(out, c, o);
-    }
-}
-
-// Q8_0 chunk layout: [d f16 x 8: 16 B/row][qs: 256 B/row at 2048, chunk c at (c & 8) | ((c & 7) ^ (row & 7))].
-__device__ __forceinline__ void q80_slice(const uint8_t *R, int r, int s, uint32_t (&out)[32]) {
-    const uint4 dv = *reinterpret_cast<const uint4 *>(R + 16 * r);
-    const uint8_t *qrow = R + 2048 + 256 * r;
-    const __half2 k1152 = __halves2half2(__int2half_rn(1152), __int2half_rn(1152));
-#pragma unroll
-    for (int cc = 0; cc < 4; cc++) {
-        const int c = 4 * s + cc;
-        const uint4 v = *reinterpret_cast<const uint4 *>(qrow + (((c & 8) | ((c & 7) ^ (r & 7))) << 4));
-        const int blk = 2 * s + (cc >> 1);
-        const int wi = blk >> 1;  // may be a runtime value: select, no local array
-        const uint32_t dwd = wi == 0 ? dv.x : wi == 1 ? dv.y : wi == 2 ? dv.z : dv.w;
-        const unsigned short dbits = (unsigned short)((dwd >> (16 * (blk & 1))) & 0xFFFF);
-        const __half dh = __ushort_as_half(dbits);
-        const __half2 d2 = __halves2half2(dh, dh);
-        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-        for (int half_ = 0; half_ < 2; half_++) {
-            uint4 o;
-            uint32_t *op = &o.x;
-#pragma unroll
-            for (int i = 0; i < 2; i++) {
-                const uint32_t x = w[2 * half_ + i] ^ 0x80808080u;
-                const uint32_t p01 = __byte_perm(x, 0x64646464u, 0x4140);
-                const uint32_t p23 = __byte_perm(x, 0x64646464u, 0x4342);
-                op[2 * i] = h2u(__hmul2(__hsub2(u2h(p01), k1152), d2));
-                op[2 * i + 1] = h2u(__hmul2(__hsub2(u2h(p23), k1152), d2));
-            }
-            put(out, 2 * cc + half_, o);
-        }
-    }
 }
 
 // ───────────── epilogues ─────────────
@@ -451,15 +273,16 @@ __device__ __forceinline__ EpiRow epi_row(const EpiArgs &e, int tile, int row) {
 
 // Output staging: a chunk of 16 tokens x the tile's output features, one per epilogue
 // half, written by the row threads and stored to global memory as whole token rows.
+// SwiGLU rows hold the tile's 64 features as a pair-layout slice (64 hi f16 then 64 lo).
 template <int EPI> struct EpiFmt {
-    static constexpr int esize = (EPI == EPI_F32 || EPI == EPI_LOGITS) ? 4 : 2;
-    static constexpr int width = EPI == EPI_SWIGLU ? 64 : 128;  // output features per tile
-    static constexpr int row_bytes = esize * width;            // staging row pitch
+    static constexpr int esize = EPI == EPI_SWIGLU ? 2 : 4;
+    static constexpr int width = 128;                  // staged elements per token row
+    static constexpr int row_bytes = esize * width;    // staging row pitch
 };
 
 // Where one tile's token rows go.
 struct EpiDst {
-    char *base;      // the tile's first output feature in row 0
+    char *base;      // the tile's first output element in row 0
     long long ld;    // bytes between rows
     int nbytes;      // valid bytes per row (0: the tile is padding)
     bool by_pos;     // row index = the token's position (else m0 + token)
@@ -470,50 +293,62 @@ __device__ __forceinline__ EpiDst epi_dst(const EpiArgs &e, int tile) {
     constexpr int es = EpiFmt<EPI>::esize, W = EpiFmt<EPI>::width;
     EpiDst d{};
     long long ld_el;
-    int n_feat, f0;
+    int n_el, e0;
     if constexpr (EPI == EPI_QKV) {
         int lt;
         const int sec = qkv_section(e, tile, lt);
-        f0 = lt * 128;
+        e0 = lt * 128;
         char *b = reinterpret_cast<char *>(sec == 0 ? e.q_out : sec == 1 ? e.k_cache : e.v_cache);
-        d.base = b + (size_t)f0 * es;
+        d.base = b + (size_t)e0 * es;
         ld_el = sec == 0 ? e.ld_q : e.ld_kv;
-        n_feat = (sec == 0 ? e.n_q : e.n_kv) - f0;
+        n_el = (sec == 0 ? e.n_q : e.n_kv) - e0;
         d.by_pos = sec != 0;
-    } else {
-        f0 = tile * W;
-        d.base = reinterpret_cast<char *>(e.out) + (size_t)f0 * es;
+    } else if constexpr (EPI == EPI_SWIGLU) {
+        // tile t holds features [64 t, +64): pair slice t of the output rows
+        e0 = tile * 128;
+        d.base = reinterpret_cast<char *>(e.out) + (size_t)e0 * es;
         ld_el = e.ld;
-        n_feat = (EPI == EPI_SWIGLU ? e.n_valid / 2 : e.n_valid) - f0;
+        n_el = (e.n_valid / 2 - tile * 64) > 0 ? 128 : 0;  // feature counts are multiples of 64
+        d.by_pos = false;
+    } else {
+        e0 = tile * W;
+        d.base = reinterpret_cast<char *>(e.out) + (size_t)e0 * es;
+        ld_el = e.ld;
+        n_el = e.n_valid - e0;
         d.by_pos = EPI == EPI_LOGITS;
     }
     d.ld = ld_el * es;
-    d.nbytes = max(0, min(W, n_feat)) * es;
+    d.nbytes = max(0, min(W, n_el)) * es;
     d.vec = (reinterpret_cast<uintptr_t>(d.base) % 16 == 0) && (d.ld % 16 == 0);
     return d;
 }
 
 // Epilogue math of 16 consecutive tokens (tl0 .. tl0+15 of the segment) for this lane's
-// row, into the staging rows.  Called by all 32 lanes of a warp together (paired
+// row, into the staging rows.  v holds the raw accumulator (pre-scaled weights): the
+// first step multiplies by out_scale.  Called by all 32 lanes of a warp together (paired
 // epilogues exchange values with the neighbouring lane).  s_pos: positions of the
 // segment's tokens (shared memory).
 template <int EPI>
 __device__ __forceinline__ void epi_values(const EpiArgs &e, const EpiRow &r, const int *s_pos, int tl0, int ntok,
                                            float (&v)[16], uint8_t *stage) {
     constexpr int RB = EpiFmt<EPI>::row_bytes;
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] *= e.out_scale;
     if constexpr (EPI == EPI_F32 || EPI == EPI_LOGITS) {
 #pragma unroll
         for (int i = 0; i < 16; i++) reinterpret_cast<float *>(stage + i * RB)[r.col] = v[i];
-    } else if constexpr (EPI == EPI_F16) {
-#pragma unroll
-        for (int i = 0; i < 16; i++) reinterpret_cast<__half *>(stage + i * RB)[r.col] = __float2half_rn(v[i]);
     } else if constexpr (EPI == EPI_SWIGLU) {
 #pragma unroll
         for (int i = 0; i < 16; i++) {
             const float up = __shfl_xor_sync(0xffffffffu, v[i], 1);
             const float g = v[i];
-            const float h = __fdividef(g * up, 1.0f + __expf(-g));  // silu(g) * up
-            if (r.writer) reinterpret_cast<__half *>(stage + i * RB)[r.col] = __float2half_rn(h);
+            const float hv = (g * up) / (1.0f + expf(-g));  // silu(g) * up (ggml_silu, ggml_mul)
+            if (r.writer) {
+                const __half hh = __float2half_rn(hv);
+                __half *row = reinterpret_cast<__half *>(stage + i * RB);
+                row[r.col] = hh;
+                row[64 + r.col] = __float2half_rn(hv - __half2float(hh));
+            }
         }
     } else if constexpr (EPI == EPI_QKV) {
         if (r.sec < 2) {
@@ -529,13 +364,14 @@ __device__ __forceinline__ void epi_values(const EpiArgs &e, const EpiRow &r, co
                 const float2 cs = csv[i];
                 const float x = v[i] + r.bias;
                 const float partner = __shfl_xor_sync(0xffffffffu, x, 1);
+                // ggml_rope_ext NEOX: (x0 cos - x1 sin, x0 sin + x1 cos)
                 const float o = r.bpair == 0 ? (x * cs.x - partner * cs.y) : (partner * cs.y + x * cs.x);
-                if (r.col < 128) reinterpret_cast<__half *>(stage + i * RB)[r.col] = __float2half_rn(o);
+                if (r.col < 128) reinterpret_cast<float *>(stage + i * RB)[r.col] = o;
             }
         } else {
 #pragma unroll
             for (int i = 0; i < 16; i++)
-                if (r.col < 128) reinterpret_cast<__half *>(stage + i * RB)[r.col] = __float2half_rn(v[i] + r.bias);
+                if (r.col < 128) reinterpret_cast<float *>(stage + i * RB)[r.col] = v[i] + r.bias;
         }
     }
 }
@@ -546,23 +382,24 @@ template <int EPI>
 __device__ __forceinline__ void epi_copyout(const EpiDst &d, const int *s_pos, int m0, int tl0, int ntok,
                                             const uint8_t *stage, int tid) {
     constexpr int es = EpiFmt<EPI>::esize, RB = EpiFmt<EPI>::row_bytes;
-    constexpr int LPR = RB / 16, RPW = 32 / LPR;  // lanes per row, rows per warp pass
+    constexpr int LPR = RB / 16, RPW = LPR >= 32 ? 1 : 32 / LPR;  // lanes per row, rows per warp pass
     const int w = tid >> 5, lane = tid & 31;
-    const int off = (lane % LPR) * 16;
-    if (off >= d.nbytes) return;
-    for (int i = w * RPW + lane / LPR; i < 16; i += 4 * RPW) {
-        const int t = tl0 + i;
-        if (t >= ntok) break;
-        const long long rowi = d.by_pos ? (long long)s_pos[t] : (long long)(m0 + t);
-        char *dst = d.base + rowi * d.ld + off;
-        const uint8_t *src = stage + i * RB + off;
-        if (d.vec && off + 16 <= d.nbytes) {
-            *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<const uint4 *>(src);
-        } else {
-            const int nb = min(16, d.nbytes - off);
-            for (int b = 0; b < nb; b += es) {
-                if constexpr (es == 4) *reinterpret_cast<float *>(dst + b) = *reinterpret_cast<const float *>(src + b);
-                else *reinterpret_cast<__half *>(dst + b) = *reinterpret_cast<const __half *>(src + b);
+    for (int off = (lane % LPR) * 16; off < RB; off += 32 * 16) {
+        if (off >= d.nbytes) return;
+        for (int i = w * RPW + (LPR >= 32 ? 0 : lane / LPR); i < 16; i += 4 * RPW) {
+            const int t = tl0 + i;
+            if (t >= ntok) break;
+            const long long rowi = d.by_pos ? (long long)s_pos[t] : (long long)(m0 + t);
+            char *dst = d.base + rowi * d.ld + off;
+            const uint8_t *src = stage + i * RB + off;
+            if (d.vec && off + 16 <= d.nbytes) {
+                *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<const uint4 *>(src);
+            } else {
+                const int nb = min(16, d.nbytes - off);
+                for (int b = 0; b < nb; b += es) {
+                    if constexpr (es == 4) *reinterpret_cast<float *>(dst + b) = *reinterpret_cast<const float *>(src + b);
+                    else *reinterpret_cast<__half *>(dst + b) = *reinterpret_cast<const __half *>(src + b);
+                }
             }
         }
     }
@@ -577,28 +414,34 @@ __device__ __forceinline__ void epi_copyout(const EpiDst &d, const int *s_pos, i
 // Barriers the MMA waits on (full_a, full_b, acc_empty) live in the even CTA; the odd
 // CTA's loads and arrivals reach them through cluster addresses.
 //
-// Shared memory (per CTA): [A ring (F16 weights only): a_stages x 16 KB][B ring][raw ring]
-// [barriers][token positions][contributor offsets].  Slice i (64 k) of the CTA's unit
-// range uses A stage i % a_stages (TMEM columns kTmemA + 32 stage for quantized weights)
-// and part i % spb of B slot (i / spb) % nbs.
+// Shared memory (per CTA): [A ring (f16 weight tiles only): a_stages x a_stage_bytes]
+// [B ring][raw ring][barriers][token positions][contributor offsets].  Slice i (64 k) of
+// the CTA's unit range uses A stage i % a_stages (TMEM columns kTmemA + 64 stage for
+// quantized weights) and part i % spb of B slot (i / spb) % nbs; a part holds the
+// slice's XS sub-slices (hi, then lo).
+//
+// MMAs per slice: W_hi.X_hi, W_hi.X_lo (XS = 2), W_lo.X_hi (weights with a lo part).
 //
 // Warps (warp_role): w0 activation producer, w1 MMA issuer (even CTA) + TMEM owner, w2
-// weight-chunk producer (F16 weights: A-tile TMA producer), w3 relay, w4-w11 dequantizers
+// weight-chunk producer (f16 weights: A-tile TMA producer), w3 relay, w4-w11 dequantizers
 // (two sets of four; thread = weight row = TMEM lane), w12-w19 epilogue (thread = TMEM
 // lane; w12-15 and w16-19 take alternate 16-column chunks).
-template <int WT, int EPI>
+template <int WT, int EPI, int XS>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     dq_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ XMaps xm, GemmParams p) {
     constexpr int RAWB = raw_chunk_bytes(WT);
     constexpr int NA = a_stages(WT), NRAW = raw_stages(WT), BRING = b_ring_bytes(WT), AR = a_ring_bytes(WT);
+    constexpr int ASB = a_stage_bytes(WT);
     constexpr int CPR = raw_cpr(WT), RSB = CPR * RAWB;  // chunks and bytes per raw stage
+    static_assert(XS == 1 || XS == 2, "activation parts");
+    static_assert(NA == 2, "dequantizer set p fills A stage p");
     // The relay frees the B slot of slice j - NA while it handles slice j, after waiting
-    // for the B loads up to slice j - 1: with one slice per load (the widest group, 12 KB
-    // loads) the producer needs 2 + (NA - 1) slots not to wait on itself.
-    static_assert(BRING / (kMaxTok / 2 * 128) >= 2 + (NA - 1), "B ring too shallow for the A ring");
+    // for the B loads up to slice j - 1: with one slice per load (the widest group, 16 or
+    // 32 KB loads) the producer needs 2 + (NA - 1) slots not to wait on itself.
+    static_assert(BRING / (kMaxTok / 2 * 128 * XS) >= 2 + (NA - 1), "B ring too shallow for the A ring");
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t *aring = smem;  // F16 weights only
+    uint8_t *aring = smem;  // f16 weight tiles only
     uint8_t *bring = smem + AR;
     uint8_t *raw = bring + BRING;
     uint8_t *epi_stage = raw + NRAW * RSB;  // [2 halves][kEpiStageBytes]
@@ -618,10 +461,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     // the next kernel of the stream may be scheduled now; it waits for this grid itself
     griddep_launch_dependents();
     if (threadIdx.x == 0) {
-        GEMM_STAMP(p, 0);
         for (int i = 0; i < NA; i++) {
-            // both CTAs' relays + F16: the expect_tx / else four dequant warps per CTA
-            mbar_init(&full_a[i], WT == W_F16 ? 3 : 10);
+            // both CTAs' relays + f16 tiles: the expect_tx / else four dequant warps per CTA
+            mbar_init(&full_a[i], w_smem(WT) ? 3 : 10);
             mbar_init(&empty_a[i], 1);                   // the paired MMA's commit
         }
         for (int i = 0; i < kMaxBSlots; i++) {
@@ -642,7 +484,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         fence_barrier_init();
     }
     const int role = warp_role(warp);
-    if (WT == W_F16 && role == R_WPROD && lane == 0) prefetch_tmap(&tm_w);
+    if (w_smem(WT) && role == R_WPROD && lane == 0) prefetch_tmap(&tm_w);
     if (role == R_MMA) {
         tmem_alloc2(tmem_holder, 512);
         tmem_relinquish2();
@@ -661,7 +503,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     // wait for the activations.
     const int M = *reinterpret_cast<volatile const int *>(p.m_dev);
     Sched S;
-    S.init(M, p.n_tiles >> 1, p.kb, n_pairs, pair, BRING);
+    S.init(M, p.n_tiles >> 1, p.kb, n_pairs, pair, BRING, XS);
     const int NBS = S.nbs;
     // barriers of the even CTA as cluster addresses
     const uint32_t full_a0 = mapa_shared(full_a, 0), acc_empty0 = mapa_shared(acc_empty, 0);
@@ -672,7 +514,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         //    also streams the weights and handles only a few operations per microsecond. ──
         griddep_wait();  // the activations are the previous kernel's output
         if (lane == 0) {
-            GEMM_STAMP(p, 1);
             if (*reinterpret_cast<volatile const int *>(p.m_dev) != M) atomicCAS(p.err, 0, kErrTimeout + 14);
             const CUtensorMap *xmap = &xm.m[S.bh / 16 - 1];
             int ob = 0, sl = 0;  // B loads issued, slot of the next one
@@ -683,17 +524,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 const int row0 = g.m0 + (int)rank * g.half;
                 for (int kbi = g.k0; kbi < g.k1 && ok; kbi++) {
                     for (int s = 0; s < 4; s += S.spb) {
-                        if (!(ok = mbar_wait(&empty_b[sl], ph ^ 1, abort_flag, p.err, kErrTimeout + 2))) break;
+                        if (!(ok = mbar_wait(&empty_b[sl], ph ^ 1, abort_flag, p.err, kErrTimeout + 2, p.timeout_ns))) break;
                         mbar_arrive_expect_tx(&full_b[sl], S.bslot);
-                        tma_load_3d(bring + sl * S.bslot, xmap, 0, row0, kbi * 4 + s, &full_b[sl]);
-                        GEMM_EVENT(p, 0, ob);
+                        tma_load_3d(bring + sl * S.bslot, xmap, 0, row0, XS * (kbi * 4 + s), &full_b[sl]);
                         ob++;
                         if (++sl == NBS) { sl = 0; ph ^= 1; }
                     }
                 }
                 u += g.k1 - g.k0;
             }
-            GEMM_STAMP(p, 2);
             if (!ok) {
                 // let the copies in flight land before the CTA can exit
                 for (int i = (ob > NBS ? ob - NBS : 0); i < ob; i++) spin_bounded(&full_b[i % NBS], (i / NBS) & 1);
@@ -701,7 +540,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
     } else if (role == R_WPROD) {
-        if constexpr (WT != W_F16) {
+        if constexpr (!w_smem(WT)) {
             // ── weight-chunk producer: this CTA's re-tiled chunk (128 rows x 256 k) per k-block ──
             if (lane == 0) {
                 auto chunk = [&](int u) {
@@ -712,11 +551,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 bool ok = true;
                 for (int u = S.u0; u < S.u1 && ok; u += CPR) {
                     const int r = rit % NRAW;
-                    if (!(ok = mbar_wait(&raw_empty[r], ((rit / NRAW) & 1) ^ 1, abort_flag, p.err, kErrTimeout + 1))) break;
+                    if (!(ok = mbar_wait(&raw_empty[r], ((rit / NRAW) & 1) ^ 1, abort_flag, p.err, kErrTimeout + 1, p.timeout_ns))) break;
                     const int nch = min(CPR, S.u1 - u);
                     mbar_arrive_expect_tx(&raw_full[r], nch * RAWB);
                     for (int c = 0; c < nch; c++) bulk_g2s(raw + r * RSB + c * RAWB, chunk(u + c), RAWB, &raw_full[r]);
-                    GEMM_EVENT(p, 1, rit);
                     rit++;
                 }
                 if (!ok)
@@ -724,7 +562,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         spin_bounded(&raw_full[i % NRAW], (i / NRAW) & 1);
             }
         } else {
-            // ── F16 weights: A-tile TMA producer (completions counted on the even CTA) ──
+            // ── f16 weight tiles: A-tile TMA producer (completions counted on the even CTA);
+            //    W_F32 stages hold the hi tile, then the lo tile (rows lo_row + ...) ──
             if (lane == 0) {
                 int it = 0;
                 bool ok = true;
@@ -733,10 +572,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     for (int kbi = g.k0; kbi < g.k1 && ok; kbi++) {
                         for (int s = 0; s < 4; s++) {  // one stage = one k-slice
                             const int st = it % NA;
-                            if (!(ok = mbar_wait(&empty_a[st], ((it / NA) & 1) ^ 1, abort_flag, p.err, kErrTimeout + 11))) break;
-                            if (rank == 0) mbar_arrive_expect_tx(&full_a[st], 2 * kABytes);
-                            tma_load_2d_pair(aring + st * kABytes, &tm_w, kbi * 256 + s * 64, (2 * g.pt + (int)rank) * 128,
-                                             full_a0 + 8 * st);
+                            if (!(ok = mbar_wait(&empty_a[st], ((it / NA) & 1) ^ 1, abort_flag, p.err, kErrTimeout + 11, p.timeout_ns))) break;
+                            if (rank == 0) mbar_arrive_expect_tx(&full_a[st], 2 * ASB);
+                            const int row = (2 * g.pt + (int)rank) * 128;
+                            tma_load_2d_pair(aring + st * ASB, &tm_w, kbi * 256 + s * 64, row, full_a0 + 8 * st);
+                            if constexpr (WT == W_F32)
+                                tma_load_2d_pair(aring + st * ASB + kSliceBytes, &tm_w, kbi * 256 + s * 64, p.lo_row + row,
+                                                 full_a0 + 8 * st);
                             it++;
                         }
                     }
@@ -755,61 +597,53 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         // ── MMA issuer (even CTA) ──
         // Every instruction on this thread's path between two slices leaves the tensor
         // pipe idle (the queue holds about one MMA), so the per-slice work is only: wait
-        // for the stage, fence, four MMAs, commit.  Each unit is one k-block = four
-        // slices, so the A stage of slice s2 is s2 (a_stages == 4) and its barrier parity
-        // flips per k-block; the four B descriptors are computed once per k-block.
-        static_assert(NA == 4, "one A stage per k-slice of a k-block");
+        // for the stage, fence, the slice's MMAs, commit.  Each unit is one k-block = four
+        // slices; slice s2 uses A stage s2 & 1, whose barrier completes twice per k-block,
+        // so its parity is s2 >> 1; the B descriptors are computed once per k-block.
         if (lane == 0 && rank == 0) {
-            int si = 0, ka = 0;  // accumulator segments, k-blocks consumed
+            int si = 0;  // accumulator segments
             bool ok = true, issued = false;
-#ifdef DFB_GEMM_TRACE
-            long long tr_nwait = 0, tr_wcyc = 0, tr_t0 = clock64();
-#endif
             const uint64_t bdesc0 = sw128_desc(smem_u32(bring)), adesc0 = sw128_desc(smem_u32(aring));
-            const int lg_spb = S.spb == 1 ? 0 : S.spb == 2 ? 1 : 2;  // B slices per ring slot: 1, 2 or 4
-            const uint32_t bpart_bytes = S.bh * 128;
+            const int lg_spb = S.spb == 1 ? 0 : S.spb == 2 ? 1 : 2;  // k-slices per ring slot: 1, 2 or 4
+            const uint32_t bsub = S.bh * 128;  // bytes of one part (hi or lo) of a k-slice
             int bslot = 0;  // ring slot of the first slice of the next k-block
             for (int u = S.u0; u < S.u1 && ok;) {
                 const Seg g = make_seg(S, u, S.u1);
                 const int acc = S.acc_of(si);
-                if (!(ok = mbar_wait(&acc_empty[acc], (S.acc_uses(si) & 1) ^ 1, abort_flag, p.err, kErrTimeout + 3))) break;
+                if (!(ok = mbar_wait(&acc_empty[acc], (S.acc_uses(si) & 1) ^ 1, abort_flag, p.err, kErrTimeout + 3, p.timeout_ns))) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * kDblTok;
                 const uint32_t idesc = idesc_f16(256, (uint32_t)g.nmma);
                 uint32_t accum = 0;
-                for (int kbi = g.k0; kbi < g.k1; kbi++, ka++) {
+                for (int kbi = g.k0; kbi < g.k1; kbi++) {
+                    // (the ring may hold fewer slots than a k-block's four loads: wrap by modulo)
                     uint64_t bd[4];
 #pragma unroll
                     for (int s2 = 0; s2 < 4; s2++) {
-                        int sl = bslot + (s2 >> lg_spb);
-                        if (sl >= NBS) sl -= NBS;
-                        bd[s2] = bdesc0 + (uint64_t)((sl * S.bslot + (s2 & (S.spb - 1)) * bpart_bytes) >> 4);
+                        const int sl = (bslot + (s2 >> lg_spb)) % NBS;
+                        bd[s2] = bdesc0 + (uint64_t)((sl * S.bslot + (s2 & (S.spb - 1)) * S.bpart) >> 4);
                     }
-                    bslot += 4 >> lg_spb;
-                    if (bslot >= NBS) bslot -= NBS;
-                    const uint32_t par = ka & 1;
+                    bslot = (bslot + (4 >> lg_spb)) % NBS;
 #pragma unroll
                     for (int s2 = 0; s2 < 4; s2++) {
+                        const int st = s2 & 1;
                         // full_a also carries the relays' arrivals: this stage's B rows have landed
-#ifdef DFB_GEMM_TRACE
-                        if (!mbar_try_wait(&full_a[s2], par)) {
-                            const long long w0 = clock64();
-                            ok = mbar_wait(&full_a[s2], par, abort_flag, p.err, kErrTimeout + 5);
-                            tr_nwait++;
-                            tr_wcyc += clock64() - w0;
-                        }
-                        if (!ok) break;
-#else
-                        if (!(ok = mbar_wait(&full_a[s2], par, abort_flag, p.err, kErrTimeout + 5))) break;
-#endif
+                        if (!(ok = mbar_wait(&full_a[st], (uint32_t)(s2 >> 1), abort_flag, p.err, kErrTimeout + 5, p.timeout_ns))) break;
                         tc_fence_after();
-                        if constexpr (WT == W_F16)
-                            mma2_f16_ss_k64(d_tmem, adesc0 + (uint64_t)((s2 * kABytes) >> 4), bd[s2], idesc, accum);
-                        else
-                            mma2_f16_ts_k64(d_tmem, tmem_base + kTmemA + s2 * kTmemAStage, bd[s2], idesc, accum);
+                        const uint64_t bhi = bd[s2], blo = bd[s2] + (uint64_t)(bsub >> 4);
+                        if constexpr (w_smem(WT)) {
+                            const uint64_t ahi = adesc0 + (uint64_t)((st * ASB) >> 4);
+                            mma2_f16_ss_k64(d_tmem, ahi, bhi, idesc, accum);
+                            if constexpr (XS == 2) mma2_f16_ss_k64(d_tmem, ahi, blo, idesc, 1);
+                            if constexpr (w_split(WT)) mma2_f16_ss_k64(d_tmem, ahi + (uint64_t)(kSliceBytes >> 4), bhi, idesc, 1);
+                        } else {
+                            const uint32_t ahi = tmem_base + kTmemA + st * kTmemAStage;
+                            mma2_f16_ts_k64(d_tmem, ahi, bhi, idesc, accum);
+                            if constexpr (XS == 2) mma2_f16_ts_k64(d_tmem, ahi, blo, idesc, 1);
+                            mma2_f16_ts_k64(d_tmem, ahi + kTmemALo, bhi, idesc, 1);
+                        }
                         accum = 1;
-                        mma2_commit_mc(&empty_a[s2], 0x3);
-                        GEMM_EVENT(p, 4, 4 * ka + s2);
+                        mma2_commit_mc(&empty_a[st], 0x3);
                     }
                     issued = true;
                     if (!ok) break;
@@ -819,13 +653,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 si++;
                 u += g.k1 - g.k0;
             }
-            GEMM_STAMP(p, 3);
-#ifdef DFB_GEMM_TRACE
-            if (p.trace && blockIdx.x < 4) {  // full_a waits that had to block: count, cycles; loop cycles; slices
-                unsigned long long *tp = p.trace + 256 * 16 + ((size_t)blockIdx.x * 8 + 5) * 64 + 56;
-                tp[0] = tr_nwait; tp[1] = tr_wcyc; tp[2] = clock64() - tr_t0; tp[3] = 4 * ka;
-            }
-#endif
             if (issued) {
                 // every MMA must have retired before TMEM is released
                 mma2_commit(drain);
@@ -855,7 +682,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 if (j >= NA) {
                     // MMA of slice j - NA done (phase (j - NA) / NA of empty_a[j % NA]); its B
                     // slot is free once the last slice of the slot's load is done
-                    if (!(ok = mbar_wait(&empty_a[j % NA], ((j / NA) & 1) ^ 1, abort_flag, p.err, kErrTimeout + 12))) break;
+                    if (!(ok = mbar_wait(&empty_a[j % NA], ((j / NA) & 1) ^ 1, abort_flag, p.err, kErrTimeout + 12, p.timeout_ns))) break;
                     if (++eo_part == spb) {
                         eo_part = 0;
                         mbar_arrive(&empty_b[eo_sl]);
@@ -864,7 +691,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 }
                 if (j < n_it) {
                     if (fo_part == 0)
-                        if (!(ok = mbar_wait(&full_b[fo_sl], fo_ph, abort_flag, p.err, kErrTimeout + 4))) break;
+                        if (!(ok = mbar_wait(&full_b[fo_sl], fo_ph, abort_flag, p.err, kErrTimeout + 4, p.timeout_ns))) break;
                     mbar_arrive_cluster(full_a0 + 8 * (j % NA));
                     if (++fo_part == spb) {
                         fo_part = 0;
@@ -877,7 +704,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     } else if (role == R_DEQ) {
         // ── dequantizers: thread = weight row of this CTA's tile; set p takes slices
         //    p and p + 2 of every k-block ──
-        if constexpr (WT != W_F16) {
+        if constexpr (!w_smem(WT)) {
             const int di = deq_index(warp);
             const int set = di >> 2;
             const int r = (di & 3) * 32 + lane;
@@ -898,7 +725,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             // phase cannot advance further without this warp), for acquire ordering.
             auto wait_warp = [&](uint64_t *bar, uint32_t parity, int code) {
                 int okw = 1;
-                if (lane == 0) okw = mbar_wait(bar, parity, abort_flag, p.err, code);
+                if (lane == 0) okw = mbar_wait(bar, parity, abort_flag, p.err, code, p.timeout_ns);
                 const bool okb = __shfl_sync(0xffffffffu, okw, 0) != 0;
                 if (okb) (void)mbar_try_wait(bar, parity);
                 return okb;
@@ -915,49 +742,35 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     if (rit % CPR == 0) {
                         ok = wait_warp(&raw_full[rs], (rst / NRAW) & 1, kErrTimeout + 6);
                         if (!ok) break;
-                        if (r == 0 && set == 0) GEMM_EVENT(p, 2, rst);
                     }
                     const uint8_t *R = raw + rs * RSB + (rit % CPR) * RAWB;
-                    // this set's k-slices of the k-block: set and set + 2, one A stage each
-                    uint32_t o[32];
-                    if constexpr (WT == W_Q4K) {
-                        Q4KMeta meta;
-                        q4k_load_meta(R, r, set, meta);
-                        #pragma unroll
-                        for (int h = 0; h < 2; h++) {
-                            const int sl = set + 2 * h, ia = 4 * rit + sl;
-                            q4k_slice(R, r, sl, 2 * h, meta, o);
-                            if (!(ok = wait_a(ia))) break;
-                            tc_fence_after();  // after the MMA that read this stage
-                            if (r == 0 && ia < 32) GEMM_EVENT(p, 7, ia);
-                            tmem_st32(a_lane + (ia % NA) * kTmemAStage, o);
-                            publish(ia % NA);
-                            if (r == 0) GEMM_EVENT(p, 3, ia);
-                        }
-                    } else if constexpr (WT == W_Q6K) {
-                        Q6KMeta meta;
-                        q6k_load_meta(R, r, set, meta);
-                        #pragma unroll
-                        for (int h = 0; h < 2; h++) {
-                            const int sl = set + 2 * h, ia = 4 * rit + sl;
-                            Q6KHalf qv;
-                            q6k_load_half(R, r, h, qv);  // slice sl uses half sl / 2 = h of ql / qh
-                            q6k_slice(qv, sl, 4 * h, meta, o);
-                            if (!(ok = wait_a(ia))) break;
-                            tc_fence_after();
-                            tmem_st32(a_lane + (ia % NA) * kTmemAStage, o);
-                            publish(ia % NA);
-                        }
-                    } else {
-                        #pragma unroll
-                        for (int h = 0; h < 2; h++) {
-                            const int sl = set + 2 * h, ia = 4 * rit + sl;
-                            q80_slice(R, r, sl, o);
-                            if (!(ok = wait_a(ia))) break;
-                            tc_fence_after();
-                            tmem_st32(a_lane + (ia % NA) * kTmemAStage, o);
-                            publish(ia % NA);
-                        }
+                    // this set's k-slices of the k-block: set and set + 2, both into A stage
+                    // `set`; each slice in two halves of 32 k (hi and lo parts, 16 columns each)
+                    [[maybe_unused]] Q4KMeta m4;
+                    [[maybe_unused]] Q6KMeta m6;
+                    if constexpr (WT == W_Q4K) q4k_load_meta(R, r, set, p.wscale, m4);
+                    if constexpr (WT == W_Q6K) q6k_load_meta(R, r, set, p.wscale, m6);
+                    auto deq = [&](int hs, int hh, uint32_t (&hi)[16], uint32_t (&lo)[16]) {
+                        const int sl = set + 2 * hs;
+                        if constexpr (WT == W_Q4K) q4k_half(R, r, sl, hh, m4.dsc[2 * hs + hh], m4.nm[2 * hs + hh], hi, lo);
+                        else if constexpr (WT == W_Q6K)
+                            q6k_half(R, r, sl, hh, m6.ds[4 * hs + 2 * hh], m6.ds[4 * hs + 2 * hh + 1], hi, lo);
+                        else q80_half(R, r, sl, hh, p.wscale, hi, lo);
+                    };
+#pragma unroll
+                    for (int hs = 0; hs < 2; hs++) {
+                        const int ia = 4 * rit + set + 2 * hs;
+                        const uint32_t at = a_lane + (uint32_t)(set * kTmemAStage);
+                        uint32_t hi[16], lo[16];
+                        deq(hs, 0, hi, lo);
+                        if (!(ok = wait_a(ia))) break;
+                        tc_fence_after();  // after the MMA that read this stage
+                        tmem_st16(at, hi);
+                        tmem_st16(at + kTmemALo, lo);
+                        deq(hs, 1, hi, lo);
+                        tmem_st16(at + 16, hi);
+                        tmem_st16(at + kTmemALo + 16, lo);
+                        publish(set);
                     }
                     __syncwarp();
                     if (lane == 0 && (rit % CPR == CPR - 1 || rit == n_units - 1)) mbar_arrive(&raw_empty[rs]);
@@ -995,11 +808,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const int tile = 2 * g.pt + (int)rank;
             const int acc = S.acc_of(si);
             // one thread waits, the barrier hands the outcome to the whole group
-            if (et == 0) *okflag = mbar_wait(&acc_full[acc], S.acc_uses(si) & 1, abort_flag, p.err, kErrTimeout + 8) ? 1 : 0;
+            if (et == 0) *okflag = mbar_wait(&acc_full[acc], S.acc_uses(si) & 1, abort_flag, p.err, kErrTimeout + 8, p.timeout_ns) ? 1 : 0;
             named_bar_sync(1, kEpiThreads);
             ok = *okflag != 0;
             if (!ok) break;
-            if (et == 0 && si < 4) GEMM_STAMP(p, 4 + 2 * si);
             tc_fence_after();
             const uint32_t taddr = tmem_base + ((uint32_t)(32 * q) << 16) + acc * kDblTok;
             const bool whole = g.k0 == 0 && g.k1 == S.kb;
@@ -1026,7 +838,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             } else {
                 const int slot = g.ot == first_ot ? 0 : 1;
                 float *wsl = p.ws + ((size_t)blockIdx.x * 2 + slot) * kWsTile;
-                if (et == 0) GEMM_EVENT(p, 6, 5 * si + 0);
                 for (int c0 = 16 * half; c0 < g.nmma; c0 += 32) {
                     uint32_t u16[16];
                     tmem_ld16(taddr + c0, u16);
@@ -1044,10 +855,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 if (et == 0) atomicAdd(&p.tile_cnt[2 * g.ot + rank], 1);
                 if (slot == 0) split_u0 = u;
                 else split_u1 = u;
-                if (et == 0) GEMM_EVENT(p, 6, 5 * si + 3);
             }
             named_bar_sync(1, kEpiThreads);  // okflag / s_pos are reused by the next segment
-            if (et == 0 && si < 4) GEMM_STAMP(p, 5 + 2 * si);
             si++;
             u += g.k1 - g.k0;
         }
@@ -1079,14 +888,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             if (et == 0) {
                 int okw = nc <= kMaxContrib;  // the launcher keeps nc <= kMaxContrib
                 if (!okw) atomicCAS(p.err, 0, kErrTimeout + 9);
-                else okw = wait_count(cntp, nc, abort_flag, p.err, kErrTimeout + 13);
+                else okw = wait_count(cntp, nc, abort_flag, p.err, kErrTimeout + 13, p.timeout_ns);
                 *okflag = okw;
                 if (okw) fence_proxy_async_all();  // the partials, seen here, before the bulk reads
             }
             named_bar_sync(1, kEpiThreads);
             ok = *okflag != 0;
             if (!ok) break;
-            if (et == 0) GEMM_EVENT(p, 6, 5 * si + 0);
             const EpiRow er = epi_row<EPI>(p.epi, tile, row);
             const EpiDst dd = epi_dst<EPI>(p.epi, tile);
             const bool staged = nc * kChunkBytes <= kStageBytes;
@@ -1099,12 +907,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         for (int c = 0; c < nc; c++)
                             bulk_g2s(smem + (size_t)c * nr * kChunkBytes, p.ws + s_contrib[c] + (size_t)r0 * 2048,
                                      (uint32_t)(nr * kChunkBytes), fix_bar);
-                        *okflag = mbar_wait(fix_bar, fix_phase, abort_flag, p.err, kErrTimeout + 10) ? 1 : 0;
+                        *okflag = mbar_wait(fix_bar, fix_phase, abort_flag, p.err, kErrTimeout + 10, p.timeout_ns) ? 1 : 0;
                     }
                     fix_phase ^= 1;
                     named_bar_sync(1, kEpiThreads);
                     if (!*okflag) { ok = false; break; }
-                    if (et == 0 && r0 == ch0) GEMM_EVENT(p, 6, 5 * si + 1);
                 }
                 for (int ch = r0 + half; ch < r0 + nr; ch += 2) {
                     float v[16];
@@ -1139,14 +946,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 // staging area before the async-proxy writes
                 named_bar_sync(1, kEpiThreads);
                 if (et == 0) fence_proxy_async_smem();
-                if (et == 0 && r0 == ch0) GEMM_EVENT(p, 6, 5 * si + 2);
             }
             if (!ok) break;
             // departure: the last of the nc contributors resets the counter for the next launch
             if (et == 0) {
                 const int old = atomicAdd(cntp, 1);
                 if (old == 2 * nc - 1) *cntp = 0;
-                GEMM_EVENT(p, 6, 5 * si + 4);
             }
             named_bar_sync(1, kEpiThreads);  // s_contrib / s_pos / okflag reused
             si++;
@@ -1156,7 +961,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     tc_fence_before();
     __syncthreads();
     cluster_sync();  // no remote arrival or copy of either CTA is still in flight
-    if (threadIdx.x == 0) GEMM_STAMP(p, 12);
     if (role == R_MMA) {
         tc_fence_after();
         tmem_dealloc2(tmem_base, 512);

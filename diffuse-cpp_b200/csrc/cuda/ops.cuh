@@ -119,11 +119,28 @@ __device__ __forceinline__ float block_sum(float v, float *red) {
     return r;
 }
 
-// h[a] = f16(x[a] * rsqrt(mean(x[a]^2) + eps) * w)  (ggml_rms_norm + ggml_mul, graph.cpp:51-58),
-// with the residual add of the projection before it folded in when y is given:
-// x[a] += y[a] first (ggml_add, graph.cpp:123 / :142), written back as the new residual
-// stream.  One block per row; 8 elements per thread per step (float4 loads, one 16-byte
-// f16 store); each thread re-reads in the second pass only the elements it wrote.
+// Pair layout of GEMM activations: per 64-wide slice of a row, 64 hi f16 values then the
+// 64 lo parts (v - hi), so that hi + lo carries ~22 significant bits of the f32 value.
+// Eight consecutive values (one slice-aligned group) as two 16-byte stores.
+__device__ __forceinline__ void store_pair8(__half *row, int i, const float (&v)[8]) {
+    uint32_t hw[4], lw[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+        const __half2 hh = __floats2half2_rn(v[2 * e], v[2 * e + 1]);
+        const float2 hf = __half22float2(hh);
+        hw[e] = h2u_(hh);
+        lw[e] = h2u_(__floats2half2_rn(v[2 * e] - hf.x, v[2 * e + 1] - hf.y));
+    }
+    __half *dst = row + (i >> 6) * 128 + (i & 63);
+    *reinterpret_cast<uint4 *>(dst) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    *reinterpret_cast<uint4 *>(dst + 64) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+}
+
+// h[a] = x[a] * (1 / sqrt(mean(x[a]^2) + eps)) * w  (ggml_rms_norm + ggml_mul,
+// graph.cpp:51-58) as pair rows (row length 2d), with the residual add of the projection
+// before it folded in when y is given: x[a] += y[a] first (ggml_add, graph.cpp:123 /
+// :142), written back as the new residual stream.  One block per row; 8 elements per
+// thread step (float4 loads); d is a multiple of 64.
 __global__ void __launch_bounds__(256) rmsnorm_kernel(float *__restrict__ x, const float *__restrict__ y,
                                                       const float *__restrict__ w, int d, float eps,
                                                       const int *__restrict__ cnt, __half *__restrict__ h) {
@@ -134,49 +151,32 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(float *__restrict__ x, con
     if (a >= cnt[CNT_M]) return;
     float *xr = x + (size_t)a * d;
     const float *yr = y ? y + (size_t)a * d : nullptr;
-    __half *hr = h + (size_t)a * d;
+    __half *hr = h + (size_t)a * 2 * d;
     float ss = 0.f;
-    if ((d & 7) == 0) {
-        for (int i = threadIdx.x * 8; i < d; i += blockDim.x * 8) {
-            float4 v0 = *reinterpret_cast<const float4 *>(xr + i);
-            float4 v1 = *reinterpret_cast<const float4 *>(xr + i + 4);
-            if (yr) {
-                const float4 y0 = *reinterpret_cast<const float4 *>(yr + i);
-                const float4 y1 = *reinterpret_cast<const float4 *>(yr + i + 4);
-                v0.x += y0.x; v0.y += y0.y; v0.z += y0.z; v0.w += y0.w;
-                v1.x += y1.x; v1.y += y1.y; v1.z += y1.z; v1.w += y1.w;
-                *reinterpret_cast<float4 *>(xr + i) = v0;
-                *reinterpret_cast<float4 *>(xr + i + 4) = v1;
-            }
-            ss += v0.x * v0.x + v0.y * v0.y + v0.z * v0.z + v0.w * v0.w;
-            ss += v1.x * v1.x + v1.y * v1.y + v1.z * v1.z + v1.w * v1.w;
+    for (int i = threadIdx.x * 8; i < d; i += blockDim.x * 8) {
+        float4 v0 = *reinterpret_cast<const float4 *>(xr + i);
+        float4 v1 = *reinterpret_cast<const float4 *>(xr + i + 4);
+        if (yr) {
+            const float4 y0 = *reinterpret_cast<const float4 *>(yr + i);
+            const float4 y1 = *reinterpret_cast<const float4 *>(yr + i + 4);
+            v0.x += y0.x; v0.y += y0.y; v0.z += y0.z; v0.w += y0.w;
+            v1.x += y1.x; v1.y += y1.y; v1.z += y1.z; v1.w += y1.w;
+            *reinterpret_cast<float4 *>(xr + i) = v0;
+            *reinterpret_cast<float4 *>(xr + i + 4) = v1;
         }
-        ss = block_sum(ss, red);
-        const float scale = 1.0f / sqrtf(ss / (float)d + eps);
-        for (int i = threadIdx.x * 8; i < d; i += blockDim.x * 8) {
-            const float4 v0 = *reinterpret_cast<const float4 *>(xr + i);
-            const float4 v1 = *reinterpret_cast<const float4 *>(xr + i + 4);
-            const float4 w0 = __ldg(reinterpret_cast<const float4 *>(w + i));
-            const float4 w1 = __ldg(reinterpret_cast<const float4 *>(w + i + 4));
-            uint4 o;
-            o.x = h2u_(__floats2half2_rn((v0.x * scale) * w0.x, (v0.y * scale) * w0.y));
-            o.y = h2u_(__floats2half2_rn((v0.z * scale) * w0.z, (v0.w * scale) * w0.w));
-            o.z = h2u_(__floats2half2_rn((v1.x * scale) * w1.x, (v1.y * scale) * w1.y));
-            o.w = h2u_(__floats2half2_rn((v1.z * scale) * w1.z, (v1.w * scale) * w1.w));
-            *reinterpret_cast<uint4 *>(hr + i) = o;
-        }
-    } else {
-        for (int i = threadIdx.x; i < d; i += blockDim.x) {
-            float v = xr[i];
-            if (yr) {
-                v += yr[i];
-                xr[i] = v;
-            }
-            ss += v * v;
-        }
-        ss = block_sum(ss, red);
-        const float scale = 1.0f / sqrtf(ss / (float)d + eps);
-        for (int i = threadIdx.x; i < d; i += blockDim.x) hr[i] = __float2half_rn((xr[i] * scale) * w[i]);
+        ss += v0.x * v0.x + v0.y * v0.y + v0.z * v0.z + v0.w * v0.w;
+        ss += v1.x * v1.x + v1.y * v1.y + v1.z * v1.z + v1.w * v1.w;
+    }
+    ss = block_sum(ss, red);
+    const float scale = 1.0f / sqrtf(ss / (float)d + eps);
+    for (int i = threadIdx.x * 8; i < d; i += blockDim.x * 8) {
+        const float4 v0 = *reinterpret_cast<const float4 *>(xr + i);
+        const float4 v1 = *reinterpret_cast<const float4 *>(xr + i + 4);
+        const float4 w0 = __ldg(reinterpret_cast<const float4 *>(w + i));
+        const float4 w1 = __ldg(reinterpret_cast<const float4 *>(w + i + 4));
+        const float v[8] = {(v0.x * scale) * w0.x, (v0.y * scale) * w0.y, (v0.z * scale) * w0.z, (v0.w * scale) * w0.w,
+                            (v1.x * scale) * w1.x, (v1.y * scale) * w1.y, (v1.z * scale) * w1.z, (v1.w * scale) * w1.w};
+        store_pair8(hr, i, v);
     }
 }
 
@@ -391,10 +391,17 @@ __global__ void __launch_bounds__(1024) select_commit_kernel(int remasking, int 
     }
 }
 
-// X (f32, host-provided for dfb_linear) -> f16 rows.
-__global__ void f32_to_f16_kernel(const float *__restrict__ x, __half *__restrict__ y, size_t n) {
-    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
-        y[i] = __float2half_rn(x[i]);
+// X (f32 [rows][K], host-provided for dfb_linear) -> pair rows [rows][2K]; K multiple of 64.
+__global__ void f32_to_pair_kernel(const float *__restrict__ x, __half *__restrict__ y, int rows, int K) {
+    const size_t groups = (size_t)rows * (K / 8);
+    for (size_t g = blockIdx.x * (size_t)blockDim.x + threadIdx.x; g < groups; g += (size_t)gridDim.x * blockDim.x) {
+        const size_t r = g / (K / 8);
+        const int i = (int)(g % (K / 8)) * 8;
+        float v[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) v[e] = x[r * K + i + e];
+        store_pair8(y + r * 2 * K, i, v);
+    }
 }
 
 }  // namespace dfb

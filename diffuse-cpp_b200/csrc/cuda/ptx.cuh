@@ -66,7 +66,7 @@ constexpr uint64_t kWaitTimeoutNs = 4000000000ull;  // 4 s
 #endif
 constexpr uint32_t kSuspendHintNs = DFB_WAIT_HINT_NS;  // per try_wait, then re-check the flags
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
-                                          int *err, int code) {
+                                          int *err, int code, uint64_t timeout_ns = kWaitTimeoutNs) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
     for (;;) {
@@ -76,7 +76,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
             *abort_flag = 1;
             return false;
         }
-        if (globaltimer() - t0 > kWaitTimeoutNs) {
+        if (globaltimer() - t0 > timeout_ns) {
             *abort_flag = 1;
             atomicCAS(err, 0, code);
             return false;
@@ -114,7 +114,8 @@ __device__ __forceinline__ int ld_acquire_gpu(const int *p) {
 // Bounded wait until the global counter *c reaches target (acquire), with the abort
 // rules of mbar_wait.  Every CTA of a launch is resident at once (one per SM), so the
 // CTAs whose arrivals this waits for are running.
-__device__ __forceinline__ bool wait_count(const int *c, int target, volatile int *abort_flag, int *err, int code) {
+__device__ __forceinline__ bool wait_count(const int *c, int target, volatile int *abort_flag, int *err, int code,
+                                           uint64_t timeout_ns = kWaitTimeoutNs) {
     const uint64_t t0 = globaltimer();
     for (;;) {
         if (ld_acquire_gpu(c) >= target) return true;
@@ -123,7 +124,7 @@ __device__ __forceinline__ bool wait_count(const int *c, int target, volatile in
             *abort_flag = 1;
             return false;
         }
-        if (globaltimer() - t0 > kWaitTimeoutNs) {
+        if (globaltimer() - t0 > timeout_ns) {
             *abort_flag = 1;
             atomicCAS(err, 0, code);
             return false;
@@ -246,16 +247,13 @@ __device__ __forceinline__ void mma2_f16_ss_k64(uint32_t d_tmem, uint64_t adesc,
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
-// 32 lanes x 32 columns of 32-bit: this thread's lane, columns [col, col+32).
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+// 32 lanes x 16 columns of 32-bit: this thread's lane, columns [col, col+16).
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
     asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
-        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
-        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
         "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
-        "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
-        "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
-        "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
         : "memory");
 }
 // This thread's tcgen05.st have completed.

@@ -118,6 +118,43 @@ static diffuse_model *load_model(const std::string &path) {
                 hp.n_head_kv, hp.n_layer, hp.n_ff);
     DIFFUSE_LOG("  rope_theta=%.0f, rms_norm_eps=%.1e, mask_token=%u", hp.rope_theta, hp.rms_norm_eps, hp.mask_token_id);
 
+    // Every tensor the forward binds (diffuse-model.cpp:146-178) is present with its shape
+    // before anything reaches the device: a missing or misshapen tensor is a host error.
+    {
+        const int64_t d = hp.n_embd, ff = hp.n_ff, V = hp.n_vocab;
+        const int64_t kvd = hp.n_head ? (int64_t)hp.n_head_kv * (d / hp.n_head) : 0;
+        auto check = [&](const std::string &n, int64_t ne0, int64_t ne1, bool optional) -> bool {
+            const GgufTensor *t = g.tensor(n);
+            if (!t) {
+                if (optional) return true;
+                set_error(DFB_ERR_ARG, "tensor not found: %s", n.c_str());
+                return false;
+            }
+            if (t->ne[0] != ne0 || t->ne[1] != ne1) {
+                set_error(DFB_ERR_ARG, "tensor %s has shape %lldx%lld, expected %lldx%lld", n.c_str(), (long long)t->ne[0],
+                          (long long)t->ne[1], (long long)ne0, (long long)ne1);
+                return false;
+            }
+            return true;
+        };
+        bool ok = check("token_embd.weight", d, V, false) && check("output_norm.weight", d, 1, false) &&
+                  check("output.weight", d, V, true);
+        const struct { const char *n; int64_t ne0, ne1; bool opt; } per_layer[] = {
+            {"attn_norm.weight", d, 1, false}, {"attn_q.weight", d, d, false}, {"attn_k.weight", d, kvd, false},
+            {"attn_v.weight", d, kvd, false}, {"attn_output.weight", d, d, false}, {"ffn_norm.weight", d, 1, false},
+            {"ffn_gate.weight", d, ff, false}, {"ffn_up.weight", d, ff, false}, {"ffn_down.weight", ff, d, false},
+            {"attn_q.bias", d, 1, true}, {"attn_k.bias", kvd, 1, true}, {"attn_v.bias", kvd, 1, true}};
+        for (uint32_t l = 0; ok && l < hp.n_layer; l++)
+            for (const auto &e : per_layer) {
+                ok = check("blk." + std::to_string(l) + "." + e.n, e.ne0, e.ne1, e.opt);
+                if (!ok) break;
+            }
+        if (!ok) {
+            delete m;
+            return nullptr;
+        }
+    }
+
     dfb_hparams dh{};
     dh.n_vocab = (int)hp.n_vocab; dh.n_embd = (int)hp.n_embd; dh.n_head = (int)hp.n_head;
     dh.n_head_kv = (int)hp.n_head_kv; dh.n_layer = (int)hp.n_layer; dh.n_ff = (int)hp.n_ff;

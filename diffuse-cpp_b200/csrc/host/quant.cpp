@@ -2,11 +2,19 @@
 // (tools/quantize.cpp:31-110), diffuse-quantize, and the random-init model
 // synthesizer used for fixtures and benchmarks.
 //
-// Q8_0 quantization follows GGML's reference rounding (amax/127, roundf), which is
-// pinned bit-for-bit against gguf-py's Q8_0.quantize in tests.  Q4_K / Q6_K use a
-// plain min/max scale search of this library's own (any valid block is a valid
-// model: the forward pass only ever reads the blocks back); their decoding is
-// pinned against gguf-py's dequantizers.
+// The quantizers restate GGML's reference algorithms (ggml_quantize_chunk, called at
+// tools/quantize.cpp:291; GGML v0.9.8 is not vendored in the reference checkout):
+//   Q8_0  d = amax / 127, q = round(x / d)            (pinned bit-for-bit to gguf-py)
+//   Q4_K  per 32-element sub-block a weighted least-squares search of scale and min
+//         over 21 candidate grids (weights sqrt(mean x^2) + |x|), then 6-bit scale and
+//         min codes relative to the block's largest, and a final rounding pass
+//   Q6_K  per 16-element group a scale search over 19 candidate grids weighted by x^2,
+//         then 8-bit signed scale codes relative to the block's largest |scale|
+// so that a file re-quantized here carries the blocks diffuse-quantize would write.  The
+// steps and constants must match GGML's for identical blocks; the code is this
+// library's.  Sums are sequential float sums (the file is built with
+// -ffp-contract=off), as written; an FMA-contracting GGML build can differ in the last
+// bit of a sum, and with it, rarely, one rounding.
 #include <algorithm>
 #include <atomic>
 #include <cmath>
@@ -49,87 +57,194 @@ static void quant_q8_0(const float *x, int64_t n, uint8_t *out) {
     }
 }
 
+// Round to nearest, ties to even (GGML's nearest_int for |v| < 2^22).
+static inline int rne(float v) { return (int)lrintf(v); }
+
+// Weighted search of (scale, min) for n values quantized to [0, nmax] as
+// x ~ scale * q + min (min <= 0): the plain min/max grid first, then grids of
+// (nmax + rmin + rdelta * i) steps over [min, max] for i = 0..nsteps, each refit by
+// weighted least squares (min clamped to 0); the grid with the smallest weighted squared
+// error wins.  Returns the scale; *neg_min = -min; q receives the codes.
+static float search_scale_min(int n, int nmax, const float *x, const float *w, uint8_t *q, float *neg_min,
+                              uint8_t *trial, float rmin, float rdelta, int nsteps) {
+    float lo = x[0], hi = x[0], sw = w[0], sx = w[0] * x[0];
+    for (int i = 1; i < n; i++) {
+        lo = std::min(lo, x[i]);
+        hi = std::max(hi, x[i]);
+        sw += w[i];
+        sx += w[i] * x[i];
+    }
+    if (lo > 0) lo = 0;
+    if (hi == lo) {
+        memset(q, 0, n);
+        *neg_min = -lo;
+        return 0.f;
+    }
+    float inv = nmax / (hi - lo);
+    float scale = 1 / inv, mn = lo, best = 0;
+    for (int i = 0; i < n; i++) {
+        q[i] = (uint8_t)std::max(0, std::min(nmax, rne(inv * (x[i] - lo))));
+        const float e = scale * q[i] + mn - x[i];
+        best += w[i] * (e * e);
+    }
+    for (int k = 0; k <= nsteps; k++) {
+        inv = (rmin + rdelta * k + nmax) / (hi - lo);
+        float sl = 0, sl2 = 0, sxl = 0;
+        for (int i = 0; i < n; i++) {
+            const int l = std::max(0, std::min(nmax, rne(inv * (x[i] - lo))));
+            trial[i] = (uint8_t)l;
+            sl += w[i] * l;
+            sl2 += w[i] * l * l;
+            sxl += w[i] * l * x[i];
+        }
+        const float det = sw * sl2 - sl * sl;
+        if (det <= 0) continue;
+        float ts = (sw * sxl - sx * sl) / det, tm = (sl2 * sx - sl * sxl) / det;
+        if (tm > 0) {
+            tm = 0;
+            ts = sxl / sl2;
+        }
+        float err = 0;
+        for (int i = 0; i < n; i++) {
+            const float e = ts * trial[i] + tm - x[i];
+            err += w[i] * (e * e);
+        }
+        if (err < best) {
+            memcpy(q, trial, n);
+            best = err;
+            scale = ts;
+            mn = tm;
+        }
+    }
+    *neg_min = -mn;
+    return scale;
+}
+
 static void quant_q4_k(const float *x, int64_t n, uint8_t *out) {
     for (int64_t b = 0; b < n / 256; b++) {
         const float *xb = x + 256 * b;
-        float scale[8], mn[8];
-        float max_scale = 0.f, max_min = 0.f;
+        uint8_t q[256], trial[32];
+        float w[32], scale[8], mn[8], max_scale = 0.f, max_min = 0.f;
         for (int j = 0; j < 8; j++) {
-            float lo = xb[32 * j], hi = xb[32 * j];
-            for (int l = 1; l < 32; l++) { lo = std::min(lo, xb[32 * j + l]); hi = std::max(hi, xb[32 * j + l]); }
-            lo = std::min(lo, 0.f);
-            scale[j] = (hi - lo) / 15.f;
-            mn[j] = -lo;
+            const float *xs = xb + 32 * j;
+            float s2 = 0;
+            for (int l = 0; l < 32; l++) s2 += xs[l] * xs[l];
+            const float rms = sqrtf(s2 / 32);
+            for (int l = 0; l < 32; l++) w[l] = rms + fabsf(xs[l]);
+            scale[j] = search_scale_min(32, 15, xs, w, q + 32 * j, &mn[j], trial, -1.f, 0.1f, 20);
             max_scale = std::max(max_scale, scale[j]);
             max_min = std::max(max_min, mn[j]);
         }
-        const float d = max_scale / 63.f, dmin = max_min / 63.f;
-        const uint16_t dh = f2h(d), mh = f2h(dmin);
-        const float dq = h2f(dh), mq = h2f(mh);
-        uint8_t sc[8], mm[8];
+        const float inv_s = max_scale > 0 ? 63.f / max_scale : 0.f, inv_m = max_min > 0 ? 63.f / max_min : 0.f;
+        uint8_t *blk = out + 144 * b, *sc = blk + 4;
+        memset(sc, 0, 12);
+        uint8_t ls[8], lm[8];
         for (int j = 0; j < 8; j++) {
-            sc[j] = (uint8_t)std::min(63, std::max(0, dq > 0 ? (int)lrintf(scale[j] / dq) : 0));
-            mm[j] = (uint8_t)std::min(63, std::max(0, mq > 0 ? (int)lrintf(mn[j] / mq) : 0));
+            ls[j] = (uint8_t)std::min(63, rne(inv_s * scale[j]));
+            lm[j] = (uint8_t)std::min(63, rne(inv_m * mn[j]));
         }
-        uint8_t *blk = out + 144 * b;
+        // 6-bit codes, GGML's packing (get_scale_min_k4 reads it back)
+        for (int j = 0; j < 4; j++) {
+            sc[j] = ls[j] | (uint8_t)((ls[j + 4] >> 4) << 6);
+            sc[j + 4] = lm[j] | (uint8_t)((lm[j + 4] >> 4) << 6);
+            sc[j + 8] = (uint8_t)((ls[j + 4] & 0xF) | ((lm[j + 4] & 0xF) << 4));
+        }
+        const uint16_t dh = f2h(max_scale / 63.f), mh = f2h(max_min / 63.f);
         memcpy(blk, &dh, 2);
         memcpy(blk + 2, &mh, 2);
-        uint8_t *s = blk + 4;
-        for (int j = 0; j < 4; j++) {
-            s[j] = (sc[j] & 63) | ((sc[j + 4] >> 4) << 6);
-            s[j + 4] = (mm[j] & 63) | ((mm[j + 4] >> 4) << 6);
-            s[j + 8] = (sc[j + 4] & 0xF) | ((mm[j + 4] & 0xF) << 4);
+        for (int j = 0; j < 8; j++) {
+            const float dj = h2f(dh) * ls[j];
+            if (dj == 0.f) continue;  // the search's codes stay (they decode to -dmin * m anyway)
+            const float mj = h2f(mh) * lm[j];
+            for (int l = 0; l < 32; l++) q[32 * j + l] = (uint8_t)std::max(0, std::min(15, rne((xb[32 * j + l] + mj) / dj)));
         }
         uint8_t *qs = blk + 16;
-        memset(qs, 0, 128);
-        for (int j = 0; j < 8; j++) {
-            const float es = dq * sc[j], em = mq * mm[j];
-            for (int l = 0; l < 32; l++) {
-                int q = es > 0 ? (int)lrintf((xb[32 * j + l] + em) / es) : 0;
-                q = std::min(15, std::max(0, q));
-                const int g = j >> 1;
-                if (j & 1) qs[32 * g + l] |= (uint8_t)(q << 4);
-                else qs[32 * g + l] |= (uint8_t)q;
-            }
+        for (int c = 0; c < 4; c++)
+            for (int l = 0; l < 32; l++) qs[32 * c + l] = (uint8_t)(q[64 * c + l] | (q[64 * c + 32 + l] << 4));
+    }
+}
+
+// Scale of n values quantized to [-nmax, nmax - 1], weighted by x^2: the grid
+// -nmax / max (max = the value of largest magnitude) refit by least squares, then 18
+// grids -(nmax + 0.1 k) / max, k = -9..9 (k != 0), kept when they improve
+// (sum w x l)^2 / (sum w l^2).  q receives codes + nmax.
+static float search_scale_sym(int n, int nmax, const float *x, uint8_t *q) {
+    float mx = 0, amx = 0;
+    for (int i = 0; i < n; i++)
+        if (fabsf(x[i]) > amx) {
+            amx = fabsf(x[i]);
+            mx = x[i];
+        }
+    if (amx < 1e-15f) {
+        memset(q, 0, n);
+        return 0.f;
+    }
+    float inv = -nmax / mx, slx = 0, sl2 = 0;
+    for (int i = 0; i < n; i++) {
+        const int l = std::max(-nmax, std::min(nmax - 1, rne(inv * x[i])));
+        q[i] = (uint8_t)(l + nmax);
+        const float w = x[i] * x[i];
+        slx += w * x[i] * l;
+        sl2 += w * l * l;
+    }
+    float scale = sl2 ? slx / sl2 : 0.0f, best = scale * slx;
+    for (int k = -9; k <= 9; k++) {
+        if (k == 0) continue;
+        inv = -(nmax + 0.1f * k) / mx;
+        slx = sl2 = 0;
+        for (int i = 0; i < n; i++) {
+            const int l = std::max(-nmax, std::min(nmax - 1, rne(inv * x[i])));
+            const float w = x[i] * x[i];
+            slx += w * x[i] * l;
+            sl2 += w * l * l;
+        }
+        if (sl2 > 0 && slx * slx > best * sl2) {
+            for (int i = 0; i < n; i++) q[i] = (uint8_t)(std::max(-nmax, std::min(nmax - 1, rne(inv * x[i]))) + nmax);
+            scale = slx / sl2;
+            best = scale * slx;
         }
     }
+    return scale;
 }
 
 static void quant_q6_k(const float *x, int64_t n, uint8_t *out) {
     for (int64_t b = 0; b < n / 256; b++) {
         const float *xb = x + 256 * b;
-        float gscale[16];
-        float amax_scale = 0.f;
+        uint8_t q[256];
+        float gs[16], max_scale = 0.f, max_abs = 0.f;
         for (int g = 0; g < 16; g++) {
-            float mx = 0.f, amx = 0.f;
-            for (int l = 0; l < 16; l++) {
-                const float v = xb[16 * g + l];
-                if (fabsf(v) > amx) { amx = fabsf(v); mx = v; }
+            gs[g] = search_scale_sym(16, 32, xb + 16 * g, q + 16 * g);
+            if (fabsf(gs[g]) > max_abs) {
+                max_abs = fabsf(gs[g]);
+                max_scale = gs[g];
             }
-            gscale[g] = mx / -32.f;
-            amax_scale = std::max(amax_scale, fabsf(gscale[g]));
         }
-        const float d = amax_scale / 127.f;
-        const uint16_t dh = f2h(d);
-        const float dq = h2f(dh);
-        int8_t sc[16];
-        for (int g = 0; g < 16; g++)
-            sc[g] = (int8_t)std::min(127, std::max(-127, dq > 0 ? (int)lrintf(gscale[g] / dq) : 0));
-        uint8_t *blk = out + 210 * b;
-        uint8_t *ql = blk, *qh = blk + 128;
-        memset(blk, 0, 192);
-        for (int e = 0; e < 256; e++) {
-            const float es = dq * sc[e / 16];
-            int q = es != 0.f ? (int)lrintf(xb[e] / es) : 0;
-            q = std::min(31, std::max(-32, q)) + 32;
-            const int h = e / 128, gg = (e % 128) / 32, l = e % 32;
-            uint8_t &lb = ql[64 * h + (gg & 1) * 32 + l];
-            if (gg >= 2) lb |= (uint8_t)((q & 0xF) << 4);
-            else lb |= (uint8_t)(q & 0xF);
-            qh[32 * h + l] |= (uint8_t)(((q >> 4) & 3) << (2 * gg));
+        uint8_t *blk = out + 210 * b, *ql = blk, *qh = blk + 128;
+        int8_t *sc = reinterpret_cast<int8_t *>(blk + 192);
+        if (max_abs < 1e-15f) {
+            memset(blk, 0, 210);
+            continue;
         }
-        memcpy(blk + 192, sc, 16);
+        const float inv = -128.f / max_scale;
+        const uint16_t dh = f2h(1 / inv);
         memcpy(blk + 208, &dh, 2);
+        for (int g = 0; g < 16; g++) sc[g] = (int8_t)std::min(127, rne(inv * gs[g]));
+        for (int g = 0; g < 16; g++) {
+            const float dg = h2f(dh) * sc[g];
+            if (dg == 0.f) continue;
+            for (int l = 0; l < 16; l++) q[16 * g + l] = (uint8_t)(std::max(-32, std::min(31, rne(xb[16 * g + l] / dg))) + 32);
+        }
+        // ql: low nibbles of elements l and l+64 (bytes 0-31), l+32 and l+96 (32-63) per
+        // 128-element half; qh: the 2-bit high parts of elements l, l+32, l+64, l+96
+        for (int h = 0; h < 2; h++) {
+            const uint8_t *qq = q + 128 * h;
+            for (int l = 0; l < 32; l++) {
+                ql[64 * h + l] = (uint8_t)((qq[l] & 0xF) | ((qq[l + 64] & 0xF) << 4));
+                ql[64 * h + 32 + l] = (uint8_t)((qq[l + 32] & 0xF) | ((qq[l + 96] & 0xF) << 4));
+                qh[32 * h + l] = (uint8_t)((qq[l] >> 4) | ((qq[l + 32] >> 4) << 2) | ((qq[l + 64] >> 4) << 4) |
+                                           ((qq[l + 96] >> 4) << 6));
+            }
+        }
     }
 }
 

@@ -105,6 +105,16 @@ int dfb_forward(dfb_ctx *c, const int32_t *tokens, int n, float *logits_host);
  * for a model weight (host buffers).  Exposed for parity tests of the GEMM alone. */
 int dfb_linear(dfb_ctx *c, int role, int layer, const float *x_host, int M, float *y_host);
 
+/* Failure-detection test hook; no counterpart in the reference (its CPU loop has no
+ * device waits).  Runs dfb_linear with one split-tile arrival counter preset so that the
+ * tile's contributors wait for arrivals that never come, and with every wait of that
+ * launch limited to timeout_ns (0 < timeout_ns <= 4 s).  The kernel gives up, raises its
+ * error flag and returns; the call returns DFB_ERR_TIMEOUT and resets the counters, so the
+ * context stays usable.  Nothing faults or hangs.  A weight and M whose tile 0 is split
+ * across CTA pairs (many k-blocks, few output tiles) are needed for the wait to occur. */
+int dfb_debug_stalled_linear(dfb_ctx *c, int role, int layer, const float *x_host, int M, float *y_host,
+                             unsigned long long timeout_ns);
+
 /* ── generation: the device side of diffuse_sample (diffuse-sampler.cpp:60-370) ── */
 /* Set up seq = prompt ‖ MASK × n_gen, masks, cache and logits buffer on the device. */
 int dfb_gen_begin(dfb_ctx *c, const int32_t *prompt, int n_prompt, int n_gen, const dfb_sampler_params *p);

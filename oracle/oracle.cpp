@@ -266,6 +266,19 @@ struct gguf_file {
         size_t data_off = (size_t)(p - (const uint8_t *)map);
         data_off = (data_off + align - 1) / align * align;
         for (auto &ti : infos) {
+            // a type GGML's CPU path here does not decode, or data past the end of the file
+            // (gguf_init_from_file fails on both, diffuse-model.cpp:92-95)
+            if (blck_size(ti.tv.type) == 0 || type_size(ti.tv.type) == 0) {
+                fprintf(stderr, "[oracle] tensor %s has unsupported type %d\n", ti.name.c_str(), ti.tv.type);
+                return false;
+            }
+            uint64_t rows = 1;
+            for (int d = 1; d < ti.tv.n_dims; d++) rows *= (uint64_t)ti.tv.ne[d];
+            const uint64_t nbytes = (uint64_t)(ti.tv.ne[0] / blck_size(ti.tv.type) * type_size(ti.tv.type)) * rows;
+            if (data_off + ti.off + nbytes > size) {
+                fprintf(stderr, "[oracle] tensor %s data past the end of the file (truncated)\n", ti.name.c_str());
+                return false;
+            }
             ti.tv.data = (const uint8_t *)map + data_off + ti.off;
             tensors[ti.name] = ti.tv;
         }
@@ -798,10 +811,19 @@ orc_model *orc_load(const char *path) {
         const tensor_view **slots[] = {&L.attn_norm, &L.wq, &L.wk, &L.wv, &L.wo, &L.ffn_norm, &L.gate, &L.up, &L.down};
         const char *names[] = {"attn_norm.weight", "attn_q.weight", "attn_k.weight", "attn_v.weight", "attn_output.weight",
                                "ffn_norm.weight", "ffn_gate.weight", "ffn_up.weight", "ffn_down.weight"};
+        const int64_t d = hp.n_embd, kvd = (int64_t)hp.n_head_kv * (hp.n_embd / hp.n_head), ff = hp.n_ff;
+        const int64_t shape[9][2] = {{d, 1}, {d, d}, {d, kvd}, {d, kvd}, {d, d}, {d, 1}, {d, ff}, {d, ff}, {ff, d}};
         for (int s = 0; s < 9; s++) {
             snprintf(buf, sizeof buf, "blk.%d.%s", i, names[s]);
             *slots[s] = need(buf);
             if (!*slots[s]) { delete m; return nullptr; }
+            const int64_t n1 = (*slots[s])->n_dims > 1 ? (*slots[s])->ne[1] : 1;
+            if ((*slots[s])->ne[0] != shape[s][0] || n1 != shape[s][1]) {
+                fprintf(stderr, "[oracle] tensor %s has shape %lldx%lld, expected %lldx%lld\n", buf,
+                        (long long)(*slots[s])->ne[0], (long long)n1, (long long)shape[s][0], (long long)shape[s][1]);
+                delete m;
+                return nullptr;
+            }
         }
         snprintf(buf, sizeof buf, "blk.%d.attn_q.bias", i); L.bq = find_tensor(*m, buf);
         snprintf(buf, sizeof buf, "blk.%d.attn_k.bias", i); L.bk = find_tensor(*m, buf);
@@ -855,70 +877,138 @@ int orc_forward_layers(const orc_model *m, const int32_t *tokens, int32_t n, flo
     return 0;
 }
 
-// diffuse_sample, diffuse-sampler.cpp:60-370
+// The state of one diffuse_sample run (diffuse-sampler.cpp:60-130): sequence, masks,
+// the persistent logits buffer, the inter-step cache and the shared mt19937.
+struct orc_session {
+    const orc_model *m = nullptr;
+    orc_sampler_params p{};
+    int mode = 0, nt = 1;
+    int n_prompt = 0, n_gen = 0, total_len = 0, n_masked = 0, last_n_active = 0;
+    bool shift_logits = false;
+    std::vector<int32_t> seq;
+    std::vector<bool> is_masked;
+    std::vector<float> logits_full;
+    step_cache cache;
+    std::vector<int> all_pos;
+    std::mt19937 rng;
+};
+
+orc_session *orc_sess_new(const orc_model *m, const int32_t *prompt, int32_t n_prompt, int32_t n_gen,
+                          const orc_sampler_params *pp, int32_t mode, int32_t nt) {
+    auto *s = new orc_session();
+    s->m = m;
+    s->p = *pp;
+    s->mode = mode;
+    s->nt = nthreads_or(nt);
+    s->n_prompt = n_prompt;
+    s->n_gen = n_gen;
+    s->shift_logits = m->model_type == "dream";  // sampler.cpp:74
+    s->seq.assign(prompt, prompt + n_prompt);     // sampler.cpp:77-87
+    s->seq.resize(n_prompt + n_gen, m->hp.mask_id);
+    s->total_len = n_prompt + n_gen;
+    s->is_masked.assign(s->total_len, false);
+    for (int i = n_prompt; i < s->total_len; i++) s->is_masked[i] = true;
+    s->n_masked = n_gen;
+    s->logits_full.assign((size_t)s->total_len * m->hp.n_vocab, 0.f);  // sampler.cpp:90
+    s->rng.seed(pp->seed);
+    if (pp->use_cache) s->cache.init(s->total_len, m->hp.n_layer, m->hp.n_head_kv * m->hp.hd());  // sampler.cpp:100
+    s->all_pos.resize(s->total_len);
+    for (int i = 0; i < s->total_len; i++) s->all_pos[i] = i;
+    return s;
+}
+
+void orc_sess_free(orc_session *s) { delete s; }
+
+// The forward of one step (diffuse-sampler.cpp:143-213): full or cached, the cache's
+// sequence snapshot taken after it (update_seq), logits_full refreshed at the active rows.
+// Returns the rows computed.
+int orc_sess_forward(orc_session *s, int32_t step) {
+    const orc_model &m = *s->m;
+    const orc_sampler_params &p = s->p;
+    const int total_len = s->total_len, n_vocab = m.hp.n_vocab;
+    const bool use_cache = p.use_cache != 0;
+    int n_active = total_len;
+    const bool force_full = !use_cache || !s->cache.initialized ||
+                            (p.cache_refresh > 0 && step > 0 && (step % p.cache_refresh == 0));
+    if (force_full) {
+        forward_rows(m, s->seq.data(), s->all_pos.data(), total_len, nullptr, use_cache ? &s->cache : nullptr,
+                     s->logits_full.data(), s->mode, s->nt);
+        if (use_cache) s->cache.update_seq(s->seq.data(), total_len);
+    } else {
+        std::vector<int> cached, active;
+        s->cache.compute_active_set(s->seq.data(), s->is_masked, total_len, step, p.cache_keep_active, cached, active);
+        n_active = (int)active.size();
+        if (n_active >= total_len || n_active == 0) {
+            forward_rows(m, s->seq.data(), s->all_pos.data(), total_len, nullptr, &s->cache, s->logits_full.data(),
+                         s->mode, s->nt);
+            s->cache.update_seq(s->seq.data(), total_len);
+            n_active = total_len;
+        } else {
+            std::vector<int32_t> toks(n_active);
+            for (int a = 0; a < n_active; a++) toks[a] = s->seq[active[a]];
+            std::vector<float> la((size_t)n_active * n_vocab);
+            forward_rows(m, toks.data(), active.data(), n_active, &cached, &s->cache, la.data(), s->mode, s->nt);
+            s->cache.update_seq(s->seq.data(), total_len);
+            for (int a = 0; a < n_active; a++)
+                memcpy(&s->logits_full[(size_t)active[a] * n_vocab], &la[(size_t)a * n_vocab], n_vocab * 4);
+        }
+    }
+    s->last_n_active = n_active;
+    return n_active;
+}
+
+// The sampler decision of one step on the session's own logits (sampler.cpp:222-323).
+int orc_sess_sample(orc_session *s, int32_t step, int32_t *commit_pos, int32_t *commit_tok) {
+    return sampler_step(s->logits_full.data(), s->m->hp.n_vocab, s->total_len, s->seq.data(), s->is_masked,
+                        s->n_masked, s->shift_logits, step, s->p, s->rng, commit_pos, commit_tok, nullptr, nullptr);
+}
+
+// Teacher forcing: apply commits decided elsewhere (sampler.cpp:316-323 with given picks).
+int orc_sess_commit(orc_session *s, const int32_t *pos, const int32_t *tok, int32_t n) {
+    for (int i = 0; i < n; i++) {
+        if (pos[i] < 0 || pos[i] >= s->total_len || !s->is_masked[pos[i]]) return -1;
+        s->seq[pos[i]] = tok[i];
+        s->is_masked[pos[i]] = false;
+        s->n_masked--;
+    }
+    return 0;
+}
+
+int orc_sess_logits(const orc_session *s, int32_t row0, int32_t nrows, float *out) {
+    if (row0 < 0 || nrows < 0 || row0 + nrows > s->total_len) return -1;
+    const size_t V = s->m->hp.n_vocab;
+    memcpy(out, s->logits_full.data() + (size_t)row0 * V, (size_t)nrows * V * 4);
+    return 0;
+}
+
+int orc_sess_tokens(const orc_session *s, int32_t *seq_out) {
+    memcpy(seq_out, s->seq.data(), s->total_len * sizeof(int32_t));
+    return s->n_masked;
+}
+
+// diffuse_sample, diffuse-sampler.cpp:60-370: forward + sampler per step until no mask is left.
 int orc_generate(const orc_model *m, const int32_t *prompt, int32_t n_prompt, int32_t n_gen,
                  const orc_sampler_params *pp, int32_t *out_tokens, orc_trace *trace, int32_t mode, int32_t nt_) {
-    const orc_sampler_params &p = *pp;
-    const int nt = nthreads_or(nt_);
-    const hparams &hp = m->hp;
-    const int mask_id = hp.mask_id, n_vocab = hp.n_vocab;
-    const bool shift_logits = m->model_type == "dream";
-    std::vector<int32_t> seq(prompt, prompt + n_prompt);
-    seq.resize(n_prompt + n_gen, mask_id);
-    const int total_len = (int)seq.size();
-    std::vector<bool> is_masked(total_len, false);
-    for (int i = n_prompt; i < total_len; i++) is_masked[i] = true;
-    int n_masked = n_gen;
-    std::vector<float> logits_full((size_t)total_len * n_vocab);
-    std::mt19937 rng(p.seed);
-    const bool use_cache = p.use_cache != 0;
-    step_cache cache;
-    if (use_cache) cache.init(total_len, hp.n_layer, hp.n_head_kv * hp.hd());
-    std::vector<int> all_pos(total_len);
-    for (int i = 0; i < total_len; i++) all_pos[i] = i;
+    orc_session *s = orc_sess_new(m, prompt, n_prompt, n_gen, pp, mode, nt_);
     int steps_run = 0;
-    for (int step = 0; step < p.n_steps && n_masked > 0; step++) {
-        int n_active = total_len;
-        const bool force_full = !use_cache || !cache.initialized ||
-                                (p.cache_refresh > 0 && step > 0 && (step % p.cache_refresh == 0));
-        if (force_full) {
-            forward_rows(*m, seq.data(), all_pos.data(), total_len, nullptr, use_cache ? &cache : nullptr,
-                         logits_full.data(), mode, nt);
-            if (use_cache) cache.update_seq(seq.data(), total_len);
-        } else {
-            std::vector<int> cached, active;
-            cache.compute_active_set(seq.data(), is_masked, total_len, step, p.cache_keep_active, cached, active);
-            n_active = (int)active.size();
-            if (n_active >= total_len || n_active == 0) {
-                forward_rows(*m, seq.data(), all_pos.data(), total_len, nullptr, &cache, logits_full.data(), mode, nt);
-                cache.update_seq(seq.data(), total_len);
-                n_active = total_len;
-            } else {
-                std::vector<int32_t> toks(n_active);
-                for (int a = 0; a < n_active; a++) toks[a] = seq[active[a]];
-                std::vector<float> la((size_t)n_active * n_vocab);
-                forward_rows(*m, toks.data(), active.data(), n_active, &cached, &cache, la.data(), mode, nt);
-                cache.update_seq(seq.data(), total_len);
-                for (int a = 0; a < n_active; a++)
-                    memcpy(&logits_full[(size_t)active[a] * n_vocab], &la[(size_t)a * n_vocab], n_vocab * 4);
-            }
-        }
+    for (int step = 0; step < pp->n_steps && s->n_masked > 0; step++) {
+        const int n_active = orc_sess_forward(s, step);
         int32_t *cp = nullptr, *ct = nullptr;
         if (trace && step < trace->max_steps) {
             trace->n_active[step] = n_active;
             cp = trace->commit_pos + (size_t)step * trace->n_gen;
             ct = trace->commit_tok + (size_t)step * trace->n_gen;
         }
-        const int done = sampler_step(logits_full.data(), n_vocab, total_len, seq.data(), is_masked, n_masked,
-                                      shift_logits, step, p, rng, cp, ct, nullptr, nullptr);
+        const int done = orc_sess_sample(s, step, cp, ct);
         if (trace && step < trace->max_steps) trace->n_unmask[step] = done;
         steps_run++;
     }
     if (trace) {
         trace->steps_run = steps_run;
-        if (trace->final_logits) memcpy(trace->final_logits, logits_full.data(), logits_full.size() * 4);
+        if (trace->final_logits) memcpy(trace->final_logits, s->logits_full.data(), s->logits_full.size() * 4);
     }
-    for (int i = 0; i < n_gen; i++) out_tokens[i] = seq[n_prompt + i];
+    for (int i = 0; i < n_gen; i++) out_tokens[i] = s->seq[n_prompt + i];
+    orc_sess_free(s);
     return steps_run;
 }
 
@@ -947,3 +1037,394 @@ int orc_rope_table(int32_t n_pos, int32_t n_dims, float base, float *c, float *s
 }
 
 }  // extern "C"
+
+// ───────────────────────── model synthesizer (CPU only) ─────────────────────────
+// Writes the same seeded random-init GGUF as the product's synthesizer, from this
+// file's own code, so that a CPU-only process (the benchmark's reference arm) can
+// create its model without the product libraries; tests/test_host_cpu.py asserts the two
+// files are byte-identical.  Quantization restates the reference's quantize tool
+// (tools/quantize.cpp:31-98 type policy; blocks by GGML's reference quantizers, which
+// ggml_quantize_chunk at tools/quantize.cpp:291 calls): Q8_0 amax / 127 rounding; Q4_K
+// weighted least-squares (scale, min) search per 32-element sub-block over 21 grids then
+// 6-bit codes; Q6_K x^2-weighted scale search per 16-element group over 19 grids then
+// 8-bit signed codes.  Sums are sequential float sums without FMA contraction (this
+// section is compiled with fp-contract off, like the product's quantizer).
+#pragma GCC push_options
+#pragma GCC optimize("fp-contract=off")
+namespace {
+
+inline int rne_i(float v) { return (int)lrintf(v); }
+
+void q80_block(const float *x, uint8_t *out) {
+    float amax = 0.f;
+    for (int j = 0; j < 32; j++) amax = std::max(amax, fabsf(x[j]));
+    const float d = amax / 127.f, id = d != 0.f ? 1.0f / d : 0.0f;
+    const uint16_t dh = f2h(d);
+    memcpy(out, &dh, 2);
+    for (int j = 0; j < 32; j++) out[2 + j] = (uint8_t)(int8_t)roundf(x[j] * id);
+}
+
+// x ~ s * q + m over q in [0, nmax], m <= 0, weights w: returns s, *neg_m = -m.
+float fit_affine(int n, int nmax, const float *x, const float *w, uint8_t *q, float *neg_m) {
+    float lo = x[0], hi = x[0], sum_w = w[0], sum_wx = w[0] * x[0];
+    for (int i = 1; i < n; i++) {
+        if (x[i] < lo) lo = x[i];
+        if (x[i] > hi) hi = x[i];
+        sum_w += w[i];
+        sum_wx += w[i] * x[i];
+    }
+    if (lo > 0) lo = 0;
+    if (hi == lo) {
+        for (int i = 0; i < n; i++) q[i] = 0;
+        *neg_m = -lo;
+        return 0.f;
+    }
+    float is = nmax / (hi - lo), s = 1 / is, m = lo, err_best = 0;
+    for (int i = 0; i < n; i++) {
+        int v = rne_i(is * (x[i] - lo));
+        q[i] = (uint8_t)(v < 0 ? 0 : v > nmax ? nmax : v);
+        const float e = s * q[i] + m - x[i];
+        err_best += w[i] * (e * e);
+    }
+    uint8_t cand[32];
+    for (int step = 0; step <= 20; step++) {
+        is = (-1.f + 0.1f * step + nmax) / (hi - lo);
+        float a = 0, b = 0, c = 0;  // sum w l, sum w l^2, sum w l x
+        for (int i = 0; i < n; i++) {
+            int v = rne_i(is * (x[i] - lo));
+            v = v < 0 ? 0 : v > nmax ? nmax : v;
+            cand[i] = (uint8_t)v;
+            a += w[i] * v;
+            b += w[i] * v * v;
+            c += w[i] * v * x[i];
+        }
+        const float det = sum_w * b - a * a;
+        if (!(det > 0)) continue;
+        float s1 = (sum_w * c - sum_wx * a) / det, m1 = (b * sum_wx - a * c) / det;
+        if (m1 > 0) {
+            m1 = 0;
+            s1 = c / b;
+        }
+        float err = 0;
+        for (int i = 0; i < n; i++) {
+            const float e = s1 * cand[i] + m1 - x[i];
+            err += w[i] * (e * e);
+        }
+        if (err < err_best) {
+            for (int i = 0; i < n; i++) q[i] = cand[i];
+            err_best = err;
+            s = s1;
+            m = m1;
+        }
+    }
+    *neg_m = -m;
+    return s;
+}
+
+void q4k_block(const float *x, uint8_t *out) {
+    uint8_t q[256];
+    float w[32], s[8], mneg[8], smax = 0.f, mmax = 0.f;
+    for (int j = 0; j < 8; j++) {
+        float ss = 0;
+        for (int l = 0; l < 32; l++) ss += x[32 * j + l] * x[32 * j + l];
+        const float r = sqrtf(ss / 32);
+        for (int l = 0; l < 32; l++) w[l] = r + fabsf(x[32 * j + l]);
+        s[j] = fit_affine(32, 15, x + 32 * j, w, q + 32 * j, &mneg[j]);
+        if (s[j] > smax) smax = s[j];
+        if (mneg[j] > mmax) mmax = mneg[j];
+    }
+    const float is = smax > 0 ? 63.f / smax : 0.f, im = mmax > 0 ? 63.f / mmax : 0.f;
+    int cs[8], cm[8];
+    for (int j = 0; j < 8; j++) {
+        cs[j] = std::min(63, rne_i(is * s[j]));
+        cm[j] = std::min(63, rne_i(im * mneg[j]));
+    }
+    uint8_t *sc = out + 4;
+    for (int j = 0; j < 8; j++) {
+        if (j < 4) {
+            sc[j] = (uint8_t)cs[j];
+            sc[j + 4] = (uint8_t)cm[j];
+        } else {
+            sc[j + 4] = (uint8_t)((cs[j] & 0xF) | ((cm[j] & 0xF) << 4));
+            sc[j - 4] |= (uint8_t)((cs[j] >> 4) << 6);
+            sc[j] |= (uint8_t)((cm[j] >> 4) << 6);
+        }
+    }
+    const uint16_t dh = f2h(smax / 63.f), mh = f2h(mmax / 63.f);
+    memcpy(out, &dh, 2);
+    memcpy(out + 2, &mh, 2);
+    for (int j = 0; j < 8; j++) {
+        uint8_t a, b;
+        q4k_scale_min(j, sc, &a, &b);
+        const float d = h2f(dh) * a;
+        if (d == 0.f) continue;
+        const float dm = h2f(mh) * b;
+        for (int l = 0; l < 32; l++) {
+            const int v = rne_i((x[32 * j + l] + dm) / d);
+            q[32 * j + l] = (uint8_t)(v < 0 ? 0 : v > 15 ? 15 : v);
+        }
+    }
+    for (int c = 0; c < 4; c++)
+        for (int l = 0; l < 32; l++) out[16 + 32 * c + l] = (uint8_t)(q[64 * c + l] | (q[64 * c + 32 + l] << 4));
+}
+
+// x ~ s * l over l in [-nmax, nmax - 1], weights x^2; codes l + nmax into q.
+float fit_scale(int n, int nmax, const float *x, uint8_t *q) {
+    float amax = 0, vmax = 0;
+    for (int i = 0; i < n; i++)
+        if (fabsf(x[i]) > amax) {
+            amax = fabsf(x[i]);
+            vmax = x[i];
+        }
+    if (amax < 1e-15f) {
+        for (int i = 0; i < n; i++) q[i] = 0;
+        return 0.f;
+    }
+    auto code = [&](float is, int i) {
+        int v = rne_i(is * x[i]);
+        return v < -nmax ? -nmax : v > nmax - 1 ? nmax - 1 : v;
+    };
+    float is = -nmax / vmax, a = 0, b = 0;  // sum w x l, sum w l^2
+    for (int i = 0; i < n; i++) {
+        const int l = code(is, i);
+        q[i] = (uint8_t)(l + nmax);
+        a += x[i] * x[i] * x[i] * l;
+        b += x[i] * x[i] * l * l;
+    }
+    float s = b ? a / b : 0.0f, best = s * a;
+    for (int k = -9; k <= 9; k++) {
+        if (!k) continue;
+        is = -(nmax + 0.1f * k) / vmax;
+        a = b = 0;
+        for (int i = 0; i < n; i++) {
+            const int l = code(is, i);
+            a += x[i] * x[i] * x[i] * l;
+            b += x[i] * x[i] * l * l;
+        }
+        if (b > 0 && a * a > best * b) {
+            for (int i = 0; i < n; i++) q[i] = (uint8_t)(code(is, i) + nmax);
+            s = a / b;
+            best = s * a;
+        }
+    }
+    return s;
+}
+
+void q6k_block(const float *x, uint8_t *out) {
+    uint8_t q[256];
+    float s[16], smax = 0.f, amax = 0.f;
+    for (int g = 0; g < 16; g++) {
+        s[g] = fit_scale(16, 32, x + 16 * g, q + 16 * g);
+        if (fabsf(s[g]) > amax) {
+            amax = fabsf(s[g]);
+            smax = s[g];
+        }
+    }
+    memset(out, 0, 210);
+    if (amax < 1e-15f) return;
+    const float is = -128.f / smax;
+    const uint16_t dh = f2h(1 / is);
+    memcpy(out + 208, &dh, 2);
+    int8_t *sc = reinterpret_cast<int8_t *>(out + 192);
+    for (int g = 0; g < 16; g++) sc[g] = (int8_t)std::min(127, rne_i(is * s[g]));
+    for (int g = 0; g < 16; g++) {
+        const float d = h2f(dh) * sc[g];
+        if (d == 0.f) continue;
+        for (int l = 0; l < 16; l++) {
+            const int v = rne_i(x[16 * g + l] / d);
+            q[16 * g + l] = (uint8_t)((v < -32 ? -32 : v > 31 ? 31 : v) + 32);
+        }
+    }
+    for (int h = 0; h < 2; h++) {
+        const uint8_t *t = q + 128 * h;
+        uint8_t *ql = out + 64 * h, *qh = out + 128 + 32 * h;
+        for (int l = 0; l < 32; l++) {
+            ql[l] = (uint8_t)((t[l] & 0xF) | ((t[l + 64] & 0xF) << 4));
+            ql[l + 32] = (uint8_t)((t[l + 32] & 0xF) | ((t[l + 96] & 0xF) << 4));
+            qh[l] = (uint8_t)((t[l] >> 4) | ((t[l + 32] >> 4) << 2) | ((t[l + 64] >> 4) << 4) | ((t[l + 96] >> 4) << 6));
+        }
+    }
+}
+
+// Counter-based N(0, std): element i of a tensor depends only on (seed, tensor name, i);
+// elements 2k and 2k + 1 are the cosine and sine halves of one Box-Muller pair.
+uint64_t mix64(uint64_t v) {
+    v += 0x9E3779B97F4A7C15ull;
+    v = (v ^ (v >> 30)) * 0xBF58476D1CE4E5B9ull;
+    v = (v ^ (v >> 27)) * 0x94D049BB133111EBull;
+    return v ^ (v >> 31);
+}
+uint64_t tensor_key(const std::string &name, uint64_t seed) {
+    uint64_t h = 1469598103934665603ull ^ seed;
+    for (unsigned char ch : name) h = (h ^ ch) * 1099511628211ull;
+    return mix64(h);
+}
+void normal_row(float *out, int64_t i0, int64_t n, uint64_t key, float sd) {
+    for (int64_t k = 0; k < n;) {
+        const int64_t i = i0 + k;
+        const uint64_t r = mix64(key ^ (uint64_t)(i >> 1) * 0xD1B54A32D192ED03ull);
+        const float u1 = ((uint32_t)(r >> 40) + 1.0f) * (1.0f / 16777217.0f);
+        const float u2 = (float)((uint32_t)r >> 8) * (1.0f / 16777216.0f);
+        const float rad = sqrtf(-2.0f * logf(u1)) * sd;
+        float sn, cs;
+        sincosf(6.2831853f * u2, &sn, &cs);
+        if ((i & 1) == 0) {
+            out[k++] = rad * cs;
+            if (k < n) out[k++] = rad * sn;
+        } else {
+            out[k++] = rad * sn;
+        }
+    }
+}
+
+// The quantize tool's type for a tensor under a scheme (tools/quantize.cpp:31-98):
+// norms and biases f32, token_embd f16, Q4_K_M: output.weight and the FFN of the first
+// and last layer Q6_K, the rest Q4_K; Q8_0: every linear Q8_0.
+int32_t policy_type(const std::string &name, int scheme, int n_layer, int64_t ne0) {
+    auto has = [&](const char *s) { return name.find(s) != std::string::npos; };
+    if (scheme == 0) return T_F32;
+    const bool norm = has("_norm") || has("norm.") || has(".bias");
+    if (scheme == 1) return norm ? T_F32 : T_F16;
+    if (norm) return T_F32;
+    if (has("token_embd")) return T_F16;
+    int32_t t;
+    if (scheme == 2) t = T_Q8_0;
+    else {
+        int layer = -1;
+        const size_t p = name.find("blk.");
+        if (p != std::string::npos) layer = atoi(name.c_str() + p + 4);
+        // attention weights first (attn_output.weight also contains "output.weight")
+        const bool attn = has("attn_q") || has("attn_k") || has("attn_v") || has("attn_output");
+        const bool ffn = has("ffn_gate") || has("ffn_up") || has("ffn_down");
+        if (attn) t = T_Q4_K;
+        else if (ffn) t = (layer == 0 || layer == n_layer - 1) ? T_Q6_K : T_Q4_K;
+        else t = (has("output.weight") || has("lm_head")) ? T_Q6_K : T_Q4_K;
+    }
+    return ne0 % blck_size(t) ? T_F16 : t;  // rows that are not whole blocks keep the source type
+}
+
+// Minimal GGUF v3 writer: metadata and tensor infos, then 32-byte-aligned data.
+struct gguf_out {
+    std::vector<uint8_t> head;
+    int n_kv = 0;
+    struct ti { std::string name; int32_t type; int64_t ne0, ne1; uint64_t off, nbytes; };
+    std::vector<ti> infos;
+    uint64_t data_size = 0;
+    void put(const void *p, size_t n) { head.insert(head.end(), (const uint8_t *)p, (const uint8_t *)p + n); }
+    void put_str(const std::string &s) { const uint64_t n = s.size(); put(&n, 8); put(s.data(), n); }
+    void kv_u32(const std::string &k, uint32_t v) { put_str(k); int32_t t = 4; put(&t, 4); put(&v, 4); n_kv++; }
+    void kv_f32(const std::string &k, float v) { put_str(k); int32_t t = 6; put(&t, 4); put(&v, 4); n_kv++; }
+    void kv_str(const std::string &k, const std::string &v) { put_str(k); int32_t t = 8; put(&t, 4); put_str(v); n_kv++; }
+    void tensor(const std::string &name, int32_t type, int64_t ne0, int64_t ne1) {
+        const uint64_t nb = (uint64_t)(ne0 / blck_size(type) * type_size(type)) * (uint64_t)ne1;
+        infos.push_back({name, type, ne0, ne1, data_size, nb});
+        data_size += (nb + 31) / 32 * 32;
+    }
+    std::vector<uint8_t> header() const {
+        std::vector<uint8_t> h;
+        auto p = [&](const void *d, size_t n) { h.insert(h.end(), (const uint8_t *)d, (const uint8_t *)d + n); };
+        const uint32_t magic = 0x46554747u, version = 3;
+        const uint64_t nt = infos.size(), nk = (uint64_t)n_kv;
+        p(&magic, 4); p(&version, 4); p(&nt, 8); p(&nk, 8);
+        h.insert(h.end(), head.begin(), head.end());
+        for (const auto &t : infos) {
+            const uint64_t n = t.name.size();
+            p(&n, 8); p(t.name.data(), n);
+            const uint32_t nd = t.ne1 > 1 ? 2 : 1;
+            p(&nd, 4);
+            p(&t.ne0, 8);
+            if (nd == 2) p(&t.ne1, 8);
+            p(&t.type, 4);
+            p(&t.off, 8);
+        }
+        h.resize((h.size() + 31) / 32 * 32, 0);
+        return h;
+    }
+};
+
+}  // namespace
+
+extern "C" int orc_synth_model(const char *path, const orc_synth_spec *s) {
+    if (!path || !s || s->n_layer <= 0 || s->n_embd <= 0 || s->n_head <= 0 || s->n_head_kv <= 0 ||
+        s->n_embd % s->n_head || s->n_head % s->n_head_kv || s->scheme < 0 || s->scheme > 3)
+        return -1;
+    const int64_t d = s->n_embd, ff = s->n_ff, V = s->n_vocab, kvd = (int64_t)s->n_head_kv * (s->n_embd / s->n_head);
+    struct T { std::string name; int64_t ne0, ne1; int kind; };  // kind 0 weight, 1 norm (ones), 2 bias
+    std::vector<T> ts = {{"token_embd.weight", d, V, 0}, {"output_norm.weight", d, 1, 1}};
+    if (!s->tied_output) ts.push_back({"output.weight", d, V, 0});
+    for (int l = 0; l < s->n_layer; l++) {
+        const std::string p = "blk." + std::to_string(l) + ".";
+        ts.push_back({p + "attn_norm.weight", d, 1, 1});
+        ts.push_back({p + "attn_q.weight", d, d, 0});
+        ts.push_back({p + "attn_k.weight", d, kvd, 0});
+        ts.push_back({p + "attn_v.weight", d, kvd, 0});
+        if (s->with_bias) {
+            ts.push_back({p + "attn_q.bias", d, 1, 2});
+            ts.push_back({p + "attn_k.bias", kvd, 1, 2});
+            ts.push_back({p + "attn_v.bias", kvd, 1, 2});
+        }
+        ts.push_back({p + "attn_output.weight", d, d, 0});
+        ts.push_back({p + "ffn_norm.weight", d, 1, 1});
+        ts.push_back({p + "ffn_gate.weight", d, ff, 0});
+        ts.push_back({p + "ffn_up.weight", d, ff, 0});
+        ts.push_back({p + "ffn_down.weight", ff, d, 0});
+    }
+    // converter metadata (tools/convert-llada.py:185-202, convert-dream.py:180-195)
+    gguf_out g;
+    g.kv_str("general.architecture", "diffuse");
+    g.kv_str("general.name", s->is_dream ? "Dream-7B-random" : "LLaDA-8B-random");
+    g.kv_u32("diffuse.block_count", s->n_layer);
+    g.kv_u32("diffuse.attention.head_count", s->n_head);
+    g.kv_u32("diffuse.attention.head_count_kv", s->n_head_kv);
+    g.kv_u32("diffuse.embedding_length", s->n_embd);
+    g.kv_u32("diffuse.feed_forward_length", s->n_ff);
+    g.kv_u32("diffuse.context_length", s->n_ctx);
+    g.kv_u32("diffuse.vocab_size", s->n_vocab);
+    g.kv_f32("diffuse.rope.freq_base", s->rope_theta);
+    g.kv_f32("diffuse.attention.layer_norm_rms_epsilon", s->rms_norm_eps);
+    g.kv_u32("diffuse.mask_token_id", s->mask_token_id);
+    g.kv_str("diffuse.model_type", s->is_dream ? "dream" : "llada");
+    std::vector<int32_t> types;
+    for (const auto &t : ts) {
+        int32_t ty = policy_type(t.name, s->scheme, s->n_layer, t.ne0);
+        if (s->scheme == 1 && t.kind != 0) ty = T_F16;  // the converter's --type f16 keeps norms f16
+        types.push_back(ty);
+        g.tensor(t.name, ty, t.ne0, t.ne1);
+    }
+    FILE *f = fopen(path, "wb");
+    if (!f) return -1;
+    const std::vector<uint8_t> h = g.header();
+    fwrite(h.data(), 1, h.size(), f);
+    const int nt = s->n_threads > 0 ? s->n_threads : omp_get_max_threads();
+    const bool src_f16 = s->scheme != 0;  // the converter writes f16 sources for every quantized scheme
+    for (size_t i = 0; i < ts.size(); i++) {
+        const T &t = ts[i];
+        const int32_t ty = types[i];
+        const int64_t rb = t.ne0 / blck_size(ty) * type_size(ty);
+        std::vector<uint8_t> buf((size_t)(rb * t.ne1));
+        const uint64_t key = tensor_key(t.name, s->seed);
+#pragma omp parallel for num_threads(nt) schedule(dynamic, 16)
+        for (int64_t r = 0; r < t.ne1; r++) {
+            std::vector<float> row(t.ne0);
+            if (t.kind == 1) std::fill(row.begin(), row.end(), 1.0f);
+            else normal_row(row.data(), r * t.ne0, t.ne0, key, s->w_std);
+            if (src_f16)
+                for (auto &v : row) v = h2f(f2h(v));
+            uint8_t *o = buf.data() + r * rb;
+            switch (ty) {
+                case T_F32: memcpy(o, row.data(), t.ne0 * 4); break;
+                case T_F16: for (int64_t k = 0; k < t.ne0; k++) { const uint16_t v = f2h(row[k]); memcpy(o + 2 * k, &v, 2); } break;
+                case T_Q8_0: for (int64_t b = 0; b < t.ne0 / 32; b++) q80_block(row.data() + 32 * b, o + 34 * b); break;
+                case T_Q4_K: for (int64_t b = 0; b < t.ne0 / 256; b++) q4k_block(row.data() + 256 * b, o + 144 * b); break;
+                case T_Q6_K: for (int64_t b = 0; b < t.ne0 / 256; b++) q6k_block(row.data() + 256 * b, o + 210 * b); break;
+            }
+        }
+        fwrite(buf.data(), 1, buf.size(), f);
+        static const uint8_t zeros[32] = {0};
+        if (buf.size() % 32) fwrite(zeros, 1, 32 - buf.size() % 32, f);
+    }
+    const bool ok = !ferror(f);
+    fclose(f);
+    return ok ? 0 : -1;
+}
+#pragma GCC pop_options

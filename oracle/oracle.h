@@ -88,6 +88,23 @@ int orc_generate(const orc_model *m, const int32_t *prompt, int32_t n_prompt, in
                  const orc_sampler_params *p, int32_t *out_tokens, orc_trace *trace,
                  int32_t mode, int32_t n_threads);
 
+// Step-by-step form of the same loop (teacher-forced checks): a session holds the
+// sequence, masks, persistent logits buffer, inter-step cache and mt19937 of one run.
+typedef struct orc_session orc_session;
+orc_session *orc_sess_new(const orc_model *m, const int32_t *prompt, int32_t n_prompt, int32_t n_gen,
+                          const orc_sampler_params *p, int32_t mode, int32_t n_threads);
+void orc_sess_free(orc_session *s);
+// The forward of `step` (full or cached by the reference's rules); returns the rows computed.
+int orc_sess_forward(orc_session *s, int32_t step);
+// The session's own sampler decision on its logits; returns the commit count.
+int orc_sess_sample(orc_session *s, int32_t step, int32_t *commit_pos, int32_t *commit_tok);
+// Apply commits decided elsewhere (teacher forcing); -1 if a position is not masked.
+int orc_sess_commit(orc_session *s, const int32_t *pos, const int32_t *tok, int32_t n);
+// Rows of the persistent logits buffer.
+int orc_sess_logits(const orc_session *s, int32_t row0, int32_t nrows, float *out);
+// Current sequence [n_prompt + n_gen]; returns the masked count.
+int orc_sess_tokens(const orc_session *s, int32_t *seq_out);
+
 // One sampler decision on a given logits buffer (teacher-forced checks):
 // restates diffuse-sampler.cpp:222-323 for temperature <= 0.  is_masked [total_len]
 // is updated in place, seq too.  Returns the number of committed positions and
@@ -103,6 +120,24 @@ int orc_tokens_to_unmask(int32_t step, int32_t total_steps, int32_t total_masked
 
 // Entropy of one logits row (diffuse-sampler.cpp:34-57).
 float orc_entropy(const float *row, int32_t n_vocab);
+
+// Seeded random-init GGUF written with the oracle's own code (no product library):
+// the converters' metadata and tensor names, weights ~ N(0, w_std) rounded through f16
+// (the converters' f16 output; scheme f32 keeps f32), norms = 1, biases ~ N(0, w_std),
+// blocks by the reference quantize tool's policy and quantizers.  Same bytes as the
+// product's synthesizer for the same spec.
+typedef struct {
+    int32_t  is_dream;
+    int32_t  n_vocab, n_embd, n_head, n_head_kv, n_layer, n_ff, n_ctx, mask_token_id;
+    float    rope_theta, rms_norm_eps;
+    int32_t  scheme;          // 0 f32, 1 f16, 2 q8_0, 3 q4_k_m
+    int32_t  with_bias;
+    int32_t  tied_output;
+    uint64_t seed;
+    float    w_std;
+    int32_t  n_threads;
+} orc_synth_spec;
+int orc_synth_model(const char *path, const orc_synth_spec *spec);
 
 // RoPE angle table of the reference (GGML NEOX): cos/sin[pos][i] for i < n_dims/2.
 int orc_rope_table(int32_t n_pos, int32_t n_dims, float freq_base, float *cos_out, float *sin_out);

@@ -27,6 +27,33 @@ class SamplerParams(C.Structure):
         super().__init__(**{k: (int(v) if isinstance(v, bool) else v) for k, v in d.items()})
 
 
+class SynthSpec(C.Structure):
+    _fields_ = [("is_dream", C.c_int32), ("n_vocab", C.c_int32), ("n_embd", C.c_int32), ("n_head", C.c_int32),
+                ("n_head_kv", C.c_int32), ("n_layer", C.c_int32), ("n_ff", C.c_int32), ("n_ctx", C.c_int32),
+                ("mask_token_id", C.c_int32), ("rope_theta", C.c_float), ("rms_norm_eps", C.c_float),
+                ("scheme", C.c_int32), ("with_bias", C.c_int32), ("tied_output", C.c_int32),
+                ("seed", C.c_uint64), ("w_std", C.c_float), ("n_threads", C.c_int32)]
+
+
+SCHEMES = {"f32": 0, "f16": 1, "q8_0": 2, "q4_k_m": 3}
+
+
+def synth_model(path, arch: dict, scheme: str = "q4_k_m", seed: int = 0, w_std: float = 0.02,
+                tied_output: bool = False, n_threads: int = 0, **overrides):
+    """Seeded random-init GGUF written by the oracle alone (no product library): the
+    same bytes as the product's synthesizer for the same arguments."""
+    a = dict(arch)
+    a.update(overrides)
+    spec = SynthSpec(is_dream=a["is_dream"], n_vocab=a["n_vocab"], n_embd=a["n_embd"], n_head=a["n_head"],
+                     n_head_kv=a["n_head_kv"], n_layer=a["n_layer"], n_ff=a["n_ff"], n_ctx=a.get("n_ctx", 4096),
+                     mask_token_id=a["mask_token_id"], rope_theta=a["rope_theta"], rms_norm_eps=a["rms_norm_eps"],
+                     scheme=SCHEMES[scheme], with_bias=a.get("with_bias", 0), tied_output=int(tied_output),
+                     seed=seed, w_std=w_std, n_threads=n_threads)
+    if lib().orc_synth_model(str(path).encode(), C.byref(spec)) != 0:
+        raise ValueError(f"oracle synth failed for {path}")
+    return str(path)
+
+
 class _Trace(C.Structure):
     _fields_ = [("max_steps", C.c_int32), ("n_gen", C.c_int32), ("steps_run", C.c_int32),
                 ("n_active", C.POINTER(C.c_int32)), ("n_unmask", C.POINTER(C.c_int32)),
@@ -54,6 +81,10 @@ def lib():
             ("orc_sampler_step", I, [P, I, I, P, P, I, I, C.POINTER(SamplerParams), P, P, P, P]),
             ("orc_tokens_to_unmask", I, [I, I, I, I]), ("orc_entropy", C.c_float, [P, I]),
             ("orc_rope_table", I, [I, I, C.c_float, P, P]),
+            ("orc_sess_new", P, [P, P, I, I, C.POINTER(SamplerParams), I, I]), ("orc_sess_free", None, [P]),
+            ("orc_sess_forward", I, [P, I]), ("orc_sess_sample", I, [P, I, P, P]), ("orc_sess_commit", I, [P, P, P, I]),
+            ("orc_sess_logits", I, [P, I, I, P]), ("orc_sess_tokens", I, [P, P]),
+            ("orc_synth_model", I, [C.c_char_p, C.POINTER(SynthSpec)]),
         ]:
             fn = getattr(_lib, name)
             fn.restype, fn.argtypes = res, args
@@ -164,3 +195,50 @@ class OracleModel:
         if self.h:
             lib().orc_free(self.h)
             self.h = None
+
+
+class OracleSession:
+    """One diffuse_sample run of the oracle, step by step (teacher-forced checks): the
+    forward of a step by the reference's full / cached rules, the session's own sampler
+    decision, or commits decided elsewhere."""
+
+    def __init__(self, model: OracleModel, prompt, n_gen, params: SamplerParams, mode=EXACT, n_threads=0):
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        self.model, self.n_prompt, self.n_gen, self.total = model, p.size, n_gen, p.size + n_gen
+        self.params = params
+        self.h = lib().orc_sess_new(model.h, _p(p), p.size, n_gen, C.byref(params), mode, n_threads)
+
+    def forward(self, step: int) -> int:
+        return lib().orc_sess_forward(self.h, step)
+
+    def sample(self, step: int):
+        cp = np.full(max(self.n_gen, 1), -1, np.int32)
+        ct = np.full(max(self.n_gen, 1), -1, np.int32)
+        k = lib().orc_sess_sample(self.h, step, _p(cp), _p(ct))
+        return cp[:k], ct[:k]
+
+    def commit(self, pos, tok):
+        pos = np.ascontiguousarray(pos, dtype=np.int32)
+        tok = np.ascontiguousarray(tok, dtype=np.int32)
+        if lib().orc_sess_commit(self.h, _p(pos), _p(tok), pos.size) != 0:
+            raise ValueError("commit at a position that is not masked")
+
+    def logits(self, row0=0, nrows=None):
+        nrows = self.total - row0 if nrows is None else nrows
+        out = np.empty((nrows, self.model.n_vocab), np.float32)
+        if lib().orc_sess_logits(self.h, row0, nrows, _p(out)) != 0:
+            raise ValueError("rows out of range")
+        return out
+
+    def tokens(self):
+        out = np.empty(self.total, np.int32)
+        n_masked = lib().orc_sess_tokens(self.h, _p(out))
+        return out, n_masked
+
+    def close(self):
+        if self.h:
+            lib().orc_sess_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()

@@ -45,7 +45,10 @@ def orc():
 TINY = dict(hidden=64, heads=4, layers=2, vocab=256, ff=128, mask=200)
 
 
-def write_tiny_gguf(path, dtype=np.float32, dream=False, kv_heads=None, seed=42, bias=False):
+def write_tiny_gguf(path, dtype=np.float32, dream=False, kv_heads=None, seed=42, bias=False, drop=(), as_q5_0=(),
+                    wrong_shape=()):
+    """drop: tensor names left out; as_q5_0: tensors written with GGML type Q5_0 (a type
+    the engine does not take); wrong_shape: tensors written with one row too many."""
     import gguf
     t = TINY
     kvh = kv_heads or t["heads"]
@@ -67,6 +70,20 @@ def write_tiny_gguf(path, dtype=np.float32, dream=False, kv_heads=None, seed=42,
     H, V, F = t["hidden"], t["vocab"], t["ff"]
     def mat(r, c):
         return rng.standard_normal((r, c)).astype(np.float32).astype(dtype)
+    add = w.add_tensor
+
+    def add_tensor(name, arr):
+        if name in drop:
+            return
+        if name in wrong_shape:
+            arr = np.concatenate([arr, arr[:1]], axis=0)
+        if name in as_q5_0:  # 22 bytes per block of 32 values
+            rows = arr.shape[0] if arr.ndim > 1 else 1
+            n = arr.shape[-1]
+            add(name, np.zeros((rows, n // 32 * 22), np.uint8), raw_dtype=gguf.GGMLQuantizationType.Q5_0)
+            return
+        add(name, arr)
+    w.add_tensor = add_tensor
     w.add_tensor("token_embd.weight", mat(V, H))
     w.add_tensor("output_norm.weight", np.ones(H, np.float32).astype(dtype))
     w.add_tensor("output.weight", mat(V, H))
