@@ -55,6 +55,12 @@ class Trace(C.Structure):
                 ("step_ms", C.POINTER(C.c_float)), ("total_ms", C.c_double)]
 
 
+class BatchTrace(C.Structure):
+    _fields_ = [("max_steps", C.c_int32), ("steps_run", C.c_int32), ("n_active", C.POINTER(C.c_int32)),
+                ("n_unmasked", C.POINTER(C.c_int32)), ("fwd_ms", C.POINTER(C.c_float)),
+                ("step_ms", C.POINTER(C.c_float)), ("total_ms", C.c_double)]
+
+
 class SynthSpec(C.Structure):
     _fields_ = [("is_dream", C.c_int32), ("n_vocab", C.c_int32), ("n_embd", C.c_int32), ("n_head", C.c_int32),
                 ("n_head_kv", C.c_int32), ("n_layer", C.c_int32), ("n_ff", C.c_int32), ("n_ctx", C.c_int32),
@@ -95,6 +101,10 @@ def _load():
         (dfb, "dfb_gen_tokens"): (I, [P, P, I]),
         (dfb, "dfb_gen_commits"): (I, [P, P, P, I]),
         (dfb, "dfb_gen_logits"): (I, [P, I, I, P]),
+        (dfb, "dfb_gen_begin_batch"): (I, [P, I, P, P, P, C.POINTER(SamplerParams)]),
+        (dfb, "dfb_gen_step_batch"): (I, [P, I, P, I, P, P]),
+        (dfb, "dfb_gen_commits_batch"): (I, [P, P, P, P, I]),
+        (dfc, "dfc_generate_batch"): (I, [P, P, P, I, I, C.POINTER(SamplerParams), P, P]),
         (dfb, "dfb_ctx_stream"): (I, [P, C.POINTER(P)]),
         (dfc, "dfc_last_error"): (C.c_char_p, []),
         (dfc, "dfc_model_load"): (P, [C.c_char_p, I]),
@@ -282,6 +292,34 @@ class Context:
         info["commit_tok"] = info["commit_tok"].reshape(params.n_steps, n_generate)
         return out, info
 
+    def generate_batch(self, prompts, n_generate: int, params: SamplerParams | None = None, trace: bool = False):
+        """Several independent sequences (prompts: list of 1-D id arrays, any lengths),
+        each running diffuse_generate's loop as alone, stepped together in one forward per
+        step.  Returns ids [n_seq, n_generate] (and a per-step trace dict)."""
+        params = params or SamplerParams()
+        ps = [np.ascontiguousarray(p, dtype=np.int32) for p in prompts]
+        lens = np.array([p.size for p in ps], np.int32)
+        cat = np.ascontiguousarray(np.concatenate(ps) if lens.sum() else np.zeros(1, np.int32), dtype=np.int32)
+        n = len(ps)
+        out = np.empty((n, n_generate), dtype=np.int32)
+        tr = None
+        if trace:
+            S = params.n_steps
+            arrs = dict(n_active=np.zeros((S, n), np.int32), n_unmasked=np.zeros((S, n), np.int32),
+                        fwd_ms=np.zeros(S, np.float32), step_ms=np.zeros(S, np.float32))
+            tr = BatchTrace(max_steps=S, **{k: v.ctypes.data_as(C.POINTER(C.c_int32 if v.dtype == np.int32 else C.c_float))
+                                            for k, v in arrs.items()})
+        rc = native()[1].dfc_generate_batch(self._h, _ptr(cat), _ptr(lens), n, n_generate, C.byref(params), _ptr(out),
+                                            C.byref(tr) if tr is not None else None)
+        if rc < 0:
+            raise DiffuseError(_dfc_err())
+        if not trace:
+            return out
+        info = dict(arrs)
+        info["steps_run"] = tr.steps_run
+        info["total_ms"] = tr.total_ms
+        return out, info
+
     # ── step-level access to the device loop (teacher-forced parity checks) ──
     def gen_begin(self, prompt, n_generate: int, params: SamplerParams):
         p = np.ascontiguousarray(prompt, dtype=np.int32)
@@ -298,6 +336,41 @@ class Context:
         f = st[4:].view(np.float32)
         return dict(n_active=int(st[0]), n_unmasked=int(st[1]), n_masked=int(st[2]), used_cache=int(st[3]),
                     fwd_ms=float(f[0]), step_ms=float(f[1]))
+
+    def gen_begin_batch(self, prompts, n_generate: int, params: SamplerParams):
+        ps = [np.ascontiguousarray(p, dtype=np.int32) for p in prompts]
+        lens = np.array([p.size for p in ps], np.int32)
+        gens = np.full(len(ps), n_generate, np.int32)
+        cat = np.ascontiguousarray(np.concatenate(ps) if lens.sum() else np.zeros(1, np.int32), dtype=np.int32)
+        if native()[0].dfb_gen_begin_batch(self.engine, len(ps), _ptr(cat), _ptr(lens), _ptr(gens), C.byref(params)) != 0:
+            raise DiffuseError(_dfb_err())
+        self._total = int(lens.sum()) + n_generate * len(ps)
+        self._n_seq = len(ps)
+
+    def gen_step_batch(self, step: int, n_unmask, force_full: bool, orders=None) -> list:
+        sched = np.ascontiguousarray(n_unmask, dtype=np.int32)
+        st = np.zeros((self._n_seq, 6), np.int32)
+        o = None if orders is None else np.ascontiguousarray(orders, dtype=np.int32)
+        rc = native()[0].dfb_gen_step_batch(self.engine, step, _ptr(sched), int(force_full),
+                                            None if o is None else _ptr(o), _ptr(st))
+        if rc != 0:
+            raise DiffuseError(_dfb_err())
+        f = st[:, 4:].copy().view(np.float32)
+        return [dict(n_active=int(r[0]), n_unmasked=int(r[1]), n_masked=int(r[2]), used_cache=int(r[3]),
+                     fwd_ms=float(f[i, 0]), step_ms=float(f[i, 1])) for i, r in enumerate(st)]
+
+    def gen_commits_batch(self):
+        pos = np.empty(self._total, np.int32)
+        tok = np.empty(self._total, np.int32)
+        cnt = np.zeros(self._n_seq, np.int32)
+        n = native()[0].dfb_gen_commits_batch(self.engine, _ptr(pos), _ptr(tok), _ptr(cnt), self._total)
+        if n < 0:
+            raise DiffuseError(_dfb_err())
+        out, w = [], 0
+        for c in cnt.tolist():
+            out.append((pos[w:w + c].copy(), tok[w:w + c].copy()))
+            w += c
+        return out
 
     def gen_tokens(self) -> np.ndarray:
         out = np.empty(self._total, np.int32)

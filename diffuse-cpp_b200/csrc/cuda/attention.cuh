@@ -15,6 +15,10 @@
 // round Q, K, P and V to 11 bits, which over 32 layers moves the logits by ~4e-3 of
 // their magnitude; f32 keeps the forward within ~1e-5 of the model's exact mathematics.
 //
+// Work list: tiles {first active row, rows (<= 32), first key position, keys} of one
+// sequence each (several sequences step together, their rows and cache positions
+// concatenated); a CTA takes tile blockIdx.x of one head.
+//
 // One CTA = 32 query rows of one head, 128 threads; key tiles of 64 (cp.async, K of tile
 // t + 1 loading during the P.V of tile t, V of tile t + 1 during the scores of t + 1).
 // Thread (ty, tx) = (tid / 16, tid % 16) owns rows 4 ty .. 4 ty + 3: scores of keys
@@ -23,6 +27,7 @@
 #pragma once
 #include <cuda_fp16.h>
 #include <cstdint>
+#include "dequant.cuh"
 #include "ptx.cuh"
 
 namespace dfb {
@@ -52,14 +57,14 @@ struct AttnSmem {
 template <int HD>
 constexpr int attn_smem_bytes() { return AttnSmem<HD>::bytes; }
 
-// q: [M][ld_q] f32 (head h at h*HD), kc/vc: [n_keys][ld_kv] f32 (kv head at kvh*HD),
-// o: [M][ld_o] f16 pair rows (ld_o = 2 * n_q).
+// q: [rows][ld_q] f32 (head h at h*HD), kc/vc: [positions][ld_kv] f32 (kv head at
+// kvh*HD), o: pair rows of ld_o bytes (4 * n_q, dequant.cuh); tiles / n_tiles: the work list.
 template <int HD>
 __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const float *__restrict__ q, int ld_q,
                                                            const float *__restrict__ kc, const float *__restrict__ vc,
-                                                           int ld_kv, __half *__restrict__ o, int ld_o,
-                                                           const int *__restrict__ m_dev, int n_keys, int n_rep,
-                                                           float scale_log2) {
+                                                           int ld_kv, uint8_t *__restrict__ o, int ld_o,
+                                                           const int4 *__restrict__ tiles, const int *__restrict__ n_tiles_dev,
+                                                           int n_rep, float scale_log2) {
     using L = AttnSmem<HD>;
     constexpr int NC = HD / 4;                   // float4 chunks per row
     constexpr int CPT = (NC + 15) / 16;          // output chunks per thread
@@ -67,10 +72,12 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const float *__restr
     float *Qs = att_smem + L::q_off, *Ks = att_smem + L::k_off, *Vs = att_smem + L::v_off, *Ps = att_smem + L::p_off;
 
     griddep_launch_dependents();
-    griddep_wait();  // q and the K/V cache come from the previous kernels
-    const int M = *m_dev;
-    const int q0 = blockIdx.x * kAttnRows;
-    if (q0 >= M) return;
+    griddep_wait();  // q, the K/V cache and the work list come from the previous kernels
+    if ((int)blockIdx.x >= *n_tiles_dev) return;
+    const int4 tile = tiles[blockIdx.x];
+    const int q0 = tile.x, M = tile.x + tile.y, n_keys = tile.w;
+    kc += (size_t)tile.z * ld_kv;  // the sequence's first cache position
+    vc += (size_t)tile.z * ld_kv;
     const int h = blockIdx.y, kvh = h / n_rep;
     const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
 
@@ -204,22 +211,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const float *__restr
         for (int i = 0; i < CPT; i++) {
             const int c = tx + 16 * i;
             if (c >= NC) continue;
-            const int f = h * HD + 4 * c;  // first of 4 features; pair slice f / 64
-            __half *dst = o + (size_t)row * ld_o + (f >> 6) * 128 + (f & 63);
             float v[4];
-            uint32_t hw[2], lw[2];
 #pragma unroll
             for (int e = 0; e < 4; e++) v[e] = acc[r][i][e] * inv;
-#pragma unroll
-            for (int e = 0; e < 2; e++) {
-                const __half2 hh = __floats2half2_rn(v[2 * e], v[2 * e + 1]);
-                const float2 hf = __half22float2(hh);
-                const __half2 ll = __floats2half2_rn(v[2 * e] - hf.x, v[2 * e + 1] - hf.y);
-                hw[e] = *reinterpret_cast<const uint32_t *>(&hh);
-                lw[e] = *reinterpret_cast<const uint32_t *>(&ll);
-            }
-            *reinterpret_cast<uint2 *>(dst) = make_uint2(hw[0], hw[1]);
-            *reinterpret_cast<uint2 *>(dst + 64) = make_uint2(lw[0], lw[1]);
+            store_pair4(o + (size_t)row * ld_o, h * HD + 4 * c, v);  // features h*HD + 4c .. +3
         }
     }
 }

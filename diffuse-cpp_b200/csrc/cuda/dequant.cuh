@@ -1,18 +1,25 @@
-// Dequantization of re-tiled GGUF weight chunks into hi / lo f16 pairs for the GEMM's
-// A operand (one TMEM lane = one weight row).
+// Dequantization of re-tiled GGUF weight chunks for the GEMM's A operand (one TMEM lane
+// = one weight row), and the operand encodings shared with the activation producers.
 //
 // Each weight is computed in f32 (Q4_K d*sc*q - dmin*m with one rounding; Q6_K
 // d*sc*(q-32) and Q8_0 d*q exactly) after multiplying the block scales by the GEMM's
-// power-of-two pre-scale `ws`, then split: hi = f16(w), lo = f16(w - hi).  hi + lo
-// carries ~22 significant bits.  The block formats are GGML's (Q4_K / Q6_K / Q8_0, the
-// weight-format contract of the reference's GGUF files); the decode rules match
-// gguf-py's dequantizers, which the host codec tests pin.
+// power-of-two pre-scale `ws`, then split into hi = f16(w) and lo = w - hi.  Two forms:
+//   corrected (activations in pair rows, the engine's path): hi as f16 plus the e4m3
+//     pair [hi * 2^-10 | lo] for the correction MMA (kind::f8f6f4), whose B side holds
+//     [x_lo * 2^10 | x_hi]: the two products w_hi x_lo + w_lo x_hi come out at their
+//     true scale and add into the same f32 accumulator as w_hi x_hi;
+//   split (plain f16 activations): hi and lo both as f16.
+// The block formats are GGML's (Q4_K / Q6_K / Q8_0, the weight-format contract of the
+// reference's GGUF files); the decode rules match gguf-py's dequantizers, which the host
+// codec tests pin.
 //
-// The output of one call is one half of a 64-wide k-slice (32 k-values) in 16 registers
-// of f16 pairs per part, in k order (register j holds k = 2j in its low half and 2j + 1
-// in its high half): the layout of one TMEM lane of 16 columns of an f16 A operand.
+// One call produces one half of a 64-wide k-slice (32 k-values) of one row, in k order:
+// f16 pairs (register j holds k = 2j in its low half and 2j + 1 in its high half, the
+// layout of one TMEM lane of 16 columns of an f16 operand) and e4m3 quads (register j
+// holds k = 4j .. 4j + 3 from its low byte up: 8 columns of an 8-bit operand).
 #pragma once
 #include <cuda_fp16.h>
+#include <cuda_fp8.h>
 #include <cstdint>
 
 namespace dfb {
@@ -20,14 +27,43 @@ namespace dfb {
 __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
 __device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
 
-// Two f32 values -> f16 pairs of their hi and lo parts (a in the low halves).  a - hi is
-// exact in f32 (hi holds a's leading 11 bits).
-__device__ __forceinline__ void split2(float a, float b, uint32_t &hi, uint32_t &lo) {
-    const __half2 h = __floats2half2_rn(a, b);
-    const float2 hf = __half22float2(h);
-    hi = h2u(h);
-    lo = h2u(__floats2half2_rn(a - hf.x, b - hf.y));
+// Scale of the hi part inside the correction operand (and 1 / scale of x_lo): keeps
+// w_hi * 2^-10 (|w_hi| <= 2^14 after the weight pre-scale) and x_lo * 2^10 (|x_lo| <=
+// 2^-11 |x|) inside e4m3's range for all but negligible values.
+constexpr float kCorrScale = 1.0f / 1024.0f;
+
+// Two f32 values -> e4m3 pair (a in the low byte), saturating to +-448.
+__host__ __device__ __forceinline__ uint32_t e4m3x2(float a, float b) {
+    return (uint32_t)__nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
 }
+
+// Output of one half-slice in the corrected form.
+struct HalfCorr {
+    uint32_t hi[16];  // f16 pairs
+    uint32_t ch[8];   // e4m3 quads of hi * 2^-10
+    uint32_t cl[8];   // e4m3 quads of lo
+    __device__ __forceinline__ void put4(int j, float w0, float w1, float w2, float w3) {
+        const __half2 h01 = __floats2half2_rn(w0, w1), h23 = __floats2half2_rn(w2, w3);
+        const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+        hi[2 * j] = h2u(h01);
+        hi[2 * j + 1] = h2u(h23);
+        ch[j] = e4m3x2(f01.x * kCorrScale, f01.y * kCorrScale) | (e4m3x2(f23.x * kCorrScale, f23.y * kCorrScale) << 16);
+        cl[j] = e4m3x2(w0 - f01.x, w1 - f01.y) | (e4m3x2(w2 - f23.x, w3 - f23.y) << 16);
+    }
+};
+// Output of one half-slice in the split form (lo exact in f32: hi holds w's leading bits).
+struct HalfSplit {
+    uint32_t hi[16];
+    uint32_t lo[16];
+    __device__ __forceinline__ void put4(int j, float w0, float w1, float w2, float w3) {
+        const __half2 h01 = __floats2half2_rn(w0, w1), h23 = __floats2half2_rn(w2, w3);
+        const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+        hi[2 * j] = h2u(h01);
+        hi[2 * j + 1] = h2u(h23);
+        lo[2 * j] = h2u(__floats2half2_rn(w0 - f01.x, w1 - f01.y));
+        lo[2 * j + 1] = h2u(__floats2half2_rn(w2 - f23.x, w3 - f23.y));
+    }
+};
 
 // Byte k (0..3) of x as the float 2^23 + byte (exact for bytes 0..255).
 template <int K>
@@ -36,13 +72,10 @@ __device__ __forceinline__ float byte_magic(uint32_t x) {
 }
 constexpr float kMagic = 8388608.0f;  // 2^23
 
-// Four elements (bytes of x) through f(value) -> two hi pairs and two lo pairs.
-template <typename F>
-__device__ __forceinline__ void quad(uint32_t x, F f, uint32_t &h01, uint32_t &h23, uint32_t &l01, uint32_t &l23) {
-    const float w0 = f(byte_magic<0>(x)), w1 = f(byte_magic<1>(x));
-    const float w2 = f(byte_magic<2>(x)), w3 = f(byte_magic<3>(x));
-    split2(w0, w1, h01, l01);
-    split2(w2, w3, h23, l23);
+// Four elements (bytes of x) through f(value) into group j of the output.
+template <typename Out, typename F>
+__device__ __forceinline__ void quad(Out &o, int j, uint32_t x, F f) {
+    o.put4(j, f(byte_magic<0>(x)), f(byte_magic<1>(x)), f(byte_magic<2>(x)), f(byte_magic<3>(x)));
 }
 
 // ── Q4_K ── chunk layout (per 128 rows): [d,dmin f16 x2: 4 B/row][scales: 12 B/row at 512]
@@ -77,19 +110,16 @@ __device__ __forceinline__ void q4k_load_meta(const uint8_t *R, int r, int set, 
     }
 }
 // Half h of slice s of row r: the low nibbles of qs bytes 32s .. 32s+31 are sub-block 2s
-// (h = 0), the high nibbles sub-block 2s + 1 (h = 1); l = local meta index.
-__device__ __forceinline__ void q4k_half(const uint8_t *R, int r, int s, int h, float dsc, float nm,
-                                         uint32_t (&hi)[16], uint32_t (&lo)[16]) {
+// (h = 0), the high nibbles sub-block 2s + 1 (h = 1).
+template <typename Out>
+__device__ __forceinline__ void q4k_half(const uint8_t *R, int r, int s, int h, float dsc, float nm, Out &o) {
     const uint8_t *qrow = R + 2048 + 128 * r;
     const uint4 qa = *reinterpret_cast<const uint4 *>(qrow + (((2 * s) ^ (r & 7)) << 4));
     const uint4 qc = *reinterpret_cast<const uint4 *>(qrow + (((2 * s + 1) ^ (r & 7)) << 4));
     const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qc.x, qc.y, qc.z, qc.w};
     auto f = [&](float mg) { return fmaf(mg - kMagic, dsc, nm); };  // q exact, one rounding
 #pragma unroll
-    for (int i = 0; i < 8; i++) {
-        const uint32_t nib = h ? ((w[i] >> 4) & 0x0F0F0F0Fu) : (w[i] & 0x0F0F0F0Fu);
-        quad(nib, f, hi[2 * i], hi[2 * i + 1], lo[2 * i], lo[2 * i + 1]);
-    }
+    for (int i = 0; i < 8; i++) quad(o, i, h ? ((w[i] >> 4) & 0x0F0F0F0Fu) : (w[i] & 0x0F0F0F0Fu), f);
 }
 
 // ── Q6_K ── chunk layout: [ql: 128 B/row, chunk c at c ^ (row & 7)]
@@ -115,8 +145,8 @@ __device__ __forceinline__ void q6k_load_meta(const uint8_t *R, int r, int set, 
 // scales ds0 (first 16) and ds1.  Slice s reads half s / 2 of ql / qh: ql bytes
 // 64 (s/2) .. +63 (low nibbles for even s, high nibbles for odd s), qh bits 2 * (2 (s&1)
 // + (byte >= 32)) of qh bytes 32 (s/2) + (l % 32).
-__device__ __forceinline__ void q6k_half(const uint8_t *R, int r, int s, int hh, float ds0, float ds1,
-                                         uint32_t (&hi)[16], uint32_t (&lo)[16]) {
+template <typename Out>
+__device__ __forceinline__ void q6k_half(const uint8_t *R, int r, int s, int hh, float ds0, float ds1, Out &o) {
     const int h = s >> 1, s2 = s & 1;
     const uint8_t *qlrow = R + 128 * r, *qhrow = R + 16384 + 64 * r;
     // ql bytes 64h + 32hh .. +31 and qh bytes 32h .. +31 (all of them: bit pair by hh)
@@ -133,15 +163,14 @@ __device__ __forceinline__ void q6k_half(const uint8_t *R, int r, int s, int hh,
         const uint32_t nib = s2 ? ((lw[i] >> 4) & 0x0F0F0F0Fu) : (lw[i] & 0x0F0F0F0Fu);
         const uint32_t q6 = nib | (((qw[i] >> shift) & 0x03030303u) << 4);
         const float ds = i < 4 ? ds0 : ds1;
-        auto f = [&](float mg) { return (mg - bias) * ds; };
-        quad(q6, f, hi[2 * i], hi[2 * i + 1], lo[2 * i], lo[2 * i + 1]);
+        quad(o, i, q6, [&](float mg) { return (mg - bias) * ds; });
     }
 }
 
 // ── Q8_0 ── chunk layout: [d f16 x 8: 16 B/row][qs: 256 B/row at 2048, chunk c at
 // (c & 8) | ((c & 7) ^ (row & 7))].  Half h of slice s is block 2s + h.
-__device__ __forceinline__ void q80_half(const uint8_t *R, int r, int s, int h, float ws, uint32_t (&hi)[16],
-                                         uint32_t (&lo)[16]) {
+template <typename Out>
+__device__ __forceinline__ void q80_half(const uint8_t *R, int r, int s, int h, float ws, Out &o) {
     const int blk = 2 * s + h;
     const uint4 dv = *reinterpret_cast<const uint4 *>(R + 16 * r);
     const int wi = blk >> 1;  // may be a runtime value: select, no local array
@@ -156,11 +185,42 @@ __device__ __forceinline__ void q80_half(const uint8_t *R, int r, int s, int h, 
         const uint4 v = *reinterpret_cast<const uint4 *>(qrow + (((c & 8) | ((c & 7) ^ (r & 7))) << 4));
         const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const int j = 4 * cc + i;
-            quad(w[i] ^ 0x80808080u, f, hi[2 * j], hi[2 * j + 1], lo[2 * j], lo[2 * j + 1]);
-        }
+        for (int i = 0; i < 4; i++) quad(o, 4 * cc + i, w[i] ^ 0x80808080u, f);
     }
+}
+
+// ── activation pair rows ── per 64-wide slice: 64 hi f16 (128 B), then the correction
+// operand: 64 e4m3 of x_lo * 2^10, 64 e4m3 of x_hi (128 B); row length 4 bytes per value.
+// Eight consecutive values of a slice: one 16-byte and two 8-byte stores.
+__device__ __forceinline__ void store_pair8(uint8_t *row, int i, const float (&v)[8]) {
+    uint32_t hw[4], cl[2], ch[2];
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+        const __half2 hh = __floats2half2_rn(v[2 * e], v[2 * e + 1]);
+        const float2 hf = __half22float2(hh);
+        hw[e] = h2u(hh);
+        const uint32_t lo = e4m3x2((v[2 * e] - hf.x) * 1024.0f, (v[2 * e + 1] - hf.y) * 1024.0f);
+        const uint32_t hi = e4m3x2(hf.x, hf.y);
+        if (e & 1) { cl[e >> 1] |= lo << 16; ch[e >> 1] |= hi << 16; }
+        else { cl[e >> 1] = lo; ch[e >> 1] = hi; }
+    }
+    uint8_t *slice = row + (i >> 6) * 256;
+    const int k = i & 63;
+    *reinterpret_cast<uint4 *>(slice + 2 * k) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    *reinterpret_cast<uint2 *>(slice + 128 + k) = make_uint2(cl[0], cl[1]);
+    *reinterpret_cast<uint2 *>(slice + 192 + k) = make_uint2(ch[0], ch[1]);
+}
+
+// Four consecutive values of a slice (i % 4 == 0): 8 + 4 + 4 bytes.
+__device__ __forceinline__ void store_pair4(uint8_t *row, int i, const float (&v)[4]) {
+    const __half2 h01 = __floats2half2_rn(v[0], v[1]), h23 = __floats2half2_rn(v[2], v[3]);
+    const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+    uint8_t *slice = row + (i >> 6) * 256;
+    const int k = i & 63;
+    *reinterpret_cast<uint2 *>(slice + 2 * k) = make_uint2(h2u(h01), h2u(h23));
+    *reinterpret_cast<uint32_t *>(slice + 128 + k) =
+        e4m3x2((v[0] - f01.x) * 1024.0f, (v[1] - f01.y) * 1024.0f) | (e4m3x2((v[2] - f23.x) * 1024.0f, (v[3] - f23.y) * 1024.0f) << 16);
+    *reinterpret_cast<uint32_t *>(slice + 192 + k) = e4m3x2(f01.x, f01.y) | (e4m3x2(f23.x, f23.y) << 16);
 }
 
 }  // namespace dfb

@@ -200,8 +200,9 @@ struct WMat {
     int n_rows = 0, n_tiles = 0, K = 0, kb = 0;
     int n_true = 0;     // output features the model defines (before padding / fusion slack)
     float wscale = 1.f; // power-of-two pre-scale of the dequantized weights (quantized types)
+    int lo_row = 0, corr_row = 0;  // f16-tile weights: first row of the lo / correction matrix
     uint8_t *d = nullptr;
-    CUtensorMap tm{};   // f16 tiles (W_F16; W_F32: hi rows [0, n_rows), lo rows [n_rows, 2 n_rows))
+    CUtensorMap tm{};   // f16-tile weights: [hi | (lo, W_F32) | correction] matrices stacked by rows
     size_t bytes = 0;
 };
 
@@ -217,30 +218,39 @@ static int wt_of(int ggml_type) {
 }
 
 // Re-tile rows (nullptr = zero row; rows.size() a multiple of 128) into the chunk
-// layouts the dequant kernel reads (dequant.cuh), or into f16 matrices: W_F16 one [rows][K]
-// matrix, W_F32 (F32 / BF16 sources) the hi matrix followed by the lo matrix.
+// layouts the dequant kernel reads (dequant.cuh), or into stacked [rows][K] matrices of
+// f16-sized elements: W_F16 the weights and their correction matrix, W_F32 (F32 / BF16
+// sources) hi, lo and correction.  A correction row holds, per 64-wide slice, 64 E4M3 of
+// hi * 2^-10 then 64 E4M3 of lo (128 bytes: the width of 64 f16), the weight side of the
+// GEMM's correction MMA (dequant.cuh).
 static void retile_range(const std::vector<const uint8_t *> &rows, int type, int64_t K, int kb, int t0, int t1,
-                         uint8_t *out) {
+                         float ws, uint8_t *out) {
     const int wt = wt_of(type);
     const int RB = raw_chunk_bytes(wt);
     if (wt == W_F16 || wt == W_F32) {
         const size_t n_rows = rows.size();
+        const int n_mats = wt == W_F32 ? 3 : 2;
         for (int r = t0 * 128; r < t1 * 128; r++) {
             uint16_t *dst = reinterpret_cast<uint16_t *>(out) + (size_t)r * K;
-            uint16_t *dlo = reinterpret_cast<uint16_t *>(out) + (n_rows + r) * K;
+            uint16_t *dlo = reinterpret_cast<uint16_t *>(out) + (n_rows + r) * K;  // W_F32 only
+            uint8_t *dcor = out + ((n_mats - 1) * n_rows + r) * K * 2;
             const uint8_t *src = rows[r];
             if (!src) {
-                memset(dst, 0, K * 2);
-                if (wt == W_F32) memset(dlo, 0, K * 2);
+                for (int mi = 0; mi < n_mats; mi++) memset(out + ((size_t)mi * n_rows + r) * K * 2, 0, K * 2);
                 continue;
             }
-            if (type == G_F16) { memcpy(dst, src, K * 2); continue; }
             for (int64_t i = 0; i < K; i++) {
                 float f;
-                if (type == G_F32) memcpy(&f, src + 4 * i, 4);
+                if (type == G_F16) { uint16_t h; memcpy(&h, src + 2 * i, 2); f = h2f_host(h); }
+                else if (type == G_F32) memcpy(&f, src + 4 * i, 4);
                 else { uint16_t b; memcpy(&b, src + 2 * i, 2); f = bf2f_host(b); }
+                f *= ws;  // power of two: F16 values stay exact
                 dst[i] = f2h_host(f);
-                dlo[i] = f2h_host(f - h2f_host(dst[i]));
+                const float hi = h2f_host(dst[i]), lo = f - hi;
+                if (wt == W_F32) dlo[i] = f2h_host(lo);
+                const int64_t sl = i / 64, k = i % 64;
+                dcor[128 * sl + k] = (uint8_t)(e4m3x2(hi * kCorrScale, 0.f) & 0xFF);
+                dcor[128 * sl + 64 + k] = (uint8_t)(e4m3x2(lo, 0.f) & 0xFF);
             }
         }
         return;
@@ -277,14 +287,21 @@ static void retile_range(const std::vector<const uint8_t *> &rows, int type, int
         }
 }
 
-// Upper bound of |w| over rows [r0, r1) of a quantized matrix, from the block scales:
-// Q4_K |d|*63*15 + |dmin|*63, Q6_K |d|*128*32, Q8_0 |d|*128.
+// Upper bound of |w| over rows [r0, r1) of a matrix: quantized types from the block
+// scales (Q4_K |d|*63*15 + |dmin|*63, Q6_K |d|*128*32, Q8_0 |d|*128), float types exactly.
 static float weight_bound_range(const std::vector<const uint8_t *> &rows, int type, int64_t K, size_t r0, size_t r1) {
     float b = 0.f;
     for (size_t r = r0; r < r1; r++) {
         const uint8_t *row = rows[r];
         if (!row) continue;
-        if (type == G_Q4_K) {
+        if (type == G_F16 || type == G_BF16 || type == G_F32) {
+            for (int64_t i = 0; i < K; i++) {
+                float f;
+                if (type == G_F32) memcpy(&f, row + 4 * i, 4);
+                else { uint16_t h; memcpy(&h, row + 2 * i, 2); f = type == G_F16 ? h2f_host(h) : bf2f_host(h); }
+                if (std::isfinite(f)) b = std::max(b, fabsf(f));
+            }
+        } else if (type == G_Q4_K) {
             for (int64_t k = 0; k < K / 256; k++) {
                 uint16_t dh, mh;
                 memcpy(&dh, row + 144 * k, 2);
@@ -325,31 +342,40 @@ static int build_wmat(const std::vector<const uint8_t *> &rows_in, int type, int
     rows.resize((rows.size() + 255) / 256 * 256, nullptr);
     if ((wt == W_Q4K || wt == W_Q6K) && K % 256) return set_err(DFB_ERR_ARG, "K-quant row length %lld not a multiple of 256", (long long)K);
     if (wt == W_Q80 && K % 32) return set_err(DFB_ERR_ARG, "Q8_0 row length %lld not a multiple of 32", (long long)K);
-    if (w_smem(wt) && K % 8) return set_err(DFB_ERR_ARG, "F16/F32 row length %lld not a multiple of 8", (long long)K);
+    if (w_smem(wt) && K % 64) return set_err(DFB_ERR_ARG, "F16/F32 row length %lld not a multiple of 64", (long long)K);
     w.wt = wt;
     w.n_rows = (int)rows.size();
     w.n_tiles = w.n_rows / 128;
     w.K = (int)K;
     w.kb = (int)((K + 255) / 256);
-    w.bytes = wt == W_F16 ? (size_t)w.n_rows * K * 2
-              : wt == W_F32 ? (size_t)2 * w.n_rows * K * 2
-                            : (size_t)w.n_tiles * w.kb * raw_chunk_bytes(wt);
+    const int n_mats = wt == W_F16 ? 2 : wt == W_F32 ? 3 : 0;
+    w.bytes = n_mats ? (size_t)n_mats * w.n_rows * K * 2 : (size_t)w.n_tiles * w.kb * raw_chunk_bytes(wt);
+    w.lo_row = wt == W_F32 ? w.n_rows : 0;
+    w.corr_row = n_mats ? (n_mats - 1) * w.n_rows : 0;
     std::vector<uint8_t> host(w.bytes);
     const int nthr = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
-    std::vector<std::thread> th;
+    // the pre-scale first (f16 tiles are written scaled), then the re-tiling
     std::vector<float> bounds(nthr, 0.f);
-    for (int i = 0; i < nthr; i++) {
-        const int t0 = (int)((int64_t)w.n_tiles * i / nthr), t1 = (int)((int64_t)w.n_tiles * (i + 1) / nthr);
-        th.emplace_back([&, t0, t1, i] {
-            retile_range(rows, type, K, w.kb, t0, t1, host.data());
-            if (!w_smem(wt)) bounds[i] = weight_bound_range(rows, type, K, (size_t)t0 * 128, (size_t)t1 * 128);
-        });
+    {
+        std::vector<std::thread> th;
+        for (int i = 0; i < nthr; i++) {
+            const size_t r0 = (size_t)w.n_rows * i / nthr, r1 = (size_t)w.n_rows * (i + 1) / nthr;
+            th.emplace_back([&, r0, r1, i] { bounds[i] = weight_bound_range(rows, type, K, r0, r1); });
+        }
+        for (auto &t : th) t.join();
     }
-    for (auto &t : th) t.join();
-    w.wscale = w_smem(wt) ? 1.f : weight_prescale(*std::max_element(bounds.begin(), bounds.end()));
+    w.wscale = weight_prescale(*std::max_element(bounds.begin(), bounds.end()));
+    {
+        std::vector<std::thread> th;
+        for (int i = 0; i < nthr; i++) {
+            const int t0 = (int)((int64_t)w.n_tiles * i / nthr), t1 = (int)((int64_t)w.n_tiles * (i + 1) / nthr);
+            th.emplace_back([&, t0, t1] { retile_range(rows, type, K, w.kb, t0, t1, w.wscale, host.data()); });
+        }
+        for (auto &t : th) t.join();
+    }
     CK(cudaMalloc(&w.d, w.bytes));
     CK(cudaMemcpy(w.d, host.data(), w.bytes, cudaMemcpyHostToDevice));
-    if (w_smem(wt)) RET(make_tmap(&w.tm, w.d, (uint64_t)K, (uint64_t)(wt == W_F32 ? 2 : 1) * w.n_rows, 128));
+    if (w_smem(wt)) RET(make_tmap(&w.tm, w.d, (uint64_t)K, (uint64_t)n_mats * w.n_rows, 128));
     return DFB_OK;
 }
 
@@ -597,7 +623,7 @@ struct dfb_ctx {
     // activations
     float *x = nullptr, *y = nullptr, *logits = nullptr;  // residual stream, projection output, logits
     float *q = nullptr, *kc = nullptr, *vc = nullptr;      // Q rows, K/V cache [layer][position][n_kv] (f32)
-    __half *h = nullptr, *att = nullptr, *ffh = nullptr;  // GEMM inputs as pair rows (2 f16 per value)
+    uint8_t *h = nullptr, *att = nullptr, *ffh = nullptr;  // GEMM inputs as pair rows (4 bytes per value)
     float2 *rope = nullptr;
     XMaps xm_h{}, xm_att{}, xm_ffh{};  // GEMM B-operand views of h, att, ffh
     // sequence state
@@ -606,6 +632,12 @@ struct dfb_ctx {
     uint8_t *masked = nullptr;
     int *active_pos = nullptr, *masked_pos = nullptr, *cnt = nullptr;
     float *cand_conf = nullptr, *cand_ent = nullptr;
+    // sequences (segments) stepping together: positions [seg_off[s], seg_off[s+1]) of the
+    // concatenated state; per-segment counters, schedule counts, finished flags, work lists
+    int *seg_off = nullptr, *seg_cnt = nullptr, *sched = nullptr, *tmp_active = nullptr, *tmp_masked = nullptr,
+        *rope_pos = nullptr, *masked_row = nullptr;
+    uint8_t *done = nullptr;
+    int4 *tiles = nullptr;
     // GEMM scratch
     float *ws = nullptr;
     int *tile_cnt = nullptr, *err = nullptr;
@@ -626,15 +658,22 @@ struct dfb_ctx {
     dfb_prof_entry prof_acc[DFB_PROF_N]{};
     // generation
     bool gen_active = false;
-    int n_prompt = 0, n_gen = 0, total = 0, n_masked = 0;
+    int total = 0;                   // positions of all segments
+    int n_seg = 0;
+    std::vector<int> seg_off_h;      // [n_seg + 1]
+    std::vector<int> seg_prompt, seg_gen, seg_masked;  // per segment, host copies
     dfb_sampler_params sp{};
 };
 
 static void ctx_free_buffers(dfb_ctx *c) {
     void *ps[] = {c->x, c->y, c->logits, c->h, c->att, c->q, c->ffh, c->kc, c->vc, c->rope, c->seq, c->prev_seq,
                   c->last_changed, c->cand_tok, c->commit_pos, c->commit_tok, c->order, c->masked, c->active_pos,
-                  c->masked_pos, c->cnt, c->cand_conf, c->cand_ent, c->ws, c->tile_cnt, c->err};
+                  c->masked_pos, c->cnt, c->cand_conf, c->cand_ent, c->ws, c->tile_cnt, c->err, c->seg_off,
+                  c->seg_cnt, c->sched, c->tmp_active, c->tmp_masked, c->rope_pos, c->masked_row, c->done, c->tiles};
     for (void *p : ps) cudaFree(p);
+    c->seg_off = c->seg_cnt = c->sched = c->tmp_active = c->tmp_masked = c->rope_pos = c->masked_row = nullptr;
+    c->done = nullptr;
+    c->tiles = nullptr;
     c->x = c->y = c->logits = c->q = c->kc = c->vc = nullptr; c->h = c->att = c->ffh = nullptr; c->rope = nullptr;
     c->seq = c->prev_seq = c->last_changed = c->cand_tok = c->commit_pos = c->commit_tok = c->order = nullptr;
     c->masked = nullptr; c->active_pos = c->masked_pos = c->cnt = nullptr; c->cand_conf = c->cand_ent = nullptr;
@@ -665,12 +704,15 @@ static int ctx_reserve(dfb_ctx *c, int n) {
     ctx_free_buffers(c);
     const size_t d = hp.n_embd, ff = hp.n_ff, V = hp.n_vocab, L = hp.n_layer, kvd = m->n_kv, hd = m->hd;
 #define AL(ptr, count) CK(cudaMalloc(&(ptr), sizeof(*(ptr)) * (size_t)(count)))
-    AL(c->x, cap * d); AL(c->y, cap * d); AL(c->h, 2 * cap * d); AL(c->att, 2 * cap * d); AL(c->q, cap * d);
-    AL(c->ffh, 2 * cap * ff);
+    AL(c->x, cap * d); AL(c->y, cap * d); AL(c->h, 4 * cap * d); AL(c->att, 4 * cap * d); AL(c->q, cap * d);
+    AL(c->ffh, 4 * cap * ff);
     AL(c->kc, L * cap * kvd); AL(c->vc, L * cap * kvd); AL(c->logits, (size_t)cap * V); AL(c->rope, cap * hd / 2);
     AL(c->seq, cap); AL(c->prev_seq, cap); AL(c->last_changed, cap); AL(c->cand_tok, cap); AL(c->commit_pos, cap);
     AL(c->commit_tok, cap); AL(c->order, cap); AL(c->masked, cap); AL(c->active_pos, cap); AL(c->masked_pos, cap);
     AL(c->cnt, CNT_N); AL(c->cand_conf, cap); AL(c->cand_ent, cap);
+    AL(c->seg_off, kMaxSeg + 1); AL(c->seg_cnt, kMaxSeg * SEG_N); AL(c->sched, kMaxSeg); AL(c->done, kMaxSeg);
+    AL(c->tmp_active, cap); AL(c->tmp_masked, cap); AL(c->rope_pos, cap); AL(c->masked_row, cap);
+    AL(c->tiles, cap / kAttnRows + kMaxSeg + 1);
     AL(c->ws, (size_t)m->n_sm * 2 * kWsTile); AL(c->err, 1);
     const int n_mg_max = (cap + kMaxTok - 1) / kMaxTok;
     int max_tiles = m->lm_head.n_tiles;
@@ -681,6 +723,7 @@ static int ctx_reserve(dfb_ctx *c, int n) {
     CK(cudaMemset(c->tile_cnt, 0, sizeof(int) * c->n_tile_cnt));
     CK(cudaMemset(c->err, 0, sizeof(int)));
     CK(cudaMemset(c->cnt, 0, sizeof(int) * CNT_N));
+    CK(cudaMemset(c->seg_cnt, 0, sizeof(int) * kMaxSeg * SEG_N));
     CK(cudaMemset(c->x, 0, sizeof(float) * cap * d));
     CK(cudaMemset(c->y, 0, sizeof(float) * cap * d));
     CK(cudaMemset(c->h, 0, 4 * cap * d));
@@ -771,7 +814,7 @@ static int gemm_max_pairs(int device, int n_sm) {
     static int cached[64] = {0};
     if (device < 0 || device >= 64) return n_sm / 2;
     if (!cached[device]) {
-        constexpr int smem = gemm_smem_bytes(WT);
+        constexpr int smem = gemm_smem_bytes(WT, XS);
         cudaLaunchConfig_t cfg{};
         cfg.gridDim = dim3(n_sm & ~1);
         cfg.blockDim = dim3(kThreads);
@@ -794,7 +837,8 @@ static GemmParams gemm_params(const WMat &w, const int *m_dev, float *ws, int *t
     p.n_tiles = w.n_tiles;
     p.kb = w.kb;
     p.wscale = w.wscale;
-    p.lo_row = w.n_rows;
+    p.lo_row = w.lo_row;
+    p.corr_row = w.corr_row;
     p.m_dev = m_dev;
     p.ws = ws;
     p.tile_cnt = tile_cnt;
@@ -807,7 +851,7 @@ static GemmParams gemm_params(const WMat &w, const int *m_dev, float *ws, int *t
 template <int WT, int EPI>
 static int launch_gemm_t(dfb_ctx *c, const WMat &w, const XMaps &xm, const EpiArgs &epi) {
     auto kern = dq_gemm_kernel<WT, EPI, 2>;
-    constexpr int smem = gemm_smem_bytes(WT);
+    constexpr int smem = gemm_smem_bytes(WT, 2);
     static bool attr_set[64] = {false};
     const int dev = c->m->device;
     if (!attr_set[dev]) {
@@ -848,6 +892,7 @@ static int launch_gemm(dfb_ctx *c, const WMat &w, const XMaps &xm, const EpiArgs
 }
 
 template <int HD>
+// n_keys: keys per query row (the sequences' length; for the profile's accounting only).
 static int launch_attn_t(dfb_ctx *c, const float *kc, const float *vc, int n_keys) {
     const dfb_model *m = c->m;
     constexpr int smem = attn_smem_bytes<HD>();
@@ -857,12 +902,13 @@ static int launch_attn_t(dfb_ctx *c, const float *kc, const float *vc, int n_key
         attr_set[m->device] = true;
     }
     const float scale_log2 = (1.0f / sqrtf((float)HD)) * 1.4426950408889634f;
-    dim3 grid((c->cap + kAttnRows - 1) / kAttnRows, m->hp.n_head);
+    // work-list bound: tiles of <= 32 active rows of one sequence each
+    dim3 grid(c->cap / kAttnRows + std::max(c->n_seg, 1) + 1, m->hp.n_head);
     cudaEvent_t ev0 = nullptr;
     prof_begin(c, &ev0);
     CK(launch_k(attn_kernel<HD>, grid, dim3(kAttnThreads), smem, c->st, !c->prof, (const float *)c->q, m->n_q, kc, vc,
-                m->n_kv, c->att, 2 * m->n_q, (const int *)(c->cnt + CNT_M), n_keys, m->hp.n_head / m->hp.n_head_kv,
-                scale_log2));
+                m->n_kv, c->att, 4 * m->n_q, (const int4 *)c->tiles, (const int *)(c->cnt + CNT_NTILES),
+                m->hp.n_head / m->hp.n_head_kv, scale_log2));
     // algorithmic bytes: K and V of every key once (f32), Q in (f32), O out (pair rows)
     prof_end(c, ev0, DFB_PROF_ATTN, 4.0 * n_keys * m->hp.n_head * HD, 2.0 * 4.0 * n_keys * m->n_kv, 8.0 * m->n_q);
     return DFB_OK;
@@ -889,7 +935,7 @@ static int run_forward(dfb_ctx *c, int n_total) {
         e.k_cache = kc; e.v_cache = vc; e.ld_kv = m->n_kv;
         e.n_q_tiles = m->nq_pad / 128; e.n_k_tiles = m->nk_pad / 128;
         e.n_q = m->n_q; e.n_kv = m->n_kv; e.head_dim = m->hd;
-        e.bias = L.bias_qkv; e.rope = c->rope; e.pos = c->active_pos;
+        e.bias = L.bias_qkv; e.rope = c->rope; e.pos = c->active_pos; e.rope_pos = c->rope_pos;
         RET(launch_gemm<EPI_QKV>(c, L.qkv, c->xm_h, e));
         switch (m->hd) {
             case 16: RET(launch_attn_t<16>(c, kc, vc, n_total)); break;
@@ -1015,6 +1061,29 @@ extern "C" int dfb_ctx_stream(dfb_ctx *c, void **stream) {
     return DFB_OK;
 }
 
+// Segment layout of the context's state: offsets [n_seg + 1] and finished flags (all 0).
+static int set_segments(dfb_ctx *c, const std::vector<int> &off) {
+    const int n = (int)off.size() - 1;
+    CK(cudaMemcpyAsync(c->seg_off, off.data(), sizeof(int) * off.size(), cudaMemcpyHostToDevice, c->st));
+    CK(cudaMemsetAsync(c->done, 0, n, c->st));
+    c->n_seg = n;
+    c->seg_off_h = off;
+    c->total = off.back();
+    return DFB_OK;
+}
+
+// Active sets and work lists of one step over all segments (seg_prepare + seg_compact).
+static int prepare_step(dfb_ctx *c, int full, int step, int keep_active) {
+    seg_prepare_kernel<<<c->n_seg, 1024, 0, c->st>>>(full, step, keep_active, c->seg_off, c->done, c->seq, c->prev_seq,
+                                                      c->last_changed, c->masked, c->tmp_active, c->tmp_masked,
+                                                      c->seg_cnt);
+    CK(cudaGetLastError());
+    CK(launch_k(seg_compact_kernel, dim3(1), dim3(1024), 0, c->st, false, c->n_seg, (const int *)c->seg_off,
+                (const int *)c->tmp_active, (const int *)c->tmp_masked, c->seg_cnt, c->m->hp.shift_logits, c->active_pos,
+                c->rope_pos, c->masked_pos, c->masked_row, c->tiles, c->cnt));
+    return DFB_OK;
+}
+
 extern "C" int dfb_forward(dfb_ctx *c, const int32_t *tokens, int n, float *logits_host) {
     if (!c || !tokens || !logits_host || n <= 0) return set_err(DFB_ERR_ARG, "bad arguments");
     std::lock_guard<std::mutex> lk(device_lock(c->m->device));
@@ -1024,11 +1093,10 @@ extern "C" int dfb_forward(dfb_ctx *c, const int32_t *tokens, int n, float *logi
         if (tokens[i] < 0 || tokens[i] >= V) return set_err(DFB_ERR_ARG, "token %d at %d outside [0, %d)", tokens[i], i, V);
     RET(ctx_reserve(c, n));
     c->gen_active = false;
+    RET(set_segments(c, {0, n}));
     CK(cudaMemcpyAsync(c->seq, tokens, n * sizeof(int32_t), cudaMemcpyHostToDevice, c->st));
     CK(cudaMemsetAsync(c->masked, 0, n, c->st));
-    step_prepare_kernel<<<1, 1024, 0, c->st>>>(1, 0, 0, n, c->seq, c->prev_seq, c->last_changed, c->masked,
-                                               c->active_pos, c->masked_pos, c->cnt);
-    CK(cudaGetLastError());
+    RET(prepare_step(c, 1, 0, 0));
     RET(run_forward(c, n));
     CK(cudaMemcpyAsync(logits_host, c->logits, (size_t)n * V * sizeof(float), cudaMemcpyDeviceToHost, c->st));
     CK(cudaStreamSynchronize(c->st));
@@ -1059,7 +1127,7 @@ extern "C" int dfb_linear(dfb_ctx *c, int role, int layer, const float *x_host, 
         }
     }
     RET(ctx_reserve(c, M));
-    __half *xh = nullptr;
+    uint8_t *xh = nullptr;
     float *xf = nullptr, *y = nullptr;
     CK(cudaMalloc(&xh, (size_t)M * K * 4));  // pair rows
     CK(cudaMalloc(&xf, (size_t)M * K * 4));
@@ -1111,89 +1179,136 @@ extern "C" int dfb_debug_stalled_linear(dfb_ctx *c, int role, int layer, const f
     return rc;
 }
 
-extern "C" int dfb_gen_begin(dfb_ctx *c, const int32_t *prompt, int n_prompt, int n_gen, const dfb_sampler_params *p) {
-    if (!c || !p || n_prompt < 0 || n_gen <= 0 || (n_prompt > 0 && !prompt)) return set_err(DFB_ERR_ARG, "bad arguments");
+extern "C" int dfb_gen_begin_batch(dfb_ctx *c, int n_seq, const int32_t *prompts, const int32_t *prompt_lens,
+                                   const int32_t *n_gens, const dfb_sampler_params *p) {
+    if (!c || !p || !prompt_lens || !n_gens || n_seq <= 0) return set_err(DFB_ERR_ARG, "bad arguments");
+    if (n_seq > kMaxSeg) return set_err(DFB_ERR_ARG, "%d sequences > %d per context", n_seq, kMaxSeg);
     if (p->temperature > 0.0f)
         return set_err(DFB_ERR_UNSUPPORTED, "temperature > 0 sampling is not implemented on the device path");
     if (p->remasking < 0 || p->remasking > 4) return set_err(DFB_ERR_ARG, "bad remasking %d", p->remasking);
     const dfb_model *m = c->m;
     CK(cudaSetDevice(m->device));
-    const int total = n_prompt + n_gen;
-    for (int i = 0; i < n_prompt; i++)
-        if (prompt[i] < 0 || prompt[i] >= m->hp.n_vocab) return set_err(DFB_ERR_ARG, "prompt token %d out of range", prompt[i]);
-    if (n_gen > 65536) return set_err(DFB_ERR_ARG, "n_generate %d too large", n_gen);
     if (m->hp.mask_token_id < 0 || m->hp.mask_token_id >= m->hp.n_vocab)
         return set_err(DFB_ERR_ARG, "mask token id %d outside the vocabulary", m->hp.mask_token_id);
+    std::vector<int> off(n_seq + 1, 0);
+    size_t n_prompt_all = 0;
+    for (int sg = 0; sg < n_seq; sg++) {
+        if (prompt_lens[sg] < 0 || n_gens[sg] <= 0 || n_gens[sg] > 65536)
+            return set_err(DFB_ERR_ARG, "sequence %d: prompt %d / n_generate %d out of range", sg, prompt_lens[sg], n_gens[sg]);
+        off[sg + 1] = off[sg] + prompt_lens[sg] + n_gens[sg];
+        n_prompt_all += prompt_lens[sg];
+    }
+    if (n_prompt_all > 0 && !prompts) return set_err(DFB_ERR_ARG, "null prompts");
+    for (size_t i = 0; i < n_prompt_all; i++)
+        if (prompts[i] < 0 || prompts[i] >= m->hp.n_vocab) return set_err(DFB_ERR_ARG, "prompt token %d out of range", prompts[i]);
+    const int total = off.back();
     RET(ctx_reserve(c, total));
+    // seq = prompt ‖ MASK x n_gen per sequence (diffuse-sampler.cpp:77-87), concatenated
     std::vector<int32_t> seq(total, m->hp.mask_token_id), neg(total, -1);
-    std::copy(prompt, prompt + n_prompt, seq.begin());
     std::vector<uint8_t> msk(total, 0);
-    std::fill(msk.begin() + n_prompt, msk.end(), 1);
+    size_t pi = 0;
+    for (int sg = 0; sg < n_seq; sg++) {
+        std::copy(prompts + pi, prompts + pi + prompt_lens[sg], seq.begin() + off[sg]);
+        pi += prompt_lens[sg];
+        std::fill(msk.begin() + off[sg] + prompt_lens[sg], msk.begin() + off[sg + 1], 1);
+    }
+    RET(set_segments(c, off));
     CK(cudaMemcpyAsync(c->seq, seq.data(), total * 4, cudaMemcpyHostToDevice, c->st));
     CK(cudaMemcpyAsync(c->prev_seq, neg.data(), total * 4, cudaMemcpyHostToDevice, c->st));
     CK(cudaMemcpyAsync(c->last_changed, neg.data(), total * 4, cudaMemcpyHostToDevice, c->st));
     CK(cudaMemcpyAsync(c->masked, msk.data(), total, cudaMemcpyHostToDevice, c->st));
     CK(cudaMemsetAsync(c->cnt, 0, sizeof(int) * CNT_N, c->st));
+    CK(cudaMemsetAsync(c->seg_cnt, 0, sizeof(int) * kMaxSeg * SEG_N, c->st));
     CK(cudaStreamSynchronize(c->st));
-    c->n_prompt = n_prompt;
-    c->n_gen = n_gen;
-    c->total = total;
-    c->n_masked = n_gen;
+    c->seg_prompt.assign(prompt_lens, prompt_lens + n_seq);
+    c->seg_gen.assign(n_gens, n_gens + n_seq);
+    c->seg_masked.assign(n_gens, n_gens + n_seq);
     c->sp = *p;
     c->gen_active = true;
+    return DFB_OK;
+}
+
+extern "C" int dfb_gen_begin(dfb_ctx *c, const int32_t *prompt, int n_prompt, int n_gen, const dfb_sampler_params *p) {
+    if (n_prompt < 0 || (n_prompt > 0 && !prompt)) return set_err(DFB_ERR_ARG, "bad arguments");
+    return dfb_gen_begin_batch(c, 1, prompt, &n_prompt, &n_gen, p);
+}
+
+extern "C" int dfb_gen_step_batch(dfb_ctx *c, int step, const int32_t *n_unmask_sched, int force_full,
+                                  const int32_t *orders, dfb_step_stats *stats) {
+    if (!c || !n_unmask_sched) return set_err(DFB_ERR_ARG, "null argument");
+    if (!c->gen_active) return set_err(DFB_ERR_STATE, "dfb_gen_begin not called");
+    const dfb_model *m = c->m;
+    std::lock_guard<std::mutex> lk(device_lock(m->device));
+    CK(cudaSetDevice(m->device));
+    const int S = c->n_seg;
+    // a sequence whose loop has ended (no position left masked) takes no part in the step
+    std::vector<int32_t> sched(n_unmask_sched, n_unmask_sched + S);
+    std::vector<uint8_t> done(S);
+    int max_masked = 0, n_live = 0, masked_all = 0;
+    for (int sg = 0; sg < S; sg++) {
+        done[sg] = c->seg_masked[sg] == 0;
+        if (done[sg]) sched[sg] = -1;
+        else n_live++;
+        max_masked = std::max(max_masked, c->seg_masked[sg]);
+        masked_all += c->seg_masked[sg];
+    }
+    if (n_live == 0) return set_err(DFB_ERR_STATE, "every sequence is complete");
+    if (c->sp.remasking == 1) {
+        if (!orders) return set_err(DFB_ERR_ARG, "RANDOM remasking needs the host shuffle orders");
+        CK(cudaMemcpyAsync(c->order, orders, sizeof(int32_t) * masked_all, cudaMemcpyHostToDevice, c->st));
+    }
+    CK(cudaMemcpyAsync(c->sched, sched.data(), sizeof(int32_t) * S, cudaMemcpyHostToDevice, c->st));
+    CK(cudaMemcpyAsync(c->done, done.data(), S, cudaMemcpyHostToDevice, c->st));
+    CK(cudaEventRecord(c->ev[0], c->st));
+    RET(prepare_step(c, force_full ? 1 : 0, step, c->sp.cache_keep_active));
+    RET(run_forward(c, c->total / S));
+    CK(cudaEventRecord(c->ev[1], c->st));
+    const int margin = c->sp.remasking == 4 ? 1 : 0;
+    row_stats_kernel<<<masked_all, 512, 0, c->st>>>(c->logits, m->hp.n_vocab, c->masked_row, c->cnt, margin, c->cand_tok,
+                                                    c->cand_conf, c->cand_ent);
+    CK(cudaGetLastError());
+    int np = 1;
+    while (np < max_masked) np <<= 1;
+    const size_t sel_smem = sizeof(unsigned long long) * (size_t)np;
+    if (sel_smem > 48 * 1024) CK(cudaFuncSetAttribute(select_commit_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sel_smem));
+    select_commit_kernel<<<S, 1024, sel_smem, c->st>>>(c->sp.remasking, c->sched, c->sp.entropy_threshold, np, c->order,
+                                                       c->masked_pos, c->cand_tok, c->cand_conf, c->cand_ent, c->seq,
+                                                       c->masked, c->commit_pos, c->commit_tok, c->seg_cnt);
+    CK(cudaGetLastError());
+    CK(cudaEventRecord(c->ev[2], c->st));
+    int h_cnt[CNT_N];
+    std::vector<int> h_seg((size_t)S * SEG_N);
+    CK(cudaMemcpyAsync(h_cnt, c->cnt, sizeof(h_cnt), cudaMemcpyDeviceToHost, c->st));
+    CK(cudaMemcpyAsync(h_seg.data(), c->seg_cnt, sizeof(int) * h_seg.size(), cudaMemcpyDeviceToHost, c->st));
+    CK(cudaStreamSynchronize(c->st));
+    prof_collect(c, h_cnt[CNT_M]);
+    RET(check_err(c));
+    float fwd = 0, all = 0;
+    cudaEventElapsedTime(&fwd, c->ev[0], c->ev[1]);
+    cudaEventElapsedTime(&all, c->ev[0], c->ev[2]);
+    for (int sg = 0; sg < S; sg++) {
+        const int *hs = &h_seg[(size_t)sg * SEG_N];
+        if (hs[SEG_ERR]) return set_err(DFB_ERR_STATE, "sequence %d: device and host disagree on the masked count", sg);
+        if (!done[sg] && hs[SEG_NMASK] != c->seg_masked[sg] - hs[SEG_COMMITTED])
+            return set_err(DFB_ERR_STATE, "sequence %d: masked count out of step", sg);
+        c->seg_masked[sg] = done[sg] ? 0 : hs[SEG_NMASK];
+        if (stats) {
+            stats[sg].n_active = hs[SEG_NACT];
+            stats[sg].n_unmasked = hs[SEG_COMMITTED];
+            stats[sg].n_masked = c->seg_masked[sg];
+            stats[sg].used_cache = hs[SEG_USED_CACHE];
+            stats[sg].fwd_ms = fwd;
+            stats[sg].step_ms = all;
+        }
+    }
     return DFB_OK;
 }
 
 extern "C" int dfb_gen_step(dfb_ctx *c, int step, int n_unmask_sched, int force_full, const int32_t *order,
                             dfb_step_stats *stats) {
     if (!c) return set_err(DFB_ERR_ARG, "null context");
-    if (!c->gen_active) return set_err(DFB_ERR_STATE, "dfb_gen_begin not called");
-    const dfb_model *m = c->m;
-    std::lock_guard<std::mutex> lk(device_lock(m->device));
-    CK(cudaSetDevice(m->device));
-    if (c->sp.remasking == 1) {
-        if (!order) return set_err(DFB_ERR_ARG, "RANDOM remasking needs the host shuffle order");
-        CK(cudaMemcpyAsync(c->order, order, sizeof(int32_t) * c->n_masked, cudaMemcpyHostToDevice, c->st));
-    }
-    CK(cudaEventRecord(c->ev[0], c->st));
-    step_prepare_kernel<<<1, 1024, 0, c->st>>>(force_full ? 1 : 0, step, c->sp.cache_keep_active, c->total, c->seq,
-                                               c->prev_seq, c->last_changed, c->masked, c->active_pos, c->masked_pos,
-                                               c->cnt);
-    CK(cudaGetLastError());
-    RET(run_forward(c, c->total));
-    CK(cudaEventRecord(c->ev[1], c->st));
-    const int margin = c->sp.remasking == 4 ? 1 : 0;
-    row_stats_kernel<<<c->n_gen, 512, 0, c->st>>>(c->logits, m->hp.n_vocab, m->hp.shift_logits, c->masked_pos, c->cnt,
-                                                  margin, c->cand_tok, c->cand_conf, c->cand_ent);
-    CK(cudaGetLastError());
-    int np = 1;
-    while (np < c->n_masked) np <<= 1;
-    const size_t sel_smem = sizeof(unsigned long long) * (size_t)np;
-    if (sel_smem > 48 * 1024) CK(cudaFuncSetAttribute(select_commit_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sel_smem));
-    select_commit_kernel<<<1, 1024, sel_smem, c->st>>>(c->sp.remasking, n_unmask_sched, c->sp.entropy_threshold, np,
-                                                       c->order, c->masked_pos, c->cand_tok, c->cand_conf, c->cand_ent,
-                                                       c->seq, c->masked, c->commit_pos, c->commit_tok, c->cnt);
-    CK(cudaGetLastError());
-    CK(cudaEventRecord(c->ev[2], c->st));
-    int h_cnt[CNT_N];
-    CK(cudaMemcpyAsync(h_cnt, c->cnt, sizeof(h_cnt), cudaMemcpyDeviceToHost, c->st));
-    CK(cudaStreamSynchronize(c->st));
-    prof_collect(c, h_cnt[CNT_M]);
-    RET(check_err(c));
-    if (h_cnt[CNT_ERR]) return set_err(DFB_ERR_STATE, "device and host disagree on the masked count");
-    c->n_masked = h_cnt[CNT_NMASKED];
-    if (stats) {
-        stats->n_active = h_cnt[CNT_M];
-        stats->n_unmasked = h_cnt[CNT_COMMITTED];
-        stats->n_masked = h_cnt[CNT_NMASKED];
-        stats->used_cache = h_cnt[CNT_USED_CACHE];
-        float a = 0, b = 0;
-        cudaEventElapsedTime(&a, c->ev[0], c->ev[1]);
-        cudaEventElapsedTime(&b, c->ev[0], c->ev[2]);
-        stats->fwd_ms = a;
-        stats->step_ms = b;
-    }
-    return DFB_OK;
+    if (c->gen_active && c->n_seg != 1) return set_err(DFB_ERR_STATE, "batch generation: use dfb_gen_step_batch");
+    return dfb_gen_step_batch(c, step, &n_unmask_sched, force_full, order, stats);
 }
 
 extern "C" int dfb_gen_tokens(dfb_ctx *c, int32_t *seq_host, int cap) {
@@ -1205,16 +1320,33 @@ extern "C" int dfb_gen_tokens(dfb_ctx *c, int32_t *seq_host, int cap) {
     return DFB_OK;
 }
 
+extern "C" int dfb_gen_commits_batch(dfb_ctx *c, int32_t *pos_host, int32_t *tok_host, int32_t *counts, int cap) {
+    if (!c || !pos_host || !tok_host || !counts) return set_err(DFB_ERR_ARG, "null pointer");
+    if (!c->gen_active) return set_err(DFB_ERR_STATE, "no generation");
+    const int S = c->n_seg;
+    std::vector<int> h_seg((size_t)S * SEG_N);
+    CK(cudaMemcpyAsync(h_seg.data(), c->seg_cnt, sizeof(int) * h_seg.size(), cudaMemcpyDeviceToHost, c->st));
+    CK(cudaStreamSynchronize(c->st));
+    int w = 0;
+    for (int sg = 0; sg < S; sg++) {
+        const int n = h_seg[(size_t)sg * SEG_N + SEG_COMMITTED], off = h_seg[(size_t)sg * SEG_N + SEG_MOFF];
+        if (w + n > cap) return set_err(DFB_ERR_ARG, "buffer of %d commits too small", cap);
+        counts[sg] = n;
+        if (n) {
+            CK(cudaMemcpyAsync(pos_host + w, c->commit_pos + off, n * 4, cudaMemcpyDeviceToHost, c->st));
+            CK(cudaMemcpyAsync(tok_host + w, c->commit_tok + off, n * 4, cudaMemcpyDeviceToHost, c->st));
+        }
+        w += n;
+    }
+    CK(cudaStreamSynchronize(c->st));
+    return w;
+}
+
 extern "C" int dfb_gen_commits(dfb_ctx *c, int32_t *pos_host, int32_t *tok_host, int cap) {
-    if (!c || !pos_host || !tok_host) return set_err(DFB_ERR_ARG, "null pointer");
-    int h_cnt[CNT_N];
-    CK(cudaMemcpyAsync(h_cnt, c->cnt, sizeof(h_cnt), cudaMemcpyDeviceToHost, c->st));
-    CK(cudaStreamSynchronize(c->st));
-    const int n = std::min(h_cnt[CNT_COMMITTED], cap);
-    CK(cudaMemcpyAsync(pos_host, c->commit_pos, n * 4, cudaMemcpyDeviceToHost, c->st));
-    CK(cudaMemcpyAsync(tok_host, c->commit_tok, n * 4, cudaMemcpyDeviceToHost, c->st));
-    CK(cudaStreamSynchronize(c->st));
-    return n;
+    if (!c) return set_err(DFB_ERR_ARG, "null context");
+    if (c->gen_active && c->n_seg != 1) return set_err(DFB_ERR_STATE, "batch generation: use dfb_gen_commits_batch");
+    int32_t count = 0;
+    return dfb_gen_commits_batch(c, pos_host, tok_host, &count, cap);
 }
 
 extern "C" int dfb_gen_logits(dfb_ctx *c, int row0, int nrows, float *host) {
@@ -1263,7 +1395,7 @@ template <int WT>
 int noalloc_launch(const WMat &w, const XMaps &xm, const EpiArgs &e, const NoallocDev &nd, int device, cudaStream_t st) {
     // the caller's x is a plain f16 matrix: one activation part (W_hi.x + W_lo.x)
     auto kern = dq_gemm_kernel<WT, EPI_F32, 1>;
-    constexpr int smem = gemm_smem_bytes(WT);
+    constexpr int smem = gemm_smem_bytes(WT, 1);
     static bool attr_set[64] = {false};  // once per device (the caller holds the device lock)
     if (!attr_set[device & 63]) {
         CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));

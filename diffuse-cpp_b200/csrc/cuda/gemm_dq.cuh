@@ -3,18 +3,23 @@
 // Replaces every ggml_mul_mat(W, x) of the reference forward (src/diffuse-graph.cpp
 // :61-63, 122, 136-140, 154 and the cached variants :451-453, 556, 570-574, 587).
 //
-// Precision.  The products are those of the model's f32 mathematics to ~2^-22: each
-// operand is carried as an unevaluated sum of two f16 values (hi = f16(v), lo =
-// f16(v - hi), ~22 significant bits) and the MMA computes W_hi.X_hi + W_hi.X_lo +
-// W_lo.X_hi (the dropped W_lo.X_lo term is ~2^-22 of the product) into one f32
-// accumulator.  Quantized weights are dequantized in f32 (exact: Q4_K d*sc*q - dmin*m is
-// one f32 rounding, Q6_K / Q8_0 products are exact) after a power-of-two pre-scale that
-// keeps W_lo in f16's normal range; the epilogue undoes the scale.  F16 weights are
-// exact as they are (two MMAs); F32 / BF16 weights are stored as hi and lo f16 matrices.
+// Precision.  Each operand is split, v = hi + lo with hi = f16(v), and the product is
+// W_hi.X_hi + W_hi.X_lo + W_lo.X_hi in one f32 accumulator (the dropped W_lo.X_lo term is
+// ~2^-22 of it): the main term as an f16 MMA, the two corrections (~2^-11 of it, needed
+// to ~5 bits) as one E4M3 MMA (kind::f8f6f4, twice the f16 rate) over the operand pairs
+// [W_hi 2^-10 | W_lo] x [X_lo 2^10 | X_hi], whose products land at their true scale.
+// Per element that is ~2^-17 of the product, below the f32 accumulation error over K.
+// Quantized weights are dequantized in f32 (exact: Q4_K d*sc*q - dmin*m is one f32
+// rounding, Q6_K / Q8_0 products are exact) after a power-of-two pre-scale that puts the
+// largest near 2^14; the epilogue undoes the scale.  F16 / F32 / BF16 weights come as
+// precomputed f16 hi and E4M3 correction matrices.  For plain f16 activations (XS = 1, the
+// allocation-free entry point) the weights are split into f16 hi and lo instead (two f16
+// MMAs, exact products).
 //
 // Operands.  W is the GGUF weight (Q4_K / Q6_K / Q8_0 raw blocks re-tiled at load, or
 // f16 matrices); X is the activation matrix [tokens][K] in "pair" layout: per 64-wide
-// k-slice, 64 hi values then 64 lo values (row length 2K f16).  The MMA is "swap-AB" and
+// k-slice, 64 hi f16 then 64 E4M3 X_lo 2^10 and 64 E4M3 X_hi (256 bytes, dequant.cuh).
+// The MMA is "swap-AB" and
 // paired (tcgen05 cta_group::2, M = 256): the A operand is a tile of 256 output
 // features, 128 dequantized into the TMEM of each CTA of a pair (f16 weights: TMA-loaded
 // into shared memory, 128-byte-swizzled K-major); the B operand is a group of up to 256
@@ -35,6 +40,7 @@
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cstdint>
+#include <type_traits>
 #include "dequant.cuh"
 #include "ptx.cuh"
 
@@ -68,7 +74,8 @@ struct EpiArgs {
     int n_q = 0, n_kv = 0, head_dim = 0;
     const float *bias = nullptr;       // [(n_q_tiles + 2 n_k_tiles) * 128], section-padded, original order
     const float2 *rope = nullptr;      // [position][head_dim/2] (cos, sin)
-    const int *pos = nullptr;          // [tokens] position of each row (QKV, LOGITS)
+    const int *pos = nullptr;          // [tokens] position of each row (QKV cache rows, LOGITS rows)
+    const int *rope_pos = nullptr;     // [tokens] position within its sequence (QKV RoPE angles)
 };
 
 // Activation tensor maps, one per token half-group size h = 16 (i + 1), i = 0..7: a 3-D
@@ -89,7 +96,8 @@ struct GemmParams {
     int n_tiles = 0;             // 128-row output tiles
     int kb = 0;                  // k-blocks of 256
     float wscale = 1.f;          // power-of-two pre-scale of the dequantized weights
-    int lo_row = 0;              // W_F32: row of the lo matrix in the weight tensor map
+    int lo_row = 0;              // f16 tile weights: row of the lo matrix (W_F32) in the tensor map
+    int corr_row = 0;            // f16 tile weights: row of the correction matrix in the tensor map
     const int *m_dev = nullptr;  // token count (device)
     float *ws = nullptr;         // split-tile partials [grid][2][256 * 128]
     int *tile_cnt = nullptr;     // [n_tiles x token groups] arrival + departure counters, left at 0
@@ -111,7 +119,8 @@ constexpr int kMaxAStages = 6, kMaxBSlots = 24, kMaxRawStages = 4;
 // to 192, one accumulator [0, 256) for larger groups (the MMA of the next segment then
 // waits for the epilogue to drain it, which costs less than dequantizing the weights once
 // per group of 128); dequantized A stages (quantized weights) at [384 + 64 st, +64):
-// lane = weight row, one k-slice each, hi part in the first 32 columns, lo in the next.
+// lane = weight row, one k-slice each: f16 hi in the first 32 columns, then the E4M3
+// correction pair (16 columns W_hi 2^-10, 16 columns W_lo), or f16 lo for XS = 1.
 constexpr int kTmemA = 2 * kDblTok;
 constexpr int kTmemAStage = 64;
 constexpr int kTmemALo = 32;
@@ -126,8 +135,12 @@ constexpr int kNA = 2;                   // A stages: set p of the dequantizers 
 //           keep many slices in flight and hide the L2 latency;
 //  raw ring re-tiled weight chunks (one k-block of 256 for 128 rows), grouped.
 __host__ __device__ constexpr int a_stages(int wt) { return kNA; }
-__host__ __device__ constexpr int a_stage_bytes(int wt) { return wt == W_F32 ? 2 * kSliceBytes : kSliceBytes; }
-__host__ __device__ constexpr int a_ring_bytes(int wt) { return w_smem(wt) ? kNA * a_stage_bytes(wt) : 0; }
+// f16 tile weights: XS = 2 stages hold the hi and correction tiles, XS = 1 the hi tile
+// (and the lo tile of W_F32)
+__host__ __device__ constexpr int a_stage_bytes(int wt, int xs) {
+    return (xs == 2 || wt == W_F32) ? 2 * kSliceBytes : kSliceBytes;
+}
+__host__ __device__ constexpr int a_ring_bytes(int wt, int xs) { return w_smem(wt) ? kNA * a_stage_bytes(wt, xs) : 0; }
 __host__ __device__ constexpr int b_ring_bytes(int wt) { return 96 * 1024; }
 // A raw stage holds raw_cpr consecutive chunks of the CTA's unit range: the weight
 // stream reached ~3.8 TB/s with 18 KB stages and ~6-7 TB/s with 36-72 KB stages
@@ -153,9 +166,9 @@ __host__ __device__ constexpr int epi_half(int w) { return w >= 16 ? 1 : 0; }
 constexpr int kEpiStageBytes = 16 * 128 * 4;  // epilogue output staging per half: 16 tokens x 128 f32
 constexpr int kMaxContrib = 64;     // split contributors (CTA pairs) of one tile tracked in shared memory
 constexpr int kBarBytes = 80 * 8;   // mbarriers and flags, see the kernel's shared-memory map
-__host__ __device__ constexpr int gemm_smem_bytes(int wt) {
-    return 1024 /*align slack*/ + a_ring_bytes(wt) + b_ring_bytes(wt) + raw_stages(wt) * raw_cpr(wt) * raw_chunk_bytes(wt) +
-           2 * kEpiStageBytes /*epilogue output staging*/ + kBarBytes /*barriers, flags*/ + 4 * kMaxTok /*token positions*/ + 8 * kMaxContrib /*contributor partial offsets*/;
+__host__ __device__ constexpr int gemm_smem_bytes(int wt, int xs) {
+    return 1024 /*align slack*/ + a_ring_bytes(wt, xs) + b_ring_bytes(wt) + raw_stages(wt) * raw_cpr(wt) * raw_chunk_bytes(wt) +
+           2 * kEpiStageBytes /*epilogue output staging*/ + kBarBytes /*barriers, flags*/ + 8 * kMaxTok /*token positions*/ + 8 * kMaxContrib /*contributor partial offsets*/;
 }
 
 // Static stream-K schedule over CTA pairs, recomputed identically by every role of
@@ -273,7 +286,7 @@ __device__ __forceinline__ EpiRow epi_row(const EpiArgs &e, int tile, int row) {
 
 // Output staging: a chunk of 16 tokens x the tile's output features, one per epilogue
 // half, written by the row threads and stored to global memory as whole token rows.
-// SwiGLU rows hold the tile's 64 features as a pair-layout slice (64 hi f16 then 64 lo).
+// SwiGLU rows hold the tile's 64 features as one pair-layout slice (256 bytes).
 template <int EPI> struct EpiFmt {
     static constexpr int esize = EPI == EPI_SWIGLU ? 2 : 4;
     static constexpr int width = 128;                  // staged elements per token row
@@ -329,7 +342,7 @@ __device__ __forceinline__ EpiDst epi_dst(const EpiArgs &e, int tile) {
 // epilogues exchange values with the neighbouring lane).  s_pos: positions of the
 // segment's tokens (shared memory).
 template <int EPI>
-__device__ __forceinline__ void epi_values(const EpiArgs &e, const EpiRow &r, const int *s_pos, int tl0, int ntok,
+__device__ __forceinline__ void epi_values(const EpiArgs &e, const EpiRow &r, const int *s_rpos, int tl0, int ntok,
                                            float (&v)[16], uint8_t *stage) {
     constexpr int RB = EpiFmt<EPI>::row_bytes;
 #pragma unroll
@@ -342,12 +355,15 @@ __device__ __forceinline__ void epi_values(const EpiArgs &e, const EpiRow &r, co
         for (int i = 0; i < 16; i++) {
             const float up = __shfl_xor_sync(0xffffffffu, v[i], 1);
             const float g = v[i];
-            const float hv = (g * up) / (1.0f + expf(-g));  // silu(g) * up (ggml_silu, ggml_mul)
-            if (r.writer) {
+            const float hv = (g / (1.0f + expf(-g))) * up;  // silu(g) * up (ggml_silu, ggml_mul)
+            if (r.writer) {  // pair-layout slice: hi f16, then E4M3 lo 2^10, E4M3 hi
                 const __half hh = __float2half_rn(hv);
-                __half *row = reinterpret_cast<__half *>(stage + i * RB);
-                row[r.col] = hh;
-                row[64 + r.col] = __float2half_rn(hv - __half2float(hh));
+                const float hf = __half2float(hh);
+                uint8_t *row = stage + i * RB;
+                reinterpret_cast<__half *>(row)[r.col] = hh;
+                const uint32_t c2 = e4m3x2((hv - hf) * 1024.0f, hf);
+                row[128 + r.col] = (uint8_t)(c2 & 0xFF);
+                row[192 + r.col] = (uint8_t)(c2 >> 8);
             }
         }
     } else if constexpr (EPI == EPI_QKV) {
@@ -356,7 +372,7 @@ __device__ __forceinline__ void epi_values(const EpiArgs &e, const EpiRow &r, co
             float2 csv[16];
 #pragma unroll
             for (int i = 0; i < 16; i++) {
-                const int pp = tl0 + i < ntok ? s_pos[tl0 + i] : 0;
+                const int pp = tl0 + i < ntok ? s_rpos[tl0 + i] : 0;
                 csv[i] = __ldg(e.rope + (size_t)pp * hh + r.ipair);
             }
 #pragma unroll
@@ -430,8 +446,8 @@ template <int WT, int EPI, int XS>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     dq_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ XMaps xm, GemmParams p) {
     constexpr int RAWB = raw_chunk_bytes(WT);
-    constexpr int NA = a_stages(WT), NRAW = raw_stages(WT), BRING = b_ring_bytes(WT), AR = a_ring_bytes(WT);
-    constexpr int ASB = a_stage_bytes(WT);
+    constexpr int NA = a_stages(WT), NRAW = raw_stages(WT), BRING = b_ring_bytes(WT), AR = a_ring_bytes(WT, XS);
+    constexpr int ASB = a_stage_bytes(WT, XS);
     constexpr int CPR = raw_cpr(WT), RSB = CPR * RAWB;  // chunks and bytes per raw stage
     static_assert(XS == 1 || XS == 2, "activation parts");
     static_assert(NA == 2, "dequantizer set p fills A stage p");
@@ -453,7 +469,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 75);
     volatile int *okflag = reinterpret_cast<volatile int *>(bars + 77);
     int *s_pos = reinterpret_cast<int *>(bars + kBarBytes / 8);                   // [kMaxTok]
-    long long *s_contrib = reinterpret_cast<long long *>(s_pos + kMaxTok);        // [kMaxContrib]
+    int *s_rpos = s_pos + kMaxTok;                                                // [kMaxTok]
+    long long *s_contrib = reinterpret_cast<long long *>(s_rpos + kMaxTok);       // [kMaxContrib]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = cluster_ctarank();
@@ -576,9 +593,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                             if (rank == 0) mbar_arrive_expect_tx(&full_a[st], 2 * ASB);
                             const int row = (2 * g.pt + (int)rank) * 128;
                             tma_load_2d_pair(aring + st * ASB, &tm_w, kbi * 256 + s * 64, row, full_a0 + 8 * st);
-                            if constexpr (WT == W_F32)
-                                tma_load_2d_pair(aring + st * ASB + kSliceBytes, &tm_w, kbi * 256 + s * 64, p.lo_row + row,
-                                                 full_a0 + 8 * st);
+                            if constexpr (ASB == 2 * kSliceBytes)
+                                tma_load_2d_pair(aring + st * ASB + kSliceBytes, &tm_w, kbi * 256 + s * 64,
+                                                 (XS == 2 ? p.corr_row : p.lo_row) + row, full_a0 + 8 * st);
                             it++;
                         }
                     }
@@ -630,17 +647,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         // full_a also carries the relays' arrivals: this stage's B rows have landed
                         if (!(ok = mbar_wait(&full_a[st], (uint32_t)(s2 >> 1), abort_flag, p.err, kErrTimeout + 5, p.timeout_ns))) break;
                         tc_fence_after();
-                        const uint64_t bhi = bd[s2], blo = bd[s2] + (uint64_t)(bsub >> 4);
+                        // main term (f16), then the corrections: XS = 2 one E4M3 MMA over the
+                        // correction pairs, XS = 1 W_lo.X (f16) for weights with a lo part
+                        const uint64_t bhi = bd[s2], bcor = bd[s2] + (uint64_t)(bsub >> 4);
                         if constexpr (w_smem(WT)) {
                             const uint64_t ahi = adesc0 + (uint64_t)((st * ASB) >> 4);
+                            const uint64_t a2 = ahi + (uint64_t)(kSliceBytes >> 4);
                             mma2_f16_ss_k64(d_tmem, ahi, bhi, idesc, accum);
-                            if constexpr (XS == 2) mma2_f16_ss_k64(d_tmem, ahi, blo, idesc, 1);
-                            if constexpr (w_split(WT)) mma2_f16_ss_k64(d_tmem, ahi + (uint64_t)(kSliceBytes >> 4), bhi, idesc, 1);
+                            if constexpr (XS == 2) mma2_f8_ss_k128(d_tmem, a2, bcor, idesc);
+                            else if constexpr (w_split(WT)) mma2_f16_ss_k64(d_tmem, a2, bhi, idesc, 1);
                         } else {
                             const uint32_t ahi = tmem_base + kTmemA + st * kTmemAStage;
                             mma2_f16_ts_k64(d_tmem, ahi, bhi, idesc, accum);
-                            if constexpr (XS == 2) mma2_f16_ts_k64(d_tmem, ahi, blo, idesc, 1);
-                            mma2_f16_ts_k64(d_tmem, ahi + kTmemALo, bhi, idesc, 1);
+                            if constexpr (XS == 2) mma2_f8_ts_k128(d_tmem, ahi + kTmemALo, bcor, idesc);
+                            else mma2_f16_ts_k64(d_tmem, ahi + kTmemALo, bhi, idesc, 1);
                         }
                         accum = 1;
                         mma2_commit_mc(&empty_a[st], 0x3);
@@ -745,31 +765,41 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     }
                     const uint8_t *R = raw + rs * RSB + (rit % CPR) * RAWB;
                     // this set's k-slices of the k-block: set and set + 2, both into A stage
-                    // `set`; each slice in two halves of 32 k (hi and lo parts, 16 columns each)
+                    // `set`; each slice in two halves of 32 k.  XS = 2: f16 hi (16 columns per
+                    // half), E4M3 hi 2^-10 and E4M3 lo (8 columns per half each, at 32 and 48);
+                    // XS = 1: f16 hi and f16 lo (16 columns per half each, at 0 and 32).
+                    using Half = typename std::conditional<XS == 2, HalfCorr, HalfSplit>::type;
                     [[maybe_unused]] Q4KMeta m4;
                     [[maybe_unused]] Q6KMeta m6;
                     if constexpr (WT == W_Q4K) q4k_load_meta(R, r, set, p.wscale, m4);
                     if constexpr (WT == W_Q6K) q6k_load_meta(R, r, set, p.wscale, m6);
-                    auto deq = [&](int hs, int hh, uint32_t (&hi)[16], uint32_t (&lo)[16]) {
+                    auto deq = [&](int hs, int hh, Half &o) {
                         const int sl = set + 2 * hs;
-                        if constexpr (WT == W_Q4K) q4k_half(R, r, sl, hh, m4.dsc[2 * hs + hh], m4.nm[2 * hs + hh], hi, lo);
+                        if constexpr (WT == W_Q4K) q4k_half(R, r, sl, hh, m4.dsc[2 * hs + hh], m4.nm[2 * hs + hh], o);
                         else if constexpr (WT == W_Q6K)
-                            q6k_half(R, r, sl, hh, m6.ds[4 * hs + 2 * hh], m6.ds[4 * hs + 2 * hh + 1], hi, lo);
-                        else q80_half(R, r, sl, hh, p.wscale, hi, lo);
+                            q6k_half(R, r, sl, hh, m6.ds[4 * hs + 2 * hh], m6.ds[4 * hs + 2 * hh + 1], o);
+                        else q80_half(R, r, sl, hh, p.wscale, o);
+                    };
+                    auto store = [&](uint32_t at, int hh, const Half &o) {
+                        tmem_st16(at + 16 * hh, o.hi);
+                        if constexpr (XS == 2) {
+                            tmem_st8(at + kTmemALo + 8 * hh, o.ch);
+                            tmem_st8(at + kTmemALo + 16 + 8 * hh, o.cl);
+                        } else {
+                            tmem_st16(at + kTmemALo + 16 * hh, o.lo);
+                        }
                     };
 #pragma unroll
                     for (int hs = 0; hs < 2; hs++) {
                         const int ia = 4 * rit + set + 2 * hs;
                         const uint32_t at = a_lane + (uint32_t)(set * kTmemAStage);
-                        uint32_t hi[16], lo[16];
-                        deq(hs, 0, hi, lo);
+                        Half o;
+                        deq(hs, 0, o);
                         if (!(ok = wait_a(ia))) break;
                         tc_fence_after();  // after the MMA that read this stage
-                        tmem_st16(at, hi);
-                        tmem_st16(at + kTmemALo, lo);
-                        deq(hs, 1, hi, lo);
-                        tmem_st16(at + 16, hi);
-                        tmem_st16(at + kTmemALo + 16, lo);
+                        store(at, 0, o);
+                        deq(hs, 1, o);
+                        store(at, 1, o);
                         publish(set);
                     }
                     __syncwarp();
@@ -819,7 +849,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 const EpiRow er = epi_row<EPI>(p.epi, tile, row);
                 const EpiDst dd = epi_dst<EPI>(p.epi, tile);
                 if constexpr (EPI == EPI_QKV || EPI == EPI_LOGITS) {
-                    for (int t = et; t < g.ntok; t += kEpiThreads) s_pos[t] = p.epi.pos[g.m0 + t];
+                    for (int t = et; t < g.ntok; t += kEpiThreads) {
+                        s_pos[t] = p.epi.pos[g.m0 + t];
+                        if constexpr (EPI == EPI_QKV) s_rpos[t] = p.epi.rope_pos[g.m0 + t];
+                    }
                     named_bar_sync(1, kEpiThreads);
                 }
                 for (int c0 = 16 * half; c0 < g.nmma; c0 += 32) {
@@ -829,7 +862,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     float v[16];
 #pragma unroll
                     for (int i = 0; i < 16; i++) v[i] = __uint_as_float(u16[i]);
-                    epi_values<EPI>(p.epi, er, s_pos, c0, g.ntok, v, my_stage);
+                    epi_values<EPI>(p.epi, er, s_rpos, c0, g.ntok, v, my_stage);
                     named_bar_sync(2 + half, kEpiThreads / 2);
                     epi_copyout<EPI>(dd, s_pos, g.m0, c0, g.ntok, my_stage, tid_h);
                     named_bar_sync(2 + half, kEpiThreads / 2);
@@ -883,7 +916,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 s_contrib[et] = ((long long)(2 * c + (int)rank) * 2 + sl) * kWsTile;
             }
             if constexpr (EPI == EPI_QKV || EPI == EPI_LOGITS) {
-                for (int t = et; t < g.ntok; t += kEpiThreads) s_pos[t] = p.epi.pos[g.m0 + t];
+                for (int t = et; t < g.ntok; t += kEpiThreads) {
+                    s_pos[t] = p.epi.pos[g.m0 + t];
+                    if constexpr (EPI == EPI_QKV) s_rpos[t] = p.epi.rope_pos[g.m0 + t];
+                }
             }
             if (et == 0) {
                 int okw = nc <= kMaxContrib;  // the launcher keeps nc <= kMaxContrib
@@ -937,7 +973,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                             v[4 * j + 3] += t[j].w;
                         }
                     }
-                    epi_values<EPI>(p.epi, er, s_pos, ch * 16, g.ntok, v, my_stage);
+                    epi_values<EPI>(p.epi, er, s_rpos, ch * 16, g.ntok, v, my_stage);
                     named_bar_sync(2 + half, kEpiThreads / 2);
                     epi_copyout<EPI>(dd, s_pos, g.m0, ch * 16, g.ntok, my_stage, tid_h);
                     named_bar_sync(2 + half, kEpiThreads / 2);

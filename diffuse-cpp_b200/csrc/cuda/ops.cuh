@@ -3,12 +3,18 @@
 #pragma once
 #include <cuda_fp16.h>
 #include <cstdint>
+#include "dequant.cuh"
 #include "ptx.cuh"
 
 namespace dfb {
 
-// Device counters of a context.
-enum { CNT_M = 0, CNT_NMASKED = 1, CNT_COMMITTED = 2, CNT_USED_CACHE = 3, CNT_ERR = 4, CNT_N = 8 };
+// Device counters of a context: totals over its sequences (segments) ...
+enum { CNT_M = 0, CNT_NMASKED = 1, CNT_NTILES = 2, CNT_ERR = 4, CNT_N = 8 };
+// ... and per segment: active rows, masked positions, commits of the last step, whether the
+// cached forward ran, offsets of the segment's rows in the active / masked lists.
+enum { SEG_NACT = 0, SEG_NMASK = 1, SEG_COMMITTED = 2, SEG_USED_CACHE = 3, SEG_AOFF = 4, SEG_MOFF = 5, SEG_ERR = 6,
+       SEG_N = 8 };
+constexpr int kMaxSeg = 256;  // sequences one context steps together
 
 // Block-wide exclusive scan of 0/1 flags for a 1024-thread block.  Returns this
 // thread's offset; *total receives the block count.
@@ -35,24 +41,32 @@ __device__ __forceinline__ int block_scan_flag(bool flag, int *warp_tot, int *to
     return off;
 }
 
-// Active set of one step (diffuse-cache.h:78-115 and diffuse-sampler.cpp:143-182).
-// full != 0: every position is active (step 0, cache off, refresh), last_changed is
-// not touched (the reference does not call compute_active_set there).  Otherwise
-// active = changed since the last forward ∪ masked ∪ changed within keep_active steps;
-// an empty or complete active set falls back to the full forward like
-// diffuse-sampler.cpp:165-173.  Also lists the masked positions (ascending) and
-// records prev_seq = seq (update_seq, cache.h:142-145).  One block of 1024 threads.
-__global__ void __launch_bounds__(1024) step_prepare_kernel(int full, int step, int keep_active, int n_total,
-                                                            int32_t *seq, int32_t *prev_seq, int32_t *last_changed,
-                                                            const uint8_t *masked, int *active_pos, int *masked_pos,
-                                                            int *cnt) {
+// Active set of one step for segment blockIdx.x, positions [seg_off[s], seg_off[s+1])
+// (diffuse-cache.h:78-115 and diffuse-sampler.cpp:143-182, per sequence).  full != 0:
+// every position is active (step 0, cache off, refresh), last_changed is not touched
+// (the reference does not call compute_active_set there).  Otherwise active = changed
+// since the last forward ∪ masked ∪ changed within keep_active steps; an empty or
+// complete active set falls back to the full forward like diffuse-sampler.cpp:165-173.
+// A finished segment (done[s], no position left masked: the reference's loop has ended
+// for it) contributes nothing.  Lists go to tmp_* at the segment's own offset; records
+// prev_seq = seq (update_seq, cache.h:142-145).  One block of 1024 threads per segment.
+__global__ void __launch_bounds__(1024) seg_prepare_kernel(int full, int step, int keep_active, const int *seg_off,
+                                                           const uint8_t *done, int32_t *seq, int32_t *prev_seq,
+                                                           int32_t *last_changed, const uint8_t *masked,
+                                                           int *tmp_active, int *tmp_masked, int *seg_cnt) {
     __shared__ int warp_tot[32];
     __shared__ int tot;
+    const int sg = blockIdx.x, p0 = seg_off[sg], n = seg_off[sg + 1] - p0;
+    int *sc = seg_cnt + sg * SEG_N;
+    if (done[sg]) {
+        if (threadIdx.x == 0) { sc[SEG_NACT] = 0; sc[SEG_NMASK] = 0; sc[SEG_USED_CACHE] = 0; }
+        return;
+    }
     int base_a = 0, base_m = 0;
-    for (int c0 = 0; c0 < n_total; c0 += 1024) {
-        const int i = c0 + threadIdx.x;
+    for (int c0 = 0; c0 < n; c0 += 1024) {
+        const int i = p0 + c0 + threadIdx.x;
         bool act = false, msk = false;
-        if (i < n_total) {
+        if (c0 + (int)threadIdx.x < n) {
             msk = masked[i] != 0;
             if (full) act = true;
             else {
@@ -64,23 +78,68 @@ __global__ void __launch_bounds__(1024) step_prepare_kernel(int full, int step, 
             }
         }
         const int oa = block_scan_flag(act, warp_tot, &tot);
-        if (act) active_pos[base_a + oa] = i;
+        if (act) tmp_active[p0 + base_a + oa] = i;
         base_a += tot;
         __syncthreads();
         const int om = block_scan_flag(msk, warp_tot, &tot);
-        if (msk) masked_pos[base_m + om] = i;
+        if (msk) tmp_masked[p0 + base_m + om] = i;
         base_m += tot;
         __syncthreads();
     }
-    const bool all = full || base_a == 0 || base_a >= n_total;
-    for (int i = threadIdx.x; i < n_total; i += 1024) {
-        if (all) active_pos[i] = i;
-        prev_seq[i] = seq[i];
+    const bool all = full || base_a == 0 || base_a >= n;
+    for (int j = threadIdx.x; j < n; j += 1024) {
+        if (all) tmp_active[p0 + j] = p0 + j;
+        prev_seq[p0 + j] = seq[p0 + j];
     }
     if (threadIdx.x == 0) {
-        cnt[CNT_M] = all ? n_total : base_a;
-        cnt[CNT_NMASKED] = base_m;
-        cnt[CNT_USED_CACHE] = all ? 0 : 1;
+        sc[SEG_NACT] = all ? n : base_a;
+        sc[SEG_NMASK] = base_m;
+        sc[SEG_USED_CACHE] = all ? 0 : 1;
+    }
+}
+
+// Dense lists over all segments: active rows (global positions, and positions within their
+// sequence for RoPE), masked positions and the logits row each reads (Dream: max(i-1, 0)
+// within its sequence, diffuse-sampler.cpp:74,235), attention tiles of <= 32 active rows
+// of one segment {first row, rows, first key position, keys}, totals.  One block.
+__global__ void __launch_bounds__(1024) seg_compact_kernel(int n_seg, const int *seg_off, const int *tmp_active,
+                                                           const int *tmp_masked, int *seg_cnt, int shift,
+                                                           int *active_pos, int *rope_pos, int *masked_pos,
+                                                           int *masked_row, int4 *tiles, int *cnt) {
+    __shared__ int aoff[kMaxSeg + 1], moff[kMaxSeg + 1];
+    griddep_wait();
+    if (threadIdx.x == 0) {
+        int a = 0, m = 0, k = 0;
+        for (int sg = 0; sg < n_seg; sg++) {
+            int *sc = seg_cnt + sg * SEG_N;
+            aoff[sg] = a;
+            moff[sg] = m;
+            sc[SEG_AOFF] = a;
+            sc[SEG_MOFF] = m;
+            const int na = sc[SEG_NACT], len = seg_off[sg + 1] - seg_off[sg];
+            for (int r = 0; r < na; r += 32) tiles[k++] = make_int4(a + r, min(32, na - r), seg_off[sg], len);
+            a += na;
+            m += sc[SEG_NMASK];
+        }
+        aoff[n_seg] = a;
+        moff[n_seg] = m;
+        cnt[CNT_M] = a;
+        cnt[CNT_NMASKED] = m;
+        cnt[CNT_NTILES] = k;
+    }
+    __syncthreads();
+    for (int sg = 0; sg < n_seg; sg++) {
+        const int p0 = seg_off[sg], na = aoff[sg + 1] - aoff[sg], nm = moff[sg + 1] - moff[sg];
+        for (int i = threadIdx.x; i < na; i += 1024) {
+            const int pos = tmp_active[p0 + i];
+            active_pos[aoff[sg] + i] = pos;
+            rope_pos[aoff[sg] + i] = pos - p0;
+        }
+        for (int i = threadIdx.x; i < nm; i += 1024) {
+            const int pos = tmp_masked[p0 + i];
+            masked_pos[moff[sg] + i] = pos;
+            masked_row[moff[sg] + i] = (shift && pos > p0) ? pos - 1 : pos;
+        }
     }
 }
 
@@ -119,31 +178,14 @@ __device__ __forceinline__ float block_sum(float v, float *red) {
     return r;
 }
 
-// Pair layout of GEMM activations: per 64-wide slice of a row, 64 hi f16 values then the
-// 64 lo parts (v - hi), so that hi + lo carries ~22 significant bits of the f32 value.
-// Eight consecutive values (one slice-aligned group) as two 16-byte stores.
-__device__ __forceinline__ void store_pair8(__half *row, int i, const float (&v)[8]) {
-    uint32_t hw[4], lw[4];
-#pragma unroll
-    for (int e = 0; e < 4; e++) {
-        const __half2 hh = __floats2half2_rn(v[2 * e], v[2 * e + 1]);
-        const float2 hf = __half22float2(hh);
-        hw[e] = h2u_(hh);
-        lw[e] = h2u_(__floats2half2_rn(v[2 * e] - hf.x, v[2 * e + 1] - hf.y));
-    }
-    __half *dst = row + (i >> 6) * 128 + (i & 63);
-    *reinterpret_cast<uint4 *>(dst) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-    *reinterpret_cast<uint4 *>(dst + 64) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-}
-
 // h[a] = x[a] * (1 / sqrt(mean(x[a]^2) + eps)) * w  (ggml_rms_norm + ggml_mul,
-// graph.cpp:51-58) as pair rows (row length 2d), with the residual add of the projection
+// graph.cpp:51-58) as pair rows (4 bytes per value, dequant.cuh), with the residual add of the projection
 // before it folded in when y is given: x[a] += y[a] first (ggml_add, graph.cpp:123 /
 // :142), written back as the new residual stream.  One block per row; 8 elements per
 // thread step (float4 loads); d is a multiple of 64.
 __global__ void __launch_bounds__(256) rmsnorm_kernel(float *__restrict__ x, const float *__restrict__ y,
                                                       const float *__restrict__ w, int d, float eps,
-                                                      const int *__restrict__ cnt, __half *__restrict__ h) {
+                                                      const int *__restrict__ cnt, uint8_t *__restrict__ h) {
     __shared__ float red[33];
     griddep_launch_dependents();
     griddep_wait();  // x, y and the row count come from the previous kernels
@@ -151,7 +193,7 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(float *__restrict__ x, con
     if (a >= cnt[CNT_M]) return;
     float *xr = x + (size_t)a * d;
     const float *yr = y ? y + (size_t)a * d : nullptr;
-    __half *hr = h + (size_t)a * 2 * d;
+    uint8_t *hr = h + (size_t)a * 4 * d;
     float ss = 0.f;
     for (int i = threadIdx.x * 8; i < d; i += blockDim.x * 8) {
         float4 v0 = *reinterpret_cast<const float4 *>(xr + i);
@@ -183,7 +225,7 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(float *__restrict__ x, con
 // Per-candidate statistics of one logits row (diffuse-sampler.cpp:34-57 and :239-255):
 // top-1 value and first index (strict '>' keeps the lowest index), top-2 value (the
 // largest value at any other index), entropy with the p > 1e-10 rule.  One block per
-// masked position; Dream reads row max(i-1, 0).
+// masked position; masked_row gives the logits row it reads (Dream's shift applied).
 struct Top2 {
     float best;
     int idx;
@@ -197,16 +239,15 @@ __device__ __forceinline__ Top2 top2_merge(Top2 a, Top2 b) {
     return r;
 }
 
-__global__ void __launch_bounds__(512) row_stats_kernel(const float *__restrict__ logits, int n_vocab, int shift,
-                                                         const int *__restrict__ masked_pos, const int *__restrict__ cnt,
+__global__ void __launch_bounds__(512) row_stats_kernel(const float *__restrict__ logits, int n_vocab,
+                                                         const int *__restrict__ masked_row, const int *__restrict__ cnt,
                                                          int margin, int32_t *__restrict__ cand_tok,
                                                          float *__restrict__ cand_conf, float *__restrict__ cand_ent) {
     __shared__ float red[33];
     __shared__ Top2 tred[16];
     const int b = blockIdx.x;
     if (b >= cnt[CNT_NMASKED]) return;
-    const int i = masked_pos[b];
-    const int row = shift ? (i > 0 ? i - 1 : 0) : i;
+    const int row = masked_row[b];
     const float *z = logits + (size_t)row * n_vocab;
     // Each pass reads the row as float4 (n_vocab % 4 == 0) with four loads in flight per
     // thread; a thread visits its elements in increasing index order, so the strict '>'
@@ -318,26 +359,34 @@ __device__ __forceinline__ uint32_t ordered_u32(float f) {
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
-// Ordering + commit (diffuse-sampler.cpp:277-323).  Candidates are in ascending
-// position order; keys: confidence descending (LOW_CONFIDENCE / MASKGIT_PLUS /
-// TOPK_MARGIN) or entropy ascending (ENTROPY_EXIT), ties by ascending position;
-// RANDOM uses the host's shuffle.  One block of 1024 threads; dynamic shared memory
-// holds the padded key array (8 bytes per candidate, power of two).
-__global__ void __launch_bounds__(1024) select_commit_kernel(int remasking, int n_unmask_sched, float tau, int key_cap,
-                                                             const int32_t *__restrict__ order,
+// Ordering + commit (diffuse-sampler.cpp:277-323) of segment blockIdx.x: its candidates
+// are [moff, moff + n) of the masked list, in ascending position order; keys: confidence
+// descending (LOW_CONFIDENCE / MASKGIT_PLUS / TOPK_MARGIN) or entropy ascending
+// (ENTROPY_EXIT), ties by ascending position; RANDOM uses the host's shuffle of the
+// segment's candidate indices (order[moff ..]).  sched[s] is tokens_to_unmask of the
+// segment's own loop; a negative value marks a finished segment.  One block of 1024
+// threads per segment; dynamic shared memory holds the padded key array (8 bytes per
+// candidate, power of two).
+__global__ void __launch_bounds__(1024) select_commit_kernel(int remasking, const int *__restrict__ sched, float tau,
+                                                             int key_cap, const int32_t *__restrict__ order,
                                                              const int *__restrict__ masked_pos,
                                                              const int32_t *__restrict__ cand_tok,
                                                              const float *__restrict__ cand_conf,
                                                              const float *__restrict__ cand_ent, int32_t *seq,
                                                              uint8_t *masked, int32_t *commit_pos,
-                                                             int32_t *commit_tok, int *cnt) {
+                                                             int32_t *commit_tok, int *seg_cnt) {
     extern __shared__ unsigned long long keys[];
     __shared__ int n_easy_s;
-    const int n = cnt[CNT_NMASKED];
+    int *sc = seg_cnt + blockIdx.x * SEG_N;
+    const int n = sc[SEG_NMASK], moff = sc[SEG_MOFF], n_unmask_sched = sched[blockIdx.x];
+    if (n_unmask_sched < 0) {  // finished segment
+        if (threadIdx.x == 0) sc[SEG_COMMITTED] = 0;
+        return;
+    }
     int np = 1;
     while (np < n) np <<= 1;
     if (np > key_cap) {  // host and device disagree on the candidate count: commit nothing
-        if (threadIdx.x == 0) { cnt[CNT_ERR] = 1; cnt[CNT_COMMITTED] = 0; }
+        if (threadIdx.x == 0) { sc[SEG_ERR] = 1; sc[SEG_COMMITTED] = 0; }
         return;
     }
     if (threadIdx.x == 0) n_easy_s = 0;
@@ -348,10 +397,10 @@ __global__ void __launch_bounds__(1024) select_commit_kernel(int remasking, int 
         if (b < n) {
             uint32_t k32;
             if (remasking == 2) {
-                k32 = ordered_u32(cand_ent[b]);
-                easy += cand_ent[b] < tau ? 1 : 0;
+                k32 = ordered_u32(cand_ent[moff + b]);
+                easy += cand_ent[moff + b] < tau ? 1 : 0;
             } else {
-                k32 = ~ordered_u32(cand_conf[b]);
+                k32 = ~ordered_u32(cand_conf[moff + b]);
             }
             k = ((unsigned long long)k32 << 32) | (uint32_t)b;
         }
@@ -377,22 +426,22 @@ __global__ void __launch_bounds__(1024) select_commit_kernel(int remasking, int 
     if (remasking == 2) n_unmask = max(n_unmask, n_easy_s);
     n_unmask = min(n_unmask, n);
     for (int j = threadIdx.x; j < n_unmask; j += blockDim.x) {
-        const int b = remasking == 1 ? order[j] : (int)(keys[j] & 0xffffffffu);
-        const int pos = masked_pos[b];
-        const int tok = cand_tok[b];
+        const int b = remasking == 1 ? order[moff + j] : (int)(keys[j] & 0xffffffffu);
+        const int pos = masked_pos[moff + b];
+        const int tok = cand_tok[moff + b];
         seq[pos] = tok;
         masked[pos] = 0;
-        commit_pos[j] = pos;
-        commit_tok[j] = tok;
+        commit_pos[moff + j] = pos;
+        commit_tok[moff + j] = tok;
     }
     if (threadIdx.x == 0) {
-        cnt[CNT_COMMITTED] = n_unmask;
-        cnt[CNT_NMASKED] = n - n_unmask;
+        sc[SEG_COMMITTED] = n_unmask;
+        sc[SEG_NMASK] = n - n_unmask;
     }
 }
 
-// X (f32 [rows][K], host-provided for dfb_linear) -> pair rows [rows][2K]; K multiple of 64.
-__global__ void f32_to_pair_kernel(const float *__restrict__ x, __half *__restrict__ y, int rows, int K) {
+// X (f32 [rows][K], host-provided for dfb_linear) -> pair rows (4 K bytes each); K multiple of 64.
+__global__ void f32_to_pair_kernel(const float *__restrict__ x, uint8_t *__restrict__ y, int rows, int K) {
     const size_t groups = (size_t)rows * (K / 8);
     for (size_t g = blockIdx.x * (size_t)blockDim.x + threadIdx.x; g < groups; g += (size_t)gridDim.x * blockDim.x) {
         const size_t r = g / (K / 8);
@@ -400,7 +449,7 @@ __global__ void f32_to_pair_kernel(const float *__restrict__ x, __half *__restri
         float v[8];
 #pragma unroll
         for (int e = 0; e < 8; e++) v[e] = x[r * K + i + e];
-        store_pair8(y + r * 2 * K, i, v);
+        store_pair8(y + r * 4 * K, i, v);
     }
 }
 

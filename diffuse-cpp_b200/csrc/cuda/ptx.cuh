@@ -231,6 +231,36 @@ __device__ __forceinline__ void mma2_f16_ts_k64(uint32_t d_tmem, uint32_t a_tmem
         "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
+// 128 k-values of 8-bit operands (kind::f8f6f4, E4M3 x E4M3 into the f32 accumulator):
+// four K = 32 MMAs, A from TMEM (four 8-bit values per 32-bit column, lower k in the low
+// byte: 8 columns per step), B descriptor advanced by 32 bytes per step.  Accumulates.
+__device__ __forceinline__ void mma2_f8_ts_k128(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc) {
+    asm volatile(
+        "{\n\t.reg .pred p1;\n\t.reg .b32 a1, a2, a3;\n\t.reg .b64 b1, b2, b3;\n\t"
+        "setp.eq.b32 p1, %3, %3;\n\t"
+        "add.u32 a1, %1, 8;\n\tadd.u32 a2, %1, 16;\n\tadd.u32 a3, %1, 24;\n\t"
+        "add.u64 b1, %2, 2;\n\tadd.u64 b2, %2, 4;\n\tadd.u64 b3, %2, 6;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], [%1], %2, %3, p1;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], [a1], b1, %3, p1;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], [a2], b2, %3, p1;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], [a3], b3, %3, p1;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc)
+        : "memory");
+}
+// Same with A from shared memory (128 bytes per row: descriptor advanced by 32 bytes per step).
+__device__ __forceinline__ void mma2_f8_ss_k128(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc) {
+    asm volatile(
+        "{\n\t.reg .pred p1;\n\t.reg .b64 a1, a2, a3, b1, b2, b3;\n\t"
+        "setp.eq.b32 p1, %3, %3;\n\t"
+        "add.u64 a1, %1, 2;\n\tadd.u64 a2, %1, 4;\n\tadd.u64 a3, %1, 6;\n\t"
+        "add.u64 b1, %2, 2;\n\tadd.u64 b2, %2, 4;\n\tadd.u64 b3, %2, 6;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p1;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], a1, b1, %3, p1;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], a2, b2, %3, p1;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], a3, b3, %3, p1;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc)
+        : "memory");
+}
 // Same with A from shared memory (descriptor advanced by 32 bytes per step).
 __device__ __forceinline__ void mma2_f16_ss_k64(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                                 uint32_t accumulate) {
@@ -255,6 +285,12 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
         "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
         "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
         : "memory");
+}
+// 32 lanes x 8 columns of 32-bit: this thread's lane, columns [col, col+8).
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
+                 "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+                 : "memory");
 }
 // This thread's tcgen05.st have completed.
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }

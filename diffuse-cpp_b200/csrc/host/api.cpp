@@ -443,6 +443,82 @@ int dfc_generate(void *ctx, const int32_t *prompt, int n_prompt, int n_generate,
     return rc;
 }
 
+// Several independent sequences, each running diffuse_sample's loop (diffuse-sampler.cpp:
+// 60-370) as it would alone -- its own schedule counts, RNG stream (seeded with params.seed,
+// as a separate diffuse_generate call would be) and end when nothing is left masked --
+// while each step's forward runs all live sequences in one pass (dfb_gen_step_batch).
+int dfc_generate_batch(void *ctx_, const int32_t *prompts, const int32_t *prompt_lens, int n_seq, int n_generate,
+                       const dfb_sampler_params *p, int32_t *out, dfc_batch_trace *trace) {
+    if (!ctx_ || !p || !out || !prompt_lens || n_generate <= 0 || n_seq <= 0) return set_error(DFB_ERR_ARG, "bad arguments");
+    diffuse_context *ctx = (diffuse_context *)ctx_;
+    using clk = std::chrono::steady_clock;
+    const auto t_start = clk::now();
+    std::vector<int32_t> gens(n_seq, n_generate);
+    if (dfb_gen_begin_batch(ctx->dc, n_seq, prompts, prompt_lens, gens.data(), p) != DFB_OK)
+        return set_error(DFB_ERR_ARG, "%s", dfb_last_error());
+    std::vector<std::mt19937> rngs(n_seq, std::mt19937(p->seed));
+    std::vector<int> n_masked(n_seq, n_generate);
+    std::vector<int32_t> sched(n_seq), orders;
+    std::vector<dfb_step_stats> st(n_seq);
+    bool cache_initialized = false;
+    int steps = 0;
+    for (int step = 0; step < p->n_steps; step++) {
+        int live = 0;
+        for (int sg = 0; sg < n_seq; sg++) live += n_masked[sg] > 0;
+        if (!live) break;
+        const bool force_full = !p->use_cache || !cache_initialized ||
+                                (p->cache_refresh > 0 && step > 0 && (step % p->cache_refresh == 0));
+        orders.clear();
+        for (int sg = 0; sg < n_seq; sg++) {
+            if (!n_masked[sg]) { sched[sg] = -1; continue; }
+            sched[sg] = tokens_to_unmask(step, p->n_steps, n_masked[sg], (diffuse_schedule)p->schedule);
+            if (p->remasking == (int)diffuse_remasking::RANDOM) {
+                // the sequence's own std::shuffle of its ascending candidate list (sampler.cpp:307)
+                std::vector<int32_t> o(n_masked[sg]);
+                std::iota(o.begin(), o.end(), 0);
+                std::shuffle(o.begin(), o.end(), rngs[sg]);
+                orders.insert(orders.end(), o.begin(), o.end());
+            }
+        }
+        if (dfb_gen_step_batch(ctx->dc, step, sched.data(), force_full ? 1 : 0, orders.empty() ? nullptr : orders.data(),
+                               st.data()) != DFB_OK)
+            return set_error(DFB_ERR_CUDA, "forward pass failed at step %d: %s", step, dfb_last_error());
+        if (p->use_cache) cache_initialized = true;
+        int active = 0, unmasked = 0, remaining = 0;
+        for (int sg = 0; sg < n_seq; sg++) {
+            if (trace && step < trace->max_steps && trace->n_active) trace->n_active[(size_t)step * n_seq + sg] = st[sg].n_active;
+            if (trace && step < trace->max_steps && trace->n_unmasked)
+                trace->n_unmasked[(size_t)step * n_seq + sg] = sched[sg] < 0 ? 0 : st[sg].n_unmasked;
+            if (sched[sg] >= 0) {
+                active += st[sg].n_active;
+                unmasked += st[sg].n_unmasked;
+                n_masked[sg] = st[sg].n_masked;
+            }
+            remaining += n_masked[sg];
+        }
+        if (trace && step < trace->max_steps && trace->fwd_ms) trace->fwd_ms[step] = st[0].fwd_ms;
+        if (trace && step < trace->max_steps && trace->step_ms) trace->step_ms[step] = st[0].step_ms;
+        DIFFUSE_LOG("  step %d/%d: %d sequences, unmasked %d tokens, %d remaining (fwd=%.1fms, active rows=%d)",
+                    step + 1, p->n_steps, live, unmasked, remaining, st[0].fwd_ms, active);
+        steps++;
+    }
+    int total = 0;
+    for (int sg = 0; sg < n_seq; sg++) total += prompt_lens[sg] + n_generate;
+    std::vector<int32_t> seq(total);
+    if (dfb_gen_tokens(ctx->dc, seq.data(), total) != DFB_OK) return set_error(DFB_ERR_CUDA, "%s", dfb_last_error());
+    int off = 0;
+    for (int sg = 0; sg < n_seq; sg++) {
+        std::copy(seq.begin() + off + prompt_lens[sg], seq.begin() + off + prompt_lens[sg] + n_generate,
+                  out + (size_t)sg * n_generate);
+        off += prompt_lens[sg] + n_generate;
+    }
+    if (trace) {
+        trace->steps_run = steps;
+        trace->total_ms = std::chrono::duration<double, std::milli>(clk::now() - t_start).count();
+    }
+    return steps;
+}
+
 int dfc_tokens_to_unmask(int step, int total_steps, int total_masked, int schedule) {
     return tokens_to_unmask(step, total_steps, total_masked, (diffuse_schedule)schedule);
 }

@@ -125,10 +125,28 @@ int dfb_gen_begin(dfb_ctx *c, const int32_t *prompt, int n_prompt, int n_gen, co
  * fills *stats (may be NULL). */
 int dfb_gen_step(dfb_ctx *c, int step, int n_unmask_sched, int force_full, const int32_t *order,
                  dfb_step_stats *stats);
-/* Copy the whole current sequence (prompt ‖ generated) to the host. */
+/* Copy the whole current sequence (prompt ‖ generated) to the host (batch: all
+ * sequences' positions, concatenated in order). */
 int dfb_gen_tokens(dfb_ctx *c, int32_t *seq_host, int cap);
 /* Positions / tokens committed by the last step, in commit order; returns the count. */
 int dfb_gen_commits(dfb_ctx *c, int32_t *pos_host, int32_t *tok_host, int cap);
+
+/* Several independent sequences stepped together (no counterpart in the reference,
+ * whose API generates one sequence per call, README.md:303 "no batching"): each sequence
+ * runs diffuse_sample's loop (diffuse-sampler.cpp:60-370) exactly as it would alone --
+ * its own active set and cache fallback, schedule, remasking order and RNG -- while every
+ * step's forward packs all sequences' active rows into one GEMM per weight.  Sequence s
+ * occupies positions [off_s, off_s + prompt_lens[s] + n_gens[s]) of the concatenated
+ * state (dfb_gen_tokens / dfb_gen_logits index it).  At most 256 sequences. */
+int dfb_gen_begin_batch(dfb_ctx *c, int n_seq, const int32_t *prompts /* concatenated */,
+                        const int32_t *prompt_lens, const int32_t *n_gens, const dfb_sampler_params *p);
+/* One step of every sequence that still has masked positions: n_unmask_sched[s] is that
+ * sequence's tokens_to_unmask; RANDOM: orders holds each live sequence's shuffle of its
+ * candidate indices, concatenated in sequence order.  stats: [n_seq]. */
+int dfb_gen_step_batch(dfb_ctx *c, int step, const int32_t *n_unmask_sched, int force_full, const int32_t *orders,
+                       dfb_step_stats *stats);
+/* Commits of the last step, concatenated in sequence order; counts[s] per sequence. */
+int dfb_gen_commits_batch(dfb_ctx *c, int32_t *pos_host, int32_t *tok_host, int32_t *counts, int cap);
 /* Rows [row0, row0+nrows) of the persistent logits buffer (parity checks). */
 int dfb_gen_logits(dfb_ctx *c, int row0, int nrows, float *host);
 

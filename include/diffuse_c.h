@@ -53,6 +53,25 @@ typedef struct {
 int   dfc_generate(void *ctx, const int32_t *prompt, int n_prompt, int n_generate,
                    const dfb_sampler_params *params, int32_t *out, dfc_trace *trace);
 
+/* Per-step record of dfc_generate_batch (arrays caller-allocated, may be NULL). */
+typedef struct {
+    int32_t  max_steps;
+    int32_t  steps_run;
+    int32_t *n_active;     /* [max_steps * n_seq] rows each sequence's forward computed */
+    int32_t *n_unmasked;   /* [max_steps * n_seq] */
+    float   *fwd_ms;       /* [max_steps] device time of the step's forward (all sequences) */
+    float   *step_ms;      /* [max_steps] device time of forward + sampler */
+    double   total_ms;     /* wall time of the whole call */
+} dfc_batch_trace;
+
+/* Several independent sequences generated together (no counterpart in the reference,
+ * which generates one sequence per call): each runs diffuse_generate's loop exactly as
+ * alone (its own schedule, order, RNG stream seeded with params->seed, and end), while
+ * every step runs one forward over all live sequences' active rows.  prompts are
+ * concatenated; out receives n_seq x n_generate ids.  Returns the steps run. */
+int   dfc_generate_batch(void *ctx, const int32_t *prompts, const int32_t *prompt_lens, int n_seq, int n_generate,
+                         const dfb_sampler_params *params, int32_t *out, dfc_batch_trace *trace);
+
 /* diffuse-quantize: type is "q8_0", "q4_k_m" (alias "q4_k"), "q6_k" or "f16". */
 int   dfc_quantize_file(const char *in_path, const char *out_path, const char *type, int n_threads);
 
