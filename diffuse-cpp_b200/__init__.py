@@ -98,6 +98,7 @@ def _load():
         (dfb, "dfb_debug_stalled_linear"): (I, [P, I, I, P, I, P, C.c_ulonglong]),
         (dfb, "dfb_gen_begin"): (I, [P, P, I, I, C.POINTER(SamplerParams)]),
         (dfb, "dfb_gen_step"): (I, [P, I, I, I, P, P]),
+        (dfb, "dfb_gen_set_uniforms"): (I, [P, P, I]),
         (dfb, "dfb_gen_tokens"): (I, [P, P, I]),
         (dfb, "dfb_gen_commits"): (I, [P, P, P, I]),
         (dfb, "dfb_gen_logits"): (I, [P, I, I, P]),
@@ -326,6 +327,12 @@ class Context:
         if native()[0].dfb_gen_begin(self.engine, _ptr(p), p.size, n_generate, C.byref(params)) != 0:
             raise DiffuseError(_dfb_err())
         self._total = p.size + n_generate
+
+    def gen_set_uniforms(self, u):
+        """temperature > 0: the next step's uniforms (one per masked position, position order)."""
+        a = np.ascontiguousarray(u, dtype=np.float64)
+        if native()[0].dfb_gen_set_uniforms(self.engine, _ptr(a) if a.size else None, a.size) != 0:
+            raise DiffuseError(_dfb_err())
 
     def gen_step(self, step: int, n_unmask: int, force_full: bool, order=None) -> dict:
         st = np.zeros(6, np.int32)  # dfb_step_stats: 4 ints + 2 floats

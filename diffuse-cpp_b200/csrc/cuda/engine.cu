@@ -99,11 +99,31 @@ static int make_tmap(CUtensorMap *m, const void *ptr, uint64_t cols, uint64_t ro
 // The 3-D activation views the GEMM loads its B operand through (XMaps in gemm_dq.cuh):
 // x is a row-major f16 matrix of rows of xs * K values (xs = 2: pair rows, xs = 1: plain),
 // K a multiple of 64, x 16-byte aligned.
-static int make_xmaps(XMaps *xm, const void *x, int K, int rows, int xs) {
+// Bytes of one sub-block sums row of an activation matrix of width K (dequant.cuh).
+static size_t sums_row_bytes(int K) { return (size_t)((K + 255) / 256) * kSumsBytes; }
+
+// sums: the sub-block sums rows of pair-row activations (xs = 2; the Q4_K min operand's B side).
+static int make_xmaps(XMaps *xm, const void *x, const void *sums, int K, int rows, int xs) {
     auto fn = encode_fn();
     if (!fn) return set_err(DFB_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
     if (K % 64) return set_err(DFB_ERR_UNSUPPORTED, "activation width %d not a multiple of 64", K);
     if (reinterpret_cast<uintptr_t>(x) % 16) return set_err(DFB_ERR_ARG, "activation matrix not 16-byte aligned");
+    memset(xm->s, 0, sizeof(xm->s));
+    if (xs == 2) {
+        if (!sums || reinterpret_cast<uintptr_t>(sums) % 16) return set_err(DFB_ERR_ARG, "sub-block sums missing or not 16-byte aligned");
+        const int kbs = (K + 255) / 256;
+        for (int i = 0; i < kXMaps; i++) {
+            const int h = 16 * (i + 1);
+            cuuint64_t dims[3] = {32, (cuuint64_t)rows, (cuuint64_t)kbs};
+            cuuint64_t strides[2] = {(cuuint64_t)sums_row_bytes(K), (cuuint64_t)kSumsBytes};
+            cuuint32_t box[3] = {32, (cuuint32_t)h, 1};
+            cuuint32_t es[3] = {1, 1, 1};
+            CUresult r = fn(&xm->s[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(sums), dims, strides, box, es,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+            if (r != CUDA_SUCCESS) return set_err(DFB_ERR_CUDA, "cuTensorMapEncodeTiled (sums) failed (%d)", (int)r);
+        }
+    }
     for (int i = 0; i < kXMaps; i++) {
         const int h = 16 * (i + 1);
         cuuint64_t dims[3] = {64, (cuuint64_t)rows, (cuuint64_t)(xs * K / 64)};
@@ -558,6 +578,8 @@ extern "C" int dfb_model_finalize(dfb_model *m) {
         }
         const HostTensor &wo = staged(m, DFB_WO, l);
         RET(check_mat(wo, "attn_output", m->n_q, d));
+        if (wo.type == G_Q4_K && m->hd % 32)  // the attention kernel writes sub-block sums per head
+            return set_err(DFB_ERR_UNSUPPORTED, "layer %d: Q4_K attn_output needs head_dim %% 32 == 0 (head_dim %d)", l, m->hd);
         {
             std::vector<const uint8_t *> rows((d + 127) / 128 * 128, nullptr);
             const int64_t rb = ggml_row_bytes(wo.type, m->n_q);
@@ -624,6 +646,7 @@ struct dfb_ctx {
     float *x = nullptr, *y = nullptr, *logits = nullptr;  // residual stream, projection output, logits
     float *q = nullptr, *kc = nullptr, *vc = nullptr;      // Q rows, K/V cache [layer][position][n_kv] (f32)
     uint8_t *h = nullptr, *att = nullptr, *ffh = nullptr;  // GEMM inputs as pair rows (4 bytes per value)
+    uint8_t *h_s = nullptr, *att_s = nullptr, *ffh_s = nullptr;  // their sub-block sums rows
     float2 *rope = nullptr;
     XMaps xm_h{}, xm_att{}, xm_ffh{};  // GEMM B-operand views of h, att, ffh
     // sequence state
@@ -632,6 +655,8 @@ struct dfb_ctx {
     uint8_t *masked = nullptr;
     int *active_pos = nullptr, *masked_pos = nullptr, *cnt = nullptr;
     float *cand_conf = nullptr, *cand_ent = nullptr;
+    double *unif = nullptr;  // temperature > 0: the host's uniforms of the next step, one per masked candidate
+    int unif_n = -1;         // how many the host set for the next step (-1: none)
     // sequences (segments) stepping together: positions [seg_off[s], seg_off[s+1]) of the
     // concatenated state; per-segment counters, schedule counts, finished flags, work lists
     int *seg_off = nullptr, *seg_cnt = nullptr, *sched = nullptr, *tmp_active = nullptr, *tmp_masked = nullptr,
@@ -669,12 +694,15 @@ static void ctx_free_buffers(dfb_ctx *c) {
     void *ps[] = {c->x, c->y, c->logits, c->h, c->att, c->q, c->ffh, c->kc, c->vc, c->rope, c->seq, c->prev_seq,
                   c->last_changed, c->cand_tok, c->commit_pos, c->commit_tok, c->order, c->masked, c->active_pos,
                   c->masked_pos, c->cnt, c->cand_conf, c->cand_ent, c->ws, c->tile_cnt, c->err, c->seg_off,
-                  c->seg_cnt, c->sched, c->tmp_active, c->tmp_masked, c->rope_pos, c->masked_row, c->done, c->tiles};
+                  c->seg_cnt, c->sched, c->tmp_active, c->tmp_masked, c->rope_pos, c->masked_row, c->done, c->tiles,
+                  c->h_s, c->att_s, c->ffh_s, c->unif};
     for (void *p : ps) cudaFree(p);
     c->seg_off = c->seg_cnt = c->sched = c->tmp_active = c->tmp_masked = c->rope_pos = c->masked_row = nullptr;
     c->done = nullptr;
     c->tiles = nullptr;
     c->x = c->y = c->logits = c->q = c->kc = c->vc = nullptr; c->h = c->att = c->ffh = nullptr; c->rope = nullptr;
+    c->h_s = c->att_s = c->ffh_s = nullptr;
+    c->unif = nullptr;
     c->seq = c->prev_seq = c->last_changed = c->cand_tok = c->commit_pos = c->commit_tok = c->order = nullptr;
     c->masked = nullptr; c->active_pos = c->masked_pos = c->cnt = nullptr; c->cand_conf = c->cand_ent = nullptr;
     c->ws = nullptr; c->tile_cnt = c->err = nullptr;
@@ -706,10 +734,11 @@ static int ctx_reserve(dfb_ctx *c, int n) {
 #define AL(ptr, count) CK(cudaMalloc(&(ptr), sizeof(*(ptr)) * (size_t)(count)))
     AL(c->x, cap * d); AL(c->y, cap * d); AL(c->h, 4 * cap * d); AL(c->att, 4 * cap * d); AL(c->q, cap * d);
     AL(c->ffh, 4 * cap * ff);
+    AL(c->h_s, cap * sums_row_bytes((int)d)); AL(c->att_s, cap * sums_row_bytes(m->n_q)); AL(c->ffh_s, cap * sums_row_bytes((int)ff));
     AL(c->kc, L * cap * kvd); AL(c->vc, L * cap * kvd); AL(c->logits, (size_t)cap * V); AL(c->rope, cap * hd / 2);
     AL(c->seq, cap); AL(c->prev_seq, cap); AL(c->last_changed, cap); AL(c->cand_tok, cap); AL(c->commit_pos, cap);
     AL(c->commit_tok, cap); AL(c->order, cap); AL(c->masked, cap); AL(c->active_pos, cap); AL(c->masked_pos, cap);
-    AL(c->cnt, CNT_N); AL(c->cand_conf, cap); AL(c->cand_ent, cap);
+    AL(c->cnt, CNT_N); AL(c->cand_conf, cap); AL(c->cand_ent, cap); AL(c->unif, cap);
     AL(c->seg_off, kMaxSeg + 1); AL(c->seg_cnt, kMaxSeg * SEG_N); AL(c->sched, kMaxSeg); AL(c->done, kMaxSeg);
     AL(c->tmp_active, cap); AL(c->tmp_masked, cap); AL(c->rope_pos, cap); AL(c->masked_row, cap);
     AL(c->tiles, cap / kAttnRows + kMaxSeg + 1);
@@ -729,14 +758,18 @@ static int ctx_reserve(dfb_ctx *c, int n) {
     CK(cudaMemset(c->h, 0, 4 * cap * d));
     CK(cudaMemset(c->att, 0, 4 * cap * d));
     CK(cudaMemset(c->ffh, 0, 4 * cap * ff));
+    // the sums rows' padding entries are read as zeros and never written
+    CK(cudaMemset(c->h_s, 0, cap * sums_row_bytes((int)d)));
+    CK(cudaMemset(c->att_s, 0, cap * sums_row_bytes(m->n_q)));
+    CK(cudaMemset(c->ffh_s, 0, cap * sums_row_bytes((int)ff)));
     CK(cudaMemset(c->kc, 0, 4 * L * cap * kvd));
     CK(cudaMemset(c->vc, 0, 4 * L * cap * kvd));
     std::vector<float2> rope;
     rope_table_host(cap, (int)hd, hp.rope_theta, rope);
     CK(cudaMemcpy(c->rope, rope.data(), rope.size() * sizeof(float2), cudaMemcpyHostToDevice));
-    RET(make_xmaps(&c->xm_h, c->h, (int)d, cap, 2));
-    RET(make_xmaps(&c->xm_att, c->att, m->n_q, cap, 2));
-    RET(make_xmaps(&c->xm_ffh, c->ffh, (int)ff, cap, 2));
+    RET(make_xmaps(&c->xm_h, c->h, c->h_s, (int)d, cap, 2));
+    RET(make_xmaps(&c->xm_att, c->att, c->att_s, m->n_q, cap, 2));
+    RET(make_xmaps(&c->xm_ffh, c->ffh, c->ffh_s, (int)ff, cap, 2));
     c->cap = cap;
     return DFB_OK;
 }
@@ -872,10 +905,11 @@ static int launch_gemm_t(dfb_ctx *c, const WMat &w, const XMaps &xm, const EpiAr
     const int n_pairs = std::min(gemm_max_pairs<WT, EPI, 2>(c->m->device, c->m->n_sm), (kMaxContrib - 2) * (w.n_tiles / 2));
     CK(launch_k(kern, dim3(2 * n_pairs), dim3(kThreads), smem, c->st, !c->prof, w.tm, xm, p));
     // algorithmic work: 2*K MACs per output, weights read once, X read (pair rows, 4 B per
-    // value), Y written (f32, or pair rows for SwiGLU: 4 B per output feature either way)
+    // value, plus the sub-block sums for Q4_K), Y written (f32, or pair rows for SwiGLU: 4 B
+    // per output feature either way)
     const int cat = WT == W_Q4K ? DFB_PROF_Q4K : WT == W_Q6K ? DFB_PROF_Q6K : WT == W_Q80 ? DFB_PROF_Q80 : DFB_PROF_F16;
     prof_end(c, ev0, EPI == EPI_LOGITS ? (int)DFB_PROF_LMHEAD : cat, 2.0 * w.K * (double)w.n_true, (double)w.bytes,
-             4.0 * w.K + 4.0 * (EPI == EPI_SWIGLU ? w.n_true / 2 : w.n_true));
+             4.0 * w.K + (WT == W_Q4K ? (double)sums_row_bytes(w.K) : 0.0) + 4.0 * (EPI == EPI_SWIGLU ? w.n_true / 2 : w.n_true));
     return DFB_OK;
 }
 
@@ -907,7 +941,8 @@ static int launch_attn_t(dfb_ctx *c, const float *kc, const float *vc, int n_key
     cudaEvent_t ev0 = nullptr;
     prof_begin(c, &ev0);
     CK(launch_k(attn_kernel<HD>, grid, dim3(kAttnThreads), smem, c->st, !c->prof, (const float *)c->q, m->n_q, kc, vc,
-                m->n_kv, c->att, 4 * m->n_q, (const int4 *)c->tiles, (const int *)(c->cnt + CNT_NTILES),
+                m->n_kv, c->att, 4 * m->n_q, c->att_s, (int)sums_row_bytes(m->n_q), (const int4 *)c->tiles,
+                (const int *)(c->cnt + CNT_NTILES),
                 m->hp.n_head / m->hp.n_head_kv, scale_log2));
     // algorithmic bytes: K and V of every key once (f32), Q in (f32), O out (pair rows)
     prof_end(c, ev0, DFB_PROF_ATTN, 4.0 * n_keys * m->hp.n_head * HD, 2.0 * 4.0 * n_keys * m->n_kv, 8.0 * m->n_q);
@@ -919,6 +954,7 @@ static int run_forward(dfb_ctx *c, int n_total) {
     const dfb_model *m = c->m;
     const dfb_hparams &hp = m->hp;
     const int d = hp.n_embd, cap = c->cap;
+    const int hs_ld = (int)sums_row_bytes(d);
     if (m->embd_f16)
         embed_kernel<__half><<<cap, 256, 0, c->st>>>((const __half *)m->embd, d, c->seq, c->active_pos, c->cnt, c->x);
     else
@@ -929,7 +965,7 @@ static int run_forward(dfb_ctx *c, int n_total) {
         float *kc = c->kc + (size_t)l * cap * m->n_kv, *vc = c->vc + (size_t)l * cap * m->n_kv;
         // the previous layer's down projection is added to the residual stream here
         CK(launch_k(rmsnorm_kernel, dim3(cap), dim3(256), 0, c->st, true, c->x, (const float *)(l ? c->y : nullptr),
-                    (const float *)L.attn_norm, d, hp.rms_norm_eps, (const int *)c->cnt, c->h));
+                    (const float *)L.attn_norm, d, hp.rms_norm_eps, (const int *)c->cnt, c->h, c->h_s, hs_ld));
         EpiArgs e;
         e.q_out = c->q; e.ld_q = m->n_q;
         e.k_cache = kc; e.v_cache = vc; e.ld_kv = m->n_kv;
@@ -947,16 +983,17 @@ static int run_forward(dfb_ctx *c, int n_total) {
         eo.out = c->y; eo.ld = d; eo.n_valid = d;
         RET(launch_gemm<EPI_F32>(c, L.o, c->xm_att, eo));
         CK(launch_k(rmsnorm_kernel, dim3(cap), dim3(256), 0, c->st, true, c->x, (const float *)c->y,
-                    (const float *)L.ffn_norm, d, hp.rms_norm_eps, (const int *)c->cnt, c->h));
+                    (const float *)L.ffn_norm, d, hp.rms_norm_eps, (const int *)c->cnt, c->h, c->h_s, hs_ld));
         EpiArgs eg;
         eg.out = c->ffh; eg.ld = 2 * hp.n_ff; eg.n_valid = 2 * hp.n_ff;  // pair rows
+        eg.sums = c->ffh_s; eg.ld_sums = (int)sums_row_bytes(hp.n_ff);
         RET(launch_gemm<EPI_SWIGLU>(c, L.gateup, c->xm_h, eg));
         EpiArgs ed;  // FFN down projection -> y, added to x by the next norm
         ed.out = c->y; ed.ld = d; ed.n_valid = d;
         RET(launch_gemm<EPI_F32>(c, L.down, c->xm_ffh, ed));
     }
     CK(launch_k(rmsnorm_kernel, dim3(cap), dim3(256), 0, c->st, true, c->x, (const float *)(hp.n_layer ? c->y : nullptr),
-                (const float *)m->output_norm, d, hp.rms_norm_eps, (const int *)c->cnt, c->h));
+                (const float *)m->output_norm, d, hp.rms_norm_eps, (const int *)c->cnt, c->h, c->h_s, hs_ld));
     EpiArgs el;
     el.out = c->logits; el.ld = hp.n_vocab; el.n_valid = hp.n_vocab; el.pos = c->active_pos;
     RET(launch_gemm<EPI_LOGITS>(c, m->lm_head, c->xm_h, el));
@@ -982,6 +1019,8 @@ static const char *gemm_err_str(int code) {
         case 12: return "relay waited for an MMA to release its stage";
         case 13: return "split-tile contributor waited for the other contributors' partial sums";
         case 14: return "token count changed between the launch and the grid-dependency wait";
+        case 15: return "activation producer waited for a free sub-block sums slot";
+        case 16: return "relay waited for sub-block sums to land";
         default: return "unknown";
     }
 }
@@ -1127,17 +1166,20 @@ extern "C" int dfb_linear(dfb_ctx *c, int role, int layer, const float *x_host, 
         }
     }
     RET(ctx_reserve(c, M));
-    uint8_t *xh = nullptr;
+    uint8_t *xh = nullptr, *xs = nullptr;
     float *xf = nullptr, *y = nullptr;
+    const size_t ls = sums_row_bytes(K);
     CK(cudaMalloc(&xh, (size_t)M * K * 4));  // pair rows
+    CK(cudaMalloc(&xs, (size_t)M * ls));     // their sub-block sums
     CK(cudaMalloc(&xf, (size_t)M * K * 4));
     CK(cudaMalloc(&y, (size_t)M * w->n_rows * 4));
     int rc = DFB_OK;
     XMaps xm;
     do {
-        if ((rc = make_xmaps(&xm, xh, K, M, 2)) != DFB_OK) break;
+        if ((rc = make_xmaps(&xm, xh, xs, K, M, 2)) != DFB_OK) break;
+        if (cudaMemsetAsync(xs, 0, (size_t)M * ls, c->st) != cudaSuccess) { rc = set_err(DFB_ERR_CUDA, "memset failed"); break; }
         if (cudaMemcpyAsync(xf, x_host, (size_t)M * K * 4, cudaMemcpyHostToDevice, c->st) != cudaSuccess) { rc = set_err(DFB_ERR_CUDA, "H2D failed"); break; }
-        f32_to_pair_kernel<<<256, 256, 0, c->st>>>(xf, xh, M, K);
+        f32_to_pair_kernel<<<256, 256, 0, c->st>>>(xf, xh, M, K, xs, (int)ls);
         if (cudaMemcpyAsync(c->cnt + CNT_M, &M, sizeof(int), cudaMemcpyHostToDevice, c->st) != cudaSuccess) { rc = set_err(DFB_ERR_CUDA, "H2D failed"); break; }
         EpiArgs e;
         e.out = y; e.ld = w->n_rows; e.n_valid = w->n_rows;
@@ -1164,7 +1206,7 @@ extern "C" int dfb_linear(dfb_ctx *c, int role, int layer, const float *x_host, 
                 y_host[(size_t)t * n_out + f] = full[(size_t)t * w->n_rows + r];
             }
     } while (0);
-    cudaFree(xh); cudaFree(xf); cudaFree(y);
+    cudaFree(xh); cudaFree(xs); cudaFree(xf); cudaFree(y);
     return rc;
 }
 
@@ -1183,8 +1225,7 @@ extern "C" int dfb_gen_begin_batch(dfb_ctx *c, int n_seq, const int32_t *prompts
                                    const int32_t *n_gens, const dfb_sampler_params *p) {
     if (!c || !p || !prompt_lens || !n_gens || n_seq <= 0) return set_err(DFB_ERR_ARG, "bad arguments");
     if (n_seq > kMaxSeg) return set_err(DFB_ERR_ARG, "%d sequences > %d per context", n_seq, kMaxSeg);
-    if (p->temperature > 0.0f)
-        return set_err(DFB_ERR_UNSUPPORTED, "temperature > 0 sampling is not implemented on the device path");
+    if (!std::isfinite(p->temperature)) return set_err(DFB_ERR_ARG, "temperature must be finite");
     if (p->remasking < 0 || p->remasking > 4) return set_err(DFB_ERR_ARG, "bad remasking %d", p->remasking);
     const dfb_model *m = c->m;
     CK(cudaSetDevice(m->device));
@@ -1224,7 +1265,20 @@ extern "C" int dfb_gen_begin_batch(dfb_ctx *c, int n_seq, const int32_t *prompts
     c->seg_gen.assign(n_gens, n_gens + n_seq);
     c->seg_masked.assign(n_gens, n_gens + n_seq);
     c->sp = *p;
+    c->unif_n = -1;
     c->gen_active = true;
+    return DFB_OK;
+}
+
+extern "C" int dfb_gen_set_uniforms(dfb_ctx *c, const double *u, int n) {
+    if (!c || n < 0 || (n > 0 && !u)) return set_err(DFB_ERR_ARG, "bad arguments");
+    if (!c->gen_active) return set_err(DFB_ERR_STATE, "dfb_gen_begin not called");
+    if (n > c->cap) return set_err(DFB_ERR_ARG, "%d uniforms > %d positions", n, c->cap);
+    for (int i = 0; i < n; i++)
+        if (!(u[i] >= 0.0 && u[i] < 1.0)) return set_err(DFB_ERR_ARG, "uniform %d outside [0, 1)", i);
+    CK(cudaSetDevice(c->m->device));
+    if (n) CK(cudaMemcpyAsync(c->unif, u, sizeof(double) * n, cudaMemcpyHostToDevice, c->st));
+    c->unif_n = n;
     return DFB_OK;
 }
 
@@ -1253,6 +1307,10 @@ extern "C" int dfb_gen_step_batch(dfb_ctx *c, int step, const int32_t *n_unmask_
         masked_all += c->seg_masked[sg];
     }
     if (n_live == 0) return set_err(DFB_ERR_STATE, "every sequence is complete");
+    const bool sampled = c->sp.temperature > 0.0f;
+    if (sampled && c->unif_n != masked_all)
+        return set_err(DFB_ERR_ARG, "temperature > 0: the step needs %d uniforms (dfb_gen_set_uniforms), %d set", masked_all,
+                       c->unif_n);
     if (c->sp.remasking == 1) {
         if (!orders) return set_err(DFB_ERR_ARG, "RANDOM remasking needs the host shuffle orders");
         CK(cudaMemcpyAsync(c->order, orders, sizeof(int32_t) * masked_all, cudaMemcpyHostToDevice, c->st));
@@ -1267,6 +1325,12 @@ extern "C" int dfb_gen_step_batch(dfb_ctx *c, int step, const int32_t *n_unmask_
     row_stats_kernel<<<masked_all, 512, 0, c->st>>>(c->logits, m->hp.n_vocab, c->masked_row, c->cnt, margin, c->cand_tok,
                                                     c->cand_conf, c->cand_ent);
     CK(cudaGetLastError());
+    if (sampled) {  // draw the candidates' tokens; the entropy stays row_stats'
+        sample_kernel<<<masked_all, kSampleThreads, 0, c->st>>>(c->logits, m->hp.n_vocab, c->masked_row, c->cnt,
+                                                                 c->sp.temperature, c->unif, c->cand_tok, c->cand_conf);
+        CK(cudaGetLastError());
+        c->unif_n = -1;
+    }
     int np = 1;
     while (np < max_masked) np <<= 1;
     const size_t sel_smem = sizeof(unsigned long long) * (size_t)np;
@@ -1430,7 +1494,7 @@ extern "C" int dfb_linear_noalloc(const dfb_model *m, int role, int layer, const
     if (w->n_tiles > kNoallocMaxTiles)
         return set_err(DFB_ERR_ARG, "weight has %d output tiles, the fixed scratch holds %d", w->n_tiles, kNoallocMaxTiles);
     XMaps xm;  // host-side descriptors of the caller's matrix (no device memory)
-    RET(make_xmaps(&xm, x_f16_dev, K, M, 1));
+    RET(make_xmaps(&xm, x_f16_dev, nullptr, K, M, 1));
     std::lock_guard<std::mutex> lk(device_lock(m->device));
     CK(cudaSetDevice(m->device));
     NoallocDev nd;

@@ -185,7 +185,8 @@ __device__ __forceinline__ float block_sum(float v, float *red) {
 // thread step (float4 loads); d is a multiple of 64.
 __global__ void __launch_bounds__(256) rmsnorm_kernel(float *__restrict__ x, const float *__restrict__ y,
                                                       const float *__restrict__ w, int d, float eps,
-                                                      const int *__restrict__ cnt, uint8_t *__restrict__ h) {
+                                                      const int *__restrict__ cnt, uint8_t *__restrict__ h,
+                                                      uint8_t *__restrict__ sums, int ld_sums) {
     __shared__ float red[33];
     griddep_launch_dependents();
     griddep_wait();  // x, y and the row count come from the previous kernels
@@ -194,6 +195,7 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(float *__restrict__ x, con
     float *xr = x + (size_t)a * d;
     const float *yr = y ? y + (size_t)a * d : nullptr;
     uint8_t *hr = h + (size_t)a * 4 * d;
+    uint8_t *sr = sums + (size_t)a * ld_sums;
     float ss = 0.f;
     for (int i = threadIdx.x * 8; i < d; i += blockDim.x * 8) {
         float4 v0 = *reinterpret_cast<const float4 *>(xr + i);
@@ -219,6 +221,12 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(float *__restrict__ x, con
         const float v[8] = {(v0.x * scale) * w0.x, (v0.y * scale) * w0.y, (v0.z * scale) * w0.z, (v0.w * scale) * w0.w,
                             (v1.x * scale) * w1.x, (v1.y * scale) * w1.y, (v1.z * scale) * w1.z, (v1.w * scale) * w1.w};
         store_pair8(hr, i, v);
+        // sub-block sum of 32 values: four consecutive threads (d % 32 == 0, so whole groups are active)
+        float ps = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+        const unsigned am = __activemask();
+        ps += __shfl_xor_sync(am, ps, 1);
+        ps += __shfl_xor_sync(am, ps, 2);
+        if ((threadIdx.x & 3) == 0) store_sum(sr, i >> 5, ps);
     }
 }
 
@@ -441,7 +449,106 @@ __global__ void __launch_bounds__(1024) select_commit_kernel(int remasking, cons
 }
 
 // X (f32 [rows][K], host-provided for dfb_linear) -> pair rows (4 K bytes each); K multiple of 64.
-__global__ void f32_to_pair_kernel(const float *__restrict__ x, uint8_t *__restrict__ y, int rows, int K) {
+// Sampling at temperature > 0 (diffuse-sampler.cpp:256-269): probabilities
+// p_v = expf((l_v - max) / T) / sum_v expf(...) in f32, then the draw of
+// std::discrete_distribution<int>(p) with the uniform u the host took from the loop's
+// mt19937 (std::generate_canonical<double, 53>, one per candidate in position order): the
+// weights as doubles divided by their double sum, cumulative sums, the first index whose
+// cumulative sum reaches u (the last index if rounding leaves every sum below u, as the
+// distribution sets its last cumulative sum to 1).  The confidence is p of the drawn
+// token.  The sums are block reductions here, serial in the reference, and the device
+// expf is not the host libm's: p agrees to a few f32 ulp, so a draw can differ only when u
+// falls within that distance of a cumulative sum.  One block per masked candidate.
+__device__ __forceinline__ double block_sum_d(double v, double *red) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+        double w = lane < nw ? red[lane] : 0.0;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) w += __shfl_xor_sync(0xffffffffu, w, o);
+        if (lane == 0) red[32] = w;
+    }
+    __syncthreads();
+    const double r = red[32];
+    __syncthreads();
+    return r;
+}
+constexpr int kSampleThreads = 512;
+__global__ void __launch_bounds__(kSampleThreads) sample_kernel(const float *__restrict__ logits, int n_vocab,
+                                                                 const int *__restrict__ masked_row, const int *__restrict__ cnt,
+                                                                 float temperature, const double *__restrict__ unif,
+                                                                 int32_t *__restrict__ cand_tok, float *__restrict__ cand_conf) {
+    __shared__ float red[33];
+    __shared__ double redd[33];
+    __shared__ double scan[kSampleThreads];
+    const int b = blockIdx.x;
+    if (b >= cnt[CNT_NMASKED]) return;
+    const float *z = logits + (size_t)masked_row[b] * n_vocab;
+    const int tid = threadIdx.x;
+    // max
+    float mx = -INFINITY;
+    for (int v = tid; v < n_vocab; v += blockDim.x) mx = fmaxf(mx, z[v]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((tid & 31) == 0) red[tid >> 5] = mx;
+    __syncthreads();
+    if (tid < 32) {
+        float w = tid < (int)(blockDim.x >> 5) ? red[tid] : -INFINITY;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) w = fmaxf(w, __shfl_xor_sync(0xffffffffu, w, o));
+        if (tid == 0) red[32] = w;
+    }
+    __syncthreads();
+    mx = red[32];
+    __syncthreads();
+    auto prob = [&](int v) { return expf((z[v] - mx) / temperature); };
+    float se = 0.f;
+    for (int v = tid; v < n_vocab; v += blockDim.x) se += prob(v);
+    const float S = block_sum(se, red);
+    // the distribution's weights: p_v = f32(prob / S) as doubles, normalised by their sum
+    double sd = 0.0;
+    for (int v = tid; v < n_vocab; v += blockDim.x) sd += (double)(prob(v) / S);
+    const double D = block_sum_d(sd, redd);
+    // cumulative sums over contiguous chunks: thread t covers [t C, t C + C)
+    const int C = (n_vocab + blockDim.x - 1) / blockDim.x;
+    const int v0 = min(n_vocab, tid * C), v1 = min(n_vocab, v0 + C);
+    double cs = 0.0;
+    for (int v = v0; v < v1; v++) cs += (double)(prob(v) / S) / D;
+    scan[tid] = cs;
+    __syncthreads();
+    for (int off = 1; off < (int)blockDim.x; off <<= 1) {  // inclusive scan (Hillis-Steele)
+        const double add = tid >= off ? scan[tid - off] : 0.0;
+        __syncthreads();
+        scan[tid] += add;
+        __syncthreads();
+    }
+    const double u = unif[b];
+    const double before = tid ? scan[tid - 1] : 0.0;
+    int pick = -1;
+    if (u <= 0.0) {
+        if (tid == 0) pick = 0;  // the first cumulative sum is >= 0
+    } else if (before < u && scan[tid] >= u) {  // the crossing lies in this thread's chunk
+        double c = before;
+        for (int v = v0; v < v1; v++) {
+            c += (double)(prob(v) / S) / D;
+            if (c >= u) { pick = v; break; }
+        }
+        if (pick < 0) pick = v1 - 1;
+    } else if (tid == (int)blockDim.x - 1 && scan[tid] < u) {
+        pick = n_vocab - 1;
+    }
+    if (pick >= 0) {
+        cand_tok[b] = pick;
+        cand_conf[b] = prob(pick) / S;
+    }
+}
+
+// ld_sums: bytes per sums row.  K % 32 == 0: the four threads of a sub-block are active together.
+__global__ void f32_to_pair_kernel(const float *__restrict__ x, uint8_t *__restrict__ y, int rows, int K,
+                                   uint8_t *__restrict__ sums, int ld_sums) {
     const size_t groups = (size_t)rows * (K / 8);
     for (size_t g = blockIdx.x * (size_t)blockDim.x + threadIdx.x; g < groups; g += (size_t)gridDim.x * blockDim.x) {
         const size_t r = g / (K / 8);
@@ -450,6 +557,11 @@ __global__ void f32_to_pair_kernel(const float *__restrict__ x, uint8_t *__restr
 #pragma unroll
         for (int e = 0; e < 8; e++) v[e] = x[r * K + i + e];
         store_pair8(y + r * 4 * K, i, v);
+        float ps = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+        const unsigned am = __activemask();
+        ps += __shfl_xor_sync(am, ps, 1);
+        ps += __shfl_xor_sync(am, ps, 2);
+        if ((g & 3) == 0) store_sum(sums + r * ld_sums, i >> 5, ps);
     }
 }
 

@@ -12,6 +12,7 @@
 #include <chrono>
 #include <cmath>
 #include <cstring>
+#include <limits>
 #include <numeric>
 #include <random>
 #include <string>
@@ -305,6 +306,7 @@ static int generate_impl(diffuse_context *ctx, const std::vector<int32_t> &promp
     double total_forward_ms = 0, total_sample_ms = 0;
     int actual_steps = 0;
     std::vector<int32_t> seq(total_len), order;
+    std::vector<double> unif;
     const auto gen_start = clk::now();
     for (int step = 0; step < params.n_steps && n_masked > 0; step++) {
         actual_steps++;
@@ -312,6 +314,14 @@ static int generate_impl(diffuse_context *ctx, const std::vector<int32_t> &promp
                                 (params.cache_refresh > 0 && step > 0 && (step % params.cache_refresh == 0));
         const int n_unmask = tokens_to_unmask(step, params.n_steps, n_masked, params.schedule);
         const int32_t *ord = nullptr;
+        if (params.temperature > 0.0f) {
+            // the sampling loop's draws come first in the reference's step (sampler.cpp:256-269):
+            // one generate_canonical per masked position, in position order
+            unif.resize(n_masked);
+            for (auto &x : unif) x = std::generate_canonical<double, std::numeric_limits<double>::digits>(rng);
+            if (dfb_gen_set_uniforms(ctx->dc, unif.data(), n_masked) != DFB_OK)
+                return set_error(DFB_ERR_ARG, "%s", dfb_last_error());
+        }
         if (params.remasking == diffuse_remasking::RANDOM) {
             // std::shuffle of the ascending candidate list with the shared mt19937
             // (sampler.cpp:307): the permutation depends only on the count and the rng.
@@ -459,6 +469,7 @@ int dfc_generate_batch(void *ctx_, const int32_t *prompts, const int32_t *prompt
     std::vector<std::mt19937> rngs(n_seq, std::mt19937(p->seed));
     std::vector<int> n_masked(n_seq, n_generate);
     std::vector<int32_t> sched(n_seq), orders;
+    std::vector<double> unif;
     std::vector<dfb_step_stats> st(n_seq);
     bool cache_initialized = false;
     int steps = 0;
@@ -469,9 +480,13 @@ int dfc_generate_batch(void *ctx_, const int32_t *prompts, const int32_t *prompt
         const bool force_full = !p->use_cache || !cache_initialized ||
                                 (p->cache_refresh > 0 && step > 0 && (step % p->cache_refresh == 0));
         orders.clear();
+        unif.clear();
         for (int sg = 0; sg < n_seq; sg++) {
             if (!n_masked[sg]) { sched[sg] = -1; continue; }
             sched[sg] = tokens_to_unmask(step, p->n_steps, n_masked[sg], (diffuse_schedule)p->schedule);
+            if (p->temperature > 0.0f)  // the sequence's sampling draws, before its shuffle (sampler.cpp:256-269)
+                for (int i = 0; i < n_masked[sg]; i++)
+                    unif.push_back(std::generate_canonical<double, std::numeric_limits<double>::digits>(rngs[sg]));
             if (p->remasking == (int)diffuse_remasking::RANDOM) {
                 // the sequence's own std::shuffle of its ascending candidate list (sampler.cpp:307)
                 std::vector<int32_t> o(n_masked[sg]);
@@ -480,6 +495,8 @@ int dfc_generate_batch(void *ctx_, const int32_t *prompts, const int32_t *prompt
                 orders.insert(orders.end(), o.begin(), o.end());
             }
         }
+        if (p->temperature > 0.0f && dfb_gen_set_uniforms(ctx->dc, unif.data(), (int)unif.size()) != DFB_OK)
+            return set_error(DFB_ERR_ARG, "%s", dfb_last_error());
         if (dfb_gen_step_batch(ctx->dc, step, sched.data(), force_full ? 1 : 0, orders.empty() ? nullptr : orders.data(),
                                st.data()) != DFB_OK)
             return set_error(DFB_ERR_CUDA, "forward pass failed at step %d: %s", step, dfb_last_error());

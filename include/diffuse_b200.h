@@ -125,6 +125,14 @@ int dfb_gen_begin(dfb_ctx *c, const int32_t *prompt, int n_prompt, int n_gen, co
  * fills *stats (may be NULL). */
 int dfb_gen_step(dfb_ctx *c, int step, int n_unmask_sched, int force_full, const int32_t *order,
                  dfb_step_stats *stats);
+/* temperature > 0: the uniforms of the next step's draws, one per masked position (batch:
+ * per live sequence, concatenated in sequence order), each in ascending position order --
+ * the values std::discrete_distribution draws from the loop's mt19937 in the reference's
+ * sampling loop (diffuse-sampler.cpp:256-269: std::generate_canonical<double, 53>, taken
+ * before any RANDOM shuffle of the same step).  Required before every step at
+ * temperature > 0; the step draws token v with probability
+ * expf((l_v - max) / T) / sum, and the candidate's confidence is that probability. */
+int dfb_gen_set_uniforms(dfb_ctx *c, const double *u, int n);
 /* Copy the whole current sequence (prompt ‖ generated) to the host (batch: all
  * sequences' positions, concatenated in order). */
 int dfb_gen_tokens(dfb_ctx *c, int32_t *seq_host, int cap);

@@ -986,6 +986,34 @@ int orc_sess_tokens(const orc_session *s, int32_t *seq_out) {
     return s->n_masked;
 }
 
+// diffuse-sampler.cpp:256-269 with the draw's uniform given (the distribution's own draw
+// is std::generate_canonical<double, 53> on the loop's rng, orc_canonical).
+int32_t orc_sample_row(const float *row, int32_t n_vocab, float temperature, double u, float *conf, double *margin) {
+    const float max_logit = *std::max_element(row, row + n_vocab);
+    std::vector<float> probs(n_vocab);
+    float sum = 0.0f;
+    for (int v = 0; v < n_vocab; v++) {
+        probs[v] = expf((row[v] - max_logit) / temperature);
+        sum += probs[v];
+    }
+    for (int v = 0; v < n_vocab; v++) probs[v] /= sum;
+    std::discrete_distribution<int>::param_type prm(probs.begin(), probs.end());
+    const std::vector<double> w = prm.probabilities();  // normalised by their double sum
+    std::vector<double> cp(w.size());
+    std::partial_sum(w.begin(), w.end(), cp.begin());
+    cp.back() = 1.0;
+    const int k = (int)(std::lower_bound(cp.begin(), cp.end(), u) - cp.begin());
+    if (conf) *conf = probs[k];
+    if (margin) *margin = std::min(cp[k] - u, k ? u - cp[k - 1] : u);
+    return k;
+}
+
+int orc_canonical(uint32_t seed, int32_t n, double *out) {
+    std::mt19937 rng(seed);
+    for (int i = 0; i < n; i++) out[i] = std::generate_canonical<double, std::numeric_limits<double>::digits>(rng);
+    return 0;
+}
+
 // diffuse_sample, diffuse-sampler.cpp:60-370: forward + sampler per step until no mask is left.
 int orc_generate(const orc_model *m, const int32_t *prompt, int32_t n_prompt, int32_t n_gen,
                  const orc_sampler_params *pp, int32_t *out_tokens, orc_trace *trace, int32_t mode, int32_t nt_) {

@@ -115,6 +115,18 @@ int orc_sampler_step(const float *logits_full, int32_t n_vocab, int32_t total_le
                      const orc_sampler_params *p, int32_t *commit_pos, int32_t *commit_tok,
                      float *cand_entropy, float *cand_conf);
 
+// One temperature > 0 draw as the reference's sampling loop makes it
+// (diffuse-sampler.cpp:256-269), with the uniform given: probabilities
+// expf((l - max) / T) / sum (f32, serial sum), std::discrete_distribution's
+// normalised cumulative sums (double), the first index reaching u.  Writes the drawn
+// token's probability (the candidate's confidence) and the distance from u to the
+// nearest cumulative sum bounding the draw.
+int32_t orc_sample_row(const float *row, int32_t n_vocab, float temperature, double u, float *conf, double *margin);
+
+// The uniforms std::discrete_distribution draws from std::mt19937(seed): n values of
+// std::generate_canonical<double, 53>.
+int orc_canonical(uint32_t seed, int32_t n, double *out);
+
 // Schedule count (diffuse-sampler.cpp:12-31).
 int orc_tokens_to_unmask(int32_t step, int32_t total_steps, int32_t total_masked, int32_t schedule);
 

@@ -85,6 +85,8 @@ def lib():
             ("orc_sess_forward", I, [P, I]), ("orc_sess_sample", I, [P, I, P, P]), ("orc_sess_commit", I, [P, P, P, I]),
             ("orc_sess_logits", I, [P, I, I, P]), ("orc_sess_tokens", I, [P, P]),
             ("orc_synth_model", I, [C.c_char_p, C.POINTER(SynthSpec)]),
+            ("orc_sample_row", I, [P, I, C.c_float, C.c_double, P, P]),
+            ("orc_canonical", I, [C.c_uint32, I, P]),
         ]:
             fn = getattr(_lib, name)
             fn.restype, fn.argtypes = res, args
@@ -132,6 +134,23 @@ def sampler_step(logits_full, seq, is_masked, is_dream, step, params: SamplerPar
     k = lib().orc_sampler_step(_p(logits_full), logits_full.shape[1], seq.size, _p(seq), _p(msk), int(is_dream),
                                step, C.byref(params), _p(cp), _p(ct), _p(ent), _p(conf))
     return dict(n=k, pos=cp[:k], tok=ct[:k], entropy=ent[:n], conf=conf[:n], seq=seq, masked=msk)
+
+
+def sample_row(row, temperature: float, u: float):
+    """The reference's temperature > 0 draw on one logits row with the uniform given:
+    (token, its probability, distance from u to the nearest bounding cumulative sum)."""
+    row = np.ascontiguousarray(row, dtype=np.float32)
+    conf = np.zeros(1, np.float32)
+    margin = np.zeros(1, np.float64)
+    k = lib().orc_sample_row(_p(row), row.size, float(temperature), float(u), _p(conf), _p(margin))
+    return int(k), float(conf[0]), float(margin[0])
+
+
+def canonical(seed: int, n: int) -> np.ndarray:
+    """The uniforms std::discrete_distribution draws from std::mt19937(seed)."""
+    out = np.zeros(max(n, 1), np.float64)
+    lib().orc_canonical(seed, n, _p(out))
+    return out[:n]
 
 
 class OracleModel:

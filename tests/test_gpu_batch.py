@@ -25,8 +25,9 @@ def _prompts(hp, lens, seed):
 @pytest.mark.parametrize("name,kw", [
     ("q4km", dict(n_steps=8, remasking=0, use_cache=1)),
     ("q4km", dict(n_steps=8, remasking=1, use_cache=1, seed=3)),
+    ("q4km", dict(n_steps=8, remasking=1, use_cache=1, seed=4, temperature=0.9)),
     ("dream", dict(n_steps=8, remasking=2, use_cache=1, entropy_threshold=1.5)),
-], ids=["lowconf", "random", "dream-entropy"])
+], ids=["lowconf", "random", "random-temperature", "dream-entropy"])
 def test_batch_matches_sequences_run_alone(pkg, models, name, kw):
     model = pkg.Model(models[name])
     ctx = pkg.Context(model, 0)

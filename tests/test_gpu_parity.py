@@ -189,12 +189,70 @@ def test_tied_lm_head_teacher_forced(pkg, orc, models):
     _teacher_forced(pkg, orc, models["tied"], 16, 24, dict(n_steps=6, remasking=0, use_cache=1))
 
 
+def test_temperature_sampling_teacher_forced(pkg, orc, models):
+    """temperature > 0 (diffuse-sampler.cpp:256-269), step by step: the host gives the
+    device the reference's uniforms (std::mt19937(seed), one std::generate_canonical per
+    masked position in position order, orc.canonical); on the device's own logits the
+    reference's draw with the same uniform (orc.sample_row) must be the device's committed
+    token, unless the uniform lies within EPS of a cumulative sum (device expf and tree
+    sums against libm expf and serial sums); the commit set must be the reference's
+    top-k by the drawn tokens' probabilities."""
+    EPS = 1e-5
+    path = models["q4km"]
+    model = pkg.Model(path)
+    ctx = pkg.Context(model, 0)
+    hp = model.hparams
+    n_prompt, n_gen, T, seed = 16, 32, 0.8, 5
+    prompt = np.random.default_rng(9).integers(0, hp.mask_token_id - 1, n_prompt).astype(np.int32)
+    P = pkg.SamplerParams(n_steps=8, remasking=0, use_cache=1, temperature=T, seed=seed)
+    U = orc.canonical(seed, n_gen * P.n_steps)
+    ctx.gen_begin(prompt, n_gen, P)
+    n_masked, initialized, off, checked, near = n_gen, False, 0, 0, 0
+    for step in range(P.n_steps):
+        if n_masked == 0:
+            break
+        seq = ctx.gen_tokens()
+        cand = np.flatnonzero(seq[n_prompt:] == hp.mask_token_id) + n_prompt
+        assert cand.size == n_masked
+        force = not initialized
+        k = pkg.tokens_to_unmask(step, P.n_steps, n_masked, P.schedule)
+        u = U[off:off + n_masked]
+        off += n_masked
+        ctx.gen_set_uniforms(u)
+        st = ctx.gen_step(step, k, force)
+        initialized = True
+        logits = ctx.logits_rows(0, seq.size)
+        pos, tok = ctx.gen_commits()
+        draws = {int(p): orc.sample_row(logits[p], T, u[i]) for i, p in enumerate(cand)}
+        assert st["n_unmasked"] == k
+        step_near = [p for p in cand.tolist() if draws[p][2] < EPS]
+        near += len(step_near)
+        for p, t in zip(pos.tolist(), tok.tolist()):
+            if draws[p][2] >= EPS:
+                assert t == draws[p][0], (step, p, t, draws[p])
+                checked += 1
+        if not step_near:
+            # LOW_CONFIDENCE: the k candidates of highest probability (ties within a few ulp may swap)
+            conf = {p: d[1] for p, d in draws.items()}
+            ranked = sorted(conf, key=lambda p: -conf[p])
+            g, r = set(pos.tolist()), set(ranked[:k])
+            if g != r:
+                cut = conf[ranked[k - 1]]
+                for p in g ^ r:
+                    assert abs(conf[p] - cut) <= 1e-5 * max(cut, 1e-30), (step, p, conf[p], cut)
+        n_masked = st["n_masked"]
+    print(f"temperature {T}: {checked} committed draws checked, {near} near a cumulative-sum boundary")
+    assert checked >= n_gen - near - 1
+    ctx.close(); model.close()
+
+
 @pytest.mark.parametrize("name,kw", [
     ("q4km", dict(n_steps=8, remasking=0, use_cache=1)),
+    ("q4km", dict(n_steps=8, remasking=0, use_cache=1, temperature=0.8, seed=3)),
     ("q4km", dict(n_steps=8, remasking=1, use_cache=1, seed=7)),
     ("dream", dict(n_steps=8, remasking=2, use_cache=1, entropy_threshold=1.5)),
     ("tiny", dict(n_steps=8, remasking=0, use_cache=0)),
-], ids=["q4km-lowconf", "q4km-random", "dream-entropy", "tiny-nocache"])
+], ids=["q4km-lowconf", "q4km-temperature", "q4km-random", "dream-entropy", "tiny-nocache"])
 def test_generate_tokens_agree_with_oracle(pkg, orc, models, name, kw):
     """Free-running runs of the whole loop through the public API (diffuse_generate)
     against the oracle's: committed tokens, per-step commit counts, active-row counts and,

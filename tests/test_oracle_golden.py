@@ -60,3 +60,32 @@ def test_entropy_reference_formula(orc):
     p = np.exp(z) / np.exp(z).sum()
     ref = float(-(p[p > 1e-10] * np.log(p[p > 1e-10])).sum())
     assert abs(orc.entropy(row) - ref) < 1e-4
+
+
+def test_temperature_draw_restatement_matches_discrete_distribution(orc):
+    """orc_sample_row (the temperature > 0 draw with its uniform given) and orc_canonical
+    (std::generate_canonical<double, 53> on std::mt19937) against the oracle's own
+    sampling loop, which calls std::discrete_distribution on the rng directly
+    (diffuse-sampler.cpp:256-269): the committed tokens and every candidate's confidence
+    must agree bit for bit."""
+    rng = np.random.default_rng(3)
+    V, n_prompt, n = 3000, 8, 24
+    total = n_prompt + n
+    logits = (rng.standard_normal((total, V)) * 3).astype(np.float32)
+    seq = np.zeros(total, np.int32)
+    masked = np.zeros(total, np.uint8)
+    masked[n_prompt:] = 1
+    for T in (0.7, 1.0, 2.5):
+        P = orc.SamplerParams(n_steps=4, temperature=T, remasking=0, seed=11)
+        ref = orc.sampler_step(logits, seq, masked, False, 0, P)
+        u = orc.canonical(11, n)
+        cand = np.flatnonzero(masked)
+        picks = {}
+        for i, p in enumerate(cand):
+            k, conf, margin = orc.sample_row(logits[p], T, u[i])
+            assert conf == ref["conf"][i], (T, i)
+            assert margin >= 0.0
+            picks[int(p)] = k
+        assert ref["n"] > 0
+        for p, t in zip(ref["pos"].tolist(), ref["tok"].tolist()):
+            assert picks[p] == t, (T, p)
