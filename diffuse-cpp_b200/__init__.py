@@ -109,6 +109,9 @@ def _load():
         (dfb, "dfb_ctx_stream"): (I, [P, C.POINTER(P)]),
         (dfc, "dfc_last_error"): (C.c_char_p, []),
         (dfc, "dfc_model_load"): (P, [C.c_char_p, I]),
+        (dfc, "dfc_model_load_tp"): (P, [C.c_char_p, I, I, P, I]),
+        (dfc, "dfc_model_tp_info"): (I, [P, P, P, P, P]),
+        (dfb, "dfb_tp_unique_id"): (I, [P, I]),
         (dfc, "dfc_model_free"): (None, [P]),
         (dfc, "dfc_model_hparams"): (I, [P, P, P]),
         (dfc, "dfc_context_new"): (P, [P, I, I]),
@@ -213,17 +216,36 @@ class HParams:
     rms_norm_eps: float
 
 
-class Model:
-    """diffuse_model: GGUF parsed and uploaded to the current CUDA device."""
+def tp_unique_id() -> bytes:
+    """A fresh NCCL id for a tensor-parallel group (one rank creates it, every rank passes it)."""
+    buf = np.zeros(128, np.uint8)
+    if native()[0].dfb_tp_unique_id(_ptr(buf), buf.size) != 0:
+        raise DiffuseError(_dfb_err())
+    return buf.tobytes()
 
-    def __init__(self, path, n_threads: int = 4):
-        self._h = native()[1].dfc_model_load(str(path).encode(), n_threads)
+
+class Model:
+    """diffuse_model: GGUF parsed and uploaded to the current CUDA device (DIFFUSE_DEVICE
+    selects another).  tp=(rank, size, nccl_id): this rank's slice of a tensor-parallel group
+    (every rank loads at the same time); logits then hold the rank's vocabulary columns
+    [tp_v0, tp_v0 + tp_vocab)."""
+
+    def __init__(self, path, n_threads: int = 4, tp=None):
+        if tp is None:
+            self._h = native()[1].dfc_model_load(str(path).encode(), n_threads)
+        else:
+            rank, size, nid = tp
+            idb = np.frombuffer(bytes(nid), np.uint8).copy()
+            self._h = native()[1].dfc_model_load_tp(str(path).encode(), rank, size, _ptr(idb), idb.size)
         if not self._h:
             raise DiffuseError(_dfc_err())
         i = np.zeros(9, np.int32)
         f = np.zeros(2, np.float32)
         native()[1].dfc_model_hparams(self._h, _ptr(i), _ptr(f))
         self.hparams = HParams(*[int(v) for v in i[:8]], bool(i[8]), float(f[0]), float(f[1]))
+        t = np.zeros(4, np.int32)
+        native()[1].dfc_model_tp_info(self._h, _ptr(t[0:]), _ptr(t[1:]), _ptr(t[2:]), _ptr(t[3:]))
+        self.tp_rank, self.tp_size, self.tp_v0, self.tp_vocab = (int(v) for v in t)
 
     def close(self):
         if self._h:
@@ -248,9 +270,10 @@ class Context:
         self.engine = native()[1].dfc_context_engine(self._h)
 
     def forward(self, tokens) -> np.ndarray:
-        """diffuse_forward: logits [n, n_vocab] for n tokens (no cache)."""
+        """diffuse_forward: logits [n, n_vocab] for n tokens (no cache); a tensor-parallel
+        rank gets its vocabulary columns [n, tp_vocab]."""
         t = np.ascontiguousarray(tokens, dtype=np.int32)
-        out = np.empty((t.size, self.model.hparams.n_vocab), dtype=np.float32)
+        out = np.empty((t.size, self.model.tp_vocab), dtype=np.float32)
         if not native()[1].dfc_forward(self._h, _ptr(t), t.size, _ptr(out)):
             raise DiffuseError(_dfc_err())
         return out
@@ -395,7 +418,7 @@ class Context:
 
     # ── direct access to the device state of the current generation ──
     def logits_rows(self, row0: int, nrows: int) -> np.ndarray:
-        out = np.empty((nrows, self.model.hparams.n_vocab), dtype=np.float32)
+        out = np.empty((nrows, self.model.tp_vocab), dtype=np.float32)
         if native()[0].dfb_gen_logits(self.engine, row0, nrows, _ptr(out)) != 0:
             raise DiffuseError(_dfb_err())
         return out

@@ -13,6 +13,8 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
+#include <dlfcn.h>
+#include <nccl.h>
 
 #include <algorithm>
 #include <cmath>
@@ -399,6 +401,40 @@ static int build_wmat(const std::vector<const uint8_t *> &rows_in, int type, int
     return DFB_OK;
 }
 
+// ───────────────────────── NCCL (tensor parallelism only) ─────────────────────────
+// Bound at run time on first use, so the library loads and runs single-GPU without NCCL; in a
+// process that already holds libnccl.so.2 (e.g. torch's) dlopen returns that copy.
+struct NcclApi {
+    bool ok = false;
+    ncclResult_t (*get_unique_id)(ncclUniqueId *) = nullptr;
+    ncclResult_t (*comm_init_rank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*all_reduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*all_gather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+    const char *(*error_string)(ncclResult_t) = nullptr;
+};
+static NcclApi &nccl_api() {
+    static NcclApi a;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) return;
+        a.get_unique_id = (decltype(a.get_unique_id))dlsym(h, "ncclGetUniqueId");
+        a.comm_init_rank = (decltype(a.comm_init_rank))dlsym(h, "ncclCommInitRank");
+        a.all_reduce = (decltype(a.all_reduce))dlsym(h, "ncclAllReduce");
+        a.all_gather = (decltype(a.all_gather))dlsym(h, "ncclAllGather");
+        a.comm_destroy = (decltype(a.comm_destroy))dlsym(h, "ncclCommDestroy");
+        a.error_string = (decltype(a.error_string))dlsym(h, "ncclGetErrorString");
+        a.ok = a.get_unique_id && a.comm_init_rank && a.all_reduce && a.all_gather && a.comm_destroy && a.error_string;
+    });
+    return a;
+}
+#define NK(call)                                                                                      \
+    do {                                                                                              \
+        ncclResult_t _r = (call);                                                                     \
+        if (_r != ncclSuccess) return set_err(DFB_ERR_CUDA, "%s: %s", #call, nccl_api().error_string(_r)); \
+    } while (0)
+
 struct LayerW {
     WMat qkv, o, gateup, down;
     float *attn_norm = nullptr, *ffn_norm = nullptr, *bias_qkv = nullptr;
@@ -414,7 +450,13 @@ struct HostTensor {
 struct dfb_model {
     dfb_hparams hp{};
     int device = 0, n_sm = 0;
+    // per-rank dimensions (the whole model's when tp_size == 1): query / KV features of the
+    // rank's heads, its FFN features and its vocabulary rows [v0, v0 + n_vocab_l)
     int hd = 0, n_q = 0, n_kv = 0, nq_pad = 0, nk_pad = 0;
+    int n_head_l = 0, n_ff_l = 0, v0 = 0, n_vocab_l = 0;
+    // tensor parallelism (dfb_model_set_tp): this rank of tp_size, its NCCL communicator
+    int tp_rank = 0, tp_size = 1;
+    ncclComm_t comm = nullptr;
     std::vector<HostTensor> staged;  // [role + DFB_N_ROLES * layer]
     // device
     void *embd = nullptr;
@@ -460,6 +502,9 @@ extern "C" int dfb_model_create(const dfb_hparams *hp, int device, dfb_model **o
     m->n_kv = hp->n_head_kv * hd;
     m->nq_pad = (m->n_q + 127) / 128 * 128;
     m->nk_pad = (m->n_kv + 127) / 128 * 128;
+    m->n_head_l = hp->n_head;
+    m->n_ff_l = hp->n_ff;
+    m->n_vocab_l = hp->n_vocab;
     m->staged.resize((size_t)DFB_N_ROLES * hp->n_layer);
     m->layers.resize(hp->n_layer);
     *out = m;
@@ -507,6 +552,21 @@ extern "C" int dfb_model_finalize(dfb_model *m) {
     CK(cudaSetDevice(m->device));
     const dfb_hparams &hp = m->hp;
     const int d = hp.n_embd, ff = hp.n_ff, V = hp.n_vocab, hd = m->hd;
+    // this rank's slices (everything when tp_size == 1): heads [h0, h0 + n_head_l) and their
+    // KV heads, FFN features [f0, f0 + ffl), vocabulary rows [v0, v0 + n_vocab_l)
+    const int gq = hp.n_embd, gkv = hp.n_head_kv * hd;             // whole-model Q / KV widths
+    const int h0 = m->tp_rank * m->n_head_l, kvh0 = m->tp_rank * (m->n_kv / hd);
+    const int ffl = m->n_ff_l, f0 = m->tp_rank * ffl;
+    // a K-range [k0, k0 + n) of a GGUF row: its byte offset (k0 on a block boundary)
+    auto k_offset = [&](int type, int64_t k0, const char *what) -> int64_t {
+        const int64_t blk = type == G_Q4_K || type == G_Q6_K ? 256 : type == G_Q8_0 ? 32 : 1;
+        if (k0 % blk) {
+            set_err(DFB_ERR_UNSUPPORTED, "%s: the rank's K slice starts at %lld, inside a %lld-value block", what,
+                    (long long)k0, (long long)blk);
+            return -1;
+        }
+        return ggml_row_bytes(type, k0);
+    };
     // embeddings: F16 kept, everything else dequantized to f32
     {
         const HostTensor &e = staged(m, DFB_TOK_EMBD, 0);
@@ -535,18 +595,19 @@ extern "C" int dfb_model_finalize(dfb_model *m) {
         if (!out.data) out = staged(m, DFB_TOK_EMBD, 0);
         RET(check_mat(out, "output", d, V));
         const int64_t rb = ggml_row_bytes(out.type, d);
-        std::vector<const uint8_t *> rows((V + 127) / 128 * 128, nullptr);
-        for (int r = 0; r < V; r++) rows[r] = out.data + r * rb;
+        const int Vl = m->n_vocab_l;
+        std::vector<const uint8_t *> rows((Vl + 127) / 128 * 128, nullptr);
+        for (int r = 0; r < Vl; r++) rows[r] = out.data + (int64_t)(m->v0 + r) * rb;
         RET(build_wmat(rows, out.type, d, m->lm_head));
-        m->lm_head.n_true = V;
+        m->lm_head.n_true = Vl;
         m->bytes += m->lm_head.bytes;
     }
     for (int l = 0; l < hp.n_layer; l++) {
         LayerW &L = m->layers[l];
         const HostTensor &wq = staged(m, DFB_WQ, l), &wk = staged(m, DFB_WK, l), &wv = staged(m, DFB_WV, l);
-        RET(check_mat(wq, "attn_q", d, m->n_q));
-        RET(check_mat(wk, "attn_k", d, m->n_kv));
-        RET(check_mat(wv, "attn_v", d, m->n_kv));
+        RET(check_mat(wq, "attn_q", d, gq));
+        RET(check_mat(wk, "attn_k", d, gkv));
+        RET(check_mat(wv, "attn_v", d, gkv));
         if (wq.type != wk.type || wq.type != wv.type)
             return set_err(DFB_ERR_UNSUPPORTED, "layer %d: attn_q/k/v have different types (%d/%d/%d)", l, wq.type, wk.type, wv.type);
         // fused QKV rows: [Q | K | V], each section padded to 128 rows; Q and K rows
@@ -555,35 +616,41 @@ extern "C" int dfb_model_finalize(dfb_model *m) {
             std::vector<const uint8_t *> rows(m->nq_pad + 2 * m->nk_pad, nullptr);
             const int64_t rb = ggml_row_bytes(wq.type, d);
             for (int r = 0; r < m->n_q; r++) {
-                const int head = r / hd, rr = r % hd, i = rr >> 1, b = rr & 1;
+                const int head = h0 + r / hd, rr = r % hd, i = rr >> 1, b = rr & 1;
                 rows[r] = wq.data + (int64_t)(head * hd + i + b * (hd >> 1)) * rb;
             }
             for (int r = 0; r < m->n_kv; r++) {
-                const int head = r / hd, rr = r % hd, i = rr >> 1, b = rr & 1;
+                const int head = kvh0 + r / hd, rr = r % hd, i = rr >> 1, b = rr & 1;
                 rows[m->nq_pad + r] = wk.data + (int64_t)(head * hd + i + b * (hd >> 1)) * rb;
-                rows[m->nq_pad + m->nk_pad + r] = wv.data + (int64_t)r * rb;
+                rows[m->nq_pad + m->nk_pad + r] = wv.data + (int64_t)(kvh0 * hd + r) * rb;
             }
             RET(build_wmat(rows, wq.type, d, L.qkv));
             L.qkv.n_true = m->n_q + 2 * m->n_kv;
         }
         const HostTensor &bq = staged(m, DFB_BQ, l), &bk = staged(m, DFB_BK, l), &bv = staged(m, DFB_BV, l);
         if (bq.data || bk.data || bv.data) {
-            std::vector<float> b(m->nq_pad + 2 * m->nk_pad, 0.f);
-            if (bq.data) dequant_row_host(bq.type, bq.data, m->n_q, b.data());
-            if (bk.data) dequant_row_host(bk.type, bk.data, m->n_kv, b.data() + m->nq_pad);
-            if (bv.data) dequant_row_host(bv.type, bv.data, m->n_kv, b.data() + m->nq_pad + m->nk_pad);
+            std::vector<float> b(m->nq_pad + 2 * m->nk_pad, 0.f), full(std::max(gq, gkv));
+            auto slice = [&](const HostTensor &t, int n_all, int first, int n, float *dst) {
+                dequant_row_host(t.type, t.data, n_all, full.data());
+                std::copy(full.begin() + first, full.begin() + first + n, dst);
+            };
+            if (bq.data) slice(bq, gq, h0 * hd, m->n_q, b.data());
+            if (bk.data) slice(bk, gkv, kvh0 * hd, m->n_kv, b.data() + m->nq_pad);
+            if (bv.data) slice(bv, gkv, kvh0 * hd, m->n_kv, b.data() + m->nq_pad + m->nk_pad);
             CK(cudaMalloc(&L.bias_qkv, b.size() * 4));
             m->allocs.push_back(L.bias_qkv);
             CK(cudaMemcpy(L.bias_qkv, b.data(), b.size() * 4, cudaMemcpyHostToDevice));
         }
         const HostTensor &wo = staged(m, DFB_WO, l);
-        RET(check_mat(wo, "attn_output", m->n_q, d));
+        RET(check_mat(wo, "attn_output", gq, d));
         if (wo.type == G_Q4_K && m->hd % 32)  // the attention kernel writes sub-block sums per head
             return set_err(DFB_ERR_UNSUPPORTED, "layer %d: Q4_K attn_output needs head_dim %% 32 == 0 (head_dim %d)", l, m->hd);
         {
+            // the rank's heads' input columns of every output row (row-parallel: partial sums)
             std::vector<const uint8_t *> rows((d + 127) / 128 * 128, nullptr);
-            const int64_t rb = ggml_row_bytes(wo.type, m->n_q);
-            for (int r = 0; r < d; r++) rows[r] = wo.data + (int64_t)r * rb;
+            const int64_t rb = ggml_row_bytes(wo.type, gq), off = k_offset(wo.type, (int64_t)h0 * hd, "attn_output");
+            if (off < 0) return DFB_ERR_UNSUPPORTED;
+            for (int r = 0; r < d; r++) rows[r] = wo.data + (int64_t)r * rb + off;
             RET(build_wmat(rows, wo.type, m->n_q, L.o));
             L.o.n_true = d;
         }
@@ -593,20 +660,22 @@ extern "C" int dfb_model_finalize(dfb_model *m) {
         RET(check_mat(wd, "ffn_down", ff, d));
         if (wg.type != wu.type) return set_err(DFB_ERR_UNSUPPORTED, "layer %d: ffn_gate/up types differ", l);
         {
-            std::vector<const uint8_t *> rows((2 * ff + 127) / 128 * 128, nullptr);
+            std::vector<const uint8_t *> rows((2 * ffl + 127) / 128 * 128, nullptr);
             const int64_t rb = ggml_row_bytes(wg.type, d);
-            for (int i = 0; i < ff; i++) {
-                rows[2 * i] = wg.data + (int64_t)i * rb;
-                rows[2 * i + 1] = wu.data + (int64_t)i * rb;
+            for (int i = 0; i < ffl; i++) {
+                rows[2 * i] = wg.data + (int64_t)(f0 + i) * rb;
+                rows[2 * i + 1] = wu.data + (int64_t)(f0 + i) * rb;
             }
             RET(build_wmat(rows, wg.type, d, L.gateup));
-            L.gateup.n_true = 2 * ff;
+            L.gateup.n_true = 2 * ffl;
         }
         {
+            // the rank's FFN features' input columns of every output row (row-parallel)
             std::vector<const uint8_t *> rows((d + 127) / 128 * 128, nullptr);
-            const int64_t rb = ggml_row_bytes(wd.type, ff);
-            for (int r = 0; r < d; r++) rows[r] = wd.data + (int64_t)r * rb;
-            RET(build_wmat(rows, wd.type, ff, L.down));
+            const int64_t rb = ggml_row_bytes(wd.type, ff), off = k_offset(wd.type, f0, "ffn_down");
+            if (off < 0) return DFB_ERR_UNSUPPORTED;
+            for (int r = 0; r < d; r++) rows[r] = wd.data + (int64_t)r * rb + off;
+            RET(build_wmat(rows, wd.type, ffl, L.down));
             L.down.n_true = d;
         }
         RET(upload_vec(m, staged(m, DFB_ATTN_NORM, l), d, &L.attn_norm));
@@ -619,9 +688,56 @@ extern "C" int dfb_model_finalize(dfb_model *m) {
     return DFB_OK;
 }
 
+extern "C" int dfb_tp_unique_id(uint8_t *id, int nbytes) {
+    if (!id || nbytes < (int)sizeof(ncclUniqueId)) return set_err(DFB_ERR_ARG, "need %d bytes", (int)sizeof(ncclUniqueId));
+    if (!nccl_api().ok) return set_err(DFB_ERR_UNSUPPORTED, "libnccl.so.2 not found");
+    ncclUniqueId u;
+    NK(nccl_api().get_unique_id(&u));
+    memcpy(id, &u, sizeof(u));
+    return DFB_OK;
+}
+
+extern "C" int dfb_model_set_tp(dfb_model *m, int rank, int size, const uint8_t *id, int nbytes) {
+    if (!m || size < 1 || rank < 0 || rank >= size) return set_err(DFB_ERR_ARG, "bad arguments");
+    if (m->finalized) return set_err(DFB_ERR_STATE, "model already finalized");
+    if (size == 1) return DFB_OK;
+    if (!id || nbytes < (int)sizeof(ncclUniqueId)) return set_err(DFB_ERR_ARG, "need the %d-byte NCCL id", (int)sizeof(ncclUniqueId));
+    const dfb_hparams &hp = m->hp;
+    if (hp.n_head % size || hp.n_head_kv % size || hp.n_ff % (64 * size))
+        return set_err(DFB_ERR_UNSUPPORTED, "%d-way tensor parallelism needs n_head %d, n_head_kv %d divisible and n_ff %d / %d a multiple of 64",
+                       size, hp.n_head, hp.n_head_kv, hp.n_ff, size);
+    if (!nccl_api().ok) return set_err(DFB_ERR_UNSUPPORTED, "libnccl.so.2 not found");
+    m->tp_rank = rank;
+    m->tp_size = size;
+    m->n_head_l = hp.n_head / size;
+    m->n_q = m->n_head_l * m->hd;
+    m->n_kv = hp.n_head_kv / size * m->hd;
+    m->nq_pad = (m->n_q + 127) / 128 * 128;
+    m->nk_pad = (m->n_kv + 127) / 128 * 128;
+    m->n_ff_l = hp.n_ff / size;
+    const int vb = (hp.n_vocab + size - 1) / size;
+    m->v0 = std::min(hp.n_vocab, rank * vb);
+    m->n_vocab_l = std::min(hp.n_vocab, m->v0 + vb) - m->v0;
+    CK(cudaSetDevice(m->device));
+    ncclUniqueId u;
+    memcpy(&u, id, sizeof(u));
+    NK(nccl_api().comm_init_rank(&m->comm, size, u, rank));
+    return DFB_OK;
+}
+
+extern "C" int dfb_model_tp_info(const dfb_model *m, int *rank, int *size, int *v0, int *n_vocab_local) {
+    if (!m) return set_err(DFB_ERR_ARG, "null model");
+    if (rank) *rank = m->tp_rank;
+    if (size) *size = m->tp_size;
+    if (v0) *v0 = m->v0;
+    if (n_vocab_local) *n_vocab_local = m->n_vocab_l;
+    return DFB_OK;
+}
+
 extern "C" void dfb_model_free(dfb_model *m) {
     if (!m) return;
     cudaSetDevice(m->device);
+    if (m->comm) nccl_api().comm_destroy(m->comm);
     for (void *p : m->allocs) cudaFree(p);
     cudaFree(m->lm_head.d);
     for (auto &L : m->layers) {
@@ -656,6 +772,8 @@ struct dfb_ctx {
     int *active_pos = nullptr, *masked_pos = nullptr, *cnt = nullptr;
     float *cand_conf = nullptr, *cand_ent = nullptr;
     double *unif = nullptr;  // temperature > 0: the host's uniforms of the next step, one per masked candidate
+    float4 *tp_stats = nullptr, *tp_gath = nullptr;  // tensor parallelism: per-candidate statistics, all ranks'
+    float2 *tp_g = nullptr;                          // their combination (max, log Z)
     int unif_n = -1;         // how many the host set for the next step (-1: none)
     // sequences (segments) stepping together: positions [seg_off[s], seg_off[s+1]) of the
     // concatenated state; per-segment counters, schedule counts, finished flags, work lists
@@ -695,7 +813,7 @@ static void ctx_free_buffers(dfb_ctx *c) {
                   c->last_changed, c->cand_tok, c->commit_pos, c->commit_tok, c->order, c->masked, c->active_pos,
                   c->masked_pos, c->cnt, c->cand_conf, c->cand_ent, c->ws, c->tile_cnt, c->err, c->seg_off,
                   c->seg_cnt, c->sched, c->tmp_active, c->tmp_masked, c->rope_pos, c->masked_row, c->done, c->tiles,
-                  c->h_s, c->att_s, c->ffh_s, c->unif};
+                  c->h_s, c->att_s, c->ffh_s, c->unif, c->tp_stats, c->tp_gath, c->tp_g};
     for (void *p : ps) cudaFree(p);
     c->seg_off = c->seg_cnt = c->sched = c->tmp_active = c->tmp_masked = c->rope_pos = c->masked_row = nullptr;
     c->done = nullptr;
@@ -703,6 +821,8 @@ static void ctx_free_buffers(dfb_ctx *c) {
     c->x = c->y = c->logits = c->q = c->kc = c->vc = nullptr; c->h = c->att = c->ffh = nullptr; c->rope = nullptr;
     c->h_s = c->att_s = c->ffh_s = nullptr;
     c->unif = nullptr;
+    c->tp_stats = c->tp_gath = nullptr;
+    c->tp_g = nullptr;
     c->seq = c->prev_seq = c->last_changed = c->cand_tok = c->commit_pos = c->commit_tok = c->order = nullptr;
     c->masked = nullptr; c->active_pos = c->masked_pos = c->cnt = nullptr; c->cand_conf = c->cand_ent = nullptr;
     c->ws = nullptr; c->tile_cnt = c->err = nullptr;
@@ -730,7 +850,8 @@ static int ctx_reserve(dfb_ctx *c, int n) {
     const dfb_hparams &hp = m->hp;
     const int cap = std::max(n, 64);
     ctx_free_buffers(c);
-    const size_t d = hp.n_embd, ff = hp.n_ff, V = hp.n_vocab, L = hp.n_layer, kvd = m->n_kv, hd = m->hd;
+    // per-rank widths: FFN features and vocabulary rows of this rank (all of them at tp_size 1)
+    const size_t d = hp.n_embd, ff = m->n_ff_l, V = m->n_vocab_l, L = hp.n_layer, kvd = m->n_kv, hd = m->hd;
 #define AL(ptr, count) CK(cudaMalloc(&(ptr), sizeof(*(ptr)) * (size_t)(count)))
     AL(c->x, cap * d); AL(c->y, cap * d); AL(c->h, 4 * cap * d); AL(c->att, 4 * cap * d); AL(c->q, cap * d);
     AL(c->ffh, 4 * cap * ff);
@@ -739,6 +860,7 @@ static int ctx_reserve(dfb_ctx *c, int n) {
     AL(c->seq, cap); AL(c->prev_seq, cap); AL(c->last_changed, cap); AL(c->cand_tok, cap); AL(c->commit_pos, cap);
     AL(c->commit_tok, cap); AL(c->order, cap); AL(c->masked, cap); AL(c->active_pos, cap); AL(c->masked_pos, cap);
     AL(c->cnt, CNT_N); AL(c->cand_conf, cap); AL(c->cand_ent, cap); AL(c->unif, cap);
+    if (m->tp_size > 1) { AL(c->tp_stats, cap); AL(c->tp_gath, (size_t)cap * m->tp_size); AL(c->tp_g, cap); }
     AL(c->seg_off, kMaxSeg + 1); AL(c->seg_cnt, kMaxSeg * SEG_N); AL(c->sched, kMaxSeg); AL(c->done, kMaxSeg);
     AL(c->tmp_active, cap); AL(c->tmp_masked, cap); AL(c->rope_pos, cap); AL(c->masked_row, cap);
     AL(c->tiles, cap / kAttnRows + kMaxSeg + 1);
@@ -903,6 +1025,9 @@ static int launch_gemm_t(dfb_ctx *c, const WMat &w, const XMaps &xm, const EpiAr
     prof_begin(c, &ev0);
     // A pair tile is split over at most n_pairs/n_ptiles + 2 pairs; keep that within kMaxContrib.
     const int n_pairs = std::min(gemm_max_pairs<WT, EPI, 2>(c->m->device, c->m->n_sm), (kMaxContrib - 2) * (w.n_tiles / 2));
+    // the device schedule multiplies unit indices by the pair count in 32 bits
+    if ((double)(w.n_tiles / 2) * ((c->cap + kMaxTok - 1) / kMaxTok) * w.kb * (n_pairs + 1) >= 4294967296.0)
+        return set_err(DFB_ERR_UNSUPPORTED, "GEMM schedule too large for %d rows", c->cap);
     CK(launch_k(kern, dim3(2 * n_pairs), dim3(kThreads), smem, c->st, !c->prof, w.tm, xm, p));
     // algorithmic work: 2*K MACs per output, weights read once, X read (pair rows, 4 B per
     // value, plus the sub-block sums for Q4_K), Y written (f32, or pair rows for SwiGLU: 4 B
@@ -937,7 +1062,7 @@ static int launch_attn_t(dfb_ctx *c, const float *kc, const float *vc, int n_key
     }
     const float scale_log2 = (1.0f / sqrtf((float)HD)) * 1.4426950408889634f;
     // work-list bound: tiles of <= 32 active rows of one sequence each
-    dim3 grid(c->cap / kAttnRows + std::max(c->n_seg, 1) + 1, m->hp.n_head);
+    dim3 grid(c->cap / kAttnRows + std::max(c->n_seg, 1) + 1, m->n_head_l);  // this rank's heads
     cudaEvent_t ev0 = nullptr;
     prof_begin(c, &ev0);
     CK(launch_k(attn_kernel<HD>, grid, dim3(kAttnThreads), smem, c->st, !c->prof, (const float *)c->q, m->n_q, kc, vc,
@@ -945,7 +1070,19 @@ static int launch_attn_t(dfb_ctx *c, const float *kc, const float *vc, int n_key
                 (const int *)(c->cnt + CNT_NTILES),
                 m->hp.n_head / m->hp.n_head_kv, scale_log2));
     // algorithmic bytes: K and V of every key once (f32), Q in (f32), O out (pair rows)
-    prof_end(c, ev0, DFB_PROF_ATTN, 4.0 * n_keys * m->hp.n_head * HD, 2.0 * 4.0 * n_keys * m->n_kv, 8.0 * m->n_q);
+    prof_end(c, ev0, DFB_PROF_ATTN, 4.0 * n_keys * m->n_head_l * HD, 2.0 * 4.0 * n_keys * m->n_kv, 8.0 * m->n_q);
+    return DFB_OK;
+}
+
+// Tensor parallelism: the O and down projections are row-parallel (each rank holds the input
+// columns of its heads / FFN features), so y holds partial sums; an NCCL all-reduce over the
+// context's rows makes it the whole projection on every rank before the RMSNorm that adds it
+// into the (replicated) residual stream (the split of diffuse-graph.cpp:122-123, 140-142).
+// All rows of the buffer are reduced: the active-row count lives on the device.
+static int tp_sum_rows(dfb_ctx *c) {
+    const dfb_model *m = c->m;
+    if (m->tp_size == 1) return DFB_OK;
+    NK(nccl_api().all_reduce(c->y, c->y, (size_t)c->cap * m->hp.n_embd, ncclFloat32, ncclSum, m->comm, c->st));
     return DFB_OK;
 }
 
@@ -982,20 +1119,22 @@ static int run_forward(dfb_ctx *c, int n_total) {
         EpiArgs eo;  // attention output projection -> y, added to x by the next norm
         eo.out = c->y; eo.ld = d; eo.n_valid = d;
         RET(launch_gemm<EPI_F32>(c, L.o, c->xm_att, eo));
+        RET(tp_sum_rows(c));  // row-parallel O: the ranks' partial sums
         CK(launch_k(rmsnorm_kernel, dim3(cap), dim3(256), 0, c->st, true, c->x, (const float *)c->y,
                     (const float *)L.ffn_norm, d, hp.rms_norm_eps, (const int *)c->cnt, c->h, c->h_s, hs_ld));
         EpiArgs eg;
-        eg.out = c->ffh; eg.ld = 2 * hp.n_ff; eg.n_valid = 2 * hp.n_ff;  // pair rows
-        eg.sums = c->ffh_s; eg.ld_sums = (int)sums_row_bytes(hp.n_ff);
+        eg.out = c->ffh; eg.ld = 2 * m->n_ff_l; eg.n_valid = 2 * m->n_ff_l;  // pair rows
+        eg.sums = c->ffh_s; eg.ld_sums = (int)sums_row_bytes(m->n_ff_l);
         RET(launch_gemm<EPI_SWIGLU>(c, L.gateup, c->xm_h, eg));
         EpiArgs ed;  // FFN down projection -> y, added to x by the next norm
         ed.out = c->y; ed.ld = d; ed.n_valid = d;
         RET(launch_gemm<EPI_F32>(c, L.down, c->xm_ffh, ed));
+        RET(tp_sum_rows(c));  // row-parallel down
     }
     CK(launch_k(rmsnorm_kernel, dim3(cap), dim3(256), 0, c->st, true, c->x, (const float *)(hp.n_layer ? c->y : nullptr),
                 (const float *)m->output_norm, d, hp.rms_norm_eps, (const int *)c->cnt, c->h, c->h_s, hs_ld));
     EpiArgs el;
-    el.out = c->logits; el.ld = hp.n_vocab; el.n_valid = hp.n_vocab; el.pos = c->active_pos;
+    el.out = c->logits; el.ld = m->n_vocab_l; el.n_valid = m->n_vocab_l; el.pos = c->active_pos;
     RET(launch_gemm<EPI_LOGITS>(c, m->lm_head, c->xm_h, el));
     CK(cudaGetLastError());
     return DFB_OK;
@@ -1137,7 +1276,8 @@ extern "C" int dfb_forward(dfb_ctx *c, const int32_t *tokens, int n, float *logi
     CK(cudaMemsetAsync(c->masked, 0, n, c->st));
     RET(prepare_step(c, 1, 0, 0));
     RET(run_forward(c, n));
-    CK(cudaMemcpyAsync(logits_host, c->logits, (size_t)n * V * sizeof(float), cudaMemcpyDeviceToHost, c->st));
+    // (tensor parallelism: this rank's vocabulary columns, n x n_vocab_local)
+    CK(cudaMemcpyAsync(logits_host, c->logits, (size_t)n * c->m->n_vocab_l * sizeof(float), cudaMemcpyDeviceToHost, c->st));
     CK(cudaStreamSynchronize(c->st));
     prof_collect(c, n);
     return check_err(c);
@@ -1146,6 +1286,7 @@ extern "C" int dfb_forward(dfb_ctx *c, const int32_t *tokens, int n, float *logi
 extern "C" int dfb_linear(dfb_ctx *c, int role, int layer, const float *x_host, int M, float *y_host) {
     if (!c || !x_host || !y_host || M <= 0) return set_err(DFB_ERR_ARG, "bad arguments");
     const dfb_model *m = c->m;
+    if (m->tp_size > 1) return set_err(DFB_ERR_UNSUPPORTED, "dfb_linear on a tensor-parallel model");
     std::lock_guard<std::mutex> lk(device_lock(m->device));
     CK(cudaSetDevice(m->device));
     const WMat *w = nullptr;
@@ -1226,6 +1367,8 @@ extern "C" int dfb_gen_begin_batch(dfb_ctx *c, int n_seq, const int32_t *prompts
     if (!c || !p || !prompt_lens || !n_gens || n_seq <= 0) return set_err(DFB_ERR_ARG, "bad arguments");
     if (n_seq > kMaxSeg) return set_err(DFB_ERR_ARG, "%d sequences > %d per context", n_seq, kMaxSeg);
     if (!std::isfinite(p->temperature)) return set_err(DFB_ERR_ARG, "temperature must be finite");
+    if (p->temperature > 0.0f && c->m->tp_size > 1)
+        return set_err(DFB_ERR_UNSUPPORTED, "temperature > 0 sampling on a tensor-parallel model");
     if (p->remasking < 0 || p->remasking > 4) return set_err(DFB_ERR_ARG, "bad remasking %d", p->remasking);
     const dfb_model *m = c->m;
     CK(cudaSetDevice(m->device));
@@ -1322,9 +1465,22 @@ extern "C" int dfb_gen_step_batch(dfb_ctx *c, int step, const int32_t *n_unmask_
     RET(run_forward(c, c->total / S));
     CK(cudaEventRecord(c->ev[1], c->st));
     const int margin = c->sp.remasking == 4 ? 1 : 0;
-    row_stats_kernel<<<masked_all, 512, 0, c->st>>>(c->logits, m->hp.n_vocab, c->masked_row, c->cnt, margin, c->cand_tok,
-                                                    c->cand_conf, c->cand_ent);
-    CK(cudaGetLastError());
+    if (m->tp_size == 1) {
+        row_stats_kernel<<<masked_all, 512, 0, c->st>>>(c->logits, m->hp.n_vocab, c->masked_row, c->cnt, margin, c->cand_tok,
+                                                        c->cand_conf, c->cand_ent);
+        CK(cudaGetLastError());
+    } else {
+        // vocabulary-parallel rows: local statistics, one all-gather, the combination, the
+        // entropy terms over local columns, one all-reduce (every rank then decides the same)
+        tp_stats_kernel<<<masked_all, 512, 0, c->st>>>(c->logits, m->n_vocab_l, m->v0, c->masked_row, c->cnt, c->tp_stats);
+        CK(cudaGetLastError());
+        NK(nccl_api().all_gather(c->tp_stats, c->tp_gath, (size_t)masked_all * 4, ncclFloat32, m->comm, c->st));
+        tp_combine_kernel<<<(masked_all + 255) / 256, 256, 0, c->st>>>(c->tp_gath, m->tp_size, masked_all, c->cnt, margin,
+                                                                      c->cand_tok, c->cand_conf, c->tp_g);
+        tp_entropy_kernel<<<masked_all, 512, 0, c->st>>>(c->logits, m->n_vocab_l, c->masked_row, c->cnt, c->tp_g, c->cand_ent);
+        CK(cudaGetLastError());
+        NK(nccl_api().all_reduce(c->cand_ent, c->cand_ent, (size_t)masked_all, ncclFloat32, ncclSum, m->comm, c->st));
+    }
     if (sampled) {  // draw the candidates' tokens; the entropy stays row_stats'
         sample_kernel<<<masked_all, kSampleThreads, 0, c->st>>>(c->logits, m->hp.n_vocab, c->masked_row, c->cnt,
                                                                  c->sp.temperature, c->unif, c->cand_tok, c->cand_conf);
@@ -1415,7 +1571,7 @@ extern "C" int dfb_gen_commits(dfb_ctx *c, int32_t *pos_host, int32_t *tok_host,
 
 extern "C" int dfb_gen_logits(dfb_ctx *c, int row0, int nrows, float *host) {
     if (!c || !host || row0 < 0 || nrows <= 0 || row0 + nrows > c->cap) return set_err(DFB_ERR_ARG, "bad arguments");
-    const size_t V = c->m->hp.n_vocab;
+    const size_t V = c->m->n_vocab_l;  // (tensor parallelism: this rank's vocabulary columns)
     CK(cudaMemcpyAsync(host, c->logits + (size_t)row0 * V, (size_t)nrows * V * 4, cudaMemcpyDeviceToHost, c->st));
     CK(cudaStreamSynchronize(c->st));
     return DFB_OK;
@@ -1500,7 +1656,7 @@ extern "C" int dfb_linear_noalloc(const dfb_model *m, int role, int layer, const
     NoallocDev nd;
     {
         // first call on this device: resolve the device addresses of the static arrays
-        // (the host-side names are only stand-ins); do it before any stream capture
+        // (the host-side names are only stand-ins)
         std::lock_guard<std::mutex> lock(g_noalloc_mu);
         NoallocDev &d = g_noalloc_dev[m->device];
         if (!d.ws) {

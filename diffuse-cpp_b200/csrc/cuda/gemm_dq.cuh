@@ -213,11 +213,12 @@ struct Sched {
         n_ot = n_ptiles * n_mg;
         U = n_ot * kb;
         G = n_pairs < U ? n_pairs : U;
+        // (unsigned 32-bit products: the launcher keeps (U + 1) * G below 2^32)
         if (M <= 0 || pair >= G) {
             u0 = u1 = 0;
         } else {
-            u0 = (int)((long long)pair * U / G);
-            u1 = (int)((long long)(pair + 1) * U / G);
+            u0 = (int)((unsigned)pair * (unsigned)U / (unsigned)G);
+            u1 = (int)((unsigned)(pair + 1) * (unsigned)U / (unsigned)G);
         }
         bh = ((gsz + 31) & ~31) >> 1;  // 16..128
         if (bh < 16) bh = 16;
@@ -230,8 +231,8 @@ struct Sched {
     // accumulator buffer of segment si and how many segments used it before
     __device__ __forceinline__ int acc_of(int si) const { return dbl ? (si & 1) : 0; }
     __device__ __forceinline__ int acc_uses(int si) const { return dbl ? (si >> 1) : si; }
-    __device__ __forceinline__ int owner(int u) const { return (int)(((long long)(u + 1) * G - 1) / U); }
-    __device__ __forceinline__ int begin_of(int c) const { return (int)((long long)c * U / G); }
+    __device__ __forceinline__ int owner(int u) const { return (int)(((unsigned)(u + 1) * (unsigned)G - 1u) / (unsigned)U); }
+    __device__ __forceinline__ int begin_of(int c) const { return (int)((unsigned)c * (unsigned)U / (unsigned)G); }
 };
 
 struct Seg {
@@ -372,14 +373,25 @@ __device__ __forceinline__ void epi_store(const EpiArgs &e, const EpiRow &r, con
         for (int i = 0; i < 16; i++)
             if (ok && tl0 + i < ntok) *reinterpret_cast<float *>(d.base + row_of(tl0 + i) * d.ld + r.col * 4) = v[i];
     } else if constexpr (EPI == EPI_SWIGLU) {
-        const bool ok = r.writer && d.nbytes > 0;
+        // lanes 2i (gate) and 2i + 1 (up) of feature i split the chunk's tokens: the even
+        // lane takes tokens 0-7, the odd lane 8-15, each after receiving its partner's values
+        // for them.  silu(g) * up = g / (1 + e^-g) * up (ggml_silu, ggml_mul), with the fast
+        // exponential and divide (a few f32 ulp).
+        const bool odd = (threadIdx.x & 1) != 0;
+        const bool ok = d.nbytes > 0;
+        float g[8], up[8];
 #pragma unroll
-        for (int i = 0; i < 16; i++) {
-            const float up = __shfl_xor_sync(0xffffffffu, v[i], 1);
-            const float g = v[i];
-            const float hv = (g / (1.0f + expf(-g))) * up;  // silu(g) * up (ggml_silu, ggml_mul)
-            if (ok && tl0 + i < ntok) {  // pair-layout slice: hi f16, then E4M3 lo 2^10, E4M3 hi
-                char *row = d.base + row_of(tl0 + i) * d.ld;
+        for (int j = 0; j < 8; j++) {
+            const float recv = __shfl_xor_sync(0xffffffffu, odd ? v[j] : v[8 + j], 1);
+            g[j] = odd ? recv : v[j];
+            up[j] = odd ? v[8 + j] : recv;
+        }
+        const int t0 = tl0 + (odd ? 8 : 0);
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const float hv = __fdividef(g[j], 1.0f + __expf(-g[j])) * up[j];
+            if (ok && t0 + j < ntok) {  // pair-layout slice: hi f16, then E4M3 lo 2^10, E4M3 hi
+                char *row = d.base + row_of(t0 + j) * d.ld;
                 const __half hh = __float2half_rn(hv);
                 const float hf = __half2float(hh);
                 reinterpret_cast<__half *>(row)[r.col] = hh;
@@ -387,11 +399,11 @@ __device__ __forceinline__ void epi_store(const EpiArgs &e, const EpiRow &r, con
                 row[128 + r.col] = (char)(c2 & 0xFF);
                 row[192 + r.col] = (char)(c2 >> 8);
             }
-            // this warp's 16 features (even lanes) of the token: partial sub-block sum
+            // the warp's 16 features of the token (lanes of one parity): partial sub-block sum
             float ps = hv;
 #pragma unroll
             for (int off = 2; off < 32; off <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
-            if ((threadIdx.x & 31) == 0) esum[((threadIdx.x >> 5) & 3) * 16 + i] = ps;
+            if ((threadIdx.x & 31) < 2) esum[((threadIdx.x >> 5) & 3) * 16 + (odd ? 8 : 0) + j] = ps;
         }
     } else if constexpr (EPI == EPI_QKV) {
         const bool ok = r.col < 128 && r.col * 4 < d.nbytes;
@@ -495,6 +507,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
     // the next kernel of the stream may be scheduled now; it waits for this grid itself
     griddep_launch_dependents();
+    // The schedule needs only the token count, which is final before any GEMM of a
+    // forward starts (the step-preparation kernel or the host writes it ahead of the
+    // forward's first launch): its load overlaps the setup below.
+    const int M = *reinterpret_cast<volatile const int *>(p.m_dev);
     if (threadIdx.x == 0) {
         for (int i = 0; i < NA; i++) {
             // both CTAs' relays + f16 tiles: the expect_tx / else four dequant warps per CTA
@@ -533,14 +549,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     cluster_sync();  // barriers of both CTAs initialised, TMEM of both allocated
     tc_fence_after();
     const uint32_t tmem_base = *tmem_holder;
-    // The schedule needs only the token count, which is final before any GEMM of a
-    // forward starts (the step-preparation kernel or the host writes it ahead of the
-    // forward's first launch), and the weights do not depend on the previous kernel.  So
-    // the weight producer and the dequantizers start now and fill the pipeline while the
-    // previous kernel finishes; the activation producer and the epilogue wait for it
-    // (griddepcontrol.wait) before they read or write anything it touches, and the MMAs
-    // wait for the activations.
-    const int M = *reinterpret_cast<volatile const int *>(p.m_dev);
+    // The weights do not depend on the previous kernel either.  So the weight producer and
+    // the dequantizers start now and fill the pipeline while the previous kernel finishes;
+    // the activation producer and the epilogue wait for it (griddepcontrol.wait) before they
+    // read or write anything it touches, and the MMAs wait for the activations.
     Sched S;
     S.init(M, p.n_tiles >> 1, p.kb, n_pairs, pair, BRING, XS);
     const int NBS = S.nbs;

@@ -449,6 +449,101 @@ __global__ void __launch_bounds__(1024) select_commit_kernel(int remasking, cons
 }
 
 // X (f32 [rows][K], host-provided for dfb_linear) -> pair rows (4 K bytes each); K multiple of 64.
+// ── tensor parallelism: the sampler statistics of vocabulary-parallel logits rows ──
+// Each rank holds the logits of its vocabulary rows [v0, v0 + n).  Per candidate, rank r
+// computes over its columns the maximum m_r, its first index, the second value s_r and
+// se_r = sum exp(x - m_r) (tp_stats_kernel); after an all-gather every rank combines them
+// (tp_combine_kernel): the maximum over ranks (ties to the lower vocabulary index, i.e. the
+// lower rank), the second value (the largest at any other index), and
+// Z = sum_r se_r exp(m_r - M); the entropy terms with the global max and log Z are then summed
+// over each rank's columns (tp_entropy_kernel) and all-reduced.  The decisions are those of
+// row_stats_kernel over the whole row up to the order of the f32 sums.
+__global__ void __launch_bounds__(512) tp_stats_kernel(const float *__restrict__ logits, int n, int v0,
+                                                        const int *__restrict__ masked_row, const int *__restrict__ cnt,
+                                                        float4 *__restrict__ stats) {
+    __shared__ float red[33];
+    __shared__ Top2 tred[16];
+    const int b = blockIdx.x;
+    if (b >= cnt[CNT_NMASKED]) return;
+    const float *z = logits + (size_t)masked_row[b] * n;
+    Top2 t{-INFINITY, 0x7fffffff, -1e30f};
+    for (int v = threadIdx.x; v < n; v += blockDim.x) {
+        const float x = z[v];
+        if (x > t.best) { t.second = fmaxf(t.second, t.best); t.best = x; t.idx = v; }
+        else t.second = fmaxf(t.second, x);
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        Top2 u;
+        u.best = __shfl_xor_sync(0xffffffffu, t.best, o);
+        u.idx = __shfl_xor_sync(0xffffffffu, t.idx, o);
+        u.second = __shfl_xor_sync(0xffffffffu, t.second, o);
+        t = top2_merge(t, u);
+    }
+    if (lane == 0) tred[warp] = t;
+    __syncthreads();
+    if (warp == 0) {
+        t = lane < (int)(blockDim.x >> 5) ? tred[lane] : Top2{-INFINITY, 0x7fffffff, -1e30f};
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            Top2 u;
+            u.best = __shfl_xor_sync(0xffffffffu, t.best, o);
+            u.idx = __shfl_xor_sync(0xffffffffu, t.idx, o);
+            u.second = __shfl_xor_sync(0xffffffffu, t.second, o);
+            t = top2_merge(t, u);
+        }
+        if (lane == 0) tred[0] = t;
+    }
+    __syncthreads();
+    t = tred[0];
+    float se = 0.f;
+    for (int v = threadIdx.x; v < n; v += blockDim.x) se += expf(z[v] - t.best);
+    se = block_sum(se, red);
+    if (threadIdx.x == 0) stats[b] = make_float4(t.best, t.second, se, __int_as_float(v0 + t.idx));
+}
+// gath: [ranks][candidates] of tp_stats_kernel's values; gstat[b] = (global max, log Z).
+__global__ void tp_combine_kernel(const float4 *__restrict__ gath, int ranks, int stride, const int *__restrict__ cnt,
+                                  int margin, int32_t *__restrict__ cand_tok, float *__restrict__ cand_conf,
+                                  float2 *__restrict__ gstat) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= cnt[CNT_NMASKED]) return;
+    float best = -INFINITY, second = -1e30f;
+    int idx = 0x7fffffff, br = 0;
+    for (int r = 0; r < ranks; r++) {  // ranks in vocabulary order: a tie keeps the lower index
+        const float4 s = gath[(size_t)r * stride + b];
+        if (s.x > best) { second = fmaxf(second, best); best = s.x; idx = __float_as_int(s.w); br = r; }
+        else second = fmaxf(second, s.x);
+        second = fmaxf(second, s.y);
+    }
+    (void)br;
+    float Z = 0.f;
+    for (int r = 0; r < ranks; r++) {
+        const float4 s = gath[(size_t)r * stride + b];
+        Z += s.z * expf(s.x - best);
+    }
+    cand_tok[b] = idx;
+    cand_conf[b] = margin ? (best - second) : best;
+    gstat[b] = make_float2(best, logf(Z));
+}
+__global__ void __launch_bounds__(512) tp_entropy_kernel(const float *__restrict__ logits, int n,
+                                                          const int *__restrict__ masked_row, const int *__restrict__ cnt,
+                                                          const float2 *__restrict__ gstat, float *__restrict__ ent_part) {
+    __shared__ float red[33];
+    const int b = blockIdx.x;
+    if (b >= cnt[CNT_NMASKED]) return;
+    const float *z = logits + (size_t)masked_row[b] * n;
+    const float mx = gstat[b].x, log_sum = gstat[b].y;
+    float ent = 0.f;
+    for (int v = threadIdx.x; v < n; v += blockDim.x) {
+        const float lp = (z[v] - mx) - log_sum;
+        const float p = expf(lp);
+        if (p > 1e-10f) ent -= p * lp;
+    }
+    ent = block_sum(ent, red);
+    if (threadIdx.x == 0) ent_part[b] = ent;
+}
+
 // Sampling at temperature > 0 (diffuse-sampler.cpp:256-269): probabilities
 // p_v = expf((l_v - max) / T) / sum_v expf(...) in f32, then the draw of
 // std::discrete_distribution<int>(p) with the uniform u the host took from the loop's

@@ -65,12 +65,21 @@ constexpr uint64_t kWaitTimeoutNs = 4000000000ull;  // 4 s
 #define DFB_WAIT_HINT_NS 200000
 #endif
 constexpr uint32_t kSuspendHintNs = DFB_WAIT_HINT_NS;  // per try_wait, then re-check the flags
+// The abort flag, the global error code and the time limit are checked every
+// kWaitCheckNs only: a woken waiter whose phase is not complete yet goes straight back to
+// sleep instead of loading them (they take issue slots and global loads from the busy
+// warps of its scheduler); an abort then reaches the other waits within that period.
+constexpr uint64_t kWaitCheckNs = 20000;
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
                                           int *err, int code, uint64_t timeout_ns = kWaitTimeoutNs) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
+    uint64_t checked = t0;
     for (;;) {
         if (mbar_try_wait_sleep(bar, parity, kSuspendHintNs)) return true;
+        const uint64_t now = globaltimer();
+        if (now - checked < kWaitCheckNs) continue;
+        checked = now;
         if (*abort_flag) return false;
         if (*reinterpret_cast<volatile int *>(err)) {
             *abort_flag = 1;
@@ -117,8 +126,13 @@ __device__ __forceinline__ int ld_acquire_gpu(const int *p) {
 __device__ __forceinline__ bool wait_count(const int *c, int target, volatile int *abort_flag, int *err, int code,
                                            uint64_t timeout_ns = kWaitTimeoutNs) {
     const uint64_t t0 = globaltimer();
+    uint64_t checked = t0;
     for (;;) {
         if (ld_acquire_gpu(c) >= target) return true;
+        __nanosleep(32);
+        const uint64_t now = globaltimer();
+        if (now - checked < kWaitCheckNs) continue;  // flags and limit every kWaitCheckNs, as mbar_wait
+        checked = now;
         if (*abort_flag) return false;
         if (*reinterpret_cast<volatile int *>(err)) {
             *abort_flag = 1;
@@ -129,7 +143,6 @@ __device__ __forceinline__ bool wait_count(const int *c, int target, volatile in
             atomicCAS(err, 0, code);
             return false;
         }
-        __nanosleep(32);
     }
 }
 // Make generic-proxy shared-memory writes visible to the async proxy (tensor core).

@@ -76,7 +76,13 @@ struct diffuse_context {
 };
 
 // Loads a GGUF and uploads it; returns nullptr with the error recorded.
-static diffuse_model *load_model(const std::string &path) {
+// tp: tensor-parallel rank / size and the NCCL id every rank of the group shares (size 1: whole model)
+struct TpSpec {
+    int rank = 0, size = 1;
+    const uint8_t *id = nullptr;
+    int id_bytes = 0;
+};
+static diffuse_model *load_model(const std::string &path, const TpSpec &tp = TpSpec{}) {
     DIFFUSE_LOG("loading model from %s", path.c_str());
     GgufReader g;
     std::string err;
@@ -166,6 +172,12 @@ static diffuse_model *load_model(const std::string &path) {
     if (const char *e = getenv("DIFFUSE_DEVICE")) device = atoi(e);
     if (dfb_model_create(&dh, device, &m->dm) != DFB_OK) {
         set_error(DFB_ERR_CUDA, "%s", dfb_last_error());
+        delete m;
+        return nullptr;
+    }
+    if (tp.size > 1 && dfb_model_set_tp(m->dm, tp.rank, tp.size, tp.id, tp.id_bytes) != DFB_OK) {
+        set_error(DFB_ERR_ARG, "%s", dfb_last_error());
+        dfb_model_free(m->dm);
         delete m;
         return nullptr;
     }
@@ -405,6 +417,12 @@ void *dfc_model_load(const char *path, int n_threads) {
     if (!path) { set_error(DFB_ERR_ARG, "null path"); return nullptr; }
     return load_model(path);
 }
+void *dfc_model_load_tp(const char *path, int rank, int size, const uint8_t *nccl_id, int id_bytes) {
+    if (!path) { set_error(DFB_ERR_ARG, "null path"); return nullptr; }
+    TpSpec tp;
+    tp.rank = rank; tp.size = size; tp.id = nccl_id; tp.id_bytes = id_bytes;
+    return load_model(path, tp);
+}
 void dfc_model_free(void *model) { diffuse_model_free((diffuse_model *)model); }
 
 int dfc_model_hparams(const void *model, int32_t *i9, float *f2) {
@@ -415,6 +433,11 @@ int dfc_model_hparams(const void *model, int32_t *i9, float *f2) {
     i9[5] = hp.n_ff; i9[6] = hp.n_ctx_max; i9[7] = hp.mask_token_id; i9[8] = m->model_type == "dream";
     f2[0] = hp.rope_theta; f2[1] = hp.rms_norm_eps;
     return DFB_OK;
+}
+
+int dfc_model_tp_info(const void *model, int32_t *rank, int32_t *size, int32_t *v0, int32_t *n_vocab_local) {
+    if (!model) return set_error(DFB_ERR_ARG, "null model");
+    return dfb_model_tp_info(((const diffuse_model *)model)->dm, rank, size, v0, n_vocab_local);
 }
 
 void *dfc_context_new(void *model, int n_ctx, int n_threads) {

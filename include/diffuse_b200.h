@@ -115,6 +115,21 @@ int dfb_linear(dfb_ctx *c, int role, int layer, const float *x_host, int M, floa
 int dfb_debug_stalled_linear(dfb_ctx *c, int role, int layer, const float *x_host, int M, float *y_host,
                              unsigned long long timeout_ns);
 
+/* ── tensor parallelism (the north-star's optional TP mode; no counterpart in the reference) ──
+ * Rank r of size holds heads [r H/size, (r+1) H/size) of Q/K/V/O (and their KV heads), FFN
+ * features [r F/size, ...) of gate/up/down and vocabulary rows [v0, v0 + n_vocab_local) of the
+ * lm_head.  O and down are row-parallel: an NCCL all-reduce of their outputs follows each (the
+ * split of the residual adds, diffuse-graph.cpp:122-123, 140-142).  The sampler's per-candidate
+ * statistics are combined with one all-gather and the entropy with one all-reduce, so every
+ * rank makes the same decisions.  temperature > 0 and dfb_linear are not supported in this
+ * mode.  NCCL is bound at run time (libnccl.so.2). */
+/* A fresh NCCL unique id (nbytes >= 128) for one rank to share with the others. */
+int dfb_tp_unique_id(uint8_t *id, int nbytes);
+/* Before dfb_model_finalize; every rank calls it at the same time (NCCL communicator setup). */
+int dfb_model_set_tp(dfb_model *m, int rank, int size, const uint8_t *id, int nbytes);
+/* This rank's place: rank, size, first vocabulary row and vocabulary rows held. */
+int dfb_model_tp_info(const dfb_model *m, int *rank, int *size, int *v0, int *n_vocab_local);
+
 /* ── generation: the device side of diffuse_sample (diffuse-sampler.cpp:60-370) ── */
 /* Set up seq = prompt ‖ MASK × n_gen, masks, cache and logits buffer on the device. */
 int dfb_gen_begin(dfb_ctx *c, const int32_t *prompt, int n_prompt, int n_gen, const dfb_sampler_params *p);
@@ -184,7 +199,7 @@ int dfb_ctx_profile_read(dfb_ctx *c, dfb_prof_entry *out, int n);      /* n <= D
  * library, held by every GPU that loads it until exit; M above 256 or a weight of more
  * than 2040 row tiles is rejected with DFB_ERR_ARG.  Nothing is allocated: no
  * cudaMalloc / cudaFree, no allocating library call.  The first call on a device looks
- * up the scratch address (make it before any stream capture).  All calls share the
+ * up the scratch address.  All calls share the
  * scratch, so calls that overlap on the GPU race; the call synchronizes `stream`
  * (cudaStream_t as void*, NULL = legacy default stream) before returning. */
 int dfb_linear_noalloc(const dfb_model *m, int role, int layer, const void *x_f16_dev, int M, float *y_dev,

@@ -23,6 +23,14 @@ extern "C" {
 const char *dfc_last_error(void);
 
 void *dfc_model_load(const char *path, int n_threads);                /* diffuse_model* or NULL */
+/* Tensor-parallel rank `rank` of `size` (no counterpart in the reference): the model's heads,
+ * FFN features and vocabulary rows are split over the ranks, one process and GPU each
+ * (DIFFUSE_DEVICE selects the device); every rank passes the same NCCL id (dfb_tp_unique_id on
+ * one rank, shared by the caller) and loads at the same time.  Logits buffers then hold the
+ * rank's vocabulary columns (dfb_model_tp_info). */
+void *dfc_model_load_tp(const char *path, int rank, int size, const uint8_t *nccl_id, int id_bytes);
+/* The loaded model's tensor-parallel place (dfb_model_tp_info). */
+int dfc_model_tp_info(const void *model, int32_t *rank, int32_t *size, int32_t *v0, int32_t *n_vocab_local);
 void  dfc_model_free(void *model);
 /* ints: n_vocab n_embd n_head n_head_kv n_layer n_ff n_ctx_max mask_token_id is_dream
  * floats: rope_theta rms_norm_eps */
