@@ -162,13 +162,21 @@ __device__ __forceinline__ void q4x_load_meta(const uint8_t *R, int r, int set, 
         m.c[l] = dmin * (float)mn;
     }
 }
-// Half h of slice s of row r (one sub-block, scale sc): f16 hi and the e4m3 correction
-// pair (hi 2^-10, lo), the HalfCorr layout.
-__device__ __forceinline__ void q4x_half(const uint8_t *R, int r, int s, int h, uint32_t sc, __half2 d2, HalfCorr &o) {
+// The quant words of one half slice (the dequantizers load the next half's while they
+// wait for the current one's stage): Q4_K / Q8_0 two 16-byte chunks, Q6_K four.
+struct HalfWords {
+    uint4 a, b, c, d;
+};
+// Q4_K: qs bytes 32 s .. 32 s + 31 of row r (both halves of slice s; the half picks nibbles).
+__device__ __forceinline__ void q4x_load(const uint8_t *R, int r, int s, HalfWords &q) {
     const uint8_t *qrow = R + 2048 + 128 * r;
-    const uint4 qa = *reinterpret_cast<const uint4 *>(qrow + (((2 * s) ^ (r & 7)) << 4));
-    const uint4 qc = *reinterpret_cast<const uint4 *>(qrow + (((2 * s + 1) ^ (r & 7)) << 4));
-    const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qc.x, qc.y, qc.z, qc.w};
+    q.a = *reinterpret_cast<const uint4 *>(qrow + (((2 * s) ^ (r & 7)) << 4));
+    q.b = *reinterpret_cast<const uint4 *>(qrow + (((2 * s + 1) ^ (r & 7)) << 4));
+}
+// Half h of a slice whose words q holds (one sub-block, scale sc): f16 hi and the e4m3
+// correction pair (hi 2^-10, lo), the HalfCorr layout.
+__device__ __forceinline__ void q4x_half(const HalfWords &q, int h, uint32_t sc, __half2 d2, HalfCorr &o) {
+    const uint32_t w[8] = {q.a.x, q.a.y, q.a.z, q.a.w, q.b.x, q.b.y, q.b.z, q.b.w};
     const __half2 off = __floats2half2_rn(-1024.f, -1024.f);
     const __half2 k10 = __floats2half2_rn(kCorrScale, kCorrScale);
 #pragma unroll
@@ -306,16 +314,20 @@ __device__ __forceinline__ void q6x_load_meta(const uint8_t *R, int r, int set, 
         m.dsl[i] = __half2half2(__float2half_rn(f.ds[i] - __half2float(h)));
     }
 }
-__device__ __forceinline__ void q6x_half(const uint8_t *R, int r, int s, int hh, __half2 dsh0, __half2 dsl0, __half2 dsh1,
-                                         __half2 dsl1, HalfCorr &o) {
-    const int h = s >> 1, s2 = s & 1;
+// Q6_K: half hh of slice s: ql bytes 64 (s / 2) + 32 hh .. +31 and qh bytes 32 (s / 2) .. +31.
+__device__ __forceinline__ void q6x_load(const uint8_t *R, int r, int s, int hh, HalfWords &q) {
+    const int h = s >> 1;
     const uint8_t *qlrow = R + 128 * r, *qhrow = R + 16384 + 64 * r;
-    const uint4 l0 = *reinterpret_cast<const uint4 *>(qlrow + (((4 * h + 2 * hh) ^ (r & 7)) << 4));
-    const uint4 l1 = *reinterpret_cast<const uint4 *>(qlrow + (((4 * h + 2 * hh + 1) ^ (r & 7)) << 4));
-    const uint4 g0 = *reinterpret_cast<const uint4 *>(qhrow + (((2 * h) ^ ((r >> 1) & 3)) << 4));
-    const uint4 g1 = *reinterpret_cast<const uint4 *>(qhrow + (((2 * h + 1) ^ ((r >> 1) & 3)) << 4));
-    const uint32_t lw[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
-    const uint32_t qw[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+    q.a = *reinterpret_cast<const uint4 *>(qlrow + (((4 * h + 2 * hh) ^ (r & 7)) << 4));
+    q.b = *reinterpret_cast<const uint4 *>(qlrow + (((4 * h + 2 * hh + 1) ^ (r & 7)) << 4));
+    q.c = *reinterpret_cast<const uint4 *>(qhrow + (((2 * h) ^ ((r >> 1) & 3)) << 4));
+    q.d = *reinterpret_cast<const uint4 *>(qhrow + (((2 * h + 1) ^ ((r >> 1) & 3)) << 4));
+}
+__device__ __forceinline__ void q6x_half(const HalfWords &q, int s, int hh, __half2 dsh0, __half2 dsl0, __half2 dsh1,
+                                         __half2 dsl1, HalfCorr &o) {
+    const int s2 = s & 1;
+    const uint32_t lw[8] = {q.a.x, q.a.y, q.a.z, q.a.w, q.b.x, q.b.y, q.b.z, q.b.w};
+    const uint32_t qw[8] = {q.c.x, q.c.y, q.c.z, q.c.w, q.d.x, q.d.y, q.d.z, q.d.w};
     const int shift = 4 * s2 + 2 * hh;
     const __half2 off = __floats2half2_rn(-1056.f, -1056.f);  // 1024 + 32
 #pragma unroll
@@ -330,19 +342,24 @@ __device__ __forceinline__ void q6x_half(const uint8_t *R, int r, int s, int hh,
         });
     }
 }
-// Q8_0: half h of slice s is block 2s + h with scale ws d (exact in f16).
-__device__ __forceinline__ void q8x_half(const uint8_t *R, int r, int s, int h, float ws, HalfCorr &o) {
+// Q8_0: half h of slice s is block 2s + h: its 32 quants (two 16-byte chunks) and, in c.x,
+// the block's f16 scale.
+__device__ __forceinline__ void q8x_load(const uint8_t *R, int r, int s, int h, HalfWords &q) {
     const int blk = 2 * s + h;
-    const uint4 dv = *reinterpret_cast<const uint4 *>(R + 16 * r);
-    const int wi = blk >> 1;
-    const uint32_t dwd = wi == 0 ? dv.x : wi == 1 ? dv.y : wi == 2 ? dv.z : dv.w;
-    const __half2 d2 = __float2half2_rn(__half2float(__ushort_as_half((unsigned short)((dwd >> (16 * (blk & 1))) & 0xFFFF))) * ws);
     const uint8_t *qrow = R + 2048 + 256 * r;
+    const int c0 = 2 * blk, c1 = 2 * blk + 1;
+    q.a = *reinterpret_cast<const uint4 *>(qrow + (((c0 & 8) | ((c0 & 7) ^ (r & 7))) << 4));
+    q.b = *reinterpret_cast<const uint4 *>(qrow + (((c1 & 8) | ((c1 & 7) ^ (r & 7))) << 4));
+    const uint16_t dh = *reinterpret_cast<const uint16_t *>(R + 16 * r + 2 * blk);
+    q.c = make_uint4(dh, 0, 0, 0);
+}
+// Q8_0 with scale ws d (exact in f16).
+__device__ __forceinline__ void q8x_half(const HalfWords &q, float ws, HalfCorr &o) {
+    const __half2 d2 = __float2half2_rn(__half2float(__ushort_as_half((unsigned short)q.c.x)) * ws);
     const __half2 off = __floats2half2_rn(-1152.f, -1152.f);  // 1024 + 128
 #pragma unroll
     for (int cc = 0; cc < 2; cc++) {
-        const int c = 2 * blk + cc;
-        const uint4 v = *reinterpret_cast<const uint4 *>(qrow + (((c & 8) | ((c & 7) ^ (r & 7))) << 4));
+        const uint4 v = cc ? q.b : q.a;
         const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
         for (int i = 0; i < 4; i++)

@@ -162,16 +162,20 @@ __host__ __device__ constexpr int a_stage_bytes(int wt, int xs) {
     return (xs == 2 || wt == W_F32) ? 2 * kSliceBytes : kSliceBytes;
 }
 __host__ __device__ constexpr int a_ring_bytes(int wt, int xs) { return w_smem(wt) ? kNA * a_stage_bytes(wt, xs) : 0; }
-__host__ __device__ constexpr int b_ring_bytes(int wt) { return 96 * 1024; }
+// The activation stream dominates the shared-memory traffic (4 bytes per value, re-read for
+// every 256-row weight tile: at 256 tokens 32 KB per k-slice and CTA against 4.6 KB of Q4_K
+// weights); a slot returns only after its load's latency and its slice's MMA, so the ring's
+// depth sets the k-slice rate: 128 KB (4 slots of the widest group).
+__host__ __device__ constexpr int b_ring_bytes(int wt) { return 128 * 1024; }
 // Sub-block sums ring (min operand's B side): two slots of one k-block's sums for up to 128
 // rows (64 bytes each, 64-byte swizzle).
 constexpr int kMinSlots = 2, kMinSlotBytes = 128 * 64;
 __host__ __device__ constexpr int min_ring_bytes(int wt, int xs) { return w_min(wt, xs) ? kMinSlots * kMinSlotBytes : 0; }
-// A raw stage holds raw_cpr consecutive chunks of the CTA's unit range: the weight
-// stream reached ~3.8 TB/s with 18 KB stages and ~6-7 TB/s with 36-72 KB stages
-// (same bytes in flight), so small chunks are grouped.
-__host__ __device__ constexpr int raw_stages(int wt) { return wt == W_Q4K ? 3 : wt == W_Q6K ? 4 : wt == W_Q80 ? 3 : 0; }
-__host__ __device__ constexpr int raw_cpr(int wt) { return wt == W_Q4K ? 2 : 1; }
+// A raw stage holds raw_cpr consecutive chunks of the CTA's unit range; stages are sized so
+// that, with the activation ring, shared memory holds 3-4 k-blocks of weights in flight
+// (several microseconds of dequantization at any token count, above the HBM latency).
+__host__ __device__ constexpr int raw_stages(int wt) { return wt == W_Q4K ? 4 : wt == W_Q6K ? 3 : wt == W_Q80 ? 2 : 0; }
+__host__ __device__ constexpr int raw_cpr(int wt) { return 1; }
 
 // Warp roles.  A warp runs on scheduler warp % 4 and may only access TMEM lanes
 // 32*(warp % 4)..+31, so the dequantizers (they write A into TMEM) and the epilogue cover
@@ -474,6 +478,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     constexpr int ASB = a_stage_bytes(WT, XS);
     constexpr int CPR = raw_cpr(WT), RSB = CPR * RAWB;  // chunks and bytes per raw stage
     constexpr bool MIN = w_min(WT, XS);
+    static_assert(gemm_smem_bytes(WT, XS) <= 227 * 1024, "shared memory per CTA");
     static_assert(XS == 1 || XS == 2, "activation parts");
     static_assert(!MIN || (AR + BRING + NRAW * RSB) % 1024 == 0, "sums ring alignment (64-byte swizzle)");
     constexpr int UPS = a_units(WT);  // A units per k-slice
@@ -859,14 +864,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     else if constexpr (WT == W_Q4K) q4k_load_meta(R, r, set, p.wscale, m4);
                     if constexpr (WT == W_Q6K && XS == 2) q6x_load_meta(R, r, set, p.wscale, m6x);
                     else if constexpr (WT == W_Q6K) q6k_load_meta(R, r, set, p.wscale, m6);
-                    // XS = 2: f16 arithmetic (dequant.cuh); XS = 1: f32
-                    auto deq = [&](int hs, int hh, Half &o) {
+                    // XS = 2: f16 arithmetic (dequant.cuh) on quant words loaded one half slice
+                    // ahead (load_words before the wait for the current half's stage, so the
+                    // shared-memory latency hides behind it); XS = 1: f32, loading as it goes.
+                    auto load_words = [&](int hs, int hh, HalfWords &q) {
                         const int sl = set + 2 * hs;
-                        if constexpr (MIN) q4x_half(R, r, sl, hh, mx.sc[2 * hs + hh], mx.d2, o);
+                        if constexpr (MIN) q4x_load(R, r, sl, q);  // both halves of the slice
+                        else if constexpr (WT == W_Q6K && XS == 2) q6x_load(R, r, sl, hh, q);
+                        else if constexpr (WT == W_Q80 && XS == 2) q8x_load(R, r, sl, hh, q);
+                    };
+                    auto deq = [&](int hs, int hh, const HalfWords &q, Half &o) {
+                        const int sl = set + 2 * hs;
+                        if constexpr (MIN) q4x_half(q, hh, mx.sc[2 * hs + hh], mx.d2, o);
                         else if constexpr (WT == W_Q6K && XS == 2)
-                            q6x_half(R, r, sl, hh, m6x.dsh[4 * hs + 2 * hh], m6x.dsl[4 * hs + 2 * hh], m6x.dsh[4 * hs + 2 * hh + 1],
+                            q6x_half(q, sl, hh, m6x.dsh[4 * hs + 2 * hh], m6x.dsl[4 * hs + 2 * hh], m6x.dsh[4 * hs + 2 * hh + 1],
                                      m6x.dsl[4 * hs + 2 * hh + 1], o);
-                        else if constexpr (WT == W_Q80 && XS == 2) q8x_half(R, r, sl, hh, p.wscale, o);
+                        else if constexpr (WT == W_Q80 && XS == 2) q8x_half(q, p.wscale, o);
                         else if constexpr (WT == W_Q4K) q4k_half(R, r, sl, hh, m4.dsc[2 * hs + hh], m4.nm[2 * hs + hh], o);
                         else if constexpr (WT == W_Q6K)
                             q6k_half(R, r, sl, hh, m6.ds[4 * hs + 2 * hh], m6.ds[4 * hs + 2 * hh + 1], o);
@@ -881,14 +894,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                             tmem_st16(at + 16, o.lo);
                         }
                     };
+                    HalfWords qw{}, qn{};
+                    load_words(0, 0, qw);
 #pragma unroll
                     for (int hs = 0; hs < 2; hs++) {
                         const int use = 2 * rit + hs;  // this set's slices so far
 #pragma unroll
                         for (int hh = 0; hh < 2; hh++) {
                             const int st = 2 * set + hh;
+                            const int un = 2 * hs + hh + 1;  // next unit (Q4_K: a slice's words serve both halves)
+                            if (un < 4 && !(MIN && (un & 1))) load_words(un >> 1, un & 1, qn);
                             Half o;
-                            deq(hs, hh, o);
+                            deq(hs, hh, qw, o);
+                            if (un < 4 && !(MIN && (un & 1))) qw = qn;
                             // the MMA of this stage's previous half slice has completed
                             if (!(ok = wait_warp(&empty_a[st], (use & 1) ^ 1, kErrTimeout + 7))) break;
                             tc_fence_after();
