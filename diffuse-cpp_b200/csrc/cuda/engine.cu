@@ -1086,6 +1086,17 @@ static int tp_sum_rows(dfb_ctx *c) {
     return DFB_OK;
 }
 
+// The value checks of the forward and the sampler (cnt[CNT_ERR]): a token id outside the
+// vocabulary reached the embedding (1), or a logits row had no finite maximum (2).  Reported
+// once and cleared; the kernels read a valid row instead, so nothing faults.
+static int check_values(dfb_ctx *c, int code) {
+    if (!code) return DFB_OK;
+    CK(cudaMemsetAsync(c->cnt + CNT_ERR, 0, sizeof(int), c->st));
+    CK(cudaStreamSynchronize(c->st));
+    return set_err(DFB_ERR_STATE, code == 1 ? "a token id outside the vocabulary reached the embedding"
+                                            : "a logits row has no finite maximum (non-finite logits)");
+}
+
 // The forward of one step over the active rows listed by step_prepare.
 static int run_forward(dfb_ctx *c, int n_total) {
     const dfb_model *m = c->m;
@@ -1093,9 +1104,9 @@ static int run_forward(dfb_ctx *c, int n_total) {
     const int d = hp.n_embd, cap = c->cap;
     const int hs_ld = (int)sums_row_bytes(d);
     if (m->embd_f16)
-        embed_kernel<__half><<<cap, 256, 0, c->st>>>((const __half *)m->embd, d, c->seq, c->active_pos, c->cnt, c->x);
+        embed_kernel<__half><<<cap, 256, 0, c->st>>>((const __half *)m->embd, d, hp.n_vocab, c->seq, c->active_pos, c->cnt, c->x);
     else
-        embed_kernel<float><<<cap, 256, 0, c->st>>>((const float *)m->embd, d, c->seq, c->active_pos, c->cnt, c->x);
+        embed_kernel<float><<<cap, 256, 0, c->st>>>((const float *)m->embd, d, hp.n_vocab, c->seq, c->active_pos, c->cnt, c->x);
     CK(cudaGetLastError());
     for (int l = 0; l < hp.n_layer; l++) {
         const LayerW &L = m->layers[l];
@@ -1278,7 +1289,10 @@ extern "C" int dfb_forward(dfb_ctx *c, const int32_t *tokens, int n, float *logi
     RET(run_forward(c, n));
     // (tensor parallelism: this rank's vocabulary columns, n x n_vocab_local)
     CK(cudaMemcpyAsync(logits_host, c->logits, (size_t)n * c->m->n_vocab_l * sizeof(float), cudaMemcpyDeviceToHost, c->st));
+    int verr = 0;
+    CK(cudaMemcpyAsync(&verr, c->cnt + CNT_ERR, sizeof(int), cudaMemcpyDeviceToHost, c->st));
     CK(cudaStreamSynchronize(c->st));
+    RET(check_values(c, verr));
     prof_collect(c, n);
     return check_err(c);
 }
@@ -1503,6 +1517,7 @@ extern "C" int dfb_gen_step_batch(dfb_ctx *c, int step, const int32_t *n_unmask_
     CK(cudaStreamSynchronize(c->st));
     prof_collect(c, h_cnt[CNT_M]);
     RET(check_err(c));
+    RET(check_values(c, h_cnt[CNT_ERR]));
     float fwd = 0, all = 0;
     cudaEventElapsedTime(&fwd, c->ev[0], c->ev[1]);
     cudaEventElapsedTime(&all, c->ev[0], c->ev[2]);

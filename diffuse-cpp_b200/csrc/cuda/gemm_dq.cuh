@@ -122,18 +122,21 @@ constexpr int kEpiThreads = 256;         // two epilogue warps per TMEM lane qua
 constexpr int kDeqWarps = 8;             // two sets of four: even / odd k-slices
 constexpr int kSliceBytes = 128 * 128;   // one 64-wide k-slice of this CTA's 128 weight rows (f16)
 constexpr int kMaxTok = 256;             // tokens per MMA group (N) of the pair
-constexpr int kDblTok = 176;             // groups up to this size double-buffer the accumulator
+constexpr int kDblTok = 160;             // groups up to this size double-buffer the accumulator
+// (an MMA's N is the group rounded up to 32, two halves of 16-row multiples: the limit is a
+// multiple of 32 so a double-buffered accumulator never reaches the next one or the A stages)
+static_assert(kDblTok % 32 == 0, "double-buffered accumulator width");
 constexpr int kWsTile = kMaxTok * 128;   // floats per partial tile (one CTA's 128 rows)
 constexpr int kErrTimeout = 0x100;
 constexpr int kMaxAStages = 6, kMaxBSlots = 24, kMaxRawStages = 4;
-// TMEM (512 columns per CTA): accumulators [0, 176) and [176, 352) for token groups of up
-// to 176, one accumulator [0, 256) for larger groups (the MMA of the next segment then
+// TMEM (512 columns per CTA): accumulators [0, 160) and [160, 320) for token groups of up
+// to 160, one accumulator [0, 256) for larger groups (the MMA of the next segment then
 // waits for the epilogue to drain it, which costs less than dequantizing the weights once
-// per group of 128); dequantized A stages (quantized weights) at [352 + 32 st, +32), four
+// per group of 128); dequantized A stages (quantized weights) at [320 + 32 st, +32), four
 // stages of half a k-slice (32 k) each, dequantizer set p filling stages 2p (first half of
 // its slices) and 2p + 1 (second half): lane = weight row, f16 hi in the first 16 columns,
 // then the E4M3 correction pair (8 columns W_hi 2^-10, 8 columns W_lo), or f16 lo for
-// XS = 1; the Q4_K min operand of the current k-block at [480, 496) (8 columns per set).
+// XS = 1; the Q4_K min operand of the current k-block at [448, 464) (8 columns per set).
 // Half-slice stages let a set store the first half of its next slice as soon as the MMA
 // of the first half of its previous one is done, so what remains after each wait is a
 // store, not a dequantization.

@@ -145,11 +145,15 @@ __global__ void __launch_bounds__(1024) seg_compact_kernel(int n_seg, const int 
 
 // x[a] = token_embd[seq[active_pos[a]]] as f32 (ggml_get_rows, graph.cpp:43/433).
 template <typename T>
-__global__ void embed_kernel(const T *__restrict__ emb, int d, const int32_t *__restrict__ seq,
-                             const int *__restrict__ active_pos, const int *__restrict__ cnt, float *__restrict__ x) {
+__global__ void embed_kernel(const T *__restrict__ emb, int d, int n_vocab, const int32_t *__restrict__ seq,
+                             const int *__restrict__ active_pos, int *__restrict__ cnt, float *__restrict__ x) {
     const int a = blockIdx.x;
     if (a >= cnt[CNT_M]) return;
-    const int tok = seq[active_pos[a]];
+    int tok = seq[active_pos[a]];
+    if (tok < 0 || tok >= n_vocab) {  // a token id outside the vocabulary: report it, read row 0
+        if (threadIdx.x == 0) atomicCAS(&cnt[CNT_ERR], 0, 1);
+        tok = 0;
+    }
     const T *src = emb + (size_t)tok * d;
     float *dst = x + (size_t)a * d;
     for (int i = threadIdx.x; i < d; i += blockDim.x) {
@@ -248,7 +252,7 @@ __device__ __forceinline__ Top2 top2_merge(Top2 a, Top2 b) {
 }
 
 __global__ void __launch_bounds__(512) row_stats_kernel(const float *__restrict__ logits, int n_vocab,
-                                                         const int *__restrict__ masked_row, const int *__restrict__ cnt,
+                                                         const int *__restrict__ masked_row, int *__restrict__ cnt,
                                                          int margin, int32_t *__restrict__ cand_tok,
                                                          float *__restrict__ cand_conf, float *__restrict__ cand_ent) {
     __shared__ float red[33];
@@ -356,6 +360,10 @@ __global__ void __launch_bounds__(512) row_stats_kernel(const float *__restrict_
     }
     ent = block_sum(ent, red);
     if (threadIdx.x == 0) {
+        if (t.idx < 0 || t.idx >= n_vocab) {  // no value compared greater than -inf (NaN logits): report it
+            atomicCAS(&cnt[CNT_ERR], 0, 2);
+            t.idx = 0;
+        }
         cand_tok[b] = t.idx;
         cand_conf[b] = margin ? (t.best - t.second) : t.best;
         cand_ent[b] = ent;

@@ -59,7 +59,7 @@ def dequantized(orc, om, tname):
 
 
 @pytest.mark.parametrize("case", GEMM_CASES, ids=lambda c: f"{c[0]}-{c[3]}")
-@pytest.mark.parametrize("M", [1, 17, 64, 200, 320, 600])
+@pytest.mark.parametrize("M", [1, 17, 64, 150, 162, 200, 320, 600])
 def test_gemm_parity(pkg, orc, models, case, M):
     """One linear layer against the exact product (f64 on the dequantized weights), within
     GEMM_MEANREL mean relative error; the oracle's f32 GEMM is reported beside it."""
