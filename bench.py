@@ -264,7 +264,8 @@ def run_reference(args, cfg):
 
 
 def layer_probe(args):
-    """Small profiling case (a few hundred MB on the device): one layer of LLaDA-8B width,
+    """Small profiling case (a few hundred MB on the device): one layer of LLaDA-8B width
+    (Dream-7B width with --probe-arch dream: GQA 28 / 4),
     `--warmup` untimed forwards, then `--steps` forwards with the engine's per-launch
     CUDA-event profiler on; prints calls, average launch time, TFLOP/s and algorithmic
     GB/s per kernel class.  Launch order of one forward: embed, norm, QKV GEMM, attention,
@@ -274,10 +275,11 @@ def layer_probe(args):
     os.environ.setdefault("DIFFUSE_LOG_LEVEL", "0")
     work = pathlib.Path(os.environ.get("DFB_BENCH_DIR", tempfile.gettempdir())) / "dfb_bench"
     work.mkdir(parents=True, exist_ok=True)
-    path = work / "llada_q4_k_m_1layer_v16384.gguf"
+    arch = pkg.DREAM_7B if args.probe_arch == "dream" else pkg.LLADA_8B
+    path = work / f"{args.probe_arch}_q4_k_m_1layer_v16384.gguf"
     if not path.exists():
         tmp = path.with_suffix(".tmp")
-        pkg.synth_model(tmp, pkg.LLADA_8B, "q4_k_m", seed=0, n_layer=1, n_vocab=16384)
+        pkg.synth_model(tmp, arch, "q4_k_m", seed=0, n_layer=1, n_vocab=16384)
         tmp.rename(path)
     model = pkg.Model(str(path))
     M = args.layer_probe
@@ -334,6 +336,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--probe-arch", default="llada", choices=["llada", "dream"])
     ap.add_argument("--layer-probe", type=int, default=0, metavar="ROWS",
                     help="profiling case instead of the benchmark: forwards of ROWS tokens through one "
                          "LLaDA-8B-width Q4_K_M layer (vocab 16384), per-kernel-class CUDA-event timings")
