@@ -15,10 +15,6 @@
 // round Q, K, P and V to 11 bits, which over 32 layers moves the logits by ~4e-3 of
 // their magnitude; f32 keeps the forward within ~1e-5 of the model's exact mathematics.
 //
-// The output rows also get their sub-block sums (sums of 32 consecutive features, the Q4_K
-// min operand's B side, dequant.cuh) when head_dim % 32 == 0 (a head's features then hold
-// whole sub-blocks; the loader rejects Q4_K output projections otherwise).
-//
 // Work list: tiles {first active row, rows (<= 32), first key position, keys} of one
 // sequence each (several sequences step together, their rows and cache positions
 // concatenated); a CTA takes tile blockIdx.x of one head.
@@ -62,13 +58,11 @@ template <int HD>
 constexpr int attn_smem_bytes() { return AttnSmem<HD>::bytes; }
 
 // q: [rows][ld_q] f32 (head h at h*HD), kc/vc: [positions][ld_kv] f32 (kv head at
-// kvh*HD), o: pair rows of ld_o bytes (4 * n_q, dequant.cuh), sums: their sub-block sums
-// rows (ld_s bytes); tiles / n_tiles: the work list.
+// kvh*HD), o: pair rows of ld_o bytes (4 * n_q, dequant.cuh); tiles / n_tiles: the work list.
 template <int HD>
 __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const float *__restrict__ q, int ld_q,
                                                            const float *__restrict__ kc, const float *__restrict__ vc,
                                                            int ld_kv, uint8_t *__restrict__ o, int ld_o,
-                                                           uint8_t *__restrict__ sums, int ld_s,
                                                            const int4 *__restrict__ tiles, const int *__restrict__ n_tiles_dev,
                                                            int n_rep, float scale_log2) {
     using L = AttnSmem<HD>;
@@ -205,31 +199,22 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const float *__restr
         __syncthreads();  // V and P of tile t consumed
         if (t + 1 < n_tiles) load_rows(Vs, HD, vc, (t + 1) * kAttnKeys);
     }
-    // row sums over the 16 threads of each row group, normalize, write pair rows and the
-    // sub-block sums (chunks 8g .. 8g + 7 of a head: eight consecutive threads of a row group)
+    // row sums over the 16 threads of each row group, normalize, write pair rows
 #pragma unroll
     for (int r = 0; r < 4; r++) {
 #pragma unroll
         for (int off = 8; off > 0; off >>= 1) l[r] += __shfl_xor_sync(0xffffffffu, l[r], off);
         const int row = q0 + 4 * ty + r;
+        if (row >= M) continue;
         const float inv = 1.f / l[r];
 #pragma unroll
         for (int i = 0; i < CPT; i++) {
             const int c = tx + 16 * i;
+            if (c >= NC) continue;
             float v[4];
 #pragma unroll
             for (int e = 0; e < 4; e++) v[e] = acc[r][i][e] * inv;
-            float ps = c < NC ? (v[0] + v[1]) + (v[2] + v[3]) : 0.f;
-            if constexpr (HD % 32 == 0) {
-                ps += __shfl_xor_sync(0xffffffffu, ps, 1);
-                ps += __shfl_xor_sync(0xffffffffu, ps, 2);
-                ps += __shfl_xor_sync(0xffffffffu, ps, 4);
-            }
-            if (row < M && c < NC) {
-                store_pair4(o + (size_t)row * ld_o, h * HD + 4 * c, v);  // features h*HD + 4c .. +3
-                if constexpr (HD % 32 == 0)
-                    if ((tx & 7) == 0) store_sum(sums + (size_t)row * ld_s, (h * HD + 4 * c) >> 5, ps);
-            }
+            store_pair4(o + (size_t)row * ld_o, h * HD + 4 * c, v);  // features h*HD + 4c .. +3
         }
     }
 }

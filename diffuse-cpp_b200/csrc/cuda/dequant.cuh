@@ -37,11 +37,6 @@ __host__ __device__ __forceinline__ uint32_t e4m3x2(float a, float b) {
     return (uint32_t)__nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
 }
 
-// Two f16 values -> e4m3 pair (low half in the low byte), saturating to +-448.
-__device__ __forceinline__ uint32_t e4m3x2h(__half2 v) {
-    return (uint32_t)__nv_cvt_halfraw2_to_fp8x2(*reinterpret_cast<const __half2_raw *>(&v), __NV_SATFINITE, __NV_E4M3);
-}
-
 // Output of one half-slice in the corrected form.
 struct HalfCorr {
     uint32_t hi[16];  // f16 pairs
@@ -127,94 +122,6 @@ __device__ __forceinline__ void q4k_half(const uint8_t *R, int r, int s, int h, 
     for (int i = 0; i < 8; i++) quad(o, i, h ? ((w[i] >> 4) & 0x0F0F0F0Fu) : (w[i] & 0x0F0F0F0Fu), f);
 }
 
-// Q4_K, exact f16 route (activations in pair rows).  w = d sc q - dmin m with the
-// pre-scaled d and dmin; v = sc q < 1024 is an integer, built as the f16 1024 + v by one
-// integer multiply-add and brought to v by a half add (exact).  d v has at most 21
-// significant bits, so hi = RN(d v) and lo = fma(d, v, -hi) are both exact f16 and
-// d v = hi + lo.  The min term c = dmin m is constant over a sub-block of 32: it enters
-// the GEMM as - sum_j c_j S_j over the sub-block sums S_j of the activations, one extra
-// MMA of K = 32 per k-block (the "min operand", q4x_min below) instead of per element.
-struct Q4XMeta {
-    __half2 d2;      // ws * d in both halves (exact: ws is a power of two)
-    uint32_t sc[4];  // 6-bit scales of the set's local sub-blocks (2 set, 2 set + 1, 2 set + 4, 2 set + 5)
-    float c[4];      // ws * dmin * m of the same sub-blocks (exact in f32: 11 + 6 bits)
-};
-__device__ __forceinline__ void q4x_load_meta(const uint8_t *R, int r, int set, float ws, Q4XMeta &m) {
-    const uint32_t dm = *reinterpret_cast<const uint32_t *>(R + 4 * r);
-    const float d = __half2float(__ushort_as_half((unsigned short)(dm & 0xFFFF))) * ws;
-    const float dmin = __half2float(__ushort_as_half((unsigned short)(dm >> 16))) * ws;
-    m.d2 = __float2half2_rn(d);
-    const uint32_t *sp = reinterpret_cast<const uint32_t *>(R + 512 + 12 * r);
-    const uint32_t s0 = sp[0], s1 = sp[1], s2 = sp[2];
-    auto qb = [&](int i) -> int { return (int)(((i < 4 ? s0 : i < 8 ? s1 : s2) >> (8 * (i & 3))) & 0xFF); };
-#pragma unroll
-    for (int l = 0; l < 4; l++) {
-        const int j = 2 * set + (l & 1) + 4 * (l >> 1);
-        int sc, mn;
-        if (l < 2) {
-            sc = qb(j) & 63;
-            mn = qb(j + 4) & 63;
-        } else {
-            sc = (qb(j + 4) & 0xF) | ((qb(j - 4) >> 6) << 4);
-            mn = (qb(j + 4) >> 4) | ((qb(j) >> 6) << 4);
-        }
-        m.sc[l] = (uint32_t)sc;
-        m.c[l] = dmin * (float)mn;
-    }
-}
-// The quant words of one half slice (the dequantizers load the next half's while they
-// wait for the current one's stage): Q4_K / Q8_0 two 16-byte chunks, Q6_K four.
-struct HalfWords {
-    uint4 a, b, c, d;
-};
-// Q4_K: qs bytes 32 s .. 32 s + 31 of row r (both halves of slice s; the half picks nibbles).
-__device__ __forceinline__ void q4x_load(const uint8_t *R, int r, int s, HalfWords &q) {
-    const uint8_t *qrow = R + 2048 + 128 * r;
-    q.a = *reinterpret_cast<const uint4 *>(qrow + (((2 * s) ^ (r & 7)) << 4));
-    q.b = *reinterpret_cast<const uint4 *>(qrow + (((2 * s + 1) ^ (r & 7)) << 4));
-}
-// Half h of a slice whose words q holds (one sub-block, scale sc): f16 hi and the e4m3
-// correction pair (hi 2^-10, lo), the HalfCorr layout.
-__device__ __forceinline__ void q4x_half(const HalfWords &q, int h, uint32_t sc, __half2 d2, HalfCorr &o) {
-    const uint32_t w[8] = {q.a.x, q.a.y, q.a.z, q.a.w, q.b.x, q.b.y, q.b.z, q.b.w};
-    const __half2 off = __floats2half2_rn(-1024.f, -1024.f);
-    const __half2 k10 = __floats2half2_rn(kCorrScale, kCorrScale);
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-        const uint32_t x = h ? ((w[i] >> 4) & 0x0F0F0F0Fu) : (w[i] & 0x0F0F0F0Fu);
-        // v of elements 4i, 4i + 1 and 4i + 2, 4i + 3 (16-bit lanes, low half first)
-        const __half2 va = __hadd2(u2h(__byte_perm(x, 0, 0x4140) * sc + 0x64006400u), off);
-        const __half2 vb = __hadd2(u2h(__byte_perm(x, 0, 0x4342) * sc + 0x64006400u), off);
-        const __half2 ha = __hmul2(d2, va), hb = __hmul2(d2, vb);
-        const __half2 la = __hfma2(d2, va, __hneg2(ha)), lb = __hfma2(d2, vb, __hneg2(hb));
-        o.hi[2 * i] = h2u(ha);
-        o.hi[2 * i + 1] = h2u(hb);
-        const __half2 sa = __hmul2(ha, k10), sb = __hmul2(hb, k10);
-        o.ch[i] = __byte_perm(e4m3x2h(sa), e4m3x2h(sb), 0x5410);
-        o.cl[i] = __byte_perm(e4m3x2h(la), e4m3x2h(lb), 0x5410);
-    }
-}
-// Min operand of one row for the set's four sub-blocks (eight TMEM columns, K = 16 f16):
-// [-c_hi x4 | -c_lo x4 | -c_hi x4 | 0 x4] with c = c_hi + c_lo (f16 each, c_lo exact); the
-// activations' side holds [S_hi x4 | S_hi x4 | S_lo x4 | 0 x4] in the same sub-block order,
-// so the product is -(c_hi S_hi + c_lo S_hi + c_hi S_lo).
-__device__ __forceinline__ void q4x_min(const Q4XMeta &m, uint32_t (&o)[8]) {
-    __half hi[4], lo[4];
-#pragma unroll
-    for (int l = 0; l < 4; l++) {
-        hi[l] = __float2half_rn(m.c[l]);
-        lo[l] = __float2half_rn(m.c[l] - __half2float(hi[l]));
-    }
-    o[0] = h2u(__hneg2(__halves2half2(hi[0], hi[1])));
-    o[1] = h2u(__hneg2(__halves2half2(hi[2], hi[3])));
-    o[2] = h2u(__hneg2(__halves2half2(lo[0], lo[1])));
-    o[3] = h2u(__hneg2(__halves2half2(lo[2], lo[3])));
-    o[4] = o[0];
-    o[5] = o[1];
-    o[6] = 0u;
-    o[7] = 0u;
-}
-
 // ── Q6_K ── chunk layout: [ql: 128 B/row, chunk c at c ^ (row & 7)]
 // [qh: 64 B/row at 16384, chunk c at c ^ ((row >> 1) & 3)][scales i8: 16 B/row at 24576]
 // [d f16: 2 B/row at 26624].
@@ -282,95 +189,6 @@ __device__ __forceinline__ void q80_half(const uint8_t *R, int r, int s, int h, 
     }
 }
 
-// ── f16 routes of Q6_K and Q8_0 (activations in pair rows) ── Both build the integer
-// quant value as the f16 1024 + u with one byte permute and bring it to q by a half add.
-// Q8_0: w = d q has at most 19 significant bits, so hi = RN(d q), lo = fma(d, q, -hi) are
-// exact.  Q6_K: w = (d sc) (q - 32) with d sc of up to 18 bits, split once per group of 16
-// as ds = ds_hi + ds_lo (f16 each, ds_lo exact); hi = RN(ds_hi v), lo = fma(ds_lo, v,
-// fma(ds_hi, v, -hi)), the inner fma exact and the outer one rounded at 2^-11 of lo.
-// Four values of a quad word u (bytes) to the e4m3 correction quads and f16 hi pairs.
-template <typename F>
-__device__ __forceinline__ void quad_f16(HalfCorr &o, int j, uint32_t u, F f) {
-    const __half2 k10 = __floats2half2_rn(kCorrScale, kCorrScale);
-    __half2 ha, la, hb, lb;
-    f(u2h(__byte_perm(u, 0x64u, 0x4140)), ha, la);  // values 4j, 4j + 1
-    f(u2h(__byte_perm(u, 0x64u, 0x4342)), hb, lb);  // values 4j + 2, 4j + 3
-    o.hi[2 * j] = h2u(ha);
-    o.hi[2 * j + 1] = h2u(hb);
-    o.ch[j] = __byte_perm(e4m3x2h(__hmul2(ha, k10)), e4m3x2h(__hmul2(hb, k10)), 0x5410);
-    o.cl[j] = __byte_perm(e4m3x2h(la), e4m3x2h(lb), 0x5410);
-}
-// Q6_K group scales of one dequantizer set as f16 pairs: dsh[g] + dsl[g] = ws d sc_g.
-struct Q6XMeta {
-    __half2 dsh[8], dsl[8];
-};
-__device__ __forceinline__ void q6x_load_meta(const uint8_t *R, int r, int set, float ws, Q6XMeta &m) {
-    Q6KMeta f;
-    q6k_load_meta(R, r, set, ws, f);
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-        const __half h = __float2half_rn(f.ds[i]);
-        m.dsh[i] = __half2half2(h);
-        m.dsl[i] = __half2half2(__float2half_rn(f.ds[i] - __half2float(h)));
-    }
-}
-// Q6_K: half hh of slice s: ql bytes 64 (s / 2) + 32 hh .. +31 and qh bytes 32 (s / 2) .. +31.
-__device__ __forceinline__ void q6x_load(const uint8_t *R, int r, int s, int hh, HalfWords &q) {
-    const int h = s >> 1;
-    const uint8_t *qlrow = R + 128 * r, *qhrow = R + 16384 + 64 * r;
-    q.a = *reinterpret_cast<const uint4 *>(qlrow + (((4 * h + 2 * hh) ^ (r & 7)) << 4));
-    q.b = *reinterpret_cast<const uint4 *>(qlrow + (((4 * h + 2 * hh + 1) ^ (r & 7)) << 4));
-    q.c = *reinterpret_cast<const uint4 *>(qhrow + (((2 * h) ^ ((r >> 1) & 3)) << 4));
-    q.d = *reinterpret_cast<const uint4 *>(qhrow + (((2 * h + 1) ^ ((r >> 1) & 3)) << 4));
-}
-__device__ __forceinline__ void q6x_half(const HalfWords &q, int s, int hh, __half2 dsh0, __half2 dsl0, __half2 dsh1,
-                                         __half2 dsl1, HalfCorr &o) {
-    const int s2 = s & 1;
-    const uint32_t lw[8] = {q.a.x, q.a.y, q.a.z, q.a.w, q.b.x, q.b.y, q.b.z, q.b.w};
-    const uint32_t qw[8] = {q.c.x, q.c.y, q.c.z, q.c.w, q.d.x, q.d.y, q.d.z, q.d.w};
-    const int shift = 4 * s2 + 2 * hh;
-    const __half2 off = __floats2half2_rn(-1056.f, -1056.f);  // 1024 + 32
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-        const uint32_t nib = s2 ? ((lw[i] >> 4) & 0x0F0F0F0Fu) : (lw[i] & 0x0F0F0F0Fu);
-        const uint32_t q6 = nib | (((qw[i] >> shift) & 0x03030303u) << 4);
-        const __half2 dh = i < 4 ? dsh0 : dsh1, dl = i < 4 ? dsl0 : dsl1;
-        quad_f16(o, i, q6, [&](__half2 m, __half2 &hi, __half2 &lo) {
-            const __half2 v = __hadd2(m, off);
-            hi = __hmul2(dh, v);
-            lo = __hfma2(dl, v, __hfma2(dh, v, __hneg2(hi)));
-        });
-    }
-}
-// Q8_0: half h of slice s is block 2s + h: its 32 quants (two 16-byte chunks) and, in c.x,
-// the block's f16 scale.
-__device__ __forceinline__ void q8x_load(const uint8_t *R, int r, int s, int h, HalfWords &q) {
-    const int blk = 2 * s + h;
-    const uint8_t *qrow = R + 2048 + 256 * r;
-    const int c0 = 2 * blk, c1 = 2 * blk + 1;
-    q.a = *reinterpret_cast<const uint4 *>(qrow + (((c0 & 8) | ((c0 & 7) ^ (r & 7))) << 4));
-    q.b = *reinterpret_cast<const uint4 *>(qrow + (((c1 & 8) | ((c1 & 7) ^ (r & 7))) << 4));
-    const uint16_t dh = *reinterpret_cast<const uint16_t *>(R + 16 * r + 2 * blk);
-    q.c = make_uint4(dh, 0, 0, 0);
-}
-// Q8_0 with scale ws d (exact in f16).
-__device__ __forceinline__ void q8x_half(const HalfWords &q, float ws, HalfCorr &o) {
-    const __half2 d2 = __float2half2_rn(__half2float(__ushort_as_half((unsigned short)q.c.x)) * ws);
-    const __half2 off = __floats2half2_rn(-1152.f, -1152.f);  // 1024 + 128
-#pragma unroll
-    for (int cc = 0; cc < 2; cc++) {
-        const uint4 v = cc ? q.b : q.a;
-        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-        for (int i = 0; i < 4; i++)
-            quad_f16(o, 4 * cc + i, w[i] ^ 0x80808080u, [&](__half2 m, __half2 &hi, __half2 &lo) {
-                const __half2 q = __hadd2(m, off);
-                hi = __hmul2(d2, q);
-                lo = __hfma2(d2, q, __hneg2(hi));
-            });
-    }
-}
-
 // ── activation pair rows ── per 64-wide slice: 64 hi f16 (128 B), then the correction
 // operand: 64 e4m3 of x_lo * 2^10, 64 e4m3 of x_hi (128 B); row length 4 bytes per value.
 // Eight consecutive values of a slice: one 16-byte and two 8-byte stores.
@@ -403,24 +221,6 @@ __device__ __forceinline__ void store_pair4(uint8_t *row, int i, const float (&v
     *reinterpret_cast<uint32_t *>(slice + 128 + k) =
         e4m3x2((v[0] - f01.x) * 1024.0f, (v[1] - f01.y) * 1024.0f) | (e4m3x2((v[2] - f23.x) * 1024.0f, (v[3] - f23.y) * 1024.0f) << 16);
     *reinterpret_cast<uint32_t *>(slice + 192 + k) = e4m3x2(f01.x, f01.y) | (e4m3x2(f23.x, f23.y) << 16);
-}
-
-// ── sub-block sums ── For Q4_K weights the GEMM also reads, per activation row and
-// k-block of 256, the sums S_j of its eight sub-blocks of 32 (f32 sums of the row's
-// values, split S = S_hi + S_lo in f16): 32 f16 (64 bytes) per k-block, two halves of 16
-// for the two dequantizer sets (sub-blocks 0, 1, 4, 5 and 2, 3, 6, 7), each
-// [S_hi x4 | S_hi x4 | S_lo x4 | 0 x4] (q4x_min holds the matching weight side).  The
-// zero entries are never written: sums buffers are zeroed once when allocated.
-constexpr int kSumsBytes = 64;  // per k-block of 256 values
-__device__ __forceinline__ void store_sum(uint8_t *sums_row, int j, float S) {
-    const int b = j >> 3, j8 = j & 7;
-    const int part = (j8 >> 1) & 1, l = (j8 & 1) | ((j8 >> 2) << 1);
-    __half *e = reinterpret_cast<__half *>(sums_row + b * kSumsBytes) + 16 * part;
-    const __half hi = __float2half_rn(S);
-    const __half lo = __float2half_rn(S - __half2float(hi));
-    e[l] = hi;
-    e[4 + l] = hi;
-    e[8 + l] = lo;
 }
 
 }  // namespace dfb

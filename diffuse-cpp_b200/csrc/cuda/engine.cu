@@ -101,31 +101,11 @@ static int make_tmap(CUtensorMap *m, const void *ptr, uint64_t cols, uint64_t ro
 // The 3-D activation views the GEMM loads its B operand through (XMaps in gemm_dq.cuh):
 // x is a row-major f16 matrix of rows of xs * K values (xs = 2: pair rows, xs = 1: plain),
 // K a multiple of 64, x 16-byte aligned.
-// Bytes of one sub-block sums row of an activation matrix of width K (dequant.cuh).
-static size_t sums_row_bytes(int K) { return (size_t)((K + 255) / 256) * kSumsBytes; }
-
-// sums: the sub-block sums rows of pair-row activations (xs = 2; the Q4_K min operand's B side).
-static int make_xmaps(XMaps *xm, const void *x, const void *sums, int K, int rows, int xs) {
+static int make_xmaps(XMaps *xm, const void *x, int K, int rows, int xs) {
     auto fn = encode_fn();
     if (!fn) return set_err(DFB_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
     if (K % 64) return set_err(DFB_ERR_UNSUPPORTED, "activation width %d not a multiple of 64", K);
     if (reinterpret_cast<uintptr_t>(x) % 16) return set_err(DFB_ERR_ARG, "activation matrix not 16-byte aligned");
-    memset(xm->s, 0, sizeof(xm->s));
-    if (xs == 2) {
-        if (!sums || reinterpret_cast<uintptr_t>(sums) % 16) return set_err(DFB_ERR_ARG, "sub-block sums missing or not 16-byte aligned");
-        const int kbs = (K + 255) / 256;
-        for (int i = 0; i < kXMaps; i++) {
-            const int h = 16 * (i + 1);
-            cuuint64_t dims[3] = {32, (cuuint64_t)rows, (cuuint64_t)kbs};
-            cuuint64_t strides[2] = {(cuuint64_t)sums_row_bytes(K), (cuuint64_t)kSumsBytes};
-            cuuint32_t box[3] = {32, (cuuint32_t)h, 1};
-            cuuint32_t es[3] = {1, 1, 1};
-            CUresult r = fn(&xm->s[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(sums), dims, strides, box, es,
-                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-            if (r != CUDA_SUCCESS) return set_err(DFB_ERR_CUDA, "cuTensorMapEncodeTiled (sums) failed (%d)", (int)r);
-        }
-    }
     for (int i = 0; i < kXMaps; i++) {
         const int h = 16 * (i + 1);
         cuuint64_t dims[3] = {64, (cuuint64_t)rows, (cuuint64_t)(xs * K / 64)};
@@ -643,8 +623,6 @@ extern "C" int dfb_model_finalize(dfb_model *m) {
         }
         const HostTensor &wo = staged(m, DFB_WO, l);
         RET(check_mat(wo, "attn_output", gq, d));
-        if (wo.type == G_Q4_K && m->hd % 32)  // the attention kernel writes sub-block sums per head
-            return set_err(DFB_ERR_UNSUPPORTED, "layer %d: Q4_K attn_output needs head_dim %% 32 == 0 (head_dim %d)", l, m->hd);
         {
             // the rank's heads' input columns of every output row (row-parallel: partial sums)
             std::vector<const uint8_t *> rows((d + 127) / 128 * 128, nullptr);
@@ -762,7 +740,6 @@ struct dfb_ctx {
     float *x = nullptr, *y = nullptr, *logits = nullptr;  // residual stream, projection output, logits
     float *q = nullptr, *kc = nullptr, *vc = nullptr;      // Q rows, K/V cache [layer][position][n_kv] (f32)
     uint8_t *h = nullptr, *att = nullptr, *ffh = nullptr;  // GEMM inputs as pair rows (4 bytes per value)
-    uint8_t *h_s = nullptr, *att_s = nullptr, *ffh_s = nullptr;  // their sub-block sums rows
     float2 *rope = nullptr;
     XMaps xm_h{}, xm_att{}, xm_ffh{};  // GEMM B-operand views of h, att, ffh
     // sequence state
@@ -813,13 +790,12 @@ static void ctx_free_buffers(dfb_ctx *c) {
                   c->last_changed, c->cand_tok, c->commit_pos, c->commit_tok, c->order, c->masked, c->active_pos,
                   c->masked_pos, c->cnt, c->cand_conf, c->cand_ent, c->ws, c->tile_cnt, c->err, c->seg_off,
                   c->seg_cnt, c->sched, c->tmp_active, c->tmp_masked, c->rope_pos, c->masked_row, c->done, c->tiles,
-                  c->h_s, c->att_s, c->ffh_s, c->unif, c->tp_stats, c->tp_gath, c->tp_g};
+                  c->unif, c->tp_stats, c->tp_gath, c->tp_g};
     for (void *p : ps) cudaFree(p);
     c->seg_off = c->seg_cnt = c->sched = c->tmp_active = c->tmp_masked = c->rope_pos = c->masked_row = nullptr;
     c->done = nullptr;
     c->tiles = nullptr;
     c->x = c->y = c->logits = c->q = c->kc = c->vc = nullptr; c->h = c->att = c->ffh = nullptr; c->rope = nullptr;
-    c->h_s = c->att_s = c->ffh_s = nullptr;
     c->unif = nullptr;
     c->tp_stats = c->tp_gath = nullptr;
     c->tp_g = nullptr;
@@ -855,7 +831,6 @@ static int ctx_reserve(dfb_ctx *c, int n) {
 #define AL(ptr, count) CK(cudaMalloc(&(ptr), sizeof(*(ptr)) * (size_t)(count)))
     AL(c->x, cap * d); AL(c->y, cap * d); AL(c->h, 4 * cap * d); AL(c->att, 4 * cap * d); AL(c->q, cap * d);
     AL(c->ffh, 4 * cap * ff);
-    AL(c->h_s, cap * sums_row_bytes((int)d)); AL(c->att_s, cap * sums_row_bytes(m->n_q)); AL(c->ffh_s, cap * sums_row_bytes((int)ff));
     AL(c->kc, L * cap * kvd); AL(c->vc, L * cap * kvd); AL(c->logits, (size_t)cap * V); AL(c->rope, cap * hd / 2);
     AL(c->seq, cap); AL(c->prev_seq, cap); AL(c->last_changed, cap); AL(c->cand_tok, cap); AL(c->commit_pos, cap);
     AL(c->commit_tok, cap); AL(c->order, cap); AL(c->masked, cap); AL(c->active_pos, cap); AL(c->masked_pos, cap);
@@ -880,18 +855,14 @@ static int ctx_reserve(dfb_ctx *c, int n) {
     CK(cudaMemset(c->h, 0, 4 * cap * d));
     CK(cudaMemset(c->att, 0, 4 * cap * d));
     CK(cudaMemset(c->ffh, 0, 4 * cap * ff));
-    // the sums rows' padding entries are read as zeros and never written
-    CK(cudaMemset(c->h_s, 0, cap * sums_row_bytes((int)d)));
-    CK(cudaMemset(c->att_s, 0, cap * sums_row_bytes(m->n_q)));
-    CK(cudaMemset(c->ffh_s, 0, cap * sums_row_bytes((int)ff)));
     CK(cudaMemset(c->kc, 0, 4 * L * cap * kvd));
     CK(cudaMemset(c->vc, 0, 4 * L * cap * kvd));
     std::vector<float2> rope;
     rope_table_host(cap, (int)hd, hp.rope_theta, rope);
     CK(cudaMemcpy(c->rope, rope.data(), rope.size() * sizeof(float2), cudaMemcpyHostToDevice));
-    RET(make_xmaps(&c->xm_h, c->h, c->h_s, (int)d, cap, 2));
-    RET(make_xmaps(&c->xm_att, c->att, c->att_s, m->n_q, cap, 2));
-    RET(make_xmaps(&c->xm_ffh, c->ffh, c->ffh_s, (int)ff, cap, 2));
+    RET(make_xmaps(&c->xm_h, c->h, (int)d, cap, 2));
+    RET(make_xmaps(&c->xm_att, c->att, m->n_q, cap, 2));
+    RET(make_xmaps(&c->xm_ffh, c->ffh, (int)ff, cap, 2));
     c->cap = cap;
     return DFB_OK;
 }
@@ -1030,11 +1001,10 @@ static int launch_gemm_t(dfb_ctx *c, const WMat &w, const XMaps &xm, const EpiAr
         return set_err(DFB_ERR_UNSUPPORTED, "GEMM schedule too large for %d rows", c->cap);
     CK(launch_k(kern, dim3(2 * n_pairs), dim3(kThreads), smem, c->st, !c->prof, w.tm, xm, p));
     // algorithmic work: 2*K MACs per output, weights read once, X read (pair rows, 4 B per
-    // value, plus the sub-block sums for Q4_K), Y written (f32, or pair rows for SwiGLU: 4 B
-    // per output feature either way)
+    // value), Y written (f32, or pair rows for SwiGLU: 4 B per output feature either way)
     const int cat = WT == W_Q4K ? DFB_PROF_Q4K : WT == W_Q6K ? DFB_PROF_Q6K : WT == W_Q80 ? DFB_PROF_Q80 : DFB_PROF_F16;
     prof_end(c, ev0, EPI == EPI_LOGITS ? (int)DFB_PROF_LMHEAD : cat, 2.0 * w.K * (double)w.n_true, (double)w.bytes,
-             4.0 * w.K + (WT == W_Q4K ? (double)sums_row_bytes(w.K) : 0.0) + 4.0 * (EPI == EPI_SWIGLU ? w.n_true / 2 : w.n_true));
+             4.0 * w.K + 4.0 * (EPI == EPI_SWIGLU ? w.n_true / 2 : w.n_true));
     return DFB_OK;
 }
 
@@ -1066,7 +1036,7 @@ static int launch_attn_t(dfb_ctx *c, const float *kc, const float *vc, int n_key
     cudaEvent_t ev0 = nullptr;
     prof_begin(c, &ev0);
     CK(launch_k(attn_kernel<HD>, grid, dim3(kAttnThreads), smem, c->st, !c->prof, (const float *)c->q, m->n_q, kc, vc,
-                m->n_kv, c->att, 4 * m->n_q, c->att_s, (int)sums_row_bytes(m->n_q), (const int4 *)c->tiles,
+                m->n_kv, c->att, 4 * m->n_q, (const int4 *)c->tiles,
                 (const int *)(c->cnt + CNT_NTILES),
                 m->hp.n_head / m->hp.n_head_kv, scale_log2));
     // algorithmic bytes: K and V of every key once (f32), Q in (f32), O out (pair rows)
@@ -1102,7 +1072,6 @@ static int run_forward(dfb_ctx *c, int n_total) {
     const dfb_model *m = c->m;
     const dfb_hparams &hp = m->hp;
     const int d = hp.n_embd, cap = c->cap;
-    const int hs_ld = (int)sums_row_bytes(d);
     if (m->embd_f16)
         embed_kernel<__half><<<cap, 256, 0, c->st>>>((const __half *)m->embd, d, hp.n_vocab, c->seq, c->active_pos, c->cnt, c->x);
     else
@@ -1113,7 +1082,7 @@ static int run_forward(dfb_ctx *c, int n_total) {
         float *kc = c->kc + (size_t)l * cap * m->n_kv, *vc = c->vc + (size_t)l * cap * m->n_kv;
         // the previous layer's down projection is added to the residual stream here
         CK(launch_k(rmsnorm_kernel, dim3(cap), dim3(256), 0, c->st, true, c->x, (const float *)(l ? c->y : nullptr),
-                    (const float *)L.attn_norm, d, hp.rms_norm_eps, (const int *)c->cnt, c->h, c->h_s, hs_ld));
+                    (const float *)L.attn_norm, d, hp.rms_norm_eps, (const int *)c->cnt, c->h));
         EpiArgs e;
         e.q_out = c->q; e.ld_q = m->n_q;
         e.k_cache = kc; e.v_cache = vc; e.ld_kv = m->n_kv;
@@ -1132,10 +1101,9 @@ static int run_forward(dfb_ctx *c, int n_total) {
         RET(launch_gemm<EPI_F32>(c, L.o, c->xm_att, eo));
         RET(tp_sum_rows(c));  // row-parallel O: the ranks' partial sums
         CK(launch_k(rmsnorm_kernel, dim3(cap), dim3(256), 0, c->st, true, c->x, (const float *)c->y,
-                    (const float *)L.ffn_norm, d, hp.rms_norm_eps, (const int *)c->cnt, c->h, c->h_s, hs_ld));
+                    (const float *)L.ffn_norm, d, hp.rms_norm_eps, (const int *)c->cnt, c->h));
         EpiArgs eg;
         eg.out = c->ffh; eg.ld = 2 * m->n_ff_l; eg.n_valid = 2 * m->n_ff_l;  // pair rows
-        eg.sums = c->ffh_s; eg.ld_sums = (int)sums_row_bytes(m->n_ff_l);
         RET(launch_gemm<EPI_SWIGLU>(c, L.gateup, c->xm_h, eg));
         EpiArgs ed;  // FFN down projection -> y, added to x by the next norm
         ed.out = c->y; ed.ld = d; ed.n_valid = d;
@@ -1143,7 +1111,7 @@ static int run_forward(dfb_ctx *c, int n_total) {
         RET(tp_sum_rows(c));  // row-parallel down
     }
     CK(launch_k(rmsnorm_kernel, dim3(cap), dim3(256), 0, c->st, true, c->x, (const float *)(hp.n_layer ? c->y : nullptr),
-                (const float *)m->output_norm, d, hp.rms_norm_eps, (const int *)c->cnt, c->h, c->h_s, hs_ld));
+                (const float *)m->output_norm, d, hp.rms_norm_eps, (const int *)c->cnt, c->h));
     EpiArgs el;
     el.out = c->logits; el.ld = m->n_vocab_l; el.n_valid = m->n_vocab_l; el.pos = c->active_pos;
     RET(launch_gemm<EPI_LOGITS>(c, m->lm_head, c->xm_h, el));
@@ -1169,8 +1137,6 @@ static const char *gemm_err_str(int code) {
         case 12: return "relay waited for an MMA to release its stage";
         case 13: return "split-tile contributor waited for the other contributors' partial sums";
         case 14: return "token count changed between the launch and the grid-dependency wait";
-        case 15: return "activation producer waited for a free sub-block sums slot";
-        case 16: return "relay waited for sub-block sums to land";
         default: return "unknown";
     }
 }
@@ -1321,20 +1287,17 @@ extern "C" int dfb_linear(dfb_ctx *c, int role, int layer, const float *x_host, 
         }
     }
     RET(ctx_reserve(c, M));
-    uint8_t *xh = nullptr, *xs = nullptr;
+    uint8_t *xh = nullptr;
     float *xf = nullptr, *y = nullptr;
-    const size_t ls = sums_row_bytes(K);
     CK(cudaMalloc(&xh, (size_t)M * K * 4));  // pair rows
-    CK(cudaMalloc(&xs, (size_t)M * ls));     // their sub-block sums
     CK(cudaMalloc(&xf, (size_t)M * K * 4));
     CK(cudaMalloc(&y, (size_t)M * w->n_rows * 4));
     int rc = DFB_OK;
     XMaps xm;
     do {
-        if ((rc = make_xmaps(&xm, xh, xs, K, M, 2)) != DFB_OK) break;
-        if (cudaMemsetAsync(xs, 0, (size_t)M * ls, c->st) != cudaSuccess) { rc = set_err(DFB_ERR_CUDA, "memset failed"); break; }
+        if ((rc = make_xmaps(&xm, xh, K, M, 2)) != DFB_OK) break;
         if (cudaMemcpyAsync(xf, x_host, (size_t)M * K * 4, cudaMemcpyHostToDevice, c->st) != cudaSuccess) { rc = set_err(DFB_ERR_CUDA, "H2D failed"); break; }
-        f32_to_pair_kernel<<<256, 256, 0, c->st>>>(xf, xh, M, K, xs, (int)ls);
+        f32_to_pair_kernel<<<256, 256, 0, c->st>>>(xf, xh, M, K);
         if (cudaMemcpyAsync(c->cnt + CNT_M, &M, sizeof(int), cudaMemcpyHostToDevice, c->st) != cudaSuccess) { rc = set_err(DFB_ERR_CUDA, "H2D failed"); break; }
         EpiArgs e;
         e.out = y; e.ld = w->n_rows; e.n_valid = w->n_rows;
@@ -1361,7 +1324,7 @@ extern "C" int dfb_linear(dfb_ctx *c, int role, int layer, const float *x_host, 
                 y_host[(size_t)t * n_out + f] = full[(size_t)t * w->n_rows + r];
             }
     } while (0);
-    cudaFree(xh); cudaFree(xs); cudaFree(xf); cudaFree(y);
+    cudaFree(xh); cudaFree(xf); cudaFree(y);
     return rc;
 }
 
@@ -1665,7 +1628,7 @@ extern "C" int dfb_linear_noalloc(const dfb_model *m, int role, int layer, const
     if (w->n_tiles > kNoallocMaxTiles)
         return set_err(DFB_ERR_ARG, "weight has %d output tiles, the fixed scratch holds %d", w->n_tiles, kNoallocMaxTiles);
     XMaps xm;  // host-side descriptors of the caller's matrix (no device memory)
-    RET(make_xmaps(&xm, x_f16_dev, nullptr, K, M, 1));
+    RET(make_xmaps(&xm, x_f16_dev, K, M, 1));
     std::lock_guard<std::mutex> lk(device_lock(m->device));
     CK(cudaSetDevice(m->device));
     NoallocDev nd;

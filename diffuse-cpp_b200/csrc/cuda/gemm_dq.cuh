@@ -9,13 +9,9 @@
 // to ~5 bits) as one E4M3 MMA (kind::f8f6f4, twice the f16 rate) over the operand pairs
 // [W_hi 2^-10 | W_lo] x [X_lo 2^10 | X_hi], whose products land at their true scale.
 // Per element that is ~2^-17 of the product, below the f32 accumulation error over K.
-// Quantized weights are pre-scaled by a power of two that puts the largest near 2^14 (the
-// epilogue undoes it).  Q4_K (pair-row activations): hi and lo of d (sc q) come exactly
-// from f16 arithmetic on the integer sc q, and the min term dmin m, constant over each
-// sub-block of 32, enters as - sum_j (dmin m)_j S_j over the activations' sub-block sums
-// (one K = 32 MMA per k-block, dequant.cuh).  Q6_K / Q8_0 and Q4_K with plain f16
-// activations are dequantized in f32 (Q4_K d*sc*q - dmin*m one f32 rounding, Q6_K / Q8_0
-// products exact).  F16 / F32 / BF16 weights come as
+// Quantized weights are dequantized in f32 (exact: Q4_K d*sc*q - dmin*m is one f32
+// rounding, Q6_K / Q8_0 products are exact) after a power-of-two pre-scale that puts the
+// largest near 2^14; the epilogue undoes the scale.  F16 / F32 / BF16 weights come as
 // precomputed f16 hi and E4M3 correction matrices.  For plain f16 activations (XS = 1, the
 // allocation-free entry point) the weights are split into f16 hi and lo instead (two f16
 // MMAs, exact products).
@@ -54,8 +50,6 @@ namespace dfb {
 enum WType : int { W_Q4K = 0, W_Q6K = 1, W_Q80 = 2, W_F16 = 3, W_F32 = 4 };
 __host__ __device__ constexpr bool w_smem(int wt) { return wt == W_F16 || wt == W_F32; }  // A by TMA into shared memory
 __host__ __device__ constexpr bool w_split(int wt) { return wt != W_F16; }               // A has a lo part
-// The min operand (Q4_K exact route): activations in pair rows with sub-block sums.
-__host__ __device__ constexpr bool w_min(int wt, int xs) { return wt == W_Q4K && xs == 2; }
 // EPI_F32: f32 rows; EPI_QKV: Q rows and K/V cache rows (f32) with bias and RoPE;
 // EPI_SWIGLU: silu(gate) * up as pair-layout rows (the down projection's X);
 // EPI_LOGITS: f32 rows at the tokens' positions.
@@ -82,8 +76,6 @@ struct EpiArgs {
     const float2 *rope = nullptr;      // [position][head_dim/2] (cos, sin)
     const int *pos = nullptr;          // [tokens] position of each row (QKV cache rows, LOGITS rows)
     const int *rope_pos = nullptr;     // [tokens] position within its sequence (QKV RoPE angles)
-    uint8_t *sums = nullptr;           // SWIGLU: sub-block sums rows of the output (dequant.cuh)
-    int ld_sums = 0;                   // their row stride in bytes
 };
 
 // Activation tensor maps, one per token half-group size h = 16 (i + 1), i = 0..7: a 3-D
@@ -94,11 +86,8 @@ struct EpiArgs {
 // K-major SW128 layout.
 constexpr int kXMaps = 8;
 __host__ __device__ constexpr int x_slices(int h) { return h <= 32 ? 4 : h <= 64 ? 2 : 1; }
-// Sub-block sums maps (pair-row activations only): a 3-D view {32 f16, rows, k-blocks}
-// of the sums rows (dequant.cuh), box {32, h, 1}, 64-byte swizzle.
 struct XMaps {
     CUtensorMap m[kXMaps];
-    CUtensorMap s[kXMaps];
 };
 
 struct GemmParams {
@@ -122,63 +111,46 @@ constexpr int kEpiThreads = 256;         // two epilogue warps per TMEM lane qua
 constexpr int kDeqWarps = 8;             // two sets of four: even / odd k-slices
 constexpr int kSliceBytes = 128 * 128;   // one 64-wide k-slice of this CTA's 128 weight rows (f16)
 constexpr int kMaxTok = 256;             // tokens per MMA group (N) of the pair
-constexpr int kDblTok = 160;             // groups up to this size double-buffer the accumulator
-// (an MMA's N is the group rounded up to 32, two halves of 16-row multiples: the limit is a
-// multiple of 32 so a double-buffered accumulator never reaches the next one or the A stages)
+constexpr int kDblTok = 192;             // groups up to this size double-buffer the accumulator
+// (an MMA's N is the group rounded up to 32: the limit is a multiple of 32 so a
+// double-buffered accumulator never reaches the next one or the A stages)
 static_assert(kDblTok % 32 == 0, "double-buffered accumulator width");
 constexpr int kWsTile = kMaxTok * 128;   // floats per partial tile (one CTA's 128 rows)
 constexpr int kErrTimeout = 0x100;
 constexpr int kMaxAStages = 6, kMaxBSlots = 24, kMaxRawStages = 4;
-// TMEM (512 columns per CTA): accumulators [0, 160) and [160, 320) for token groups of up
-// to 160, one accumulator [0, 256) for larger groups (the MMA of the next segment then
+// TMEM (512 columns per CTA): accumulators [0, 192) and [192, 384) for token groups of up
+// to 192, one accumulator [0, 256) for larger groups (the MMA of the next segment then
 // waits for the epilogue to drain it, which costs less than dequantizing the weights once
-// per group of 128); dequantized A stages (quantized weights) at [320 + 32 st, +32), four
-// stages of half a k-slice (32 k) each, dequantizer set p filling stages 2p (first half of
-// its slices) and 2p + 1 (second half): lane = weight row, f16 hi in the first 16 columns,
-// then the E4M3 correction pair (8 columns W_hi 2^-10, 8 columns W_lo), or f16 lo for
-// XS = 1; the Q4_K min operand of the current k-block at [448, 464) (8 columns per set).
-// Half-slice stages let a set store the first half of its next slice as soon as the MMA
-// of the first half of its previous one is done, so what remains after each wait is a
-// store, not a dequantization.
+// per group of 128); dequantized A stages (quantized weights) at [384 + 64 st, +64):
+// lane = weight row, one k-slice each: f16 hi in the first 32 columns, then the E4M3
+// correction pair (16 columns W_hi 2^-10, 16 columns W_lo), or f16 lo for XS = 1.
 constexpr int kTmemA = 2 * kDblTok;
-constexpr int kTmemAStage = 32;
-constexpr int kNAT = 4;                  // TMEM A stages (half slices)
-constexpr int kNA = 2;                   // shared-memory A stages (f16 tile weights: whole slices)
-constexpr int kTmemMin = kTmemA + kNAT * kTmemAStage;
-static_assert(kTmemMin + 16 <= 512, "TMEM columns");
+constexpr int kTmemAStage = 64;
+constexpr int kTmemALo = 32;
+constexpr int kNA = 2;                   // A stages: set p of the dequantizers fills stage p
+static_assert(kTmemA + kNA * kTmemAStage <= 512, "TMEM columns");
 
 // Rings per weight type, sized so that shared memory (227 KB) holds them:
-//  A        dequantized weights go to TMEM, four half-slice stages (written by tcgen05.st,
-//           read by the MMA from TMEM: no shared-memory round trip and no proxy fence,
-//           which cost ~1.2k cycles per warp and stage); f16 weight tiles are TMA-loaded
-//           into a shared-memory ring of two whole-slice stages instead (hi and lo tiles
-//           for W_F32);
+//  A        one k-slice per stage, two stages: dequantized weights go to TMEM (written by
+//           tcgen05.st, read by the MMA from TMEM: no shared-memory round trip and no
+//           proxy fence, which cost ~1.2k cycles per warp and stage); f16 weight tiles
+//           are TMA-loaded into a shared-memory ring instead (hi and lo tiles for W_F32);
 //  B ring   this CTA's activation rows of 1-4 k-slices per slot, so small token counts
 //           keep many slices in flight and hide the L2 latency;
 //  raw ring re-tiled weight chunks (one k-block of 256 for 128 rows), grouped.
-__host__ __device__ constexpr int a_stages(int wt) { return w_smem(wt) ? kNA : kNAT; }
-// A units per k-slice: whole slices (shared-memory A) or halves (TMEM A)
-__host__ __device__ constexpr int a_units(int wt) { return w_smem(wt) ? 1 : 2; }
+__host__ __device__ constexpr int a_stages(int wt) { return kNA; }
 // f16 tile weights: XS = 2 stages hold the hi and correction tiles, XS = 1 the hi tile
 // (and the lo tile of W_F32)
 __host__ __device__ constexpr int a_stage_bytes(int wt, int xs) {
     return (xs == 2 || wt == W_F32) ? 2 * kSliceBytes : kSliceBytes;
 }
 __host__ __device__ constexpr int a_ring_bytes(int wt, int xs) { return w_smem(wt) ? kNA * a_stage_bytes(wt, xs) : 0; }
-// The activation stream dominates the shared-memory traffic (4 bytes per value, re-read for
-// every 256-row weight tile: at 256 tokens 32 KB per k-slice and CTA against 4.6 KB of Q4_K
-// weights); a slot returns only after its load's latency and its slice's MMA, so the ring's
-// depth sets the k-slice rate: 128 KB (4 slots of the widest group).
-__host__ __device__ constexpr int b_ring_bytes(int wt) { return 128 * 1024; }
-// Sub-block sums ring (min operand's B side): two slots of one k-block's sums for up to 128
-// rows (64 bytes each, 64-byte swizzle).
-constexpr int kMinSlots = 2, kMinSlotBytes = 128 * 64;
-__host__ __device__ constexpr int min_ring_bytes(int wt, int xs) { return w_min(wt, xs) ? kMinSlots * kMinSlotBytes : 0; }
-// A raw stage holds raw_cpr consecutive chunks of the CTA's unit range; stages are sized so
-// that, with the activation ring, shared memory holds 3-4 k-blocks of weights in flight
-// (several microseconds of dequantization at any token count, above the HBM latency).
-__host__ __device__ constexpr int raw_stages(int wt) { return wt == W_Q4K ? 4 : wt == W_Q6K ? 3 : wt == W_Q80 ? 2 : 0; }
-__host__ __device__ constexpr int raw_cpr(int wt) { return 1; }
+__host__ __device__ constexpr int b_ring_bytes(int wt) { return 96 * 1024; }
+// A raw stage holds raw_cpr consecutive chunks of the CTA's unit range: the weight
+// stream reached ~3.8 TB/s with 18 KB stages and ~6-7 TB/s with 36-72 KB stages
+// (same bytes in flight), so small chunks are grouped.
+__host__ __device__ constexpr int raw_stages(int wt) { return wt == W_Q4K ? 3 : wt == W_Q6K ? 4 : wt == W_Q80 ? 3 : 0; }
+__host__ __device__ constexpr int raw_cpr(int wt) { return wt == W_Q4K ? 2 : 1; }
 
 // Warp roles.  A warp runs on scheduler warp % 4 and may only access TMEM lanes
 // 32*(warp % 4)..+31, so the dequantizers (they write A into TMEM) and the epilogue cover
@@ -195,13 +167,12 @@ __host__ __device__ constexpr int deq_index(int w) { return w - 4; }
 // epilogue thread group: warps 12-15 and 16-19 each cover the four lane quarters
 __host__ __device__ constexpr int epi_half(int w) { return w >= 16 ? 1 : 0; }
 
+constexpr int kEpiStageBytes = 16 * 128 * 4;  // epilogue output staging per half: 16 tokens x 128 f32
 constexpr int kMaxContrib = 64;     // split contributors (CTA pairs) of one tile tracked in shared memory
-constexpr int kBarBytes = 84 * 8;   // mbarriers and flags, see the kernel's shared-memory map
-constexpr int kEpiSumBytes = 2 * 4 * 16 * 4;  // SwiGLU epilogue: per half, warp and token, a partial sub-block sum
+constexpr int kBarBytes = 80 * 8;   // mbarriers and flags, see the kernel's shared-memory map
 __host__ __device__ constexpr int gemm_smem_bytes(int wt, int xs) {
     return 1024 /*align slack*/ + a_ring_bytes(wt, xs) + b_ring_bytes(wt) + raw_stages(wt) * raw_cpr(wt) * raw_chunk_bytes(wt) +
-           min_ring_bytes(wt, xs) + kBarBytes /*barriers, flags*/ +
-           8 * kMaxTok /*token positions*/ + 8 * kMaxContrib /*contributor partial offsets*/ + kEpiSumBytes;
+           2 * kEpiStageBytes /*epilogue output staging*/ + kBarBytes /*barriers, flags*/ + 8 * kMaxTok /*token positions*/ + 2 * 8 * kMaxContrib /*contributor partial offsets*/;
 }
 
 // Static stream-K schedule over CTA pairs, recomputed identically by every role of
@@ -266,7 +237,6 @@ struct EpiRow {
     int f;          // output feature written by this lane (after un-fusing)
     int col;        // its column in the tile's staging rows
     bool fvalid;    // f is a real feature (not tile padding)
-    bool writer;    // this lane stores (SwiGLU: the gate lane of each pair)
     int sec;        // QKV: 0 Q, 1 K, 2 V
     int ipair;      // QKV: NEOX pair index i (angle index)
     int bpair;      // QKV: 0 for element i, 1 for element i + head_dim/2
@@ -289,7 +259,6 @@ __device__ __forceinline__ EpiRow epi_row(const EpiArgs &e, int tile, int row) {
         r.f = tile * 64 + (row >> 1);
         r.col = row >> 1;
         r.fvalid = 2 * r.f < e.n_valid;
-        r.writer = (row & 1) == 0;
     } else if constexpr (EPI == EPI_QKV) {
         const int hd = e.head_dim;
         int lt;
@@ -308,15 +277,22 @@ __device__ __forceinline__ EpiRow epi_row(const EpiArgs &e, int tile, int row) {
         r.col = r.f - lt * 128;  // heads divide the 128-row tile, so the tile's features stay in it
         r.fvalid = r.f < (r.sec == 0 ? e.n_q : e.n_kv);
         r.bias = (e.bias && r.fvalid) ? __ldg(e.bias + sec_off + r.f) : 0.f;
-        r.writer = true;
     } else {
         r.f = tile * 128 + row;
         r.col = row;
         r.fvalid = r.f < e.n_valid;
-        r.writer = true;
     }
     return r;
 }
+
+// Output staging: a chunk of 16 tokens x the tile's output features, one per epilogue
+// half, written by the row threads and stored to global memory as whole token rows.
+// SwiGLU rows hold the tile's 64 features as one pair-layout slice (256 bytes).
+template <int EPI> struct EpiFmt {
+    static constexpr int esize = EPI == EPI_SWIGLU ? 2 : 4;
+    static constexpr int width = 128;                  // staged elements per token row
+    static constexpr int row_bytes = esize * width;    // staging row pitch
+};
 
 // Where one tile's token rows go.
 struct EpiDst {
@@ -324,11 +300,11 @@ struct EpiDst {
     long long ld;    // bytes between rows
     int nbytes;      // valid bytes per row (0: the tile is padding)
     bool by_pos;     // row index = the token's position (else m0 + token)
+    bool vec;        // 16-byte vector stores are aligned
 };
 template <int EPI>
 __device__ __forceinline__ EpiDst epi_dst(const EpiArgs &e, int tile) {
-    constexpr int es = EPI == EPI_SWIGLU ? 2 : 4;  // SwiGLU: f16 units of the pair rows
-    constexpr int W = 128;
+    constexpr int es = EpiFmt<EPI>::esize, W = EpiFmt<EPI>::width;
     EpiDst d{};
     long long ld_el;
     int n_el, e0;
@@ -357,35 +333,29 @@ __device__ __forceinline__ EpiDst epi_dst(const EpiArgs &e, int tile) {
     }
     d.ld = ld_el * es;
     d.nbytes = max(0, min(W, n_el)) * es;
+    d.vec = (reinterpret_cast<uintptr_t>(d.base) % 16 == 0) && (d.ld % 16 == 0);
     return d;
 }
 
-// Epilogue of 16 consecutive tokens (tl0 .. tl0+15 of the segment) for this lane's row,
-// stored straight to the output rows: lane = output feature, consecutive lanes hold
-// consecutive features (QKV: two runs per warp, NEOX halves), so each token's store of a
-// warp is one or two contiguous segments.  v holds the raw accumulator (pre-scaled
-// weights): the first step multiplies by out_scale.  Called by all 32 lanes of a warp
-// together (paired epilogues exchange values with the neighbouring lane).  s_pos / s_rpos:
-// the segment's token positions (shared memory).  SwiGLU also leaves the warp's partial
-// sub-block sums of the 16 tokens in esum (lane 0 of each warp).
+// Epilogue math of 16 consecutive tokens (tl0 .. tl0+15 of the segment) for this lane's
+// row, into the staging rows.  v holds the raw accumulator (pre-scaled weights): the
+// first step multiplies by out_scale.  Called by all 32 lanes of a warp together (paired
+// epilogues exchange values with the neighbouring lane).  s_pos: positions of the
+// segment's tokens (shared memory).
 template <int EPI>
-__device__ __forceinline__ void epi_store(const EpiArgs &e, const EpiRow &r, const EpiDst &d, const int *s_pos,
-                                          const int *s_rpos, int m0, int tl0, int ntok, float (&v)[16], float *esum) {
+__device__ __forceinline__ void epi_values(const EpiArgs &e, const EpiRow &r, const int *s_rpos, int tl0, int ntok,
+                                           float (&v)[16], uint8_t *stage) {
+    constexpr int RB = EpiFmt<EPI>::row_bytes;
 #pragma unroll
     for (int i = 0; i < 16; i++) v[i] *= e.out_scale;
-    auto row_of = [&](int t) -> long long { return d.by_pos ? (long long)s_pos[t] : (long long)(m0 + t); };
     if constexpr (EPI == EPI_F32 || EPI == EPI_LOGITS) {
-        const bool ok = r.col * 4 < d.nbytes;
 #pragma unroll
-        for (int i = 0; i < 16; i++)
-            if (ok && tl0 + i < ntok) *reinterpret_cast<float *>(d.base + row_of(tl0 + i) * d.ld + r.col * 4) = v[i];
+        for (int i = 0; i < 16; i++) reinterpret_cast<float *>(stage + i * RB)[r.col] = v[i];
     } else if constexpr (EPI == EPI_SWIGLU) {
         // lanes 2i (gate) and 2i + 1 (up) of feature i split the chunk's tokens: the even
         // lane takes tokens 0-7, the odd lane 8-15, each after receiving its partner's values
-        // for them.  silu(g) * up = g / (1 + e^-g) * up (ggml_silu, ggml_mul), with the fast
-        // exponential and divide (a few f32 ulp).
+        // for them
         const bool odd = (threadIdx.x & 1) != 0;
-        const bool ok = d.nbytes > 0;
         float g[8], up[8];
 #pragma unroll
         for (int j = 0; j < 8; j++) {
@@ -393,58 +363,70 @@ __device__ __forceinline__ void epi_store(const EpiArgs &e, const EpiRow &r, con
             g[j] = odd ? recv : v[j];
             up[j] = odd ? v[8 + j] : recv;
         }
-        const int t0 = tl0 + (odd ? 8 : 0);
 #pragma unroll
         for (int j = 0; j < 8; j++) {
-            const float hv = __fdividef(g[j], 1.0f + __expf(-g[j])) * up[j];
-            if (ok && t0 + j < ntok) {  // pair-layout slice: hi f16, then E4M3 lo 2^10, E4M3 hi
-                char *row = d.base + row_of(t0 + j) * d.ld;
-                const __half hh = __float2half_rn(hv);
-                const float hf = __half2float(hh);
-                reinterpret_cast<__half *>(row)[r.col] = hh;
-                const uint32_t c2 = e4m3x2((hv - hf) * 1024.0f, hf);
-                row[128 + r.col] = (char)(c2 & 0xFF);
-                row[192 + r.col] = (char)(c2 >> 8);
-            }
-            // the warp's 16 features of the token (lanes of one parity): partial sub-block sum
-            float ps = hv;
-#pragma unroll
-            for (int off = 2; off < 32; off <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
-            if ((threadIdx.x & 31) < 2) esum[((threadIdx.x >> 5) & 3) * 16 + (odd ? 8 : 0) + j] = ps;
+            const float hv = (g[j] / (1.0f + expf(-g[j]))) * up[j];  // silu(g) * up (ggml_silu, ggml_mul)
+            // pair-layout slice: hi f16, then E4M3 lo 2^10, E4M3 hi
+            const __half hh = __float2half_rn(hv);
+            const float hf = __half2float(hh);
+            uint8_t *row = stage + (j + (odd ? 8 : 0)) * RB;
+            reinterpret_cast<__half *>(row)[r.col] = hh;
+            const uint32_t c2 = e4m3x2((hv - hf) * 1024.0f, hf);
+            row[128 + r.col] = (uint8_t)(c2 & 0xFF);
+            row[192 + r.col] = (uint8_t)(c2 >> 8);
         }
     } else if constexpr (EPI == EPI_QKV) {
-        const bool ok = r.col < 128 && r.col * 4 < d.nbytes;
         if (r.sec < 2) {
             const int hh = e.head_dim >> 1;
-#pragma unroll 4
+            float2 csv[16];
+#pragma unroll
             for (int i = 0; i < 16; i++) {
                 const int pp = tl0 + i < ntok ? s_rpos[tl0 + i] : 0;
-                const float2 cs = __ldg(e.rope + (size_t)pp * hh + r.ipair);
+                csv[i] = __ldg(e.rope + (size_t)pp * hh + r.ipair);
+            }
+#pragma unroll
+            for (int i = 0; i < 16; i++) {
+                const float2 cs = csv[i];
                 const float x = v[i] + r.bias;
                 const float partner = __shfl_xor_sync(0xffffffffu, x, 1);
                 // ggml_rope_ext NEOX: (x0 cos - x1 sin, x0 sin + x1 cos)
                 const float o = r.bpair == 0 ? (x * cs.x - partner * cs.y) : (partner * cs.y + x * cs.x);
-                if (ok && tl0 + i < ntok) *reinterpret_cast<float *>(d.base + row_of(tl0 + i) * d.ld + r.col * 4) = o;
+                if (r.col < 128) reinterpret_cast<float *>(stage + i * RB)[r.col] = o;
             }
         } else {
 #pragma unroll
             for (int i = 0; i < 16; i++)
-                if (ok && tl0 + i < ntok) *reinterpret_cast<float *>(d.base + row_of(tl0 + i) * d.ld + r.col * 4) = v[i] + r.bias;
+                if (r.col < 128) reinterpret_cast<float *>(stage + i * RB)[r.col] = v[i] + r.bias;
         }
     }
 }
 
-// SwiGLU: the sub-block sums of the chunk's 16 tokens (the tile's 64 features are two
-// sub-blocks of 32, lane quarters 0-1 and 2-3), from the warps' partial sums, in a fixed
-// order.  tid: 0..127 within the epilogue half.
+// Stores the staged chunk as token rows: lanes of a warp cover a row in 16-byte pieces.
+// tid: 0..127 within the epilogue half.
 template <int EPI>
-__device__ __forceinline__ void epi_sums(const EpiArgs &e, int tile, int m0, int tl0, int ntok, const float *esum, int tid) {
-    if constexpr (EPI == EPI_SWIGLU) {
-        if (tid >= 32 || e.n_valid / 2 <= tile * 64) return;
-        const int i = tid & 15, sb = tid >> 4;
-        if (tl0 + i >= ntok) return;
-        const float S = esum[(2 * sb) * 16 + i] + esum[(2 * sb + 1) * 16 + i];
-        store_sum(e.sums + (size_t)(m0 + tl0 + i) * e.ld_sums, 2 * tile + sb, S);
+__device__ __forceinline__ void epi_copyout(const EpiDst &d, const int *s_pos, int m0, int tl0, int ntok,
+                                            const uint8_t *stage, int tid) {
+    constexpr int es = EpiFmt<EPI>::esize, RB = EpiFmt<EPI>::row_bytes;
+    constexpr int LPR = RB / 16, RPW = LPR >= 32 ? 1 : 32 / LPR;  // lanes per row, rows per warp pass
+    const int w = tid >> 5, lane = tid & 31;
+    for (int off = (lane % LPR) * 16; off < RB; off += 32 * 16) {
+        if (off >= d.nbytes) return;
+        for (int i = w * RPW + (LPR >= 32 ? 0 : lane / LPR); i < 16; i += 4 * RPW) {
+            const int t = tl0 + i;
+            if (t >= ntok) break;
+            const long long rowi = d.by_pos ? (long long)s_pos[t] : (long long)(m0 + t);
+            char *dst = d.base + rowi * d.ld + off;
+            const uint8_t *src = stage + i * RB + off;
+            if (d.vec && off + 16 <= d.nbytes) {
+                *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<const uint4 *>(src);
+            } else {
+                const int nb = min(16, d.nbytes - off);
+                for (int b = 0; b < nb; b += es) {
+                    if constexpr (es == 4) *reinterpret_cast<float *>(dst + b) = *reinterpret_cast<const float *>(src + b);
+                    else *reinterpret_cast<__half *>(dst + b) = *reinterpret_cast<const __half *>(src + b);
+                }
+            }
+        }
     }
 }
 
@@ -458,16 +440,12 @@ __device__ __forceinline__ void epi_sums(const EpiArgs &e, int tile, int m0, int
 // CTA's loads and arrivals reach them through cluster addresses.
 //
 // Shared memory (per CTA): [A ring (f16 weight tiles only): a_stages x a_stage_bytes]
-// [B ring][raw ring][sums ring (Q4_K)][barriers][token positions][contributor offsets]
-// [SwiGLU partial sums].  Slice i (64 k) of
-// the CTA's unit range is a_units A units (whole slice, or two halves for TMEM A); unit u
-// uses A stage u % a_stages (TMEM columns kTmemA + 32 stage for quantized weights); the
-// slice is part i % spb of B slot (i / spb) % nbs; a part holds the slice's XS sub-slices
-// (hi, then lo).
+// [B ring][raw ring][barriers][token positions][contributor offsets].  Slice i (64 k) of
+// the CTA's unit range uses A stage i % a_stages (TMEM columns kTmemA + 64 stage for
+// quantized weights) and part i % spb of B slot (i / spb) % nbs; a part holds the
+// slice's XS sub-slices (hi, then lo).
 //
-// MMAs per slice: W_hi.X_hi, W_hi.X_lo (XS = 2), W_lo.X_hi (weights with a lo part);
-// Q4_K with pair rows: after the last slice of each k-block, the min operand times the
-// k-block's sub-block sums (K = 32).
+// MMAs per slice: W_hi.X_hi, W_hi.X_lo (XS = 2), W_lo.X_hi (weights with a lo part).
 //
 // Warps (warp_role): w0 activation producer, w1 MMA issuer (even CTA) + TMEM owner, w2
 // weight-chunk producer (f16 weights: A-tile TMA producer), w3 relay, w4-w11 dequantizers
@@ -480,45 +458,35 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     constexpr int NA = a_stages(WT), NRAW = raw_stages(WT), BRING = b_ring_bytes(WT), AR = a_ring_bytes(WT, XS);
     constexpr int ASB = a_stage_bytes(WT, XS);
     constexpr int CPR = raw_cpr(WT), RSB = CPR * RAWB;  // chunks and bytes per raw stage
-    constexpr bool MIN = w_min(WT, XS);
     static_assert(gemm_smem_bytes(WT, XS) <= 227 * 1024, "shared memory per CTA");
     static_assert(XS == 1 || XS == 2, "activation parts");
-    static_assert(!MIN || (AR + BRING + NRAW * RSB) % 1024 == 0, "sums ring alignment (64-byte swizzle)");
-    constexpr int UPS = a_units(WT);  // A units per k-slice
-    static_assert(NA == 2 * UPS, "dequantizer set p fills A stages p UPS .. p UPS + UPS - 1");
-    // The relay frees the B slot of A unit j - NA (slice (j - NA) / UPS, NA / UPS slices back)
-    // while it handles unit j, after waiting for the B loads up to the slice before: with one
-    // slice per load (the widest group, 16 or 32 KB loads) the producer needs
-    // 2 + (NA / UPS - 1) slots not to wait on itself.
-    static_assert(BRING / (kMaxTok / 2 * 128 * XS) >= 2 + (NA / UPS - 1), "B ring too shallow for the A ring");
+    static_assert(NA == 2, "dequantizer set p fills A stage p");
+    // The relay frees the B slot of slice j - NA while it handles slice j, after waiting
+    // for the B loads up to slice j - 1: with one slice per load (the widest group, 16 or
+    // 32 KB loads) the producer needs 2 + (NA - 1) slots not to wait on itself.
+    static_assert(BRING / (kMaxTok / 2 * 128 * XS) >= 2 + (NA - 1), "B ring too shallow for the A ring");
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *aring = smem;  // f16 weight tiles only
     uint8_t *bring = smem + AR;
     uint8_t *raw = bring + BRING;
-    uint8_t *minr = raw + NRAW * RSB;                     // sums ring (Q4_K with pair rows)
-    uint64_t *bars = reinterpret_cast<uint64_t *>(minr + min_ring_bytes(WT, XS));
+    uint8_t *epi_stage = raw + NRAW * RSB;  // [2 halves][kEpiStageBytes]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(epi_stage + 2 * kEpiStageBytes);
     uint64_t *full_a = bars, *empty_a = bars + 6, *full_b = bars + 12, *empty_b = bars + 36, *raw_full = bars + 60,
              *raw_empty = bars + 64, *acc_full = bars + 68, *acc_empty = bars + 70, *drain = bars + 72,
-             *fix_bar = bars + 73;
+             *fix_bar = bars + 73, *fix_bar2 = bars + 78;
     uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 74);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 75);
     volatile int *okflag = reinterpret_cast<volatile int *>(bars + 77);
-    uint64_t *full_m = bars + 78, *empty_m = bars + 80;  // sums ring
     int *s_pos = reinterpret_cast<int *>(bars + kBarBytes / 8);                   // [kMaxTok]
     int *s_rpos = s_pos + kMaxTok;                                                // [kMaxTok]
-    long long *s_contrib = reinterpret_cast<long long *>(s_rpos + kMaxTok);       // [kMaxContrib]
-    float *s_esum = reinterpret_cast<float *>(s_contrib + kMaxContrib);           // [2 halves][4 warps][16 tokens]
+    long long *s_contrib = reinterpret_cast<long long *>(s_rpos + kMaxTok);       // [2][kMaxContrib]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = cluster_ctarank();
     const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
     // the next kernel of the stream may be scheduled now; it waits for this grid itself
     griddep_launch_dependents();
-    // The schedule needs only the token count, which is final before any GEMM of a
-    // forward starts (the step-preparation kernel or the host writes it ahead of the
-    // forward's first launch): its load overlaps the setup below.
-    const int M = *reinterpret_cast<volatile const int *>(p.m_dev);
     if (threadIdx.x == 0) {
         for (int i = 0; i < NA; i++) {
             // both CTAs' relays + f16 tiles: the expect_tx / else four dequant warps per CTA
@@ -537,12 +505,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             mbar_init(&acc_full[i], 1);
             mbar_init(&acc_empty[i], 2 * kEpiThreads / 32);  // every epilogue warp of both CTAs
         }
-        for (int i = 0; i < kMinSlots; i++) {
-            mbar_init(&full_m[i], 1);   // the producer's expect_tx
-            mbar_init(&empty_m[i], 1);  // the relay, once the k-block's MMAs completed
-        }
         mbar_init(drain, 1);
         mbar_init(fix_bar, 1);
+        mbar_init(fix_bar2, 1);
         *abort_flag = 0;
         fence_barrier_init();
     }
@@ -557,10 +522,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     cluster_sync();  // barriers of both CTAs initialised, TMEM of both allocated
     tc_fence_after();
     const uint32_t tmem_base = *tmem_holder;
-    // The weights do not depend on the previous kernel either.  So the weight producer and
-    // the dequantizers start now and fill the pipeline while the previous kernel finishes;
-    // the activation producer and the epilogue wait for it (griddepcontrol.wait) before they
-    // read or write anything it touches, and the MMAs wait for the activations.
+    // The schedule needs only the token count, which is final before any GEMM of a
+    // forward starts (the step-preparation kernel or the host writes it ahead of the
+    // forward's first launch), and the weights do not depend on the previous kernel.  So
+    // the weight producer and the dequantizers start now and fill the pipeline while the
+    // previous kernel finishes; the activation producer and the epilogue wait for it
+    // (griddepcontrol.wait) before they read or write anything it touches, and the MMAs
+    // wait for the activations.
+    const int M = *reinterpret_cast<volatile const int *>(p.m_dev);
     Sched S;
     S.init(M, p.n_tiles >> 1, p.kb, n_pairs, pair, BRING, XS);
     const int NBS = S.nbs;
@@ -575,22 +544,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             if (*reinterpret_cast<volatile const int *>(p.m_dev) != M) atomicCAS(p.err, 0, kErrTimeout + 14);
             const CUtensorMap *xmap = &xm.m[S.bh / 16 - 1];
-            const CUtensorMap *smap = &xm.s[S.bh / 16 - 1];
             int ob = 0, sl = 0;  // B loads issued, slot of the next one
             uint32_t ph = 0;     // ring pass parity of the next load
-            int mi = 0;          // sums loads issued (one per k-block)
             bool ok = true;
             for (int u = S.u0; u < S.u1 && ok;) {
                 const Seg g = make_seg(S, u, S.u1);
                 const int row0 = g.m0 + (int)rank * g.half;
                 for (int kbi = g.k0; kbi < g.k1 && ok; kbi++) {
-                    if constexpr (MIN) {  // the k-block's sub-block sums
-                        const int ms = mi % kMinSlots;
-                        if (!(ok = mbar_wait(&empty_m[ms], ((mi / kMinSlots) & 1) ^ 1, abort_flag, p.err, kErrTimeout + 15, p.timeout_ns))) break;
-                        mbar_arrive_expect_tx(&full_m[ms], (uint32_t)(S.bh * 64));
-                        tma_load_3d(minr + ms * kMinSlotBytes, smap, 0, row0, kbi, &full_m[ms]);
-                        mi++;
-                    }
                     for (int s = 0; s < 4; s += S.spb) {
                         if (!(ok = mbar_wait(&empty_b[sl], ph ^ 1, abort_flag, p.err, kErrTimeout + 2, p.timeout_ns))) break;
                         mbar_arrive_expect_tx(&full_b[sl], S.bslot);
@@ -604,8 +564,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             if (!ok) {
                 // let the copies in flight land before the CTA can exit
                 for (int i = (ob > NBS ? ob - NBS : 0); i < ob; i++) spin_bounded(&full_b[i % NBS], (i / NBS) & 1);
-                for (int i = (mi > kMinSlots ? mi - kMinSlots : 0); i < mi; i++)
-                    spin_bounded(&full_m[i % kMinSlots], (i / kMinSlots) & 1);
             }
         }
         __syncwarp();
@@ -677,7 +635,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const int lg_spb = S.spb == 1 ? 0 : S.spb == 2 ? 1 : 2;  // k-slices per ring slot: 1, 2 or 4
             const uint32_t bsub = S.bh * 128;  // bytes of one part (hi or lo) of a k-slice
             int bslot = 0;  // ring slot of the first slice of the next k-block
-            int mslot = 0;  // sums ring slot of the next k-block
             for (int u = S.u0; u < S.u1 && ok;) {
                 const Seg g = make_seg(S, u, S.u1);
                 const int acc = S.acc_of(si);
@@ -697,54 +654,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     bslot = (bslot + (4 >> lg_spb)) % NBS;
 #pragma unroll
                     for (int s2 = 0; s2 < 4; s2++) {
-                        // the slice's B parts: hi, then the correction operand (XS = 2)
+                        const int st = s2 & 1;
+                        // full_a also carries the relays' arrivals: this stage's B rows have landed
+                        if (!(ok = mbar_wait(&full_a[st], (uint32_t)(s2 >> 1), abort_flag, p.err, kErrTimeout + 5, p.timeout_ns))) break;
+                        tc_fence_after();
+                        // main term (f16), then the corrections: XS = 2 one E4M3 MMA over the
+                        // correction pairs, XS = 1 W_lo.X (f16) for weights with a lo part
                         const uint64_t bhi = bd[s2], bcor = bd[s2] + (uint64_t)(bsub >> 4);
                         if constexpr (w_smem(WT)) {
-                            // A from shared memory, whole-slice stages: stage s2 & 1, whose barrier
-                            // completes twice per k-block, so its parity is s2 >> 1
-                            const int st = s2 & 1;
-                            // full_a also carries the relays' arrivals: this stage's B rows have landed
-                            if (!(ok = mbar_wait(&full_a[st], (uint32_t)(s2 >> 1), abort_flag, p.err, kErrTimeout + 5, p.timeout_ns))) break;
-                            tc_fence_after();
-                            // main term (f16), then the corrections: XS = 2 one E4M3 MMA over the
-                            // correction pairs, XS = 1 W_lo.X (f16) for weights with a lo part
                             const uint64_t ahi = adesc0 + (uint64_t)((st * ASB) >> 4);
                             const uint64_t a2 = ahi + (uint64_t)(kSliceBytes >> 4);
                             mma2_f16_ss_k64(d_tmem, ahi, bhi, idesc, accum);
                             if constexpr (XS == 2) mma2_f8_ss_k128(d_tmem, a2, bcor, idesc);
                             else if constexpr (w_split(WT)) mma2_f16_ss_k64(d_tmem, a2, bhi, idesc, 1);
-                            accum = 1;
-                            mma2_commit_mc(&empty_a[st], 0x3);
                         } else {
-                            // A from TMEM, half-slice stages 2 (s2 & 1) + h (parity s2 >> 1 as above)
-#pragma unroll
-                            for (int h = 0; h < 2; h++) {
-                                const int st = 2 * (s2 & 1) + h;
-                                if (!(ok = mbar_wait(&full_a[st], (uint32_t)(s2 >> 1), abort_flag, p.err, kErrTimeout + 5, p.timeout_ns))) break;
-                                tc_fence_after();
-                                const uint32_t a = tmem_base + kTmemA + st * kTmemAStage;
-                                // B: elements 32 h .. 32 h + 31 of the slice: hi part +64 h bytes; the
-                                // correction operand's x_lo 2^10 half +32 h, its x_hi half +64 + 32 h
-                                mma2_f16_ts_h32(d_tmem, a, bhi + (uint64_t)(4 * h), idesc, accum);
-                                if constexpr (XS == 2) {
-                                    mma2_f8_ts_k32(d_tmem, a + 16, bcor + (uint64_t)(2 * h), idesc);
-                                    mma2_f8_ts_k32(d_tmem, a + 24, bcor + (uint64_t)(4 + 2 * h), idesc);
-                                } else {
-                                    mma2_f16_ts_h32(d_tmem, a + 16, bhi + (uint64_t)(4 * h), idesc, 1);
-                                }
-                                accum = 1;
-                                if constexpr (MIN) {
-                                    // after the k-block's last half slice: min operand x sub-block sums
-                                    // (K = 32); the commit below covers it (the relay frees the sums slot then)
-                                    if (s2 == 3 && h == 1)
-                                        mma2_f16_ts_k32(d_tmem, tmem_base + kTmemMin, sw64_desc(smem_u32(minr + mslot * kMinSlotBytes)), idesc);
-                                }
-                                mma2_commit_mc(&empty_a[st], 0x3);
-                            }
-                            if (!ok) break;
+                            const uint32_t ahi = tmem_base + kTmemA + st * kTmemAStage;
+                            mma2_f16_ts_k64(d_tmem, ahi, bhi, idesc, accum);
+                            if constexpr (XS == 2) mma2_f8_ts_k128(d_tmem, ahi + kTmemALo, bcor, idesc);
+                            else mma2_f16_ts_k64(d_tmem, ahi + kTmemALo, bhi, idesc, 1);
                         }
+                        accum = 1;
+                        mma2_commit_mc(&empty_a[st], 0x3);
                     }
-                    if constexpr (MIN) mslot = (mslot + 1) % kMinSlots;
                     issued = true;
                     if (!ok) break;
                 }
@@ -761,50 +692,39 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
     } else if (role == R_RELAY) {
-        // ── relay (one thread per CTA), A unit by A unit (whole or half slices, UPS per
-        //    slice): once the MMA of unit j - NA has completed (empty_a, the same wait the A
-        //    writers do), its B slot is free again after the slot's last unit; once this
-        //    CTA's B rows of unit j's slice have landed (full_b; for the last unit of a
-        //    k-block with the min operand also its sums, full_m), arrive on full_a of unit j
-        //    in the even CTA.  The MMA issuer so waits on one barrier per unit, and no relay
+        // ── relay (one thread per CTA), slice by slice: once the MMA of slice j - NA has
+        //    completed (empty_a, the same wait the A writers do), its B slot is free again
+        //    (after the last slice of the slot's load); once this CTA's B rows of slice j
+        //    have landed (full_b), arrive on full_a of slice j in the even CTA.  The MMA issuer so waits on one barrier per stage, and no relay
         //    can fall a full phase behind the barriers it polls. ──
         if (lane == 0) {
-            int n_it = 0;  // A units of the range
+            int n_it = 0;
             for (int u = S.u0; u < S.u1;) {
                 const Seg g = make_seg(S, u, S.u1);
-                n_it += 4 * UPS * (g.k1 - g.k0);
+                n_it += 4 * (g.k1 - g.k0);
                 u += g.k1 - g.k0;
             }
             bool ok = true;
             const int spb = S.spb;
-            // running ring positions (no divisions): B load of unit j and of unit j - NA
+            // running ring positions (no divisions): B load of slice j and of slice j - NA
             int fo_sl = 0, fo_part = 0, eo_sl = 0, eo_part = 0;
             uint32_t fo_ph = 0;
-            for (int j = 0; j < n_it + NA && ok; j++) {  // A stage j % NA
+            for (int j = 0; j < n_it + NA && ok; j++) {  // A stage = slice j
                 if (j >= NA) {
-                    // MMA of unit j - NA done (phase (j - NA) / NA of empty_a[j % NA]); its B
-                    // slot is free once the last unit of the slot's last slice is done
+                    // MMA of slice j - NA done (phase (j - NA) / NA of empty_a[j % NA]); its B
+                    // slot is free once the last slice of the slot's load is done
                     if (!(ok = mbar_wait(&empty_a[j % NA], ((j / NA) & 1) ^ 1, abort_flag, p.err, kErrTimeout + 12, p.timeout_ns))) break;
-                    const int ju = j - NA;
-                    if (ju % UPS == UPS - 1) {
-                        if (++eo_part == spb) {
-                            eo_part = 0;
-                            mbar_arrive(&empty_b[eo_sl]);
-                            if (++eo_sl == NBS) eo_sl = 0;
-                        }
-                        // the k-block's sums slot, once its last unit (and the min MMA) completed
-                        if (MIN && ((ju / UPS) & 3) == 3) mbar_arrive(&empty_m[(ju / UPS >> 2) % kMinSlots]);
+                    if (++eo_part == spb) {
+                        eo_part = 0;
+                        mbar_arrive(&empty_b[eo_sl]);
+                        if (++eo_sl == NBS) eo_sl = 0;
                     }
                 }
                 if (j < n_it) {
-                    const int js = j / UPS;  // slice
-                    if (j % UPS == 0 && fo_part == 0)
+                    if (fo_part == 0)
                         if (!(ok = mbar_wait(&full_b[fo_sl], fo_ph, abort_flag, p.err, kErrTimeout + 4, p.timeout_ns))) break;
-                    if (MIN && (js & 3) == 3 && j % UPS == UPS - 1)  // the min MMA follows this unit: its sums have landed
-                        if (!(ok = mbar_wait(&full_m[(js >> 2) % kMinSlots], ((js >> 2) / kMinSlots) & 1, abort_flag, p.err,
-                                             kErrTimeout + 16, p.timeout_ns))) break;
                     mbar_arrive_cluster(full_a0 + 8 * (j % NA));
-                    if (j % UPS == UPS - 1 && ++fo_part == spb) {
+                    if (++fo_part == spb) {
                         fo_part = 0;
                         if (++fo_sl == NBS) { fo_sl = 0; fo_ph ^= 1; }
                     }
@@ -814,8 +734,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         __syncwarp();
     } else if (role == R_DEQ) {
         // ── dequantizers: thread = weight row of this CTA's tile; set p takes slices
-        //    p and p + 2 of every k-block, first halves into A stage 2p, second halves
-        //    into 2p + 1 (each stage used once per slice of the set) ──
+        //    p and p + 2 of every k-block ──
         if constexpr (!w_smem(WT)) {
             const int di = deq_index(warp);
             const int set = di >> 2;
@@ -824,7 +743,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             bool ok = true;
             // This warp's TMEM lane quarter holds its 32 weight rows of every A stage.
             const uint32_t a_lane = tmem_base + ((uint32_t)(32 * (warp & 3)) << 16) + kTmemA;
-            const uint32_t min_lane = tmem_base + ((uint32_t)(32 * (warp & 3)) << 16) + kTmemMin + 8 * set;
             // The stage's tcgen05.st have completed; order them before the arrival the MMA
             // issuer waits on (no shared memory, so no proxy fence).
             auto publish = [&](int st) {
@@ -843,6 +761,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 if (okb) (void)mbar_try_wait(bar, parity);
                 return okb;
             };
+            auto wait_a = [&](int ia) {
+                return wait_warp(&empty_a[ia % NA], ((ia / NA) & 1) ^ 1, kErrTimeout + 7);
+            };
             const int n_units = S.u1 - S.u0;
             for (int u = S.u0; u < S.u1 && ok;) {
                 const Seg g = make_seg(S, u, S.u1);
@@ -854,78 +775,43 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         if (!ok) break;
                     }
                     const uint8_t *R = raw + rs * RSB + (rit % CPR) * RAWB;
-                    // this set's k-slices of the k-block: set and set + 2, each in two halves of
-                    // 32 k (stages 2 set and 2 set + 1).  XS = 2: f16 hi (16 columns), E4M3 hi
-                    // 2^-10 and E4M3 lo (8 columns each, at 16 and 24); XS = 1: f16 hi and f16
-                    // lo (16 columns each, at 0 and 16).
+                    // this set's k-slices of the k-block: set and set + 2, both into A stage
+                    // `set`; each slice in two halves of 32 k.  XS = 2: f16 hi (16 columns per
+                    // half), E4M3 hi 2^-10 and E4M3 lo (8 columns per half each, at 32 and 48);
+                    // XS = 1: f16 hi and f16 lo (16 columns per half each, at 0 and 32).
                     using Half = typename std::conditional<XS == 2, HalfCorr, HalfSplit>::type;
                     [[maybe_unused]] Q4KMeta m4;
-                    [[maybe_unused]] Q4XMeta mx;
                     [[maybe_unused]] Q6KMeta m6;
-                    [[maybe_unused]] Q6XMeta m6x;
-                    if constexpr (MIN) q4x_load_meta(R, r, set, p.wscale, mx);
-                    else if constexpr (WT == W_Q4K) q4k_load_meta(R, r, set, p.wscale, m4);
-                    if constexpr (WT == W_Q6K && XS == 2) q6x_load_meta(R, r, set, p.wscale, m6x);
-                    else if constexpr (WT == W_Q6K) q6k_load_meta(R, r, set, p.wscale, m6);
-                    // XS = 2: f16 arithmetic (dequant.cuh) on quant words loaded one half slice
-                    // ahead (load_words before the wait for the current half's stage, so the
-                    // shared-memory latency hides behind it); XS = 1: f32, loading as it goes.
-                    auto load_words = [&](int hs, int hh, HalfWords &q) {
+                    if constexpr (WT == W_Q4K) q4k_load_meta(R, r, set, p.wscale, m4);
+                    if constexpr (WT == W_Q6K) q6k_load_meta(R, r, set, p.wscale, m6);
+                    auto deq = [&](int hs, int hh, Half &o) {
                         const int sl = set + 2 * hs;
-                        if constexpr (MIN) q4x_load(R, r, sl, q);  // both halves of the slice
-                        else if constexpr (WT == W_Q6K && XS == 2) q6x_load(R, r, sl, hh, q);
-                        else if constexpr (WT == W_Q80 && XS == 2) q8x_load(R, r, sl, hh, q);
-                    };
-                    auto deq = [&](int hs, int hh, const HalfWords &q, Half &o) {
-                        const int sl = set + 2 * hs;
-                        if constexpr (MIN) q4x_half(q, hh, mx.sc[2 * hs + hh], mx.d2, o);
-                        else if constexpr (WT == W_Q6K && XS == 2)
-                            q6x_half(q, sl, hh, m6x.dsh[4 * hs + 2 * hh], m6x.dsl[4 * hs + 2 * hh], m6x.dsh[4 * hs + 2 * hh + 1],
-                                     m6x.dsl[4 * hs + 2 * hh + 1], o);
-                        else if constexpr (WT == W_Q80 && XS == 2) q8x_half(q, p.wscale, o);
-                        else if constexpr (WT == W_Q4K) q4k_half(R, r, sl, hh, m4.dsc[2 * hs + hh], m4.nm[2 * hs + hh], o);
+                        if constexpr (WT == W_Q4K) q4k_half(R, r, sl, hh, m4.dsc[2 * hs + hh], m4.nm[2 * hs + hh], o);
                         else if constexpr (WT == W_Q6K)
                             q6k_half(R, r, sl, hh, m6.ds[4 * hs + 2 * hh], m6.ds[4 * hs + 2 * hh + 1], o);
                         else q80_half(R, r, sl, hh, p.wscale, o);
                     };
-                    auto store = [&](uint32_t at, const Half &o) {
-                        tmem_st16(at, o.hi);
+                    auto store = [&](uint32_t at, int hh, const Half &o) {
+                        tmem_st16(at + 16 * hh, o.hi);
                         if constexpr (XS == 2) {
-                            tmem_st8(at + 16, o.ch);
-                            tmem_st8(at + 24, o.cl);
+                            tmem_st8(at + kTmemALo + 8 * hh, o.ch);
+                            tmem_st8(at + kTmemALo + 16 + 8 * hh, o.cl);
                         } else {
-                            tmem_st16(at + 16, o.lo);
+                            tmem_st16(at + kTmemALo + 16 * hh, o.lo);
                         }
                     };
-                    HalfWords qw{}, qn{};
-                    load_words(0, 0, qw);
 #pragma unroll
                     for (int hs = 0; hs < 2; hs++) {
-                        const int use = 2 * rit + hs;  // this set's slices so far
-#pragma unroll
-                        for (int hh = 0; hh < 2; hh++) {
-                            const int st = 2 * set + hh;
-                            const int un = 2 * hs + hh + 1;  // next unit (Q4_K: a slice's words serve both halves)
-                            if (un < 4 && !(MIN && (un & 1))) load_words(un >> 1, un & 1, qn);
-                            Half o;
-                            deq(hs, hh, qw, o);
-                            if (un < 4 && !(MIN && (un & 1))) qw = qn;
-                            // the MMA of this stage's previous half slice has completed
-                            if (!(ok = wait_warp(&empty_a[st], (use & 1) ^ 1, kErrTimeout + 7))) break;
-                            tc_fence_after();
-                            store(a_lane + (uint32_t)(st * kTmemAStage), o);
-                            if constexpr (MIN) {
-                                // the set's half of the k-block's min operand, with its last half slice
-                                // (the min MMA of the previous k-block completed before the wait above)
-                                if (hs == 1 && hh == 1) {
-                                    uint32_t mo[8];
-                                    q4x_min(mx, mo);
-                                    tmem_st8(min_lane, mo);
-                                }
-                            }
-                            publish(st);
-                        }
-                        if (!ok) break;
+                        const int ia = 4 * rit + set + 2 * hs;
+                        const uint32_t at = a_lane + (uint32_t)(set * kTmemAStage);
+                        Half o;
+                        deq(hs, 0, o);
+                        if (!(ok = wait_a(ia))) break;
+                        tc_fence_after();  // after the MMA that read this stage
+                        store(at, 0, o);
+                        deq(hs, 1, o);
+                        store(at, 1, o);
+                        publish(set);
                     }
                     __syncwarp();
                     if (lane == 0 && (rit % CPR == CPR - 1 || rit == n_units - 1)) mbar_arrive(&raw_empty[rs]);
@@ -948,7 +834,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const int half = epi_half(warp);
         const int et = half * 128 + q * 32 + lane;  // 0..255
         const int tid_h = q * 32 + lane;            // 0..127 within the half
-        float *my_esum = s_esum + half * 64;
+        uint8_t *my_stage = epi_stage + half * kEpiStageBytes;
         int si = 0;
         bool ok = true;
         const int first_ot = S.begin_of(pair) / S.kb;
@@ -958,10 +844,31 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(acc_empty0 + 8 * acc);
         };
+        // token positions of the token group starting at m0 (QKV cache rows and RoPE angles,
+        // logits rows), loaded once per group: the first group's while the MMAs run
+        int pos_m0 = -1;
+        auto load_pos = [&](int m0, int ntok) {
+            if constexpr (EPI == EPI_QKV || EPI == EPI_LOGITS) {
+                if (m0 == pos_m0) return;
+                named_bar_sync(1, kEpiThreads);  // earlier readers are done
+                for (int t = et; t < ntok; t += kEpiThreads) {
+                    s_pos[t] = p.epi.pos[m0 + t];
+                    if constexpr (EPI == EPI_QKV) s_rpos[t] = p.epi.rope_pos[m0 + t];
+                }
+                named_bar_sync(1, kEpiThreads);
+                pos_m0 = m0;
+            }
+        };
+        if (S.u0 < S.u1) {
+            const Seg g0 = make_seg(S, S.u0, S.u1);
+            load_pos(g0.m0, g0.ntok);
+        }
         for (int u = S.u0; u < S.u1 && ok;) {
             const Seg g = make_seg(S, u, S.u1);
             const int tile = 2 * g.pt + (int)rank;
             const int acc = S.acc_of(si);
+            const bool whole = g.k0 == 0 && g.k1 == S.kb;
+            if (whole) load_pos(g.m0, g.ntok);
             // one thread waits, the barrier hands the outcome to the whole group
             if (et == 0) *okflag = mbar_wait(&acc_full[acc], S.acc_uses(si) & 1, abort_flag, p.err, kErrTimeout + 8, p.timeout_ns) ? 1 : 0;
             named_bar_sync(1, kEpiThreads);
@@ -969,48 +876,36 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             if (!ok) break;
             tc_fence_after();
             const uint32_t taddr = tmem_base + ((uint32_t)(32 * q) << 16) + acc * kDblTok;
-            const bool whole = g.k0 == 0 && g.k1 == S.kb;
+            // the next chunk's TMEM load is in flight while this chunk is handled
+            uint32_t u16[16];
+            if (16 * half < g.nmma) tmem_ld16(taddr + 16 * half, u16);
             if (whole) {
                 const EpiRow er = epi_row<EPI>(p.epi, tile, row);
                 const EpiDst dd = epi_dst<EPI>(p.epi, tile);
-                if constexpr (EPI == EPI_QKV || EPI == EPI_LOGITS) {
-                    for (int t = et; t < g.ntok; t += kEpiThreads) {
-                        s_pos[t] = p.epi.pos[g.m0 + t];
-                        if constexpr (EPI == EPI_QKV) s_rpos[t] = p.epi.rope_pos[g.m0 + t];
-                    }
-                    named_bar_sync(1, kEpiThreads);
-                }
-                // the next chunk's TMEM load is in flight while this chunk is stored
-                uint32_t u16[16];
-                if (16 * half < g.nmma) tmem_ld16(taddr + 16 * half, u16);
                 for (int c0 = 16 * half; c0 < g.nmma; c0 += 32) {
                     tmem_ld_wait(u16);
                     float v[16];
 #pragma unroll
                     for (int i = 0; i < 16; i++) v[i] = __uint_as_float(u16[i]);
                     if (c0 + 32 < g.nmma) tmem_ld16(taddr + c0 + 32, u16);
-                    epi_store<EPI>(p.epi, er, dd, s_pos, s_rpos, g.m0, c0, g.ntok, v, my_esum);
-                    if constexpr (EPI == EPI_SWIGLU) {  // combine the lane quarters' partial sums
-                        named_bar_sync(2 + half, kEpiThreads / 2);
-                        epi_sums<EPI>(p.epi, tile, g.m0, c0, g.ntok, my_esum, tid_h);
-                        named_bar_sync(2 + half, kEpiThreads / 2);
-                    }
+                    epi_values<EPI>(p.epi, er, s_rpos, c0, g.ntok, v, my_stage);
+                    named_bar_sync(2 + half, kEpiThreads / 2);
+                    epi_copyout<EPI>(dd, s_pos, g.m0, c0, g.ntok, my_stage, tid_h);
+                    named_bar_sync(2 + half, kEpiThreads / 2);
                 }
                 release_acc(acc);
             } else {
                 const int slot = g.ot == first_ot ? 0 : 1;
                 float *wsl = p.ws + ((size_t)blockIdx.x * 2 + slot) * kWsTile;
-                uint32_t u16[16];
-                if (16 * half < g.nmma) tmem_ld16(taddr + 16 * half, u16);
                 for (int c0 = 16 * half; c0 < g.nmma; c0 += 32) {
                     tmem_ld_wait(u16);
-                    uint4 q[4];
+                    uint4 qv[4];
 #pragma unroll
-                    for (int j = 0; j < 4; j++) q[j] = make_uint4(u16[4 * j], u16[4 * j + 1], u16[4 * j + 2], u16[4 * j + 3]);
+                    for (int j = 0; j < 4; j++) qv[j] = make_uint4(u16[4 * j], u16[4 * j + 1], u16[4 * j + 2], u16[4 * j + 3]);
                     if (c0 + 32 < g.nmma) tmem_ld16(taddr + c0 + 32, u16);
                     float *dst = wsl + (size_t)c0 * 128 + row * 4;  // column group c0/4, this row
 #pragma unroll
-                    for (int j = 0; j < 4; j++) *reinterpret_cast<uint4 *>(dst + j * 512) = q[j];
+                    for (int j = 0; j < 4; j++) *reinterpret_cast<uint4 *>(dst + j * 512) = qv[j];
                 }
                 // the accumulator is in registers / on its way to the workspace
                 release_acc(acc);
@@ -1020,110 +915,166 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 if (slot == 0) split_u0 = u;
                 else split_u1 = u;
             }
-            named_bar_sync(1, kEpiThreads);  // okflag / s_pos are reused by the next segment
+            named_bar_sync(1, kEpiThreads);  // okflag is reused by the next segment
             si++;
             u += g.k1 - g.k0;
         }
 
         // ── deferred split-tile fixups: every MMA of this CTA has completed, so the rings
-        //    (everything below the barriers) are free for staging ──
-        constexpr int kStageBytes = AR + BRING + NRAW * RSB + min_ring_bytes(WT, XS);
+        //    (everything below the barriers) are free for staging.  Both split tiles (the
+        //    pair's first and last) are waited for together and, when this contributor's
+        //    shares of both fit, staged by one round of bulk copies. ──
+        constexpr int kStageBytes = AR + BRING + NRAW * RSB;
         constexpr int kChunkBytes = 16 * 128 * 4;  // one 16-column chunk of one partial
-        const float *sbuf = reinterpret_cast<const float *>(smem);
-        uint32_t fix_phase = 0;
-        for (int i = 0; i < 2 && ok; i++) {
+        struct Fix {
+            Seg g;
+            int nc, ch0, ch1, me;
+        };
+        Fix fx[2];
+        int nfx = 0;
+        for (int i = 0; i < 2; i++) {
             const int su = i == 0 ? split_u0 : split_u1;
             if (su < 0) continue;
-            const Seg g = make_seg(S, su, S.u1);
-            const int tile = 2 * g.pt + (int)rank;
-            const int c_first = S.owner(g.ot * S.kb), c_last = S.owner((g.ot + 1) * S.kb - 1);
-            const int nc = c_last - c_first + 1, me = pair - c_first;
-            const int nch = g.nmma >> 4;
-            const int ch0 = me * nch / nc, ch1 = (me + 1) * nch / nc;
-            int *cntp = p.tile_cnt + 2 * g.ot + rank;
-            if (et < nc && et < kMaxContrib) {
+            Fix &f = fx[nfx++];
+            f.g = make_seg(S, su, S.u1);
+            const int c_first = S.owner(f.g.ot * S.kb), c_last = S.owner((f.g.ot + 1) * S.kb - 1);
+            f.nc = c_last - c_first + 1;
+            f.me = pair - c_first;
+            const int nch = f.g.nmma >> 4;
+            f.ch0 = f.me * nch / f.nc;
+            f.ch1 = (f.me + 1) * nch / f.nc;
+            if (et < f.nc && et < kMaxContrib) {
                 const int c = c_first + et;
-                const int sl = (S.begin_of(c) / S.kb == g.ot) ? 0 : 1;
-                s_contrib[et] = ((long long)(2 * c + (int)rank) * 2 + sl) * kWsTile;
+                const int sl = (S.begin_of(c) / S.kb == f.g.ot) ? 0 : 1;
+                s_contrib[(nfx - 1) * kMaxContrib + et] = ((long long)(2 * c + (int)rank) * 2 + sl) * kWsTile;
             }
-            if constexpr (EPI == EPI_QKV || EPI == EPI_LOGITS) {
-                for (int t = et; t < g.ntok; t += kEpiThreads) {
-                    s_pos[t] = p.epi.pos[g.m0 + t];
-                    if constexpr (EPI == EPI_QKV) s_rpos[t] = p.epi.rope_pos[g.m0 + t];
-                }
-            }
+        }
+        if (nfx > 0 && ok) {
             if (et == 0) {
-                int okw = nc <= kMaxContrib;  // the launcher keeps nc <= kMaxContrib
-                if (!okw) atomicCAS(p.err, 0, kErrTimeout + 9);
-                else okw = wait_count(cntp, nc, abort_flag, p.err, kErrTimeout + 13, p.timeout_ns);
+                int okw = 1;
+                for (int i = 0; i < nfx && okw; i++) {
+                    if (fx[i].nc > kMaxContrib) {  // the launcher keeps nc <= kMaxContrib
+                        atomicCAS(p.err, 0, kErrTimeout + 9);
+                        okw = 0;
+                    } else {
+                        okw = wait_count(p.tile_cnt + 2 * fx[i].g.ot + rank, fx[i].nc, abort_flag, p.err, kErrTimeout + 13,
+                                         p.timeout_ns);
+                    }
+                }
                 *okflag = okw;
                 if (okw) fence_proxy_async_all();  // the partials, seen here, before the bulk reads
             }
             named_bar_sync(1, kEpiThreads);
             ok = *okflag != 0;
-            if (!ok) break;
+        }
+        // Staged rounds (a fix's chunk range in pieces of at most half the staging area),
+        // double-buffered: the copies of round k + 1 land while round k is summed.  A fix
+        // whose contributors' chunk does not fit half the area reads the workspace directly.
+        constexpr int kHalfStage = (kStageBytes / 2) & ~1023;
+        const float *sbuf = reinterpret_cast<const float *>(smem);
+        auto staged_fix = [&](int i) { return fx[i].nc * kChunkBytes <= kHalfStage; };
+        auto per_round = [&](int i) { return kHalfStage / (fx[i].nc * kChunkBytes); };
+        // bulk copies of chunks [r0, r0 + nr) of every contributor of fix i into smem + off
+        auto stage_chunks = [&](int i, int r0, int nr, size_t off, uint64_t *bar) {
+            mbar_arrive_expect_tx(bar, (uint32_t)(fx[i].nc * nr * kChunkBytes));
+            for (int c = 0; c < fx[i].nc; c++)
+                bulk_g2s(smem + off + (size_t)c * nr * kChunkBytes, p.ws + s_contrib[i * kMaxContrib + c] + (size_t)r0 * 2048,
+                         (uint32_t)(nr * kChunkBytes), bar);
+        };
+        // sum and finish chunks [r0, r0 + nr) of fix i, staged at smem + off (or read from the
+        // workspace when not staged)
+        auto finish_chunks = [&](int i, int r0, int nr, bool staged, size_t off) {
+            const Fix &f = fx[i];
+            const int tile = 2 * f.g.pt + (int)rank;
             const EpiRow er = epi_row<EPI>(p.epi, tile, row);
             const EpiDst dd = epi_dst<EPI>(p.epi, tile);
-            const bool staged = nc * kChunkBytes <= kStageBytes;
-            const int per_round = staged ? kStageBytes / (nc * kChunkBytes) : 1;
-            for (int r0 = ch0; r0 < ch1; r0 += per_round) {
-                const int nr = min(ch1, r0 + per_round) - r0;
-                if (staged) {
-                    if (et == 0) {
-                        mbar_arrive_expect_tx(fix_bar, (uint32_t)(nc * nr * kChunkBytes));
-                        for (int c = 0; c < nc; c++)
-                            bulk_g2s(smem + (size_t)c * nr * kChunkBytes, p.ws + s_contrib[c] + (size_t)r0 * 2048,
-                                     (uint32_t)(nr * kChunkBytes), fix_bar);
-                        *okflag = mbar_wait(fix_bar, fix_phase, abort_flag, p.err, kErrTimeout + 10, p.timeout_ns) ? 1 : 0;
+            const float *base = sbuf + off / 4;
+            for (int ch = r0 + half; ch < r0 + nr; ch += 2) {
+                float v[16];
+#pragma unroll
+                for (int k = 0; k < 16; k++) v[k] = 0.f;
+                for (int c = 0; c < f.nc; c++) {
+                    float4 t[4];
+                    if (staged) {
+                        const float4 *src = reinterpret_cast<const float4 *>(base + ((size_t)c * nr + (ch - r0)) * 2048 + row * 4);
+#pragma unroll
+                        for (int j = 0; j < 4; j++) t[j] = src[j * 128];
+                    } else {
+                        const float4 *src =
+                            reinterpret_cast<const float4 *>(p.ws + s_contrib[i * kMaxContrib + c] + (size_t)ch * 2048 + row * 4);
+#pragma unroll
+                        for (int j = 0; j < 4; j++) t[j] = __ldcg(src + j * 128);
                     }
-                    fix_phase ^= 1;
-                    named_bar_sync(1, kEpiThreads);
-                    if (!*okflag) { ok = false; break; }
-                }
-                for (int ch = r0 + half; ch < r0 + nr; ch += 2) {
-                    float v[16];
 #pragma unroll
-                    for (int k = 0; k < 16; k++) v[k] = 0.f;
-                    for (int c = 0; c < nc; c++) {
-                        float4 t[4];
-                        if (staged) {
-                            const float4 *src =
-                                reinterpret_cast<const float4 *>(sbuf + ((size_t)c * nr + (ch - r0)) * 2048 + row * 4);
-#pragma unroll
-                            for (int j = 0; j < 4; j++) t[j] = src[j * 128];
-                        } else {
-                            const float4 *src = reinterpret_cast<const float4 *>(p.ws + s_contrib[c] + (size_t)ch * 2048 + row * 4);
-#pragma unroll
-                            for (int j = 0; j < 4; j++) t[j] = __ldcg(src + j * 128);
-                        }
-#pragma unroll
-                        for (int j = 0; j < 4; j++) {
-                            v[4 * j] += t[j].x;
-                            v[4 * j + 1] += t[j].y;
-                            v[4 * j + 2] += t[j].z;
-                            v[4 * j + 3] += t[j].w;
-                        }
-                    }
-                    epi_store<EPI>(p.epi, er, dd, s_pos, s_rpos, g.m0, ch * 16, g.ntok, v, my_esum);
-                    if constexpr (EPI == EPI_SWIGLU) {
-                        named_bar_sync(2 + half, kEpiThreads / 2);
-                        epi_sums<EPI>(p.epi, tile, g.m0, ch * 16, g.ntok, my_esum, tid_h);
-                        named_bar_sync(2 + half, kEpiThreads / 2);
+                    for (int j = 0; j < 4; j++) {
+                        v[4 * j] += t[j].x;
+                        v[4 * j + 1] += t[j].y;
+                        v[4 * j + 2] += t[j].z;
+                        v[4 * j + 3] += t[j].w;
                     }
                 }
-                // staged chunks consumed before the next round's copies; generic reads of the
+                epi_values<EPI>(p.epi, er, s_rpos, ch * 16, f.g.ntok, v, my_stage);
+                named_bar_sync(2 + half, kEpiThreads / 2);
+                epi_copyout<EPI>(dd, s_pos, f.g.m0, ch * 16, f.g.ntok, my_stage, tid_h);
+                named_bar_sync(2 + half, kEpiThreads / 2);
+            }
+        };
+        if (ok && nfx > 0) {
+            // round cursors (fix, first chunk) over the staged fixes: next to issue, next to sum
+            auto skip = [&](int &i, int &r) {
+                while (i < nfx && (r >= fx[i].ch1 || !staged_fix(i))) {
+                    if (++i < nfx) r = fx[i].ch0;
+                }
+            };
+            int ii = 0, ir = fx[0].ch0, ci = 0, cr = fx[0].ch0;
+            skip(ii, ir);
+            skip(ci, cr);
+            uint32_t ph[2] = {0, 0};
+            int pend[2] = {0, 0};  // rounds issued into each buffer and not yet waited for
+            auto issue = [&](int b) {
+                const int nr = min(fx[ii].ch1, ir + per_round(ii)) - ir;
+                if (et == 0) stage_chunks(ii, ir, nr, (size_t)b * kHalfStage, b ? fix_bar2 : fix_bar);
+                pend[b]++;
+                ir += nr;
+                skip(ii, ir);
+            };
+            if (ii < nfx) issue(0);
+            for (int k = 0; ci < nfx && ok; k++) {
+                const int b = k & 1;
+                const int nr = min(fx[ci].ch1, cr + per_round(ci)) - cr;
+                // the other buffer's last round was summed (barrier and proxy fence below)
+                if (ii < nfx) issue(b ^ 1);
+                if (et == 0) *okflag = mbar_wait(b ? fix_bar2 : fix_bar, ph[b], abort_flag, p.err, kErrTimeout + 10, p.timeout_ns) ? 1 : 0;
+                named_bar_sync(1, kEpiThreads);
+                if (!*okflag) { ok = false; break; }
+                ph[b] ^= 1;
+                pend[b]--;
+                load_pos(fx[ci].g.m0, fx[ci].g.ntok);
+                finish_chunks(ci, cr, nr, true, (size_t)b * kHalfStage);
+                // staged chunks consumed before the buffer's next copies; generic reads of the
                 // staging area before the async-proxy writes
                 named_bar_sync(1, kEpiThreads);
                 if (et == 0) fence_proxy_async_smem();
+                cr += nr;
+                skip(ci, cr);
             }
-            if (!ok) break;
+            // after an abort: the copies in flight land before the CTA can exit
+            if (!ok && et == 0)
+                for (int b = 0; b < 2; b++)
+                    if (pend[b] > 0) spin_bounded(b ? fix_bar2 : fix_bar, ph[b]);
+            for (int i = 0; i < nfx && ok; i++) {
+                if (staged_fix(i) || fx[i].ch1 <= fx[i].ch0) continue;
+                load_pos(fx[i].g.m0, fx[i].g.ntok);
+                finish_chunks(i, fx[i].ch0, fx[i].ch1 - fx[i].ch0, false, 0);
+            }
             // departure: the last of the nc contributors resets the counter for the next launch
-            if (et == 0) {
-                const int old = atomicAdd(cntp, 1);
-                if (old == 2 * nc - 1) *cntp = 0;
+            if (ok && et == 0) {
+                for (int i = 0; i < nfx; i++) {
+                    int *cntp = p.tile_cnt + 2 * fx[i].g.ot + rank;
+                    const int old = atomicAdd(cntp, 1);
+                    if (old == 2 * fx[i].nc - 1) *cntp = 0;
+                }
             }
-            named_bar_sync(1, kEpiThreads);  // s_contrib / s_pos / okflag reused
-            si++;
         }
     }
 

@@ -189,8 +189,7 @@ __device__ __forceinline__ float block_sum(float v, float *red) {
 // thread step (float4 loads); d is a multiple of 64.
 __global__ void __launch_bounds__(256) rmsnorm_kernel(float *__restrict__ x, const float *__restrict__ y,
                                                       const float *__restrict__ w, int d, float eps,
-                                                      const int *__restrict__ cnt, uint8_t *__restrict__ h,
-                                                      uint8_t *__restrict__ sums, int ld_sums) {
+                                                      const int *__restrict__ cnt, uint8_t *__restrict__ h) {
     __shared__ float red[33];
     griddep_launch_dependents();
     griddep_wait();  // x, y and the row count come from the previous kernels
@@ -199,7 +198,6 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(float *__restrict__ x, con
     float *xr = x + (size_t)a * d;
     const float *yr = y ? y + (size_t)a * d : nullptr;
     uint8_t *hr = h + (size_t)a * 4 * d;
-    uint8_t *sr = sums + (size_t)a * ld_sums;
     float ss = 0.f;
     for (int i = threadIdx.x * 8; i < d; i += blockDim.x * 8) {
         float4 v0 = *reinterpret_cast<const float4 *>(xr + i);
@@ -225,12 +223,6 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(float *__restrict__ x, con
         const float v[8] = {(v0.x * scale) * w0.x, (v0.y * scale) * w0.y, (v0.z * scale) * w0.z, (v0.w * scale) * w0.w,
                             (v1.x * scale) * w1.x, (v1.y * scale) * w1.y, (v1.z * scale) * w1.z, (v1.w * scale) * w1.w};
         store_pair8(hr, i, v);
-        // sub-block sum of 32 values: four consecutive threads (d % 32 == 0, so whole groups are active)
-        float ps = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
-        const unsigned am = __activemask();
-        ps += __shfl_xor_sync(am, ps, 1);
-        ps += __shfl_xor_sync(am, ps, 2);
-        if ((threadIdx.x & 3) == 0) store_sum(sr, i >> 5, ps);
     }
 }
 
@@ -649,9 +641,7 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const float *__r
     }
 }
 
-// ld_sums: bytes per sums row.  K % 32 == 0: the four threads of a sub-block are active together.
-__global__ void f32_to_pair_kernel(const float *__restrict__ x, uint8_t *__restrict__ y, int rows, int K,
-                                   uint8_t *__restrict__ sums, int ld_sums) {
+__global__ void f32_to_pair_kernel(const float *__restrict__ x, uint8_t *__restrict__ y, int rows, int K) {
     const size_t groups = (size_t)rows * (K / 8);
     for (size_t g = blockIdx.x * (size_t)blockDim.x + threadIdx.x; g < groups; g += (size_t)gridDim.x * blockDim.x) {
         const size_t r = g / (K / 8);
@@ -660,11 +650,6 @@ __global__ void f32_to_pair_kernel(const float *__restrict__ x, uint8_t *__restr
 #pragma unroll
         for (int e = 0; e < 8; e++) v[e] = x[r * K + i + e];
         store_pair8(y + r * 4 * K, i, v);
-        float ps = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
-        const unsigned am = __activemask();
-        ps += __shfl_xor_sync(am, ps, 1);
-        ps += __shfl_xor_sync(am, ps, 2);
-        if ((g & 3) == 0) store_sum(sums + r * ld_sums, i >> 5, ps);
     }
 }
 

@@ -260,41 +260,6 @@ __device__ __forceinline__ void mma2_f8_ts_k128(uint32_t d_tmem, uint32_t a_tmem
         "r"(a_tmem), "l"(bdesc), "r"(idesc)
         : "memory");
 }
-// D[tmem] += A * B^T, kind::f16, K = 32 (two steps of 16): A from TMEM (8 columns per
-// step), B from shared memory (descriptor advanced by 32 bytes per step).
-__device__ __forceinline__ void mma2_f16_ts_k32(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc) {
-    asm volatile(
-        "{\n\t.reg .pred p1;\n\t.reg .b32 a1;\n\t.reg .b64 b1;\n\t"
-        "setp.eq.b32 p1, %3, %3;\n\t"
-        "add.u32 a1, %1, 8;\n\tadd.u64 b1, %2, 2;\n\t"
-        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p1;\n\t"
-        "tcgen05.mma.cta_group::2.kind::f16 [%0], [a1], b1, %3, p1;\n\t}" ::"r"(d_tmem),
-        "r"(a_tmem), "l"(bdesc), "r"(idesc)
-        : "memory");
-}
-// Half a k-slice: D += A * B^T over K = 32, kind::f16 (two steps of 16, A 8 TMEM columns
-// per step, B descriptor advanced by 32 bytes per step); accumulate = 0 overwrites D.
-__device__ __forceinline__ void mma2_f16_ts_h32(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
-                                                uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p0, p1;\n\t.reg .b32 a1;\n\t.reg .b64 b1;\n\t"
-        "setp.ne.b32 p0, %4, 0;\n\t"
-        "setp.eq.b32 p1, %4, %4;\n\t"
-        "add.u32 a1, %1, 8;\n\tadd.u64 b1, %2, 2;\n\t"
-        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p0;\n\t"
-        "tcgen05.mma.cta_group::2.kind::f16 [%0], [a1], b1, %3, p1;\n\t}" ::"r"(d_tmem),
-        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-// D += A * B^T, kind::f8f6f4 (E4M3), K = 32: one instruction, A 8 TMEM columns.
-__device__ __forceinline__ void mma2_f8_ts_k32(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc) {
-    asm volatile(
-        "{\n\t.reg .pred p1;\n\t"
-        "setp.eq.b32 p1, %3, %3;\n\t"
-        "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], [%1], %2, %3, p1;\n\t}" ::"r"(d_tmem),
-        "r"(a_tmem), "l"(bdesc), "r"(idesc)
-        : "memory");
-}
 // Same with A from shared memory (128 bytes per row: descriptor advanced by 32 bytes per step).
 __device__ __forceinline__ void mma2_f8_ss_k128(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc) {
     asm volatile(
@@ -386,17 +351,6 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t smem_addr) {
     d |= (uint64_t)(1024 >> 4) << 32;              // SBO
     d |= (uint64_t)1 << 46;                        // version
     d |= (uint64_t)2 << 61;                        // SWIZZLE_128B
-    return d;
-}
-// Shared-memory matrix descriptor, K-major, 64-byte swizzle (rows of 64 bytes, 8-row
-// groups 512 bytes apart), as a TMA load with CU_TENSOR_MAP_SWIZZLE_64B writes it.
-__device__ __forceinline__ uint64_t sw64_desc(uint32_t smem_addr) {
-    uint64_t d = 0;
-    d |= (uint64_t)((smem_addr & 0x3FFFF) >> 4);  // start address
-    d |= (uint64_t)1 << 16;                        // LBO (unused for swizzled K-major)
-    d |= (uint64_t)(512 >> 4) << 32;               // SBO
-    d |= (uint64_t)1 << 46;                        // version
-    d |= (uint64_t)4 << 61;                        // SWIZZLE_64B
     return d;
 }
 // Instruction descriptor: kind::f16, A/B f16, D f32, both K-major, M=m, N=n.
