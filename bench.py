@@ -269,17 +269,21 @@ def layer_probe(args):
     `--warmup` untimed forwards, then `--steps` forwards with the engine's per-launch
     CUDA-event profiler on; prints calls, average launch time, TFLOP/s and algorithmic
     GB/s per kernel class.  Launch order of one forward: embed, norm, QKV GEMM, attention,
-    output GEMM, norm, gate/up GEMM, down GEMM (Q6_K: first FFN), final norm, lm_head."""
+    output GEMM, norm, gate/up GEMM, down GEMM (Q6_K: first FFN), final norm, lm_head.
+    --probe-vocab sets the vocabulary (126464: LLaDA-8B's, so the sampler kernels read
+    full-size logits rows); --probe-generate then runs one denoising step of a ROWS-token
+    block (the sampler kernels: candidate statistics, commit) after the forwards."""
     import ctypes as C
     pkg = load_pkg()
     os.environ.setdefault("DIFFUSE_LOG_LEVEL", "0")
     work = pathlib.Path(os.environ.get("DFB_BENCH_DIR", tempfile.gettempdir())) / "dfb_bench"
     work.mkdir(parents=True, exist_ok=True)
     arch = pkg.DREAM_7B if args.probe_arch == "dream" else pkg.LLADA_8B
-    path = work / f"{args.probe_arch}_q4_k_m_1layer_v16384.gguf"
+    V = args.probe_vocab
+    path = work / f"{args.probe_arch}_q4_k_m_1layer_v{V}.gguf"
     if not path.exists():
         tmp = path.with_suffix(".tmp")
-        pkg.synth_model(tmp, arch, "q4_k_m", seed=0, n_layer=1, n_vocab=16384)
+        pkg.synth_model(tmp, arch, "q4_k_m", seed=0, n_layer=1, n_vocab=V)
         tmp.rename(path)
     model = pkg.Model(str(path))
     M = args.layer_probe
@@ -290,7 +294,7 @@ def layer_probe(args):
         _fields_ = [("calls", C.c_int32), ("ms", C.c_double), ("flops", C.c_double), ("bytes", C.c_double)]
     dfb.dfb_ctx_profile.argtypes = [C.c_void_p, C.c_int]
     dfb.dfb_ctx_profile_read.argtypes = [C.c_void_p, C.c_void_p, C.c_int]
-    toks = np.random.default_rng(0).integers(0, 16000, M).astype(np.int32)
+    toks = np.random.default_rng(0).integers(0, min(V, 16000), M).astype(np.int32)
     for _ in range(args.warmup):
         ctx.forward(toks)
     dfb.dfb_ctx_profile(ctx.engine, 1)
@@ -304,6 +308,12 @@ def layer_probe(args):
         if p.calls:
             print(f"rows {M:4d} {n:9s} calls {p.calls:4d} avg {p.ms / p.calls * 1e3:8.1f} us "
                   f"{p.flops / (p.ms * 1e-3) / 1e12:7.1f} TFLOP/s {p.bytes / (p.ms * 1e-3) / 1e9:7.1f} GB/s", flush=True)
+    if args.probe_generate:
+        P = 16
+        hp = model.hparams
+        prompt = np.random.default_rng(1).integers(0, min(hp.mask_token_id, V) - 1, P).astype(np.int32)
+        out, tr = ctx.generate(prompt, M - P, pkg.SamplerParams(n_steps=1, remasking=0, use_cache=0), trace=True)
+        print(f"generate: one step over {M} rows, {int(tr['n_unmasked'][0])} committed, {float(tr['step_ms'][0]):.3f} ms", flush=True)
     ctx.close()
     model.close()
     return 0
@@ -337,6 +347,8 @@ def main():
     ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--probe-arch", default="llada", choices=["llada", "dream"])
+    ap.add_argument("--probe-vocab", type=int, default=16384)
+    ap.add_argument("--probe-generate", action="store_true")
     ap.add_argument("--layer-probe", type=int, default=0, metavar="ROWS",
                     help="profiling case instead of the benchmark: forwards of ROWS tokens through one "
                          "LLaDA-8B-width Q4_K_M layer (vocab 16384), per-kernel-class CUDA-event timings")

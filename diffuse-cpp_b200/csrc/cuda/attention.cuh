@@ -34,15 +34,6 @@ namespace dfb {
 
 constexpr int kAttnRows = 32, kAttnKeys = 64, kAttnThreads = 128;
 
-__device__ __forceinline__ void cp_async16(void *dst, const void *src, bool valid) {
-    const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
-    const int sz = valid ? 16 : 0;
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(sz) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-
 template <int HD>
 struct AttnSmem {
     static constexpr int QP = HD + 4;   // Q / K row pitch (floats): conflict-free float4 reads

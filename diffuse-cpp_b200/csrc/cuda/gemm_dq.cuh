@@ -340,8 +340,8 @@ __device__ __forceinline__ EpiDst epi_dst(const EpiArgs &e, int tile) {
 // Epilogue math of 16 consecutive tokens (tl0 .. tl0+15 of the segment) for this lane's
 // row, into the staging rows.  v holds the raw accumulator (pre-scaled weights): the
 // first step multiplies by out_scale.  Called by all 32 lanes of a warp together (paired
-// epilogues exchange values with the neighbouring lane).  s_pos: positions of the
-// segment's tokens (shared memory).
+// epilogues exchange values with the neighbouring lane).  s_rpos: the segment's token
+// positions within their sequences (RoPE angles, shared memory).
 template <int EPI>
 __device__ __forceinline__ void epi_values(const EpiArgs &e, const EpiRow &r, const int *s_rpos, int tl0, int ntok,
                                            float (&v)[16], uint8_t *stage) {
@@ -377,21 +377,26 @@ __device__ __forceinline__ void epi_values(const EpiArgs &e, const EpiRow &r, co
         }
     } else if constexpr (EPI == EPI_QKV) {
         if (r.sec < 2) {
+            // (cos, sin) of this lane's angle, eight tokens at a time (the loads in flight
+            // together, few registers)
             const int hh = e.head_dim >> 1;
-            float2 csv[16];
 #pragma unroll
-            for (int i = 0; i < 16; i++) {
-                const int pp = tl0 + i < ntok ? s_rpos[tl0 + i] : 0;
-                csv[i] = __ldg(e.rope + (size_t)pp * hh + r.ipair);
-            }
+            for (int i8 = 0; i8 < 16; i8 += 8) {
+                float2 csv[8];
 #pragma unroll
-            for (int i = 0; i < 16; i++) {
-                const float2 cs = csv[i];
-                const float x = v[i] + r.bias;
-                const float partner = __shfl_xor_sync(0xffffffffu, x, 1);
-                // ggml_rope_ext NEOX: (x0 cos - x1 sin, x0 sin + x1 cos)
-                const float o = r.bpair == 0 ? (x * cs.x - partner * cs.y) : (partner * cs.y + x * cs.x);
-                if (r.col < 128) reinterpret_cast<float *>(stage + i * RB)[r.col] = o;
+                for (int i = 0; i < 8; i++) {
+                    const int pp = tl0 + i8 + i < ntok ? s_rpos[tl0 + i8 + i] : 0;
+                    csv[i] = __ldg(e.rope + (size_t)pp * hh + r.ipair);
+                }
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    const float2 cs = csv[i];
+                    const float x = v[i8 + i] + r.bias;
+                    const float partner = __shfl_xor_sync(0xffffffffu, x, 1);
+                    // ggml_rope_ext NEOX: (x0 cos - x1 sin, x0 sin + x1 cos)
+                    const float o = r.bpair == 0 ? (x * cs.x - partner * cs.y) : (partner * cs.y + x * cs.x);
+                    if (r.col < 128) reinterpret_cast<float *>(stage + (i8 + i) * RB)[r.col] = o;
+                }
             }
         } else {
 #pragma unroll
@@ -473,8 +478,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     uint8_t *epi_stage = raw + NRAW * RSB;  // [2 halves][kEpiStageBytes]
     uint64_t *bars = reinterpret_cast<uint64_t *>(epi_stage + 2 * kEpiStageBytes);
     uint64_t *full_a = bars, *empty_a = bars + 6, *full_b = bars + 12, *empty_b = bars + 36, *raw_full = bars + 60,
-             *raw_empty = bars + 64, *acc_full = bars + 68, *acc_empty = bars + 70, *drain = bars + 72,
-             *fix_bar = bars + 73, *fix_bar2 = bars + 78;
+             *raw_empty = bars + 64, *acc_full = bars + 68, *acc_empty = bars + 70, *drain = bars + 72;
     uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 74);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 75);
     volatile int *okflag = reinterpret_cast<volatile int *>(bars + 77);
@@ -506,8 +510,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             mbar_init(&acc_empty[i], 2 * kEpiThreads / 32);  // every epilogue warp of both CTAs
         }
         mbar_init(drain, 1);
-        mbar_init(fix_bar, 1);
-        mbar_init(fix_bar2, 1);
         *abort_flag = 0;
         fence_barrier_init();
     }
@@ -823,22 +825,36 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     } else {
         // ── epilogue: thread = TMEM lane = output feature of this CTA's tile ──
         griddep_wait();  // outputs, workspace and counters are the previous kernel's until it completes
-        // A whole tile is finished straight from TMEM.  A split tile's partial goes to
-        // the workspace (f32 [column / 4][row][column % 4], slot 0 for the pair's first
-        // tile, 1 for its last) and its arrival is counted; once every MMA of this CTA is done, each
+        // A whole tile is finished straight from TMEM.  A split tile's partial goes to the
+        // workspace (f32 [column / 4][row][column % 4], slot 0 for the pair's first tile, 1
+        // for its last) and its arrival is counted; once every MMA of this CTA is done, each
         // contributor of a split tile finishes its share of the tile's 16-column chunks,
-        // summing all contributors' partials in contributor order (so the result does
-        // not depend on timing), staged into the drained rings by bulk copies.
+        // summing all contributors' partials in contributor order (so the result does not
+        // depend on timing).  A split segment whose accumulator no later segment reuses stays
+        // in TMEM: only the other contributors' shares go to the workspace, and its own share
+        // is read back from TMEM.
         const int q = warp & 3;
         const int row = 32 * q + lane;
         const int half = epi_half(warp);
         const int et = half * 128 + q * 32 + lane;  // 0..255
         const int tid_h = q * 32 + lane;            // 0..127 within the half
         uint8_t *my_stage = epi_stage + half * kEpiStageBytes;
-        int si = 0;
         bool ok = true;
         const int first_ot = S.begin_of(pair) / S.kb;
-        int split_u0 = -1, split_u1 = -1;  // first units of this CTA's split segments (first, last)
+        int nseg = 0;  // segments of this pair's range
+        for (int u = S.u0; u < S.u1; nseg++) {
+            const Seg g = make_seg(S, u, S.u1);
+            u += g.k1 - g.k0;
+        }
+        // split tiles of this CTA: the pair's first and last tile (when split), with this
+        // contributor's share of their chunks
+        struct Fix {
+            Seg g;
+            int nc, me, ch0, ch1;
+            int tm;  // TMEM column of the resident accumulator, or -1
+        };
+        Fix fx[2];
+        int nfx = 0;
         auto release_acc = [&](int acc) {
             tc_fence_before();
             __syncwarp();
@@ -863,6 +879,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const Seg g0 = make_seg(S, S.u0, S.u1);
             load_pos(g0.m0, g0.ntok);
         }
+        int si = 0;
         for (int u = S.u0; u < S.u1 && ok;) {
             const Seg g = make_seg(S, u, S.u1);
             const int tile = 2 * g.pt + (int)rank;
@@ -876,18 +893,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             if (!ok) break;
             tc_fence_after();
             const uint32_t taddr = tmem_base + ((uint32_t)(32 * q) << 16) + acc * kDblTok;
-            // the next chunk's TMEM load is in flight while this chunk is handled
-            uint32_t u16[16];
-            if (16 * half < g.nmma) tmem_ld16(taddr + 16 * half, u16);
             if (whole) {
                 const EpiRow er = epi_row<EPI>(p.epi, tile, row);
                 const EpiDst dd = epi_dst<EPI>(p.epi, tile);
+                // the next chunk's TMEM load is in flight while this chunk is handled (QKV,
+                // whose RoPE loads take registers, loads each chunk when it needs it)
+                constexpr bool kAhead = EPI != EPI_QKV;
+                uint32_t u16[16];
+                if (kAhead && 16 * half < g.nmma) tmem_ld16(taddr + 16 * half, u16);
                 for (int c0 = 16 * half; c0 < g.nmma; c0 += 32) {
+                    if (!kAhead) tmem_ld16(taddr + c0, u16);
                     tmem_ld_wait(u16);
                     float v[16];
 #pragma unroll
                     for (int i = 0; i < 16; i++) v[i] = __uint_as_float(u16[i]);
-                    if (c0 + 32 < g.nmma) tmem_ld16(taddr + c0 + 32, u16);
+                    if (kAhead && c0 + 32 < g.nmma) tmem_ld16(taddr + c0 + 32, u16);
                     epi_values<EPI>(p.epi, er, s_rpos, c0, g.ntok, v, my_stage);
                     named_bar_sync(2 + half, kEpiThreads / 2);
                     epi_copyout<EPI>(dd, s_pos, g.m0, c0, g.ntok, my_stage, tid_h);
@@ -896,59 +916,65 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 release_acc(acc);
             } else {
                 const int slot = g.ot == first_ot ? 0 : 1;
-                float *wsl = p.ws + ((size_t)blockIdx.x * 2 + slot) * kWsTile;
-                for (int c0 = 16 * half; c0 < g.nmma; c0 += 32) {
-                    tmem_ld_wait(u16);
-                    uint4 qv[4];
-#pragma unroll
-                    for (int j = 0; j < 4; j++) qv[j] = make_uint4(u16[4 * j], u16[4 * j + 1], u16[4 * j + 2], u16[4 * j + 3]);
-                    if (c0 + 32 < g.nmma) tmem_ld16(taddr + c0 + 32, u16);
-                    float *dst = wsl + (size_t)c0 * 128 + row * 4;  // column group c0/4, this row
-#pragma unroll
-                    for (int j = 0; j < 4; j++) *reinterpret_cast<uint4 *>(dst + j * 512) = qv[j];
+                Fix &f = fx[nfx++];
+                f.g = g;
+                const int c_first = S.owner(g.ot * S.kb), c_last = S.owner((g.ot + 1) * S.kb - 1);
+                f.nc = c_last - c_first + 1;
+                f.me = pair - c_first;
+                const int nch = g.nmma >> 4;
+                f.ch0 = f.me * nch / f.nc;
+                f.ch1 = (f.me + 1) * nch / f.nc;
+                // resident: no later segment of this pair reuses the accumulator
+                const bool resident = si + (S.dbl ? 2 : 1) >= nseg;
+                f.tm = resident ? acc * kDblTok : -1;
+                if (et < f.nc && et < kMaxContrib) {
+                    const int c = c_first + et;
+                    const int sl = (S.begin_of(c) / S.kb == g.ot) ? 0 : 1;
+                    s_contrib[(nfx - 1) * kMaxContrib + et] = ((long long)(2 * c + (int)rank) * 2 + sl) * kWsTile;
                 }
-                // the accumulator is in registers / on its way to the workspace
-                release_acc(acc);
+                float *wsl = p.ws + ((size_t)blockIdx.x * 2 + slot) * kWsTile;
+                if (resident) {
+                    // the other contributors' shares only
+                    for (int c0 = 16 * half; c0 < g.nmma; c0 += 32) {
+                        if ((c0 >> 4) >= f.ch0 && (c0 >> 4) < f.ch1) continue;
+                        uint32_t u16[16];
+                        tmem_ld16(taddr + c0, u16);
+                        tmem_ld_wait(u16);
+                        float *dst = wsl + (size_t)c0 * 128 + row * 4;  // column group c0/4, this row
+#pragma unroll
+                        for (int j = 0; j < 4; j++)
+                            *reinterpret_cast<uint4 *>(dst + j * 512) =
+                                make_uint4(u16[4 * j], u16[4 * j + 1], u16[4 * j + 2], u16[4 * j + 3]);
+                    }
+                } else {
+                    uint32_t u16[16];
+                    if (16 * half < g.nmma) tmem_ld16(taddr + 16 * half, u16);
+                    for (int c0 = 16 * half; c0 < g.nmma; c0 += 32) {
+                        tmem_ld_wait(u16);
+                        uint4 qv[4];
+#pragma unroll
+                        for (int j = 0; j < 4; j++) qv[j] = make_uint4(u16[4 * j], u16[4 * j + 1], u16[4 * j + 2], u16[4 * j + 3]);
+                        if (c0 + 32 < g.nmma) tmem_ld16(taddr + c0 + 32, u16);
+                        float *dst = wsl + (size_t)c0 * 128 + row * 4;
+#pragma unroll
+                        for (int j = 0; j < 4; j++) *reinterpret_cast<uint4 *>(dst + j * 512) = qv[j];
+                    }
+                    // the accumulator is in registers / on its way to the workspace
+                    release_acc(acc);
+                }
                 __threadfence();
                 named_bar_sync(1, kEpiThreads);
                 if (et == 0) atomicAdd(&p.tile_cnt[2 * g.ot + rank], 1);
-                if (slot == 0) split_u0 = u;
-                else split_u1 = u;
             }
             named_bar_sync(1, kEpiThreads);  // okflag is reused by the next segment
             si++;
             u += g.k1 - g.k0;
         }
 
-        // ── deferred split-tile fixups: every MMA of this CTA has completed, so the rings
-        //    (everything below the barriers) are free for staging.  Both split tiles (the
-        //    pair's first and last) are waited for together and, when this contributor's
-        //    shares of both fit, staged by one round of bulk copies. ──
-        constexpr int kStageBytes = AR + BRING + NRAW * RSB;
-        constexpr int kChunkBytes = 16 * 128 * 4;  // one 16-column chunk of one partial
-        struct Fix {
-            Seg g;
-            int nc, ch0, ch1, me;
-        };
-        Fix fx[2];
-        int nfx = 0;
-        for (int i = 0; i < 2; i++) {
-            const int su = i == 0 ? split_u0 : split_u1;
-            if (su < 0) continue;
-            Fix &f = fx[nfx++];
-            f.g = make_seg(S, su, S.u1);
-            const int c_first = S.owner(f.g.ot * S.kb), c_last = S.owner((f.g.ot + 1) * S.kb - 1);
-            f.nc = c_last - c_first + 1;
-            f.me = pair - c_first;
-            const int nch = f.g.nmma >> 4;
-            f.ch0 = f.me * nch / f.nc;
-            f.ch1 = (f.me + 1) * nch / f.nc;
-            if (et < f.nc && et < kMaxContrib) {
-                const int c = c_first + et;
-                const int sl = (S.begin_of(c) / S.kb == f.g.ot) ? 0 : 1;
-                s_contrib[(nfx - 1) * kMaxContrib + et] = ((long long)(2 * c + (int)rank) * 2 + sl) * kWsTile;
-            }
-        }
+        // ── deferred split-tile fixups, once every MMA of this CTA has completed (the rings
+        //    are drained): both split tiles are waited for together, then each chunk of this
+        //    contributor's shares is summed from the workspace (own share of a resident
+        //    accumulator from TMEM) ──
         if (nfx > 0 && ok) {
             if (et == 0) {
                 int okw = 1;
@@ -962,46 +988,79 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     }
                 }
                 *okflag = okw;
-                if (okw) fence_proxy_async_all();  // the partials, seen here, before the bulk reads
             }
             named_bar_sync(1, kEpiThreads);
             ok = *okflag != 0;
         }
-        // Staged rounds (a fix's chunk range in pieces of at most half the staging area),
-        // double-buffered: the copies of round k + 1 land while round k is summed.  A fix
-        // whose contributors' chunk does not fit half the area reads the workspace directly.
-        constexpr int kHalfStage = (kStageBytes / 2) & ~1023;
-        const float *sbuf = reinterpret_cast<const float *>(smem);
-        auto staged_fix = [&](int i) { return fx[i].nc * kChunkBytes <= kHalfStage; };
-        auto per_round = [&](int i) { return kHalfStage / (fx[i].nc * kChunkBytes); };
-        // bulk copies of chunks [r0, r0 + nr) of every contributor of fix i into smem + off
-        auto stage_chunks = [&](int i, int r0, int nr, size_t off, uint64_t *bar) {
-            mbar_arrive_expect_tx(bar, (uint32_t)(fx[i].nc * nr * kChunkBytes));
-            for (int c = 0; c < fx[i].nc; c++)
-                bulk_g2s(smem + off + (size_t)c * nr * kChunkBytes, p.ws + s_contrib[i * kMaxContrib + c] + (size_t)r0 * 2048,
-                         (uint32_t)(nr * kChunkBytes), bar);
-        };
-        // sum and finish chunks [r0, r0 + nr) of fix i, staged at smem + off (or read from the
-        // workspace when not staged)
-        auto finish_chunks = [&](int i, int r0, int nr, bool staged, size_t off) {
+        // Each thread prefetches, per chunk of its half, the other contributors' partials of
+        // its row into its own slots of the drained rings by cp.async, one chunk ahead, so the
+        // L2 latency of chunk n + 1 overlaps chunk n.  Slots per buffer: [remote contributor]
+        // [4 float4][256 threads] (consecutive threads hold consecutive 16 bytes).  The layout
+        // depends on the tile, so both halves finish a tile before either starts the next.
+        constexpr int kStageBytes = AR + BRING + NRAW * RSB;
+        for (int i = 0; i < nfx && ok; i++) {
             const Fix &f = fx[i];
+            if (i > 0) named_bar_sync(1, kEpiThreads);
+            load_pos(f.g.m0, f.g.ntok);
             const int tile = 2 * f.g.pt + (int)rank;
             const EpiRow er = epi_row<EPI>(p.epi, tile, row);
             const EpiDst dd = epi_dst<EPI>(p.epi, tile);
-            const float *base = sbuf + off / 4;
-            for (int ch = r0 + half; ch < r0 + nr; ch += 2) {
+            const long long *contrib = s_contrib + i * kMaxContrib;
+            const bool own_tm = f.tm >= 0;
+            const uint32_t taddr = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(own_tm ? f.tm : 0);
+            const int part_bytes = (f.nc - (own_tm ? 1 : 0)) * 4 * 16 * kEpiThreads;
+            const int buf_bytes = part_bytes;
+            const int nbuf = 2 * buf_bytes <= kStageBytes ? 2 : buf_bytes <= kStageBytes ? 1 : 0;
+            auto issue = [&](int ch, int b) {
+                uint8_t *base = smem + (size_t)b * buf_bytes;
+                int slot = 0;
+                for (int c = 0; c < f.nc; c++) {
+                    if (c == f.me && own_tm) continue;
+                    const float *src = p.ws + contrib[c] + (size_t)ch * 2048 + row * 4;
+#pragma unroll
+                    for (int j = 0; j < 4; j++) cp_async16(base + ((size_t)(slot * 4 + j) * kEpiThreads + et) * 16, src + j * 512);
+                    slot++;
+                }
+                cp_async_commit();
+            };
+            if (nbuf == 2 && f.ch0 + half < f.ch1) issue(f.ch0 + half, 0);
+            int k = 0;
+            for (int ch = f.ch0 + half; ch < f.ch1; ch += 2, k++) {
+                const int b = nbuf == 2 ? (k & 1) : 0;
+                if (nbuf == 2) {
+                    if (ch + 2 < f.ch1) {
+                        issue(ch + 2, b ^ 1);
+                        cp_async_wait<1>();
+                    } else {
+                        cp_async_wait<0>();
+                    }
+                } else if (nbuf == 1) {
+                    issue(ch, 0);
+                    cp_async_wait<0>();
+                }
+                const uint8_t *base = smem + (size_t)b * buf_bytes;
+                // contributors in order
                 float v[16];
 #pragma unroll
-                for (int k = 0; k < 16; k++) v[k] = 0.f;
+                for (int kk = 0; kk < 16; kk++) v[kk] = 0.f;
+                int slot = 0;
                 for (int c = 0; c < f.nc; c++) {
                     float4 t[4];
-                    if (staged) {
-                        const float4 *src = reinterpret_cast<const float4 *>(base + ((size_t)c * nr + (ch - r0)) * 2048 + row * 4);
+                    if (c == f.me && own_tm) {
+                        uint32_t u16[16];
+                        tmem_ld16(taddr + 16 * ch, u16);
+                        tmem_ld_wait(u16);
 #pragma unroll
-                        for (int j = 0; j < 4; j++) t[j] = src[j * 128];
+                        for (int j = 0; j < 4; j++)
+                            t[j] = make_float4(__uint_as_float(u16[4 * j]), __uint_as_float(u16[4 * j + 1]),
+                                               __uint_as_float(u16[4 * j + 2]), __uint_as_float(u16[4 * j + 3]));
+                    } else if (nbuf) {
+#pragma unroll
+                        for (int j = 0; j < 4; j++)
+                            t[j] = *reinterpret_cast<const float4 *>(base + ((size_t)(slot * 4 + j) * kEpiThreads + et) * 16);
+                        slot++;
                     } else {
-                        const float4 *src =
-                            reinterpret_cast<const float4 *>(p.ws + s_contrib[i * kMaxContrib + c] + (size_t)ch * 2048 + row * 4);
+                        const float4 *src = reinterpret_cast<const float4 *>(p.ws + contrib[c] + (size_t)ch * 2048 + row * 4);
 #pragma unroll
                         for (int j = 0; j < 4; j++) t[j] = __ldcg(src + j * 128);
                     }
@@ -1018,62 +1077,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 epi_copyout<EPI>(dd, s_pos, f.g.m0, ch * 16, f.g.ntok, my_stage, tid_h);
                 named_bar_sync(2 + half, kEpiThreads / 2);
             }
-        };
-        if (ok && nfx > 0) {
-            // round cursors (fix, first chunk) over the staged fixes: next to issue, next to sum
-            auto skip = [&](int &i, int &r) {
-                while (i < nfx && (r >= fx[i].ch1 || !staged_fix(i))) {
-                    if (++i < nfx) r = fx[i].ch0;
-                }
-            };
-            int ii = 0, ir = fx[0].ch0, ci = 0, cr = fx[0].ch0;
-            skip(ii, ir);
-            skip(ci, cr);
-            uint32_t ph[2] = {0, 0};
-            int pend[2] = {0, 0};  // rounds issued into each buffer and not yet waited for
-            auto issue = [&](int b) {
-                const int nr = min(fx[ii].ch1, ir + per_round(ii)) - ir;
-                if (et == 0) stage_chunks(ii, ir, nr, (size_t)b * kHalfStage, b ? fix_bar2 : fix_bar);
-                pend[b]++;
-                ir += nr;
-                skip(ii, ir);
-            };
-            if (ii < nfx) issue(0);
-            for (int k = 0; ci < nfx && ok; k++) {
-                const int b = k & 1;
-                const int nr = min(fx[ci].ch1, cr + per_round(ci)) - cr;
-                // the other buffer's last round was summed (barrier and proxy fence below)
-                if (ii < nfx) issue(b ^ 1);
-                if (et == 0) *okflag = mbar_wait(b ? fix_bar2 : fix_bar, ph[b], abort_flag, p.err, kErrTimeout + 10, p.timeout_ns) ? 1 : 0;
-                named_bar_sync(1, kEpiThreads);
-                if (!*okflag) { ok = false; break; }
-                ph[b] ^= 1;
-                pend[b]--;
-                load_pos(fx[ci].g.m0, fx[ci].g.ntok);
-                finish_chunks(ci, cr, nr, true, (size_t)b * kHalfStage);
-                // staged chunks consumed before the buffer's next copies; generic reads of the
-                // staging area before the async-proxy writes
-                named_bar_sync(1, kEpiThreads);
-                if (et == 0) fence_proxy_async_smem();
-                cr += nr;
-                skip(ci, cr);
-            }
-            // after an abort: the copies in flight land before the CTA can exit
-            if (!ok && et == 0)
-                for (int b = 0; b < 2; b++)
-                    if (pend[b] > 0) spin_bounded(b ? fix_bar2 : fix_bar, ph[b]);
-            for (int i = 0; i < nfx && ok; i++) {
-                if (staged_fix(i) || fx[i].ch1 <= fx[i].ch0) continue;
-                load_pos(fx[i].g.m0, fx[i].g.ntok);
-                finish_chunks(i, fx[i].ch0, fx[i].ch1 - fx[i].ch0, false, 0);
-            }
+        }
+        if (ok && et == 0) {
             // departure: the last of the nc contributors resets the counter for the next launch
-            if (ok && et == 0) {
-                for (int i = 0; i < nfx; i++) {
-                    int *cntp = p.tile_cnt + 2 * fx[i].g.ot + rank;
-                    const int old = atomicAdd(cntp, 1);
-                    if (old == 2 * fx[i].nc - 1) *cntp = 0;
-                }
+            for (int i = 0; i < nfx; i++) {
+                int *cntp = p.tile_cnt + 2 * fx[i].g.ot + rank;
+                const int old = atomicAdd(cntp, 1);
+                if (old == 2 * fx[i].nc - 1) *cntp = 0;
             }
         }
     }
