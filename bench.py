@@ -346,6 +346,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tp", action="store_true",
+                    help="under torchrun: the ranks run one sequence tensor-parallel instead of one each")
     ap.add_argument("--probe-arch", default="llada", choices=["llada", "dream"])
     ap.add_argument("--probe-vocab", type=int, default=16384)
     ap.add_argument("--probe-generate", action="store_true")
@@ -377,17 +379,26 @@ def main():
     if rank != 0:
         path, arch = model_file(pkg, cfg, work)
     t_synth = time.perf_counter() - t_synth
-    model = pkg.Model(path)
+    # --tp: the ranks form one tensor-parallel group over a single sequence (heads, FFN features
+    # and vocabulary split; NCCL all-reduce after O and down) instead of independent replicas
+    tp = bool(args.tp) and world > 1
+    if tp and cfg.get("n_seq"):
+        raise SystemExit("--tp runs the single-sequence configurations (c1, c2, c3)")
+    if tp:
+        nid = dp.broadcast_bytes(pkg.tp_unique_id() if rank == 0 else b"")
+        model = pkg.Model(path, tp=(rank, world, nid))
+    else:
+        model = pkg.Model(path)
     hp = model.hparams
     P, B = cfg["prompt"], cfg["block"]
     params = pkg.SamplerParams(n_steps=cfg["steps"], remasking=cfg["remasking"], entropy_threshold=cfg["tau"],
                                use_cache=cfg["cache"])
-    rng = np.random.default_rng(1234 + rank)
+    rng = np.random.default_rng(1234 if tp else 1234 + rank)  # one shared sequence under --tp
     # sequences of one bench step on this rank: one (configs 1-3) or this rank's share of
     # n_seq, all stepped together in one forward per denoising step (generate_batch)
     batched = bool(cfg.get("n_seq"))
     my_seq = pkg.dp.shard(cfg["n_seq"], rank, world) if batched else range(1)
-    n_seq_total = cfg["n_seq"] if batched else world
+    n_seq_total = cfg["n_seq"] if batched else (1 if tp else world)
     ctx = pkg.Context(model, (P + B) * len(my_seq))
     prompts = [[rng.integers(0, min(hp.mask_token_id, hp.n_vocab) - 1, P).astype(np.int32) for _ in my_seq]
                for _ in range(args.warmup + args.steps)]
@@ -462,7 +473,8 @@ def main():
         "metric": "denoised tok/s per B200 (LLaDA-8B Q4_K_M, B=256, 16 steps)" if args.config == "c2" else
         f"denoised tok/s ({args.config})",
         "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": tot_dev / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "ms_per_step": tot_dev / args.steps, "higher_is_better": True, "scaling": "strong" if tp else "weak",
+        "vs_baseline": None,
         "dtype": "f32-exact products (f16 hi x f16 hi + e4m3 corrections, f32 accumulation); f32 attention",
         "data": "synthetic",
         "config": {"workload": cfg["desc"], "prompt_len": P, "block": B, "denoise_steps": cfg["steps"],
@@ -470,7 +482,9 @@ def main():
                                        if batched else "one diffuse_generate call (all denoising steps of one sequence)"),
                    "sequences_per_rank": len(my_seq),
                    "l2": "inputs larger than L2: the weights (4.4-15 GB) stream from HBM every denoising step",
-                   "parallelism": f"dp{world} (independent sequences)",
+                   "parallelism": (f"tp{world} (one sequence; NCCL all-reduce after O and down)" if tp
+                                   else f"dp{world} (independent sequences)"),
+                   "value_scope": "tokens of all ranks / the slowest rank's device time",
                    "active_rows_per_denoising_step": actives,
                    "denoising_step_ms": (tot_dev / args.steps) / max(len(actives), 1),
                    "algorithmic_tflop_per_step": flops_run / 1e12,

@@ -87,6 +87,20 @@ class DataParallel:
             return float(x)
         return self._reduce(x, self._dist.ReduceOp.SUM)
 
+    def broadcast_bytes(self, data: bytes) -> bytes:
+        """Rank 0's bytes on every rank (e.g. the NCCL unique id of tensor parallelism)."""
+        if self._dist is None:
+            return bytes(data)
+        import torch
+        n = torch.tensor([len(data)], dtype=torch.int64, device=self._device())
+        self._dist.broadcast(n, src=0)
+        buf = np.zeros(int(n.item()), np.uint8)
+        if self.rank == 0:
+            buf[:] = np.frombuffer(data, np.uint8)
+        t = torch.from_numpy(buf).to(self._device())
+        self._dist.broadcast(t, src=0)
+        return t.cpu().numpy().tobytes()
+
     def gather_rows(self, rows: np.ndarray, n_total: int) -> np.ndarray | None:
         """Concatenates every rank's int32 [n_local, L] block in rank order on rank 0
         (the blocks of shard(n_total, r, world)); other ranks get None."""

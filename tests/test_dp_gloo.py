@@ -42,7 +42,9 @@ def _rank_main(rank, world, port, n_seq, n_gen, out_q):
     slowest = dp.max_over_ranks(10.0 + rank)
     total = dp.sum_over_ranks(len(mine))
     gathered = dp.gather_rows(rows, n_seq)
-    out_q.put((rank, slowest, total, None if gathered is None else gathered.tolist()))
+    # rank 0's bytes (the tensor-parallel NCCL id under bench.py --tp) reach every rank
+    shared = dp.broadcast_bytes(bytes(range(128)) if rank == 0 else b"")
+    out_q.put((rank, slowest, total, None if gathered is None else gathered.tolist(), shared))
     dp.close()
 
 
@@ -56,8 +58,9 @@ def test_two_rank_gloo_sharding(n_seq):
         p.start()
     res = {}
     for _ in range(world):
-        rank, slowest, total, gathered = q.get(timeout=120)
+        rank, slowest, total, gathered, shared = q.get(timeout=120)
         res[rank] = (slowest, total, gathered)
+        assert shared == bytes(range(128))
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
