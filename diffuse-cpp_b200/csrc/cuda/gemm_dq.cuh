@@ -112,23 +112,33 @@ constexpr int kDeqWarps = 8;             // two sets of four: even / odd k-slice
 constexpr int kSliceBytes = 128 * 128;   // one 64-wide k-slice of this CTA's 128 weight rows (f16)
 constexpr int kMaxTok = 256;             // tokens per MMA group (N) of the pair
 constexpr int kDblTok = 192;             // groups up to this size double-buffer the accumulator
-// (an MMA's N is the group rounded up to 32: the limit is a multiple of 32 so a
+// (an MMA's N is the group rounded up to 32: the limits are multiples of 32 so a
 // double-buffered accumulator never reaches the next one or the A stages)
 static_assert(kDblTok % 32 == 0, "double-buffered accumulator width");
+constexpr int kDbl4Tok = 128;            // ... and groups up to this size also get four A stages
 constexpr int kWsTile = kMaxTok * 128;   // floats per partial tile (one CTA's 128 rows)
 constexpr int kErrTimeout = 0x100;
 constexpr int kMaxAStages = 6, kMaxBSlots = 24, kMaxRawStages = 4;
-// TMEM (512 columns per CTA): accumulators [0, 192) and [192, 384) for token groups of up
-// to 192, one accumulator [0, 256) for larger groups (the MMA of the next segment then
-// waits for the epilogue to drain it, which costs less than dequantizing the weights once
-// per group of 128); dequantized A stages (quantized weights) at [384 + 64 st, +64):
-// lane = weight row, one k-slice each: f16 hi in the first 32 columns, then the E4M3
-// correction pair (16 columns W_hi 2^-10, 16 columns W_lo), or f16 lo for XS = 1.
-constexpr int kTmemA = 2 * kDblTok;
+// TMEM (512 columns per CTA), by token-group size (Sched::init):
+//   <= 128: accumulators [0, 128), [128, 256), four A stages at [256, 512);
+//   <= 192: accumulators [0, 192), [192, 384), two A stages at [384, 512);
+//   larger: one accumulator [0, 256) (the MMA of the next segment waits for the epilogue to
+//           drain it, which costs less than dequantizing the weights once per group of
+//           128), four A stages at [256, 512).
+// An A stage (quantized weights) holds one k-slice, lane = weight row: f16 hi in the first
+// 32 columns, then the E4M3 correction pair (16 columns W_hi 2^-10, 16 columns W_lo), or
+// f16 lo for XS = 1.  Dequantizer set p fills the stages of its slices (p, or p and p + 2
+// alternately with four stages), so with four stages a set runs a whole slice ahead of the
+// MMA that frees its previous stage.  f16 / f32 weight tiles come through shared memory
+// (two stages) instead; their accumulators are always double-buffered ([0, 256), [256, 512)).
 constexpr int kTmemAStage = 64;
 constexpr int kTmemALo = 32;
-constexpr int kNA = 2;                   // A stages: set p of the dequantizers fills stage p
-static_assert(kTmemA + kNA * kTmemAStage <= 512, "TMEM columns");
+constexpr int kNA = 2;                   // shared-memory A stages (f16 / f32 weight tiles)
+constexpr int kMaxNA = 4;                // TMEM A stages
+static_assert(2 * kDblTok + 2 * kTmemAStage <= 512 && 2 * kDbl4Tok + 4 * kTmemAStage <= 512 &&
+              kMaxTok + 4 * kTmemAStage <= 512, "TMEM columns");
+// The relay returns the activation slot of slice j - kRelayLag while it handles slice j.
+constexpr int kRelayLag = 2;
 
 // Rings per weight type, sized so that shared memory (227 KB) holds them:
 //  A        one k-slice per stage, two stages: dequantized weights go to TMEM (written by
@@ -179,15 +189,27 @@ __host__ __device__ constexpr int gemm_smem_bytes(int wt, int xs) {
 // both CTAs of a pair.  Units are (pair tile of 256 weight rows, token group, k-block).
 struct Sched {
     int M, n_mg, gsz, kb, n_ot, U, G, u0, u1;
-    bool dbl;                 // double-buffered accumulator (gsz <= kDblTok)
+    bool dbl;                 // double-buffered accumulator
+    int na;                   // A stages (TMEM: 2 or 4; shared-memory tiles: 2)
+    int acc_stride;           // TMEM columns between the two accumulators
+    int tmem_a;               // TMEM column of A stage 0
     int bh, spb, bpart, bslot, nbs;  // B ring: rows per CTA (widest group), k-slices per load, bytes per
                                      // k-slice (all parts), slot bytes, slots
-    __device__ __forceinline__ void init(int M_, int n_ptiles, int kb_, int n_pairs, int pair, int ring_bytes, int xs) {
+    __device__ __forceinline__ void init(int M_, int n_ptiles, int kb_, int n_pairs, int pair, int ring_bytes, int xs,
+                                         bool a_in_tmem) {
         M = M_;
         kb = kb_;
         n_mg = (M + kMaxTok - 1) / kMaxTok;
         gsz = (((M + n_mg - 1) / n_mg) + 15) & ~15;
-        dbl = gsz <= kDblTok;
+        if (!a_in_tmem) {
+            dbl = true; na = kNA; acc_stride = kMaxTok; tmem_a = 0;
+        } else if (gsz <= kDbl4Tok) {
+            dbl = true; na = 4; acc_stride = kDbl4Tok; tmem_a = 2 * kDbl4Tok;
+        } else if (gsz <= kDblTok) {
+            dbl = true; na = 2; acc_stride = kDblTok; tmem_a = 2 * kDblTok;
+        } else {
+            dbl = false; na = 4; acc_stride = 0; tmem_a = kMaxTok;
+        }
         n_ot = n_ptiles * n_mg;
         U = n_ot * kb;
         G = n_pairs < U ? n_pairs : U;
@@ -446,8 +468,8 @@ __device__ __forceinline__ void epi_copyout(const EpiDst &d, const int *s_pos, i
 //
 // Shared memory (per CTA): [A ring (f16 weight tiles only): a_stages x a_stage_bytes]
 // [B ring][raw ring][barriers][token positions][contributor offsets].  Slice i (64 k) of
-// the CTA's unit range uses A stage i % a_stages (TMEM columns kTmemA + 64 stage for
-// quantized weights) and part i % spb of B slot (i / spb) % nbs; a part holds the
+// the CTA's unit range uses A stage i % na (TMEM columns tmem_a + 64 stage for quantized
+// weights, Sched::init) and part i % spb of B slot (i / spb) % nbs; a part holds the
 // slice's XS sub-slices (hi, then lo).
 //
 // MMAs per slice: W_hi.X_hi, W_hi.X_lo (XS = 2), W_lo.X_hi (weights with a lo part).
@@ -465,11 +487,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     constexpr int CPR = raw_cpr(WT), RSB = CPR * RAWB;  // chunks and bytes per raw stage
     static_assert(gemm_smem_bytes(WT, XS) <= 227 * 1024, "shared memory per CTA");
     static_assert(XS == 1 || XS == 2, "activation parts");
-    static_assert(NA == 2, "dequantizer set p fills A stage p");
-    // The relay frees the B slot of slice j - NA while it handles slice j, after waiting
+    static_assert(NA == 2, "shared-memory A tiles: two stages");
+    // The relay frees the B slot of slice j - kRelayLag while it handles slice j, after waiting
     // for the B loads up to slice j - 1: with one slice per load (the widest group, 16 or
-    // 32 KB loads) the producer needs 2 + (NA - 1) slots not to wait on itself.
-    static_assert(BRING / (kMaxTok / 2 * 128 * XS) >= 2 + (NA - 1), "B ring too shallow for the A ring");
+    // 32 KB loads) the producer needs 2 + (kRelayLag - 1) slots not to wait on itself.
+    static_assert(BRING / (kMaxTok / 2 * 128 * XS) >= 2 + (kRelayLag - 1), "B ring too shallow for the relay");
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *aring = smem;  // f16 weight tiles only
@@ -492,7 +514,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     // the next kernel of the stream may be scheduled now; it waits for this grid itself
     griddep_launch_dependents();
     if (threadIdx.x == 0) {
-        for (int i = 0; i < NA; i++) {
+        for (int i = 0; i < kMaxNA; i++) {
             // both CTAs' relays + f16 tiles: the expect_tx / else four dequant warps per CTA
             mbar_init(&full_a[i], w_smem(WT) ? 3 : 10);
             mbar_init(&empty_a[i], 1);                   // the paired MMA's commit
@@ -533,7 +555,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     // wait for the activations.
     const int M = *reinterpret_cast<volatile const int *>(p.m_dev);
     Sched S;
-    S.init(M, p.n_tiles >> 1, p.kb, n_pairs, pair, BRING, XS);
+    S.init(M, p.n_tiles >> 1, p.kb, n_pairs, pair, BRING, XS, !w_smem(WT));
+    const int lg_na = S.na == 4 ? 2 : 1;
     const int NBS = S.nbs;
     // barriers of the even CTA as cluster addresses
     const uint32_t full_a0 = mapa_shared(full_a, 0), acc_empty0 = mapa_shared(acc_empty, 0);
@@ -628,10 +651,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         // Every instruction on this thread's path between two slices leaves the tensor
         // pipe idle (the queue holds about one MMA), so the per-slice work is only: wait
         // for the stage, fence, the slice's MMAs, commit.  Each unit is one k-block = four
-        // slices; slice s2 uses A stage s2 & 1, whose barrier completes twice per k-block,
-        // so its parity is s2 >> 1; the B descriptors are computed once per k-block.
+        // slices; slice j of the range uses A stage j % na, whose barrier completes once per
+        // use, so its parity is (j / na) & 1; the B descriptors are computed once per k-block.
         if (lane == 0 && rank == 0) {
-            int si = 0;  // accumulator segments
+            int si = 0;   // accumulator segments
+            int kbc = 0;  // k-blocks issued
             bool ok = true, issued = false;
             const uint64_t bdesc0 = sw128_desc(smem_u32(bring)), adesc0 = sw128_desc(smem_u32(aring));
             const int lg_spb = S.spb == 1 ? 0 : S.spb == 2 ? 1 : 2;  // k-slices per ring slot: 1, 2 or 4
@@ -642,7 +666,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 const int acc = S.acc_of(si);
                 if (!(ok = mbar_wait(&acc_empty[acc], (S.acc_uses(si) & 1) ^ 1, abort_flag, p.err, kErrTimeout + 3, p.timeout_ns))) break;
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + acc * kDblTok;
+                const uint32_t d_tmem = tmem_base + acc * S.acc_stride;
                 const uint32_t idesc = idesc_f16(256, (uint32_t)g.nmma);
                 uint32_t accum = 0;
                 for (int kbi = g.k0; kbi < g.k1; kbi++) {
@@ -656,9 +680,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     bslot = (bslot + (4 >> lg_spb)) % NBS;
 #pragma unroll
                     for (int s2 = 0; s2 < 4; s2++) {
-                        const int st = s2 & 1;
+                        // slice j = 4 kbc + s2 of the range: stage j % na, use j / na of it
+                        const int j = 4 * kbc + s2;
+                        const int st = j & (S.na - 1);
                         // full_a also carries the relays' arrivals: this stage's B rows have landed
-                        if (!(ok = mbar_wait(&full_a[st], (uint32_t)(s2 >> 1), abort_flag, p.err, kErrTimeout + 5, p.timeout_ns))) break;
+                        if (!(ok = mbar_wait(&full_a[st], (uint32_t)((j >> lg_na) & 1), abort_flag, p.err, kErrTimeout + 5, p.timeout_ns))) break;
                         tc_fence_after();
                         // main term (f16), then the corrections: XS = 2 one E4M3 MMA over the
                         // correction pairs, XS = 1 W_lo.X (f16) for weights with a lo part
@@ -670,7 +696,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                             if constexpr (XS == 2) mma2_f8_ss_k128(d_tmem, a2, bcor, idesc);
                             else if constexpr (w_split(WT)) mma2_f16_ss_k64(d_tmem, a2, bhi, idesc, 1);
                         } else {
-                            const uint32_t ahi = tmem_base + kTmemA + st * kTmemAStage;
+                            const uint32_t ahi = tmem_base + (uint32_t)S.tmem_a + st * kTmemAStage;
                             mma2_f16_ts_k64(d_tmem, ahi, bhi, idesc, accum);
                             if constexpr (XS == 2) mma2_f8_ts_k128(d_tmem, ahi + kTmemALo, bcor, idesc);
                             else mma2_f16_ts_k64(d_tmem, ahi + kTmemALo, bhi, idesc, 1);
@@ -679,6 +705,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         mma2_commit_mc(&empty_a[st], 0x3);
                     }
                     issued = true;
+                    kbc++;
                     if (!ok) break;
                 }
                 if (!ok) break;
@@ -694,8 +721,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
     } else if (role == R_RELAY) {
-        // ── relay (one thread per CTA), slice by slice: once the MMA of slice j - NA has
-        //    completed (empty_a, the same wait the A writers do), its B slot is free again
+        // ── relay (one thread per CTA), slice by slice: once the MMA of slice j - kRelayLag
+        //    has completed (empty_a of its stage), its B slot is free again
         //    (after the last slice of the slot's load); once this CTA's B rows of slice j
         //    have landed (full_b), arrive on full_a of slice j in the even CTA.  The MMA issuer so waits on one barrier per stage, and no relay
         //    can fall a full phase behind the barriers it polls. ──
@@ -708,14 +735,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             }
             bool ok = true;
             const int spb = S.spb;
-            // running ring positions (no divisions): B load of slice j and of slice j - NA
+            // running ring positions (no divisions): B load of slice j and of slice j - kRelayLag
             int fo_sl = 0, fo_part = 0, eo_sl = 0, eo_part = 0;
             uint32_t fo_ph = 0;
-            for (int j = 0; j < n_it + NA && ok; j++) {  // A stage = slice j
-                if (j >= NA) {
-                    // MMA of slice j - NA done (phase (j - NA) / NA of empty_a[j % NA]); its B
-                    // slot is free once the last slice of the slot's load is done
-                    if (!(ok = mbar_wait(&empty_a[j % NA], ((j / NA) & 1) ^ 1, abort_flag, p.err, kErrTimeout + 12, p.timeout_ns))) break;
+            for (int j = 0; j < n_it + kRelayLag && ok; j++) {  // A stage = slice j % na
+                if (j >= kRelayLag) {
+                    // MMA of slice jd = j - kRelayLag done (use jd / na of its stage; the stage's
+                    // next use needs this relay's arrival for slice jd + na > j first, so the
+                    // barrier cannot be a phase ahead); its B slot is free once the last slice
+                    // of the slot's load is done
+                    const int jd = j - kRelayLag;
+                    if (!(ok = mbar_wait(&empty_a[jd & (S.na - 1)], (uint32_t)((jd >> lg_na) & 1), abort_flag, p.err,
+                                         kErrTimeout + 12, p.timeout_ns))) break;
                     if (++eo_part == spb) {
                         eo_part = 0;
                         mbar_arrive(&empty_b[eo_sl]);
@@ -725,7 +756,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 if (j < n_it) {
                     if (fo_part == 0)
                         if (!(ok = mbar_wait(&full_b[fo_sl], fo_ph, abort_flag, p.err, kErrTimeout + 4, p.timeout_ns))) break;
-                    mbar_arrive_cluster(full_a0 + 8 * (j % NA));
+                    mbar_arrive_cluster(full_a0 + 8 * (j & (S.na - 1)));
                     if (++fo_part == spb) {
                         fo_part = 0;
                         if (++fo_sl == NBS) { fo_sl = 0; fo_ph ^= 1; }
@@ -744,7 +775,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             int rit = 0;
             bool ok = true;
             // This warp's TMEM lane quarter holds its 32 weight rows of every A stage.
-            const uint32_t a_lane = tmem_base + ((uint32_t)(32 * (warp & 3)) << 16) + kTmemA;
+            const uint32_t a_lane = tmem_base + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)S.tmem_a;
             // The stage's tcgen05.st have completed; order them before the arrival the MMA
             // issuer waits on (no shared memory, so no proxy fence).
             auto publish = [&](int st) {
@@ -764,7 +795,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 return okb;
             };
             auto wait_a = [&](int ia) {
-                return wait_warp(&empty_a[ia % NA], ((ia / NA) & 1) ^ 1, kErrTimeout + 7);
+                return wait_warp(&empty_a[ia & (S.na - 1)], ((ia >> lg_na) & 1) ^ 1, kErrTimeout + 7);
             };
             const int n_units = S.u1 - S.u0;
             for (int u = S.u0; u < S.u1 && ok;) {
@@ -777,8 +808,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         if (!ok) break;
                     }
                     const uint8_t *R = raw + rs * RSB + (rit % CPR) * RAWB;
-                    // this set's k-slices of the k-block: set and set + 2, both into A stage
-                    // `set`; each slice in two halves of 32 k.  XS = 2: f16 hi (16 columns per
+                    // this set's k-slices of the k-block: set and set + 2 (A stage set, or set and
+                    // set + 2 with four stages); each slice in two halves of 32 k.  XS = 2: f16 hi (16 columns per
                     // half), E4M3 hi 2^-10 and E4M3 lo (8 columns per half each, at 32 and 48);
                     // XS = 1: f16 hi and f16 lo (16 columns per half each, at 0 and 32).
                     using Half = typename std::conditional<XS == 2, HalfCorr, HalfSplit>::type;
@@ -804,8 +835,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     };
 #pragma unroll
                     for (int hs = 0; hs < 2; hs++) {
-                        const int ia = 4 * rit + set + 2 * hs;
-                        const uint32_t at = a_lane + (uint32_t)(set * kTmemAStage);
+                        const int ia = 4 * rit + set + 2 * hs;  // slice of the range
+                        const int st = ia & (S.na - 1);          // its stage: set, or set + 2 hs
+                        const uint32_t at = a_lane + (uint32_t)(st * kTmemAStage);
                         Half o;
                         deq(hs, 0, o);
                         if (!(ok = wait_a(ia))) break;
@@ -813,7 +845,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         store(at, 0, o);
                         deq(hs, 1, o);
                         store(at, 1, o);
-                        publish(set);
+                        publish(st);
                     }
                     __syncwarp();
                     if (lane == 0 && (rit % CPR == CPR - 1 || rit == n_units - 1)) mbar_arrive(&raw_empty[rs]);
@@ -892,7 +924,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             ok = *okflag != 0;
             if (!ok) break;
             tc_fence_after();
-            const uint32_t taddr = tmem_base + ((uint32_t)(32 * q) << 16) + acc * kDblTok;
+            const uint32_t taddr = tmem_base + ((uint32_t)(32 * q) << 16) + acc * S.acc_stride;
             if (whole) {
                 const EpiRow er = epi_row<EPI>(p.epi, tile, row);
                 const EpiDst dd = epi_dst<EPI>(p.epi, tile);
@@ -926,7 +958,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 f.ch1 = (f.me + 1) * nch / f.nc;
                 // resident: no later segment of this pair reuses the accumulator
                 const bool resident = si + (S.dbl ? 2 : 1) >= nseg;
-                f.tm = resident ? acc * kDblTok : -1;
+                f.tm = resident ? acc * S.acc_stride : -1;
                 if (et < f.nc && et < kMaxContrib) {
                     const int c = c_first + et;
                     const int sl = (S.begin_of(c) / S.kb == g.ot) ? 0 : 1;
