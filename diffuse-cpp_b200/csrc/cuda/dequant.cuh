@@ -189,6 +189,90 @@ __device__ __forceinline__ void q80_half(const uint8_t *R, int r, int s, int h, 
     }
 }
 
+__device__ __forceinline__ uint32_t e4m3x2h(__half2 v) {
+    return (uint32_t)__nv_cvt_halfraw2_to_fp8x2(*reinterpret_cast<const __half2_raw *>(&v), __NV_SATFINITE, __NV_E4M3);
+}
+
+// ── f16 routes of Q6_K and Q8_0 (activations in pair rows) ── Both build the integer
+// quant value as the f16 1024 + u with one byte permute and bring it to q by a half add.
+// Q8_0: w = d q has at most 19 significant bits, so hi = RN(d q), lo = fma(d, q, -hi) are
+// exact.  Q6_K: w = (d sc) (q - 32) with d sc of up to 18 bits, split once per group of 16
+// as ds = ds_hi + ds_lo (f16 each, ds_lo exact); hi = RN(ds_hi v), lo = fma(ds_lo, v,
+// fma(ds_hi, v, -hi)), the inner fma exact and the outer one rounded at 2^-11 of lo.
+// Four values of a quad word u (bytes) to the e4m3 correction quads and f16 hi pairs.
+template <typename F>
+__device__ __forceinline__ void quad_f16(HalfCorr &o, int j, uint32_t u, F f) {
+    const __half2 k10 = __floats2half2_rn(kCorrScale, kCorrScale);
+    __half2 ha, la, hb, lb;
+    f(u2h(__byte_perm(u, 0x64u, 0x4140)), ha, la);  // values 4j, 4j + 1
+    f(u2h(__byte_perm(u, 0x64u, 0x4342)), hb, lb);  // values 4j + 2, 4j + 3
+    o.hi[2 * j] = h2u(ha);
+    o.hi[2 * j + 1] = h2u(hb);
+    o.ch[j] = __byte_perm(e4m3x2h(__hmul2(ha, k10)), e4m3x2h(__hmul2(hb, k10)), 0x5410);
+    o.cl[j] = __byte_perm(e4m3x2h(la), e4m3x2h(lb), 0x5410);
+}
+// Q6_K group scales of one dequantizer set as f16 pairs: dsh[g] + dsl[g] = ws d sc_g.
+struct Q6XMeta {
+    __half2 dsh[8], dsl[8];
+};
+__device__ __forceinline__ void q6x_load_meta(const uint8_t *R, int r, int set, float ws, Q6XMeta &m) {
+    Q6KMeta f;
+    q6k_load_meta(R, r, set, ws, f);
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const __half h = __float2half_rn(f.ds[i]);
+        m.dsh[i] = __half2half2(h);
+        m.dsl[i] = __half2half2(__float2half_rn(f.ds[i] - __half2float(h)));
+    }
+}
+__device__ __forceinline__ void q6x_half(const uint8_t *R, int r, int s, int hh, __half2 dsh0, __half2 dsl0, __half2 dsh1,
+                                         __half2 dsl1, HalfCorr &o) {
+    const int h = s >> 1, s2 = s & 1;
+    const uint8_t *qlrow = R + 128 * r, *qhrow = R + 16384 + 64 * r;
+    const uint4 l0 = *reinterpret_cast<const uint4 *>(qlrow + (((4 * h + 2 * hh) ^ (r & 7)) << 4));
+    const uint4 l1 = *reinterpret_cast<const uint4 *>(qlrow + (((4 * h + 2 * hh + 1) ^ (r & 7)) << 4));
+    const uint4 g0 = *reinterpret_cast<const uint4 *>(qhrow + (((2 * h) ^ ((r >> 1) & 3)) << 4));
+    const uint4 g1 = *reinterpret_cast<const uint4 *>(qhrow + (((2 * h + 1) ^ ((r >> 1) & 3)) << 4));
+    const uint32_t lw[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+    const uint32_t qw[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+    const int shift = 4 * s2 + 2 * hh;
+    const __half2 off = __floats2half2_rn(-1056.f, -1056.f);  // 1024 + 32
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const uint32_t nib = s2 ? ((lw[i] >> 4) & 0x0F0F0F0Fu) : (lw[i] & 0x0F0F0F0Fu);
+        const uint32_t q6 = nib | (((qw[i] >> shift) & 0x03030303u) << 4);
+        const __half2 dh = i < 4 ? dsh0 : dsh1, dl = i < 4 ? dsl0 : dsl1;
+        quad_f16(o, i, q6, [&](__half2 m, __half2 &hi, __half2 &lo) {
+            const __half2 v = __hadd2(m, off);
+            hi = __hmul2(dh, v);
+            lo = __hfma2(dl, v, __hfma2(dh, v, __hneg2(hi)));
+        });
+    }
+}
+// Q8_0: half h of slice s is block 2s + h with scale ws d (exact in f16).
+__device__ __forceinline__ void q8x_half(const uint8_t *R, int r, int s, int h, float ws, HalfCorr &o) {
+    const int blk = 2 * s + h;
+    const uint4 dv = *reinterpret_cast<const uint4 *>(R + 16 * r);
+    const int wi = blk >> 1;
+    const uint32_t dwd = wi == 0 ? dv.x : wi == 1 ? dv.y : wi == 2 ? dv.z : dv.w;
+    const __half2 d2 = __float2half2_rn(__half2float(__ushort_as_half((unsigned short)((dwd >> (16 * (blk & 1))) & 0xFFFF))) * ws);
+    const uint8_t *qrow = R + 2048 + 256 * r;
+    const __half2 off = __floats2half2_rn(-1152.f, -1152.f);  // 1024 + 128
+#pragma unroll
+    for (int cc = 0; cc < 2; cc++) {
+        const int c = 2 * blk + cc;
+        const uint4 v = *reinterpret_cast<const uint4 *>(qrow + (((c & 8) | ((c & 7) ^ (r & 7))) << 4));
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+            quad_f16(o, 4 * cc + i, w[i] ^ 0x80808080u, [&](__half2 m, __half2 &hi, __half2 &lo) {
+                const __half2 q = __hadd2(m, off);
+                hi = __hmul2(d2, q);
+                lo = __hfma2(d2, q, __hneg2(hi));
+            });
+    }
+}
+
 // ── activation pair rows ── per 64-wide slice: 64 hi f16 (128 B), then the correction
 // operand: 64 e4m3 of x_lo * 2^10, 64 e4m3 of x_hi (128 B); row length 4 bytes per value.
 // Eight consecutive values of a slice: one 16-byte and two 8-byte stores.

@@ -815,13 +815,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     using Half = typename std::conditional<XS == 2, HalfCorr, HalfSplit>::type;
                     [[maybe_unused]] Q4KMeta m4;
                     [[maybe_unused]] Q6KMeta m6;
+                    [[maybe_unused]] Q6XMeta m6x;
                     if constexpr (WT == W_Q4K) q4k_load_meta(R, r, set, p.wscale, m4);
-                    if constexpr (WT == W_Q6K) q6k_load_meta(R, r, set, p.wscale, m6);
+                    if constexpr (WT == W_Q6K && XS == 2) q6x_load_meta(R, r, set, p.wscale, m6x);
+                    else if constexpr (WT == W_Q6K) q6k_load_meta(R, r, set, p.wscale, m6);
+                    // Q6_K / Q8_0 with pair-row activations: f16 arithmetic (one conversion per
+                    // weight fewer than the f32 route, dequant.cuh); otherwise f32
                     auto deq = [&](int hs, int hh, Half &o) {
                         const int sl = set + 2 * hs;
+                        const int gi = 4 * hs + 2 * hh;  // Q6_K group of the half's first 16 values
                         if constexpr (WT == W_Q4K) q4k_half(R, r, sl, hh, m4.dsc[2 * hs + hh], m4.nm[2 * hs + hh], o);
-                        else if constexpr (WT == W_Q6K)
-                            q6k_half(R, r, sl, hh, m6.ds[4 * hs + 2 * hh], m6.ds[4 * hs + 2 * hh + 1], o);
+                        else if constexpr (WT == W_Q6K && XS == 2)
+                            q6x_half(R, r, sl, hh, m6x.dsh[gi], m6x.dsl[gi], m6x.dsh[gi + 1], m6x.dsl[gi + 1], o);
+                        else if constexpr (WT == W_Q6K) q6k_half(R, r, sl, hh, m6.ds[gi], m6.ds[gi + 1], o);
+                        else if constexpr (XS == 2) q8x_half(R, r, sl, hh, p.wscale, o);
                         else q80_half(R, r, sl, hh, p.wscale, o);
                     };
                     auto store = [&](uint32_t at, int hh, const Half &o) {
