@@ -141,10 +141,11 @@ static_assert(2 * kDblTok + 2 * kTmemAStage <= 512 && 2 * kDbl4Tok + 4 * kTmemAS
 constexpr int kRelayLag = 2;
 
 // Rings per weight type, sized so that shared memory (227 KB) holds them:
-//  A        one k-slice per stage, two stages: dequantized weights go to TMEM (written by
-//           tcgen05.st, read by the MMA from TMEM: no shared-memory round trip and no
-//           proxy fence, which cost ~1.2k cycles per warp and stage); f16 weight tiles
-//           are TMA-loaded into a shared-memory ring instead (hi and lo tiles for W_F32);
+//  A        one k-slice per stage: dequantized weights go to TMEM (two or four stages, see
+//           above; written by tcgen05.st, read by the MMA from TMEM: no shared-memory round
+//           trip and no proxy fence, which cost ~1.2k cycles per warp and stage); f16
+//           weight tiles are TMA-loaded into a two-stage shared-memory ring instead (hi and
+//           lo tiles for W_F32);
 //  B ring   this CTA's activation rows of 1-4 k-slices per slot, so small token counts
 //           keep many slices in flight and hide the L2 latency;
 //  raw ring re-tiled weight chunks (one k-block of 256 for 128 rows), grouped.
