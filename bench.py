@@ -198,12 +198,17 @@ def step_flops(arch, n_active, n_keys):
     return n_active * (L * 2 * (2 * d * d + 2 * d * kvd + 3 * d * ff) + 2 * d * V + L * 4 * n_keys * d)
 
 
+_ORACLE_MODELS = {}
+
+
 def reference_sample(path, cfg, prompt, threads):
     """The reference's loop (the CPU oracle's session: full forward of step 0, then the
     sampler, then the cached forward of step 1, all layers) on the host cores; returns
     (seconds of the two forwards, their algorithmic FLOPs, rows of step 1)."""
     from oracle import oracle
-    om = oracle.OracleModel(path)
+    om = _ORACLE_MODELS.get(path)
+    if om is None:  # loaded once per process: every bench step samples the same file
+        om = _ORACLE_MODELS[path] = oracle.OracleModel(path)
     prm = oracle.SamplerParams(n_steps=cfg["steps"], remasking=cfg["remasking"], entropy_threshold=cfg["tau"],
                                use_cache=cfg["cache"])
     sess = oracle.OracleSession(om, prompt, cfg["block"], prm, n_threads=threads)
@@ -216,7 +221,6 @@ def reference_sample(path, cfg, prompt, threads):
     rows1 = sess.forward(1)
     t3 = time.perf_counter()
     sess.close()
-    om.close()
     arch = ARCH[cfg["arch"]]
     return (t1 - t0) + (t3 - t2), step_flops(arch, rows0, n) + step_flops(arch, rows1, n), rows1
 
