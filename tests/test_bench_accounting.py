@@ -46,3 +46,25 @@ def test_c2_algorithmic_flops(bench, pkg):
     # step 0 alone (320 rows, full forward) is 4.852 TFLOP
     f0 = bench.c2_algorithmic_flops(hp, [320], 320)
     assert abs(f0 / 1e12 - 4.852) < 0.002
+
+
+def test_reference_arm_runs_the_oracle_only(bench, tmp_path, monkeypatch, capsys):
+    """`bench.py --impl reference` on a two-layer architecture of the same family: one JSON
+    line whose bench step is the timed sample (two full-depth denoising steps) and whose
+    generation time is extrapolated, with no product library loaded on that path."""
+    import json
+    import types
+    monkeypatch.setitem(bench.ARCH, "tiny", dict(is_dream=0, n_vocab=512, n_embd=256, n_head=4, n_head_kv=4,
+                                                 n_layer=2, n_ff=512, n_ctx=512, mask_token_id=500,
+                                                 rope_theta=10000.0, rms_norm_eps=1e-5, with_bias=0))
+    monkeypatch.setenv("DFB_BENCH_DIR", str(tmp_path))
+    cfg = dict(bench.CONFIGS["c2"], arch="tiny", desc="tiny")
+    loaded_before = set(sys.modules)
+    assert bench.run_reference(types.SimpleNamespace(steps=2, warmup=1, gpus=1, config="c2"), cfg) == 0
+    line = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert line["impl"] == "reference" and line["extrapolated"] is True
+    assert line["value"] > 0 and line["e2e"]["value"] == line["value"]
+    assert 0 < line["ms_per_step"] < line["extrapolated_ms_per_generation"]
+    assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["cores"] >= 1
+    # the product package (its ctypes bindings of libdfb_cuda / libdiffuse) was not imported here
+    assert not any(m.startswith("diffuse_b200") for m in set(sys.modules) - loaded_before)
